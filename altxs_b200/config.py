@@ -1,0 +1,190 @@
+"""Model and run configuration for the B200 model-and-code loop.
+
+``ModelConfig`` mirrors the subset of the reference ``XsaTttConfig``
+(altxs ``src/xsa_ttt/config.py:20-189``) that the per-symbol loop reads.  The
+reference motifs that sit on top of the plain GPT (XSA, SmearGate,
+SparseAttnGate, depth loops, parallel residual lanes, asymmetric softcap) are
+not part of this engine; ``from_reference_cfg`` refuses configs that enable
+them instead of silently computing a different model.
+
+The always-on pieces of the reference block are kept: QK-RMSNorm, per-head
+``q_gain``, partial RoPE over ``rope_dims``, ``resid_mix`` against ``x0``,
+``attn_scale``/``mlp_scale``, ``ln_scale = 1/sqrt(layer+1)``,
+LeakyReLU(0.5)^2 MLP, tied embeddings with ``softcap * tanh(logits/softcap)``,
+U-Net skips with sigmoid skip gates (altxs ``src/xsa_ttt/model.py:885-979,
+1377-1476``).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+import json
+from dataclasses import dataclass, field
+from typing import Any
+
+
+@dataclass
+class ModelConfig:
+    vocab_size: int = 16384
+    num_layers: int = 8
+    model_dim: int = 512
+    num_heads: int = 8
+    num_kv_heads: int = 8
+    mlp_mult: float = 4.0
+    rope_base: float = 1e4
+    rope_dims: int = 16
+    qk_gain_init: float = 5.0
+    logit_softcap: float = 30.0
+    ln_scale: bool = True
+    skip_gates_enabled: bool = True
+    tied_embed_init_std: float = 0.005
+    # sequence / lockstep (reference: block_size / online_retrain_every)
+    block_size: int = 2048
+    online_retrain_every: int = 16384
+    seed: int = 1337
+    # test-time LoRA (reference ttt_* fields, config.py:144-165)
+    retrain_mode: str = "lora"  # "lora" or "none"
+    ttt_lora_rank: int = 8
+    ttt_lora_alpha: float = 144.0
+    ttt_lora_lr: float = 1e-3
+    ttt_beta1: float = 0.0
+    ttt_beta2: float = 0.99
+    ttt_weight_decay: float = 0.0
+    ttt_k_lora: bool = True
+    ttt_o_lora: bool = True
+    ttt_mlp_lora: bool = False
+    ttt_use_rslora: bool = False
+    grad_clip: float = 1.0
+    # framework CDF rule: "fixed" (integer fixed-point softmax, total
+    # <= 2^cdf_bits) or "ref" (reference max(1, floor(p*1e6+0.5)) masses)
+    cdf_mode: str = "fixed"
+    cdf_bits: int = 20
+
+    # ---- derived ---------------------------------------------------------
+    @property
+    def head_dim(self) -> int:
+        return self.model_dim // self.num_heads
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+    @property
+    def mlp_hidden(self) -> int:
+        return int(self.mlp_mult * self.model_dim)
+
+    @property
+    def num_encoder_layers(self) -> int:
+        return self.num_layers // 2
+
+    @property
+    def num_skip_weights(self) -> int:
+        return min(self.num_encoder_layers, self.num_layers - self.num_encoder_layers)
+
+    @property
+    def ctx(self) -> int:
+        return self.block_size
+
+    @property
+    def lora_scale(self) -> float:
+        r = float(self.ttt_lora_rank)
+        if self.ttt_use_rslora:
+            return float(self.ttt_lora_alpha) / r**0.5
+        return float(self.ttt_lora_alpha) / r
+
+    @property
+    def lora_enabled(self) -> bool:
+        return self.retrain_mode == "lora" and self.ttt_lora_rank > 0
+
+    def validate(self) -> None:
+        if self.model_dim % self.num_heads:
+            raise ValueError("model_dim must be divisible by num_heads")
+        if self.num_heads % self.num_kv_heads:
+            raise ValueError("num_heads must be divisible by num_kv_heads")
+        if self.head_dim % 2 or self.rope_dims % 2 or self.rope_dims > self.head_dim:
+            raise ValueError("head_dim and rope_dims must be even, rope_dims <= head_dim")
+        for k in (self.model_dim, self.mlp_hidden):
+            if k % 64:
+                raise ValueError("model_dim and mlp hidden must be multiples of 64")
+        if self.head_dim > 128 or self.head_dim % 8:
+            raise ValueError("head_dim must be a multiple of 8 and <= 128")
+        if self.vocab_size < 2:
+            raise ValueError("vocab_size must be >= 2")
+        if self.cdf_mode not in ("fixed", "ref"):
+            raise ValueError("cdf_mode must be 'fixed' or 'ref'")
+        if self.cdf_mode == "fixed" and not (self.vocab_size < (1 << self.cdf_bits) <= (1 << 30)):
+            raise ValueError("cdf_bits must satisfy vocab < 2^cdf_bits <= 2^30")
+        if self.ttt_mlp_lora:
+            raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
+        if self.retrain_mode not in ("lora", "none"):
+            raise ValueError("retrain_mode must be 'lora' or 'none'")
+
+    def to_dict(self) -> dict[str, Any]:
+        return dataclasses.asdict(self)
+
+    def fingerprint(self) -> str:
+        """Hash of every field that changes the bitstream (lockstep key)."""
+        blob = json.dumps(self.to_dict(), sort_keys=True).encode()
+        return hashlib.sha256(blob).hexdigest()[:16]
+
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "ModelConfig":
+        names = {f.name for f in dataclasses.fields(cls)}
+        return cls(**{k: v for k, v in d.items() if k in names})
+
+    @classmethod
+    def from_reference_cfg(cls, ref: Any) -> "ModelConfig":
+        """Map a reference ``XsaTttConfig`` (object or dict) onto this engine."""
+        get = (lambda k, dflt=None: ref.get(k, dflt)) if isinstance(ref, dict) else (
+            lambda k, dflt=None: getattr(ref, k, dflt)
+        )
+        unsupported = {
+            "xsa_last_n": get("xsa_last_n", 0) > 0,
+            "smear_gate_enabled": bool(get("smear_gate_enabled", False)),
+            "sparse_attn_gate_enabled": bool(get("sparse_attn_gate_enabled", False)),
+            "attn_out_gate_enabled": bool(get("attn_out_gate_enabled", False)),
+            "gated_attn_enabled": bool(get("gated_attn_enabled", False)),
+            "num_loops": get("num_loops", 0) > 0,
+            "parallel_start_layer": get("parallel_start_layer", 0) > 0,
+            "asym_logit_rescale": bool(get("asym_logit_rescale", False)),
+            "rope_yarn": bool(get("rope_yarn", False)),
+            "tie_embeddings": not bool(get("tie_embeddings", True)),
+        }
+        bad = [k for k, v in unsupported.items() if v]
+        if bad:
+            raise ValueError(f"reference motifs not supported by this engine: {bad}")
+        out = cls()
+        for f in dataclasses.fields(cls):
+            v = get(f.name, None)
+            if v is not None:
+                setattr(out, f.name, v)
+        return out
+
+
+def c1_config() -> ModelConfig:
+    """CPU plumbing config: 2L/128d/4h, ctx 256, V 4096, rank-4 q/v LoRA."""
+    return ModelConfig(
+        vocab_size=4096, num_layers=2, model_dim=128, num_heads=4, num_kv_heads=4,
+        mlp_mult=4.0, block_size=256, online_retrain_every=4096, seed=0,
+        ttt_lora_rank=4, ttt_lora_lr=1e-3, ttt_k_lora=False, ttt_o_lora=False,
+    )
+
+
+def c3_config() -> ModelConfig:
+    """33M config: 8L/512d/8h (hd 64, MHA), MLP 2048, V 16384, ctx 2048."""
+    return ModelConfig(
+        vocab_size=16384, num_layers=8, model_dim=512, num_heads=8, num_kv_heads=8,
+        mlp_mult=4.0, block_size=2048, online_retrain_every=16384, seed=1337,
+        ttt_lora_rank=8, ttt_lora_lr=1e-3, ttt_k_lora=True, ttt_o_lora=True,
+    )
+
+
+@dataclass
+class RunStats:
+    """Per-run counters reported by the entry points."""
+
+    n_symbols: int = 0
+    payload_bytes: int = 0
+    retrain_count: int = 0
+    segments: list = field(default_factory=list)

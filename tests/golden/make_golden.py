@@ -1,0 +1,274 @@
+"""Generate the golden fixtures by running the altxs reference itself.
+
+Run in a container where the reference checkout is importable:
+
+    ALTXS_REFERENCE=/path/to/altxs python tests/golden/make_golden.py
+
+The fixtures pin the CPU oracle (``oracle/``) to the reference:
+
+* ``coder_probs.npz``  reference ``encode_with_probs`` bitstreams for float
+  probability rows (the reference's own test vector, n=64 V=256 rng(0),
+  plus a peaked V=1024 case);
+* ``coder_cum.npz``    reference coder bitstreams for given integer CDFs
+  (``_scale_cum_np`` replaced by a lookup of the supplied tables), including
+  extreme tables (one dominant symbol, total = 2^30, V = 2);
+* ``model_small.npz``  sliding-window logits from the reference ``GPT``
+  (``prefill_cache`` + ``extend_cache`` with the KV tuples truncated to
+  ``ctx-1`` rows before each extend) for seeded synthetic mixed-bit weights;
+* ``lora_small.npz``   reference ``TTTLoRA`` init and one
+  ``ce_with_lora`` -> backward -> clip -> AdamW step, plus the updated
+  window logits;
+* ``codec_small.json`` checks that the reference ``dequantize_channels``
+  decodes this framework's codec writer output to the same dense weights.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+REF = Path(os.environ.get("ALTXS_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(REPO))
+for p in (REF / "src", REF / "src" / "model"):
+    sys.path.insert(0, str(p))
+
+import arithmetic_coder_lm as acl  # noqa: E402  (reference)
+from hyperflow_distillation.mixed_bit_delta import dequantize_channels  # noqa: E402
+from xsa_ttt.config import XsaTttConfig  # noqa: E402
+from xsa_ttt.model import GPT  # noqa: E402
+from xsa_ttt.ttt_lora import TTTLoRA, _forward_logits_lora, ce_with_lora, make_ttt_optimizer  # noqa: E402
+
+from altxs_b200 import codec as C  # noqa: E402
+from altxs_b200.config import ModelConfig  # noqa: E402
+from oracle import coder as oc  # noqa: E402
+
+SMALL = dict(
+    vocab_size=512, num_layers=3, model_dim=128, num_heads=4, num_kv_heads=2,
+    mlp_mult=4.0, rope_dims=16, block_size=32, online_retrain_every=64, seed=11,
+    ttt_lora_rank=4, ttt_lora_lr=1e-3, ttt_k_lora=True, ttt_o_lora=True,
+)
+
+
+def small_cfg() -> ModelConfig:
+    return ModelConfig(**SMALL)
+
+
+def ref_cfg(cfg: ModelConfig) -> XsaTttConfig:
+    h = XsaTttConfig(seed=cfg.seed)
+    for k in ("vocab_size", "num_layers", "model_dim", "num_heads", "num_kv_heads", "mlp_mult",
+              "rope_base", "rope_dims", "qk_gain_init", "logit_softcap", "ln_scale",
+              "skip_gates_enabled", "block_size", "online_retrain_every", "ttt_lora_rank",
+              "ttt_lora_alpha", "ttt_lora_lr", "ttt_beta1", "ttt_beta2", "ttt_weight_decay",
+              "ttt_k_lora", "ttt_o_lora", "ttt_mlp_lora", "ttt_use_rslora", "grad_clip"):
+        setattr(h, k, getattr(cfg, k))
+    # plain GPT: every reference motif off (the engine's supported subset)
+    h.xsa_last_n = 0
+    h.num_loops = 0
+    h.parallel_start_layer = 0
+    h.smear_gate_enabled = False
+    h.sparse_attn_gate_enabled = False
+    h.attn_out_gate_enabled = False
+    h.gated_attn_enabled = False
+    h.asym_logit_rescale = False
+    h.rope_yarn = False
+    h.tie_embeddings = True
+    h.ttt_warm_start_a = True
+    h.retrain_mode = "lora"
+    h.gradient_checkpointing = False
+    return h
+
+
+def ref_model(cfg: ModelConfig, weights: C.ModelWeights) -> GPT:
+    torch.manual_seed(0)
+    m = GPT(ref_cfg(cfg))
+    sd = m.state_dict()
+    for k, v in weights.dense().items():
+        sd[k] = torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32))
+    m.load_state_dict(sd, strict=True)
+    m.eval()
+    return m
+
+
+# ---------------------------------------------------------------------------
+
+
+def gen_coder_probs() -> None:
+    rng = np.random.default_rng(0)
+    n, v = 64, 256
+    rows = rng.random((n, v)).astype(np.float32)
+    rows /= rows.sum(axis=1, keepdims=True)
+    syms = rng.integers(0, v, size=n, dtype=np.int64)
+    bs_a = acl.encode_with_probs(syms, lambda i, _p: rows[i], alphabet_size=v)
+    rng = np.random.default_rng(1)
+    n2, v2 = 64, 1024
+    lg = rng.normal(0, 4.0, size=(n2, v2))
+    p2 = np.exp(lg - lg.max(axis=1, keepdims=True))
+    p2 = (p2 / p2.sum(axis=1, keepdims=True)).astype(np.float32)
+    p64 = p2.astype(np.float64)
+    syms2 = np.array([rng.choice(v2, p=p64[i] / p64[i].sum()) for i in range(n2)])
+    bs_b = acl.encode_with_probs(syms2, lambda i, _p: p2[i], alphabet_size=v2)
+    np.savez_compressed(
+        HERE / "coder_probs.npz",
+        a_probs=rows, a_syms=syms.astype(np.int32), a_bits=np.frombuffer(bs_a, np.uint8),
+        b_probs=p2, b_syms=syms2.astype(np.int32), b_bits=np.frombuffer(bs_b, np.uint8),
+    )
+
+
+def _ref_encode_cum(cum: np.ndarray, syms: np.ndarray) -> bytes:
+    """Reference coder with the supplied integer tables as its masses."""
+    v = cum.shape[1] - 1
+    orig = acl._scale_cum_np
+    rows = iter(range(cum.shape[0]))
+
+    def fake(_probs, *, alphabet_size):
+        i = next(rows)
+        return cum[i].astype(np.int64), int(cum[i][v])
+
+    acl._scale_cum_np = fake
+    try:
+        carrier = np.zeros(v, dtype=np.float32)
+        return acl.encode_with_probs(syms.astype(np.int64), lambda i, _p: carrier, alphabet_size=v)
+    finally:
+        acl._scale_cum_np = orig
+
+
+def gen_coder_cum() -> None:
+    out = {}
+    rng = np.random.default_rng(2)
+    # (a) framework fixed-point CDFs of random logits, V=512 (tables are
+    # recomputed from the stored logits by the oracle rule)
+    n, v = 96, 512
+    lg = (30 * np.tanh(rng.normal(0, 3.0, size=(n, v)) / 30)).astype(np.float32)
+    cum = oc.cum_from_logits(lg, "fixed", 20)
+    syms = rng.integers(0, v, size=n).astype(np.int32)
+    out["a_logits"], out["a_syms"] = lg, syms
+    out["a_bits"] = np.frombuffer(_ref_encode_cum(cum, syms), np.uint8)
+    # (b) reference-scale rule on the same logits
+    cumr = oc.cum_from_logits(lg, "ref")
+    out["b_bits"] = np.frombuffer(_ref_encode_cum(cumr, syms), np.uint8)
+    # (c) extreme tables: one dominant symbol (long pending runs), total 2^30
+    n3, v3 = 300, 64
+    cum3 = np.zeros((n3, v3 + 1), dtype=np.uint64)
+    syms3 = np.zeros(n3, dtype=np.int32)
+    for i in range(n3):
+        f = np.ones(v3, dtype=np.uint64)
+        dom = int(rng.integers(0, v3))
+        f[dom] = (1 << 30) - (v3 - 1)
+        cum3[i, 1:] = np.cumsum(f)
+        syms3[i] = dom if rng.random() < 0.97 else int(rng.integers(0, v3))
+    out["c_cum"], out["c_syms"] = cum3, syms3
+    out["c_bits"] = np.frombuffer(_ref_encode_cum(cum3, syms3), np.uint8)
+    # (d) binary alphabet, balanced and skewed masses
+    n4 = 400
+    cum4 = np.zeros((n4, 3), dtype=np.uint64)
+    p = rng.integers(1, 1 << 20, size=n4).astype(np.uint64)
+    cum4[:, 1] = p
+    cum4[:, 2] = p + rng.integers(1, 1 << 20, size=n4).astype(np.uint64)
+    syms4 = rng.integers(0, 2, size=n4).astype(np.int32)
+    out["d_cum"], out["d_syms"] = cum4, syms4
+    out["d_bits"] = np.frombuffer(_ref_encode_cum(cum4, syms4), np.uint8)
+    np.savez_compressed(HERE / "coder_cum.npz", **out)
+
+
+def gen_codec() -> dict:
+    cfg = small_cfg()
+    w = C.synth_weights(cfg, seed=7)
+    res = {}
+    for name, mats in C._bank_mats(w).items():
+        bits = np.concatenate([m.bits.reshape(-1) for m in mats])
+        codes = np.concatenate([m.codes.reshape(-1, 64) for m in mats])
+        scales = np.concatenate([m.scales.reshape(-1) for m in mats])
+        packed = {b: C._pack_lsb(codes[bits == b], b).reshape(-1) for b in (2, 3, 4)}
+        cbs = {b: scales[bits == b].reshape(-1, 1).astype(np.float16) for b in (2, 3, 4)}
+        ref_ch = dequantize_channels(bits, cbs, packed, channel_width=64, codebook_mode="symmetric")
+        mine = np.concatenate([m.dequant().reshape(-1, 64) for m in mats])
+        res[name] = bool(np.array_equal(ref_ch, mine))
+    dense = w.dense()
+    h = hashlib.sha256()
+    for k in sorted(dense):
+        h.update(np.ascontiguousarray(dense[k], dtype=np.float32).tobytes())
+    res["dense_sha256"] = h.hexdigest()
+    (HERE / "codec_small.json").write_text(json.dumps(res, indent=1) + "\n")
+    assert all(v for k, v in res.items() if k != "dense_sha256"), res
+    return res
+
+
+def gen_model() -> None:
+    cfg = small_cfg()
+    w = C.synth_weights(cfg, seed=7)
+    m = ref_model(cfg, w)
+    rng = np.random.default_rng(5)
+    n = 80
+    toks = rng.integers(0, cfg.vocab_size, size=n).astype(np.int64)
+    logits = np.zeros((n, cfg.vocab_size), dtype=np.float32)
+    keep = cfg.block_size - 1
+    with torch.no_grad():
+        cache = m.prefill_cache(torch.tensor([[int(toks[0])]]))
+        logits[0] = m.logits_from_cache(cache)[0, -1].numpy()
+        for i in range(1, n):
+            cache.kv_slots = [(k[:, -keep:], v[:, -keep:]) for (k, v) in cache.kv_slots]
+            cache, lg = m.extend_cache(cache, int(toks[i]))
+            logits[i] = lg[0, -1].numpy()
+    np.savez_compressed(HERE / "model_small.npz", tokens=toks.astype(np.int32), logits=logits)
+
+
+def gen_lora() -> None:
+    cfg = small_cfg()
+    w = C.synth_weights(cfg, seed=7)
+    m = ref_model(cfg, w)
+    h = m.cfg
+    for p in m.parameters():
+        p.requires_grad_(False)
+    torch.manual_seed(int(h.seed) ^ 0xA5A51070)
+    lora = TTTLoRA(m, h)
+    init = {k: v.detach().clone().numpy() for k, v in lora.state_dict().items()}
+    opt = make_ttt_optimizer(lora, h)
+    rng = np.random.default_rng(9)
+    arr = rng.integers(0, cfg.vocab_size, size=100).astype(np.int64)
+    end = 64
+    t = min(cfg.block_size, end - 1)
+    s0 = end - t - 1
+    x = torch.tensor(arr[s0: s0 + t])[None]
+    y = torch.tensor(arr[s0 + 1: s0 + 1 + t])[None]
+    losses = []
+    for _ in range(2):  # two boundaries on the same window: A moves on the 2nd
+        opt.zero_grad(set_to_none=True)
+        loss = ce_with_lora(m, x, y, lora)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(lora.parameters(), h.grad_clip)
+        opt.step()
+        losses.append(float(loss.detach()))
+    with torch.no_grad():
+        after = _forward_logits_lora(m, x, lora)[0].numpy()
+    fin = {k: v.detach().clone().numpy() for k, v in lora.state_dict().items()}
+    out = {"arr": arr.astype(np.int32), "end": np.array(end), "losses": np.array(losses),
+           "logits_after": after.astype(np.float32)}
+    out.update({f"init/{k}": v for k, v in init.items()})
+    out.update({f"final/{k}": v for k, v in fin.items()})
+    np.savez_compressed(HERE / "lora_small.npz", **out)
+
+
+def gen_zipf() -> None:
+    from altxs_b200.synth import zipf_markov
+
+    s = zipf_markov(256, 4096, [1, 2, 3])
+    np.savez_compressed(HERE / "zipf_markov.npz", seeds=np.array([1, 2, 3]), streams=s)
+
+
+if __name__ == "__main__":
+    gen_coder_probs()
+    gen_coder_cum()
+    print(gen_codec())
+    gen_model()
+    gen_lora()
+    gen_zipf()
+    for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
+        print(f.name, f.stat().st_size)

@@ -1,0 +1,148 @@
+"""The CPU oracle against golden vectors produced by the altxs reference.
+
+These pin the oracle before it is trusted as the checker of the CUDA path
+(fixtures: ``tests/golden/make_golden.py``).
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from altxs_b200 import codec as C
+from altxs_b200.config import ModelConfig
+from oracle import coder as oc
+from oracle.model import OracleModel, OracleTTT, OracleWeights
+from tests.conftest import GOLDEN
+
+SMALL = dict(
+    vocab_size=512, num_layers=3, model_dim=128, num_heads=4, num_kv_heads=2,
+    mlp_mult=4.0, rope_dims=16, block_size=32, online_retrain_every=64, seed=11,
+    ttt_lora_rank=4, ttt_lora_lr=1e-3, ttt_k_lora=True, ttt_o_lora=True,
+)
+
+
+def _bits(a) -> bytes:
+    return np.asarray(a, dtype=np.uint8).tobytes()
+
+
+def test_coder_probs_matches_reference(golden):
+    g = golden("coder_probs.npz")
+    for c in ("a", "b"):
+        probs, syms, ref = g[f"{c}_probs"], g[f"{c}_syms"], _bits(g[f"{c}_bits"])
+        got = oc.encode_probs(probs, syms)
+        assert got == ref
+        assert np.array_equal(oc.decode_probs(probs, got, len(syms)), syms)
+
+
+def test_coder_cum_matches_reference(golden):
+    g = golden("coder_cum.npz")
+    lg, syms = g["a_logits"], g["a_syms"]
+    for rule, key in (("fixed", "a_bits"), ("ref", "b_bits")):
+        cum = oc.cum_from_logits(lg, rule, 20) if rule == "fixed" else oc.cum_from_logits(lg, "ref")
+        got = oc.encode_cum(cum, syms)
+        assert got == _bits(g[key]), rule
+        assert np.array_equal(oc.decode_cum(cum, got, len(syms)), syms)
+    for c in ("c", "d"):
+        cum, s = g[f"{c}_cum"], g[f"{c}_syms"]
+        got = oc.encode_cum(cum, s)
+        assert got == _bits(g[f"{c}_bits"]), c
+        assert np.array_equal(oc.decode_cum(cum, got, len(s)), s)
+
+
+def test_fixed_cdf_rule_properties():
+    rng = np.random.default_rng(0)
+    lg = (30 * np.tanh(rng.normal(0, 4, size=(50, 300)) / 30)).astype(np.float32)
+    for bits in (16, 20, 24, 30):
+        cum = oc.cum_from_logits(lg, "fixed", bits)
+        f = np.diff(cum.astype(np.int64), axis=1)
+        assert (f >= 1).all()
+        assert (cum[:, -1] <= (1 << bits)).all()
+        # order independence: permuting the alphabet permutes the masses
+        perm = rng.permutation(300)
+        cum_p = oc.cum_from_logits(lg[:, perm], "fixed", bits)
+        assert np.array_equal(np.diff(cum_p.astype(np.int64), axis=1), f[:, perm])
+
+
+def test_codec_golden():
+    res = json.loads((GOLDEN / "codec_small.json").read_text())
+    w = C.synth_weights(ModelConfig(**SMALL), seed=7)
+    import hashlib
+
+    d = w.dense()
+    h = hashlib.sha256()
+    for k in sorted(d):
+        h.update(np.ascontiguousarray(d[k], dtype=np.float32).tobytes())
+    assert h.hexdigest() == res["dense_sha256"]
+    assert all(v for k, v in res.items() if k != "dense_sha256")
+
+
+def test_codec_roundtrip(tmp_path):
+    w = C.synth_weights(ModelConfig(**SMALL), seed=7)
+    p = C.write_codec(w, tmp_path / "m")
+    w2 = C.read_codec(p)
+    a, b = w.dense(), w2.dense()
+    for k in a:
+        assert np.array_equal(np.asarray(a[k]), np.asarray(b[k])), k
+
+
+def test_oracle_step_matches_reference_sliding_window(golden):
+    g = golden("model_small.npz")
+    cfg = ModelConfig(**SMALL)
+    m = OracleModel(OracleWeights.from_model_weights(C.synth_weights(cfg, seed=7)))
+    st = m.new_stream()
+    toks = g["tokens"]
+    ref = g["logits"]
+    got = np.stack([m.step(st, int(t)).numpy() for t in toks])
+    err = np.abs(got - ref).max()
+    assert err < 2e-4, err
+
+
+def test_oracle_lora_matches_reference(golden):
+    g = golden("lora_small.npz")
+    cfg = ModelConfig(**SMALL)
+    m = OracleModel(OracleWeights.from_model_weights(C.synth_weights(cfg, seed=7)))
+    ttt = OracleTTT(m)
+    # init: bit-identical A matrices, in the reference's parameter order
+    names = {"lm": "lm_head_lora"}
+    for i in range(cfg.num_layers):
+        for t in ("q", "k", "v", "o"):
+            names[f"{t}{i}"] = f"{t}_loras.{i}"
+    for ours, ref in names.items():
+        assert torch.equal(ttt.lora.A[ours], torch.from_numpy(g[f"init/{ref}.A"])), ours
+    arr, end = g["arr"], int(g["end"])
+    losses = [ttt.update(arr, end) for _ in range(2)]
+    np.testing.assert_allclose(losses, g["losses"], rtol=1e-5)
+    for ours, ref in names.items():
+        np.testing.assert_allclose(ttt.lora.A[ours].detach().numpy(), g[f"final/{ref}.A"], atol=1e-6)
+        np.testing.assert_allclose(ttt.lora.B[ours].detach().numpy(), g[f"final/{ref}.B"], atol=1e-6)
+    t = min(cfg.block_size, end - 1)
+    x = torch.from_numpy(arr[end - t - 1: end - 1].astype(np.int64))
+    with torch.no_grad():
+        after = m.window_logits(x, ttt.lora).numpy()
+    assert np.abs(after - g["logits_after"]).max() < 2e-4
+
+
+def test_zipf_markov_fixture(golden):
+    from altxs_b200.synth import zipf_markov
+
+    g = golden("zipf_markov.npz")
+    assert np.array_equal(zipf_markov(256, 4096, g["seeds"]), g["streams"])
+
+
+@pytest.mark.parametrize("vocab", [2, 7, 256])
+def test_oracle_coder_roundtrip_edge(vocab):
+    rng = np.random.default_rng(vocab)
+    n = 257
+    lg = rng.normal(0, 6, size=(n, vocab)).astype(np.float32)
+    syms = rng.integers(0, vocab, size=n).astype(np.int32)
+    for rule in ("fixed", "ref"):
+        cum = oc.cum_from_logits(lg, rule, 20)
+        bs = oc.encode_cum(cum, syms)
+        assert np.array_equal(oc.decode_cum(cum, bs, n), syms)
+    # empty input: flush only
+    cum0 = np.zeros((0, vocab + 1), dtype=np.uint64)
+    assert len(oc.encode_cum(cum0, np.zeros(0, np.int32))) == 1
