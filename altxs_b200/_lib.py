@@ -1,0 +1,111 @@
+"""ctypes binding of ``libaltxs_b200.so`` (declarations in include/altxs_b200.h).
+
+The product path has no fallback: if the library is missing or fails to
+load, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libaltxs_b200.so"
+
+ALTXS_OK = 0
+ST_OVERFLOW, ST_BAD_SYMBOL, ST_BAD_TOTAL, ST_NONFINITE, ST_TIMEOUT, ST_BAD_POS = 1, 2, 4, 8, 16, 32
+CDF_FIXED, CDF_REF = 0, 1
+STEP_LOGITS, STEP_ENCODE, STEP_DECODE = 0, 1, 2
+
+EXPORTS = (
+    "altxs_ac_init", "altxs_ac_encode_probs", "altxs_ac_encode_cum", "altxs_ac_flush",
+    "altxs_ac_begin_decode", "altxs_ac_decode_probs", "altxs_ac_decode_cum",
+    "altxs_cdf_from_logits", "altxs_workspace_bytes", "altxs_lora_floats", "altxs_step",
+    "altxs_version",
+)
+
+
+class AcState(C.Structure):
+    _fields_ = [
+        ("low", C.c_uint64), ("high", C.c_uint64), ("pending", C.c_uint64), ("nbits", C.c_uint64),
+        ("value", C.c_uint64), ("bpos", C.c_uint64), ("n_in_bits", C.c_uint64),
+        ("status", C.c_uint32), ("reserved", C.c_uint32),
+    ]
+
+
+class QMat(C.Structure):
+    _fields_ = [
+        ("codes", C.c_void_p), ("row_off8", C.c_void_p), ("gdesc", C.c_void_p),
+        ("lut", C.c_void_p), ("glut", C.c_void_p), ("rows", C.c_int32), ("cols", C.c_int32),
+    ]
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [
+        ("vocab", C.c_int32), ("n_layers", C.c_int32), ("d_model", C.c_int32), ("n_heads", C.c_int32),
+        ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("mlp_hidden", C.c_int32),
+        ("ctx", C.c_int32), ("rope_dims", C.c_int32), ("skip_gates", C.c_int32),
+        ("lora_rank", C.c_int32), ("lora_mask", C.c_int32), ("cdf_mode", C.c_int32),
+        ("cdf_bits", C.c_int32), ("logit_softcap", C.c_float), ("lora_scale", C.c_float),
+    ]
+
+
+class Weights(C.Structure):
+    _fields_ = [
+        ("emb", QMat), ("qkv", QMat), ("o", QMat), ("up", QMat), ("down", QMat),
+        ("q_gain", C.c_void_p), ("attn_scale", C.c_void_p), ("mlp_scale", C.c_void_p),
+        ("resid_mix", C.c_void_p), ("ln_scale", C.c_void_p), ("skip_weights", C.c_void_p),
+        ("skip_gates", C.c_void_p), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("rope_positions", C.c_int64),
+    ]
+
+
+class Batch(C.Structure):
+    _fields_ = [
+        ("n_streams", C.c_int32), ("tok", C.c_void_p), ("pos", C.c_void_p), ("active", C.c_void_p),
+        ("kv", C.c_void_p), ("lora", C.c_void_p), ("lora_stride", C.c_int64), ("ac", C.c_void_p),
+        ("bits", C.c_void_p), ("words_per_stream", C.c_int64), ("sym", C.c_void_p),
+        ("hist", C.c_void_p), ("hist_len", C.c_int32), ("logits_out", C.c_void_p),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    """Load the library (raises if it is not built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m altxs_b200.build` "
+                "(there is no CPU fallback)"
+            )
+        L = C.CDLL(str(LIB_PATH))
+        i64, vp = C.c_int64, C.c_void_p
+        sig = {
+            "altxs_ac_init": (C.c_int, [C.c_int, vp, vp, vp]),
+            "altxs_ac_encode_probs": (C.c_int, [C.c_int, vp, C.c_int, vp, i64, vp, vp, vp, i64, vp]),
+            "altxs_ac_decode_probs": (C.c_int, [C.c_int, vp, C.c_int, vp, i64, vp, vp, vp, i64, vp]),
+            "altxs_ac_encode_cum": (C.c_int, [C.c_int, vp, C.c_int, vp, i64, vp, vp, vp, i64, vp]),
+            "altxs_ac_decode_cum": (C.c_int, [C.c_int, vp, C.c_int, vp, i64, vp, vp, vp, i64, vp]),
+            "altxs_ac_flush": (C.c_int, [C.c_int, vp, vp, vp, i64, vp]),
+            "altxs_ac_begin_decode": (C.c_int, [C.c_int, vp, vp, vp, vp, i64, vp]),
+            "altxs_cdf_from_logits": (C.c_int, [C.c_int, C.c_int, vp, i64, C.c_int, C.c_int, vp, i64, vp]),
+            "altxs_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.c_int]),
+            "altxs_lora_floats": (i64, [C.POINTER(ModelDesc)]),
+            "altxs_step": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int, vp]),
+            "altxs_version": (C.c_char_p, []),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != ALTXS_OK:
+        raise RuntimeError(f"{what} failed with code {rc}")

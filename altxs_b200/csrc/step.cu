@@ -1,0 +1,808 @@
+// One batched symbol step of the GPT model-and-code loop (sm_100a).
+//
+// Per layer (reference Block.forward, altxs src/xsa_ttt/model.py:948-979):
+//   x_in = mix0*x + mix1*x0 ; n = rms(x_in)*ln
+//   q,k,v = W n (+ LoRA) ; q,k = rms per head ; RoPE ; q *= q_gain
+//   y = softmax(q k^T / sqrt(hd)) v over the sliding window ; o = W_o y (+ LoRA(n))
+//   x = x_in + attn_scale*o ; x += mlp_scale * W_down leaky(W_up (rms(x)*ln), .5)^2
+// with U-Net skips before decoder layers (model.py:1395-1436), then tied
+// logits with tanh softcap (model.py:1460-1500), the integer CDF and the coder.
+#include <math.h>
+
+#include "coder.cuh"
+#include "qmm.cuh"
+
+using namespace altxs;
+
+namespace {
+
+constexpr int kSplit = 128;  // keys per attention split (fixed: numerics independent of n)
+constexpr int kAttnThreads = 128;
+constexpr int kCdfThreads = 512;
+
+// KV rows are stored in a 24-bit split format: fp32 rounded to nearest-even
+// at bit 8, the high 16 bits (a bf16) and the next 8 mantissa bits kept in
+// separate parts of the row: [hd x u16 high][hd x u8 low] = 3*hd bytes.
+// fp16 K/V rounding moves the logits by up to ~1e-2 (the q_gain-scaled
+// scores are sensitive to K); 24 bits keep them within ~3e-4 of fp32.
+__device__ __forceinline__ uint32_t round24(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b + 0x7Fu + ((b >> 8) & 1u)) >> 8;  // 24-bit pattern
+}
+__device__ __forceinline__ float from24(uint32_t hi16, uint32_t lo8) {
+    return __uint_as_float((hi16 << 16) | (lo8 << 8));
+}
+__device__ __forceinline__ void store_kv_row(uint8_t *row, int hd, int k, float v) {
+    const uint32_t r = round24(v);
+    reinterpret_cast<uint16_t *>(row)[k] = (uint16_t)(r >> 8);
+    row[2 * hd + k] = (uint8_t)(r & 0xFFu);
+}
+
+struct Dims {
+    int n, V, L, d, H, Hkv, hd, F, ctx, rd, r, nsplit, enc, nskip, qkv_n, kvd;
+    int64_t lora_stride;
+};
+
+// LoRA arena offsets (floats) in TTTLoRA.parameters() order: lm, q_i, v_i, k_i, o_i.
+struct LoraOff {
+    int64_t lmA, lmB, qA, qB, vA, vB, kA, kB, oA, oB;  // per-layer blocks start; stride below
+    int64_t q_stride, v_stride, k_stride, o_stride, total;
+};
+
+__host__ __device__ inline LoraOff lora_offsets(const altxs_model_desc &dsc) {
+    LoraOff o{};
+    const int64_t r = dsc.lora_rank, d = dsc.d_model, kvd = (int64_t)dsc.n_kv_heads * dsc.head_dim;
+    const int64_t V = dsc.vocab, L = dsc.n_layers;
+    int64_t cur = 0;
+    if (r <= 0) return o;
+    o.lmA = cur;
+    cur += r * d;
+    o.lmB = cur;
+    cur += V * r;
+    o.q_stride = r * d + d * r;
+    o.qA = cur;
+    o.qB = cur + r * d;
+    cur += L * o.q_stride;
+    o.v_stride = r * d + kvd * r;
+    o.vA = cur;
+    o.vB = cur + r * d;
+    cur += L * o.v_stride;
+    if (dsc.lora_mask & 2) {
+        o.k_stride = r * d + kvd * r;
+        o.kA = cur;
+        o.kB = cur + r * d;
+        cur += L * o.k_stride;
+    }
+    if (dsc.lora_mask & 8) {
+        o.o_stride = r * d + d * r;
+        o.oA = cur;
+        o.oB = cur + r * d;
+        cur += L * o.o_stride;
+    }
+    o.total = cur;
+    return o;
+}
+
+struct StepCtx {
+    altxs_model_desc dsc;
+    altxs_weights w;
+    altxs_batch b;
+    Dims D;
+    LoraOff lo;
+    // workspace
+    float *x, *x0, *nrm, *nrm2, *skip, *qkv, *q, *part, *y, *ao, *hid, *logits, *lt;
+};
+
+__device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return !b.active || b.active[i]; }
+
+__device__ __forceinline__ float rms_inv(float ss, int n) {
+    const float ms = __fdiv_rn(ss, (float)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, kRmsEps)));
+}
+
+__device__ __forceinline__ float sigmoidf_(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))); }
+
+// torch.lerp(start, end, weight)
+__device__ __forceinline__ float lerp_t(float start, float end, float wgt) {
+    const float diff = __fsub_rn(end, start);
+    return wgt < 0.5f ? __fadd_rn(start, __fmul_rn(wgt, diff))
+                      : __fsub_rn(end, __fmul_rn(diff, __fsub_rn(1.0f, wgt)));
+}
+
+// dequantised W[row][col] (exact fp32 level*scale)
+__device__ __forceinline__ float qmat_elem(const altxs_qmat &W, int row, int col) {
+    const int G = W.cols / 64, g = col >> 6, i = col & 63;
+    const uint32_t d = W.gdesc[(int64_t)row * G + g];
+    const int c = (d >> 16) & 15;
+    const int b = c == 0 ? 0 : c == 1 ? 2 : c == 2 ? 3 : c == 3 ? 4 : 32;
+    if (b == 0) return 0.0f;
+    const uint8_t *gp = W.codes + 8ull * ((uint64_t)W.row_off8[row] + (d >> 20));
+    if (b == 32) return reinterpret_cast<const float *>(gp)[i];
+    const int bp = i * b, wi = bp >> 5, sh = bp & 31;
+    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(gp);
+    uint32_t v = w32[wi] >> sh;
+    if (sh + b > 32) v |= w32[wi + 1] << (32 - sh);
+    const uint32_t code = v & ((1u << b) - 1u);
+    const float s = h2f((uint16_t)(d & 0xffffu));
+    float lev;
+    if (W.lut) lev = h2f(W.lut[16ull * W.glut[(int64_t)row * G + g] + code]);
+    else lev = __fsub_rn((float)code, (float)((1 << b) - 1) * 0.5f);
+    return __fmul_rn(lev, s);
+}
+
+// ---------------------------------------------------------------------------
+
+__global__ void k_embed(StepCtx c) {
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int d = c.D.d, tok = c.b.tok[i];
+    float *x = c.x + (int64_t)i * d, *x0 = c.x0 + (int64_t)i * d;
+    if (tok < 0 || tok >= c.D.V) {
+        for (int k = threadIdx.x; k < d; k += blockDim.x) x[k] = x0[k] = 0.0f;
+        return;
+    }
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float v = qmat_elem(c.w.emb, tok, k);
+        x[k] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
+    const float inv = rms_inv(block_sum(ss, red), d);
+    __syncthreads();
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float v = __fmul_rn(x[k], inv);
+        x[k] = v;
+        x0[k] = v;
+    }
+}
+
+// skip lerp (decoder layers) + resid_mix + rms * ln  -> x (= x_in), nrm
+__global__ void k_prenorm(StepCtx c, int l) {
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int d = c.D.d, n = c.D.n;
+    float *x = c.x + (int64_t)i * d;
+    const float *x0 = c.x0 + (int64_t)i * d;
+    const float *mix = c.w.resid_mix + (int64_t)l * 2 * d;
+    const int j = l - c.D.enc;  // decoder skip index
+    const bool skip = j >= 0 && j < c.D.nskip;
+    const float *sk = skip ? c.skip + ((int64_t)(c.D.enc - 1 - j) * n + i) * d : nullptr;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float xv = x[k];
+        if (skip) {
+            const float scaled = __fmul_rn(c.w.skip_weights[(int64_t)j * d + k], sk[k]);
+            if (c.dsc.skip_gates) xv = lerp_t(scaled, xv, sigmoidf_(c.w.skip_gates[(int64_t)j * d + k]));
+            else xv = __fadd_rn(xv, scaled);
+        }
+        const float xin = __fadd_rn(__fmul_rn(mix[k], xv), __fmul_rn(mix[d + k], x0[k]));
+        x[k] = xin;
+        ss = __fmaf_rn(xin, xin, ss);
+    }
+    const float inv = rms_inv(block_sum(ss, red), d);
+    const float ln = c.w.ln_scale[l];
+    __syncthreads();
+    float *nr = c.nrm + (int64_t)i * d;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) nr[k] = __fmul_rn(__fmul_rn(x[k], inv), ln);
+}
+
+// t[r] = A[r] . x  (warp per rank row; lane-strided sums, fixed tree)
+__device__ inline void lora_t(const float *A, const float *x, int rank, int d, float *t) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int r = wid; r < rank; r += nw) {
+        float s = 0.0f;
+        for (int k = lane; k < d; k += 32) s = __fmaf_rn(x[k], A[(int64_t)r * d + k], s);
+        s = warp_sum(s);
+        if (lane == 0) t[r] = s;
+    }
+}
+// delta = (B[j] . t) * scale
+__device__ __forceinline__ float lora_u(const float *B, const float *t, int rank, int j, float scale) {
+    float u = 0.0f;
+    for (int r = 0; r < rank; ++r) u = __fmaf_rn(B[(int64_t)j * rank + r], t[r], u);
+    return __fmul_rn(u, scale);
+}
+
+// LoRA on q/k/v, per-head RMSNorm, partial RoPE, q_gain, KV ring write.
+__global__ void k_qkv_post(StepCtx c, int l) {
+    extern __shared__ __align__(16) float sm[];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int tok = c.b.tok[i];
+    if (tok < 0) return;
+    const Dims &D = c.D;
+    const int d = D.d, kvd = D.kvd, hd = D.hd, R = D.r;
+    float *v = sm;                   // [qkv_n]
+    float *tq = sm + D.qkv_n;        // [3][R]
+    float *nx = tq + 3 * (R > 0 ? R : 1);  // [d]
+    const float *src = c.qkv + (int64_t)i * D.qkv_n;
+    for (int k = threadIdx.x; k < D.qkv_n; k += blockDim.x) v[k] = src[k];
+    if (R > 0 && c.b.lora) {
+        const float *nr = c.nrm + (int64_t)i * d;
+        for (int k = threadIdx.x; k < d; k += blockDim.x) nx[k] = nr[k];
+        __syncthreads();
+        const float *P = c.b.lora + (int64_t)i * c.b.lora_stride;
+        const LoraOff &o = c.lo;
+        lora_t(P + o.qA + l * o.q_stride, nx, R, d, tq);
+        if (c.dsc.lora_mask & 2) lora_t(P + o.kA + l * o.k_stride, nx, R, d, tq + R);
+        lora_t(P + o.vA + l * o.v_stride, nx, R, d, tq + 2 * R);
+        __syncthreads();
+        const float sc = c.dsc.lora_scale;
+        for (int k = threadIdx.x; k < D.qkv_n; k += blockDim.x) {
+            if (k < d) {
+                v[k] = __fadd_rn(v[k], lora_u(P + o.qB + l * o.q_stride, tq, R, k, sc));
+            } else if (k < d + kvd) {
+                if (c.dsc.lora_mask & 2)
+                    v[k] = __fadd_rn(v[k], lora_u(P + o.kB + l * o.k_stride, tq + R, R, k - d, sc));
+            } else {
+                v[k] = __fadd_rn(v[k], lora_u(P + o.vB + l * o.v_stride, tq + 2 * R, R, k - d - kvd, sc));
+            }
+        }
+    }
+    __syncthreads();
+    const int64_t pos = c.b.pos[i];
+    if (pos < 0 || pos >= c.w.rope_positions) {
+        if (threadIdx.x == 0) atomicOr(&c.b.ac[i].status, ALTXS_ST_BAD_POS);
+        return;
+    }
+    const int slot = (int)(pos % D.ctx);
+    const int half = D.rd / 2;
+    const float *cs = c.w.rope_cos + pos * half, *sn = c.w.rope_sin + pos * half;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    // heads: 0..H-1 q, H..H+Hkv-1 k (normed + rope), H+Hkv.. v (copy)
+    const int nhead = D.H + 2 * D.Hkv;
+    const int64_t rb = 3 * (int64_t)hd;  // bytes per KV row
+    uint8_t *kvbase = c.b.kv + ((int64_t)i * D.L + l) * 2 * D.Hkv * D.ctx * rb;
+    for (int h = wid; h < nhead; h += nw) {
+        float *e = v + h * hd;  // q heads, then k heads, then v heads are contiguous
+        if (h >= D.H + D.Hkv) {
+            const int kvh = h - D.H - D.Hkv;
+            uint8_t *dst = kvbase + (((int64_t)D.Hkv + kvh) * D.ctx + slot) * rb;
+            for (int k = lane; k < hd; k += 32) store_kv_row(dst, hd, k, e[k]);
+            continue;
+        }
+        float ss = 0.0f;
+        for (int k = lane; k < hd; k += 32) ss = __fmaf_rn(e[k], e[k], ss);
+        const float inv = rms_inv(warp_sum(ss), hd);
+        float outv[4];  // hd <= 128 -> <= 4 per lane
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = lane + 32 * u;
+            if (k >= hd) break;
+            const float a = __fmul_rn(e[k], inv);
+            float r = a;
+            if (k < D.rd) {
+                if (k < half) {
+                    const float b2 = __fmul_rn(e[k + half], inv);
+                    r = __fadd_rn(__fmul_rn(a, cs[k]), __fmul_rn(b2, sn[k]));
+                } else {
+                    const float a1 = __fmul_rn(e[k - half], inv);
+                    r = __fadd_rn(__fmul_rn(a1, -sn[k - half]), __fmul_rn(a, cs[k - half]));
+                }
+            }
+            outv[u] = r;
+        }
+        __syncwarp();
+        if (h < D.H) {
+            const float g = c.w.q_gain[(int64_t)l * D.H + h];
+            float *qd = c.q + ((int64_t)i * D.H + h) * hd;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = lane + 32 * u;
+                if (k < hd) qd[k] = __fmul_rn(outv[u], g);
+            }
+        } else {
+            const int kvh = h - D.H;
+            uint8_t *dst = kvbase + ((int64_t)kvh * D.ctx + slot) * rb;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = lane + 32 * u;
+                if (k < hd) store_kv_row(dst, hd, k, outv[u]);
+            }
+        }
+    }
+}
+
+// Split-K decode attention over the sliding window.  One CTA per
+// (split, kv head, stream): the split's K and V rows (contiguous fp16) are
+// brought into shared memory with two TMA bulk copies, then scores, softmax
+// partial (max, sum) and the weighted V sum for each query head of the group.
+__global__ void __launch_bounds__(kAttnThreads) k_attn_partial(StepCtx c, int l) {
+    extern __shared__ __align__(128) unsigned char smraw[];
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ float red[32];
+    const Dims &D = c.D;
+    const int s = blockIdx.x, kvh = blockIdx.y, i = blockIdx.z;
+    const int hd = D.hd, G = D.H / D.Hkv;
+    float *part_base = c.part + (((int64_t)i * D.H + (int64_t)kvh * G) * D.nsplit + s) * (hd + 2);
+    if (!row_active(c.b, i) || c.b.tok[i] < 0) return;
+    const int64_t pos = c.b.pos[i];
+    const int npos = (int)(pos + 1 < (int64_t)D.ctx ? pos + 1 : (int64_t)D.ctx);
+    const int k0 = s * kSplit;
+    const int nvalid = max(0, min(min(kSplit, D.ctx - k0), npos - k0));
+    if (nvalid == 0) {
+        for (int g = 0; g < G; ++g) {
+            float *pp = part_base + (int64_t)g * D.nsplit * (hd + 2);
+            for (int k = threadIdx.x; k < hd; k += blockDim.x) pp[k] = 0.0f;
+            if (threadIdx.x == 0) {
+                pp[hd] = -INFINITY;
+                pp[hd + 1] = 0.0f;
+            }
+        }
+        return;
+    }
+    const int rb = 3 * hd;  // bytes per KV row (24-bit split format)
+    uint8_t *Ks = smraw;
+    uint8_t *Vs = Ks + (int64_t)kSplit * rb;
+    float *sc = reinterpret_cast<float *>(Vs + (int64_t)kSplit * rb);  // [G][kSplit]
+    float *accs = sc + (int64_t)G * kSplit;                            // [warps][G][hd]
+    const uint8_t *kvb = c.b.kv + ((int64_t)i * D.L + l) * 2 * D.Hkv * D.ctx * rb;
+    const uint8_t *Kg = kvb + ((int64_t)kvh * D.ctx + k0) * rb;
+    const uint8_t *Vg = kvb + ((int64_t)(D.Hkv + kvh) * D.ctx + k0) * rb;
+    const uint32_t bytes = (uint32_t)nvalid * rb;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(&bar[0], bytes);
+        bulk_g2s(Ks, Kg, bytes, &bar[0]);
+        mbar_expect_tx(&bar[1], bytes);
+        bulk_g2s(Vs, Vg, bytes, &bar[1]);
+    }
+    // q for the group's heads (registers): lane owns dims [ds*8, ds*8+8)
+    const int lpk = hd / 8, kpp = 32 / lpk;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int ds = lane % lpk, kl = lane / lpk;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+    const bool ok0 = mbar_wait_bounded(&bar[0], 0, kWaitLimit);
+    if (!__syncthreads_and(ok0)) {
+        if (threadIdx.x == 0) atomicOr(&c.b.ac[i].status, ALTXS_ST_TIMEOUT);
+        mbar_wait_bounded(&bar[0], 0, kWaitLimit);
+        mbar_wait_bounded(&bar[1], 0, kWaitLimit);
+        return;
+    }
+    for (int g = 0; g < G; ++g) {
+        const float *qh = c.q + ((int64_t)i * D.H + kvh * G + g) * hd + ds * 8;
+        float qv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) qv[u] = qh[u];
+        for (int j0 = 0; j0 < nvalid; j0 += nw * kpp) {
+            const int j = j0 + wid * kpp + kl;
+            float dot = 0.0f;
+            if (j < nvalid) {
+                const uint8_t *row = Ks + (int64_t)j * rb;
+                const uint4 hi = *reinterpret_cast<const uint4 *>(row + ds * 16);
+                const uint2 lo = *reinterpret_cast<const uint2 *>(row + 2 * hd + ds * 8);
+                const uint32_t h[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t l8 = (u < 2 ? lo.x : lo.y) >> (16 * (u & 1));
+                    const float f0 = from24(h[u] & 0xFFFFu, l8 & 0xFFu);
+                    const float f1 = from24(h[u] >> 16, (l8 >> 8) & 0xFFu);
+                    dot = __fmaf_rn(qv[2 * u], f0, dot);
+                    dot = __fmaf_rn(qv[2 * u + 1], f1, dot);
+                }
+            }
+            for (int o = 1; o < lpk; o <<= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, o));
+            if (j < nvalid && ds == 0) sc[g * kSplit + j] = __fmul_rn(dot, scale);
+        }
+    }
+    __syncthreads();
+    float mx[4], lsum[4];  // G <= 4 query heads per kv head
+    for (int g = 0; g < G; ++g) {
+        float m = -INFINITY;
+        for (int j = threadIdx.x; j < nvalid; j += blockDim.x) m = fmaxf(m, sc[g * kSplit + j]);
+        m = block_max(m, red);
+        __syncthreads();
+        float l = 0.0f;
+        for (int j = threadIdx.x; j < nvalid; j += blockDim.x) {
+            const float e = expf(__fsub_rn(sc[g * kSplit + j], m));
+            sc[g * kSplit + j] = e;
+            l = __fadd_rn(l, e);
+        }
+        l = block_sum(l, red);
+        mx[g] = m;
+        lsum[g] = l;
+    }
+    __syncthreads();
+    const bool ok1 = mbar_wait_bounded(&bar[1], 0, kWaitLimit);
+    if (!__syncthreads_and(ok1)) {
+        if (threadIdx.x == 0) atomicOr(&c.b.ac[i].status, ALTXS_ST_TIMEOUT);
+        mbar_wait_bounded(&bar[1], 0, kWaitLimit);
+        return;
+    }
+    for (int g = 0; g < G; ++g) {
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
+        for (int j0 = 0; j0 < nvalid; j0 += nw * kpp) {
+            const int j = j0 + wid * kpp + kl;
+            if (j < nvalid) {
+                const float e = sc[g * kSplit + j];
+                const uint8_t *row = Vs + (int64_t)j * rb;
+                const uint4 hi = *reinterpret_cast<const uint4 *>(row + ds * 16);
+                const uint2 lo = *reinterpret_cast<const uint2 *>(row + 2 * hd + ds * 8);
+                const uint32_t h[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t l8 = (u < 2 ? lo.x : lo.y) >> (16 * (u & 1));
+                    acc[2 * u] = __fmaf_rn(e, from24(h[u] & 0xFFFFu, l8 & 0xFFu), acc[2 * u]);
+                    acc[2 * u + 1] = __fmaf_rn(e, from24(h[u] >> 16, (l8 >> 8) & 0xFFu), acc[2 * u + 1]);
+                }
+            }
+        }
+        // reduce lanes holding the same dims (xor over the key-lane bits)
+        for (int o = lpk; o < 32; o <<= 1)
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[u] = __fadd_rn(acc[u], __shfl_xor_sync(0xffffffffu, acc[u], o));
+        if (kl == 0) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) accs[((int64_t)wid * G + g) * hd + ds * 8 + u] = acc[u];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+        const int g = idx / hd, k = idx - g * hd;
+        float a = 0.0f;
+        for (int w2 = 0; w2 < nw; ++w2) a = __fadd_rn(a, accs[((int64_t)w2 * G + g) * hd + k]);
+        part_base[(int64_t)g * D.nsplit * (hd + 2) + k] = a;
+    }
+    if (threadIdx.x < G) {
+        float *pp = part_base + (int64_t)threadIdx.x * D.nsplit * (hd + 2);
+        pp[hd] = mx[threadIdx.x];
+        pp[hd + 1] = lsum[threadIdx.x];
+    }
+}
+
+// Fixed-order merge of the split partials -> y [n][H*hd]
+__global__ void k_attn_merge(StepCtx c) {
+    const Dims &D = c.D;
+    const int i = blockIdx.x / D.H, h = blockIdx.x % D.H, k = threadIdx.x;
+    if (!row_active(c.b, i) || c.b.tok[i] < 0 || k >= D.hd) return;
+    const float *pp = c.part + ((int64_t)i * D.H + h) * D.nsplit * (D.hd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < D.nsplit; ++s)
+        if (pp[s * (D.hd + 2) + D.hd + 1] > 0.0f) M = fmaxf(M, pp[s * (D.hd + 2) + D.hd]);
+    float l = 0.0f, a = 0.0f;
+    for (int s = 0; s < D.nsplit; ++s) {
+        const float *q = pp + s * (D.hd + 2);
+        if (q[D.hd + 1] > 0.0f) {
+            const float f = expf(__fsub_rn(q[D.hd], M));
+            l = __fmaf_rn(q[D.hd + 1], f, l);
+            a = __fmaf_rn(q[k], f, a);
+        }
+    }
+    c.y[(int64_t)i * D.d + h * D.hd + k] = l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
+}
+
+// o-LoRA on the pre-attention normed input, residual, rms*ln for the MLP.
+__global__ void k_post_attn(StepCtx c, int l) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int d = c.D.d, R = c.D.r;
+    float *x = c.x + (int64_t)i * d;
+    const float *ao = c.ao + (int64_t)i * d;
+    const float *as = c.w.attn_scale + (int64_t)l * d;
+    float *t = sm;  // [R]
+    const bool has_o = R > 0 && c.b.lora && (c.dsc.lora_mask & 8);
+    const float *P = has_o ? c.b.lora + (int64_t)i * c.b.lora_stride : nullptr;
+    if (has_o) lora_t(P + c.lo.oA + l * c.lo.o_stride, c.nrm + (int64_t)i * d, R, d, t);
+    __syncthreads();
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float o = ao[k];
+        if (has_o) o = __fadd_rn(o, lora_u(P + c.lo.oB + l * c.lo.o_stride, t, R, k, c.dsc.lora_scale));
+        const float xv = __fadd_rn(x[k], __fmul_rn(as[k], o));
+        x[k] = xv;
+        ss = __fmaf_rn(xv, xv, ss);
+    }
+    const float inv = rms_inv(block_sum(ss, red), d);
+    const float ln = c.w.ln_scale[l];
+    __syncthreads();
+    float *nr = c.nrm2 + (int64_t)i * d;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) nr[k] = __fmul_rn(__fmul_rn(x[k], inv), ln);
+}
+
+// final RMSNorm (+ lm_head LoRA t)
+__global__ void k_final(StepCtx c) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float red[32];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int d = c.D.d, R = c.D.r;
+    const float *x = c.x + (int64_t)i * d;
+    float *nr = c.nrm + (int64_t)i * d;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) ss = __fmaf_rn(x[k], x[k], ss);
+    const float inv = rms_inv(block_sum(ss, red), d);
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float v = __fmul_rn(x[k], inv);
+        nr[k] = v;
+        sm[k] = v;
+    }
+    __syncthreads();
+    if (R > 0 && c.b.lora && (c.dsc.lora_mask & 16)) {
+        const float *P = c.b.lora + (int64_t)i * c.b.lora_stride;
+        lora_t(P + c.lo.lmA, sm, R, d, c.lt + (int64_t)i * R);
+    }
+}
+
+// logits (+ lm LoRA) -> softcap -> integer CDF -> encode / decode
+__global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
+    extern __shared__ __align__(16) float buf[];  // [V]
+    __shared__ CdfScratch sc;
+    __shared__ float tl[64];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const Dims &D = c.D;
+    const int V = D.V, R = D.r, tok = c.b.tok[i];
+    const float cap = c.dsc.logit_softcap;
+    const bool has_lm = R > 0 && c.b.lora && (c.dsc.lora_mask & 16) && tok >= 0;
+    const float *P = has_lm ? c.b.lora + (int64_t)i * c.b.lora_stride + c.lo.lmB : nullptr;
+    if (has_lm && threadIdx.x < R) tl[threadIdx.x] = c.lt[(int64_t)i * R + threadIdx.x];
+    __syncthreads();
+    const float *raw = c.logits + (int64_t)i * V;
+    for (int k = threadIdx.x; k < V; k += blockDim.x) {
+        float lg = 0.0f;
+        if (tok >= 0) {
+            float v = raw[k];
+            if (has_lm) v = __fadd_rn(v, lora_u(P, tl, R, k, c.dsc.lora_scale));
+            lg = __fmul_rn(cap, tanhf(__fdiv_rn(v, cap)));
+        }
+        buf[k] = lg;
+        if (c.b.logits_out) c.b.logits_out[(int64_t)i * V + k] = lg;
+    }
+    __syncthreads();
+    if (mode == ALTXS_STEP_LOGITS) return;
+    uint32_t status = 0;
+    const uint64_t total = logits_to_masses(buf, V, c.dsc.cdf_mode, c.dsc.cdf_bits, sc, status);
+    const uint32_t *m = reinterpret_cast<const uint32_t *>(buf);
+    altxs_ac_state st = c.b.ac[i];
+    uint32_t *bits = c.b.bits + (int64_t)i * c.b.words_per_stream;
+    int sym;
+    if (mode == ALTXS_STEP_ENCODE) {
+        sym = c.b.sym[i];
+        if (sym < 0 || sym >= V) {
+            if (threadIdx.x == 0) {
+                st.status |= ALTXS_ST_BAD_SYMBOL | status;
+                c.b.ac[i] = st;
+            }
+            return;
+        }
+        const uint64_t sl = mass_below(m, V, sym, sc);
+        if (threadIdx.x == 0) {
+            if (total == 0 || total > kQuarter) {
+                st.status |= ALTXS_ST_BAD_TOTAL;
+            } else {
+                BitWriter bw;
+                bw.begin(bits, c.b.words_per_stream, st.nbits);
+                enc_symbol(st, bw, sl, sl + m[sym], total);
+                bw.end();
+                st.nbits = bw.nbits;
+                st.status |= bw.status;
+            }
+        }
+    } else {
+        if (threadIdx.x == 0) sc.bcast[2] = dec_offset(st, total);
+        __syncthreads();
+        const uint64_t off = sc.bcast[2];
+        uint64_t sl, sh;
+        find_symbol(m, V, off, sc, sym, sl, sh);
+        if (threadIdx.x == 0) {
+            dec_symbol(st, bits, sl, sh, total);
+            c.b.sym[i] = sym;
+        }
+    }
+    if (threadIdx.x == 0) {
+        st.status |= status;
+        c.b.ac[i] = st;
+        int64_t p = c.b.pos[i];
+        if (tok >= 0) p += 1;
+        c.b.pos[i] = p;
+        c.b.tok[i] = sym;
+        if (c.b.hist) c.b.hist[(int64_t)i * c.b.hist_len + (p % c.b.hist_len)] = sym;
+    }
+}
+
+// ---------------------------------------------------------------------------
+
+inline int64_t ws_size(const Dims &D) {
+    auto A = [](int64_t x) { return align_up(x * 4, 256); };
+    int64_t s = 0;
+    s += 4 * A((int64_t)D.n * D.d);                   // x, x0, nrm, nrm2
+    s += A((int64_t)D.nskip * D.n * D.d);             // skip
+    s += A((int64_t)D.n * D.qkv_n);                   // qkv
+    s += A((int64_t)D.n * D.H * D.hd);                // q
+    s += A((int64_t)D.n * D.H * D.nsplit * (D.hd + 2));  // attention partials
+    s += 2 * A((int64_t)D.n * D.d);                   // y, ao
+    s += A((int64_t)D.n * D.F);                       // hid
+    s += A((int64_t)D.n * D.V);                       // logits
+    s += A((int64_t)D.n * (D.r > 0 ? D.r : 1));       // lm LoRA t
+    return s;
+}
+
+int fill_dims(const altxs_model_desc *dsc, int n, Dims &D) {
+    if (!dsc || n < 0) return ALTXS_EINVAL;
+    D.n = n;
+    D.V = dsc->vocab;
+    D.L = dsc->n_layers;
+    D.d = dsc->d_model;
+    D.H = dsc->n_heads;
+    D.Hkv = dsc->n_kv_heads;
+    D.hd = dsc->head_dim;
+    D.F = dsc->mlp_hidden;
+    D.ctx = dsc->ctx;
+    D.rd = dsc->rope_dims;
+    D.r = dsc->lora_rank;
+    if (D.V < 2 || D.L < 1 || D.d % 64 || D.F % 64 || D.H < 1 || D.Hkv < 1 || D.H % D.Hkv) return ALTXS_EINVAL;
+    if (D.hd * D.H != D.d || D.hd % 16 || D.hd > 128 || 32 % (D.hd / 8) || D.H / D.Hkv > 4) return ALTXS_ENOTSUP;
+    if (D.rd % 2 || D.rd > D.hd || D.ctx < 1 || D.r < 0 || D.r > 64) return ALTXS_EINVAL;
+    if ((int64_t)D.V * 4 > 160 * 1024) return ALTXS_ENOTSUP;
+    if (dsc->cdf_mode != ALTXS_CDF_FIXED && dsc->cdf_mode != ALTXS_CDF_REF) return ALTXS_EINVAL;
+    if (dsc->cdf_mode == ALTXS_CDF_FIXED && (dsc->cdf_bits > 30 || (1ll << dsc->cdf_bits) <= D.V))
+        return ALTXS_EINVAL;
+    D.kvd = D.Hkv * D.hd;
+    D.qkv_n = D.d + 2 * D.kvd;
+    D.nsplit = (D.ctx + kSplit - 1) / kSplit;
+    D.enc = D.L / 2;
+    D.nskip = D.enc < D.L - D.enc ? D.enc : D.L - D.enc;
+    return ALTXS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t altxs_workspace_bytes(const altxs_model_desc *desc, int n_streams) {
+    Dims D{};
+    if (fill_dims(desc, n_streams, D) != ALTXS_OK) return -1;
+    return ws_size(D);
+}
+
+int64_t altxs_lora_floats(const altxs_model_desc *desc) {
+    if (!desc) return -1;
+    return lora_offsets(*desc).total;
+}
+
+int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b, int mode,
+               altxs_stream_t stream) {
+    if (!desc || !w || !b) return ALTXS_EINVAL;
+    if (mode < ALTXS_STEP_LOGITS || mode > ALTXS_STEP_DECODE) return ALTXS_EINVAL;
+    StepCtx c{};
+    c.dsc = *desc;
+    c.w = *w;
+    c.b = *b;
+    int rc = fill_dims(desc, b->n_streams, c.D);
+    if (rc) return rc;
+    Dims &D = c.D;
+    if (D.n == 0) return ALTXS_OK;
+    if (!b->tok || !b->pos || !b->kv || !b->workspace || b->workspace_bytes < ws_size(D)) return ALTXS_EINVAL;
+    if (mode != ALTXS_STEP_LOGITS && (!b->ac || !b->bits || !b->sym || b->words_per_stream < 1))
+        return ALTXS_EINVAL;
+    if (b->hist && b->hist_len < 1) return ALTXS_EINVAL;
+    if (reinterpret_cast<uintptr_t>(b->kv) & 15) return ALTXS_EINVAL;
+    if (w->emb.rows != D.V || w->emb.cols != D.d || w->qkv.rows != D.L * D.qkv_n || w->qkv.cols != D.d ||
+        w->o.rows != D.L * D.d || w->o.cols != D.d || w->up.rows != D.L * D.F || w->up.cols != D.d ||
+        w->down.rows != D.L * D.d || w->down.cols != D.F)
+        return ALTXS_EINVAL;
+    c.lo = lora_offsets(*desc);
+    if (D.r > 0 && b->lora && b->lora_stride < c.lo.total) return ALTXS_EINVAL;
+    D.lora_stride = b->lora_stride;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // carve workspace
+    unsigned char *p = static_cast<unsigned char *>(b->workspace);
+    auto take = [&](int64_t nfl) {
+        float *r = reinterpret_cast<float *>(p);
+        p += align_up(nfl * 4, 256);
+        return r;
+    };
+    c.x = take((int64_t)D.n * D.d);
+    c.x0 = take((int64_t)D.n * D.d);
+    c.nrm = take((int64_t)D.n * D.d);
+    c.nrm2 = take((int64_t)D.n * D.d);
+    c.skip = take((int64_t)D.nskip * D.n * D.d);
+    c.qkv = take((int64_t)D.n * D.qkv_n);
+    c.q = take((int64_t)D.n * D.H * D.hd);
+    c.part = take((int64_t)D.n * D.H * D.nsplit * (D.hd + 2));
+    c.y = take((int64_t)D.n * D.d);
+    c.ao = take((int64_t)D.n * D.d);
+    c.hid = take((int64_t)D.n * D.F);
+    c.logits = take((int64_t)D.n * D.V);
+    c.lt = take((int64_t)D.n * (D.r > 0 ? D.r : 1));
+
+    k_embed<<<D.n, 128, 0, st>>>(c);
+    ALTXS_LAUNCH_CHECK();
+    const int G = D.H / D.Hkv;
+    const size_t attn_sm = (size_t)2 * kSplit * 3 * D.hd + (size_t)G * kSplit * 4 + (size_t)(kAttnThreads / 32) * G * D.hd * 4;
+    {
+        static bool attr_done[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+            cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            cudaFuncSetAttribute(k_cdf_code, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            if (dev >= 0 && dev < 64) attr_done[dev] = true;
+        }
+    }
+    const size_t qkv_sm = ((size_t)D.qkv_n + 3 * (D.r > 0 ? D.r : 1) + D.d) * 4;
+    for (int l = 0; l < D.L; ++l) {
+        k_prenorm<<<D.n, 128, 0, st>>>(c, l);
+        ALTXS_LAUNCH_CHECK();
+        QmmArgs a{};
+        a.X = c.nrm;
+        a.ldx = D.d;
+        a.M = D.n;
+        a.W = w->qkv;
+        a.row0 = l * D.qkv_n;
+        a.N = D.qkv_n;
+        a.K = D.d;
+        a.Y = c.qkv;
+        a.ldy = D.qkv_n;
+        a.epi = kEpiStore;
+        if ((rc = launch_qmm(a, st))) return rc;
+        k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, l);
+        ALTXS_LAUNCH_CHECK();
+        k_attn_partial<<<dim3(D.nsplit, D.Hkv, D.n), kAttnThreads, attn_sm, st>>>(c, l);
+        ALTXS_LAUNCH_CHECK();
+        k_attn_merge<<<D.n * D.H, D.hd, 0, st>>>(c);
+        ALTXS_LAUNCH_CHECK();
+        a.X = c.y;
+        a.W = w->o;
+        a.row0 = l * D.d;
+        a.N = D.d;
+        a.Y = c.ao;
+        a.ldy = D.d;
+        if ((rc = launch_qmm(a, st))) return rc;
+        k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l);
+        ALTXS_LAUNCH_CHECK();
+        a.X = c.nrm2;
+        a.W = w->up;
+        a.row0 = l * D.F;
+        a.N = D.F;
+        a.Y = c.hid;
+        a.ldy = D.F;
+        a.epi = kEpiLeaky2;
+        if ((rc = launch_qmm(a, st))) return rc;
+        a.X = c.hid;
+        a.ldx = D.F;
+        a.W = w->down;
+        a.row0 = l * D.d;
+        a.N = D.d;
+        a.K = D.F;
+        a.Y = c.x;
+        a.ldy = D.d;
+        a.epi = kEpiResid;
+        a.R = c.x;
+        a.ldr = D.d;
+        a.colscale = w->mlp_scale + (int64_t)l * D.d;
+        a.Y2 = l < D.enc ? c.skip + (int64_t)l * D.n * D.d : nullptr;
+        a.ldy2 = D.d;
+        if ((rc = launch_qmm(a, st))) return rc;
+    }
+    k_final<<<D.n, 128, D.d * 4, st>>>(c);
+    ALTXS_LAUNCH_CHECK();
+    QmmArgs a{};
+    a.X = c.nrm;
+    a.ldx = D.d;
+    a.M = D.n;
+    a.W = w->emb;
+    a.row0 = 0;
+    a.N = D.V;
+    a.K = D.d;
+    a.Y = c.logits;
+    a.ldy = D.V;
+    a.epi = kEpiStore;
+    if ((rc = launch_qmm(a, st))) return rc;
+    k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode);
+    ALTXS_LAUNCH_CHECK();
+    return ALTXS_OK;
+}
+
+}  // extern "C"

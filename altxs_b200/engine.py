@@ -1,0 +1,388 @@
+"""Host side of the B200 model-and-code loop.
+
+``DeviceModel`` uploads one model (packed mixed-bit weights + small params +
+RoPE tables) to a GPU.  ``StreamBatch`` owns the device state of n
+independent symbol streams (KV rings, LoRA adapters, coder states, bit
+buffers) and drives the C-ABI step.  ``Engine`` runs whole streams: symbols
+are coded in segments of ``online_retrain_every`` symbols, each segment
+flushed separately and framed as ``<u64 LE len><segment bytes>`` like the
+reference (altxs src/xsa_ttt/incremental.py:1721-1722, 1782-1796); the
+test-time LoRA update runs at every segment boundary on both sides.
+
+Stream semantics (identical on encode and decode): symbol 0 is coded with the
+uniform distribution (reference ``uniform_probs``, compress.py:53-56);
+symbol t >= 1 is coded with the model's distribution after consuming symbols
+0..t-1, attending over the last ``block_size`` positions.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+import struct
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .codec import ModelWeights, PackedMatrix
+from .config import ModelConfig
+from .lora import init_lora_A, lora_shapes, rope_tables
+
+ST_NAMES = {1: "bit buffer overflow", 2: "bad symbol", 4: "bad CDF total", 8: "non-finite logits",
+            16: "device wait timeout", 32: "position beyond the RoPE table"}
+
+
+def _i32(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a).view(np.int32)
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def lora_mask(cfg: ModelConfig) -> int:
+    if not cfg.lora_enabled:
+        return 0
+    m = 1 | 4 | 16  # q, v, lm_head always (reference TTTLoRA)
+    if cfg.ttt_k_lora:
+        m |= 2
+    if cfg.ttt_o_lora:
+        m |= 8
+    return m
+
+
+class DeviceModel:
+    """One model resident on one GPU."""
+
+    def __init__(self, weights: ModelWeights, device: torch.device | str, *, rope_positions: int = 1 << 16):
+        self.cfg = cfg = weights.cfg
+        cfg.validate()
+        self.device = device = torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("the B200 engine needs a CUDA device (there is no CPU path)")
+        _lib.lib()
+        self._keep: list[torch.Tensor] = []
+        packed = weights.packed()
+        self.weight_bytes = sum(p.nbytes for p in packed.values())
+        self.q = {k: self._qmat(v) for k, v in packed.items()}
+        s = weights.small
+        L = cfg.num_layers
+        f32 = lambda a: self._up(np.ascontiguousarray(a, dtype=np.float32))  # noqa: E731
+        self.small = {
+            "q_gain": f32(s["q_gain"]),
+            "attn_scale": f32(s["attn_scale"]),
+            "mlp_scale": f32(s["mlp_scale"]),
+            "resid_mix": f32(s["resid_mix"]),
+            "ln_scale": f32(
+                np.array([1.0 / math.sqrt(i + 1) if cfg.ln_scale else 1.0 for i in range(L)], dtype=np.float32)
+            ),
+            "skip_weights": f32(s["skip_weights"] if s["skip_weights"].size else np.zeros((1, cfg.model_dim))),
+            "skip_gates": f32(s["skip_gates"] if s["skip_gates"].size else np.zeros((1, cfg.model_dim))),
+        }
+        self.rope_positions = 0
+        self.ensure_rope(rope_positions)
+        self.desc = _lib.ModelDesc(
+            vocab=cfg.vocab_size, n_layers=L, d_model=cfg.model_dim, n_heads=cfg.num_heads,
+            n_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, mlp_hidden=cfg.mlp_hidden,
+            ctx=cfg.ctx, rope_dims=cfg.rope_dims, skip_gates=int(cfg.skip_gates_enabled),
+            lora_rank=cfg.ttt_lora_rank if cfg.lora_enabled else 0, lora_mask=lora_mask(cfg),
+            cdf_mode=_lib.CDF_FIXED if cfg.cdf_mode == "fixed" else _lib.CDF_REF, cdf_bits=cfg.cdf_bits,
+            logit_softcap=cfg.logit_softcap, lora_scale=cfg.lora_scale if cfg.lora_enabled else 0.0,
+        )
+        self.lora_floats = int(_lib.lib().altxs_lora_floats(C.byref(self.desc)))
+
+    def _up(self, a: np.ndarray) -> torch.Tensor:
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+        self._keep.append(t)
+        return t
+
+    def _qmat(self, p: PackedMatrix) -> _lib.QMat:
+        codes = self._up(p.codes)
+        ro = self._up(_i32(p.row_off8))
+        gd = self._up(_i32(p.gdesc))
+        lut = self._up(p.lut.view(np.int16)) if p.lut is not None else None
+        glut = self._up(_i32(p.glut)) if p.glut is not None else None
+        return _lib.QMat(
+            codes=codes.data_ptr(), row_off8=ro.data_ptr(), gdesc=gd.data_ptr(),
+            lut=lut.data_ptr() if lut is not None else None,
+            glut=glut.data_ptr() if glut is not None else None,
+            rows=p.rows, cols=p.cols,
+        )
+
+    def ensure_rope(self, n_pos: int) -> None:
+        """RoPE tables must cover every absolute position a stream reaches."""
+        if n_pos <= self.rope_positions:
+            return
+        n = 1 << max(12, (int(n_pos) - 1).bit_length())
+        cos, sin = rope_tables(self.cfg, n)
+        self.rope_cos = self._up(cos)
+        self.rope_sin = self._up(sin)
+        self.rope_positions = n
+        self._weights_struct = None
+
+    @property
+    def weights_struct(self) -> _lib.Weights:
+        if getattr(self, "_weights_struct", None) is None:
+            s = self.small
+            self._weights_struct = _lib.Weights(
+                emb=self.q["emb"], qkv=self.q["qkv"], o=self.q["o"], up=self.q["up"], down=self.q["down"],
+                q_gain=s["q_gain"].data_ptr(), attn_scale=s["attn_scale"].data_ptr(),
+                mlp_scale=s["mlp_scale"].data_ptr(), resid_mix=s["resid_mix"].data_ptr(),
+                ln_scale=s["ln_scale"].data_ptr(), skip_weights=s["skip_weights"].data_ptr(),
+                skip_gates=s["skip_gates"].data_ptr(), rope_cos=self.rope_cos.data_ptr(),
+                rope_sin=self.rope_sin.data_ptr(), rope_positions=self.rope_positions,
+            )
+        return self._weights_struct
+
+
+class StreamBatch:
+    """Device state of n independent streams on one GPU."""
+
+    def __init__(self, dm: DeviceModel, n: int, *, words_per_stream: int, hist_len: int = 0,
+                 keep_logits: bool = False):
+        cfg, dev = dm.cfg, dm.device
+        self.dm, self.n, self.cfg = dm, int(n), cfg
+        self.words_per_stream = int(words_per_stream)
+        L, Hkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
+        self.tok = torch.full((n,), -1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(n, dtype=torch.int64, device=dev)
+        self.active = torch.ones(n, dtype=torch.uint8, device=dev)
+        # sliding-window ring, rows in the 24-bit split format (3 bytes/value)
+        self.kv = torch.zeros((n, L, 2, Hkv, cfg.ctx, 3 * hd), dtype=torch.uint8, device=dev)
+        self.ac = torch.zeros((n, 8), dtype=torch.int64, device=dev)
+        self.bits = torch.zeros((n, self.words_per_stream), dtype=torch.int32, device=dev)
+        self.sym = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.hist_len = int(hist_len)
+        self.hist = torch.zeros((n, max(1, self.hist_len)), dtype=torch.int32, device=dev) if hist_len else None
+        self.lora = None
+        if dm.lora_floats > 0:
+            self.lora = torch.zeros((n, dm.lora_floats), dtype=torch.float32, device=dev)
+            self.reset_lora()
+        self.logits = torch.zeros((n, cfg.vocab_size), dtype=torch.float32, device=dev) if keep_logits else None
+        wsb = int(_lib.lib().altxs_workspace_bytes(C.byref(dm.desc), n))
+        if wsb < 0:
+            raise ValueError("model shape not supported by the kernels")
+        self.workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        self.rows_all = None
+        self._batch = _lib.Batch(
+            n_streams=n, tok=self.tok.data_ptr(), pos=self.pos.data_ptr(), active=self.active.data_ptr(),
+            kv=self.kv.data_ptr(), lora=self.lora.data_ptr() if self.lora is not None else None,
+            lora_stride=dm.lora_floats, ac=self.ac.data_ptr(), bits=self.bits.data_ptr(),
+            words_per_stream=self.words_per_stream, sym=self.sym.data_ptr(),
+            hist=self.hist.data_ptr() if self.hist is not None else None, hist_len=self.hist_len,
+            logits_out=self.logits.data_ptr() if self.logits is not None else None,
+            workspace=self.workspace.data_ptr(), workspace_bytes=wsb,
+        )
+        self.ac_init()
+
+    # ---- adapters -----------------------------------------------------------
+    def reset_lora(self) -> None:
+        """Reference init: A ~ U(+-1/sqrt(in)) from the seeded generator, B = 0."""
+        if self.lora is None:
+            return
+        flat = []
+        A = init_lora_A(self.cfg)
+        for name, (a_shape, b_shape) in lora_shapes(self.cfg).items():
+            flat.append(A[name].reshape(-1))
+            flat.append(np.zeros(b_shape[0] * b_shape[1], dtype=np.float32))
+        vec = torch.from_numpy(np.concatenate(flat))
+        if vec.numel() != self.dm.lora_floats:
+            raise RuntimeError("LoRA layout mismatch between host and library")
+        self.lora.copy_(vec.to(self.lora.device).expand_as(self.lora))
+
+    # ---- coder --------------------------------------------------------------
+    def _rows(self, rows):
+        if rows is None:
+            return None, self.n
+        r = torch.as_tensor(np.asarray(rows, dtype=np.int32), device=self.dm.device)
+        self._rows_keep = r
+        return r.data_ptr(), int(r.numel())
+
+    def ac_init(self, rows=None) -> None:
+        rp, n = self._rows(rows)
+        _lib.check(_lib.lib().altxs_ac_init(n, rp, self.ac.data_ptr(), _stream_handle(self.dm.device)), "ac_init")
+
+    def ac_flush(self, rows=None) -> None:
+        rp, n = self._rows(rows)
+        _lib.check(
+            _lib.lib().altxs_ac_flush(n, rp, self.ac.data_ptr(), self.bits.data_ptr(), self.words_per_stream,
+                                      _stream_handle(self.dm.device)), "ac_flush")
+
+    def begin_decode(self, payloads: dict[int, bytes]) -> None:
+        """Load one segment payload per listed stream and seed its decoder."""
+        rows = sorted(payloads)
+        host = np.zeros((len(rows), self.words_per_stream), dtype=np.uint32)
+        nb = np.zeros(len(rows), dtype=np.uint64)
+        for j, r in enumerate(rows):
+            p = payloads[r]
+            if len(p) > self.words_per_stream * 4:
+                raise ValueError(f"segment of {len(p)} bytes exceeds the bit buffer")
+            buf = np.zeros(self.words_per_stream * 4, dtype=np.uint8)
+            buf[: len(p)] = np.frombuffer(p, dtype=np.uint8)
+            host[j] = buf.view(np.uint32)
+            nb[j] = len(p) * 8
+        idx = torch.as_tensor(np.asarray(rows, dtype=np.int64), device=self.dm.device)
+        self.bits.index_copy_(0, idx, torch.from_numpy(host.view(np.int32)).to(self.dm.device))
+        nbt = torch.from_numpy(nb.view(np.int64)).to(self.dm.device)
+        rp, n = self._rows(rows)
+        _lib.check(
+            _lib.lib().altxs_ac_begin_decode(n, rp, self.ac.data_ptr(), self.bits.data_ptr(), nbt.data_ptr(),
+                                             self.words_per_stream, _stream_handle(self.dm.device)),
+            "ac_begin_decode")
+        self._nbt_keep = nbt
+
+    def segment_bytes(self, rows) -> dict[int, bytes]:
+        """Bytes written by the listed (flushed) encoders."""
+        ac = self.ac[rows].cpu().numpy()
+        nbits = ac[:, 3].astype(np.int64)
+        bits = self.bits[rows].cpu().numpy().view(np.uint8)
+        return {int(r): bits[j, : (int(nbits[j]) + 7) // 8].tobytes() for j, r in enumerate(rows)}
+
+    def status(self) -> np.ndarray:
+        return (self.ac[:, 7].cpu().numpy() & 0xFFFFFFFF).astype(np.uint32)
+
+    def check_status(self) -> None:
+        st = self.status()
+        bad = np.flatnonzero(st)
+        if bad.size:
+            i = int(bad[0])
+            names = [v for k, v in ST_NAMES.items() if st[i] & k]
+            raise RuntimeError(f"stream {i}: device status {int(st[i]):#x} ({', '.join(names)})")
+
+    # ---- step ---------------------------------------------------------------
+    def step(self, mode: int) -> None:
+        rc = _lib.lib().altxs_step(
+            C.byref(self.dm.desc), C.byref(self.dm.weights_struct), C.byref(self._batch), int(mode),
+            _stream_handle(self.dm.device),
+        )
+        _lib.check(rc, "altxs_step")
+
+    def set_active(self, mask: np.ndarray | None) -> None:
+        if mask is None:
+            self.active.fill_(1)
+        else:
+            self.active.copy_(torch.from_numpy(np.asarray(mask, dtype=np.uint8)).to(self.dm.device))
+
+
+def words_for_segment(every: int, cdf_bits: int = 20) -> int:
+    """Bit-buffer words that always hold one segment (<= cdf_bits+2 bits/symbol)."""
+    return int(every) * (max(int(cdf_bits), 20) + 2) // 32 + 4
+
+
+@dataclass
+class StreamResult:
+    payload: bytes
+    segments: list
+    n_symbols: int
+
+
+class Engine:
+    """Encode / decode many independent streams in lockstep on one GPU."""
+
+    def __init__(self, dm: DeviceModel, *, ttt=None):
+        self.dm = dm
+        self.cfg = dm.cfg
+        self.ttt = ttt  # optional callable(batch, rows, hist_end) for the boundary update
+
+    def _new_batch(self, n: int, max_len: int) -> StreamBatch:
+        cfg = self.cfg
+        self.dm.ensure_rope(max_len + 2)
+        hist = cfg.ctx + 2 if self.ttt is not None else 0
+        return StreamBatch(self.dm, n, words_per_stream=words_for_segment(cfg.online_retrain_every, cfg.cdf_bits),
+                           hist_len=hist)
+
+    def encode(self, streams: list[np.ndarray]) -> list[StreamResult]:
+        cfg, dev = self.cfg, self.dm.device
+        n = len(streams)
+        lens = np.array([len(s) for s in streams], dtype=np.int64)
+        T = int(lens.max()) if n else 0
+        every = max(1, int(cfg.online_retrain_every))
+        b = self._new_batch(n, T)
+        symsT = np.zeros((max(T, 1), n), dtype=np.int32)
+        for i, s in enumerate(streams):
+            symsT[: len(s), i] = np.asarray(s, dtype=np.int32)
+        if n and (symsT.min() < 0 or symsT.max() >= cfg.vocab_size):
+            raise ValueError("symbol outside the alphabet")
+        symsT_d = torch.from_numpy(symsT).to(dev)
+        segs: list[list[bytes]] = [[] for _ in range(n)]
+        for t in range(T):
+            if t > 0 and t % every == 0:
+                rows = [i for i in range(n) if lens[i] > t]
+                self._boundary_encode(b, rows, segs, t)
+            active = lens > t
+            if not active.all():
+                b.set_active(active)
+            b.sym.copy_(symsT_d[t])
+            b.step(_lib.STEP_ENCODE)
+        rows = [i for i in range(n) if lens[i] > 0]
+        if rows:
+            b.set_active(None)
+            b.ac_flush(rows)
+            for r, p in b.segment_bytes(rows).items():
+                segs[r].append(p)
+        torch.cuda.synchronize(dev)
+        b.check_status()
+        out = []
+        for i in range(n):
+            payload = b"".join(struct.pack("<Q", len(p)) + p for p in segs[i])
+            out.append(StreamResult(payload=payload, segments=segs[i], n_symbols=int(lens[i])))
+        return out
+
+    def _boundary_encode(self, b: StreamBatch, rows, segs, t: int) -> None:
+        b.set_active(None)
+        b.ac_flush(rows)
+        for r, p in b.segment_bytes(rows).items():
+            segs[r].append(p)
+        b.ac_init(rows)
+        if self.ttt is not None:
+            self.ttt(b, rows, t)
+
+    def decode(self, payloads: list[bytes], n_symbols: list[int]) -> list[np.ndarray]:
+        cfg, dev = self.cfg, self.dm.device
+        n = len(payloads)
+        lens = np.asarray(n_symbols, dtype=np.int64)
+        T = int(lens.max()) if n else 0
+        every = max(1, int(cfg.online_retrain_every))
+        segs = [list(iter_framed_segments(p)) for p in payloads]
+        for i in range(n):
+            need = (int(lens[i]) + every - 1) // every
+            if len(segs[i]) != need:
+                raise ValueError(f"stream {i}: {len(segs[i])} segments, expected {need}")
+        b = self._new_batch(n, T)
+        out = torch.zeros((max(T, 1), n), dtype=torch.int32, device=dev)
+        first = {i: segs[i][0] for i in range(n) if lens[i] > 0}
+        if first:
+            b.begin_decode(first)
+        for t in range(T):
+            if t > 0 and t % every == 0:
+                rows = [i for i in range(n) if lens[i] > t]
+                if rows:
+                    b.set_active(None)
+                    if self.ttt is not None:
+                        self.ttt(b, rows, t)
+                    b.begin_decode({i: segs[i][t // every] for i in rows})
+            active = lens > t
+            if not active.all():
+                b.set_active(active)
+            b.step(_lib.STEP_DECODE)
+            out[t].copy_(b.sym)
+        torch.cuda.synchronize(dev)
+        b.check_status()
+        host = out.cpu().numpy()
+        return [host[: int(lens[i]), i].copy() for i in range(n)]
+
+
+def iter_framed_segments(payload: bytes):
+    """Walk the ``<u64 len><segment bytes>`` framing (incremental.py:1782-1796)."""
+    off, total = 0, len(payload)
+    while off < total:
+        if off + 8 > total:
+            raise ValueError(f"truncated segment header at offset {off}")
+        (ln,) = struct.unpack_from("<Q", payload, off)
+        off += 8
+        if off + ln > total:
+            raise ValueError(f"truncated segment at offset {off}: need {ln}, have {total - off}")
+        yield payload[off: off + ln]
+        off += ln

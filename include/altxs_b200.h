@@ -1,0 +1,203 @@
+/*
+ * altxs_b200 -- C ABI of the B200 model-and-code loop.
+ *
+ * Plain pointers and sizes only.  Every pointer marked "device" is CUDA
+ * device memory owned by the caller; the library never allocates, never
+ * synchronises the stream (except where stated) and enqueues all work on the
+ * stream it is given (a cudaStream_t passed as void*, NULL = legacy default
+ * stream).  Return values: 0 on success, a negative errno-style code
+ * otherwise.  Device-side faults of the data (bit buffer full, symbol out of
+ * range, bad CDF total, non-finite logits, bounded wait expired) are recorded
+ * in the per-stream status word of altxs_ac_state and never trap the GPU.
+ *
+ * Bit buffers hold the reference's byte stream: stream s owns
+ * words_per_stream uint32 words at bits + s*words_per_stream and byte k of
+ * that region (little-endian word order) is byte k of the payload the
+ * reference's _pack_bits would produce (MSB-first bits, zero padded).
+ */
+#ifndef ALTXS_B200_H
+#define ALTXS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ALTXS_OK 0
+#define ALTXS_EINVAL (-22)
+#define ALTXS_ENOSPC (-28)
+#define ALTXS_ENOTSUP (-95)
+#define ALTXS_ECUDA (-5)
+
+/* per-stream device status bits (altxs_ac_state.status) */
+#define ALTXS_ST_OVERFLOW 1u    /* bit buffer full: further bits dropped */
+#define ALTXS_ST_BAD_SYMBOL 2u  /* symbol outside [0, V) or zero mass */
+#define ALTXS_ST_BAD_TOTAL 4u   /* CDF total 0 or above 2^30 */
+#define ALTXS_ST_NONFINITE 8u   /* NaN/inf logits */
+#define ALTXS_ST_TIMEOUT 16u    /* a bounded device wait gave up */
+#define ALTXS_ST_BAD_POS 32u    /* position beyond weights->rope_positions */
+
+/* CDF rules */
+#define ALTXS_CDF_FIXED 0 /* integer fixed-point softmax, total <= 2^cdf_bits */
+#define ALTXS_CDF_REF 1   /* reference masses max(1, floor(p*1e6 + 0.5)) */
+
+/* altxs_step modes */
+#define ALTXS_STEP_LOGITS 0 /* model only: logits into batch->logits_out */
+#define ALTXS_STEP_ENCODE 1
+#define ALTXS_STEP_DECODE 2
+
+typedef void *altxs_stream_t;
+
+/* Range-coder state of one stream (64 bytes). */
+typedef struct altxs_ac_state {
+    uint64_t low, high, pending, nbits; /* encoder */
+    uint64_t value, bpos, n_in_bits;    /* decoder: value, next bit, payload bits */
+    uint32_t status, reserved;
+} altxs_ac_state;
+
+/* ---- range coder ---------------------------------------------------------
+ * Replaces the reference's single-stream CUDA coder module xsa_gpu_ac
+ * (altxs src/xsa_ttt/gpu_ac.py:26-341): one 1-thread kernel per symbol with
+ * one int64 per bit becomes one CTA per stream over many streams, 32 bits per
+ * word, with error status instead of silent truncation.  `rows` (device,
+ * optional) selects which streams a call touches; NULL = streams 0..n-1.
+ */
+
+/* Reset encoders (low = 0, high = 2^32 - 1, pending = nbits = status = 0).
+ * Replaces GpuRangeCoder.__init__ state setup (gpu_ac.py:400-415). */
+int altxs_ac_init(int n, const int32_t *rows, altxs_ac_state *st, altxs_stream_t stream);
+
+/* Encode one symbol per stream from fp32 probabilities with the reference
+ * mass rule.  probs: device [n][ld] (row i for stream rows[i]).
+ * Replaces encode_sym / launch_encode_sym (gpu_ac.py:84-116, 224-230, 271-290). */
+int altxs_ac_encode_probs(int n, const int32_t *rows, int vocab, const float *probs, int64_t ld,
+                          const int32_t *syms, altxs_ac_state *st, uint32_t *bits,
+                          int64_t words_per_stream, altxs_stream_t stream);
+
+/* Encode with caller-supplied integer CDFs: cum device [n][ld] uint32,
+ * cum[0] = 0, cum[V] = total <= 2^30.  Same coder arithmetic as
+ * arithmetic_coder_lm.encode_with_probs (arithmetic_coder_lm.py:175-180). */
+int altxs_ac_encode_cum(int n, const int32_t *rows, int vocab, const uint32_t *cum, int64_t ld,
+                        const int32_t *syms, altxs_ac_state *st, uint32_t *bits,
+                        int64_t words_per_stream, altxs_stream_t stream);
+
+/* Final flush (pending+1, one bit and the pending run).
+ * Replaces flush_bits / flush_kernel (gpu_ac.py:118-142, 292-304). */
+int altxs_ac_flush(int n, const int32_t *rows, altxs_ac_state *st, uint32_t *bits,
+                   int64_t words_per_stream, altxs_stream_t stream);
+
+/* Start decoding: n_bits device [n] payload length in bits, value = first
+ * 32 bits.  Replaces seed_value / begin_decode (gpu_ac.py:144-156, 448-466). */
+int altxs_ac_begin_decode(int n, const int32_t *rows, altxs_ac_state *st, const uint32_t *bits,
+                          const uint64_t *n_bits, int64_t words_per_stream, altxs_stream_t stream);
+
+/* Decode one symbol per stream (reference mass rule / supplied CDFs).
+ * Replaces decode_sym / decode_sym_kernel (gpu_ac.py:158-222, 306-330). */
+int altxs_ac_decode_probs(int n, const int32_t *rows, int vocab, const float *probs, int64_t ld,
+                          int32_t *syms_out, altxs_ac_state *st, const uint32_t *bits,
+                          int64_t words_per_stream, altxs_stream_t stream);
+int altxs_ac_decode_cum(int n, const int32_t *rows, int vocab, const uint32_t *cum, int64_t ld,
+                        int32_t *syms_out, altxs_ac_state *st, const uint32_t *bits,
+                        int64_t words_per_stream, altxs_stream_t stream);
+
+/* Integer CDFs of softcapped logits under a framework rule (parity/debug).
+ * Replaces the host rule _scale_cum_np over torch.softmax rows
+ * (arithmetic_coder_lm.py:49-64, incremental.py:603-633). */
+int altxs_cdf_from_logits(int n, int vocab, const float *logits, int64_t ld, int mode, int cdf_bits,
+                          uint32_t *cum, int64_t cum_ld, altxs_stream_t stream);
+
+/* ---- model ------------------------------------------------------------- */
+
+/* One mixed-bit matrix W[rows][cols] in 64-wide groups along cols.
+ * gdesc[r][g] = fp16 scale | width code << 16 (0:0 1:2 2:3 3:4 4:fp32 bits)
+ *               | in-row offset in 8-byte units << 20.
+ * Replaces the dense bf16 banks + F.linear of the reference step
+ * (model.py:997-1011, 1183-1236; ac_gemv.py:27-60) and the host-side
+ * dequantisation of the v5 codec (mixed_bit_delta.py:96-229). */
+typedef struct altxs_qmat {
+    const uint8_t *codes;     /* device: packed codes, 16-byte aligned */
+    const uint32_t *row_off8; /* device [rows]: row start in 8-byte units */
+    const uint32_t *gdesc;    /* device [rows][cols/64] */
+    const uint16_t *lut;      /* device fp16 [n][16] codebooks, NULL = symmetric */
+    const uint32_t *glut;     /* device [rows][cols/64] codebook index, or NULL */
+    int32_t rows, cols;
+} altxs_qmat;
+
+typedef struct altxs_model_desc {
+    int32_t vocab, n_layers, d_model, n_heads, n_kv_heads, head_dim, mlp_hidden;
+    int32_t ctx;        /* sliding window (reference block_size) */
+    int32_t rope_dims;  /* partial RoPE width */
+    int32_t skip_gates; /* sigmoid-gated U-Net skips */
+    int32_t lora_rank;  /* 0 = no adapters */
+    int32_t lora_mask;  /* bit0 q, bit1 k, bit2 v, bit3 o, bit4 lm_head */
+    int32_t cdf_mode, cdf_bits;
+    float logit_softcap, lora_scale;
+} altxs_model_desc;
+
+typedef struct altxs_weights {
+    altxs_qmat emb;  /* [V][d], tied LM head */
+    altxs_qmat qkv;  /* [L*(d+2*kv)][d]: per layer q rows, k rows, v rows */
+    altxs_qmat o;    /* [L*d][d] */
+    altxs_qmat up;   /* [L*F][d] */
+    altxs_qmat down; /* [L*d][F] */
+    const float *q_gain;       /* [L][H] */
+    const float *attn_scale;   /* [L][d] */
+    const float *mlp_scale;    /* [L][d] */
+    const float *resid_mix;    /* [L][2][d] */
+    const float *ln_scale;     /* [L] (1/sqrt(i+1) or 1) */
+    const float *skip_weights; /* [L/2][d] */
+    const float *skip_gates;   /* [L/2][d] */
+    const float *rope_cos;     /* [rope_positions][rope_dims/2] */
+    const float *rope_sin;
+    int64_t rope_positions;
+} altxs_weights;
+
+/* Per-stream state and scratch of a batch of n streams.  Stream i of the
+ * batch lives in slot i of every per-stream array. */
+typedef struct altxs_batch {
+    int32_t n_streams;
+    int32_t *tok;           /* [n] token consumed this step (<0: none, uniform row) */
+    int64_t *pos;           /* [n] position tok is written at (tokens consumed) */
+    const uint8_t *active;  /* [n] 0 = leave the stream untouched (NULL = all) */
+    uint8_t *kv;            /* [n][L][2 (K,V)][Hkv][ctx][3*hd] sliding-window ring, rows in
+                               24-bit split format: hd x u16 (bf16 high half of the
+                               round-to-nearest 24-bit value) then hd x u8 (low byte) */
+    float *lora;            /* [n][lora_floats] adapters (NULL if lora_rank = 0) */
+    int64_t lora_stride;    /* floats per stream */
+    altxs_ac_state *ac;     /* [n] */
+    uint32_t *bits;         /* [n][words_per_stream] */
+    int64_t words_per_stream;
+    int32_t *sym;           /* [n] encode: input symbols; decode: output */
+    int32_t *hist;          /* [n][hist_len] coded-symbol ring (TTT windows) or NULL */
+    int32_t hist_len;
+    float *logits_out;      /* [n][V] final logits copy, or NULL */
+    void *workspace;        /* >= altxs_workspace_bytes(desc, n) bytes, 256-aligned */
+    int64_t workspace_bytes;
+} altxs_batch;
+
+/* Workspace needed by altxs_step for n streams (bytes). */
+int64_t altxs_workspace_bytes(const altxs_model_desc *desc, int n_streams);
+
+/* Floats per stream in the LoRA arena: adapters in the reference
+ * TTTLoRA.parameters() order lm(A,B), q_i(A,B).., v_i.., k_i.., o_i..
+ * (ttt_lora.py:67-105), A [r][in] then B [out][r]. */
+int64_t altxs_lora_floats(const altxs_model_desc *desc);
+
+/* One symbol step for every active stream: embed tok, run the L-layer GPT
+ * step over the sliding KV window (writing tok's K/V at pos), tied logits with
+ * tanh softcap, integer CDF, then range-code sym (encode) or decode it
+ * (decode).  Afterwards tok = coded symbol and pos advances if a token was
+ * consumed.  Replaces one W=1 window step plus coder call of the reference
+ * engine (incremental.py:1083-1130 run_decode_row_dev + gpu_ac decode_sym,
+ * and the encode-side run_window + encode_sym, :1268-1290). */
+int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b, int mode,
+               altxs_stream_t stream);
+
+/* Library build string (for logs). */
+const char *altxs_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ALTXS_B200_H */
