@@ -21,8 +21,10 @@ EXPORTS = (
     "altxs_ac_init", "altxs_ac_encode_probs", "altxs_ac_encode_cum", "altxs_ac_flush",
     "altxs_ac_begin_decode", "altxs_ac_decode_probs", "altxs_ac_decode_cum",
     "altxs_cdf_from_logits", "altxs_workspace_bytes", "altxs_lora_floats", "altxs_step",
-    "altxs_version",
+    "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
 )
+KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
+                  "final_norm", "cdf_code", "coder", "ttt")
 
 
 class AcState(C.Structure):
@@ -97,6 +99,9 @@ def lib():
             "altxs_lora_floats": (i64, [C.POINTER(ModelDesc)]),
             "altxs_step": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int, vp]),
             "altxs_version": (C.c_char_p, []),
+            "altxs_launch_count": (i64, []),
+            "altxs_profile": (C.c_int, [C.c_int]),
+            "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

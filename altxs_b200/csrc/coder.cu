@@ -1,5 +1,6 @@
 // Batched range-coder entry points (one stream per CTA or per thread).
 #include "coder.cuh"
+#include "prof.cuh"
 
 using namespace altxs;
 
@@ -204,8 +205,7 @@ extern "C" {
 int altxs_ac_init(int n, const int32_t *rows, altxs_ac_state *st, altxs_stream_t stream) {
     if (n < 0 || (n > 0 && !st)) return ALTXS_EINVAL;
     if (n == 0) return ALTXS_OK;
-    k_ac_init<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, st);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_init<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, st));
     return ALTXS_OK;
 }
 
@@ -219,9 +219,8 @@ int altxs_ac_encode_probs(int n, const int32_t *rows, int vocab, const float *pr
     const size_t sm = (size_t)vocab * 4;
     if (sm > 48 * 1024)
         cudaFuncSetAttribute(k_ac_probs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    k_ac_probs<<<n, kCoderThreads, sm, S(stream)>>>(n, rows, vocab, probs, ld, const_cast<int32_t *>(syms), st,
-                                                    bits, wps, 0);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_probs<<<n, kCoderThreads, sm, S(stream)>>>(n, rows, vocab, probs, ld, const_cast<int32_t *>(syms), st,
+                                                    bits, wps, 0));
     return ALTXS_OK;
 }
 
@@ -233,9 +232,8 @@ int altxs_ac_decode_probs(int n, const int32_t *rows, int vocab, const float *pr
     const size_t sm = (size_t)vocab * 4;
     if (sm > 48 * 1024)
         cudaFuncSetAttribute(k_ac_probs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    k_ac_probs<<<n, kCoderThreads, sm, S(stream)>>>(n, rows, vocab, probs, ld, syms_out, st,
-                                                    const_cast<uint32_t *>(bits), wps, 1);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_probs<<<n, kCoderThreads, sm, S(stream)>>>(n, rows, vocab, probs, ld, syms_out, st,
+                                                    const_cast<uint32_t *>(bits), wps, 1));
     return ALTXS_OK;
 }
 
@@ -244,8 +242,7 @@ int altxs_ac_encode_cum(int n, const int32_t *rows, int vocab, const uint32_t *c
                         altxs_stream_t stream) {
     if (n < 0 || vocab < 1 || ld < vocab + 1 || wps < 1) return ALTXS_EINVAL;
     if (n == 0) return ALTXS_OK;
-    k_ac_encode_cum<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, vocab, cum, ld, syms, st, bits, wps);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_encode_cum<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, vocab, cum, ld, syms, st, bits, wps));
     return ALTXS_OK;
 }
 
@@ -254,8 +251,7 @@ int altxs_ac_decode_cum(int n, const int32_t *rows, int vocab, const uint32_t *c
                         altxs_stream_t stream) {
     if (n < 0 || vocab < 1 || ld < vocab + 1 || wps < 1) return ALTXS_EINVAL;
     if (n == 0) return ALTXS_OK;
-    k_ac_decode_cum<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, vocab, cum, ld, syms_out, st, bits, wps);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_decode_cum<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, vocab, cum, ld, syms_out, st, bits, wps));
     return ALTXS_OK;
 }
 
@@ -263,8 +259,7 @@ int altxs_ac_flush(int n, const int32_t *rows, altxs_ac_state *st, uint32_t *bit
                    altxs_stream_t stream) {
     if (n < 0 || wps < 1) return ALTXS_EINVAL;
     if (n == 0) return ALTXS_OK;
-    k_ac_flush<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, st, bits, wps);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_flush<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, st, bits, wps));
     return ALTXS_OK;
 }
 
@@ -272,8 +267,7 @@ int altxs_ac_begin_decode(int n, const int32_t *rows, altxs_ac_state *st, const 
                           const uint64_t *n_bits, int64_t wps, altxs_stream_t stream) {
     if (n < 0 || wps < 1) return ALTXS_EINVAL;
     if (n == 0) return ALTXS_OK;
-    k_ac_begin_decode<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, st, bits, n_bits, wps);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_ac_begin_decode<<<grid1(n, 128), 128, 0, S(stream)>>>(n, rows, st, bits, n_bits, wps));
     return ALTXS_OK;
 }
 
@@ -286,8 +280,7 @@ int altxs_cdf_from_logits(int n, int vocab, const float *logits, int64_t ld, int
     const size_t sm = (size_t)vocab * 4;
     if (sm > 48 * 1024)
         cudaFuncSetAttribute(k_cdf_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    k_cdf_rows<<<n, kCoderThreads, sm, S(stream)>>>(vocab, logits, ld, mode, cdf_bits, cum, cum_ld);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCoder, S(stream), k_cdf_rows<<<n, kCoderThreads, sm, S(stream)>>>(vocab, logits, ld, mode, cdf_bits, cum, cum_ld));
     return ALTXS_OK;
 }
 

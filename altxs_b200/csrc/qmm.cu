@@ -12,6 +12,7 @@
 // (mixed_bit_delta.py:147-213 then F.linear); dequantised values are exact in
 // fp32, so the two differ only in rounding order.
 #include "qmm.cuh"
+#include "prof.cuh"
 
 namespace altxs {
 namespace {
@@ -279,18 +280,18 @@ int launch_qmm_path(const QmmArgs &a, cudaStream_t stream, int force_path) {
         const int grid = (a.N + rows_per_cta - 1) / rows_per_cta;
         if (a.M <= 1) {
             if (sm > 48 * 1024) cudaFuncSetAttribute(k_qgemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-            k_qgemv<1><<<grid, kGemvThreads, sm, stream>>>(a);
+            ALTXS_LAUNCH(::altxs::kKQmm, stream, k_qgemv<1><<<grid, kGemvThreads, sm, stream>>>(a));
         } else if (a.M <= 4) {
             if (sm > 48 * 1024) cudaFuncSetAttribute(k_qgemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-            k_qgemv<4><<<grid, kGemvThreads, sm, stream>>>(a);
+            ALTXS_LAUNCH(::altxs::kKQmm, stream, k_qgemv<4><<<grid, kGemvThreads, sm, stream>>>(a));
         } else {
             if (sm > 48 * 1024) cudaFuncSetAttribute(k_qgemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-            k_qgemv<16><<<grid, kGemvThreads, sm, stream>>>(a);
+            ALTXS_LAUNCH(::altxs::kKQmm, stream, k_qgemv<16><<<grid, kGemvThreads, sm, stream>>>(a));
         }
     } else {
         if ((a.ldx % 4) || (reinterpret_cast<uintptr_t>(a.X) & 15)) return ALTXS_EINVAL;
         dim3 grid((a.N + kTN - 1) / kTN, (a.M + kTM - 1) / kTM);
-        k_qgemm<<<grid, kTThreads, 0, stream>>>(a);
+        ALTXS_LAUNCH(::altxs::kKQmm, stream, k_qgemm<<<grid, kTThreads, 0, stream>>>(a));
     }
     ALTXS_LAUNCH_CHECK();
     return ALTXS_OK;

@@ -11,6 +11,7 @@
 
 #include "coder.cuh"
 #include "qmm.cuh"
+#include "prof.cuh"
 
 using namespace altxs;
 
@@ -717,8 +718,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     c.logits = take((int64_t)D.n * D.V);
     c.lt = take((int64_t)D.n * (D.r > 0 ? D.r : 1));
 
-    k_embed<<<D.n, 128, 0, st>>>(c);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKEmbed, st, k_embed<<<D.n, 128, 0, st>>>(c));
     const int G = D.H / D.Hkv;
     const size_t attn_sm = (size_t)2 * kSplit * 3 * D.hd + (size_t)G * kSplit * 4 + (size_t)(kAttnThreads / 32) * G * D.hd * 4;
     {
@@ -733,8 +733,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     }
     const size_t qkv_sm = ((size_t)D.qkv_n + 3 * (D.r > 0 ? D.r : 1) + D.d) * 4;
     for (int l = 0; l < D.L; ++l) {
-        k_prenorm<<<D.n, 128, 0, st>>>(c, l);
-        ALTXS_LAUNCH_CHECK();
+        ALTXS_LAUNCH(::altxs::kKPrenorm, st, k_prenorm<<<D.n, 128, 0, st>>>(c, l));
         QmmArgs a{};
         a.X = c.nrm;
         a.ldx = D.d;
@@ -747,12 +746,9 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.ldy = D.qkv_n;
         a.epi = kEpiStore;
         if ((rc = launch_qmm(a, st))) return rc;
-        k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, l);
-        ALTXS_LAUNCH_CHECK();
-        k_attn_partial<<<dim3(D.nsplit, D.Hkv, D.n), kAttnThreads, attn_sm, st>>>(c, l);
-        ALTXS_LAUNCH_CHECK();
-        k_attn_merge<<<D.n * D.H, D.hd, 0, st>>>(c);
-        ALTXS_LAUNCH_CHECK();
+        ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, l));
+        ALTXS_LAUNCH(::altxs::kKAttn, st, k_attn_partial<<<dim3(D.nsplit, D.Hkv, D.n), kAttnThreads, attn_sm, st>>>(c, l));
+        ALTXS_LAUNCH(::altxs::kKAttnMerge, st, k_attn_merge<<<D.n * D.H, D.hd, 0, st>>>(c));
         a.X = c.y;
         a.W = w->o;
         a.row0 = l * D.d;
@@ -760,8 +756,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.Y = c.ao;
         a.ldy = D.d;
         if ((rc = launch_qmm(a, st))) return rc;
-        k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l);
-        ALTXS_LAUNCH_CHECK();
+        ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l));
         a.X = c.nrm2;
         a.W = w->up;
         a.row0 = l * D.F;
@@ -786,8 +781,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.ldy2 = D.d;
         if ((rc = launch_qmm(a, st))) return rc;
     }
-    k_final<<<D.n, 128, D.d * 4, st>>>(c);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKFinal, st, k_final<<<D.n, 128, D.d * 4, st>>>(c));
     QmmArgs a{};
     a.X = c.nrm;
     a.ldx = D.d;
@@ -800,8 +794,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     a.ldy = D.V;
     a.epi = kEpiStore;
     if ((rc = launch_qmm(a, st))) return rc;
-    k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode);
-    ALTXS_LAUNCH_CHECK();
+    ALTXS_LAUNCH(::altxs::kKCdfCode, st, k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode));
     return ALTXS_OK;
 }
 

@@ -259,6 +259,60 @@ class StreamBatch:
         )
         _lib.check(rc, "altxs_step")
 
+    # ---- chunk API: one flushed segment per stream ---------------------------
+    def encode_chunk(self, symbols: torch.Tensor) -> list[bytes]:
+        """Code ``symbols[t][i]`` (host or device, [n_steps][n]) as one segment
+        per stream, continuing every stream's model state; returns the bytes."""
+        dev = self.dm.device
+        syms = symbols.to(dev, non_blocking=True)
+        self.ac_init()
+        for t in range(syms.shape[0]):
+            self.sym.copy_(syms[t])
+            self.step(_lib.STEP_ENCODE)
+        self.ac_flush()
+        out = self.segment_bytes(list(range(self.n)))
+        self.check_status()
+        return [out[i] for i in range(self.n)]
+
+    def pack_payloads(self, payloads: list[bytes], pin: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+        """Host staging of one segment per stream: ([n][words] int32, [n] bits)."""
+        host = np.zeros((self.n, self.words_per_stream * 4), dtype=np.uint8)
+        nb = np.zeros(self.n, dtype=np.int64)
+        for i, p in enumerate(payloads):
+            if len(p) > host.shape[1]:
+                raise ValueError(f"segment of {len(p)} bytes exceeds the bit buffer")
+            host[i, : len(p)] = np.frombuffer(p, dtype=np.uint8)
+            nb[i] = len(p) * 8
+        words = torch.from_numpy(host.view(np.int32))
+        nbits = torch.from_numpy(nb)
+        if pin:
+            words, nbits = words.pin_memory(), nbits.pin_memory()
+        return words, nbits
+
+    def decode_chunk(self, words: torch.Tensor, nbits: torch.Tensor, n_steps: int,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+        """Decode ``n_steps`` symbols per stream from one segment per stream.
+
+        ``words``/``nbits`` are host (ideally pinned) buffers from
+        ``pack_payloads``; the result is a host tensor [n_steps][n] (int32).
+        Host->device copy, the decode steps and the device->host copy are
+        all enqueued on the current stream."""
+        dev = self.dm.device
+        self.bits.copy_(words, non_blocking=True)
+        nb = nbits.to(dev, non_blocking=True)
+        _lib.check(
+            _lib.lib().altxs_ac_begin_decode(self.n, None, self.ac.data_ptr(), self.bits.data_ptr(), nb.data_ptr(),
+                                             self.words_per_stream, _stream_handle(dev)), "ac_begin_decode")
+        dsyms = torch.empty((n_steps, self.n), dtype=torch.int32, device=dev)
+        for t in range(n_steps):
+            self.step(_lib.STEP_DECODE)
+            dsyms[t].copy_(self.sym)
+        if out is None:
+            out = torch.empty((n_steps, self.n), dtype=torch.int32).pin_memory()
+        out.copy_(dsyms, non_blocking=True)
+        self._nb_keep = nb
+        return out
+
     def set_active(self, mask: np.ndarray | None) -> None:
         if mask is None:
             self.active.fill_(1)

@@ -194,6 +194,25 @@ int64_t altxs_lora_floats(const altxs_model_desc *desc);
 int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b, int mode,
                altxs_stream_t stream);
 
+/* ---- accounting -----------------------------------------------------------
+ * No counterpart in the reference (which has no tracing); these
+ * give the benchmark per-kernel device time measured live on the launch
+ * stream and the number of kernels launched. */
+
+/* Kernels launched by this library since load (monotonic). */
+int64_t altxs_launch_count(void);
+
+/* 1: reset and start recording a CUDA event pair around every launch
+ * (host-side only, at most 16384 launches); 0: stop. */
+int altxs_profile(int enable);
+
+/* Synchronises the recorded events and returns, per kernel class c <
+ * n_classes, the summed duration ms[c] and launch count counts[c].  Classes:
+ * 0 embed, 1 prenorm, 2 mixed-bit linear, 3 qkv post, 4 attention partials,
+ * 5 attention merge, 6 post-attention, 7 final norm, 8 logits->CDF->coder,
+ * 9 standalone coder, 10 test-time LoRA.  Returns the number of pairs read. */
+int altxs_profile_read(int n_classes, double *ms, int64_t *counts);
+
 /* Library build string (for logs). */
 const char *altxs_version(void);
 

@@ -145,6 +145,83 @@ int64_t oc_decode_cum(int64_t n, int32_t V, const uint64_t *cum,
     return 0;
 }
 
+/* ---- incremental forms (one symbol per call) for model-in-the-loop use --- */
+typedef struct {
+    uint64_t low, high, value, bpos, n_bits;
+    const uint8_t *in;
+} oc_dec;
+
+void oc_dec_begin(oc_dec *d, const uint8_t *in, int64_t n_bytes) {
+    d->low = 0;
+    d->high = OC_TOP - 1;
+    d->value = 0;
+    d->bpos = 0;
+    d->n_bits = (uint64_t)n_bytes * 8;
+    d->in = in;
+    for (int i = 0; i < 32; i++) d->value = (d->value << 1) | (uint64_t)get_bit(in, d->n_bits, d->bpos++);
+}
+
+int32_t oc_dec_next(oc_dec *d, int32_t V, const uint64_t *c) {
+    uint64_t total = c[V];
+    if (total == 0 || total > OC_QUARTER) return -1;
+    uint64_t range = d->high - d->low + 1;
+    uint64_t offset = ((d->value - d->low + 1) * total - 1) / range;
+    int32_t lo = 0, hi = V, sym = 0;
+    while (lo < hi) {
+        int32_t mid = (lo + hi) / 2;
+        if (c[mid] <= offset) { sym = mid; lo = mid + 1; } else { hi = mid; }
+    }
+    d->high = d->low + (range * c[sym + 1]) / total - 1;
+    d->low = d->low + (range * c[sym]) / total;
+    for (;;) {
+        if (d->high < OC_HALF) {
+        } else if (d->low >= OC_HALF) {
+            d->low -= OC_HALF; d->high -= OC_HALF; d->value -= OC_HALF;
+        } else if (d->low >= OC_QUARTER && d->high < 3 * OC_QUARTER) {
+            d->low -= OC_QUARTER; d->high -= OC_QUARTER; d->value -= OC_QUARTER;
+        } else {
+            break;
+        }
+        d->low <<= 1;
+        d->high = (d->high << 1) | 1;
+        d->value = (d->value << 1) | (uint64_t)get_bit(d->in, d->n_bits, d->bpos++);
+    }
+    return sym;
+}
+
+typedef struct {
+    oc_enc s;
+    uint8_t *out;
+    uint64_t cap_bits;
+} oc_enc_inc;
+
+void oc_enc_begin(oc_enc_inc *e, uint8_t *out, int64_t cap_bytes) {
+    e->s.low = 0;
+    e->s.high = OC_TOP - 1;
+    e->s.pending = 0;
+    e->s.nbits = 0;
+    e->s.status = 0;
+    e->out = out;
+    e->cap_bits = (uint64_t)cap_bytes * 8;
+    memset(out, 0, (size_t)cap_bytes);
+}
+
+int oc_enc_next(oc_enc_inc *e, int32_t V, const uint64_t *c, int32_t sym) {
+    if (sym < 0 || sym >= V || c[sym + 1] <= c[sym]) return -OC_ST_BAD_SYMBOL;
+    if (c[V] == 0 || c[V] > OC_QUARTER) return -OC_ST_BAD_TOTAL;
+    enc_interval(&e->s, e->out, e->cap_bits, c[sym], c[sym + 1], c[V]);
+    return -e->s.status;
+}
+
+int64_t oc_enc_finish(oc_enc_inc *e) {
+    enc_flush(&e->s, e->out, e->cap_bits);
+    if (e->s.status) return -e->s.status;
+    return (int64_t)e->s.nbits;
+}
+
+int64_t oc_dec_state_size(void) { return (int64_t)sizeof(oc_dec); }
+int64_t oc_enc_state_size(void) { return (int64_t)sizeof(oc_enc_inc); }
+
 /* Reference mass rule: freq = max(1, floor((double)p * 1e6 + 0.5)). */
 void oc_cum_from_probs_ref(int64_t n, int32_t V, const float *probs, uint64_t *cum) {
     for (int64_t r = 0; r < n; r++) {

@@ -45,6 +45,18 @@ def _lib():
         lib.oc_cum_from_logits_fixed.argtypes = [i64, i32, vp, i32, vp]
         lib.oc_cum_from_logits_ref.restype = ctypes.c_int
         lib.oc_cum_from_logits_ref.argtypes = [i64, i32, vp, vp]
+        lib.oc_dec_begin.restype = None
+        lib.oc_dec_begin.argtypes = [vp, vp, i64]
+        lib.oc_dec_next.restype = i32
+        lib.oc_dec_next.argtypes = [vp, i32, vp]
+        lib.oc_enc_begin.restype = None
+        lib.oc_enc_begin.argtypes = [vp, vp, i64]
+        lib.oc_enc_next.restype = ctypes.c_int
+        lib.oc_enc_next.argtypes = [vp, i32, vp, i32]
+        lib.oc_enc_finish.restype = i64
+        lib.oc_enc_finish.argtypes = [vp]
+        lib.oc_dec_state_size.restype = i64
+        lib.oc_enc_state_size.restype = i64
         _LIB = lib
     return _LIB
 
@@ -118,7 +130,46 @@ def decode_probs(probs: np.ndarray, payload: bytes, n: int) -> np.ndarray:
     return decode_cum(cum_from_probs_ref(probs), payload, n)
 
 
+class IncrementalEncoder:
+    """One symbol per call, for model-in-the-loop coding on the CPU."""
+
+    def __init__(self, capacity_bytes: int):
+        L = _lib()
+        self._st = ctypes.create_string_buffer(int(L.oc_enc_state_size()))
+        self._out = np.zeros(int(capacity_bytes), dtype=np.uint8)
+        L.oc_enc_begin(self._st, _ptr(self._out), self._out.size)
+
+    def encode(self, cum_row: np.ndarray, sym: int) -> None:
+        c = np.ascontiguousarray(cum_row, dtype=np.uint64)
+        rc = _lib().oc_enc_next(self._st, c.shape[0] - 1, _ptr(c), int(sym))
+        if rc != 0:
+            raise ValueError(f"oracle encode failed (status {-rc})")
+
+    def finish(self) -> bytes:
+        nbits = _lib().oc_enc_finish(self._st)
+        if nbits < 0:
+            raise ValueError(f"oracle encode failed (status {-nbits})")
+        return self._out[: (nbits + 7) // 8].tobytes()
+
+
+class IncrementalDecoder:
+    def __init__(self, payload: bytes):
+        L = _lib()
+        self._st = ctypes.create_string_buffer(int(L.oc_dec_state_size()))
+        self._buf = np.frombuffer(bytes(payload) + b"\0" * 8, dtype=np.uint8).copy()
+        L.oc_dec_begin(self._st, _ptr(self._buf), len(payload))
+
+    def decode(self, cum_row: np.ndarray) -> int:
+        c = np.ascontiguousarray(cum_row, dtype=np.uint64)
+        s = _lib().oc_dec_next(self._st, c.shape[0] - 1, _ptr(c))
+        if s < 0:
+            raise ValueError("oracle decode failed (bad CDF total)")
+        return int(s)
+
+
 __all__ = [
+    "IncrementalEncoder",
+    "IncrementalDecoder",
     "build",
     "cum_from_probs_ref",
     "cum_from_logits",

@@ -230,6 +230,21 @@ class OracleModel:
         st["pos"] = pos + 1
         return logits[0]
 
+    @torch.no_grad()
+    def prefill(self, st, tokens, lora: OracleLoRA | None = None) -> torch.Tensor:
+        """Consume ``tokens`` from an empty stream in one causal pass (the
+        last ``ctx-1`` keys are kept); returns the last position's logits."""
+        if st["pos"] != 0:
+            raise ValueError("prefill starts from an empty stream")
+        toks = torch.as_tensor(np.asarray(tokens, dtype=np.int64))
+        T = toks.shape[0]
+        if T > self.cfg.ctx:
+            raise ValueError("prefill longer than the window is not a sliding-window pass")
+        logits, new_kv = self._stack(toks, torch.arange(T), [None] * self.cfg.num_layers, lora, causal=True)
+        st["kv"] = list(new_kv)
+        st["pos"] = T
+        return logits[-1]
+
     # ---- teacher-forced window (training forward) --------------------------
     def window_logits(self, tokens: torch.Tensor, lora: OracleLoRA | None) -> torch.Tensor:
         T = tokens.shape[0]
