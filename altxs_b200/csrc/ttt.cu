@@ -1,0 +1,819 @@
+// Test-time LoRA update of one stream over its last window (sm_100a).
+//
+// Restates the reference online update in lora mode (altxs
+// src/xsa_ttt/compress.py:1104-1137 with ttt_lora.py:124-179, 258-374):
+// teacher-forced forward over x = window[0..T), targets window[1..T] with
+// positions 0..T-1 and causal attention, LoRA deltas (x A^T B^T) * alpha/r on
+// q/k/v/o (o on the block's normed input) and on the tied LM head, tanh
+// softcap, mean cross-entropy; backward into the adapters only (frozen
+// mixed-bit base); global-norm clip; AdamW step.  Every reduction runs in a
+// fixed order (no atomics), so encoder and decoder compute identical updates.
+#include <math.h>
+
+#include "gemm.cuh"
+#include "model.cuh"
+#include "prof.cuh"
+#include "qmm.cuh"
+
+using namespace altxs;
+
+namespace {
+
+struct TD {
+    int T, V, L, d, H, Hkv, hd, kvd, F, qn, r, enc, nskip, G, rd;
+};
+
+struct Tape {
+    // forward state
+    float *x0, *x, *skip;  // skip [enc][T][d]
+    // per layer [L][...]
+    float *xin, *inv1, *n, *qkv, *hinv, *qr, *kr, *P, *tq, *tk, *tv, *to, *xmid, *inv2, *n2, *u;
+    // scratch
+    float *y, *ao, *hbuf;
+    // head
+    float *invf, *hf, *logits, *tlm, *rowloss;
+    // backward
+    float *dx, *dskip, *dd, *dh, *dn, *dn2, *dqkv, *dqr, *dkr, *dy, *dao, *dS, *dt, *grad, *red;
+};
+
+int fill(const altxs_model_desc &dsc, int T, TD &D) {
+    D.T = T;
+    D.V = dsc.vocab;
+    D.L = dsc.n_layers;
+    D.d = dsc.d_model;
+    D.H = dsc.n_heads;
+    D.Hkv = dsc.n_kv_heads;
+    D.hd = dsc.head_dim;
+    D.kvd = D.Hkv * D.hd;
+    D.F = dsc.mlp_hidden;
+    D.qn = D.d + 2 * D.kvd;
+    D.r = dsc.lora_rank;
+    D.enc = D.L / 2;
+    D.nskip = D.enc < D.L - D.enc ? D.enc : D.L - D.enc;
+    D.G = D.H / (D.Hkv > 0 ? D.Hkv : 1);
+    D.rd = dsc.rope_dims;
+    if (T < 2 || D.r < 1 || D.r > 64 || D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
+    if (D.hd > 128 || D.rd > D.hd || D.rd % 2) return ALTXS_EINVAL;
+    return ALTXS_OK;
+}
+
+int64_t carve(const TD &D, void *base, Tape *tp) {
+    unsigned char *p = static_cast<unsigned char *>(base);
+    int64_t off = 0;
+    auto take = [&](int64_t nfl) -> float * {
+        float *r = base ? reinterpret_cast<float *>(p + off) : nullptr;
+        off += align_up(nfl * 4, 256);
+        return r;
+    };
+    const int64_t T = D.T, L = D.L, d = D.d;
+    Tape t{};
+    t.x0 = take(T * d);
+    t.x = take(T * d);
+    t.skip = take((int64_t)(D.enc > 0 ? D.enc : 1) * T * d);
+    t.xin = take(L * T * d);
+    t.inv1 = take(L * T);
+    t.n = take(L * T * d);
+    t.qkv = take(L * T * D.qn);
+    t.hinv = take(L * T * (D.H + D.Hkv));
+    t.qr = take(L * T * d);
+    t.kr = take(L * T * D.kvd);
+    t.P = take(L * D.H * T * T);
+    t.tq = take(L * T * D.r);
+    t.tk = take(L * T * D.r);
+    t.tv = take(L * T * D.r);
+    t.to = take(L * T * D.r);
+    t.xmid = take(L * T * d);
+    t.inv2 = take(L * T);
+    t.n2 = take(L * T * d);
+    t.u = take(L * T * D.F);
+    t.y = take(T * d);
+    t.ao = take(T * d);
+    t.hbuf = take(T * D.F);
+    t.invf = take(T);
+    t.hf = take(T * d);
+    t.logits = take(T * D.V);
+    t.tlm = take(T * D.r);
+    t.rowloss = take(T);
+    t.dx = take(T * d);
+    t.dskip = take((int64_t)(D.enc > 0 ? D.enc : 1) * T * d);
+    t.dd = take(T * d);
+    t.dh = take(T * D.F);
+    t.dn = take(T * d);
+    t.dn2 = take(T * d);
+    t.dqkv = take(T * D.qn);
+    t.dqr = take(T * d);
+    t.dkr = take(T * D.kvd);
+    t.dy = take(T * d);
+    t.dao = take(T * d);
+    t.dS = take((int64_t)D.H * T * T);
+    t.dt = take(T * D.r);
+    t.grad = nullptr;  // set by caller (lora_floats)
+    t.red = take(1024);
+    if (tp) *tp = t;
+    return off;
+}
+
+// ---- forward row kernels -------------------------------------------------
+
+__global__ void t_embed(TD D, const int32_t *tok, altxs_qmat emb, float *x0, float *x) {
+    __shared__ float red[32];
+    const int t = blockIdx.x;
+    const int tk = tok[t];
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < D.d; k += blockDim.x) {
+        const float v = (tk >= 0 && tk < D.V) ? qmat_elem(emb, tk, k) : 0.0f;
+        x0[(int64_t)t * D.d + k] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
+    const float inv = rms_inv(block_sum(ss, red), D.d);
+    __syncthreads();
+    for (int k = threadIdx.x; k < D.d; k += blockDim.x) {
+        const float v = __fmul_rn(x0[(int64_t)t * D.d + k], inv);
+        x0[(int64_t)t * D.d + k] = v;
+        x[(int64_t)t * D.d + k] = v;
+    }
+}
+
+__global__ void t_prenorm(TD D, int l, Tape tp, altxs_weights w, int skip_gates) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, d = D.d;
+    float *x = tp.x + (int64_t)t * d;
+    const float *x0 = tp.x0 + (int64_t)t * d;
+    const float *mix = w.resid_mix + (int64_t)l * 2 * d;
+    const int j = l - D.enc;
+    const bool skip = j >= 0 && j < D.nskip;
+    const float *sk = skip ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
+    float *xin = tp.xin + ((int64_t)l * D.T + t) * d;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float xv = x[k];
+        if (skip) {
+            const float scaled = __fmul_rn(w.skip_weights[(int64_t)j * d + k], sk[k]);
+            xv = skip_gates ? lerp_t(scaled, xv, sigmoidf_(w.skip_gates[(int64_t)j * d + k])) : __fadd_rn(xv, scaled);
+        }
+        const float v = __fadd_rn(__fmul_rn(mix[k], xv), __fmul_rn(mix[d + k], x0[k]));
+        xin[k] = v;
+        x[k] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
+    const float inv = rms_inv(block_sum(ss, red), d);
+    const float ln = w.ln_scale[l];
+    if (threadIdx.x == 0) tp.inv1[(int64_t)l * D.T + t] = inv;
+    __syncthreads();
+    float *nr = tp.n + ((int64_t)l * D.T + t) * d;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) nr[k] = __fmul_rn(__fmul_rn(xin[k], inv), ln);
+}
+
+// per-head RMSNorm + RoPE (positions 0..T-1) + q_gain; one warp per head
+__global__ void t_qk(TD D, int l, Tape tp, altxs_weights w) {
+    const int t = blockIdx.x, hd = D.hd, half = D.rd / 2;
+    const float *qkv = tp.qkv + ((int64_t)l * D.T + t) * D.qn;
+    const float *cs = w.rope_cos + (int64_t)t * half, *sn = w.rope_sin + (int64_t)t * half;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int h = wid; h < D.H + D.Hkv; h += nw) {
+        const float *e = qkv + (int64_t)h * hd;
+        float ss = 0.0f;
+        for (int k = lane; k < hd; k += 32) ss = __fmaf_rn(e[k], e[k], ss);
+        const float inv = rms_inv(warp_sum(ss), hd);
+        if (lane == 0) tp.hinv[((int64_t)l * D.T + t) * (D.H + D.Hkv) + h] = inv;
+        float *dst;
+        float g = 1.0f;
+        if (h < D.H) {
+            dst = tp.qr + ((int64_t)l * D.T + t) * D.d + (int64_t)h * hd;
+            g = w.q_gain[(int64_t)l * D.H + h];
+        } else {
+            dst = tp.kr + ((int64_t)l * D.T + t) * D.kvd + (int64_t)(h - D.H) * hd;
+        }
+        for (int k = lane; k < hd; k += 32) {
+            const float a = __fmul_rn(e[k], inv);
+            float r = a;
+            if (k < D.rd) {
+                if (k < half) {
+                    r = __fadd_rn(__fmul_rn(a, cs[k]), __fmul_rn(__fmul_rn(e[k + half], inv), sn[k]));
+                } else {
+                    r = __fadd_rn(__fmul_rn(__fmul_rn(e[k - half], inv), -sn[k - half]), __fmul_rn(a, cs[k - half]));
+                }
+            }
+            dst[k] = h < D.H ? __fmul_rn(r, g) : r;
+        }
+    }
+}
+
+// causal softmax over rows of S (in place): one block per (head, t)
+__global__ void t_softmax(TD D, float *P) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;  // h * T + t
+    const int t = row % D.T;
+    float *s = P + (int64_t)row * D.T;
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j <= t; j += blockDim.x) m = fmaxf(m, s[j]);
+    m = block_max(m, red);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j < D.T; j += blockDim.x) {
+        const float e = j <= t ? expf(__fsub_rn(s[j], m)) : 0.0f;
+        s[j] = e;
+        sum = __fadd_rn(sum, e);
+    }
+    sum = block_sum(sum, red);
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, sum);
+    for (int j = threadIdx.x; j < D.T; j += blockDim.x) s[j] = __fmul_rn(s[j], inv);
+}
+
+__global__ void t_post_attn(TD D, int l, Tape tp, altxs_weights w) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, d = D.d;
+    const float *xin = tp.xin + ((int64_t)l * D.T + t) * d;
+    const float *ao = tp.ao + (int64_t)t * d;
+    const float *as = w.attn_scale + (int64_t)l * d;
+    float *xm = tp.xmid + ((int64_t)l * D.T + t) * d;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float v = __fadd_rn(xin[k], __fmul_rn(as[k], ao[k]));
+        xm[k] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
+    const float inv = rms_inv(block_sum(ss, red), d);
+    const float ln = w.ln_scale[l];
+    if (threadIdx.x == 0) tp.inv2[(int64_t)l * D.T + t] = inv;
+    __syncthreads();
+    float *n2 = tp.n2 + ((int64_t)l * D.T + t) * d;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) n2[k] = __fmul_rn(__fmul_rn(xm[k], inv), ln);
+}
+
+__global__ void t_leaky(int64_t n, const float *u, float *h) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = u[i];
+    const float a = v >= 0.0f ? v : __fmul_rn(v, 0.5f);
+    h[i] = __fmul_rn(a, a);
+}
+
+__global__ void t_final(TD D, Tape tp) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, d = D.d;
+    const float *x = tp.x + (int64_t)t * d;
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) ss = __fmaf_rn(x[k], x[k], ss);
+    const float inv = rms_inv(block_sum(ss, red), d);
+    if (threadIdx.x == 0) tp.invf[t] = inv;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) tp.hf[(int64_t)t * d + k] = __fmul_rn(x[k], inv);
+}
+
+// softcap + cross-entropy; logits row -> d(loss)/d(raw logits) in place
+__global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap) {
+    __shared__ float red[32];
+    const int t = blockIdx.x;
+    float *l = tp.logits + (int64_t)t * D.V;
+    const int y = tgt[t];
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
+        const float z = __fmul_rn(cap, tanhf(__fdiv_rn(l[j], cap)));
+        m = fmaxf(m, z);
+    }
+    m = block_max(m, red);
+    __syncthreads();
+    float s = 0.0f;
+    for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
+        const float z = __fmul_rn(cap, tanhf(__fdiv_rn(l[j], cap)));
+        s = __fadd_rn(s, expf(__fsub_rn(z, m)));
+    }
+    s = block_sum(s, red);
+    __syncthreads();
+    const float lse = __fadd_rn(m, logf(s));
+    const float invT = __fdiv_rn(1.0f, (float)D.T);
+    for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
+        const float th = tanhf(__fdiv_rn(l[j], cap));
+        const float z = __fmul_rn(cap, th);
+        if (j == y) tp.rowloss[t] = __fsub_rn(lse, z);
+        float p = __fdiv_rn(expf(__fsub_rn(z, m)), s);
+        if (j == y) p = __fsub_rn(p, 1.0f);
+        l[j] = __fmul_rn(__fmul_rn(p, invT), __fsub_rn(1.0f, __fmul_rn(th, th)));
+    }
+}
+
+__global__ void t_loss_sum(int T, const float *rowloss, float *out) {
+    __shared__ float red[32];
+    float s = 0.0f;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) s = __fadd_rn(s, rowloss[t]);
+    s = block_sum(s, red);
+    if (threadIdx.x == 0 && out) *out = __fdiv_rn(s, (float)T);
+}
+
+// ---- backward row kernels -----------------------------------------------
+
+// out = (add ? add : 0) + d/dx[rms(x) * scale] applied to g
+__global__ void t_rms_bwd(int d, const float *g, int64_t ldg, const float *x, const float *inv,
+                          const float *scale_ptr, const float *add, float *out) {
+    __shared__ float red[32];
+    const int t = blockIdx.x;
+    const float scale = scale_ptr ? *scale_ptr : 1.0f;
+    const float *gr = g + (int64_t)t * ldg, *xr = x + (int64_t)t * d;
+    const float iv = inv[t];
+    float dot = 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) dot = __fmaf_rn(__fmul_rn(gr[k], scale), xr[k], dot);
+    dot = block_sum(dot, red);
+    const float c = __fdiv_rn(__fmul_rn(__fmul_rn(iv, iv), __fmul_rn(iv, dot)), (float)d);
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float v = __fsub_rn(__fmul_rn(iv, __fmul_rn(gr[k], scale)), __fmul_rn(xr[k], c));
+        if (add) v = __fadd_rn(add[(int64_t)t * d + k], v);
+        out[(int64_t)t * d + k] = v;
+    }
+}
+
+__global__ void t_scale_cols(int64_t n, int d, const float *a, const float *col, float *out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    out[i] = __fmul_rn(a[i], col[i % d]);
+}
+
+__global__ void t_leaky_bwd(int64_t n, const float *dh, const float *u, float *du) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = u[i];
+    du[i] = __fmul_rn(dh[i], v >= 0.0f ? __fmul_rn(2.0f, v) : __fmul_rn(0.5f, v));
+}
+
+// dS = P * (dP - sum_j dP P) * scale, per (head, row), in place over dP
+__global__ void t_softmax_bwd(TD D, const float *P, float *dS, float scale) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const float *p = P + (int64_t)row * D.T;
+    float *g = dS + (int64_t)row * D.T;
+    float s = 0.0f;
+    for (int j = threadIdx.x; j < D.T; j += blockDim.x) s = __fmaf_rn(g[j], p[j], s);
+    s = block_sum(s, red);
+    for (int j = threadIdx.x; j < D.T; j += blockDim.x) g[j] = __fmul_rn(__fmul_rn(p[j], __fsub_rn(g[j], s)), scale);
+}
+
+// q/k: undo gain, RoPE transpose, per-head RMSNorm backward -> dqkv
+__global__ void t_qk_bwd(TD D, int l, Tape tp, altxs_weights w) {
+    const int t = blockIdx.x, hd = D.hd, half = D.rd / 2;
+    const float *qkv = tp.qkv + ((int64_t)l * D.T + t) * D.qn;
+    const float *cs = w.rope_cos + (int64_t)t * half, *sn = w.rope_sin + (int64_t)t * half;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float *dq = tp.dqkv + (int64_t)t * D.qn;
+    for (int h = wid; h < D.H + D.Hkv; h += nw) {
+        const float *e = qkv + (int64_t)h * hd;
+        const float inv = tp.hinv[((int64_t)l * D.T + t) * (D.H + D.Hkv) + h];
+        const float *gsrc;
+        float g = 1.0f;
+        if (h < D.H) {
+            gsrc = tp.dqr + (int64_t)t * D.d + (int64_t)h * hd;
+            g = w.q_gain[(int64_t)l * D.H + h];
+        } else {
+            gsrc = tp.dkr + (int64_t)t * D.kvd + (int64_t)(h - D.H) * hd;
+        }
+        // grad wrt the normed (pre-rope) vector a_k, then RMS backward
+        float dot = 0.0f;
+        float ga[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = lane + 32 * u;
+            float v = 0.0f;
+            if (k < hd) {
+                if (k < D.rd) {
+                    if (k < half) {  // a_k feeds out_k (cos) and out_{k+half} (-sin)
+                        v = __fsub_rn(__fmul_rn(__fmul_rn(gsrc[k], g), cs[k]), __fmul_rn(__fmul_rn(gsrc[k + half], g), sn[k]));
+                    } else {  // a_k feeds out_{k-half} (sin) and out_k (cos)
+                        v = __fadd_rn(__fmul_rn(__fmul_rn(gsrc[k - half], g), sn[k - half]), __fmul_rn(__fmul_rn(gsrc[k], g), cs[k - half]));
+                    }
+                } else {
+                    v = __fmul_rn(gsrc[k], g);
+                }
+                dot = __fmaf_rn(v, e[k], dot);
+            }
+            ga[u] = v;
+        }
+        dot = warp_sum(dot);
+        const float c = __fdiv_rn(__fmul_rn(__fmul_rn(inv, inv), __fmul_rn(inv, dot)), (float)hd);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = lane + 32 * u;
+            if (k < hd) dq[(int64_t)h * hd + k] = __fsub_rn(__fmul_rn(inv, ga[u]), __fmul_rn(e[k], c));
+        }
+    }
+}
+
+// residual mix and skip lerp backward: dx <- d(loss)/d(layer input)
+__global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates) {
+    const int t = blockIdx.x, d = D.d;
+    const float *mix = w.resid_mix + (int64_t)l * 2 * d;
+    const int j = l - D.enc;
+    const bool skip = j >= 0 && j < D.nskip;
+    float *dx = tp.dx + (int64_t)t * d;
+    float *ds = skip ? tp.dskip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float gx = __fmul_rn(dx[k], mix[k]);
+        if (skip) {
+            const float sw = w.skip_weights[(int64_t)j * d + k];
+            if (skip_gates) {
+                const float gg = sigmoidf_(w.skip_gates[(int64_t)j * d + k]);
+                ds[k] = __fmul_rn(__fmul_rn(gx, __fsub_rn(1.0f, gg)), sw);
+                dx[k] = __fmul_rn(gx, gg);
+            } else {
+                ds[k] = __fmul_rn(gx, sw);
+                dx[k] = gx;
+            }
+        } else {
+            dx[k] = gx;
+        }
+    }
+}
+
+__global__ void t_add(int64_t n, float *a, const float *b) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) a[i] = __fadd_rn(a[i], b[i]);
+}
+
+// global grad norm: partial sums over fixed chunks, then a single-block sum
+__global__ void t_sqsum_part(int64_t n, const float *g, float *part) {
+    __shared__ float red[32];
+    const int64_t chunk = (n + gridDim.x - 1) / gridDim.x;
+    const int64_t b0 = (int64_t)blockIdx.x * chunk, b1 = b0 + chunk < n ? b0 + chunk : n;
+    float s = 0.0f;
+    for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) s = __fmaf_rn(g[i], g[i], s);
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+__global__ void t_adam(int64_t n, float *p, const float *g, float *m, float *v, const float *part, int nparts,
+                       altxs_ttt_hparams hp, int step) {
+    __shared__ float coef_s;
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < nparts; ++i) s = __fadd_rn(s, part[i]);
+        const float norm = __fsqrt_rn(s);
+        const float c = __fdiv_rn(hp.grad_clip, __fadd_rn(norm, 1e-6f));
+        coef_s = c < 1.0f ? c : 1.0f;
+    }
+    __syncthreads();
+    const float coef = coef_s;
+    const float bc1 = 1.0f - powf(hp.beta1, (float)step);
+    const float bc2 = 1.0f - powf(hp.beta2, (float)step);
+    const float step_size = __fdiv_rn(hp.lr, bc1);
+    const float bc2s = __fsqrt_rn(bc2);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float gi = __fmul_rn(g[i], coef);
+        float pi = p[i];
+        if (hp.weight_decay != 0.0f) pi = __fmul_rn(pi, __fsub_rn(1.0f, __fmul_rn(hp.lr, hp.weight_decay)));
+        const float mi = lerp_t(m[i], gi, __fsub_rn(1.0f, hp.beta1));  // exp_avg.lerp_(grad, 1 - beta1)
+        const float vi = __fadd_rn(__fmul_rn(v[i], hp.beta2), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, hp.beta2), gi), gi));
+        const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), bc2s), hp.eps);
+        p[i] = __fsub_rn(pi, __fmul_rn(step_size, __fdiv_rn(mi, den)));
+        m[i] = mi;
+        v[i] = vi;
+    }
+}
+
+inline int g1(int64_t n, int t) { return (int)((n + t - 1) / t); }
+
+// GEMM helper with the common fields
+inline GemmArgs G(const float *A, int64_t lda, int tA, const float *B, int64_t ldb, int tB, float *C, int64_t ldc,
+                  int M, int N, int K, float alpha = 1.0f, float beta = 0.0f) {
+    GemmArgs g{};
+    g.A = A;
+    g.B = B;
+    g.C = C;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.lda = lda;
+    g.ldb = ldb;
+    g.ldc = ldc;
+    g.tA = tA;
+    g.tB = tB;
+    g.batch = 1;
+    g.adiv = 1;
+    g.bdiv = 1;
+    g.alpha = alpha;
+    g.beta = beta;
+    return g;
+}
+
+#define TRY(x)                 \
+    do {                       \
+        int rc_ = (x);         \
+        if (rc_) return rc_;   \
+    } while (0)
+
+// LoRA forward for one target: t = X A^T ; Y += s * t B^T
+int lora_fwd(const float *X, int din, const float *A, const float *B, int dout, int r, float s, float *t, float *Y,
+             int64_t ldy, int T, cudaStream_t st) {
+    TRY(launch_gemm(G(X, din, 0, A, din, 1, t, r, T, r, din), st));
+    TRY(launch_gemm(G(t, r, 0, B, r, 1, Y, ldy, T, dout, r, s, 1.0f), st));
+    return ALTXS_OK;
+}
+
+// LoRA backward: grads dA, dB (written), dX += dt A (if dX)
+int lora_bwd(const float *X, int din, const float *A, const float *B, int dout, int r, float s, const float *t,
+             const float *Gy, int64_t ldg, float *dA, float *dB, float *dt, float *dX, int T, cudaStream_t st) {
+    TRY(launch_gemm(G(Gy, ldg, 1, t, r, 0, dB, r, dout, r, T, s), st));        // dB = s G^T t
+    TRY(launch_gemm(G(Gy, ldg, 0, B, r, 0, dt, r, T, r, dout, s), st));        // dt = s G B
+    TRY(launch_gemm(G(dt, r, 1, X, din, 0, dA, din, r, din, T), st));          // dA = dt^T X
+    if (dX) TRY(launch_gemm(G(dt, r, 0, A, din, 0, dX, din, T, din, r, 1.0f, 1.0f), st));  // dX += dt A
+    return ALTXS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T) {
+    TD D{};
+    if (!desc || fill(*desc, T, D)) return -1;
+    return carve(D, nullptr, nullptr) + align_up(lora_offsets(*desc).total * 4, 256);
+}
+
+int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_ttt_hparams *hp,
+                     const int32_t *tokens, int T, float *lora, float *adam_m, float *adam_v, int step,
+                     float *loss_out, void *workspace, int64_t workspace_bytes, altxs_stream_t stream) {
+    if (!desc || !w || !hp || !tokens || !lora || !adam_m || !adam_v || !workspace || step < 1) return ALTXS_EINVAL;
+    TD D{};
+    TRY(fill(*desc, T, D));
+    if (workspace_bytes < altxs_ttt_workspace_bytes(desc, T)) return ALTXS_EINVAL;
+    if (w->rope_positions < T) return ALTXS_EINVAL;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    Tape tp{};
+    const int64_t tape_bytes = carve(D, workspace, &tp);
+    tp.grad = reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + tape_bytes);
+    const LoraOff lo = lora_offsets(*desc);
+    const int mask = desc->lora_mask;
+    const float s = desc->lora_scale;
+    const int Tn = D.T, d = D.d, r = D.r;
+    const int32_t *tok = tokens, *tgt = tokens + 1;
+    const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
+    cudaMemsetAsync(tp.grad, 0, lo.total * 4, st);
+
+    // ---------------- forward ----------------
+    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, tp.x0, tp.x));
+    for (int l = 0; l < D.L; ++l) {
+        ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, tp, *w, desc->skip_gates));
+        const float *n = tp.n + (int64_t)l * Tn * d;
+        float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
+        QmmArgs a{};
+        a.X = n;
+        a.ldx = d;
+        a.M = Tn;
+        a.W = w->qkv;
+        a.row0 = l * D.qn;
+        a.N = D.qn;
+        a.K = d;
+        a.Y = qkv;
+        a.ldy = D.qn;
+        a.epi = kEpiStore;
+        TRY(launch_qmm(a, st));
+        TRY(lora_fwd(n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, r, s,
+                     tp.tq + (int64_t)l * Tn * r, qkv, D.qn, Tn, st));
+        if (mask & 2)
+            TRY(lora_fwd(n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, r, s,
+                         tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn, Tn, st));
+        TRY(lora_fwd(n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, r, s,
+                     tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn, Tn, st));
+        ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, tp, *w));
+        float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
+        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        {
+            GemmArgs g = G(qr, D.H * D.hd, 0, kr, D.kvd, 1, P, Tn, Tn, Tn, D.hd, att_scale);
+            g.batch = D.H;
+            g.sA = D.hd;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = (int64_t)Tn * Tn;
+            TRY(launch_gemm(g, st));
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, P));
+        {
+            GemmArgs g = G(P, Tn, 0, qkv + d + D.kvd, D.qn, 0, tp.y, d, Tn, D.hd, Tn);
+            g.batch = D.H;
+            g.sA = (int64_t)Tn * Tn;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = D.hd;
+            TRY(launch_gemm(g, st));
+        }
+        a.X = tp.y;
+        a.W = w->o;
+        a.row0 = l * d;
+        a.N = d;
+        a.Y = tp.ao;
+        a.ldy = d;
+        TRY(launch_qmm(a, st));
+        if (mask & 8)
+            TRY(lora_fwd(n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, r, s,
+                         tp.to + (int64_t)l * Tn * r, tp.ao, d, Tn, st));
+        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w));
+        float *u = tp.u + (int64_t)l * Tn * D.F;
+        a.X = tp.n2 + (int64_t)l * Tn * d;
+        a.W = w->up;
+        a.row0 = l * D.F;
+        a.N = D.F;
+        a.Y = u;
+        a.ldy = D.F;
+        TRY(launch_qmm(a, st));
+        ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
+        a.X = tp.hbuf;
+        a.ldx = D.F;
+        a.W = w->down;
+        a.row0 = l * d;
+        a.N = d;
+        a.K = D.F;
+        a.Y = tp.x;
+        a.ldy = d;
+        a.epi = kEpiResid;
+        a.R = tp.xmid + (int64_t)l * Tn * d;
+        a.ldr = d;
+        a.colscale = w->mlp_scale + (int64_t)l * d;
+        a.Y2 = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
+        a.ldy2 = d;
+        TRY(launch_qmm(a, st));
+    }
+    ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp));
+    {
+        QmmArgs a{};
+        a.X = tp.hf;
+        a.ldx = d;
+        a.M = Tn;
+        a.W = w->emb;
+        a.row0 = 0;
+        a.N = D.V;
+        a.K = d;
+        a.Y = tp.logits;
+        a.ldy = D.V;
+        a.epi = kEpiStore;
+        TRY(launch_qmm(a, st));
+    }
+    if (mask & 16)
+        TRY(lora_fwd(tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, r, s, tp.tlm, tp.logits, D.V, Tn, st));
+    ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, desc->logit_softcap));
+    ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, tp.rowloss, loss_out));
+
+    // ---------------- backward ----------------
+    // LM head: dhf = dlogits E + LoRA
+    {
+        QmmTArgs q{};
+        q.dY = tp.logits;
+        q.lddy = D.V;
+        q.M = Tn;
+        q.W = w->emb;
+        q.row0 = 0;
+        q.N = D.V;
+        q.K = d;
+        q.dX = tp.dn;
+        q.lddx = d;
+        q.alpha = 1.0f;
+        q.beta = 0.0f;
+        TRY(launch_qmm_t(q, st));
+    }
+    if (mask & 16)
+        TRY(lora_bwd(tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, r, s, tp.tlm, tp.logits, D.V, tp.grad + lo.lmA,
+                     tp.grad + lo.lmB, tp.dt, tp.dn, Tn, st));
+    ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.x, tp.invf, nullptr, nullptr, tp.dx));
+    for (int l = D.L - 1; l >= 0; --l) {
+        if (l < D.enc) {
+            ALTXS_LAUNCH(kKTtt, st, t_add<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                        (int64_t)Tn * d, tp.dx, tp.dskip + (int64_t)l * Tn * d));
+        }
+        // MLP
+        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                    (int64_t)Tn * d, d, tp.dx, w->mlp_scale + (int64_t)l * d, tp.dd));
+        {
+            QmmTArgs q{};
+            q.dY = tp.dd;
+            q.lddy = d;
+            q.M = Tn;
+            q.W = w->down;
+            q.row0 = l * d;
+            q.N = d;
+            q.K = D.F;
+            q.dX = tp.dh;
+            q.lddx = D.F;
+            q.alpha = 1.0f;
+            TRY(launch_qmm_t(q, st));
+        }
+        const float *u = tp.u + (int64_t)l * Tn * D.F;
+        ALTXS_LAUNCH(kKTtt, st, t_leaky_bwd<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
+                                    (int64_t)Tn * D.F, tp.dh, u, tp.dh));
+        {
+            QmmTArgs q{};
+            q.dY = tp.dh;
+            q.lddy = D.F;
+            q.M = Tn;
+            q.W = w->up;
+            q.row0 = l * D.F;
+            q.N = D.F;
+            q.K = d;
+            q.dX = tp.dn2;
+            q.lddx = d;
+            q.alpha = 1.0f;
+            TRY(launch_qmm_t(q, st));
+        }
+        // dxmid = dx + rms_bwd(dn2 * ln)
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Tn * d,
+                                                             tp.inv2 + (int64_t)l * Tn, w->ln_scale + l, tp.dx, tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                    (int64_t)Tn * d, d, tp.dx, w->attn_scale + (int64_t)l * d, tp.dao));
+        const float *n = tp.n + (int64_t)l * Tn * d;
+        // dn accumulates: o-LoRA, then qkv
+        cudaMemsetAsync(tp.dn, 0, (size_t)Tn * d * 4, st);
+        if (mask & 8)
+            TRY(lora_bwd(n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, r, s,
+                         tp.to + (int64_t)l * Tn * r, tp.dao, d, tp.grad + lo.oA + l * lo.o_stride,
+                         tp.grad + lo.oB + l * lo.o_stride, tp.dt, tp.dn, Tn, st));
+        {
+            QmmTArgs q{};
+            q.dY = tp.dao;
+            q.lddy = d;
+            q.M = Tn;
+            q.W = w->o;
+            q.row0 = l * d;
+            q.N = d;
+            q.K = d;
+            q.dX = tp.dy;
+            q.lddx = d;
+            q.alpha = 1.0f;
+            TRY(launch_qmm_t(q, st));
+        }
+        // attention backward
+        const float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
+        const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
+        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        {
+            GemmArgs g = G(tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy V^T
+            g.batch = D.H;
+            g.sA = D.hd;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = (int64_t)Tn * Tn;
+            TRY(launch_gemm(g, st));
+        }
+        for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
+            GemmArgs g = G(P + (int64_t)gi * Tn * Tn, Tn, 1, tp.dy + gi * D.hd, d, 0, tp.dqkv + d + D.kvd, D.qn,
+                           Tn, D.hd, Tn, 1.0f, gi ? 1.0f : 0.0f);
+            g.batch = D.Hkv;
+            g.sA = (int64_t)D.G * Tn * Tn;
+            g.sB = (int64_t)D.G * D.hd;
+            g.sC = D.hd;
+            TRY(launch_gemm(g, st));
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_softmax_bwd<<<D.H * Tn, 256, 0, st>>>(D, P, tp.dS, att_scale));
+        {
+            GemmArgs g = G(tp.dS, Tn, 0, kr, D.kvd, 0, tp.dqr, d, Tn, D.hd, Tn);  // dq = dS k
+            g.batch = D.H;
+            g.sA = (int64_t)Tn * Tn;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = D.hd;
+            TRY(launch_gemm(g, st));
+        }
+        for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
+            GemmArgs g = G(tp.dS + (int64_t)gi * Tn * Tn, Tn, 1, qr + gi * D.hd, d, 0, tp.dkr, D.kvd, Tn, D.hd, Tn,
+                           1.0f, gi ? 1.0f : 0.0f);
+            g.batch = D.Hkv;
+            g.sA = (int64_t)D.G * Tn * Tn;
+            g.sB = (int64_t)D.G * D.hd;
+            g.sC = D.hd;
+            TRY(launch_gemm(g, st));
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, tp, *w));
+        // LoRA q/k/v grads and their dn contributions
+        TRY(lora_bwd(n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, r, s,
+                     tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, tp.grad + lo.qA + l * lo.q_stride,
+                     tp.grad + lo.qB + l * lo.q_stride, tp.dt, tp.dn, Tn, st));
+        if (mask & 2)
+            TRY(lora_bwd(n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, r, s,
+                         tp.tk + (int64_t)l * Tn * r, tp.dqkv + d, D.qn, tp.grad + lo.kA + l * lo.k_stride,
+                         tp.grad + lo.kB + l * lo.k_stride, tp.dt, tp.dn, Tn, st));
+        TRY(lora_bwd(n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, r, s,
+                     tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, tp.grad + lo.vA + l * lo.v_stride,
+                     tp.grad + lo.vB + l * lo.v_stride, tp.dt, tp.dn, Tn, st));
+        {
+            QmmTArgs q{};
+            q.dY = tp.dqkv;
+            q.lddy = D.qn;
+            q.M = Tn;
+            q.W = w->qkv;
+            q.row0 = l * D.qn;
+            q.N = D.qn;
+            q.K = d;
+            q.dX = tp.dn;
+            q.lddx = d;
+            q.alpha = 1.0f;
+            q.beta = 1.0f;
+            TRY(launch_qmm_t(q, st));
+        }
+        // dxin = dxmid + rms_bwd(dn * ln); then mix / skip backward
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Tn * d,
+                                                             tp.inv1 + (int64_t)l * Tn, w->ln_scale + l, tp.dx, tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_mix_bwd<<<Tn, 128, 0, st>>>(D, l, tp, *w, desc->skip_gates));
+    }
+    // ---------------- clip + AdamW ----------------
+    const int nparts = 256;
+    ALTXS_LAUNCH(kKTtt, st, t_sqsum_part<<<nparts, 256, 0, st>>>(lo.total, tp.grad, tp.red));
+    ALTXS_LAUNCH(kKTtt, st, t_adam<<<g1(lo.total, 1024), 1024, 0, st>>>(lo.total, lora, tp.grad, adam_m, adam_v,
+                                                                         tp.red, nparts, *hp, step));
+    return ALTXS_OK;
+}
+
+}  // extern "C"

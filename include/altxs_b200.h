@@ -194,6 +194,28 @@ int64_t altxs_lora_floats(const altxs_model_desc *desc);
 int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b, int mode,
                altxs_stream_t stream);
 
+/* ---- test-time LoRA update ------------------------------------------------ */
+
+typedef struct altxs_ttt_hparams {
+    float lr, beta1, beta2, eps, weight_decay, grad_clip;
+} altxs_ttt_hparams;
+
+/* Workspace for one update over a T-token window (bytes). */
+int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T);
+
+/* One boundary update of one stream's adapters: teacher-forced forward over
+ * tokens[0..T) (positions 0..T-1, causal), targets tokens[1..T], tied logits
+ * with tanh softcap, mean cross-entropy, backward into the adapters only,
+ * global-norm clip, AdamW step number `step` (1-based).  lora / adam_m /
+ * adam_v: device [altxs_lora_floats] in the arena layout; loss_out: device
+ * float or NULL.  Replaces the lora branch of online_retrain
+ * (compress.py:1104-1137: ce_with_lora, backward, clip_grad_norm_, AdamW
+ * step; ttt_lora.py:124-179, 258-374) on the window of _window_xy
+ * (compress.py:301-320). */
+int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_ttt_hparams *hp,
+                     const int32_t *tokens, int T, float *lora, float *adam_m, float *adam_v, int step,
+                     float *loss_out, void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these
  * give the benchmark per-kernel device time measured live on the launch
