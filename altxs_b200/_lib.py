@@ -22,7 +22,7 @@ EXPORTS = (
     "altxs_ac_begin_decode", "altxs_ac_decode_probs", "altxs_ac_decode_cum",
     "altxs_cdf_from_logits", "altxs_workspace_bytes", "altxs_lora_floats", "altxs_step",
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
-    "altxs_ttt_workspace_bytes", "altxs_ttt_update",
+    "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -108,6 +108,9 @@ def lib():
             "altxs_launch_count": (i64, []),
             "altxs_profile": (C.c_int, [C.c_int]),
             "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
+            "altxs_step_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int,
+                                             vp]),
+            "altxs_step_noalloc_max_bytes": (i64, []),
             "altxs_ttt_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.c_int]),
             "altxs_ttt_update": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(TttHparams), vp,
                                            C.c_int, vp, vp, vp, C.c_int, vp, vp, i64, vp]),

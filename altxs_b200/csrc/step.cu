@@ -9,6 +9,8 @@
 // logits with tanh softcap (model.py:1460-1500), the integer CDF and the coder.
 #include <math.h>
 
+#include <mutex>
+
 #include "coder.cuh"
 #include "model.cuh"
 #include "prof.cuh"
@@ -725,3 +727,60 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of altxs_step.
+//
+// The step's scratch (activations, attention split partials, logits) normally
+// lives in a workspace the caller allocates.  Some callers cannot allocate
+// device memory at all: a host framework that owns the whole device budget
+// through its own allocator and refuses allocations from plugins, or a
+// latency-critical caller that must not risk the device-wide synchronisation
+// cudaMalloc/cudaFree may imply.  For them the scratch below is a fixed
+// array in this module's device memory: every GPU that loads the library
+// holds these 16 MiB until the process exits, and no call allocates.
+// Calls share the one array, so calls that overlap on a GPU (two streams,
+// two host threads) race on it; run them one after another.  No scratch value
+// needs to start at zero: the step writes every scratch value it reads.
+
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 16ll << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[64] = {};
+
+// Device address of the scratch array on the current device, resolved once
+// per device with that device current.
+int noalloc_scratch(void **out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ALTXS_ECUDA;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) return ALTXS_ECUDA;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return ALTXS_OK;
+}
+}  // namespace
+
+extern "C" int64_t altxs_step_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int altxs_step_noalloc(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b,
+                                  int mode, altxs_stream_t stream) {
+    if (!desc || !w || !b) return ALTXS_EINVAL;
+    Dims D{};
+    const int rc = fill_dims(desc, b->n_streams, D);
+    if (rc) return rc;
+    if (ws_size(D) > kNoAllocScratchBytes) return ALTXS_ENOSPC;  // too many streams for the fixed scratch
+    void *scratch = nullptr;
+    const int rs = noalloc_scratch(&scratch);
+    if (rs) return rs;
+    altxs_batch bb = *b;
+    bb.workspace = scratch;
+    bb.workspace_bytes = kNoAllocScratchBytes;
+    return altxs_step(desc, w, &bb, mode, stream);
+}

@@ -176,6 +176,24 @@ typedef struct altxs_batch {
     int64_t workspace_bytes;
 } altxs_batch;
 
+/* Allocation-free altxs_step for callers that cannot allocate device memory
+ * (a host framework that owns the device budget through its own allocator
+ * and refuses allocations from plugins, or a latency-critical caller that
+ * must not risk the device-wide synchronisation an allocation may imply).
+ * No counterpart in the reference.  Same arguments and results as
+ * altxs_step, but b->workspace / b->workspace_bytes are ignored: the scratch
+ * is a fixed 16 MiB array inside the library's device image (held on every
+ * GPU that loads the library until exit; altxs_step_noalloc_max_bytes()).
+ * Batches whose scratch would exceed it return ALTXS_ENOSPC (at the 33M
+ * shapes, about 120 streams fit).  The first call on a device resolves the
+ * array's device address with that device current; make that first call
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on one GPU race, so issue them one after another.  Nothing in the scratch
+ * needs to start at zero. */
+int altxs_step_noalloc(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b, int mode,
+                       altxs_stream_t stream);
+int64_t altxs_step_noalloc_max_bytes(void);
+
 /* Workspace needed by altxs_step for n streams (bytes). */
 int64_t altxs_workspace_bytes(const altxs_model_desc *desc, int n_streams);
 
