@@ -23,6 +23,7 @@ EXPORTS = (
     "altxs_cdf_from_logits", "altxs_workspace_bytes", "altxs_lora_floats", "altxs_step",
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
+    "altxs_dequant",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -66,6 +67,11 @@ class Weights(C.Structure):
 class TttHparams(C.Structure):
     _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
                 ("weight_decay", C.c_float), ("grad_clip", C.c_float)]
+
+
+class DenseWeights(C.Structure):
+    _fields_ = [("emb", C.c_void_p), ("qkv", C.c_void_p), ("o", C.c_void_p), ("up", C.c_void_p),
+                ("down", C.c_void_p)]
 
 
 class Batch(C.Structure):
@@ -112,8 +118,10 @@ def lib():
                                              vp]),
             "altxs_step_noalloc_max_bytes": (i64, []),
             "altxs_ttt_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.c_int]),
-            "altxs_ttt_update": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(TttHparams), vp,
-                                           C.c_int, vp, vp, vp, C.c_int, vp, vp, i64, vp]),
+            "altxs_ttt_update": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(DenseWeights),
+                                           C.POINTER(TttHparams), vp, C.c_int, vp, vp, vp, C.c_int, vp, vp, i64,
+                                           vp]),
+            "altxs_dequant": (C.c_int, [C.POINTER(QMat), vp, i64, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

@@ -5,54 +5,50 @@
 namespace altxs {
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 16, NT = 256;
+constexpr int BM = 64, BN = 64, BK = 32, NT = 256;
 
-__global__ void __launch_bounds__(NT) k_gemm(GemmArgs g) {
-    __shared__ __align__(16) float As[BK][BM + 4];
-    __shared__ __align__(16) float Bs[BK][BN + 4];
-    const int b = blockIdx.z;
-    const float *A = g.A + (int64_t)(b / g.adiv) * g.sA;
-    const float *B = g.B + (int64_t)(b / g.bdiv) * g.sB;
-    float *C = g.C + (int64_t)b * g.sC;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+// One (m0, n0) tile of one batch entry over the K range [kb, ke).  The raw
+// accumulators are returned in acc (alpha/beta applied by the caller).
+__device__ __forceinline__ void gemm_tile(const GemmArgs &g, const float *A, const float *B, int m0, int n0,
+                                          int kb, int ke, float (&acc)[4][4], float (*As)[BM + 4],
+                                          float (*Bs)[BN + 4]) {
     const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
-    float acc[4][4];
+    for (int k0 = kb; k0 < ke; k0 += BK) {
+        // op(A)[m0..+63][k0..+31] -> As[k][m]; op(B)[k0..+31][n0..+63] -> Bs[k][n]
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    for (int k0 = 0; k0 < g.K; k0 += BK) {
-        // A tile: op(A)[m0..m0+63][k0..k0+15] -> As[k][m]
-        for (int idx = t; idx < BM * BK; idx += NT) {
+        for (int it = 0; it < (BM * BK) / NT; ++it) {
+            const int idx = t + it * NT;
             int m, k;
-            float v = 0.0f;
             if (g.tA) {
                 m = idx % BM;
-                k = idx / BM;  // coalesced along m
-                if (m0 + m < g.M && k0 + k < g.K) v = A[(int64_t)(k0 + k) * g.lda + m0 + m];
+                k = idx / BM;
             } else {
                 k = idx % BK;
                 m = idx / BK;
-                if (m0 + m < g.M && k0 + k < g.K) v = A[(int64_t)(m0 + m) * g.lda + k0 + k];
             }
+            float v = 0.0f;
+            if (m0 + m < g.M && k0 + k < ke)
+                v = g.tA ? A[(int64_t)(k0 + k) * g.lda + m0 + m] : A[(int64_t)(m0 + m) * g.lda + k0 + k];
             As[k][m] = v;
         }
-        for (int idx = t; idx < BN * BK; idx += NT) {
+#pragma unroll
+        for (int it = 0; it < (BN * BK) / NT; ++it) {
+            const int idx = t + it * NT;
             int n, k;
-            float v = 0.0f;
             if (g.tB) {
                 k = idx % BK;
                 n = idx / BK;
-                if (n0 + n < g.N && k0 + k < g.K) v = B[(int64_t)(n0 + n) * g.ldb + k0 + k];
             } else {
                 n = idx % BN;
                 k = idx / BN;
-                if (n0 + n < g.N && k0 + k < g.K) v = B[(int64_t)(k0 + k) * g.ldb + n0 + n];
             }
+            float v = 0.0f;
+            if (n0 + n < g.N && k0 + k < ke)
+                v = g.tB ? B[(int64_t)(n0 + n) * g.ldb + k0 + k] : B[(int64_t)(k0 + k) * g.ldb + n0 + n];
             Bs[k][n] = v;
         }
         __syncthreads();
-#pragma unroll
+#pragma unroll 8
         for (int k = 0; k < BK; ++k) {
             const float4 a4 = *reinterpret_cast<const float4 *>(&As[k][ty * 4]);
             const float4 b4 = *reinterpret_cast<const float4 *>(&Bs[k][tx * 4]);
@@ -65,6 +61,30 @@ __global__ void __launch_bounds__(NT) k_gemm(GemmArgs g) {
         }
         __syncthreads();
     }
+}
+
+// K range of an output tile under the causal modes (see GemmArgs::causal).
+__device__ __forceinline__ void k_range(const GemmArgs &g, int m0, int &kb, int &ke) {
+    kb = 0;
+    ke = g.K;
+    if (g.causal == 2) ke = min(g.K, m0 + BM);
+    if (g.causal == 3) kb = (m0 / BK) * BK;
+}
+
+__global__ void __launch_bounds__(NT) k_gemm(GemmArgs g) {
+    __shared__ __align__(16) float As[BK][BM + 4];
+    __shared__ __align__(16) float Bs[BK][BN + 4];
+    const int b = blockIdx.z;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    if (g.causal == 1 && n0 > m0 + BM - 1) return;  // tile entirely above the diagonal
+    const float *A = g.A + (int64_t)(b / g.adiv) * g.sA;
+    const float *B = g.B + (int64_t)(b / g.bdiv) * g.sB;
+    float *C = g.C + (int64_t)b * g.sC;
+    float acc[4][4] = {};
+    int kb, ke;
+    k_range(g, m0, kb, ke);
+    gemm_tile(g, A, B, m0, n0, kb, ke, acc, As, Bs);
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int m = m0 + ty * 4 + i;
@@ -78,6 +98,48 @@ __global__ void __launch_bounds__(NT) k_gemm(GemmArgs g) {
             *c = g.beta == 0.0f ? v : __fmaf_rn(g.beta, *c, v);
         }
     }
+}
+
+// split-K: blockIdx.z = batch * splits + split; raw partials into g.ws
+__global__ void __launch_bounds__(NT) k_gemm_split(GemmArgs g, int splits, int kchunk) {
+    __shared__ __align__(16) float As[BK][BM + 4];
+    __shared__ __align__(16) float Bs[BK][BN + 4];
+    const int b = blockIdx.z / splits, sp = blockIdx.z % splits;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const float *A = g.A + (int64_t)(b / g.adiv) * g.sA;
+    const float *B = g.B + (int64_t)(b / g.bdiv) * g.sB;
+    float acc[4][4] = {};
+    int kb, ke;
+    k_range(g, m0, kb, ke);
+    const int sb = max(kb, sp * kchunk), se = min(ke, (sp + 1) * kchunk);
+    if (sb < se) gemm_tile(g, A, B, m0, n0, sb, se, acc, As, Bs);
+    float *P = g.ws + ((int64_t)b * splits + sp) * g.M * g.N;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + tx * 4 + j;
+            if (n < g.N) P[(int64_t)m * g.N + n] = acc[i][j];
+        }
+    }
+}
+
+// fixed-order sum over splits, then alpha/beta into C
+__global__ void k_split_reduce(GemmArgs g, int splits) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t mn = (int64_t)g.M * g.N;
+    if (i >= mn * g.batch) return;
+    const int b = (int)(i / mn);
+    const int64_t r = i % mn;
+    const int m = (int)(r / g.N), n = (int)(r % g.N);
+    float s = 0.0f;
+    for (int sp = 0; sp < splits; ++sp) s = __fadd_rn(s, g.ws[((int64_t)b * splits + sp) * mn + r]);
+    float *c = g.C + (int64_t)b * g.sC + (int64_t)m * g.ldc + n;
+    const float v = __fmul_rn(g.alpha, s);
+    *c = g.beta == 0.0f ? v : __fmaf_rn(g.beta, *c, v);
 }
 
 __device__ __forceinline__ float qelem(const altxs_qmat &W, int row, int col) {
@@ -99,17 +161,21 @@ __device__ __forceinline__ float qelem(const altxs_qmat &W, int row, int col) {
     return __fmul_rn(lev, s);
 }
 
+// dense fp32 copy of rows [row0, row0 + rows) of a mixed-bit matrix
+__global__ void k_dequant(altxs_qmat W, int row0, int rows, float *out, int64_t ld) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * W.cols) return;
+    const int r = (int)(i / W.cols), c = (int)(i % W.cols);
+    out[(int64_t)r * ld + c] = qelem(W, row0 + r, c);
+}
+
 // dX tile 64 (m) x 64 (k = one group column); reduction over W rows in chunks of 64
 __global__ void __launch_bounds__(NT) k_qmm_t(QmmTArgs a) {
     __shared__ __align__(16) float Ys[64][64 + 4];  // [n][m]
     __shared__ __align__(16) float Ws[64][64 + 4];  // [n][k]
     const int m0 = blockIdx.y * 64, k0 = blockIdx.x * 64;
     const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    float acc[4][4] = {};
     for (int n0 = 0; n0 < a.N; n0 += 64) {
         for (int idx = t; idx < 64 * 64; idx += NT) {
             const int n = idx & 63, m = idx >> 6;  // coalesced along n
@@ -157,7 +223,26 @@ __global__ void __launch_bounds__(NT) k_qmm_t(QmmTArgs a) {
 int launch_gemm(const GemmArgs &g, cudaStream_t s) {
     if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
     if (g.adiv < 1 || g.bdiv < 1) return ALTXS_EINVAL;
-    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+    const int tm = (g.M + BM - 1) / BM, tn = (g.N + BN - 1) / BN;
+    const int64_t tiles = (int64_t)tm * tn * g.batch;
+    // Split the reduction when the tile grid cannot fill the GPU and K is long.
+    // The split count depends only on the shape, so results are deterministic.
+    int splits = 1;
+    if (g.ws && g.causal != 1 && tiles < 296 && g.K >= 4 * BK) {
+        splits = (int)((592 + tiles - 1) / tiles);
+        splits = min(splits, g.K / (2 * BK));
+        const int64_t cap = g.ws_floats / ((int64_t)g.M * g.N * g.batch);
+        if (splits > cap) splits = (int)cap;
+    }
+    if (splits > 1) {
+        const int kchunk = ((g.K + splits - 1) / splits + BK - 1) / BK * BK;
+        dim3 grid(tn, tm, g.batch * splits);
+        ALTXS_LAUNCH(kKTtt, s, k_gemm_split<<<grid, NT, 0, s>>>(g, splits, kchunk));
+        const int64_t total = (int64_t)g.M * g.N * g.batch;
+        ALTXS_LAUNCH(kKTtt, s, k_split_reduce<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(g, splits));
+        return ALTXS_OK;
+    }
+    dim3 grid(tn, tm, g.batch);
     ALTXS_LAUNCH(kKTtt, s, k_gemm<<<grid, NT, 0, s>>>(g));
     return ALTXS_OK;
 }
@@ -167,6 +252,14 @@ int launch_qmm_t(const QmmTArgs &a, cudaStream_t s) {
     if (a.K != a.W.cols || a.row0 < 0 || a.row0 + a.N > a.W.rows) return ALTXS_EINVAL;
     dim3 grid((a.K + 63) / 64, (a.M + 63) / 64);
     ALTXS_LAUNCH(kKTtt, s, k_qmm_t<<<grid, NT, 0, s>>>(a));
+    return ALTXS_OK;
+}
+
+int launch_dequant(const altxs_qmat &W, int row0, int rows, float *out, int64_t ld, cudaStream_t s) {
+    if (rows <= 0) return ALTXS_OK;
+    if (row0 < 0 || row0 + rows > W.rows || ld < W.cols) return ALTXS_EINVAL;
+    const int64_t n = (int64_t)rows * W.cols;
+    ALTXS_LAUNCH(kKTtt, s, k_dequant<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(W, row0, rows, out, ld));
     return ALTXS_OK;
 }
 

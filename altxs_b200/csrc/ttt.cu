@@ -335,16 +335,28 @@ __global__ void t_leaky_bwd(int64_t n, const float *dh, const float *u, float *d
     du[i] = __fmul_rn(dh[i], v >= 0.0f ? __fmul_rn(2.0f, v) : __fmul_rn(0.5f, v));
 }
 
-// dS = P * (dP - sum_j dP P) * scale, per (head, row), in place over dP
+// dS = P * (dP - sum_j dP P) * scale, per (head, row), in place over dP.
+// Only j <= t is read (dP above the diagonal is never computed); dS there is 0.
 __global__ void t_softmax_bwd(TD D, const float *P, float *dS, float scale) {
     __shared__ float red[32];
     const int row = blockIdx.x;
+    const int t = row % D.T;
     const float *p = P + (int64_t)row * D.T;
     float *g = dS + (int64_t)row * D.T;
     float s = 0.0f;
-    for (int j = threadIdx.x; j < D.T; j += blockDim.x) s = __fmaf_rn(g[j], p[j], s);
+    for (int j = threadIdx.x; j <= t; j += blockDim.x) s = __fmaf_rn(g[j], p[j], s);
     s = block_sum(s, red);
-    for (int j = threadIdx.x; j < D.T; j += blockDim.x) g[j] = __fmul_rn(__fmul_rn(p[j], __fsub_rn(g[j], s)), scale);
+    for (int j = threadIdx.x; j < D.T; j += blockDim.x)
+        g[j] = j <= t ? __fmul_rn(__fmul_rn(p[j], __fsub_rn(g[j], s)), scale) : 0.0f;
+}
+
+// x = r + colscale * y (row stride d), optional copy into y2
+__global__ void t_resid(int64_t n, int d, const float *r, const float *col, const float *y, float *x, float *y2) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = __fadd_rn(r[i], __fmul_rn(col[i % d], y[i]));
+    x[i] = v;
+    if (y2) y2[i] = v;
 }
 
 // q/k: undo gain, RoPE transpose, per-head RMSNorm backward -> dqkv
@@ -469,9 +481,26 @@ __global__ void t_adam(int64_t n, float *p, const float *g, float *m, float *v, 
 
 inline int g1(int64_t n, int t) { return (int)((n + t - 1) / t); }
 
-// GEMM helper with the common fields
-inline GemmArgs G(const float *A, int64_t lda, int tA, const float *B, int64_t ldb, int tB, float *C, int64_t ldc,
-                  int M, int N, int K, float alpha = 1.0f, float beta = 0.0f) {
+#define TRY(x)                 \
+    do {                       \
+        int rc_ = (x);         \
+        if (rc_) return rc_;   \
+    } while (0)
+
+struct Run {
+    TD D;
+    const altxs_model_desc *desc;
+    const altxs_weights *w;
+    const altxs_dense_weights *dw;  // dense fp32 base, or NULL
+    Tape tp;
+    float *splitk;
+    int64_t splitk_floats;
+    cudaStream_t st;
+};
+
+// GEMM with the common fields (split-K scratch attached)
+GemmArgs G(const Run &R, const float *A, int64_t lda, int tA, const float *B, int64_t ldb, int tB, float *C,
+           int64_t ldc, int M, int N, int K, float alpha = 1.0f, float beta = 0.0f) {
     GemmArgs g{};
     g.A = A;
     g.B = B;
@@ -489,32 +518,266 @@ inline GemmArgs G(const float *A, int64_t lda, int tA, const float *B, int64_t l
     g.bdiv = 1;
     g.alpha = alpha;
     g.beta = beta;
+    g.ws = R.splitk;
+    g.ws_floats = R.splitk_floats;
     return g;
 }
 
-#define TRY(x)                 \
-    do {                       \
-        int rc_ = (x);         \
-        if (rc_) return rc_;   \
-    } while (0)
+// Y[T][N] = X[T][K] W[row0.., :]^T  (dense copy of the base if present)
+int lin_fwd(const Run &R, const altxs_qmat &Wq, const float *Wd, int row0, int N, int K, const float *X, int64_t ldx,
+            float *Y, int64_t ldy) {
+    if (Wd) return launch_gemm(G(R, X, ldx, 0, Wd + (int64_t)row0 * K, K, 1, Y, ldy, R.D.T, N, K), R.st);
+    QmmArgs a{};
+    a.X = X;
+    a.ldx = ldx;
+    a.M = R.D.T;
+    a.W = Wq;
+    a.row0 = row0;
+    a.N = N;
+    a.K = K;
+    a.Y = Y;
+    a.ldy = ldy;
+    a.epi = kEpiStore;
+    return launch_qmm(a, R.st);
+}
+
+// dX[T][K] (= or +=) dY[T][N] W[row0.., :]
+int lin_bwd(const Run &R, const altxs_qmat &Wq, const float *Wd, int row0, int N, int K, const float *dY,
+            int64_t lddy, float *dX, int64_t lddx, float beta) {
+    if (Wd)
+        return launch_gemm(G(R, dY, lddy, 0, Wd + (int64_t)row0 * K, K, 0, dX, lddx, R.D.T, K, N, 1.0f, beta), R.st);
+    QmmTArgs q{};
+    q.dY = dY;
+    q.lddy = lddy;
+    q.M = R.D.T;
+    q.W = Wq;
+    q.row0 = row0;
+    q.N = N;
+    q.K = K;
+    q.dX = dX;
+    q.lddx = lddx;
+    q.alpha = 1.0f;
+    q.beta = beta;
+    return launch_qmm_t(q, R.st);
+}
 
 // LoRA forward for one target: t = X A^T ; Y += s * t B^T
-int lora_fwd(const float *X, int din, const float *A, const float *B, int dout, int r, float s, float *t, float *Y,
-             int64_t ldy, int T, cudaStream_t st) {
-    TRY(launch_gemm(G(X, din, 0, A, din, 1, t, r, T, r, din), st));
-    TRY(launch_gemm(G(t, r, 0, B, r, 1, Y, ldy, T, dout, r, s, 1.0f), st));
+int lora_fwd(const Run &R, const float *X, int din, const float *A, const float *B, int dout, float s, float *t,
+             float *Y, int64_t ldy) {
+    const int T = R.D.T, r = R.D.r;
+    TRY(launch_gemm(G(R, X, din, 0, A, din, 1, t, r, T, r, din), R.st));
+    TRY(launch_gemm(G(R, t, r, 0, B, r, 1, Y, ldy, T, dout, r, s, 1.0f), R.st));
     return ALTXS_OK;
 }
 
 // LoRA backward: grads dA, dB (written), dX += dt A (if dX)
-int lora_bwd(const float *X, int din, const float *A, const float *B, int dout, int r, float s, const float *t,
-             const float *Gy, int64_t ldg, float *dA, float *dB, float *dt, float *dX, int T, cudaStream_t st) {
-    TRY(launch_gemm(G(Gy, ldg, 1, t, r, 0, dB, r, dout, r, T, s), st));        // dB = s G^T t
-    TRY(launch_gemm(G(Gy, ldg, 0, B, r, 0, dt, r, T, r, dout, s), st));        // dt = s G B
-    TRY(launch_gemm(G(dt, r, 1, X, din, 0, dA, din, r, din, T), st));          // dA = dt^T X
-    if (dX) TRY(launch_gemm(G(dt, r, 0, A, din, 0, dX, din, T, din, r, 1.0f, 1.0f), st));  // dX += dt A
+int lora_bwd(const Run &R, const float *X, int din, const float *A, const float *B, int dout, float s,
+             const float *t, const float *Gy, int64_t ldg, float *dA, float *dB, float *dX) {
+    const int T = R.D.T, r = R.D.r;
+    float *dt = R.tp.dt;
+    TRY(launch_gemm(G(R, Gy, ldg, 1, t, r, 0, dB, r, dout, r, T, s), R.st));  // dB = s G^T t
+    TRY(launch_gemm(G(R, Gy, ldg, 0, B, r, 0, dt, r, T, r, dout, s), R.st));  // dt = s G B
+    TRY(launch_gemm(G(R, dt, r, 1, X, din, 0, dA, din, r, din, T), R.st));    // dA = dt^T X
+    if (dX) TRY(launch_gemm(G(R, dt, r, 0, A, din, 0, dX, din, T, din, r, 1.0f, 1.0f), R.st));  // dX += dt A
     return ALTXS_OK;
 }
+
+int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out) {
+    const TD &D = R.D;
+    const Tape &tp = R.tp;
+    const altxs_weights *w = R.w;
+    const altxs_dense_weights *dw = R.dw;
+    const LoraOff lo = lora_offsets(*R.desc);
+    const int mask = R.desc->lora_mask;
+    const float s = R.desc->lora_scale;
+    const int Tn = D.T, d = D.d, r = D.r;
+    const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
+    cudaStream_t st = R.st;
+    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, tp.x0, tp.x));
+    for (int l = 0; l < D.L; ++l) {
+        ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
+        const float *n = tp.n + (int64_t)l * Tn * d;
+        float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
+        TRY(lin_fwd(R, w->qkv, dw ? dw->qkv : nullptr, l * D.qn, D.qn, d, n, d, qkv, D.qn));
+        TRY(lora_fwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
+                     tp.tq + (int64_t)l * Tn * r, qkv, D.qn));
+        if (mask & 2)
+            TRY(lora_fwd(R, n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, s,
+                         tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn));
+        TRY(lora_fwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
+                     tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
+        ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, tp, *w));
+        float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
+        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        {
+            GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, P, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
+            g.batch = D.H;
+            g.sA = D.hd;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = (int64_t)Tn * Tn;
+            g.causal = 1;
+            TRY(launch_gemm(g, st));
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, P));
+        {
+            GemmArgs g = G(R, P, Tn, 0, qkv + d + D.kvd, D.qn, 0, tp.y, d, Tn, D.hd, Tn);  // y = P v
+            g.batch = D.H;
+            g.sA = (int64_t)Tn * Tn;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = D.hd;
+            g.causal = 2;
+            TRY(launch_gemm(g, st));
+        }
+        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, l * d, d, d, tp.y, d, tp.ao, d));
+        if (mask & 8)
+            TRY(lora_fwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
+                         tp.to + (int64_t)l * Tn * r, tp.ao, d));
+        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w));
+        float *u = tp.u + (int64_t)l * Tn * D.F;
+        TRY(lin_fwd(R, w->up, dw ? dw->up : nullptr, l * D.F, D.F, d, tp.n2 + (int64_t)l * Tn * d, d, u, D.F));
+        ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
+        float *sk = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
+        const float *xm = tp.xmid + (int64_t)l * Tn * d;
+        if (dw) {
+            TRY(lin_fwd(R, w->down, dw->down, l * d, d, D.F, tp.hbuf, D.F, tp.dd, d));
+            ALTXS_LAUNCH(kKTtt, st, t_resid<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                        (int64_t)Tn * d, d, xm, w->mlp_scale + (int64_t)l * d, tp.dd, tp.x, sk));
+        } else {
+            QmmArgs a{};
+            a.X = tp.hbuf;
+            a.ldx = D.F;
+            a.M = Tn;
+            a.W = w->down;
+            a.row0 = l * d;
+            a.N = d;
+            a.K = D.F;
+            a.Y = tp.x;
+            a.ldy = d;
+            a.epi = kEpiResid;
+            a.R = xm;
+            a.ldr = d;
+            a.colscale = w->mlp_scale + (int64_t)l * d;
+            a.Y2 = sk;
+            a.ldy2 = d;
+            TRY(launch_qmm(a, st));
+        }
+    }
+    ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp));
+    TRY(lin_fwd(R, w->emb, dw ? dw->emb : nullptr, 0, D.V, d, tp.hf, d, tp.logits, D.V));
+    if (mask & 16) TRY(lora_fwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V));
+    ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, R.desc->logit_softcap));
+    ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, tp.rowloss, loss_out));
+    return ALTXS_OK;
+}
+
+int backward(const Run &R, const float *lora, float *grad) {
+    const TD &D = R.D;
+    const Tape &tp = R.tp;
+    const altxs_weights *w = R.w;
+    const altxs_dense_weights *dw = R.dw;
+    const LoraOff lo = lora_offsets(*R.desc);
+    const int mask = R.desc->lora_mask;
+    const float s = R.desc->lora_scale;
+    const int Tn = D.T, d = D.d, r = D.r;
+    const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
+    cudaStream_t st = R.st;
+    // LM head: dhf = dlogits E (+ LoRA)
+    TRY(lin_bwd(R, w->emb, dw ? dw->emb : nullptr, 0, D.V, d, tp.logits, D.V, tp.dn, d, 0.0f));
+    if (mask & 16)
+        TRY(lora_bwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V, grad + lo.lmA,
+                     grad + lo.lmB, tp.dn));
+    ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.x, tp.invf, nullptr, nullptr, tp.dx));
+    for (int l = D.L - 1; l >= 0; --l) {
+        if (l < D.enc)
+            ALTXS_LAUNCH(kKTtt, st, t_add<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                        (int64_t)Tn * d, tp.dx, tp.dskip + (int64_t)l * Tn * d));
+        // MLP
+        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                    (int64_t)Tn * d, d, tp.dx, w->mlp_scale + (int64_t)l * d, tp.dd));
+        TRY(lin_bwd(R, w->down, dw ? dw->down : nullptr, l * d, d, D.F, tp.dd, d, tp.dh, D.F, 0.0f));
+        ALTXS_LAUNCH(kKTtt, st, t_leaky_bwd<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
+                                    (int64_t)Tn * D.F, tp.dh, tp.u + (int64_t)l * Tn * D.F, tp.dh));
+        TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, l * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Tn * d,
+                                                             tp.inv2 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
+                                                             tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                    (int64_t)Tn * d, d, tp.dx, w->attn_scale + (int64_t)l * d, tp.dao));
+        const float *n = tp.n + (int64_t)l * Tn * d;
+        cudaMemsetAsync(tp.dn, 0, (size_t)Tn * d * 4, st);
+        if (mask & 8)
+            TRY(lora_bwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
+                         tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
+                         grad + lo.oB + l * lo.o_stride, tp.dn));
+        TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, l * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
+        // attention backward
+        const float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
+        const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
+        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        {
+            GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
+            g.batch = D.H;
+            g.sA = D.hd;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = (int64_t)Tn * Tn;
+            g.causal = 1;
+            TRY(launch_gemm(g, st));
+        }
+        for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
+            GemmArgs g = G(R, P + (int64_t)gi * Tn * Tn, Tn, 1, tp.dy + gi * D.hd, d, 0, tp.dqkv + d + D.kvd,
+                           D.qn, Tn, D.hd, Tn, 1.0f, gi ? 1.0f : 0.0f);
+            g.batch = D.Hkv;
+            g.sA = (int64_t)D.G * Tn * Tn;
+            g.sB = (int64_t)D.G * D.hd;
+            g.sC = D.hd;
+            g.causal = 3;
+            TRY(launch_gemm(g, st));
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_softmax_bwd<<<D.H * Tn, 256, 0, st>>>(D, P, tp.dS, att_scale));
+        {
+            GemmArgs g = G(R, tp.dS, Tn, 0, kr, D.kvd, 0, tp.dqr, d, Tn, D.hd, Tn);  // dq = dS k
+            g.batch = D.H;
+            g.sA = (int64_t)Tn * Tn;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = D.hd;
+            g.causal = 2;
+            TRY(launch_gemm(g, st));
+        }
+        for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
+            GemmArgs g = G(R, tp.dS + (int64_t)gi * Tn * Tn, Tn, 1, qr + gi * D.hd, d, 0, tp.dkr, D.kvd, Tn, D.hd,
+                           Tn, 1.0f, gi ? 1.0f : 0.0f);
+            g.batch = D.Hkv;
+            g.sA = (int64_t)D.G * Tn * Tn;
+            g.sB = (int64_t)D.G * D.hd;
+            g.sC = D.hd;
+            g.causal = 3;
+            TRY(launch_gemm(g, st));
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, tp, *w));
+        TRY(lora_bwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
+                     tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, grad + lo.qA + l * lo.q_stride,
+                     grad + lo.qB + l * lo.q_stride, tp.dn));
+        if (mask & 2)
+            TRY(lora_bwd(R, n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, s,
+                         tp.tk + (int64_t)l * Tn * r, tp.dqkv + d, D.qn, grad + lo.kA + l * lo.k_stride,
+                         grad + lo.kB + l * lo.k_stride, tp.dn));
+        TRY(lora_bwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
+                     tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, grad + lo.vA + l * lo.v_stride,
+                     grad + lo.vB + l * lo.v_stride, tp.dn));
+        TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, l * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Tn * d,
+                                                             tp.inv1 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
+                                                             tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_mix_bwd<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
+    }
+    return ALTXS_OK;
+}
+
+constexpr int64_t kSplitkFloats = 16ll << 20;  // 64 MiB of split-K partials
 
 }  // namespace
 
@@ -523,296 +786,43 @@ extern "C" {
 int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T) {
     TD D{};
     if (!desc || fill(*desc, T, D)) return -1;
-    return carve(D, nullptr, nullptr) + align_up(lora_offsets(*desc).total * 4, 256);
+    return carve(D, nullptr, nullptr) + align_up(lora_offsets(*desc).total * 4, 256) + kSplitkFloats * 4;
 }
 
-int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_ttt_hparams *hp,
-                     const int32_t *tokens, int T, float *lora, float *adam_m, float *adam_v, int step,
-                     float *loss_out, void *workspace, int64_t workspace_bytes, altxs_stream_t stream) {
+int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t stream) {
+    if (!m || !out) return ALTXS_EINVAL;
+    return launch_dequant(*m, 0, m->rows, out, ld, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
+                     const altxs_ttt_hparams *hp, const int32_t *tokens, int T, float *lora, float *adam_m,
+                     float *adam_v, int step, float *loss_out, void *workspace, int64_t workspace_bytes,
+                     altxs_stream_t stream) {
     if (!desc || !w || !hp || !tokens || !lora || !adam_m || !adam_v || !workspace || step < 1) return ALTXS_EINVAL;
-    TD D{};
-    TRY(fill(*desc, T, D));
+    Run R{};
+    TRY(fill(*desc, T, R.D));
     if (workspace_bytes < altxs_ttt_workspace_bytes(desc, T)) return ALTXS_EINVAL;
     if (w->rope_positions < T) return ALTXS_EINVAL;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    Tape tp{};
-    const int64_t tape_bytes = carve(D, workspace, &tp);
-    tp.grad = reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + tape_bytes);
+    if (dense && (!dense->emb || !dense->qkv || !dense->o || !dense->up || !dense->down)) return ALTXS_EINVAL;
+    R.desc = desc;
+    R.w = w;
+    R.dw = dense;
+    R.st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t tape_bytes = carve(R.D, workspace, &R.tp);
     const LoraOff lo = lora_offsets(*desc);
-    const int mask = desc->lora_mask;
-    const float s = desc->lora_scale;
-    const int Tn = D.T, d = D.d, r = D.r;
-    const int32_t *tok = tokens, *tgt = tokens + 1;
-    const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
-    cudaMemsetAsync(tp.grad, 0, lo.total * 4, st);
-
-    // ---------------- forward ----------------
-    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, tp.x0, tp.x));
-    for (int l = 0; l < D.L; ++l) {
-        ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, tp, *w, desc->skip_gates));
-        const float *n = tp.n + (int64_t)l * Tn * d;
-        float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
-        QmmArgs a{};
-        a.X = n;
-        a.ldx = d;
-        a.M = Tn;
-        a.W = w->qkv;
-        a.row0 = l * D.qn;
-        a.N = D.qn;
-        a.K = d;
-        a.Y = qkv;
-        a.ldy = D.qn;
-        a.epi = kEpiStore;
-        TRY(launch_qmm(a, st));
-        TRY(lora_fwd(n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, r, s,
-                     tp.tq + (int64_t)l * Tn * r, qkv, D.qn, Tn, st));
-        if (mask & 2)
-            TRY(lora_fwd(n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, r, s,
-                         tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn, Tn, st));
-        TRY(lora_fwd(n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, r, s,
-                     tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn, Tn, st));
-        ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, tp, *w));
-        float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
-        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
-        {
-            GemmArgs g = G(qr, D.H * D.hd, 0, kr, D.kvd, 1, P, Tn, Tn, Tn, D.hd, att_scale);
-            g.batch = D.H;
-            g.sA = D.hd;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = (int64_t)Tn * Tn;
-            TRY(launch_gemm(g, st));
-        }
-        ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, P));
-        {
-            GemmArgs g = G(P, Tn, 0, qkv + d + D.kvd, D.qn, 0, tp.y, d, Tn, D.hd, Tn);
-            g.batch = D.H;
-            g.sA = (int64_t)Tn * Tn;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = D.hd;
-            TRY(launch_gemm(g, st));
-        }
-        a.X = tp.y;
-        a.W = w->o;
-        a.row0 = l * d;
-        a.N = d;
-        a.Y = tp.ao;
-        a.ldy = d;
-        TRY(launch_qmm(a, st));
-        if (mask & 8)
-            TRY(lora_fwd(n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, r, s,
-                         tp.to + (int64_t)l * Tn * r, tp.ao, d, Tn, st));
-        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w));
-        float *u = tp.u + (int64_t)l * Tn * D.F;
-        a.X = tp.n2 + (int64_t)l * Tn * d;
-        a.W = w->up;
-        a.row0 = l * D.F;
-        a.N = D.F;
-        a.Y = u;
-        a.ldy = D.F;
-        TRY(launch_qmm(a, st));
-        ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
-        a.X = tp.hbuf;
-        a.ldx = D.F;
-        a.W = w->down;
-        a.row0 = l * d;
-        a.N = d;
-        a.K = D.F;
-        a.Y = tp.x;
-        a.ldy = d;
-        a.epi = kEpiResid;
-        a.R = tp.xmid + (int64_t)l * Tn * d;
-        a.ldr = d;
-        a.colscale = w->mlp_scale + (int64_t)l * d;
-        a.Y2 = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
-        a.ldy2 = d;
-        TRY(launch_qmm(a, st));
-    }
-    ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp));
-    {
-        QmmArgs a{};
-        a.X = tp.hf;
-        a.ldx = d;
-        a.M = Tn;
-        a.W = w->emb;
-        a.row0 = 0;
-        a.N = D.V;
-        a.K = d;
-        a.Y = tp.logits;
-        a.ldy = D.V;
-        a.epi = kEpiStore;
-        TRY(launch_qmm(a, st));
-    }
-    if (mask & 16)
-        TRY(lora_fwd(tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, r, s, tp.tlm, tp.logits, D.V, Tn, st));
-    ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, desc->logit_softcap));
-    ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, tp.rowloss, loss_out));
-
-    // ---------------- backward ----------------
-    // LM head: dhf = dlogits E + LoRA
-    {
-        QmmTArgs q{};
-        q.dY = tp.logits;
-        q.lddy = D.V;
-        q.M = Tn;
-        q.W = w->emb;
-        q.row0 = 0;
-        q.N = D.V;
-        q.K = d;
-        q.dX = tp.dn;
-        q.lddx = d;
-        q.alpha = 1.0f;
-        q.beta = 0.0f;
-        TRY(launch_qmm_t(q, st));
-    }
-    if (mask & 16)
-        TRY(lora_bwd(tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, r, s, tp.tlm, tp.logits, D.V, tp.grad + lo.lmA,
-                     tp.grad + lo.lmB, tp.dt, tp.dn, Tn, st));
-    ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.x, tp.invf, nullptr, nullptr, tp.dx));
-    for (int l = D.L - 1; l >= 0; --l) {
-        if (l < D.enc) {
-            ALTXS_LAUNCH(kKTtt, st, t_add<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                        (int64_t)Tn * d, tp.dx, tp.dskip + (int64_t)l * Tn * d));
-        }
-        // MLP
-        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                    (int64_t)Tn * d, d, tp.dx, w->mlp_scale + (int64_t)l * d, tp.dd));
-        {
-            QmmTArgs q{};
-            q.dY = tp.dd;
-            q.lddy = d;
-            q.M = Tn;
-            q.W = w->down;
-            q.row0 = l * d;
-            q.N = d;
-            q.K = D.F;
-            q.dX = tp.dh;
-            q.lddx = D.F;
-            q.alpha = 1.0f;
-            TRY(launch_qmm_t(q, st));
-        }
-        const float *u = tp.u + (int64_t)l * Tn * D.F;
-        ALTXS_LAUNCH(kKTtt, st, t_leaky_bwd<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
-                                    (int64_t)Tn * D.F, tp.dh, u, tp.dh));
-        {
-            QmmTArgs q{};
-            q.dY = tp.dh;
-            q.lddy = D.F;
-            q.M = Tn;
-            q.W = w->up;
-            q.row0 = l * D.F;
-            q.N = D.F;
-            q.K = d;
-            q.dX = tp.dn2;
-            q.lddx = d;
-            q.alpha = 1.0f;
-            TRY(launch_qmm_t(q, st));
-        }
-        // dxmid = dx + rms_bwd(dn2 * ln)
-        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Tn * d,
-                                                             tp.inv2 + (int64_t)l * Tn, w->ln_scale + l, tp.dx, tp.dx));
-        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                    (int64_t)Tn * d, d, tp.dx, w->attn_scale + (int64_t)l * d, tp.dao));
-        const float *n = tp.n + (int64_t)l * Tn * d;
-        // dn accumulates: o-LoRA, then qkv
-        cudaMemsetAsync(tp.dn, 0, (size_t)Tn * d * 4, st);
-        if (mask & 8)
-            TRY(lora_bwd(n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, r, s,
-                         tp.to + (int64_t)l * Tn * r, tp.dao, d, tp.grad + lo.oA + l * lo.o_stride,
-                         tp.grad + lo.oB + l * lo.o_stride, tp.dt, tp.dn, Tn, st));
-        {
-            QmmTArgs q{};
-            q.dY = tp.dao;
-            q.lddy = d;
-            q.M = Tn;
-            q.W = w->o;
-            q.row0 = l * d;
-            q.N = d;
-            q.K = d;
-            q.dX = tp.dy;
-            q.lddx = d;
-            q.alpha = 1.0f;
-            TRY(launch_qmm_t(q, st));
-        }
-        // attention backward
-        const float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
-        const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
-        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
-        {
-            GemmArgs g = G(tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy V^T
-            g.batch = D.H;
-            g.sA = D.hd;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = (int64_t)Tn * Tn;
-            TRY(launch_gemm(g, st));
-        }
-        for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
-            GemmArgs g = G(P + (int64_t)gi * Tn * Tn, Tn, 1, tp.dy + gi * D.hd, d, 0, tp.dqkv + d + D.kvd, D.qn,
-                           Tn, D.hd, Tn, 1.0f, gi ? 1.0f : 0.0f);
-            g.batch = D.Hkv;
-            g.sA = (int64_t)D.G * Tn * Tn;
-            g.sB = (int64_t)D.G * D.hd;
-            g.sC = D.hd;
-            TRY(launch_gemm(g, st));
-        }
-        ALTXS_LAUNCH(kKTtt, st, t_softmax_bwd<<<D.H * Tn, 256, 0, st>>>(D, P, tp.dS, att_scale));
-        {
-            GemmArgs g = G(tp.dS, Tn, 0, kr, D.kvd, 0, tp.dqr, d, Tn, D.hd, Tn);  // dq = dS k
-            g.batch = D.H;
-            g.sA = (int64_t)Tn * Tn;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = D.hd;
-            TRY(launch_gemm(g, st));
-        }
-        for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
-            GemmArgs g = G(tp.dS + (int64_t)gi * Tn * Tn, Tn, 1, qr + gi * D.hd, d, 0, tp.dkr, D.kvd, Tn, D.hd, Tn,
-                           1.0f, gi ? 1.0f : 0.0f);
-            g.batch = D.Hkv;
-            g.sA = (int64_t)D.G * Tn * Tn;
-            g.sB = (int64_t)D.G * D.hd;
-            g.sC = D.hd;
-            TRY(launch_gemm(g, st));
-        }
-        ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, tp, *w));
-        // LoRA q/k/v grads and their dn contributions
-        TRY(lora_bwd(n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, r, s,
-                     tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, tp.grad + lo.qA + l * lo.q_stride,
-                     tp.grad + lo.qB + l * lo.q_stride, tp.dt, tp.dn, Tn, st));
-        if (mask & 2)
-            TRY(lora_bwd(n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, r, s,
-                         tp.tk + (int64_t)l * Tn * r, tp.dqkv + d, D.qn, tp.grad + lo.kA + l * lo.k_stride,
-                         tp.grad + lo.kB + l * lo.k_stride, tp.dt, tp.dn, Tn, st));
-        TRY(lora_bwd(n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, r, s,
-                     tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, tp.grad + lo.vA + l * lo.v_stride,
-                     tp.grad + lo.vB + l * lo.v_stride, tp.dt, tp.dn, Tn, st));
-        {
-            QmmTArgs q{};
-            q.dY = tp.dqkv;
-            q.lddy = D.qn;
-            q.M = Tn;
-            q.W = w->qkv;
-            q.row0 = l * D.qn;
-            q.N = D.qn;
-            q.K = d;
-            q.dX = tp.dn;
-            q.lddx = d;
-            q.alpha = 1.0f;
-            q.beta = 1.0f;
-            TRY(launch_qmm_t(q, st));
-        }
-        // dxin = dxmid + rms_bwd(dn * ln); then mix / skip backward
-        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Tn * d,
-                                                             tp.inv1 + (int64_t)l * Tn, w->ln_scale + l, tp.dx, tp.dx));
-        ALTXS_LAUNCH(kKTtt, st, t_mix_bwd<<<Tn, 128, 0, st>>>(D, l, tp, *w, desc->skip_gates));
-    }
-    // ---------------- clip + AdamW ----------------
+    float *grad = reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + tape_bytes);
+    R.tp.grad = grad;
+    R.splitk = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(grad) + align_up(lo.total * 4, 256));
+    R.splitk_floats = kSplitkFloats;
+    cudaStream_t st = R.st;
+    cudaMemsetAsync(grad, 0, lo.total * 4, st);
+    TRY(forward(R, tokens, tokens + 1, lora, loss_out));
+    TRY(backward(R, lora, grad));
+    // global-norm clip + AdamW
     const int nparts = 256;
-    ALTXS_LAUNCH(kKTtt, st, t_sqsum_part<<<nparts, 256, 0, st>>>(lo.total, tp.grad, tp.red));
-    ALTXS_LAUNCH(kKTtt, st, t_adam<<<g1(lo.total, 1024), 1024, 0, st>>>(lo.total, lora, tp.grad, adam_m, adam_v,
-                                                                         tp.red, nparts, *hp, step));
+    ALTXS_LAUNCH(kKTtt, st, t_sqsum_part<<<nparts, 256, 0, st>>>(lo.total, grad, R.tp.red));
+    ALTXS_LAUNCH(kKTtt, st, t_adam<<<g1(lo.total, 1024), 1024, 0, st>>>(lo.total, lora, grad, adam_m, adam_v,
+                                                                         R.tp.red, nparts, *hp, step));
     return ALTXS_OK;
 }
 

@@ -122,6 +122,22 @@ class DeviceModel:
         self.rope_positions = n
         self._weights_struct = None
 
+    def dense_weights(self) -> _lib.DenseWeights:
+        """Dense fp32 copies of the frozen base for the test-time update
+        (built once on first use, exact values; 4 bytes per weight)."""
+        if getattr(self, "_dense", None) is None:
+            L = _lib.lib()
+            bufs = {}
+            for name in ("emb", "qkv", "o", "up", "down"):
+                q = self.q[name]
+                t = torch.empty((q.rows, q.cols), dtype=torch.float32, device=self.device)
+                _lib.check(L.altxs_dequant(C.byref(q), t.data_ptr(), q.cols, _stream_handle(self.device)),
+                           "altxs_dequant")
+                bufs[name] = t
+            self._dense_bufs = bufs
+            self._dense = _lib.DenseWeights(**{k: v.data_ptr() for k, v in bufs.items()})
+        return self._dense
+
     @property
     def weights_struct(self) -> _lib.Weights:
         if getattr(self, "_weights_struct", None) is None:

@@ -21,8 +21,9 @@ from .engine import DeviceModel, StreamBatch, _stream_handle
 
 
 class LoraTTT:
-    def __init__(self, dm: DeviceModel):
+    def __init__(self, dm: DeviceModel, *, dense_base: bool = True):
         self.dm = dm
+        self.dense = dm.dense_weights() if dense_base else None
         cfg = dm.cfg
         if not cfg.lora_enabled:
             raise ValueError("test-time update needs retrain_mode='lora' and a positive rank")
@@ -62,7 +63,8 @@ class LoraTTT:
             window = b.hist[r].index_select(0, idx).contiguous()
             steps[r] = steps.get(r, 0) + 1
             rc = L.altxs_ttt_update(
-                C.byref(self.dm.desc), C.byref(self.dm.weights_struct), C.byref(self.hp), window.data_ptr(), T,
+                C.byref(self.dm.desc), C.byref(self.dm.weights_struct),
+                C.byref(self.dense) if self.dense is not None else None, C.byref(self.hp), window.data_ptr(), T,
                 b.lora[r].data_ptr(), m[r].data_ptr(), v[r].data_ptr(), steps[r], self.loss.data_ptr(),
                 self.ws.data_ptr(), self.ws_bytes, _stream_handle(dev))
             _lib.check(rc, "altxs_ttt_update")

@@ -218,6 +218,16 @@ typedef struct altxs_ttt_hparams {
     float lr, beta1, beta2, eps, weight_decay, grad_clip;
 } altxs_ttt_hparams;
 
+/* Optional dense fp32 copies of the frozen base (same row layout as the
+ * altxs_qmat views), built once with altxs_dequant; the update's linear
+ * layers then run as plain fp32 GEMMs instead of re-dequantising per tile. */
+typedef struct altxs_dense_weights {
+    const float *emb, *qkv, *o, *up, *down;
+} altxs_dense_weights;
+
+/* out[r][c] = exact fp32 value of m[r][c] (row stride ld floats). */
+int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t stream);
+
 /* Workspace for one update over a T-token window (bytes). */
 int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T);
 
@@ -226,13 +236,14 @@ int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T);
  * with tanh softcap, mean cross-entropy, backward into the adapters only,
  * global-norm clip, AdamW step number `step` (1-based).  lora / adam_m /
  * adam_v: device [altxs_lora_floats] in the arena layout; loss_out: device
- * float or NULL.  Replaces the lora branch of online_retrain
- * (compress.py:1104-1137: ce_with_lora, backward, clip_grad_norm_, AdamW
- * step; ttt_lora.py:124-179, 258-374) on the window of _window_xy
- * (compress.py:301-320). */
-int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_ttt_hparams *hp,
-                     const int32_t *tokens, int T, float *lora, float *adam_m, float *adam_v, int step,
-                     float *loss_out, void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+ * float or NULL; dense: NULL or the dense base copies.  Replaces the lora
+ * branch of online_retrain (compress.py:1104-1137: ce_with_lora, backward,
+ * clip_grad_norm_, AdamW step; ttt_lora.py:124-179, 258-374) on the window
+ * of _window_xy (compress.py:301-320). */
+int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
+                     const altxs_ttt_hparams *hp, const int32_t *tokens, int T, float *lora, float *adam_m,
+                     float *adam_v, int step, float *loss_out, void *workspace, int64_t workspace_bytes,
+                     altxs_stream_t stream);
 
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these

@@ -22,7 +22,7 @@ SMALL = dict(
 )
 
 
-def _device_update(dm, lora_vec, window, steps=1):
+def _device_update(dm, lora_vec, window, steps=1, dense=True):
     from altxs_b200 import _lib
 
     L = _lib.lib()
@@ -38,7 +38,8 @@ def _device_update(dm, lora_vec, window, steps=1):
     loss = torch.zeros(1, device=DEV)
     losses = []
     for s in range(1, steps + 1):
-        rc = L.altxs_ttt_update(C.byref(dm.desc), C.byref(dm.weights_struct), C.byref(hp), tok.data_ptr(), T,
+        dw = C.byref(dm.dense_weights()) if dense else None
+        rc = L.altxs_ttt_update(C.byref(dm.desc), C.byref(dm.weights_struct), dw, C.byref(hp), tok.data_ptr(), T,
                                 p.data_ptr(), m.data_ptr(), v.data_ptr(), s, loss.data_ptr(), ws.data_ptr(), wsb,
                                 torch.cuda.current_stream().cuda_stream)
         assert rc == 0
@@ -55,7 +56,8 @@ def _arena(lora, cfg):
     return np.concatenate(out)
 
 
-def test_ttt_update_matches_oracle(golden):
+@pytest.mark.parametrize("dense", [True, False])
+def test_ttt_update_matches_oracle(golden, dense):
     from altxs_b200.engine import DeviceModel
 
     g = golden("lora_small.npz")
@@ -68,7 +70,7 @@ def test_ttt_update_matches_oracle(golden):
     arr, end = g["arr"], int(g["end"])
     t = min(cfg.block_size, end - 1)
     window = arr[end - t - 1: end]
-    got, losses = _device_update(dm, vec0, window, steps=2)
+    got, losses = _device_update(dm, vec0, window, steps=2, dense=dense)
     ref_losses = [ttt.update(arr, end) for _ in range(2)]
     np.testing.assert_allclose(losses, ref_losses, rtol=2e-5)
     np.testing.assert_allclose(losses, g["losses"], rtol=2e-5)  # the reference itself
