@@ -6,7 +6,10 @@ split evenly over N GPUs (one process per GPU), the 33M model (8L/512d/8h,
 MLP 2048, V 16384) with seeded random mixed 2/3/4-bit weights, sliding
 window filled to 2048 of 2048, symbols from the seeded Zipf-Markov source.
 A step decodes one symbol for every stream on every GPU: model step over the
-full window, logits -> integer CDF, range decode.  Streams share no data, so
+full window, logits -> integer CDF, range decode.  The LoRA schedule runs
+inside the timed steps: segment boundaries every 16,384 symbols per stream,
+staggered over the streams, each one a coder reload plus a test-time update
+over the stream's last 2048 symbols.  Streams share no data, so
 there is no collective on the hot path (weak per-stream work, fixed total
 streams -> "strong" scaling); NCCL only gathers per-stream byte counts.
 
@@ -44,7 +47,7 @@ WEIGHT_SEED = 1234
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--streams", type=int, default=GLOBAL_STREAMS, help="global stream count")
@@ -177,17 +180,39 @@ def config_block(world: int, streams: int) -> dict:
     }
 
 
+def boundary_plan(gids: np.ndarray, n_global: int, world: int, n_local: int, every: int, p0: int, chunk: int):
+    """Rows that cross a segment boundary before each chunk step.
+
+    Stream g runs its segment clock shifted by phi_g, so boundaries (flush,
+    test-time update, next segment) fall at positions p with
+    (p + phi_g) % every == 0.  phi spreads the streams evenly over the clock
+    and interleaves ranks, so every timed window carries its share of the
+    LoRA schedule on every GPU."""
+    stride = max(1, every // n_global)
+    rank_of = gids // n_local
+    j = gids % n_local
+    phi = ((j * world + rank_of) * stride) % every
+    plan = []
+    for t in range(chunk):
+        pos = p0 + t
+        plan.append([int(i) for i in np.flatnonzero((pos + phi) % every == 0)] if pos > 0 else [])
+    return plan
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    import ctypes
+
     from altxs_b200 import _lib
     from altxs_b200 import codec as C
     from altxs_b200.config import c3_config
-    from altxs_b200.engine import DeviceModel, StreamBatch, words_for_segment
+    from altxs_b200.engine import DeviceModel, StreamBatch, _stream_handle, words_for_segment
     from altxs_b200.synth import zipf_markov
+    from altxs_b200.ttt import LoraTTT
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -198,24 +223,29 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
         pg = dist
     cfg = c3_config()
-    cfg.retrain_mode = "lora"  # adapters present in every step (B = 0 before the first boundary)
     n_local = args.streams // world
+    n_global = n_local * world
     W, K = max(3, args.warmup), max(1, args.steps)
     chunk = W + K
+    every = cfg.online_retrain_every
     w = C.synth_weights(cfg, seed=WEIGHT_SEED)
     dm = DeviceModel(w, dev, rope_positions=cfg.ctx + chunk + 8)
     gids = np.arange(rank * n_local, (rank + 1) * n_local)
     data = zipf_markov(cfg.ctx + chunk, cfg.vocab_size, 1000 + gids)  # [n][T]
     symsT = torch.from_numpy(np.ascontiguousarray(data.T)).to(dev)     # [T][n]
-    b = StreamBatch(dm, n_local, words_per_stream=words_for_segment(max(cfg.ctx, chunk), cfg.cdf_bits))
+    wps = words_for_segment(max(cfg.ctx, chunk), cfg.cdf_bits)
+    b = StreamBatch(dm, n_local, words_per_stream=wps, hist_len=cfg.ctx + 2)
+    ttt = LoraTTT(dm)
     L = _lib.lib()
+    stream_h = _stream_handle(dev)
 
     if args.fill == "prefill":
         # fill every window: code the first ctx symbols (state warm-up, not timed)
         b.encode_chunk(symsT[: cfg.ctx])
     else:
         # seeded random K/V rows (unit-RMS keys, V ~ N(0, 1.5^2)) in the 24-bit
-        # split format, every stream positioned with a full window
+        # split format, every stream positioned with a full window; the symbol
+        # ring gets the same seeded symbols
         g = torch.Generator(device=dev)
         g.manual_seed(77 + rank)
         hd = cfg.head_dim
@@ -231,62 +261,136 @@ def main():
                 b.kv[:, li, kvi, :, :, 2 * hd:] = lo
         b.pos.fill_(cfg.ctx - 1)
         b.tok.copy_(symsT[cfg.ctx - 1])
+        idx = torch.arange(cfg.ctx, device=dev) % b.hist_len
+        b.hist[:, idx] = symsT[: cfg.ctx].T.contiguous()
     torch.cuda.synchronize(dev)
-    # snapshot what the timed chunk overwrites, so encode and decode start equal
-    p0 = int(b.pos[0].item())
-    slots = torch.arange(p0, p0 + chunk, device=dev) % cfg.ctx
+    p0 = cfg.ctx  # symbols coded before the chunk
+    plan = boundary_plan(gids, n_global, world, n_local, every, p0, chunk)
+    brows = sorted({r for rows in plan for r in rows})
+    # snapshot everything the chunk changes, so encode and decode start equal
+    pstart = int(b.pos[0].item())
+    slots = torch.arange(pstart, pstart + chunk, device=dev) % cfg.ctx
     kv_saved = b.kv.index_select(4, slots)
     tok_saved, pos_saved = b.tok.clone(), b.pos.clone()
+    hist_saved = b.hist.clone()
+    bidx = torch.as_tensor(brows, dtype=torch.int64, device=dev)
+    lora_saved = b.lora.index_select(0, bidx) if brows else None
 
     def restore():
         b.kv.index_copy_(4, slots, kv_saved)
         b.tok.copy_(tok_saved)
         b.pos.copy_(pos_saved)
+        b.hist.copy_(hist_saved)
+        if brows:
+            b.lora.index_copy_(0, bidx, lora_saved)
+            m, v = ttt._moments(b)
+            m.index_fill_(0, bidx, 0.0)
+            v.index_fill_(0, bidx, 0.0)
+        ttt.steps[id(b)] = {}
 
-    chunk_syms = symsT[cfg.ctx: cfg.ctx + chunk]
-    payloads = b.encode_chunk(chunk_syms)
-    bits_total = sum(len(p) for p in payloads) * 8
-    words_h, nbits_h = b.pack_payloads(payloads)
+    # ---- encode the chunk (untimed), segment per boundary -------------------
+    chunk_syms = symsT[p0: p0 + chunk]
+    segs = [[] for _ in range(b.n)]
+    b.ac_init()
+    for t in range(chunk):
+        rows = plan[t]
+        if rows:
+            b.ac_flush(rows)
+            for r, p in b.segment_bytes(rows).items():
+                segs[r].append(p)
+            b.ac_init(rows)
+            ttt(b, rows, p0 + t)
+        b.sym.copy_(chunk_syms[t])
+        b.step(_lib.STEP_ENCODE)
+    b.ac_flush()
+    for r, p in b.segment_bytes(list(range(b.n))).items():
+        segs[r].append(p)
+    b.check_status()
+    bits_total = sum(len(p) for sg in segs for p in sg) * 8
+    max_segs = max(len(sg) for sg in segs)
+    # host staging of every stream's segments: [n][max_segs][wps] words + bit counts
+    stage_h = torch.zeros((b.n, max_segs, wps), dtype=torch.int32)
+    nbits_h = torch.zeros((b.n, max_segs), dtype=torch.int64)
+    for i, sg in enumerate(segs):
+        for k, p in enumerate(sg):
+            buf = np.zeros(wps * 4, dtype=np.uint8)
+            buf[: len(p)] = np.frombuffer(p, dtype=np.uint8)
+            stage_h[i, k] = torch.from_numpy(buf.view(np.int32))
+            nbits_h[i, k] = len(p) * 8
+    stage_h, nbits_h = stage_h.pin_memory(), nbits_h.pin_memory()
+    stage_d = torch.empty_like(stage_h, device=dev)
+    nbits_d = torch.empty_like(nbits_h, device=dev)
+    seg_idx = torch.zeros(b.n, dtype=torch.int64, device=dev)
+
+    def load_segments(rows, which):
+        """bits[rows] <- stage[rows, which]; seed their decoders (device only)."""
+        ri = torch.as_tensor(rows, dtype=torch.int64, device=dev)
+        wi = torch.as_tensor(which, dtype=torch.int64, device=dev)
+        b.bits.index_copy_(0, ri, stage_d[ri, wi])
+        nb = nbits_d[ri, wi].contiguous()
+        rr = ri.to(torch.int32)
+        _lib.check(L.altxs_ac_begin_decode(len(rows), rr.data_ptr(), b.ac.data_ptr(), b.bits.data_ptr(),
+                                           nb.data_ptr(), b.words_per_stream, stream_h), "begin_decode")
+        return rr, nb  # keep alive until the launch ran
+
+    def decode_chunk(timed_from: int, dsyms: torch.Tensor, on_start=None, on_end=None):
+        """Decode the chunk from the restored state; on_start/on_end bracket
+        steps [timed_from, chunk)."""
+        nxt = [1] * b.n
+        keep = [load_segments(list(range(b.n)), [0] * b.n)]
+        for t in range(chunk):
+            if on_start is not None and t == timed_from:
+                on_start()
+            rows = plan[t]
+            if rows:
+                ttt(b, rows, p0 + t)
+                keep.append(load_segments(rows, [nxt[r] for r in rows]))
+                for r in rows:
+                    nxt[r] += 1
+            b.step(_lib.STEP_DECODE)
+            dsyms[t].copy_(b.sym)
+        if on_end is not None:
+            on_end()
+        return keep
 
     # ---- device-resident decode: value ------------------------------------
     restore()
-    b.bits.copy_(words_h.to(dev))
-    nb_d = nbits_h.to(dev)
-    _lib.check(L.altxs_ac_begin_decode(b.n, None, b.ac.data_ptr(), b.bits.data_ptr(), nb_d.data_ptr(),
-                                       b.words_per_stream, torch.cuda.current_stream(dev).cuda_stream), "bd")
+    stage_d.copy_(stage_h)
+    nbits_d.copy_(nbits_h)
     dsyms = torch.empty((chunk, b.n), dtype=torch.int32, device=dev)
-    for t in range(W):
-        b.step(_lib.STEP_DECODE)
-        dsyms[t].copy_(b.sym)
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
-    time.sleep(0.3)
-    L.altxs_profile(1)
-    launches0 = L.altxs_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.nvtx.range_push("timed")
-    e0.record()
-    for t in range(W, chunk):
-        b.step(_lib.STEP_DECODE)
-        dsyms[t].copy_(b.sym)
-    e1.record()
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize(dev)
-    launches = L.altxs_launch_count() - launches0
-    L.altxs_profile(0)
-    clk = clocks.stop()
-    if pg:
-        pg.barrier()
+    state = {}
+
+    def on_start():  # after the W warm-up steps
+        torch.cuda.synchronize(dev)
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+        state["clocks"] = ClockSampler(local)
+        time.sleep(0.3)
+        L.altxs_profile(1)
+        state["launches0"] = L.altxs_launch_count()
+        torch.cuda.nvtx.range_push("timed")
+        e0.record()
+
+    def on_end():
+        e1.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(dev)
+        state["launches"] = L.altxs_launch_count() - state["launches0"]
+        L.altxs_profile(0)
+        state["clk"] = state["clocks"].stop()
+        if pg:
+            pg.barrier()
+
+    decode_chunk(W, dsyms, on_start, on_end)
+    launches, clk = state["launches"], state["clk"]
     ms_local = e0.elapsed_time(e1)
     ms_max = ms_local
     if pg:
-        t = torch.tensor([ms_local], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms_max = float(t.item())
-    import ctypes
-
+        t_ = torch.tensor([ms_local], device=dev)
+        pg.all_reduce(t_, op=pg.ReduceOp.MAX)
+        ms_max = float(t_.item())
     ncls = len(_lib.KERNEL_CLASSES)
     pms = (ctypes.c_double * ncls)()
     pcnt = (ctypes.c_int64 * ncls)()
@@ -295,33 +399,37 @@ def main():
             for i, name in enumerate(_lib.KERNEL_CLASSES) if pcnt[i]}
     ok = torch.equal(dsyms, chunk_syms)
     b.check_status()
+    timed_boundaries = sum(len(plan[t]) for t in range(W, chunk))
 
-    # ---- end to end through the chunk API, host buffers --------------------
+    # ---- end to end: host segments in, host symbols out --------------------
     restore()
     out_h = torch.empty((chunk, b.n), dtype=torch.int32).pin_memory()
+    dsyms2 = torch.empty((chunk, b.n), dtype=torch.int32, device=dev)
     if pg:
         pg.barrier()
     torch.cuda.synchronize(dev)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
-    b.decode_chunk(words_h, nbits_h, chunk, out=out_h)
+    stage_d.copy_(stage_h, non_blocking=True)
+    nbits_d.copy_(nbits_h, non_blocking=True)
+    decode_chunk(0, dsyms2)
+    out_h.copy_(dsyms2, non_blocking=True)
     f1.record()
     torch.cuda.synchronize(dev)
     e2e_ms = f0.elapsed_time(f1)
     if pg:
-        t = torch.tensor([e2e_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        t_ = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t_, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t_.item())
     ok_e2e = torch.equal(out_h, chunk_syms.cpu())
 
     # per-stream (symbols, bytes) gathered over NCCL (the only collective)
-    counts = torch.tensor([[chunk, len(p)] for p in payloads], dtype=torch.int64, device=dev)
+    counts = torch.tensor([[chunk, sum(len(p) for p in sg)] for sg in segs], dtype=torch.int64, device=dev)
     if pg:
         allc = [torch.empty_like(counts) for _ in range(world)]
         pg.all_gather(allc, counts)
         counts = torch.cat(allc)
     total_bytes = int(counts[:, 1].sum().item())
-    n_global = n_local * world
 
     value = n_global * K / (ms_max / 1000.0)
     peaks, peak_kind = load_peaks()
@@ -348,6 +456,7 @@ def main():
 
         r = cpu_decode_baseline(w, target_s=args.cpu_seconds, seed=1)
         cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    h2d = int(stage_h.numel() * 4 + nbits_h.numel() * 8)
     line = {
         "metric": METRIC,
         "value": value,
@@ -364,12 +473,12 @@ def main():
         "config": config_block(world, n_global),
         "bits_per_symbol": bits_total / (n_local * chunk),
         "roundtrip_ok": bool(ok and ok_e2e),
+        "ttt_updates_timed": timed_boundaries,
         "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": n_global * chunk / (e2e_ms / 1000.0), "unit": "sym/s",
-                "h2d_bytes_per_step": int(words_h.numel() * 4 + nbits_h.numel() * 8) // chunk,
-                "d2h_bytes_per_step": int(b.n * 4),
-                "path": "StreamBatch.decode_chunk (pinned host segment in, host symbols out)"},
+                "h2d_bytes_per_step": h2d // chunk, "d2h_bytes_per_step": int(b.n * 4),
+                "path": "StreamBatch steps + LoraTTT with pinned host segments in, host symbols out"},
         "gpu_launches": int(launches),
         "kernel_ms_per_step": prof,
         "clocks": clk,
