@@ -20,8 +20,10 @@ using namespace altxs;
 
 namespace {
 
-constexpr int kSplit = 128;  // keys per attention split (fixed: numerics independent of n)
-constexpr int kAttnThreads = 128;
+#ifndef ALTXS_ATTN_SPLIT
+#define ALTXS_ATTN_SPLIT 256
+#endif
+constexpr int kSplit = ALTXS_ATTN_SPLIT;  // keys per attention split (fixed: numerics independent of n)
 constexpr int kCdfThreads = 512;
 
 // KV rows are stored in a 24-bit split format: fp32 rounded to nearest-even
@@ -32,9 +34,6 @@ constexpr int kCdfThreads = 512;
 __device__ __forceinline__ uint32_t round24(float x) {
     const uint32_t b = __float_as_uint(x);
     return (b + 0x7Fu + ((b >> 8) & 1u)) >> 8;  // 24-bit pattern
-}
-__device__ __forceinline__ float from24(uint32_t hi16, uint32_t lo8) {
-    return __uint_as_float((hi16 << 16) | (lo8 << 8));
 }
 __device__ __forceinline__ void store_kv_row(uint8_t *row, int hd, int k, float v) {
     const uint32_t r = round24(v);
@@ -234,158 +233,312 @@ __global__ void k_qkv_post(StepCtx c, int l) {
     }
 }
 
-// Split-K decode attention over the sliding window.  One CTA per
-// (split, kv head, stream): the split's K and V rows (contiguous fp16) are
-// brought into shared memory with two TMA bulk copies, then scores, softmax
-// partial (max, sum) and the weighted V sum for each query head of the group.
-__global__ void __launch_bounds__(kAttnThreads) k_attn_partial(StepCtx c, int l) {
-    extern __shared__ __align__(128) unsigned char smraw[];
-    __shared__ __align__(8) uint64_t bar[2];
-    __shared__ float red[32];
+// two floats from a u32 of two bf16 high halves and two low bytes (24-bit split)
+__device__ __forceinline__ void unpack24x2(uint32_t h, uint32_t lo2, float &f0, float &f1) {
+    // lo2: low byte of element 0 in bits 0-7, element 1 in bits 8-15, zeros above
+    f0 = __uint_as_float(__byte_perm(h, lo2, 0x1046));
+    f1 = __uint_as_float(__byte_perm(h, lo2, 0x3256));
+}
+
+// ---------------------------------------------------------------------------
+// Warp-pipelined split attention.  Item t of a layer (stream, kv head, split
+// of kSplit keys; split fastest) is taken by warp t mod (total warps).  A warp
+// streams its items' keys in chunks of 32 rows: lane 0 issues the TMA bulk
+// copies of a chunk's K and V rows into one of the warp's `slots` shared-memory
+// slots (one mbarrier each), and the warp computes on the oldest slot while
+// the others are in flight, so each warp keeps slots-1 chunks of HBM reads
+// outstanding with no CTA-wide barrier.  Within an item the softmax runs
+// online over its chunks (running max, rescaled sums).  The arithmetic of an
+// item is fixed, so the partials do not depend on the number of streams or on
+// which warp took the item.
+//
+// Lane layout (LPK = hd/8 lanes per key, 32/LPK keys per pass, LPK passes per
+// chunk): lane (kl = lane/LPK, ds = lane%LPK) holds dims ds*8..ds*8+7 of key
+// kl + (32/LPK)*p in pass p.  The LPK partial dots of a lane are summed across
+// its LPK-lane group by recursive halving, which leaves lane (kl, ds) with the
+// full score of key kl + (32/LPK)*ds: one score, one exp per lane per chunk.
+constexpr int kRingChunk = 32;     // key rows per TMA chunk
+constexpr int kRingMaxWarps = 8;   // warps per CTA
+constexpr int kRingMaxSlots = 4;   // chunk slots per warp
+#ifndef ALTXS_RING_WARPS
+#define ALTXS_RING_WARPS 2  // 2 warps x 2 slots x 12 KB (hd 64): four CTAs per SM
+#endif
+#ifndef ALTXS_RING_SLOTS
+#define ALTXS_RING_SLOTS 2
+#endif
+
+struct RingItem {
+    int i, kvh, sp, nvalid;
+    bool live;
+};
+
+__device__ __forceinline__ RingItem ring_item(const StepCtx &c, int t) {
     const Dims &D = c.D;
-    const int s = blockIdx.x, kvh = blockIdx.y, i = blockIdx.z;
-    const int hd = D.hd, G = D.H / D.Hkv;
-    float *part_base = c.part + (((int64_t)i * D.H + (int64_t)kvh * G) * D.nsplit + s) * (hd + 2);
-    if (!row_active(c.b, i) || c.b.tok[i] < 0) return;
-    const int64_t pos = c.b.pos[i];
-    const int npos = (int)(pos + 1 < (int64_t)D.ctx ? pos + 1 : (int64_t)D.ctx);
-    const int k0 = s * kSplit;
-    const int nvalid = max(0, min(min(kSplit, D.ctx - k0), npos - k0));
-    if (nvalid == 0) {
-        for (int g = 0; g < G; ++g) {
-            float *pp = part_base + (int64_t)g * D.nsplit * (hd + 2);
-            for (int k = threadIdx.x; k < hd; k += blockDim.x) pp[k] = 0.0f;
-            if (threadIdx.x == 0) {
-                pp[hd] = -INFINITY;
-                pp[hd + 1] = 0.0f;
-            }
-        }
-        return;
+    RingItem it;
+    it.sp = t % D.nsplit;
+    const int r = t / D.nsplit;
+    it.kvh = r % D.Hkv;
+    it.i = r / D.Hkv;
+    it.live = row_active(c.b, it.i) && c.b.tok[it.i] >= 0;
+    it.nvalid = 0;
+    if (it.live) {
+        const int64_t pos = c.b.pos[it.i];
+        const int npos = (int)(pos + 1 < (int64_t)D.ctx ? pos + 1 : (int64_t)D.ctx);
+        const int k0 = it.sp * kSplit;
+        it.nvalid = max(0, min(min(kSplit, D.ctx - k0), npos - k0));
     }
-    const int rb = 3 * hd;  // bytes per KV row (24-bit split format)
-    uint8_t *Ks = smraw;
-    uint8_t *Vs = Ks + (int64_t)kSplit * rb;
-    float *sc = reinterpret_cast<float *>(Vs + (int64_t)kSplit * rb);  // [G][kSplit]
-    float *accs = sc + (int64_t)G * kSplit;                            // [warps][G][hd]
-    const uint8_t *kvb = c.b.kv + ((int64_t)i * D.L + l) * 2 * D.Hkv * D.ctx * rb;
-    const uint8_t *Kg = kvb + ((int64_t)kvh * D.ctx + k0) * rb;
-    const uint8_t *Vg = kvb + ((int64_t)(D.Hkv + kvh) * D.ctx + k0) * rb;
-    const uint32_t bytes = (uint32_t)nvalid * rb;
-    if (threadIdx.x == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+    return it;
+}
+
+template <int LPK, int G>
+__global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int l, int n_items, int slots) {
+    constexpr int KPP = 32 / LPK;  // keys per pass
+    constexpr int HD = LPK * 8, RB = 3 * HD;
+    constexpr uint32_t kChunkBytes = (uint32_t)kRingChunk * RB;  // K (or V) rows of one chunk
+    constexpr unsigned FULL = 0xffffffffu;
+    extern __shared__ __align__(128) unsigned char smraw[];
+    __shared__ __align__(8) uint64_t bars[kRingMaxWarps * kRingMaxSlots];
+    const Dims &D = c.D;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int ds = lane % LPK, kl = lane / LPK;
+    const int GW = gridDim.x * W, gw = blockIdx.x * W + w;
+    uint8_t *wbuf = smraw + (int64_t)w * slots * 2 * kChunkBytes;
+    uint64_t *bar = bars + w * kRingMaxSlots;
+    if (lane == 0) {
+        for (int s = 0; s < slots; ++s) mbar_init(&bar[s], 1);
         fence_mbar_init();
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        mbar_expect_tx(&bar[0], bytes);
-        bulk_g2s(Ks, Kg, bytes, &bar[0]);
-        mbar_expect_tx(&bar[1], bytes);
-        bulk_g2s(Vs, Vg, bytes, &bar[1]);
+    __syncwarp();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+
+    // Load cursor (tracked by every lane, issued by lane 0): chunk lc of the
+    // lnch chunks of item lt.  After seek(), lt >= n_items or lc < lnch.
+    int lt = gw, lc = 0, lnch = 0;
+    RingItem lit{};
+    if (lt < n_items) {
+        lit = ring_item(c, lt);
+        lnch = (lit.nvalid + kRingChunk - 1) / kRingChunk;
     }
-    // q for the group's heads (registers): lane owns dims [ds*8, ds*8+8)
-    const int lpk = hd / 8, kpp = 32 / lpk;
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int ds = lane % lpk, kl = lane / lpk;
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-    const bool ok0 = mbar_wait_bounded(&bar[0], 0, kWaitLimit);
-    if (!__syncthreads_and(ok0)) {
-        if (threadIdx.x == 0) atomicOr(&c.b.ac[i].status, ALTXS_ST_TIMEOUT);
-        mbar_wait_bounded(&bar[0], 0, kWaitLimit);
-        mbar_wait_bounded(&bar[1], 0, kWaitLimit);
-        return;
-    }
-    for (int g = 0; g < G; ++g) {
-        const float *qh = c.q + ((int64_t)i * D.H + kvh * G + g) * hd + ds * 8;
-        float qv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) qv[u] = qh[u];
-        for (int j0 = 0; j0 < nvalid; j0 += nw * kpp) {
-            const int j = j0 + wid * kpp + kl;
-            float dot = 0.0f;
-            if (j < nvalid) {
-                const uint8_t *row = Ks + (int64_t)j * rb;
-                const uint4 hi = *reinterpret_cast<const uint4 *>(row + ds * 16);
-                const uint2 lo = *reinterpret_cast<const uint2 *>(row + 2 * hd + ds * 8);
-                const uint32_t h[4] = {hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const uint32_t l8 = (u < 2 ? lo.x : lo.y) >> (16 * (u & 1));
-                    const float f0 = from24(h[u] & 0xFFFFu, l8 & 0xFFu);
-                    const float f1 = from24(h[u] >> 16, (l8 >> 8) & 0xFFu);
-                    dot = __fmaf_rn(qv[2 * u], f0, dot);
-                    dot = __fmaf_rn(qv[2 * u + 1], f1, dot);
-                }
-            }
-            for (int o = 1; o < lpk; o <<= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, o));
-            if (j < nvalid && ds == 0) sc[g * kSplit + j] = __fmul_rn(dot, scale);
-        }
-    }
-    __syncthreads();
-    float mx[4], lsum[4];  // G <= 4 query heads per kv head
-    for (int g = 0; g < G; ++g) {
-        float m = -INFINITY;
-        for (int j = threadIdx.x; j < nvalid; j += blockDim.x) m = fmaxf(m, sc[g * kSplit + j]);
-        m = block_max(m, red);
-        __syncthreads();
-        float l = 0.0f;
-        for (int j = threadIdx.x; j < nvalid; j += blockDim.x) {
-            const float e = expf(__fsub_rn(sc[g * kSplit + j], m));
-            sc[g * kSplit + j] = e;
-            l = __fadd_rn(l, e);
-        }
-        l = block_sum(l, red);
-        mx[g] = m;
-        lsum[g] = l;
-    }
-    __syncthreads();
-    const bool ok1 = mbar_wait_bounded(&bar[1], 0, kWaitLimit);
-    if (!__syncthreads_and(ok1)) {
-        if (threadIdx.x == 0) atomicOr(&c.b.ac[i].status, ALTXS_ST_TIMEOUT);
-        mbar_wait_bounded(&bar[1], 0, kWaitLimit);
-        return;
-    }
-    for (int g = 0; g < G; ++g) {
-        float acc[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
-        for (int j0 = 0; j0 < nvalid; j0 += nw * kpp) {
-            const int j = j0 + wid * kpp + kl;
-            if (j < nvalid) {
-                const float e = sc[g * kSplit + j];
-                const uint8_t *row = Vs + (int64_t)j * rb;
-                const uint4 hi = *reinterpret_cast<const uint4 *>(row + ds * 16);
-                const uint2 lo = *reinterpret_cast<const uint2 *>(row + 2 * hd + ds * 8);
-                const uint32_t h[4] = {hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const uint32_t l8 = (u < 2 ? lo.x : lo.y) >> (16 * (u & 1));
-                    acc[2 * u] = __fmaf_rn(e, from24(h[u] & 0xFFFFu, l8 & 0xFFu), acc[2 * u]);
-                    acc[2 * u + 1] = __fmaf_rn(e, from24(h[u] >> 16, (l8 >> 8) & 0xFFu), acc[2 * u + 1]);
-                }
+    auto seek = [&]() {
+        while (lt < n_items && lc >= lnch) {
+            lt += GW;
+            lc = 0;
+            lnch = 0;
+            if (lt < n_items) {
+                lit = ring_item(c, lt);
+                lnch = (lit.nvalid + kRingChunk - 1) / kRingChunk;
             }
         }
-        // reduce lanes holding the same dims (xor over the key-lane bits)
-        for (int o = lpk; o < 32; o <<= 1)
+    };
+    auto issue = [&](int s) {
+        if (lane == 0) {
+            const int rows = min(kRingChunk, lit.nvalid - lc * kRingChunk);
+            const uint32_t bytes = (uint32_t)rows * RB;
+            const int64_t k0 = (int64_t)lit.sp * kSplit + lc * kRingChunk;
+            const uint8_t *kvb = c.b.kv + ((int64_t)lit.i * D.L + l) * 2 * D.Hkv * D.ctx * RB;
+            uint8_t *dst = wbuf + (int64_t)s * 2 * kChunkBytes;
+            mbar_expect_tx(&bar[s], 2 * bytes);
+            bulk_g2s(dst, kvb + ((int64_t)lit.kvh * D.ctx + k0) * RB, bytes, &bar[s]);
+            bulk_g2s(dst + kChunkBytes, kvb + ((int64_t)(D.Hkv + lit.kvh) * D.ctx + k0) * RB, bytes, &bar[s]);
+        }
+        ++lc;
+        seek();
+    };
+    seek();
+    uint32_t par = 0, pend = 0;  // bit s: parity of slot s's next completion / a copy into s in flight
+    for (int s = 0; s < slots && lt < n_items; ++s) {
+        issue(s);
+        pend |= 1u << s;
+    }
+    int slot = 0;
+    for (int t = gw; t < n_items; t += GW) {
+        const RingItem it = ring_item(c, t);
+        if (!it.live) continue;
+        float *part_base = c.part + (((int64_t)it.i * D.H + (int64_t)it.kvh * G) * D.nsplit + it.sp) * (HD + 2);
+        if (it.nvalid == 0) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) acc[u] = __fadd_rn(acc[u], __shfl_xor_sync(0xffffffffu, acc[u], o));
-        if (kl == 0) {
+            for (int g = 0; g < G; ++g) {
+                float *pp = part_base + (int64_t)g * D.nsplit * (HD + 2);
+                for (int k = lane; k < HD; k += 32) pp[k] = 0.0f;
+                if (lane == 0) {
+                    pp[HD] = -INFINITY;
+                    pp[HD + 1] = 0.0f;
+                }
+            }
+            continue;
+        }
+        float qv[G][8], M[G], Ls[G], acc[G][8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) accs[((int64_t)wid * G + g) * hd + ds * 8 + u] = acc[u];
+        for (int g = 0; g < G; ++g) {
+            M[g] = -INFINITY;
+            Ls[g] = 0.0f;
+            const float4 *qh =
+                reinterpret_cast<const float4 *>(c.q + ((int64_t)it.i * D.H + it.kvh * G + g) * HD + ds * 8);
+            const float4 a = qh[0], b2 = qh[1];
+            qv[g][0] = a.x, qv[g][1] = a.y, qv[g][2] = a.z, qv[g][3] = a.w;
+            qv[g][4] = b2.x, qv[g][5] = b2.y, qv[g][6] = b2.z, qv[g][7] = b2.w;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[g][u] = 0.0f;
+        }
+        const int nch = (it.nvalid + kRingChunk - 1) / kRingChunk;
+        for (int cc = 0; cc < nch; ++cc) {
+            const bool ok = __all_sync(FULL, mbar_wait_bounded(&bar[slot], (par >> slot) & 1u, kWaitLimit));
+            if (!ok) {  // a copy did not land in time: record it, let this warp's copies drain, leave
+                if (lane == 0) atomicOr(&c.b.ac[it.i].status, ALTXS_ST_TIMEOUT);
+                for (int s = 0; s < slots; ++s)
+                    if (pend & (1u << s)) mbar_wait_bounded(&bar[s], (par >> s) & 1u, kWaitLimit);
+                return;
+            }
+            par ^= 1u << slot;
+            pend &= ~(1u << slot);
+            const uint8_t *Kc = wbuf + (int64_t)slot * 2 * kChunkBytes;
+            const uint8_t *Vc = Kc + kChunkBytes;
+            const int nv = min(kRingChunk, it.nvalid - cc * kRingChunk);
+            // ---- scores: partial dots over this lane's 8 dims, one per pass
+            float pd[G][LPK];
+#pragma unroll
+            for (int p = 0; p < LPK; ++p) {
+                const int j = kl + KPP * p;
+                float f[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) f[u] = 0.0f;
+                if (j < nv) {
+                    const uint8_t *row = Kc + j * RB;
+                    const uint4 hi = *reinterpret_cast<const uint4 *>(row + ds * 16);
+                    const uint2 lo = *reinterpret_cast<const uint2 *>(row + 2 * HD + ds * 8);
+                    unpack24x2(hi.x, lo.x & 0xFFFFu, f[0], f[1]);
+                    unpack24x2(hi.y, lo.x >> 16, f[2], f[3]);
+                    unpack24x2(hi.z, lo.y & 0xFFFFu, f[4], f[5]);
+                    unpack24x2(hi.w, lo.y >> 16, f[6], f[7]);
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float dot = 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) dot = __fmaf_rn(qv[g][u], f[u], dot);
+                    pd[g][p] = dot;
+                }
+            }
+            // ---- recursive-halving sum across the LPK lanes of a key group,
+            // then the online softmax update with this chunk's scores
+            const int jd = kl + KPP * ds;  // the key whose score this lane ends with
+            float e[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+#pragma unroll
+                for (int o = LPK / 2; o >= 1; o >>= 1) {
+                    const bool up = (ds & o) != 0;
+#pragma unroll
+                    for (int q = 0; q < o; ++q) {
+                        const float send = up ? pd[g][q] : pd[g][q + o];
+                        const float keep = up ? pd[g][q + o] : pd[g][q];
+                        pd[g][q] = __fadd_rn(keep, __shfl_xor_sync(FULL, send, o));
+                    }
+                }
+                const float s = jd < nv ? __fmul_rn(pd[g][0], scale) : -INFINITY;
+                const float mn = fmaxf(M[g], warp_max(s));
+                const float alpha = expf(__fsub_rn(M[g], mn));
+                e[g] = jd < nv ? expf(__fsub_rn(s, mn)) : 0.0f;
+                Ls[g] = __fmaf_rn(Ls[g], alpha, e[g]);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc[g][u] = __fmul_rn(acc[g][u], alpha);
+                M[g] = mn;
+            }
+            // ---- weighted V rows
+#pragma unroll
+            for (int p = 0; p < LPK; ++p) {
+                const int j = kl + KPP * p;
+                float ej[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) ej[g] = __shfl_sync(FULL, e[g], kl * LPK + p);
+                if (j < nv) {
+                    const uint8_t *row = Vc + j * RB;
+                    const uint4 hi = *reinterpret_cast<const uint4 *>(row + ds * 16);
+                    const uint2 lo = *reinterpret_cast<const uint2 *>(row + 2 * HD + ds * 8);
+                    float f[8];
+                    unpack24x2(hi.x, lo.x & 0xFFFFu, f[0], f[1]);
+                    unpack24x2(hi.y, lo.x >> 16, f[2], f[3]);
+                    unpack24x2(hi.z, lo.y & 0xFFFFu, f[4], f[5]);
+                    unpack24x2(hi.w, lo.y >> 16, f[6], f[7]);
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) acc[g][u] = __fmaf_rn(ej[g], f[u], acc[g][u]);
+                }
+            }
+            __syncwarp();  // every lane is done with this slot: refill it
+            if (lt < n_items) {
+                issue(slot);
+                pend |= 1u << slot;
+            }
+            slot = slot + 1 == slots ? 0 : slot + 1;
+        }
+        // ---- item partial: (max, sum of exp, unnormalised weighted V)
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int o = LPK; o < 32; o <<= 1)
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc[g][u] = __fadd_rn(acc[g][u], __shfl_xor_sync(FULL, acc[g][u], o));
+            const float lsum = warp_sum(Ls[g]);
+            float *pp = part_base + (int64_t)g * D.nsplit * (HD + 2);
+            if (kl == 0) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) pp[ds * 8 + u] = acc[g][u];
+            }
+            if (lane == 0) {
+                pp[HD] = M[g];
+                pp[HD + 1] = lsum;
+            }
         }
     }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-        const int g = idx / hd, k = idx - g * hd;
-        float a = 0.0f;
-        for (int w2 = 0; w2 < nw; ++w2) a = __fadd_rn(a, accs[((int64_t)w2 * G + g) * hd + k]);
-        part_base[(int64_t)g * D.nsplit * (hd + 2) + k] = a;
+}
+
+// Launch of the ring kernel for this model's head size and group size:
+// a persistent grid of as many CTAs as fit on the device at once.
+template <int LPK, int G>
+cudaError_t launch_ring(const StepCtx &c, int l, cudaStream_t st) {
+    const Dims &D = c.D;
+    const int warps = ALTXS_RING_WARPS, slots = ALTXS_RING_SLOTS;
+    const size_t smem = (size_t)warps * slots * 2 * kRingChunk * 3 * (LPK * 8);
+    static int grid_max[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (grid_max[dev] == 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_ring<LPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        int per_sm = 0, sms = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attn_ring<LPK, G>, warps * 32, smem);
+        if (e != cudaSuccess) return e;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        grid_max[dev] = (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 1);
     }
-    if (threadIdx.x < G) {
-        float *pp = part_base + (int64_t)threadIdx.x * D.nsplit * (hd + 2);
-        pp[hd] = mx[threadIdx.x];
-        pp[hd + 1] = lsum[threadIdx.x];
+    const int n_items = D.n * D.Hkv * D.nsplit;
+    const int need = (n_items + warps - 1) / warps;
+    const int grid = need < grid_max[dev] ? need : grid_max[dev];
+    k_attn_ring<LPK, G><<<grid, warps * 32, smem, st>>>(c, l, n_items, slots);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn(const StepCtx &c, int l, cudaStream_t st) {
+    const int G = c.D.H / c.D.Hkv;
+#define ALTXS_RING_G(LPK)                               \
+    switch (G) {                                        \
+        case 1: return launch_ring<LPK, 1>(c, l, st);   \
+        case 2: return launch_ring<LPK, 2>(c, l, st);   \
+        case 3: return launch_ring<LPK, 3>(c, l, st);   \
+        case 4: return launch_ring<LPK, 4>(c, l, st);   \
+        default: return cudaErrorInvalidValue;          \
     }
+    switch (c.D.hd / 8) {
+        case 2: ALTXS_RING_G(2)
+        case 4: ALTXS_RING_G(4)
+        case 8: ALTXS_RING_G(8)
+        case 16: ALTXS_RING_G(16)
+        default: return cudaErrorInvalidValue;
+    }
+#undef ALTXS_RING_G
 }
 
 // Fixed-order merge of the split partials -> y [n][H*hd]
@@ -647,14 +800,11 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     c.lt = take((int64_t)D.n * (D.r > 0 ? D.r : 1));
 
     ALTXS_LAUNCH(::altxs::kKEmbed, st, k_embed<<<D.n, 128, 0, st>>>(c));
-    const int G = D.H / D.Hkv;
-    const size_t attn_sm = (size_t)2 * kSplit * 3 * D.hd + (size_t)G * kSplit * 4 + (size_t)(kAttnThreads / 32) * G * D.hd * 4;
     {
         static bool attr_done[64] = {};
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-            cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
             cudaFuncSetAttribute(k_cdf_code, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
             if (dev >= 0 && dev < 64) attr_done[dev] = true;
         }
@@ -675,7 +825,11 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.epi = kEpiStore;
         if ((rc = launch_qmm(a, st))) return rc;
         ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, l));
-        ALTXS_LAUNCH(::altxs::kKAttn, st, k_attn_partial<<<dim3(D.nsplit, D.Hkv, D.n), kAttnThreads, attn_sm, st>>>(c, l));
+        {
+            cudaError_t ae = cudaSuccess;
+            ALTXS_LAUNCH(::altxs::kKAttn, st, ae = launch_attn(c, l, st));
+            if (ae != cudaSuccess) return ALTXS_ECUDA;
+        }
         ALTXS_LAUNCH(::altxs::kKAttnMerge, st, k_attn_merge<<<D.n * D.H, D.hd, 0, st>>>(c));
         a.X = c.y;
         a.W = w->o;

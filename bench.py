@@ -442,11 +442,11 @@ def main():
         avg_ms = attn["ms_per_step"] * K / attn["launches"]
         achieved = bytes_launch / (avg_ms / 1000.0) / 1e9
         traffic = None
-        tfile = ROOT / "profiles" / "attn_partial_traffic.json"
+        tfile = ROOT / "profiles" / "attn_ring_traffic.json"
         if tfile.exists():
             tj = json.loads(tfile.read_text())
             traffic = tj["dram_bytes_per_kv_row"] * n_local * cfg.num_kv_heads * cfg.ctx * 2
-        roof = {"bound": "hbm", "kernel": "k_attn_partial", "achieved": achieved,
+        roof = {"bound": "hbm", "kernel": "k_attn_ring", "achieved": achieved,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "traffic": traffic, "bytes_per_launch": bytes_launch, "avg_launch_ms": avg_ms,
                 "peak_source": f"{peak_kind} hbm_gbs"}
