@@ -23,7 +23,7 @@ EXPORTS = (
     "altxs_cdf_from_logits", "altxs_workspace_bytes", "altxs_lora_floats", "altxs_step",
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
-    "altxs_dequant",
+    "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -54,13 +54,17 @@ class ModelDesc(C.Structure):
     ]
 
 
+class SplitPlanes(C.Structure):
+    _fields_ = [(f"{m}_{h}", C.c_void_p) for m in ("emb", "qkv", "o", "up", "down") for h in ("hi", "lo")]
+
+
 class Weights(C.Structure):
     _fields_ = [
         ("emb", QMat), ("qkv", QMat), ("o", QMat), ("up", QMat), ("down", QMat),
         ("q_gain", C.c_void_p), ("attn_scale", C.c_void_p), ("mlp_scale", C.c_void_p),
         ("resid_mix", C.c_void_p), ("ln_scale", C.c_void_p), ("skip_weights", C.c_void_p),
         ("skip_gates", C.c_void_p), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
-        ("rope_positions", C.c_int64),
+        ("rope_positions", C.c_int64), ("split", C.POINTER(SplitPlanes)),
     ]
 
 
@@ -122,6 +126,9 @@ def lib():
                                            C.POINTER(TttHparams), vp, C.c_int, vp, vp, vp, C.c_int, vp, vp, i64,
                                            vp]),
             "altxs_dequant": (C.c_int, [C.POINTER(QMat), vp, i64, vp]),
+            "altxs_split_weights": (C.c_int, [C.POINTER(QMat), vp, vp, vp]),
+            "altxs_linear_workspace_bytes": (i64, [C.c_int, C.c_int]),
+            "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

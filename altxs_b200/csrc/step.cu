@@ -15,6 +15,7 @@
 #include "model.cuh"
 #include "prof.cuh"
 #include "qmm.cuh"
+#include "tc.cuh"
 
 using namespace altxs;
 
@@ -54,6 +55,9 @@ struct StepCtx {
     LoraOff lo;
     // workspace
     float *x, *x0, *nrm, *nrm2, *skip, *qkv, *q, *part, *y, *ao, *hid, *logits, *lt;
+    // tensor-core path: hi/lo bf16 planes of the linear layers' inputs
+    int tc;
+    uint16_t *nrm_h, *nrm_l, *y_h, *y_l, *nrm2_h, *nrm2_l, *hid_h, *hid_l;
 };
 
 __device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return !b.active || b.active[i]; }
@@ -113,7 +117,11 @@ __global__ void k_prenorm(StepCtx c, int l) {
     const float ln = c.w.ln_scale[l];
     __syncthreads();
     float *nr = c.nrm + (int64_t)i * d;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) nr[k] = __fmul_rn(__fmul_rn(x[k], inv), ln);
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(x[k], inv), ln);
+        nr[k] = v;
+        if (c.tc) split_store(c.nrm_h, c.nrm_l, (int64_t)i * d + k, v);
+    }
 }
 
 // t[r] = A[r] . x  (warp per rank row; lane-strided sums, fixed tree)
@@ -559,7 +567,9 @@ __global__ void k_attn_merge(StepCtx c) {
             a = __fmaf_rn(q[k], f, a);
         }
     }
-    c.y[(int64_t)i * D.d + h * D.hd + k] = l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
+    const float yv = l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
+    c.y[(int64_t)i * D.d + h * D.hd + k] = yv;
+    if (c.tc) split_store(c.y_h, c.y_l, (int64_t)i * D.d + h * D.hd + k, yv);
 }
 
 // o-LoRA on the pre-attention normed input, residual, rms*ln for the MLP.
@@ -589,7 +599,11 @@ __global__ void k_post_attn(StepCtx c, int l) {
     const float ln = c.w.ln_scale[l];
     __syncthreads();
     float *nr = c.nrm2 + (int64_t)i * d;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) nr[k] = __fmul_rn(__fmul_rn(x[k], inv), ln);
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(x[k], inv), ln);
+        nr[k] = v;
+        if (c.tc) split_store(c.nrm2_h, c.nrm2_l, (int64_t)i * d + k, v);
+    }
 }
 
 // final RMSNorm (+ lm_head LoRA t)
@@ -608,6 +622,7 @@ __global__ void k_final(StepCtx c) {
         const float v = __fmul_rn(x[k], inv);
         nr[k] = v;
         sm[k] = v;
+        if (c.tc) split_store(c.nrm_h, c.nrm_l, (int64_t)i * d + k, v);
     }
     __syncthreads();
     if (R > 0 && c.b.lora && (c.dsc.lora_mask & 16)) {
@@ -707,6 +722,7 @@ inline int64_t ws_size(const Dims &D) {
     s += A((int64_t)D.n * D.F);                       // hid
     s += A((int64_t)D.n * D.V);                       // logits
     s += A((int64_t)D.n * (D.r > 0 ? D.r : 1));       // lm LoRA t
+    s += 3 * A((int64_t)D.n * D.d);                   // hi/lo bf16 planes of nrm, y, nrm2
     return s;
 }
 
@@ -798,6 +814,55 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     c.hid = take((int64_t)D.n * D.F);
     c.logits = take((int64_t)D.n * D.V);
     c.lt = take((int64_t)D.n * (D.r > 0 ? D.r : 1));
+    {
+        const int64_t nd = (int64_t)D.n * D.d;
+        c.nrm_h = reinterpret_cast<uint16_t *>(take(nd));
+        c.nrm_l = c.nrm_h + nd;
+        c.y_h = reinterpret_cast<uint16_t *>(take(nd));
+        c.y_l = c.y_h + nd;
+        c.nrm2_h = reinterpret_cast<uint16_t *>(take(nd));
+        c.nrm2_l = c.nrm2_h + nd;
+        // the MLP hidden planes take the place of the fp32 hidden buffer (unused on this path)
+        c.hid_h = reinterpret_cast<uint16_t *>(c.hid);
+        c.hid_l = c.hid_h + (int64_t)D.n * D.F;
+    }
+    const altxs_split_planes *sp = w->split;
+    c.tc = sp != nullptr;
+    if (sp && (!sp->emb_hi || !sp->emb_lo || !sp->qkv_hi || !sp->qkv_lo || !sp->o_hi || !sp->o_lo || !sp->up_hi ||
+               !sp->up_lo || !sp->down_hi || !sp->down_lo))
+        return ALTXS_EINVAL;
+    // one linear layer: tensor cores from the bf16 planes, or CUDA cores from the packed codes
+    auto linear = [&](const QmmArgs &q, const uint16_t *xh, const uint16_t *xl, const uint16_t *wh, const uint16_t *wl,
+                      uint16_t *ph, uint16_t *pl) -> int {
+        if (!c.tc) return launch_qmm(q, st);
+        TcArgs t{};
+        t.a_hi = xh;
+        t.a_lo = xl;
+        t.lda = q.ldx;
+        t.M = q.M;
+        t.b_hi = wh;
+        t.b_lo = wl;
+        t.b_rows = q.W.rows;
+        t.row0 = q.row0;
+        t.N = q.N;
+        t.K = q.K;
+        t.epi = q.epi;
+        t.Y = ph ? nullptr : q.Y;
+        t.ldy = q.ldy;
+        t.R = q.R;
+        t.ldr = q.ldr;
+        t.colscale = q.colscale;
+        t.Y2 = q.Y2;
+        t.ldy2 = q.ldy2;
+        t.p_hi = ph;
+        t.p_lo = pl;
+        t.ldp = q.N;
+        if (b->ac) {
+            t.status = &b->ac[0].status;
+            t.status_stride = sizeof(altxs_ac_state) / sizeof(uint32_t);
+        }
+        return launch_tc(t, st);
+    };
 
     ALTXS_LAUNCH(::altxs::kKEmbed, st, k_embed<<<D.n, 128, 0, st>>>(c));
     {
@@ -823,7 +888,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.Y = c.qkv;
         a.ldy = D.qkv_n;
         a.epi = kEpiStore;
-        if ((rc = launch_qmm(a, st))) return rc;
+        if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->qkv_hi : nullptr, c.tc ? sp->qkv_lo : nullptr, nullptr, nullptr))) return rc;
         ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, l));
         {
             cudaError_t ae = cudaSuccess;
@@ -837,7 +902,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.N = D.d;
         a.Y = c.ao;
         a.ldy = D.d;
-        if ((rc = launch_qmm(a, st))) return rc;
+        if ((rc = linear(a, c.y_h, c.y_l, c.tc ? sp->o_hi : nullptr, c.tc ? sp->o_lo : nullptr, nullptr, nullptr))) return rc;
         ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l));
         a.X = c.nrm2;
         a.W = w->up;
@@ -846,7 +911,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.Y = c.hid;
         a.ldy = D.F;
         a.epi = kEpiLeaky2;
-        if ((rc = launch_qmm(a, st))) return rc;
+        if ((rc = linear(a, c.nrm2_h, c.nrm2_l, c.tc ? sp->up_hi : nullptr, c.tc ? sp->up_lo : nullptr, c.tc ? c.hid_h : nullptr, c.tc ? c.hid_l : nullptr))) return rc;
         a.X = c.hid;
         a.ldx = D.F;
         a.W = w->down;
@@ -861,7 +926,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.colscale = w->mlp_scale + (int64_t)l * D.d;
         a.Y2 = l < D.enc ? c.skip + (int64_t)l * D.n * D.d : nullptr;
         a.ldy2 = D.d;
-        if ((rc = launch_qmm(a, st))) return rc;
+        if ((rc = linear(a, c.hid_h, c.hid_l, c.tc ? sp->down_hi : nullptr, c.tc ? sp->down_lo : nullptr, nullptr, nullptr))) return rc;
     }
     ALTXS_LAUNCH(::altxs::kKFinal, st, k_final<<<D.n, 128, D.d * 4, st>>>(c));
     QmmArgs a{};
@@ -875,7 +940,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     a.Y = c.logits;
     a.ldy = D.V;
     a.epi = kEpiStore;
-    if ((rc = launch_qmm(a, st))) return rc;
+    if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->emb_hi : nullptr, c.tc ? sp->emb_lo : nullptr, nullptr, nullptr))) return rc;
     ALTXS_LAUNCH(::altxs::kKCdfCode, st, k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode));
     return ALTXS_OK;
 }

@@ -54,9 +54,17 @@ def lora_mask(cfg: ModelConfig) -> int:
 
 
 class DeviceModel:
-    """One model resident on one GPU."""
+    """One model resident on one GPU.
 
-    def __init__(self, weights: ModelWeights, device: torch.device | str, *, rope_positions: int = 1 << 16):
+    ``tensor_cores=True`` (default) also keeps the hi/lo bf16 planes of every
+    mixed-bit matrix (4 bytes per weight) and runs the step's linear layers on
+    the tensor cores; ``False`` runs them on CUDA cores from the packed codes.
+    The two differ in the last bits of the logits, so an encoder and its
+    decoder must use the same setting.
+    """
+
+    def __init__(self, weights: ModelWeights, device: torch.device | str, *, rope_positions: int = 1 << 16,
+                 tensor_cores: bool = True):
         self.cfg = cfg = weights.cfg
         cfg.validate()
         self.device = device = torch.device(device)
@@ -92,6 +100,8 @@ class DeviceModel:
             logit_softcap=cfg.logit_softcap, lora_scale=cfg.lora_scale if cfg.lora_enabled else 0.0,
         )
         self.lora_floats = int(_lib.lib().altxs_lora_floats(C.byref(self.desc)))
+        self.tensor_cores = bool(tensor_cores)
+        self._split = self._split_planes() if self.tensor_cores else None
 
     def _up(self, a: np.ndarray) -> torch.Tensor:
         t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
@@ -110,6 +120,20 @@ class DeviceModel:
             glut=glut.data_ptr() if glut is not None else None,
             rows=p.rows, cols=p.cols,
         )
+
+    def _split_planes(self) -> _lib.SplitPlanes:
+        L = _lib.lib()
+        fields = {}
+        self._split_bufs = []
+        for name in ("emb", "qkv", "o", "up", "down"):
+            q = self.q[name]
+            hi = torch.empty((q.rows, q.cols), dtype=torch.bfloat16, device=self.device)
+            lo = torch.empty_like(hi)
+            _lib.check(L.altxs_split_weights(C.byref(q), hi.data_ptr(), lo.data_ptr(), _stream_handle(self.device)),
+                       "altxs_split_weights")
+            self._split_bufs += [hi, lo]
+            fields[f"{name}_hi"], fields[f"{name}_lo"] = hi.data_ptr(), lo.data_ptr()
+        return _lib.SplitPlanes(**fields)
 
     def ensure_rope(self, n_pos: int) -> None:
         """RoPE tables must cover every absolute position a stream reaches."""
@@ -149,6 +173,7 @@ class DeviceModel:
                 ln_scale=s["ln_scale"].data_ptr(), skip_weights=s["skip_weights"].data_ptr(),
                 skip_gates=s["skip_gates"].data_ptr(), rope_cos=self.rope_cos.data_ptr(),
                 rope_sin=self.rope_sin.data_ptr(), rope_positions=self.rope_positions,
+                split=C.pointer(self._split) if self._split is not None else None,
             )
         return self._weights_struct
 

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: decode symbols/sec of the 33M, 3.15-bpw model-and-code loop.
 
-Workload (BASELINE config "box-scale sharded run"): 2048 independent streams
+Workload (the reference's "box-scale sharded run" configuration): 2048 independent streams
 split evenly over N GPUs (one process per GPU), the 33M model (8L/512d/8h,
 MLP 2048, V 16384) with seeded random mixed 2/3/4-bit weights, sliding
 window filled to 2048 of 2048, symbols from the seeded Zipf-Markov source.

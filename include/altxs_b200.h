@@ -135,6 +135,19 @@ typedef struct altxs_model_desc {
     float logit_softcap, lora_scale;
 } altxs_model_desc;
 
+/* Tensor-core operand form of the five mixed-bit matrices: every dequantised
+ * weight w = level*scale as two bf16 planes hi = bf16(w), lo = bf16(w - hi)
+ * ([rows][cols], row stride cols), filled once by altxs_split_weights.
+ * hi + lo == w exactly for the 2/3/4-bit symmetric levels.  No counterpart
+ * in the reference, which multiplies dequantised fp32/bf16 tensors. */
+typedef struct altxs_split_planes {
+    const uint16_t *emb_hi, *emb_lo;
+    const uint16_t *qkv_hi, *qkv_lo;
+    const uint16_t *o_hi, *o_lo;
+    const uint16_t *up_hi, *up_lo;
+    const uint16_t *down_hi, *down_lo;
+} altxs_split_planes;
+
 typedef struct altxs_weights {
     altxs_qmat emb;  /* [V][d], tied LM head */
     altxs_qmat qkv;  /* [L*(d+2*kv)][d]: per layer q rows, k rows, v rows */
@@ -151,6 +164,12 @@ typedef struct altxs_weights {
     const float *rope_cos;     /* [rope_positions][rope_dims/2] */
     const float *rope_sin;
     int64_t rope_positions;
+    /* NULL: the step's linear layers run on CUDA cores in exact fp32 order
+     * (sum over 64-wide groups of scale * sum of level*x).  Non-NULL: they run
+     * on the tensor cores from these planes (products within 2^-16 relative).
+     * Either way results do not depend on the batch; an encoder and its
+     * decoder must make the same choice. */
+    const altxs_split_planes *split;
 } altxs_weights;
 
 /* Per-stream state and scratch of a batch of n streams.  Stream i of the
@@ -228,6 +247,21 @@ typedef struct altxs_dense_weights {
 /* out[r][c] = exact fp32 value of m[r][c] (row stride ld floats). */
 int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t stream);
 
+/* hi/lo bf16 planes [m->rows][m->cols] of a mixed-bit matrix (see
+ * altxs_split_planes); both 16-byte aligned. */
+int altxs_split_weights(const altxs_qmat *m, uint16_t *hi, uint16_t *lo, altxs_stream_t stream);
+
+/* One linear layer, Y[i][j] = sum_k X[i][k] * m[row0 + j][k] for i < M,
+ * j < N (X row stride m->cols, Y row stride N): the reference's
+ * F.linear on the dequantised weight (altxs src/xsa_ttt/model.py:123-127,
+ * CastedLinear.forward).  With w_hi/w_lo (planes
+ * of m from altxs_split_weights) it runs on the tensor cores and needs
+ * altxs_linear_workspace_bytes(M, m->cols) of device workspace; without, on
+ * CUDA cores (workspace unused). */
+int64_t altxs_linear_workspace_bytes(int M, int K);
+int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo, int row0, int N, const float *X,
+                 int M, float *Y, void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+
 /* Workspace for one update over a T-token window (bytes). */
 int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T);
 
@@ -246,7 +280,7 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
                      altxs_stream_t stream);
 
 /* ---- accounting -----------------------------------------------------------
- * No counterpart in the reference (which has no tracing, SURVEY 5); these
+ * No counterpart in the reference (which has no tracing); these
  * give the benchmark per-kernel device time measured live on the launch
  * stream and the number of kernels launched. */
 

@@ -1,6 +1,6 @@
 """Timed CPU baseline: the reference's eager fp32 decode path, restated.
 
-TEST/BASELINE INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).  Used by
+Test and CPU-baseline infrastructure only (see ``oracle/__init__.py``).  Used by
 ``bench.py`` for its ``cpu_baseline`` leg and for ``--impl reference``: one
 stream of the benchmark workload (33M model, full ``ctx`` window) is decoded
 symbol by symbol on the host cores with the torch fp32 step

@@ -35,7 +35,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("ALTXS_REFERENCE", "/root/reference"))
+if "ALTXS_REFERENCE" not in os.environ:
+    sys.exit("set ALTXS_REFERENCE to the root of a read-only altvectra/altxs checkout")
+REF = Path(os.environ["ALTXS_REFERENCE"])
 sys.path.insert(0, str(REPO))
 for p in (REF / "src", REF / "src" / "model"):
     sys.path.insert(0, str(p))

@@ -1,0 +1,90 @@
+"""One mixed-bit linear layer through ``altxs_linear``: tensor cores and CUDA
+cores against a float64 product of the exact dequantised weights."""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from altxs_b200 import codec as Cd
+from altxs_b200.config import ModelConfig
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+CFG = dict(vocab_size=1000, num_layers=2, model_dim=256, num_heads=4, num_kv_heads=2, mlp_mult=4.0,
+           rope_dims=16, block_size=32, seed=11)
+
+
+@pytest.fixture(scope="module")
+def model():
+    from altxs_b200.engine import DeviceModel
+
+    cfg = ModelConfig(**CFG)
+    return DeviceModel(Cd.synth_weights(cfg, seed=21), DEV)
+
+
+def _dense(dm, name):
+    from altxs_b200 import _lib
+
+    q = dm.q[name]
+    t = torch.empty((q.rows, q.cols), dtype=torch.float32, device=DEV)
+    _lib.check(_lib.lib().altxs_dequant(C.byref(q), t.data_ptr(), q.cols, None), "altxs_dequant")
+    return t.cpu().numpy().astype(np.float64)
+
+
+def _linear(dm, name, X, row0, N, tensor_cores):
+    from altxs_b200 import _lib
+
+    L = _lib.lib()
+    q = dm.q[name]
+    M = X.shape[0]
+    Xd = torch.as_tensor(X, device=DEV).contiguous()
+    Y = torch.full((M, N), float("nan"), dtype=torch.float32, device=DEV)
+    ws_b = int(L.altxs_linear_workspace_bytes(M, q.cols))
+    ws = torch.empty(max(ws_b, 1), dtype=torch.uint8, device=DEV)
+    sp = dm._split
+    hi = getattr(sp, f"{name}_hi") if tensor_cores else None
+    lo = getattr(sp, f"{name}_lo") if tensor_cores else None
+    rc = L.altxs_linear(C.byref(q), hi, lo, row0, N, Xd.data_ptr(), M, Y.data_ptr(), ws.data_ptr(), ws_b, None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return Y.cpu().numpy()
+
+
+def test_split_planes_are_exact_for_symmetric_levels(model):
+    """hi + lo reproduces every dequantised weight of the 2/3/4-bit groups."""
+    for name in ("qkv", "down", "emb"):
+        W = _dense(model, name)
+        hi = model._split_bufs[2 * ("emb", "qkv", "o", "up", "down").index(name)].float().cpu().numpy()
+        lo = model._split_bufs[2 * ("emb", "qkv", "o", "up", "down").index(name) + 1].float().cpu().numpy()
+        assert np.array_equal((hi.astype(np.float64) + lo), W), name
+
+
+@pytest.mark.parametrize("tensor_cores", [True, False])
+@pytest.mark.parametrize("name,row0,N,M", [("qkv", 0, 512, 1), ("qkv", 512, 512, 130), ("down", 256, 256, 300),
+                                          ("emb", 0, 1000, 77), ("up", 1024, 136, 5)])
+def test_linear_matches_float64(model, tensor_cores, name, row0, N, M):
+    W = _dense(model, name)
+    rng = np.random.default_rng(M + N)
+    X = rng.normal(0, 1, size=(M, W.shape[1])).astype(np.float32)
+    got = _linear(model, name, X, row0, N, tensor_cores)
+    ref = X.astype(np.float64) @ W[row0: row0 + N].T
+    bound = np.abs(X.astype(np.float64)) @ np.abs(W[row0: row0 + N]).T
+    # tensor cores: products within 2^-16 relative; CUDA cores: fp32 rounding
+    rel = 2.0 ** -15 if tensor_cores else 2.0 ** -18
+    assert np.all(np.isfinite(got))
+    assert np.all(np.abs(got - ref) <= rel * bound + 1e-30), float(np.max(np.abs(got - ref) / (bound + 1e-30)))
+
+
+def test_tensor_core_rows_do_not_depend_on_the_batch(model):
+    """Row i of a 300-row call equals the same row computed alone, bit for bit."""
+    rng = np.random.default_rng(5)
+    X = rng.normal(0, 1, size=(300, 256)).astype(np.float32)
+    full = _linear(model, "qkv", X, 0, 512, True)
+    for i in (0, 127, 128, 255, 299):
+        alone = _linear(model, "qkv", X[i: i + 1], 0, 512, True)
+        assert np.array_equal(alone.view(np.uint32), full[i: i + 1].view(np.uint32)), i

@@ -63,13 +63,14 @@ def _lora_vec(cfg, rng):
     return np.concatenate(flat), lo
 
 
+@pytest.mark.parametrize("tensor_cores", [True, False])
 @pytest.mark.parametrize("use_lora", [False, True])
-def test_step_logits_match_oracle(use_lora):
+def test_step_logits_match_oracle(use_lora, tensor_cores):
     from altxs_b200.engine import DeviceModel
 
     cfg = _small()
     w = C.synth_weights(cfg, seed=7)
-    dm = DeviceModel(w, DEV)
+    dm = DeviceModel(w, DEV, tensor_cores=tensor_cores)
     om = OracleModel(OracleWeights.from_model_weights(w))
     rng = np.random.default_rng(1)
     T = 80  # > ctx: exercises the sliding window
@@ -94,20 +95,25 @@ def test_step_matches_reference_golden(golden):
     assert err < TOL, err
 
 
-def test_step_is_batch_independent():
-    """Stream 0's logits are bit-identical alone (GEMV path) and in a batch of 40
-    (tiled path), whatever the other streams hold."""
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_step_is_batch_independent(tensor_cores):
+    """A stream's logits are bit-identical alone and inside batches of 40 and
+    200 (first slot; slot 137, i.e. the second 128-row tile and another
+    tensor-memory lane), whatever the other streams hold.  On CUDA cores this
+    also crosses the GEMV/tiled split."""
     from altxs_b200.engine import DeviceModel
 
     cfg = _small(block_size=64)
-    dm = DeviceModel(C.synth_weights(cfg, seed=3), DEV)
+    dm = DeviceModel(C.synth_weights(cfg, seed=3), DEV, tensor_cores=tensor_cores)
     rng = np.random.default_rng(2)
-    T = 40
+    T = 24
     base = rng.integers(0, cfg.vocab_size, size=T)
     alone = _run_logits(dm, [base])[0]
-    others = [rng.integers(0, cfg.vocab_size, size=T) for _ in range(39)]
-    batched = _run_logits(dm, [base] + others)[0]
+    others = [rng.integers(0, cfg.vocab_size, size=T) for _ in range(199)]
+    batched = _run_logits(dm, [base] + others[:39])[0]
     assert np.array_equal(alone.view(np.uint32), batched.view(np.uint32))
+    big = _run_logits(dm, others[:137] + [base] + others[137:199])[137]
+    assert np.array_equal(alone.view(np.uint32), big.view(np.uint32))
 
 
 def test_fused_cdf_and_coder_bit_exact_vs_oracle():
