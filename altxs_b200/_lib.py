@@ -24,6 +24,7 @@ EXPORTS = (
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
+    "altxs_gemm_workspace_bytes", "altxs_gemm",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -129,6 +130,9 @@ def lib():
             "altxs_split_weights": (C.c_int, [C.POINTER(QMat), vp, vp, vp]),
             "altxs_linear_workspace_bytes": (i64, [C.c_int, C.c_int]),
             "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
+            "altxs_gemm_workspace_bytes": (i64, [C.c_int] * 6),
+            "altxs_gemm": (C.c_int, [C.c_int, C.c_int, C.c_int, vp, i64, i64, C.c_int, vp, i64, i64, C.c_int, vp, i64,
+                                     i64, C.c_int, C.c_float, C.c_float, C.c_int, vp, i64, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

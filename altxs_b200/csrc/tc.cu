@@ -1,16 +1,19 @@
-// tcgen05 tensor-core GEMM for the mixed-bit linear layers (sm_100a).
+// tcgen05 tensor-core GEMM on hi/lo bf16 planes (sm_100a).
 //
-// Y[m][n] = epi( sum_k X[m][k] W[row0+n][k] ) with X and W given as hi/lo
-// bf16 planes (tc.cuh).  One CTA computes a 128 x BN tile:
-//   warp 4      TMA producer: the four K-major tiles (X hi, X lo, W hi, W lo)
-//               of each 64-wide K slice into a ring of shared-memory stages
-//               (128-byte swizzle), one mbarrier per stage (full / empty);
+// C[b] = epi( sum_k A(b)[m][k] B(b)[n][k] ) with A and B given as hi/lo bf16
+// planes (tc.cuh), each K-major or MN-major.  A persistent grid (one CTA per
+// SM) walks 128 x BN output tiles:
+//   warp 4      TMA producer: the four tiles (A hi, A lo, B hi, B lo) of each
+//               64-wide K slice into a ring of shared-memory stages (128-byte
+//               swizzle), one mbarrier per stage (full / empty), across tiles;
 //   warp 5      MMA issuer: one thread issues tcgen05.mma (kind::f16, bf16 in,
-//               fp32 accumulate in tensor memory) for Xhi*Whi, Xhi*Wlo, Xlo*Whi
+//               fp32 accumulate in tensor memory) for Ahi*Bhi, Ahi*Blo, Alo*Bhi
 //               over the four 16-wide K steps of a stage, then tcgen05.commit
-//               frees the stage; a final commit signals the epilogue;
-//   warps 0-3   epilogue: tcgen05.ld of the accumulator (one tile row per
-//               thread), the layer's epilogue, stores.
+//               frees the stage; two accumulators in tensor memory, so the
+//               MMAs of tile i+1 run while the epilogue drains tile i;
+//   warps 0-3   epilogue: tcgen05.ld of the accumulator in 32 x 32 blocks,
+//               transposed through shared memory so that every warp store
+//               writes one contiguous row segment.
 // Every wait is bounded; a wait that gives up marks the rows of the tile with
 // ALTXS_ST_TIMEOUT (when a status array is given), lets the CTA's own copies
 // and MMAs drain (bounded) and frees the tensor memory.
@@ -19,6 +22,7 @@
 
 #include <mutex>
 
+#include "gemm.cuh"
 #include "model.cuh"
 #include "prof.cuh"
 #include "qmm.cuh"
@@ -32,37 +36,45 @@ constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of bf1
 constexpr int kTcThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 MMA
 constexpr unsigned kFull = 0xffffffffu;
 
-template <int BN>
+template <int BN, int AMN, int BMN>
 struct TcCfg {
-    static constexpr int kATile = kBM * kBK * 2;  // bytes of one X plane tile
-    static constexpr int kBTile = BN * kBK * 2;   // bytes of one W plane tile
+    static constexpr int kATile = kBM * kBK * 2;  // bytes of one A plane tile
+    static constexpr int kBTile = BN * kBK * 2;   // bytes of one B plane tile
     static constexpr int kStage = 2 * kATile + 2 * kBTile;
-    static constexpr int kStages = (192 * 1024) / kStage;  // BN 64: 4, 128: 3, 256: 2
+    static constexpr int kStages = (192 * 1024) / kStage;  // BN 64: 4, 128: 3
     static constexpr int kSmem = kStages * kStage + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
-    // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both
-    // K-major, M = 128, N = BN
-    static constexpr uint32_t kIdesc =
-        (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B,
+    // A/B major-ness, M = 128, N = BN
+    static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)AMN << 15) |
+                                       ((uint32_t)BMN << 16) | ((uint32_t)(BN >> 3) << 17) |
+                                       ((uint32_t)(kBM >> 4) << 24);
 };
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major tile written by TMA with the
-// 128-byte swizzle: 8-row x 128-byte swizzle atoms stacked every 1024 bytes.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// Shared-memory matrix descriptors of tiles written by TMA with the 128-byte
+// swizzle (8-row x 128-byte atoms).  K-major: rows are MN, 128 bytes of K per
+// row, 8-row groups every 1024 bytes.  MN-major: rows are K, 64 MN elements
+// per row; 8-K-row groups every 1024 bytes, 64-element MN chunks every 8 KB.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo) {
     uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
-    d |= (uint64_t)1 << 16;                           // leading byte offset (unused for this layout)
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;      // leading byte offset
     d |= (uint64_t)(1024 >> 4) << 32;                 // stride byte offset: next 8-row group
     d |= (uint64_t)1 << 46;                           // descriptor version
     d |= (uint64_t)2 << 61;                           // 128-byte swizzle
     return d;
+}
+template <int MN>
+__device__ __forceinline__ uint64_t op_desc(uint32_t tile, int kk) {
+    // K step of 16: 32 bytes along a K-major row, or two 8-row groups of an MN-major tile
+    return MN ? sw128_desc(tile + kk * 2048, 8192) : sw128_desc(tile + kk * 32, 16);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -82,17 +94,26 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
                  : "memory");
 }
 
-// 8 consecutive fp32 accumulator columns of this thread's tensor-memory lane
-__device__ __forceinline__ void tc_ld8(uint32_t taddr, float *v) {
-    uint32_t r0, r1, r2, r3, r4, r5, r6, r7;
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(r4), "=r"(r5), "=r"(r6), "=r"(r7)
-                 : "r"(taddr));
+// 32 consecutive fp32 accumulator columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float *v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
     // the registers are defined once the wait returns: tie them to it
     asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r0), "+r"(r1), "+r"(r2), "+r"(r3), "+r"(r4), "+r"(r5), "+r"(r6), "+r"(r7)::"memory");
-    v[0] = __uint_as_float(r0), v[1] = __uint_as_float(r1), v[2] = __uint_as_float(r2), v[3] = __uint_as_float(r3);
-    v[4] = __uint_as_float(r4), v[5] = __uint_as_float(r5), v[6] = __uint_as_float(r6), v[7] = __uint_as_float(r7);
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])::"memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ float leaky2(float v) {  // leaky_relu(v, 0.5)^2 (model.py:874-882)
@@ -100,34 +121,61 @@ __device__ __forceinline__ float leaky2(float v) {  // leaky_relu(v, 0.5)^2 (mod
     return __fmul_rn(t, t);
 }
 
-template <int BN>
+struct Tile {
+    int m0, n0, b, kb0, kb1;
+    bool skip;
+};
+
+// tile t: m-tile fastest (CTAs running at the same time share B tiles), then n-tile, then batch
+__device__ __forceinline__ Tile tile_of(const TcGemm &g, int t, int mt, int ntl, int nk, int bn) {
+    Tile T;
+    T.m0 = (t % mt) * kBM;
+    const int r = t / mt;
+    T.n0 = (r % ntl) * bn;
+    T.b = r / ntl;
+    T.kb0 = 0;
+    T.kb1 = nk;
+    T.skip = g.causal == 1 && T.n0 > T.m0 + kBM - 1;
+    if (g.causal == 2) T.kb1 = min(nk, (T.m0 + kBM + kBK - 1) / kBK);
+    if (g.causal == 3) T.kb0 = min(nk, T.m0 / kBK);
+    return T;
+}
+
+__device__ __forceinline__ int op_batch(const TcOp &o, int b) { return (b / o.div) * o.mul + o.add; }
+
+template <int BN, int AMN, int BMN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
-              const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo, TcArgs a) {
-    using Cfg = TcCfg<BN>;
+              const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo, TcGemm g) {
+    using Cfg = TcCfg<BN, AMN, BMN>;
     constexpr int S = Cfg::kStages;
     extern __shared__ unsigned char tc_smem_raw[];
-    __shared__ __align__(8) uint64_t full[S], empty[S], accb, drainb;
+    __shared__ __align__(8) uint64_t full[S], empty[S], tfull[2], tempty[2], drainb;
     __shared__ uint32_t tmem_sh;
     __shared__ volatile int abort_sh;
+    __shared__ float ebuf[4][32][33];  // epilogue: one 32 x 32 accumulator block per warp (padded)
     const uint32_t raw_s = smem_u32(tc_smem_raw);
     unsigned char *sm = tc_smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);  // 1024-byte aligned stages
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-    const int nk = a.K / kBK;
+    const int nk = (g.K + kBK - 1) / kBK;
+    const int mt = (g.M + kBM - 1) / kBM, ntl = (g.N + BN - 1) / BN;
+    const int n_tiles = mt * ntl * g.batch;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&accb, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+        }
         mbar_init(&drainb, 1);
         abort_sh = 0;
         fence_mbar_init();
     }
     if (warp == 5) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_sh)),
-                     "r"(Cfg::kTmemCols)
+                     "r"(2 * Cfg::kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -138,101 +186,153 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 4) {
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % S, r = kb / S;
-                if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, kWaitLimit)) {
-                    abort_sh = 1;
-                    break;
+            int q = 0;  // stage fills issued by this CTA (all tiles)
+            for (int t = blockIdx.x; t < n_tiles && !abort_sh; t += gridDim.x) {
+                const Tile T = tile_of(g, t, mt, ntl, nk, BN);
+                if (T.skip) continue;
+                const int ab = op_batch(g.a, T.b), bb = op_batch(g.b, T.b);
+                for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
+                    const int s = q % S, r = q / S;
+                    if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, kWaitLimit)) {
+                        abort_sh = 1;
+                        break;
+                    }
+                    if (abort_sh) break;
+                    unsigned char *st = sm + s * Cfg::kStage;
+                    unsigned char *sa = st, *sb = st + 2 * Cfg::kATile;
+                    const int k0 = kb * kBK;
+                    mbar_expect_tx(&full[s], Cfg::kStage);
+                    if (!AMN) {
+                        tma_load_3d(sa, &ta_hi, k0, (int)g.a.row_off + T.m0, ab, &full[s]);
+                        tma_load_3d(sa + Cfg::kATile, &ta_lo, k0, (int)g.a.row_off + T.m0, ab, &full[s]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < kBM / 64; ++c) {
+                            tma_load_3d(sa + c * 8192, &ta_hi, T.m0 + 64 * c, (int)g.a.row_off + k0, ab, &full[s]);
+                            tma_load_3d(sa + Cfg::kATile + c * 8192, &ta_lo, T.m0 + 64 * c, (int)g.a.row_off + k0, ab,
+                                        &full[s]);
+                        }
+                    }
+                    if (!BMN) {
+                        tma_load_3d(sb, &tb_hi, k0, (int)g.b.row_off + T.n0, bb, &full[s]);
+                        tma_load_3d(sb + Cfg::kBTile, &tb_lo, k0, (int)g.b.row_off + T.n0, bb, &full[s]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < BN / 64; ++c) {
+                            tma_load_3d(sb + c * 8192, &tb_hi, T.n0 + 64 * c, (int)g.b.row_off + k0, bb, &full[s]);
+                            tma_load_3d(sb + Cfg::kBTile + c * 8192, &tb_lo, T.n0 + 64 * c, (int)g.b.row_off + k0, bb,
+                                        &full[s]);
+                        }
+                    }
                 }
-                if (abort_sh) break;
-                unsigned char *st = sm + s * Cfg::kStage;
-                mbar_expect_tx(&full[s], Cfg::kStage);
-                tma_load_2d(st, &ta_hi, kb * kBK, m0, &full[s]);
-                tma_load_2d(st + Cfg::kATile, &ta_lo, kb * kBK, m0, &full[s]);
-                tma_load_2d(st + 2 * Cfg::kATile, &tb_hi, kb * kBK, a.row0 + n0, &full[s]);
-                tma_load_2d(st + 2 * Cfg::kATile + Cfg::kBTile, &tb_lo, kb * kBK, a.row0 + n0, &full[s]);
-                issued = kb + 1;
             }
             if (abort_sh) {  // let this CTA's copies land before the CTA can exit
-                for (int kb = issued - S > 0 ? issued - S : 0; kb < issued; ++kb)
-                    mbar_wait_bounded(&full[kb % S], (kb / S) & 1, kWaitLimit);
+                for (int p = q - S > 0 ? q - S : 0; p < q; ++p) mbar_wait_bounded(&full[p % S], (p / S) & 1, kWaitLimit);
             }
         }
     } else if (warp == 5) {
         if (lane == 0) {
             bool ok = true;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % S, r = kb / S;
-                if (!mbar_wait_bounded(&full[s], r & 1, kWaitLimit)) {
+            int q = 0, j = 0;  // stage fills consumed, tiles done by this CTA
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const Tile T = tile_of(g, t, mt, ntl, nk, BN);
+                if (T.skip) continue;
+                const int buf = j & 1, use = j >> 1;
+                ++j;
+                if (use > 0 && !mbar_wait_bounded(&tempty[buf], (use - 1) & 1, kWaitLimit)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ah = smem_u32(sm + s * Cfg::kStage);
-                const uint32_t al = ah + Cfg::kATile, bh = ah + 2 * Cfg::kATile, bl = bh + Cfg::kBTile;
+                const uint32_t acc = tmem + buf * Cfg::kTmemCols;
+                for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
+                    const int s = q % S, r = q / S;
+                    if (!mbar_wait_bounded(&full[s], r & 1, kWaitLimit)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(sm + s * Cfg::kStage);
+                    const uint32_t al = ah + Cfg::kATile, bh = ah + 2 * Cfg::kATile, bl = bh + Cfg::kBTile;
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    const uint32_t off = kk * 32;  // 16 bf16 along K
-                    tc_mma(tmem, sw128_desc(ah + off), sw128_desc(bh + off), Cfg::kIdesc, (kb | kk) != 0);
-                    tc_mma(tmem, sw128_desc(ah + off), sw128_desc(bl + off), Cfg::kIdesc, 1u);
-                    tc_mma(tmem, sw128_desc(al + off), sw128_desc(bh + off), Cfg::kIdesc, 1u);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint32_t first = kb == T.kb0 && kk == 0;
+                        tc_mma(acc, op_desc<AMN>(ah, kk), op_desc<BMN>(bh, kk), Cfg::kIdesc, !first);
+                        tc_mma(acc, op_desc<AMN>(ah, kk), op_desc<BMN>(bl, kk), Cfg::kIdesc, 1u);
+                        tc_mma(acc, op_desc<AMN>(al, kk), op_desc<BMN>(bh, kk), Cfg::kIdesc, 1u);
+                    }
+                    tc_commit(&empty[s]);
                 }
-                tc_commit(&empty[s]);
+                if (ok) tc_commit(&tfull[buf]);
             }
-            if (ok) {
-                tc_commit(&accb);
-            } else {  // no result: wait for the MMAs already issued, then leave
+            if (!ok) {  // no result for this tile: wait for the MMAs already issued, then leave
                 abort_sh = 1;
                 tc_commit(&drainb);
                 mbar_wait_bounded(&drainb, 0, kWaitLimit);
             }
         }
     } else {
-        // epilogue: warp w reads tensor-memory lanes 32w .. 32w+31 = tile rows
-        const bool ok = __all_sync(kFull, mbar_wait_bounded(&accb, 0, kWaitLimit));
-        tc_fence_after();
-        const int row = m0 + warp * 32 + lane;
-        if (ok) {
-            const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+        // epilogue: warp w reads tensor-memory lanes 32w .. 32w+31 = tile rows.
+        // Per 32-column block: lane = tile row on the way out of tensor
+        // memory, lane = column on the way to global memory.
+        float(*eb)[33] = ebuf[warp];
+        int j = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+            const Tile T = tile_of(g, t, mt, ntl, nk, BN);
+            if (T.skip) continue;
+            const int buf = j & 1, use = j >> 1;
+            ++j;
+            const bool gave_up = __any_sync(kFull, abort_sh != 0);  // warp-uniform
+            const bool ok = !gave_up && __all_sync(kFull, mbar_wait_bounded(&tfull[buf], use & 1, kWaitLimit));
+            if (!ok) {
+                const int row = T.m0 + warp * 32 + lane;
+                if (g.status && row < g.M) atomicOr(g.status + (int64_t)row * g.status_stride, ALTXS_ST_TIMEOUT);
+                continue;
+            }
+            tc_fence_after();
+            const bool no_k = T.kb0 >= T.kb1;  // nothing accumulated: the product is zero
+            const uint32_t tl = tmem + buf * Cfg::kTmemCols + ((uint32_t)(warp * 32) << 16);
+            float *Cb = g.C ? g.C + (int64_t)T.b * g.sC : nullptr;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 8) {
-                float v[8];
-                __syncwarp();  // the load below is warp-collective
-                tc_ld8(tl + c0, v);
-                const int n = n0 + c0;
-                if (row >= a.M || n >= a.N) continue;
-                const int cnt = a.N - n < 8 ? a.N - n : 8;
-                if (a.epi == kEpiLeaky2) {
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+                __syncwarp();  // warp-collective load; the block buffer is free again
+                tc_ld32(tl + c0, v);
+                if (c0 + 32 >= BN) {  // accumulator fully read: hand it back to the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[buf]);
+                }
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) v[u] = leaky2(v[u]);
-                } else if (a.epi == kEpiResid) {
-                    const float *rr = a.R + (int64_t)row * a.ldr + n;
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        if (u < cnt) v[u] = __fadd_rn(rr[u], __fmul_rn(a.colscale[n + u], v[u]));
-                }
-                if (a.Y) {
-                    float *yy = a.Y + (int64_t)row * a.ldy + n;
-                    for (int u = 0; u < cnt; ++u) yy[u] = v[u];
-                }
-                if (a.Y2) {
-                    float *yy = a.Y2 + (int64_t)row * a.ldy2 + n;
-                    for (int u = 0; u < cnt; ++u) yy[u] = v[u];
-                }
-                if (a.p_hi) {
-                    for (int u = 0; u < cnt; ++u) split_store(a.p_hi, a.p_lo, (int64_t)row * a.ldp + n + u, v[u]);
+                for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
+                __syncwarp();
+                const int n = T.n0 + c0 + lane;
+                const bool col_ok = n < g.N;
+                const float cs = (g.epi == kEpiResid && col_ok) ? g.colscale[n] : 0.0f;
+#pragma unroll 4
+                for (int rr = 0; rr < 32; ++rr) {
+                    const int m = T.m0 + warp * 32 + rr;
+                    if (m >= g.M || !col_ok) continue;
+                    float x = eb[rr][lane];
+                    if (g.epi == kEpiResid) {
+                        x = __fadd_rn(g.R[(int64_t)m * g.ldr + n], __fmul_rn(cs, x));
+                    } else {
+                        if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
+                        if (g.beta != 0.0f) x = __fadd_rn(x, __fmul_rn(g.beta, Cb[(int64_t)m * g.ldc + n]));
+                        if (g.epi == kEpiLeaky2) x = leaky2(x);
+                    }
+                    if (Cb) Cb[(int64_t)m * g.ldc + n] = x;
+                    if (g.Y2) g.Y2[(int64_t)m * g.ldy2 + n] = x;
+                    if (g.p_hi) split_store(g.p_hi, g.p_lo, (int64_t)m * g.ldp + n, x);
                 }
             }
-        } else if (a.status && row < a.M) {
-            atomicOr(a.status + (int64_t)row * a.status_stride, ALTXS_ST_TIMEOUT);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 5) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * Cfg::kTmemCols)
                      : "memory");
     }
 }
@@ -241,6 +341,15 @@ __global__ void k_split_weights(altxs_qmat W, uint16_t *hi, uint16_t *lo) {
     const int row = blockIdx.x;
     for (int k = threadIdx.x; k < W.cols; k += blockDim.x)
         split_store(hi, lo, (int64_t)row * W.cols + k, qmat_elem(W, row, k));
+}
+
+// one CTA per (row, batch); planes compact with row stride ldo
+__global__ void k_split_f32(const float *src, int64_t cols, int64_t ld, int64_t bs, int64_t rows, int64_t ldo,
+                            uint16_t *hi, uint16_t *lo) {
+    const int64_t row = blockIdx.x, b = blockIdx.y;
+    const float *s = src + b * bs + row * ld;
+    const int64_t o = (b * rows + row) * ldo;
+    for (int64_t k = threadIdx.x; k < ldo; k += blockDim.x) split_store(hi, lo, o + k, k < cols ? s[k] : 0.0f);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -256,68 +365,204 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
     return fn;
 }
 
-// 2-D bf16 tensor map over [rows][cols] (row stride ld elements), box 64 x box_rows, 128-byte swizzle
-bool make_map(CUtensorMap *m, const uint16_t *p, int64_t cols, int64_t rows, int64_t ld, int box_rows) {
+// 3-D bf16 tensor map over [nb][rows][cols], box 64 (cols) x box_rows x 1, 128-byte swizzle
+bool make_map(CUtensorMap *m, const uint16_t *p, const TcOp &o, int box_rows) {
     auto enc = encoder();
     if (!enc) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-    cuuint32_t es[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(p), dims, strides, box, es,
+    cuuint64_t dims[3] = {(cuuint64_t)o.cols, (cuuint64_t)o.rows, (cuuint64_t)(o.nb > 0 ? o.nb : 1)};
+    cuuint64_t strides[2] = {(cuuint64_t)(o.ld * 2), (cuuint64_t)((o.bstride > 0 ? o.bstride : o.ld * o.rows) * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t *>(p), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
-int launch_bn(const TcArgs &a, cudaStream_t st) {
-    using Cfg = TcCfg<BN>;
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool op_ok(const TcOp &o) {
+    if (!o.hi || !o.lo || !aligned16(o.hi) || !aligned16(o.lo)) return false;
+    if (o.ld % 8 || o.ld < o.cols || o.rows < 1 || o.cols < 1 || o.div < 1 || o.mul < 0 || o.add < 0) return false;
+    if (o.nb > 1 && o.bstride % 8) return false;
+    return o.row_off >= 0;
+}
+
+template <int BN, int AMN, int BMN>
+int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
+    using Cfg = TcCfg<BN, AMN, BMN>;
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return ALTXS_ECUDA;
     if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(k_tc_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
+        if (cudaFuncSetAttribute(k_tc_gemm<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
             cudaSuccess)
             return ALTXS_ECUDA;
         attr_done[dev] = true;
     }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-    if (!make_map(&ta_hi, a.a_hi, a.K, a.M, a.lda, kBM) || !make_map(&ta_lo, a.a_lo, a.K, a.M, a.lda, kBM) ||
-        !make_map(&tb_hi, a.b_hi, a.K, a.b_rows, a.K, BN) || !make_map(&tb_lo, a.b_lo, a.K, a.b_rows, a.K, BN))
+    const int abox = AMN ? 64 : kBM, bbox = BMN ? 64 : BN;
+    if (!make_map(&ta_hi, g.a.hi, g.a, abox) || !make_map(&ta_lo, g.a.lo, g.a, abox) ||
+        !make_map(&tb_hi, g.b.hi, g.b, bbox) || !make_map(&tb_lo, g.b.lo, g.b, bbox))
         return ALTXS_EINVAL;
-    dim3 grid((a.M + kBM - 1) / kBM, (a.N + BN - 1) / BN);
-    ALTXS_LAUNCH(::altxs::kKQmm, st, k_tc_gemm<BN><<<grid, kTcThreads, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, a));
+    // persistent: at most one CTA per SM walks the tiles
+    const int64_t tiles = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch;
+    const int grid = (int)(tiles < sms ? tiles : sms);
+    ALTXS_LAUNCH(::altxs::kKQmm, st,
+                 k_tc_gemm<BN, AMN, BMN><<<grid, kTcThreads, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, g));
     return ALTXS_OK;
 }
 
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+template <int BN>
+int launch_bn(const TcGemm &g, int sms, cudaStream_t st) {
+    if (!g.a.mn_major && !g.b.mn_major) return launch_cfg<BN, 0, 0>(g, sms, st);
+    if (!g.a.mn_major && g.b.mn_major) return launch_cfg<BN, 0, 1>(g, sms, st);
+    if (g.a.mn_major && !g.b.mn_major) return launch_cfg<BN, 1, 0>(g, sms, st);
+    return launch_cfg<BN, 1, 1>(g, sms, st);
+}
 
 }  // namespace
 
-int launch_tc(const TcArgs &a, cudaStream_t st) {
-    if (a.M <= 0 || a.N <= 0) return ALTXS_OK;
-    if (a.K <= 0 || a.K % kBK || a.lda % 8 || a.lda < a.K || a.row0 < 0 || a.row0 + a.N > a.b_rows) return ALTXS_EINVAL;
-    if (!a.a_hi || !a.a_lo || !a.b_hi || !a.b_lo || !aligned16(a.a_hi) || !aligned16(a.a_lo) || !aligned16(a.b_hi) ||
-        !aligned16(a.b_lo))
-        return ALTXS_EINVAL;
-    if (a.p_hi && (!a.p_lo || a.ldp < a.N)) return ALTXS_EINVAL;
-    if (a.epi == kEpiResid && (!a.R || !a.colscale)) return ALTXS_EINVAL;
+int launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
+    if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
+    if (g.K <= 0 || !op_ok(g.a) || !op_ok(g.b)) return ALTXS_EINVAL;
+    if (g.causal < 0 || g.causal > 3) return ALTXS_EINVAL;
+    if (g.epi == kEpiResid && (!g.R || !g.colscale || g.batch != 1)) return ALTXS_EINVAL;
+    if ((g.p_hi && (!g.p_lo || g.ldp < g.N || g.batch != 1)) || (g.Y2 && g.batch != 1)) return ALTXS_EINVAL;
+    if (g.beta != 0.0f && !g.C) return ALTXS_EINVAL;
+    // the K extent of each operand must be covered by its stored array (zeros beyond come from the bounds)
+    const int64_t ka = g.a.mn_major ? g.a.rows - g.a.row_off : g.a.cols;
+    const int64_t kbx = g.b.mn_major ? g.b.rows - g.b.row_off : g.b.cols;
+    if (ka < g.K || kbx < g.K) return ALTXS_EINVAL;
+    // a K slice reads 64 values: past K they must come from the bounds (zeros), not from stored data
+    if (g.K % kBK && (ka != g.K || kbx != g.K)) return ALTXS_EINVAL;
     static int sms[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return ALTXS_ECUDA;
     if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int64_t mt = (a.M + kBM - 1) / kBM;
+    const int64_t mt = (g.M + kBM - 1) / kBM;
     // wide tiles when they still fill the device, narrow ones otherwise
-    if (mt * ((a.N + 127) / 128) >= sms[dev]) return launch_bn<128>(a, st);
-    return launch_bn<64>(a, st);
+    if (mt * ((g.N + 127) / 128) * g.batch >= sms[dev]) return launch_bn<128>(g, sms[dev], st);
+    return launch_bn<64>(g, sms[dev], st);
+}
+
+int launch_tc(const TcArgs &a, cudaStream_t st) {
+    TcGemm g{};
+    g.a.hi = a.a_hi;
+    g.a.lo = a.a_lo;
+    g.a.rows = a.M;
+    g.a.cols = a.K;
+    g.a.ld = a.lda;
+    g.a.nb = 1;
+    g.a.div = g.a.mul = 1;
+    g.b.hi = a.b_hi;
+    g.b.lo = a.b_lo;
+    g.b.rows = a.b_rows;
+    g.b.cols = a.K;
+    g.b.ld = a.K;
+    g.b.nb = 1;
+    g.b.row_off = a.row0;
+    g.b.div = g.b.mul = 1;
+    if (a.row0 < 0 || a.row0 + a.N > a.b_rows || a.K % kBK) return ALTXS_EINVAL;
+    g.M = a.M;
+    g.N = a.N;
+    g.K = a.K;
+    g.batch = 1;
+    g.alpha = 1.0f;
+    g.epi = a.epi;
+    g.C = a.Y;
+    g.ldc = a.ldy;
+    g.R = a.R;
+    g.ldr = a.ldr;
+    g.colscale = a.colscale;
+    g.Y2 = a.Y2;
+    g.ldy2 = a.ldy2;
+    g.p_hi = a.p_hi;
+    g.p_lo = a.p_lo;
+    g.ldp = a.ldp;
+    g.status = a.status;
+    g.status_stride = a.status_stride;
+    return launch_tc_gemm(g, st);
 }
 
 int launch_split_weights(const altxs_qmat &W, uint16_t *hi, uint16_t *lo, cudaStream_t st) {
     if (!hi || !lo || W.rows <= 0 || W.cols <= 0 || W.cols % 64) return ALTXS_EINVAL;
     ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_weights<<<W.rows, 256, 0, st>>>(W, hi, lo));
     return ALTXS_OK;
+}
+
+int launch_split_f32(const float *src, int64_t rows, int64_t cols, int64_t ld, int nb, int64_t bs, uint16_t *hi,
+                     uint16_t *lo, cudaStream_t st, int kernel_class) {
+    if (rows <= 0 || cols <= 0 || nb <= 0) return ALTXS_OK;
+    if (!src || !hi || !lo || rows > 2147483647 || nb > 65535) return ALTXS_EINVAL;
+    const int64_t ldo = align_up(cols, 8);
+    ALTXS_LAUNCH(kernel_class, st,
+                 k_split_f32<<<dim3((unsigned)rows, (unsigned)nb), 256, 0, st>>>(src, cols, ld, bs, rows, ldo, hi, lo));
+    return ALTXS_OK;
+}
+
+namespace {
+
+// stored shape of an fp32 GemmArgs operand: op(A) is M x K, stored [M][lda] or [K][lda] (tA)
+struct F32Op {
+    int64_t rows, cols, ldo, nb;
+};
+F32Op f32_a(const GemmArgs &g) {
+    F32Op o;
+    o.rows = g.tA ? g.K : g.M;
+    o.cols = g.tA ? g.M : g.K;
+    o.ldo = align_up(o.cols, 8);
+    o.nb = (g.batch + g.adiv - 1) / g.adiv;
+    return o;
+}
+// op(B) is K x N, stored [K][ldb] or [N][ldb] (tB)
+F32Op f32_b(const GemmArgs &g) {
+    F32Op o;
+    o.rows = g.tB ? g.N : g.K;
+    o.cols = g.tB ? g.K : g.N;
+    o.ldo = align_up(o.cols, 8);
+    o.nb = (g.batch + g.bdiv - 1) / g.bdiv;
+    return o;
+}
+
+}  // namespace
+
+void tc_f32_scratch(const GemmArgs &g, int64_t *a_elems, int64_t *b_elems) {
+    const F32Op a = f32_a(g), b = f32_b(g);
+    *a_elems = 2 * align_up(a.nb * a.rows * a.ldo, 128);
+    *b_elems = 2 * align_up(b.nb * b.rows * b.ldo, 128);
+}
+
+int tc_gemm_f32(const GemmArgs &g, uint16_t *a_scr, int64_t a_elems, uint16_t *b_scr, int64_t b_elems,
+                cudaStream_t st, int kernel_class) {
+    if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
+    if (g.K <= 0 || g.adiv < 1 || g.bdiv < 1) return ALTXS_EINVAL;
+    int64_t need_a, need_b;
+    tc_f32_scratch(g, &need_a, &need_b);
+    if (!a_scr || !b_scr || a_elems < need_a || b_elems < need_b) return ALTXS_EINVAL;
+    const F32Op a = f32_a(g), b = f32_b(g);
+    uint16_t *ahi = a_scr, *alo = a_scr + need_a / 2, *bhi = b_scr, *blo = b_scr + need_b / 2;
+    int rc = launch_split_f32(g.A, a.rows, a.cols, g.lda, (int)a.nb, g.sA, ahi, alo, st, kernel_class);
+    if (rc) return rc;
+    rc = launch_split_f32(g.B, b.rows, b.cols, g.ldb, (int)b.nb, g.sB, bhi, blo, st, kernel_class);
+    if (rc) return rc;
+    TcGemm t{};
+    t.a = TcOp{ahi, alo, g.tA ? 1 : 0, a.rows, a.cols, a.ldo, a.rows * a.ldo, (int)a.nb, 0, g.adiv, 1, 0};
+    // tc reads B as [n][k]: stored [N][K] (tB) is K-major, stored [K][N] is MN-major
+    t.b = TcOp{bhi, blo, g.tB ? 0 : 1, b.rows, b.cols, b.ldo, b.rows * b.ldo, (int)b.nb, 0, g.bdiv, 1, 0};
+    t.M = g.M;
+    t.N = g.N;
+    t.K = g.K;
+    t.batch = g.batch;
+    t.causal = g.causal;
+    t.alpha = g.alpha;
+    t.beta = g.beta;
+    t.epi = kEpiStore;
+    t.C = g.C;
+    t.ldc = g.ldc;
+    t.sC = g.sC;
+    return launch_tc_gemm(t, st);
 }
 
 }  // namespace altxs
@@ -338,6 +583,55 @@ int altxs_split_weights(const altxs_qmat *m, uint16_t *hi, uint16_t *lo, altxs_s
     if (!m) return ALTXS_EINVAL;
     if ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) return ALTXS_EINVAL;
     return altxs::launch_split_weights(*m, hi, lo, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int64_t altxs_gemm_workspace_bytes(int M, int N, int K, int tA, int tB, int batch) {
+    if (M < 0 || N < 0 || K < 0 || batch < 0) return -1;
+    altxs::GemmArgs g{};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.tA = tA;
+    g.tB = tB;
+    g.batch = batch;
+    g.adiv = g.bdiv = 1;
+    int64_t a, b;
+    altxs::tc_f32_scratch(g, &a, &b);
+    return altxs::align_up(a * 2, 256) + altxs::align_up(b * 2, 256);
+}
+
+int altxs_gemm(int M, int N, int K, const float *A, int64_t lda, int64_t sA, int tA, const float *B, int64_t ldb,
+               int64_t sB, int tB, float *C, int64_t ldc, int64_t sC, int batch, float alpha, float beta, int causal,
+               void *workspace, int64_t workspace_bytes, altxs_stream_t stream) {
+    using namespace altxs;
+    if (M < 0 || N < 0 || K < 0 || batch < 0 || !A || !B || !C || (tA | tB) & ~1) return ALTXS_EINVAL;
+    if (M == 0 || N == 0 || batch == 0) return ALTXS_OK;
+    if (workspace_bytes < altxs_gemm_workspace_bytes(M, N, K, tA, tB, batch) || !workspace) return ALTXS_EINVAL;
+    GemmArgs g{};
+    g.A = A;
+    g.B = B;
+    g.C = C;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.lda = lda;
+    g.ldb = ldb;
+    g.ldc = ldc;
+    g.sA = sA;
+    g.sB = sB;
+    g.sC = sC;
+    g.tA = tA;
+    g.tB = tB;
+    g.batch = batch;
+    g.adiv = g.bdiv = 1;
+    g.alpha = alpha;
+    g.beta = beta;
+    g.causal = causal;
+    int64_t a, b;
+    tc_f32_scratch(g, &a, &b);
+    uint16_t *as = static_cast<uint16_t *>(workspace);
+    uint16_t *bs = reinterpret_cast<uint16_t *>(static_cast<unsigned char *>(workspace) + align_up(a * 2, 256));
+    return tc_gemm_f32(g, as, a, bs, b, reinterpret_cast<cudaStream_t>(stream), kKQmm);
 }
 
 int64_t altxs_linear_workspace_bytes(int M, int K) {

@@ -14,6 +14,7 @@
 #include "model.cuh"
 #include "prof.cuh"
 #include "qmm.cuh"
+#include "tc.cuh"
 
 using namespace altxs;
 
@@ -77,7 +78,7 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.hinv = take(L * T * (D.H + D.Hkv));
     t.qr = take(L * T * d);
     t.kr = take(L * T * D.kvd);
-    t.P = take(L * D.H * T * T);
+    t.P = take(L * D.H * T * align_up(T, 8));  // fp32 [H][T][T], or bf16 hi/lo planes [2][H][T][align8(T)]
     t.tq = take(L * T * D.r);
     t.tk = take(L * T * D.r);
     t.tv = take(L * T * D.r);
@@ -350,6 +351,43 @@ __global__ void t_softmax_bwd(TD D, const float *P, float *dS, float scale) {
         g[j] = j <= t ? __fmul_rn(__fmul_rn(p[j], __fsub_rn(g[j], s)), scale) : 0.0f;
 }
 
+// Plane forms of the two softmax kernels (tensor-core path): the scores S
+// come in fp32 (row stride T), P leaves as hi/lo bf16 planes [H][T][ldp]
+// (zero above the diagonal); the backward reads P from its planes and writes
+// dS as planes.
+__global__ void t_softmax_pl(TD D, const float *S, uint16_t *ph, uint16_t *pl, int64_t ldp) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;  // h * T + t
+    const int t = row % D.T;
+    const float *s = S + (int64_t)row * D.T;
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j <= t; j += blockDim.x) m = fmaxf(m, s[j]);
+    m = block_max(m, red);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j <= t; j += blockDim.x) sum = __fadd_rn(sum, expf(__fsub_rn(s[j], m)));
+    sum = block_sum(sum, red);
+    const float inv = __fdiv_rn(1.0f, sum);
+    const int64_t o = (int64_t)row * ldp;
+    for (int j = threadIdx.x; j < ldp; j += blockDim.x)
+        split_store(ph, pl, o + j, j <= t ? __fmul_rn(expf(__fsub_rn(s[j], m)), inv) : 0.0f);
+}
+
+__global__ void t_softmax_bwd_pl(TD D, const uint16_t *ph, const uint16_t *pl, int64_t ldp, const float *dP,
+                                 uint16_t *gh, uint16_t *gl, float scale) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const int t = row % D.T;
+    const int64_t o = (int64_t)row * ldp;
+    const float *g = dP + (int64_t)row * D.T;
+    float s = 0.0f;
+    for (int j = threadIdx.x; j <= t; j += blockDim.x) s = __fmaf_rn(g[j], split_load(ph, pl, o + j), s);
+    s = block_sum(s, red);
+    for (int j = threadIdx.x; j < ldp; j += blockDim.x)
+        split_store(gh, gl, o + j,
+                    j <= t ? __fmul_rn(__fmul_rn(split_load(ph, pl, o + j), __fsub_rn(g[j], s)), scale) : 0.0f);
+}
+
 // x = r + colscale * y (row stride d), optional copy into y2
 __global__ void t_resid(int64_t n, int d, const float *r, const float *col, const float *y, float *x, float *y2) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -495,8 +533,45 @@ struct Run {
     Tape tp;
     float *splitk;
     int64_t splitk_floats;
+    // tensor-core path (weights given as hi/lo planes): operand plane scratch
+    const altxs_split_planes *sp;
+    uint16_t *tca, *tcb;
+    int64_t tca_n, tcb_n;
     cudaStream_t st;
 };
+
+// Batched/causal GEMMs of the update: tensor cores when the model carries
+// bf16 planes, CUDA cores otherwise (the two differ in the last bits; the
+// choice is the caller's and is the same at the encoder and the decoder).
+int gemm(const Run &R, const GemmArgs &g) {
+    if (R.sp) return tc_gemm_f32(g, R.tca, R.tca_n, R.tcb, R.tcb_n, R.st, kKTtt);
+    return launch_gemm(g, R.st);
+}
+
+// A = X (split into planes in the A scratch), B = weight planes rows row0..: Y (+)= X W^T or dX (+)= dY W
+int tc_lin(const Run &R, const uint16_t *wh, const uint16_t *wl, int64_t wrows, int row0, int N, int K,
+           const float *X, int64_t ldx, float *Y, int64_t ldy, bool transposed_w, float beta) {
+    const int T = R.D.T;
+    const int kx = transposed_w ? N : K;  // columns of the fp32 input
+    const int64_t ldo = align_up(kx, 8);
+    if (R.tca_n < 2 * align_up((int64_t)T * ldo, 128)) return ALTXS_EINVAL;
+    uint16_t *xh = R.tca, *xl = R.tca + align_up((int64_t)T * ldo, 128);
+    TRY(launch_split_f32(X, T, kx, ldx, 1, 0, xh, xl, R.st, kKTtt));
+    TcGemm t{};
+    t.a = TcOp{xh, xl, 0, T, kx, ldo, T * ldo, 1, 0, 1, 1, 0};
+    // forward: B[n][k] = W[row0 + n][k] (K-major); backward: B[n][k] = W[row0 + k][n] (MN-major)
+    t.b = TcOp{wh, wl, transposed_w ? 1 : 0, wrows, K, K, wrows * (int64_t)K, 1, row0, 1, 1, 0};
+    t.M = T;
+    t.N = transposed_w ? K : N;
+    t.K = kx;
+    t.batch = 1;
+    t.alpha = 1.0f;
+    t.beta = beta;
+    t.epi = kEpiStore;
+    t.C = Y;
+    t.ldc = ldy;
+    return launch_tc_gemm(t, R.st);
+}
 
 // GEMM with the common fields (split-K scratch attached)
 GemmArgs G(const Run &R, const float *A, int64_t lda, int tA, const float *B, int64_t ldb, int tB, float *C,
@@ -523,9 +598,41 @@ GemmArgs G(const Run &R, const float *A, int64_t lda, int tA, const float *B, in
     return g;
 }
 
-// Y[T][N] = X[T][K] W[row0.., :]^T  (dense copy of the base if present)
-int lin_fwd(const Run &R, const altxs_qmat &Wq, const float *Wd, int row0, int N, int K, const float *X, int64_t ldx,
-            float *Y, int64_t ldy) {
+// B operand from an fp32 array [nb][rows][cols] (row stride ld, batch stride bs), split into the B scratch
+int split_b(const Run &R, const float *src, int64_t rows, int64_t cols, int64_t ld, int nb, int64_t bs, int mn_major,
+            int div, int mul, int add, TcOp &op) {
+    const int64_t ldo = align_up(cols, 8), n = align_up((int64_t)nb * rows * ldo, 128);
+    if (2 * n > R.tcb_n) return ALTXS_EINVAL;
+    TRY(launch_split_f32(src, rows, cols, ld, nb, bs, R.tcb, R.tcb + n, R.st, kKTtt));
+    op = TcOp{R.tcb, R.tcb + n, mn_major, rows, cols, ldo, rows * ldo, nb, 0, div, mul, add};
+    return ALTXS_OK;
+}
+
+// one attention product on the tensor cores: per-head [T][T] planes (P or dS) with a split right operand
+int tc_att(const Run &R, const TcOp &a, const TcOp &b, int M, int N, int K, int batch, int causal, float beta,
+           float *C, int64_t ldc, int64_t sC) {
+    TcGemm t{};
+    t.a = a;
+    t.b = b;
+    t.M = M;
+    t.N = N;
+    t.K = K;
+    t.batch = batch;
+    t.causal = causal;
+    t.alpha = 1.0f;
+    t.beta = beta;
+    t.epi = kEpiStore;
+    t.C = C;
+    t.ldc = ldc;
+    t.sC = sC;
+    return launch_tc_gemm(t, R.st);
+}
+
+// Y[T][N] = X[T][K] W[row0.., :]^T  (tensor cores from the planes wh/wl, else the dense
+// copy of the base if present, else the packed codes)
+int lin_fwd(const Run &R, const altxs_qmat &Wq, const float *Wd, const uint16_t *wh, const uint16_t *wl, int row0,
+            int N, int K, const float *X, int64_t ldx, float *Y, int64_t ldy) {
+    if (R.sp) return tc_lin(R, wh, wl, Wq.rows, row0, N, K, X, ldx, Y, ldy, false, 0.0f);
     if (Wd) return launch_gemm(G(R, X, ldx, 0, Wd + (int64_t)row0 * K, K, 1, Y, ldy, R.D.T, N, K), R.st);
     QmmArgs a{};
     a.X = X;
@@ -542,8 +649,9 @@ int lin_fwd(const Run &R, const altxs_qmat &Wq, const float *Wd, int row0, int N
 }
 
 // dX[T][K] (= or +=) dY[T][N] W[row0.., :]
-int lin_bwd(const Run &R, const altxs_qmat &Wq, const float *Wd, int row0, int N, int K, const float *dY,
-            int64_t lddy, float *dX, int64_t lddx, float beta) {
+int lin_bwd(const Run &R, const altxs_qmat &Wq, const float *Wd, const uint16_t *wh, const uint16_t *wl, int row0,
+            int N, int K, const float *dY, int64_t lddy, float *dX, int64_t lddx, float beta) {
+    if (R.sp) return tc_lin(R, wh, wl, Wq.rows, row0, N, K, dY, lddy, dX, lddx, true, beta);
     if (Wd)
         return launch_gemm(G(R, dY, lddy, 0, Wd + (int64_t)row0 * K, K, 0, dX, lddx, R.D.T, K, N, 1.0f, beta), R.st);
     QmmTArgs q{};
@@ -582,6 +690,9 @@ int lora_bwd(const Run &R, const float *X, int din, const float *A, const float 
     return ALTXS_OK;
 }
 
+// the weight planes of matrix field f (NULL on the CUDA-core path)
+#define PL(f) (R.sp ? R.sp->f : nullptr)
+
 int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out) {
     const TD &D = R.D;
     const Tape &tp = R.tp;
@@ -598,7 +709,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
         const float *n = tp.n + (int64_t)l * Tn * d;
         float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
-        TRY(lin_fwd(R, w->qkv, dw ? dw->qkv : nullptr, l * D.qn, D.qn, d, n, d, qkv, D.qn));
+        TRY(lin_fwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), l * D.qn, D.qn, d, n, d, qkv, D.qn));
         TRY(lora_fwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
                      tp.tq + (int64_t)l * Tn * r, qkv, D.qn));
         if (mask & 2)
@@ -609,7 +720,22 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, tp, *w));
         float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
         const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
-        {
+        const int64_t ldp = align_up(Tn, 8);
+        uint16_t *Ph = reinterpret_cast<uint16_t *>(tp.P + (int64_t)l * D.H * Tn * ldp), *Pl = Ph + D.H * Tn * ldp;
+        if (R.sp) {  // tensor cores: S in fp32 scratch, P kept as planes for y = P v and the backward
+            GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, tp.dS, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
+            g.batch = D.H;
+            g.sA = D.hd;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = (int64_t)Tn * Tn;
+            g.causal = 1;
+            TRY(gemm(R, g));
+            ALTXS_LAUNCH(kKTtt, st, t_softmax_pl<<<D.H * Tn, 256, 0, st>>>(D, tp.dS, Ph, Pl, ldp));
+            TcOp a{Ph, Pl, 0, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, 1, 0}, b{};
+            TRY(split_b(R, qkv + d + D.kvd, Tn, D.hd, D.qn, D.Hkv, D.hd, 1, D.G, 1, 0, b));  // v, [n=c][k=t']
+            TRY(tc_att(R, a, b, Tn, D.hd, Tn, D.H, 2, 0.0f, tp.y, d, D.hd));                 // y = P v
+        } else {
             GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, P, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
             g.batch = D.H;
             g.sA = D.hd;
@@ -617,31 +743,29 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             g.bdiv = D.G;
             g.sC = (int64_t)Tn * Tn;
             g.causal = 1;
-            TRY(launch_gemm(g, st));
-        }
-        ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, P));
-        {
-            GemmArgs g = G(R, P, Tn, 0, qkv + d + D.kvd, D.qn, 0, tp.y, d, Tn, D.hd, Tn);  // y = P v
+            TRY(gemm(R, g));
+            ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, P));
+            g = G(R, P, Tn, 0, qkv + d + D.kvd, D.qn, 0, tp.y, d, Tn, D.hd, Tn);  // y = P v
             g.batch = D.H;
             g.sA = (int64_t)Tn * Tn;
             g.sB = D.hd;
             g.bdiv = D.G;
             g.sC = D.hd;
             g.causal = 2;
-            TRY(launch_gemm(g, st));
+            TRY(gemm(R, g));
         }
-        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, l * d, d, d, tp.y, d, tp.ao, d));
+        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, tp.y, d, tp.ao, d));
         if (mask & 8)
             TRY(lora_fwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, tp.ao, d));
         ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w));
         float *u = tp.u + (int64_t)l * Tn * D.F;
-        TRY(lin_fwd(R, w->up, dw ? dw->up : nullptr, l * D.F, D.F, d, tp.n2 + (int64_t)l * Tn * d, d, u, D.F));
+        TRY(lin_fwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), l * D.F, D.F, d, tp.n2 + (int64_t)l * Tn * d, d, u, D.F));
         ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
         float *sk = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
         const float *xm = tp.xmid + (int64_t)l * Tn * d;
-        if (dw) {
-            TRY(lin_fwd(R, w->down, dw->down, l * d, d, D.F, tp.hbuf, D.F, tp.dd, d));
+        if (dw || R.sp) {
+            TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.hbuf, D.F, tp.dd, d));
             ALTXS_LAUNCH(kKTtt, st, t_resid<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
                                         (int64_t)Tn * d, d, xm, w->mlp_scale + (int64_t)l * d, tp.dd, tp.x, sk));
         } else {
@@ -665,7 +789,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         }
     }
     ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp));
-    TRY(lin_fwd(R, w->emb, dw ? dw->emb : nullptr, 0, D.V, d, tp.hf, d, tp.logits, D.V));
+    TRY(lin_fwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.hf, d, tp.logits, D.V));
     if (mask & 16) TRY(lora_fwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V));
     ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, R.desc->logit_softcap));
     ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, tp.rowloss, loss_out));
@@ -684,7 +808,7 @@ int backward(const Run &R, const float *lora, float *grad) {
     const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
     cudaStream_t st = R.st;
     // LM head: dhf = dlogits E (+ LoRA)
-    TRY(lin_bwd(R, w->emb, dw ? dw->emb : nullptr, 0, D.V, d, tp.logits, D.V, tp.dn, d, 0.0f));
+    TRY(lin_bwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.logits, D.V, tp.dn, d, 0.0f));
     if (mask & 16)
         TRY(lora_bwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V, grad + lo.lmA,
                      grad + lo.lmB, tp.dn));
@@ -696,10 +820,10 @@ int backward(const Run &R, const float *lora, float *grad) {
         // MLP
         ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
                                     (int64_t)Tn * d, d, tp.dx, w->mlp_scale + (int64_t)l * d, tp.dd));
-        TRY(lin_bwd(R, w->down, dw ? dw->down : nullptr, l * d, d, D.F, tp.dd, d, tp.dh, D.F, 0.0f));
+        TRY(lin_bwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.dd, d, tp.dh, D.F, 0.0f));
         ALTXS_LAUNCH(kKTtt, st, t_leaky_bwd<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
                                     (int64_t)Tn * D.F, tp.dh, tp.u + (int64_t)l * Tn * D.F, tp.dh));
-        TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, l * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
+        TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), l * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
         ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Tn * d,
                                                              tp.inv2 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
                                                              tp.dx));
@@ -711,11 +835,45 @@ int backward(const Run &R, const float *lora, float *grad) {
             TRY(lora_bwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
                          grad + lo.oB + l * lo.o_stride, tp.dn));
-        TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, l * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
+        TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
         // attention backward
         const float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
         const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
         const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        if (R.sp) {  // tensor cores: P and dS as planes, K-major or read transposed (MN-major)
+            const int64_t ldp = align_up(Tn, 8);
+            const uint16_t *Ph = reinterpret_cast<const uint16_t *>(tp.P + (int64_t)l * D.H * Tn * ldp);
+            const uint16_t *Pl = Ph + D.H * Tn * ldp;
+            GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
+            g.batch = D.H;
+            g.sA = D.hd;
+            g.sB = D.hd;
+            g.bdiv = D.G;
+            g.sC = (int64_t)Tn * Tn;
+            g.causal = 1;
+            TRY(gemm(R, g));
+            TcOp b{};
+            TRY(split_b(R, tp.dy, Tn, D.hd, d, D.H, D.hd, 1, 1, 1, 0, b));  // dy per head, [n=c][k=t]
+            for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
+                TcOp a{Ph, Pl, 1, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, D.G, gi};
+                b.mul = D.G;
+                b.add = gi;
+                TRY(tc_att(R, a, b, Tn, D.hd, Tn, D.Hkv, 3, gi ? 1.0f : 0.0f, tp.dqkv + d + D.kvd, D.qn, D.hd));
+            }
+            uint16_t *Gh = R.tca, *Gl = R.tca + D.H * Tn * ldp;  // dS planes
+            ALTXS_LAUNCH(kKTtt, st,
+                         t_softmax_bwd_pl<<<D.H * Tn, 256, 0, st>>>(D, Ph, Pl, ldp, tp.dS, Gh, Gl, att_scale));
+            TRY(split_b(R, kr, Tn, D.hd, D.kvd, D.Hkv, D.hd, 1, D.G, 1, 0, b));  // k, [n=c][k=t']
+            TRY(tc_att(R, TcOp{Gh, Gl, 0, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, 1, 0}, b, Tn, D.hd, Tn, D.H, 2, 0.0f,
+                       tp.dqr, d, D.hd));  // dq = dS k
+            TRY(split_b(R, qr, Tn, D.hd, d, D.H, D.hd, 1, 1, 1, 0, b));  // q per head, [n=c][k=t]
+            for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
+                b.mul = D.G;
+                b.add = gi;
+                TRY(tc_att(R, TcOp{Gh, Gl, 1, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, D.G, gi}, b, Tn, D.hd, Tn, D.Hkv, 3,
+                           gi ? 1.0f : 0.0f, tp.dkr, D.kvd, D.hd));
+            }
+        } else {
         {
             GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
             g.batch = D.H;
@@ -724,7 +882,7 @@ int backward(const Run &R, const float *lora, float *grad) {
             g.bdiv = D.G;
             g.sC = (int64_t)Tn * Tn;
             g.causal = 1;
-            TRY(launch_gemm(g, st));
+            TRY(gemm(R, g));
         }
         for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
             GemmArgs g = G(R, P + (int64_t)gi * Tn * Tn, Tn, 1, tp.dy + gi * D.hd, d, 0, tp.dqkv + d + D.kvd,
@@ -734,7 +892,7 @@ int backward(const Run &R, const float *lora, float *grad) {
             g.sB = (int64_t)D.G * D.hd;
             g.sC = D.hd;
             g.causal = 3;
-            TRY(launch_gemm(g, st));
+            TRY(gemm(R, g));
         }
         ALTXS_LAUNCH(kKTtt, st, t_softmax_bwd<<<D.H * Tn, 256, 0, st>>>(D, P, tp.dS, att_scale));
         {
@@ -745,7 +903,7 @@ int backward(const Run &R, const float *lora, float *grad) {
             g.bdiv = D.G;
             g.sC = D.hd;
             g.causal = 2;
-            TRY(launch_gemm(g, st));
+            TRY(gemm(R, g));
         }
         for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
             GemmArgs g = G(R, tp.dS + (int64_t)gi * Tn * Tn, Tn, 1, qr + gi * D.hd, d, 0, tp.dkr, D.kvd, Tn, D.hd,
@@ -755,7 +913,8 @@ int backward(const Run &R, const float *lora, float *grad) {
             g.sB = (int64_t)D.G * D.hd;
             g.sC = D.hd;
             g.causal = 3;
-            TRY(launch_gemm(g, st));
+            TRY(gemm(R, g));
+        }
         }
         ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, tp, *w));
         TRY(lora_bwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
@@ -768,7 +927,7 @@ int backward(const Run &R, const float *lora, float *grad) {
         TRY(lora_bwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
                      tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, grad + lo.vA + l * lo.v_stride,
                      grad + lo.vB + l * lo.v_stride, tp.dn));
-        TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, l * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
+        TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), l * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
         ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Tn * d,
                                                              tp.inv1 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
                                                              tp.dx));
@@ -779,6 +938,19 @@ int backward(const Run &R, const float *lora, float *grad) {
 
 constexpr int64_t kSplitkFloats = 16ll << 20;  // 64 MiB of split-K partials
 
+// plane scratch of the tensor-core path (uint16 elements): A = the largest
+// split operand (P, dS [H][T][T]; dlogits [T][V]; MLP [T][F]), B = the
+// attention right operands ([T][H*hd] at most)
+void tc_scratch(const TD &D, int64_t *a_n, int64_t *b_n) {
+    const int64_t T = D.T;
+    int64_t a = (int64_t)D.H * T * align_up(T, 8);
+    a = a > T * align_up(D.V, 8) ? a : T * align_up(D.V, 8);
+    a = a > T * align_up(D.F, 8) ? a : T * align_up(D.F, 8);
+    a = a > T * align_up(D.qn, 8) ? a : T * align_up(D.qn, 8);
+    *a_n = 2 * align_up(a, 128);
+    *b_n = 2 * align_up(T * align_up(D.hd, 8) * (D.H > D.Hkv ? D.H : D.Hkv), 128);
+}
+
 }  // namespace
 
 extern "C" {
@@ -786,7 +958,10 @@ extern "C" {
 int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T) {
     TD D{};
     if (!desc || fill(*desc, T, D)) return -1;
-    return carve(D, nullptr, nullptr) + align_up(lora_offsets(*desc).total * 4, 256) + kSplitkFloats * 4;
+    int64_t a_n, b_n;
+    tc_scratch(D, &a_n, &b_n);
+    return carve(D, nullptr, nullptr) + align_up(lora_offsets(*desc).total * 4, 256) + kSplitkFloats * 4 +
+           align_up(a_n * 2, 256) + align_up(b_n * 2, 256);
 }
 
 int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t stream) {
@@ -814,6 +989,12 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
     R.tp.grad = grad;
     R.splitk = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(grad) + align_up(lo.total * 4, 256));
     R.splitk_floats = kSplitkFloats;
+    R.sp = w->split;
+    if (R.sp) {
+        tc_scratch(R.D, &R.tca_n, &R.tcb_n);
+        R.tca = reinterpret_cast<uint16_t *>(R.splitk + kSplitkFloats);
+        R.tcb = R.tca + align_up(R.tca_n, 128);
+    }
     cudaStream_t st = R.st;
     cudaMemsetAsync(grad, 0, lo.total * 4, st);
     TRY(forward(R, tokens, tokens + 1, lora, loss_out));

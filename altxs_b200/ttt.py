@@ -23,7 +23,8 @@ from .engine import DeviceModel, StreamBatch, _stream_handle
 class LoraTTT:
     def __init__(self, dm: DeviceModel, *, dense_base: bool = True):
         self.dm = dm
-        self.dense = dm.dense_weights() if dense_base else None
+        # the tensor-core path reads the bf16 planes; the dense fp32 copy serves the CUDA-core path
+        self.dense = dm.dense_weights() if dense_base and not dm.tensor_cores else None
         cfg = dm.cfg
         if not cfg.lora_enabled:
             raise ValueError("test-time update needs retrain_mode='lora' and a positive rank")

@@ -251,6 +251,21 @@ int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t st
  * altxs_split_planes); both 16-byte aligned. */
 int altxs_split_weights(const altxs_qmat *m, uint16_t *hi, uint16_t *lo, altxs_stream_t stream);
 
+/* Batched fp32 GEMM on the tensor cores (hi/lo bf16 planes, fp32
+ * accumulate; products within 2^-16 relative):
+ *   C[b] = alpha * op(A[b]) op(B[b]) + beta * C[b],  b < batch,
+ * op(A) M x K: A stored [M][lda] (tA = 0) or [K][lda] (tA = 1), batch stride sA;
+ * op(B) K x N: B stored [K][ldb] (tB = 0) or [N][ldb] (tB = 1), batch stride sB;
+ * C [M][ldc], batch stride sC.  causal: 0 all of C; 1 output tiles wholly
+ * above the diagonal (n > m) may be left unwritten; 2 op(A) is zero for
+ * k > m; 3 op(A) is zero for k < m.  These are the products of the
+ * test-time update's forward and backward (the reference's torch matmuls in
+ * ttt_lora.py and the training attention, train_attn.py:578). */
+int64_t altxs_gemm_workspace_bytes(int M, int N, int K, int tA, int tB, int batch);
+int altxs_gemm(int M, int N, int K, const float *A, int64_t lda, int64_t sA, int tA, const float *B, int64_t ldb,
+               int64_t sB, int tB, float *C, int64_t ldc, int64_t sC, int batch, float alpha, float beta, int causal,
+               void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+
 /* One linear layer, Y[i][j] = sum_k X[i][k] * m[row0 + j][k] for i < M,
  * j < N (X row stride m->cols, Y row stride N): the reference's
  * F.linear on the dequantised weight (altxs src/xsa_ttt/model.py:123-127,

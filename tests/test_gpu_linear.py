@@ -88,3 +88,52 @@ def test_tensor_core_rows_do_not_depend_on_the_batch(model):
     for i in (0, 127, 128, 255, 299):
         alone = _linear(model, "qkv", X[i: i + 1], 0, 512, True)
         assert np.array_equal(alone.view(np.uint32), full[i: i + 1].view(np.uint32)), i
+
+
+def _gemm(A, B, M, N, K, tA, tB, batch, alpha=1.0, beta=0.0, C0=None, causal=0):
+    from altxs_b200 import _lib
+
+    L = _lib.lib()
+    Ad = torch.as_tensor(A, device=DEV).contiguous()
+    Bd = torch.as_tensor(B, device=DEV).contiguous()
+    C = torch.as_tensor(C0 if C0 is not None else np.zeros((batch, M, N), np.float32), device=DEV).contiguous()
+    lda, ldb = Ad.shape[-1], Bd.shape[-1]
+    wsb = int(L.altxs_gemm_workspace_bytes(M, N, K, tA, tB, batch))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=DEV)
+    rc = L.altxs_gemm(M, N, K, Ad.data_ptr(), lda, Ad[0].numel(), tA, Bd.data_ptr(), ldb, Bd[0].numel(), tB,
+                      C.data_ptr(), N, M * N, batch, alpha, beta, causal, ws.data_ptr(), wsb, None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return C.cpu().numpy()
+
+
+@pytest.mark.parametrize("tA,tB", [(0, 1), (0, 0), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K,batch", [(200, 96, 333, 3), (64, 64, 2048, 2), (300, 130, 64, 1)])
+def test_gemm_transposes_match_float64(tA, tB, M, N, K, batch):
+    """Every operand orientation (K-major and MN-major tensor-core tiles),
+    ragged sizes, batches, alpha and beta, against float64."""
+    rng = np.random.default_rng(M * 7 + N + K + 3 * tA + tB)
+    A = rng.normal(0, 1, size=(batch, K, M) if tA else (batch, M, K)).astype(np.float32)
+    B = rng.normal(0, 1, size=(batch, N, K) if tB else (batch, K, N)).astype(np.float32)
+    C0 = rng.normal(0, 1, size=(batch, M, N)).astype(np.float32)
+    got = _gemm(A, B, M, N, K, tA, tB, batch, alpha=0.5, beta=0.25, C0=C0)
+    opA = np.swapaxes(A, 1, 2) if tA else A
+    opB = np.swapaxes(B, 1, 2) if tB else B
+    ref = 0.5 * np.einsum("bmk,bkn->bmn", opA.astype(np.float64), opB.astype(np.float64)) + 0.25 * C0
+    bound = 0.5 * np.einsum("bmk,bkn->bmn", np.abs(opA).astype(np.float64), np.abs(opB).astype(np.float64))
+    err = np.abs(got - ref)
+    assert np.all(err <= 2.0 ** -15 * bound + 2.0 ** -22 * np.abs(ref) + 1e-30), float((err / (bound + 1e-30)).max())
+
+
+@pytest.mark.parametrize("causal", [2, 3])
+def test_gemm_triangular_operands(causal):
+    """Modes 2/3 read only the K range a triangular op(A) can be nonzero in."""
+    rng = np.random.default_rng(causal)
+    T, N = 300, 64
+    A = rng.normal(0, 1, size=(1, T, T)).astype(np.float32)
+    A[0] = np.tril(A[0]) if causal == 2 else np.triu(A[0])
+    B = rng.normal(0, 1, size=(1, T, N)).astype(np.float32)
+    got = _gemm(A, B, T, N, T, 0, 0, 1, causal=causal)
+    ref = A[0].astype(np.float64) @ B[0].astype(np.float64)
+    bound = np.abs(A[0]).astype(np.float64) @ np.abs(B[0]).astype(np.float64)
+    assert np.all(np.abs(got[0] - ref) <= 2.0 ** -15 * bound + 1e-30)

@@ -56,14 +56,17 @@ def _arena(lora, cfg):
     return np.concatenate(out)
 
 
-@pytest.mark.parametrize("dense", [True, False])
-def test_ttt_update_matches_oracle(golden, dense):
+@pytest.mark.parametrize("path", ["tensor_cores", "dense", "packed"])
+def test_ttt_update_matches_oracle(golden, path):
+    """The update on the tensor cores, on CUDA cores from a dense fp32 copy of
+    the base, and on CUDA cores from the packed codes."""
     from altxs_b200.engine import DeviceModel
 
     g = golden("lora_small.npz")
     cfg = ModelConfig(**SMALL)
     w = C_.synth_weights(cfg, seed=7)
-    dm = DeviceModel(w, DEV)
+    dm = DeviceModel(w, DEV, tensor_cores=path == "tensor_cores")
+    dense = path == "dense"
     om = OracleModel(OracleWeights.from_model_weights(w))
     ttt = OracleTTT(om)
     vec0 = _arena(ttt.lora, cfg)
