@@ -176,9 +176,16 @@ __device__ inline uint64_t logits_to_masses(float *buf, int V, int mode, int cdf
         }
         S = block_sum_u64(S, sc.ured);
         const uint64_t budget = (1ull << cdf_bits) - (uint64_t)V;
+        // floor(u * budget / S) for every entry: a double-precision estimate
+        // (off by at most one or two) corrected with exact integer products
+        const double inv = (double)budget / (double)S;
         unsigned long long tot = 0;
         for (int i = tid; i < V; i += nt) {
-            const uint32_t f = 1u + (uint32_t)(((uint64_t)m[i] * budget) / S);
+            const uint64_t a = (uint64_t)m[i] * budget;
+            uint64_t q = (uint64_t)((double)m[i] * inv);
+            while (q > 0 && q * S > a) --q;
+            while ((q + 1) * S <= a) ++q;
+            const uint32_t f = 1u + (uint32_t)q;
             m[i] = f;
             tot += f;
         }

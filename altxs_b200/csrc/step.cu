@@ -124,25 +124,57 @@ __global__ void k_prenorm(StepCtx c, int l) {
     }
 }
 
-// t[r] = A[r] . x  (warp per rank row; lane-strided sums, fixed tree)
+// t[r] = A[r] . x  (warp per rank row; each lane sums its 16-byte chunks of
+// the row in order, then a fixed warp tree; the chunk loads of a row are
+// issued before the sums).  Unaligned operands take the scalar order.
 __device__ inline void lora_t(const float *A, const float *x, int rank, int d, float *t) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(x)) & 15) || (d & 3)) {
+        for (int r = wid; r < rank; r += nw) {
+            float s = 0.0f;
+            for (int k = lane; k < d; k += 32) s = __fmaf_rn(x[k], A[(int64_t)r * d + k], s);
+            s = warp_sum(s);
+            if (lane == 0) t[r] = s;
+        }
+        return;
+    }
+    const int d4 = d >> 2;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
     for (int r = wid; r < rank; r += nw) {
+        const float4 *a4 = reinterpret_cast<const float4 *>(A + (int64_t)r * d);
         float s = 0.0f;
-        for (int k = lane; k < d; k += 32) s = __fmaf_rn(x[k], A[(int64_t)r * d + k], s);
+#pragma unroll 4
+        for (int k = lane; k < d4; k += 32) {
+            const float4 a = a4[k], xv = x4[k];
+            s = __fmaf_rn(xv.x, a.x, s);
+            s = __fmaf_rn(xv.y, a.y, s);
+            s = __fmaf_rn(xv.z, a.z, s);
+            s = __fmaf_rn(xv.w, a.w, s);
+        }
         s = warp_sum(s);
         if (lane == 0) t[r] = s;
     }
 }
-// delta = (B[j] . t) * scale
+// delta = (B[j] . t) * scale (ascending r; 16-byte loads when the rank allows)
 __device__ __forceinline__ float lora_u(const float *B, const float *t, int rank, int j, float scale) {
     float u = 0.0f;
-    for (int r = 0; r < rank; ++r) u = __fmaf_rn(B[(int64_t)j * rank + r], t[r], u);
+    if ((rank & 3) == 0 && !(reinterpret_cast<uintptr_t>(B) & 15)) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(B + (int64_t)j * rank);
+        for (int r4 = 0; r4 < (rank >> 2); ++r4) {
+            const float4 b = b4[r4];
+            u = __fmaf_rn(b.x, t[4 * r4], u);
+            u = __fmaf_rn(b.y, t[4 * r4 + 1], u);
+            u = __fmaf_rn(b.z, t[4 * r4 + 2], u);
+            u = __fmaf_rn(b.w, t[4 * r4 + 3], u);
+        }
+    } else {
+        for (int r = 0; r < rank; ++r) u = __fmaf_rn(B[(int64_t)j * rank + r], t[r], u);
+    }
     return __fmul_rn(u, scale);
 }
 
 // LoRA on q/k/v, per-head RMSNorm, partial RoPE, q_gain, KV ring write.
-__global__ void k_qkv_post(StepCtx c, int l) {
+__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, int l) {
     extern __shared__ __align__(16) float sm[];
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;

@@ -343,13 +343,29 @@ __global__ void k_split_weights(altxs_qmat W, uint16_t *hi, uint16_t *lo) {
         split_store(hi, lo, (int64_t)row * W.cols + k, qmat_elem(W, row, k));
 }
 
-// one CTA per (row, batch); planes compact with row stride ldo
+// 8 consecutive output columns per thread (one 16-byte store per plane);
+// planes compact [nb][rows][ldo], ldo a multiple of 8, zero past cols
 __global__ void k_split_f32(const float *src, int64_t cols, int64_t ld, int64_t bs, int64_t rows, int64_t ldo,
-                            uint16_t *hi, uint16_t *lo) {
-    const int64_t row = blockIdx.x, b = blockIdx.y;
-    const float *s = src + b * bs + row * ld;
-    const int64_t o = (b * rows + row) * ldo;
-    for (int64_t k = threadIdx.x; k < ldo; k += blockDim.x) split_store(hi, lo, o + k, k < cols ? s[k] : 0.0f);
+                            int64_t n8, uint16_t *hi, uint16_t *lo) {
+    const int64_t g8 = ldo / 8;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c0 = (i % g8) * 8, br = i / g8, r = br % rows, b = br / rows;
+        const float *s = src + b * bs + r * ld;
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t c = c0 + 2 * u;
+            const float v0 = c < cols ? s[c] : 0.0f, v1 = c + 1 < cols ? s[c + 1] : 0.0f;
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
+            const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(v0, __bfloat162float(h0)));
+            const __nv_bfloat16 l1 = __float2bfloat16_rn(__fsub_rn(v1, __bfloat162float(h1)));
+            h[u] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+            l[u] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+        }
+        const int64_t o = br * ldo + c0;
+        *reinterpret_cast<uint4 *>(hi + o) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4 *>(lo + o) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -495,10 +511,12 @@ int launch_split_weights(const altxs_qmat &W, uint16_t *hi, uint16_t *lo, cudaSt
 int launch_split_f32(const float *src, int64_t rows, int64_t cols, int64_t ld, int nb, int64_t bs, uint16_t *hi,
                      uint16_t *lo, cudaStream_t st, int kernel_class) {
     if (rows <= 0 || cols <= 0 || nb <= 0) return ALTXS_OK;
-    if (!src || !hi || !lo || rows > 2147483647 || nb > 65535) return ALTXS_EINVAL;
-    const int64_t ldo = align_up(cols, 8);
-    ALTXS_LAUNCH(kernel_class, st,
-                 k_split_f32<<<dim3((unsigned)rows, (unsigned)nb), 256, 0, st>>>(src, cols, ld, bs, rows, ldo, hi, lo));
+    if (!src || !hi || !lo) return ALTXS_EINVAL;
+    const int64_t ldo = align_up(cols, 8), n8 = (int64_t)nb * rows * (ldo / 8);
+    if (!aligned16(hi) || !aligned16(lo)) return ALTXS_EINVAL;
+    const int64_t blocks = (n8 + 255) / 256;
+    const unsigned grid = (unsigned)(blocks < 148 * 16 ? blocks : 148 * 16);
+    ALTXS_LAUNCH(kernel_class, st, k_split_f32<<<grid, 256, 0, st>>>(src, cols, ld, bs, rows, ldo, n8, hi, lo));
     return ALTXS_OK;
 }
 
