@@ -24,7 +24,7 @@ EXPORTS = (
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
-    "altxs_gemm_workspace_bytes", "altxs_gemm",
+    "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -118,6 +118,7 @@ def lib():
             "altxs_version": (C.c_char_p, []),
             "altxs_launch_count": (i64, []),
             "altxs_profile": (C.c_int, [C.c_int]),
+            "altxs_profile_mask": (C.c_int, [C.c_uint32]),
             "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
             "altxs_step_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int,
                                              vp]),

@@ -9,6 +9,7 @@ namespace altxs {
 namespace {
 
 std::atomic<int64_t> g_launches{0};
+std::atomic<uint32_t> g_mask{0xffffffffu};  // kernel classes recorded while profiling
 
 struct Profiler {
     std::mutex mu;
@@ -25,7 +26,7 @@ constexpr size_t kMaxPairs = 16384;
 
 void prof_begin(cudaStream_t s, int c) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    if (!g_prof.on) return;
+    if (!g_prof.on || c < 0 || c > 31 || !((g_mask.load(std::memory_order_relaxed) >> c) & 1u)) return;
     std::lock_guard<std::mutex> lk(g_prof.mu);
     if (g_prof.used >= g_prof.cls.size()) {
         g_prof.pending_cls = -1;
@@ -68,6 +69,11 @@ int altxs_profile(int enable) {
     } else {
         g_prof.on = false;
     }
+    return ALTXS_OK;
+}
+
+int altxs_profile_mask(uint32_t mask) {
+    g_mask.store(mask);
     return ALTXS_OK;
 }
 

@@ -306,24 +306,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
                 __syncwarp();
+                // this lane's column of the block: all reads first (the residual
+                // input may be the output array itself), then the stores
+                float col[32];
+#pragma unroll
+                for (int rr = 0; rr < 32; ++rr) col[rr] = eb[rr][lane];
                 const int n = T.n0 + c0 + lane;
-                const bool col_ok = n < g.N;
-                const float cs = (g.epi == kEpiResid && col_ok) ? g.colscale[n] : 0.0f;
-#pragma unroll 4
-                for (int rr = 0; rr < 32; ++rr) {
-                    const int m = T.m0 + warp * 32 + rr;
-                    if (m >= g.M || !col_ok) continue;
-                    float x = eb[rr][lane];
-                    if (g.epi == kEpiResid) {
-                        x = __fadd_rn(g.R[(int64_t)m * g.ldr + n], __fmul_rn(cs, x));
-                    } else {
-                        if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
-                        if (g.beta != 0.0f) x = __fadd_rn(x, __fmul_rn(g.beta, Cb[(int64_t)m * g.ldc + n]));
-                        if (g.epi == kEpiLeaky2) x = leaky2(x);
+                const int mb = T.m0 + warp * 32;
+                const int nr = g.M - mb < 32 ? g.M - mb : 32;
+                if (n >= g.N || nr <= 0) continue;
+                if (g.epi == kEpiResid) {
+                    const float cs = g.colscale[n];
+                    float rv[32];
+#pragma unroll
+                    for (int rr = 0; rr < 32; ++rr) rv[rr] = rr < nr ? g.R[(int64_t)(mb + rr) * g.ldr + n] : 0.0f;
+#pragma unroll
+                    for (int rr = 0; rr < 32; ++rr) col[rr] = __fadd_rn(rv[rr], __fmul_rn(cs, col[rr]));
+                } else {
+                    if (g.alpha != 1.0f) {
+#pragma unroll
+                        for (int rr = 0; rr < 32; ++rr) col[rr] = __fmul_rn(g.alpha, col[rr]);
                     }
-                    if (Cb) Cb[(int64_t)m * g.ldc + n] = x;
-                    if (g.Y2) g.Y2[(int64_t)m * g.ldy2 + n] = x;
-                    if (g.p_hi) split_store(g.p_hi, g.p_lo, (int64_t)m * g.ldp + n, x);
+                    if (g.beta != 0.0f) {
+                        float cv[32];
+#pragma unroll
+                        for (int rr = 0; rr < 32; ++rr) cv[rr] = rr < nr ? Cb[(int64_t)(mb + rr) * g.ldc + n] : 0.0f;
+#pragma unroll
+                        for (int rr = 0; rr < 32; ++rr) col[rr] = __fadd_rn(col[rr], __fmul_rn(g.beta, cv[rr]));
+                    }
+                    if (g.epi == kEpiLeaky2) {
+#pragma unroll
+                        for (int rr = 0; rr < 32; ++rr) col[rr] = leaky2(col[rr]);
+                    }
+                }
+#pragma unroll
+                for (int rr = 0; rr < 32; ++rr) {
+                    if (rr >= nr) break;
+                    const int64_t m = mb + rr;
+                    if (Cb) Cb[m * g.ldc + n] = col[rr];
+                    if (g.Y2) g.Y2[m * g.ldy2 + n] = col[rr];
+                    if (g.p_hi) split_store(g.p_hi, g.p_lo, m * g.ldp + n, col[rr]);
                 }
             }
         }

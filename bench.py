@@ -57,6 +57,10 @@ def parse_args():
                     help="how the windows are filled before timing: code the preceding 2048 symbols "
                          "(default) or write seeded random K/V rows (profiling runs: same per-step work, "
                          "no 2048-step warm-up)")
+    ap.add_argument("--c2", action="store_true",
+                    help="instead of the decode benchmark: the linear-layer microbenchmark (the C3 layer "
+                         "shapes K x N at M = 1, 16, 128, 512 rows, tensor-core and CUDA-core paths), one "
+                         "JSON line per case")
     return ap.parse_args()
 
 
@@ -167,6 +171,75 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_c2(args) -> None:
+    """Linear-layer microbenchmark: Y = X W^T for the C3 layer shapes (layer 0
+    of the benchmark model's qkv, o, up, down matrices; 3.15-bit mixed-bit
+    weights + fp16 group scales) at M rows of N(0,1) activations.  Each timed
+    call is one ``altxs_linear`` (tensor cores: hi/lo split of X + tcgen05
+    GEMM; CUDA cores: packed-code GEMV/GEMM), CUDA events around the call, L2
+    flushed (256 MB written, then read) before every call, median of 20.  Roofline: HBM for
+    M <= 64 on the algorithmic bytes K*N*3.40/8 + 2*M*K + 2*M*N (packed weights
+    incl. scales, bf16 activations), tensor cores above on 2*M*K*N."""
+    import ctypes
+
+    from altxs_b200 import _lib
+    from altxs_b200 import codec as C
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import DeviceModel
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = c3_config()
+    dm = DeviceModel(C.synth_weights(cfg, seed=WEIGHT_SEED), dev)
+    L = _lib.lib()
+    peaks, kind = load_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    st = torch.cuda.current_stream().cuda_stream
+    for name, K, N in (("qkv", 512, 1536), ("o", 512, 512), ("up", 512, 2048), ("down", 2048, 512)):
+        q = dm.q[name]
+        for M in (1, 16, 128, 512, 2048):  # the C2 sizes, then the bench's per-GPU batch
+            X = torch.randn(M, K, generator=g, device=dev)
+            Y = torch.empty(M, N, device=dev)
+            wsb = int(L.altxs_linear_workspace_bytes(M, K))
+            ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+            for path in ("tensor", "cuda_core"):
+                hi = getattr(dm._split, f"{name}_hi") if path == "tensor" else None
+                lo = getattr(dm._split, f"{name}_lo") if path == "tensor" else None
+
+                def call():
+                    rc = L.altxs_linear(ctypes.byref(q), hi, lo, 0, N, X.data_ptr(), M, Y.data_ptr(),
+                                        ws.data_ptr(), wsb, st)
+                    _lib.check(rc, "altxs_linear")
+
+                for _ in range(3):
+                    call()
+                times = []
+                for _ in range(20):
+                    # write then read 256 MB: L2 holds none of the operands, and no dirty
+                    # lines whose write-back would land inside the timed call
+                    flush.zero_()
+                    flush.sum()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    call()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    times.append(e0.elapsed_time(e1) / 1000.0)
+                t = statistics.median(times)
+                alg_bytes = K * N * 3.40 / 8 + 2 * M * K + 2 * M * N
+                flops = 2.0 * M * K * N
+                if M <= 64:
+                    bound, achieved, peak, unit = "hbm", alg_bytes / t / 1e9, peaks["hbm_gbs"], "GB/s"
+                else:
+                    bound, achieved, peak, unit = "tensor", flops / t / 1e12, peaks["bf16_tflops"], "TFLOP/s"
+                print(json.dumps({"c2": True, "matrix": name, "K": K, "N": N, "M": M, "path": path,
+                                  "us": t * 1e6, "tflops": flops / t / 1e12, "alg_gbs": alg_bytes / t / 1e9,
+                                  "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                                  "frac": achieved / peak, "peak_source": f"{kind}"}), flush=True)
+
+
 def config_block(world: int, streams: int) -> dict:
     return {
         "workload": "box-scale sharded decode: 2048 independent streams split over N GPUs, 33M model "
@@ -202,6 +275,10 @@ def boundary_plan(gids: np.ndarray, n_global: int, world: int, n_local: int, eve
 def main():
     args = parse_args()
     rank, world, local = dist_env()
+    if args.c2:
+        if rank == 0:
+            run_c2(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
@@ -368,6 +445,9 @@ def main():
         torch.cuda.synchronize(dev)
         state["clocks"] = ClockSampler(local)
         time.sleep(0.3)
+        # live events around the attention launches only (the roofline kernel);
+        # the per-class breakdown comes from a separate profiled pass below
+        L.altxs_profile_mask(1 << _lib.KERNEL_CLASSES.index("attn_partial"))
         L.altxs_profile(1)
         state["launches0"] = L.altxs_launch_count()
         torch.cuda.nvtx.range_push("timed")
@@ -379,6 +459,7 @@ def main():
         torch.cuda.synchronize(dev)
         state["launches"] = L.altxs_launch_count() - state["launches0"]
         L.altxs_profile(0)
+        L.altxs_profile_mask(0xFFFFFFFF)
         state["clk"] = state["clocks"].stop()
         if pg:
             pg.barrier()
@@ -422,6 +503,26 @@ def main():
         pg.all_reduce(t_, op=pg.ReduceOp.MAX)
         e2e_ms = float(t_.item())
     ok_e2e = torch.equal(out_h, chunk_syms.cpu())
+
+    # ---- per-class breakdown: the same K steps again, every launch bracketed
+    # by events (untimed; event pairs cost time of their own) ----------------
+    restore()
+    stage_d.copy_(stage_h)
+    nbits_d.copy_(nbits_h)
+    dsyms3 = torch.empty((chunk, b.n), dtype=torch.int32, device=dev)
+
+    def on_start_prof():
+        torch.cuda.synchronize(dev)
+        L.altxs_profile(1)
+
+    def on_end_prof():
+        torch.cuda.synchronize(dev)
+        L.altxs_profile(0)
+
+    decode_chunk(W, dsyms3, on_start_prof, on_end_prof)
+    L.altxs_profile_read(ncls, pms, pcnt)
+    breakdown = {name: {"ms_per_step": pms[i] / K, "launches": int(pcnt[i])}
+                 for i, name in enumerate(_lib.KERNEL_CLASSES) if pcnt[i]}
 
     # per-stream (symbols, bytes) gathered over NCCL (the only collective)
     counts = torch.tensor([[chunk, sum(len(p) for p in sg)] for sg in segs], dtype=torch.int64, device=dev)
@@ -480,7 +581,7 @@ def main():
                 "h2d_bytes_per_step": h2d // chunk, "d2h_bytes_per_step": int(b.n * 4),
                 "path": "StreamBatch steps + LoraTTT with pinned host segments in, host symbols out"},
         "gpu_launches": int(launches),
-        "kernel_ms_per_step": prof,
+        "kernel_ms_per_step": breakdown,
         "clocks": clk,
         "total_payload_bytes": total_bytes,
         "weights_device_bytes": dm.weight_bytes,

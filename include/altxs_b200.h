@@ -313,6 +313,11 @@ int altxs_profile(int enable);
  * 9 standalone coder, 10 test-time LoRA.  Returns the number of pairs read. */
 int altxs_profile_read(int n_classes, double *ms, int64_t *counts);
 
+/* Restrict recording to the classes whose bit is set in mask (bit c = class
+ * c above; default all).  A benchmark times one class live without paying for
+ * event pairs around every other launch. */
+int altxs_profile_mask(uint32_t mask);
+
 /* Library build string (for logs). */
 const char *altxs_version(void);
 

@@ -137,3 +137,19 @@ def test_gemm_triangular_operands(causal):
     ref = A[0].astype(np.float64) @ B[0].astype(np.float64)
     bound = np.abs(A[0]).astype(np.float64) @ np.abs(B[0]).astype(np.float64)
     assert np.all(np.abs(got[0] - ref) <= 2.0 ** -15 * bound + 1e-30)
+
+
+def test_rows_do_not_depend_on_tile_width():
+    """At the 33M shapes a 2048-row call runs 128-wide output tiles and a
+    1-row call 64-wide ones: rows must agree bit for bit all the same."""
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import DeviceModel
+
+    dm = DeviceModel(Cd.synth_weights(c3_config(), seed=5), DEV)
+    rng = np.random.default_rng(9)
+    for name, N in (("qkv", 1536), ("emb", 16384)):
+        X = rng.normal(0, 1, size=(2048, 512)).astype(np.float32)
+        full = _linear(dm, name, X, 0, N, True)
+        for i in (0, 700, 2047):
+            alone = _linear(dm, name, X[i: i + 1], 0, N, True)
+            assert np.array_equal(alone.view(np.uint32), full[i: i + 1].view(np.uint32)), (name, i)
