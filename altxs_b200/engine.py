@@ -182,8 +182,17 @@ class StreamBatch:
     """Device state of n independent streams on one GPU."""
 
     def __init__(self, dm: DeviceModel, n: int, *, words_per_stream: int, hist_len: int = 0,
-                 keep_logits: bool = False):
+                 keep_logits: bool = False, graphs: bool = False):
+        """``graphs=True`` replays each step mode from a CUDA graph captured on
+        its second call (every call still runs exactly one step): the step's
+        kernels read their per-step inputs from device memory, so one capture
+        serves every later step of this batch."""
         cfg, dev = dm.cfg, dm.device
+        self.graphs = bool(graphs)
+        self._graphs: dict = {}
+        self._graph_seen: set = set()
+        self.graph_kernels: dict = {}  # kernels per captured step, by key
+        self.replays = 0
         self.dm, self.n, self.cfg = dm, int(n), cfg
         self.words_per_stream = int(words_per_stream)
         L, Hkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
@@ -294,6 +303,28 @@ class StreamBatch:
 
     # ---- step ---------------------------------------------------------------
     def step(self, mode: int) -> None:
+        if self.graphs:
+            key = (int(mode), id(self.dm.weights_struct))
+            g = self._graphs.get(key)
+            if g is None and key in self._graph_seen:
+                dev = self.dm.device
+                g = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream(device=dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                n0 = _lib.lib().altxs_launch_count()
+                with torch.cuda.graph(g, stream=side):
+                    self._launch(mode)
+                self.graph_kernels[key] = int(_lib.lib().altxs_launch_count() - n0)
+                torch.cuda.current_stream(dev).wait_stream(side)
+                self._graphs[key] = g
+            if g is not None:
+                g.replay()
+                self.replays += 1
+                return
+            self._graph_seen.add(key)
+        self._launch(mode)
+
+    def _launch(self, mode: int) -> None:
         rc = _lib.lib().altxs_step(
             C.byref(self.dm.desc), C.byref(self.dm.weights_struct), C.byref(self._batch), int(mode),
             _stream_handle(self.dm.device),

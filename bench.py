@@ -14,9 +14,13 @@ there is no collective on the hot path (weak per-stream work, fixed total
 streams -> "strong" scaling); NCCL only gathers per-stream byte counts.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
-cuda synchronize, CUDA events on the launch stream, max over ranks.  The KV
-windows (~103 GB per GPU at N=1) are far larger than L2, so every step
-streams its inputs from HBM.
+cuda synchronize, CUDA events on the launch stream, max over ranks.  Each
+step replays the decode step from a CUDA graph (captured on its first calls);
+updates and segment reloads launch eagerly in between.  The KV windows
+(~103 GB per GPU at N=1) are far larger than L2, so every step streams its
+inputs from HBM.  The per-kernel breakdown and the attention roofline come
+from re-running the same K steps launch by launch with CUDA events around
+every launch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -311,7 +315,8 @@ def main():
     data = zipf_markov(cfg.ctx + chunk, cfg.vocab_size, 1000 + gids)  # [n][T]
     symsT = torch.from_numpy(np.ascontiguousarray(data.T)).to(dev)     # [T][n]
     wps = words_for_segment(max(cfg.ctx, chunk), cfg.cdf_bits)
-    b = StreamBatch(dm, n_local, words_per_stream=wps, hist_len=cfg.ctx + 2)
+    # each step mode is replayed from a CUDA graph after its first call
+    b = StreamBatch(dm, n_local, words_per_stream=wps, hist_len=cfg.ctx + 2, graphs=True)
     ttt = LoraTTT(dm)
     L = _lib.lib()
     stream_h = _stream_handle(dev)
@@ -445,11 +450,8 @@ def main():
         torch.cuda.synchronize(dev)
         state["clocks"] = ClockSampler(local)
         time.sleep(0.3)
-        # live events around the attention launches only (the roofline kernel);
-        # the per-class breakdown comes from a separate profiled pass below
-        L.altxs_profile_mask(1 << _lib.KERNEL_CLASSES.index("attn_partial"))
-        L.altxs_profile(1)
-        state["launches0"] = L.altxs_launch_count()
+        state["launches0"] = L.altxs_launch_count()  # eager launches (updates, segment loads)
+        state["replays0"] = b.replays
         torch.cuda.nvtx.range_push("timed")
         e0.record()
 
@@ -457,9 +459,8 @@ def main():
         e1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(dev)
-        state["launches"] = L.altxs_launch_count() - state["launches0"]
-        L.altxs_profile(0)
-        L.altxs_profile_mask(0xFFFFFFFF)
+        per_graph = b.graph_kernels.get((_lib.STEP_DECODE, id(dm.weights_struct)), 0)
+        state["launches"] = (L.altxs_launch_count() - state["launches0"]) + (b.replays - state["replays0"]) * per_graph
         state["clk"] = state["clocks"].stop()
         if pg:
             pg.barrier()
@@ -475,9 +476,6 @@ def main():
     ncls = len(_lib.KERNEL_CLASSES)
     pms = (ctypes.c_double * ncls)()
     pcnt = (ctypes.c_int64 * ncls)()
-    L.altxs_profile_read(ncls, pms, pcnt)
-    prof = {name: {"ms_per_step": pms[i] / K, "launches": int(pcnt[i])}
-            for i, name in enumerate(_lib.KERNEL_CLASSES) if pcnt[i]}
     ok = torch.equal(dsyms, chunk_syms)
     b.check_status()
     timed_boundaries = sum(len(plan[t]) for t in range(W, chunk))
@@ -504,8 +502,10 @@ def main():
         e2e_ms = float(t_.item())
     ok_e2e = torch.equal(out_h, chunk_syms.cpu())
 
-    # ---- per-class breakdown: the same K steps again, every launch bracketed
-    # by events (untimed; event pairs cost time of their own) ----------------
+    # ---- per-class breakdown: the same K steps again, launched one by one
+    # (no graph) with every launch bracketed by CUDA events on its stream
+    # (event pairs cost time of their own, so this pass is not the value) ---
+    b.graphs = False
     restore()
     stage_d.copy_(stage_h)
     nbits_d.copy_(nbits_h)
@@ -520,9 +520,12 @@ def main():
         L.altxs_profile(0)
 
     decode_chunk(W, dsyms3, on_start_prof, on_end_prof)
+    b.graphs = True
     L.altxs_profile_read(ncls, pms, pcnt)
     breakdown = {name: {"ms_per_step": pms[i] / K, "launches": int(pcnt[i])}
                  for i, name in enumerate(_lib.KERNEL_CLASSES) if pcnt[i]}
+    ok = ok and torch.equal(dsyms3, chunk_syms)
+    prof = breakdown
 
     # per-stream (symbols, bytes) gathered over NCCL (the only collective)
     counts = torch.tensor([[chunk, sum(len(p) for p in sg)] for sg in segs], dtype=torch.int64, device=dev)
@@ -550,7 +553,9 @@ def main():
         roof = {"bound": "hbm", "kernel": "k_attn_ring", "achieved": achieved,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "traffic": traffic, "bytes_per_launch": bytes_launch, "avg_launch_ms": avg_ms,
-                "peak_source": f"{peak_kind} hbm_gbs"}
+                "peak_source": f"{peak_kind} hbm_gbs",
+                "timing": "CUDA events around each attention launch on its stream, over the same K "
+                          "steps re-run launch by launch after the graph-replayed timed pass"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.baseline import cpu_decode_baseline

@@ -191,3 +191,28 @@ def test_c3_shape_step_runs_and_is_batch_independent():
     st = om.new_stream()
     ref = np.stack([om.step(st, int(t)).numpy() for t in toks[0]])
     assert float(np.abs(one - ref).max()) < TOL
+
+
+def test_graph_replay_matches_launches():
+    """StreamBatch(graphs=True) replays captured steps: same symbols, same bytes."""
+    from altxs_b200 import _lib
+    from altxs_b200.engine import DeviceModel, StreamBatch
+
+    cfg = _small()
+    dm = DeviceModel(C.synth_weights(cfg, seed=5), DEV)
+    rng = np.random.default_rng(8)
+    n, T = 5, 30
+    syms = rng.integers(0, cfg.vocab_size, size=(n, T)).astype(np.int32)
+    out = []
+    for graphs in (False, True):
+        b = StreamBatch(dm, n, words_per_stream=T + 8, graphs=graphs)
+        b.ac_init()
+        for t in range(T):
+            b.sym.copy_(torch.as_tensor(syms[:, t], device=DEV))
+            b.step(_lib.STEP_ENCODE)
+        b.ac_flush()
+        b.check_status()
+        out.append(b.segment_bytes(list(range(n))))
+        if graphs:
+            assert b.replays == T - 1
+    assert out[0] == out[1]
