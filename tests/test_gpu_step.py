@@ -216,3 +216,25 @@ def test_graph_replay_matches_launches():
         if graphs:
             assert b.replays == T - 1
     assert out[0] == out[1]
+
+
+def test_bpe_token_file_roundtrip(tmp_path):
+    """A BPE token file (uint16 ids, sidecar vocabulary) through the
+    reference-named entry points: encode, decode, identical tokens."""
+    import json
+
+    from altxs_b200.data import load_symbols
+    from altxs_b200.incremental import compress_full_sha_incremental, decompress_full_sha_incremental
+    from altxs_b200.synth import zipf_markov
+
+    cfg = _small()
+    toks = zipf_markov(150, cfg.vocab_size, np.array([77]))[0].astype("<u2")
+    p = tmp_path / "tokens.bin"
+    p.write_bytes(toks.tobytes())
+    (tmp_path / "tokens.bin.json").write_text(json.dumps({"format": "blsmc-bpe-v1", "vocab_size": cfg.vocab_size}))
+    arr, info = load_symbols(p)
+    assert info.vocab_size == cfg.vocab_size
+    w = C.synth_weights(cfg, seed=12)
+    enc = compress_full_sha_incremental(w, np.asarray(arr), cfg=cfg, progress=False)
+    dec = decompress_full_sha_incremental(w, enc["payload"], enc["n_symbols"], cfg=cfg, progress=False)
+    assert dec["decoded_sha256"] == enc["sha256"]
