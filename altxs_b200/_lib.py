@@ -24,7 +24,8 @@ EXPORTS = (
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
-    "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask",
+    "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
+    "altxs_prefill_workspace_bytes",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -85,7 +86,7 @@ class Batch(C.Structure):
         ("kv", C.c_void_p), ("lora", C.c_void_p), ("lora_stride", C.c_int64), ("ac", C.c_void_p),
         ("bits", C.c_void_p), ("words_per_stream", C.c_int64), ("sym", C.c_void_p),
         ("hist", C.c_void_p), ("hist_len", C.c_int32), ("logits_out", C.c_void_p),
-        ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64), ("pos_base", C.c_void_p),
     ]
 
 
@@ -128,6 +129,9 @@ def lib():
                                            C.POINTER(TttHparams), vp, C.c_int, vp, vp, vp, C.c_int, vp, vp, i64,
                                            vp]),
             "altxs_dequant": (C.c_int, [C.POINTER(QMat), vp, i64, vp]),
+            "altxs_prefill_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.c_int]),
+            "altxs_prefill": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(DenseWeights), vp,
+                                        C.c_int, vp, vp, vp, i64, vp]),
             "altxs_split_weights": (C.c_int, [C.POINTER(QMat), vp, vp, vp]),
             "altxs_linear_workspace_bytes": (i64, [C.c_int, C.c_int]),
             "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),

@@ -42,6 +42,12 @@ class ModelConfig:
     # sequence / lockstep (reference: block_size / online_retrain_every)
     block_size: int = 2048
     online_retrain_every: int = 16384
+    # context across segments: "sliding" keeps the last block_size tokens in a
+    # ring at absolute positions (this engine's default); "reset" rebuilds the
+    # context from the previous block_size symbols at positions 0.. after every
+    # boundary update and attends to the whole segment (the reference engine's
+    # reset_segment, incremental.py:858-897)
+    context_mode: str = "sliding"
     seed: int = 1337
     # test-time LoRA (reference ttt_* fields, config.py:144-165)
     retrain_mode: str = "lora"  # "lora" or "none"
@@ -87,6 +93,13 @@ class ModelConfig:
         return self.block_size
 
     @property
+    def kv_len(self) -> int:
+        """Rows of the per-stream KV ring: the window, or context + segment."""
+        if self.context_mode == "reset":
+            return self.block_size + self.online_retrain_every
+        return self.block_size
+
+    @property
     def lora_scale(self) -> float:
         r = float(self.ttt_lora_rank)
         if self.ttt_use_rslora:
@@ -119,6 +132,8 @@ class ModelConfig:
             raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
         if self.retrain_mode not in ("lora", "none"):
             raise ValueError("retrain_mode must be 'lora' or 'none'")
+        if self.context_mode not in ("sliding", "reset"):
+            raise ValueError("context_mode must be 'sliding' or 'reset'")
 
     def to_dict(self) -> dict[str, Any]:
         return dataclasses.asdict(self)

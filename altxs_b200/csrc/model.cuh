@@ -59,6 +59,21 @@ __device__ __forceinline__ float lerp_t(float start, float end, float wgt) {
                       : __fsub_rn(end, __fmul_rn(diff, __fsub_rn(1.0f, wgt)));
 }
 
+// KV rows are stored in a 24-bit split format: fp32 rounded to nearest-even
+// at bit 8, the high 16 bits (a bf16) and the next 8 mantissa bits kept in
+// separate parts of the row: [hd x u16 high][hd x u8 low] = 3*hd bytes.
+// fp16 K/V rounding moves the logits by up to ~1e-2 (the q_gain-scaled
+// scores are sensitive to K); 24 bits keep them within ~3e-4 of fp32.
+__device__ __forceinline__ uint32_t round24(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b + 0x7Fu + ((b >> 8) & 1u)) >> 8;  // 24-bit pattern
+}
+__device__ __forceinline__ void store_kv_row(uint8_t *row, int hd, int k, float v) {
+    const uint32_t r = round24(v);
+    reinterpret_cast<uint16_t *>(row)[k] = (uint16_t)(r >> 8);
+    row[2 * hd + k] = (uint8_t)(r & 0xFFu);
+}
+
 // dequantised W[row][col] (exact fp32 level*scale)
 __device__ __forceinline__ float qmat_elem(const altxs_qmat &W, int row, int col) {
     const int G = W.cols / 64, g = col >> 6, i = col & 63;

@@ -27,21 +27,6 @@ namespace {
 constexpr int kSplit = ALTXS_ATTN_SPLIT;  // keys per attention split (fixed: numerics independent of n)
 constexpr int kCdfThreads = 512;
 
-// KV rows are stored in a 24-bit split format: fp32 rounded to nearest-even
-// at bit 8, the high 16 bits (a bf16) and the next 8 mantissa bits kept in
-// separate parts of the row: [hd x u16 high][hd x u8 low] = 3*hd bytes.
-// fp16 K/V rounding moves the logits by up to ~1e-2 (the q_gain-scaled
-// scores are sensitive to K); 24 bits keep them within ~3e-4 of fp32.
-__device__ __forceinline__ uint32_t round24(float x) {
-    const uint32_t b = __float_as_uint(x);
-    return (b + 0x7Fu + ((b >> 8) & 1u)) >> 8;  // 24-bit pattern
-}
-__device__ __forceinline__ void store_kv_row(uint8_t *row, int hd, int k, float v) {
-    const uint32_t r = round24(v);
-    reinterpret_cast<uint16_t *>(row)[k] = (uint16_t)(r >> 8);
-    row[2 * hd + k] = (uint8_t)(r & 0xFFu);
-}
-
 struct Dims {
     int n, V, L, d, H, Hkv, hd, F, ctx, rd, r, nsplit, enc, nskip, qkv_n, kvd;
     int64_t lora_stride;
@@ -736,7 +721,10 @@ __global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
         if (tok >= 0) p += 1;
         c.b.pos[i] = p;
         c.b.tok[i] = sym;
-        if (c.b.hist) c.b.hist[(int64_t)i * c.b.hist_len + (p % c.b.hist_len)] = sym;
+        if (c.b.hist) {
+            const int64_t ap = p + (c.b.pos_base ? c.b.pos_base[i] : 0);  // absolute symbol index
+            c.b.hist[(int64_t)i * c.b.hist_len + (ap % c.b.hist_len)] = sym;
+        }
     }
 }
 

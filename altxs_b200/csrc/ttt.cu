@@ -37,7 +37,7 @@ struct Tape {
     float *dx, *dskip, *dd, *dh, *dn, *dn2, *dqkv, *dqr, *dkr, *dy, *dao, *dS, *dt, *grad, *red;
 };
 
-int fill(const altxs_model_desc &dsc, int T, TD &D) {
+int fill(const altxs_model_desc &dsc, int T, TD &D, bool prefill = false) {
     D.T = T;
     D.V = dsc.vocab;
     D.L = dsc.n_layers;
@@ -53,7 +53,9 @@ int fill(const altxs_model_desc &dsc, int T, TD &D) {
     D.nskip = D.enc < D.L - D.enc ? D.enc : D.L - D.enc;
     D.G = D.H / (D.Hkv > 0 ? D.Hkv : 1);
     D.rd = dsc.rope_dims;
-    if (T < 2 || D.r < 1 || D.r > 64 || D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
+    // an update trains adapters over >= 2 positions; a context prefill needs neither
+    if (T < (prefill ? 1 : 2) || D.r < (prefill ? 0 : 1) || D.r > 64) return ALTXS_EINVAL;
+    if (D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
     if (D.hd > 128 || D.rd > D.hd || D.rd % 2) return ALTXS_EINVAL;
     return ALTXS_OK;
 }
@@ -388,6 +390,21 @@ __global__ void t_softmax_bwd_pl(TD D, const uint16_t *ph, const uint16_t *pl, i
                     j <= t ? __fmul_rn(__fmul_rn(split_load(ph, pl, o + j), __fsub_rn(g[j], s)), scale) : 0.0f);
 }
 
+// context prefill: K (normed, roped) and V rows of position t, layer l into
+// slot t % ctx of one stream's ring [L][2][Hkv][ctx][3*hd] (24-bit rows)
+__global__ void t_kv_write(TD D, Tape tp, uint8_t *kv, int64_t ctx) {
+    const int t = blockIdx.x, l = blockIdx.y, hd = D.hd;
+    const int64_t rb = 3 * (int64_t)hd, slot = t % ctx;
+    const float *kr = tp.kr + ((int64_t)l * D.T + t) * D.kvd;
+    const float *v = tp.qkv + ((int64_t)l * D.T + t) * D.qn + D.d + D.kvd;
+    uint8_t *base = kv + (int64_t)l * 2 * D.Hkv * ctx * rb;
+    for (int e = threadIdx.x; e < D.kvd; e += blockDim.x) {
+        const int h = e / hd, c = e - h * hd;
+        store_kv_row(base + ((int64_t)h * ctx + slot) * rb, hd, c, kr[e]);
+        store_kv_row(base + ((int64_t)(D.Hkv + h) * ctx + slot) * rb, hd, c, v[e]);
+    }
+}
+
 // x = r + colscale * y (row stride d), optional copy into y2
 __global__ void t_resid(int64_t n, int d, const float *r, const float *col, const float *y, float *x, float *y2) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -537,6 +554,7 @@ struct Run {
     const altxs_split_planes *sp;
     uint16_t *tca, *tcb;
     int64_t tca_n, tcb_n;
+    bool no_lora;  // context prefill of a model without adapters
     cudaStream_t st;
 };
 
@@ -672,6 +690,7 @@ int lin_bwd(const Run &R, const altxs_qmat &Wq, const float *Wd, const uint16_t 
 // LoRA forward for one target: t = X A^T ; Y += s * t B^T
 int lora_fwd(const Run &R, const float *X, int din, const float *A, const float *B, int dout, float s, float *t,
              float *Y, int64_t ldy) {
+    if (R.no_lora) return ALTXS_OK;
     const int T = R.D.T, r = R.D.r;
     TRY(launch_gemm(G(R, X, din, 0, A, din, 1, t, r, T, r, din), R.st));
     TRY(launch_gemm(G(R, t, r, 0, B, r, 1, Y, ldy, T, dout, r, s, 1.0f), R.st));
@@ -693,7 +712,8 @@ int lora_bwd(const Run &R, const float *X, int din, const float *A, const float 
 // the weight planes of matrix field f (NULL on the CUDA-core path)
 #define PL(f) (R.sp ? R.sp->f : nullptr)
 
-int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out) {
+int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out,
+            bool head = true) {
     const TD &D = R.D;
     const Tape &tp = R.tp;
     const altxs_weights *w = R.w;
@@ -788,6 +808,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             TRY(launch_qmm(a, st));
         }
     }
+    if (!head) return ALTXS_OK;  // context prefill: the layers' K/V rows are all it needs
     ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp));
     TRY(lin_fwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.hf, d, tp.logits, D.V));
     if (mask & 16) TRY(lora_fwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V));
@@ -967,6 +988,49 @@ int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T) {
 int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t stream) {
     if (!m || !out) return ALTXS_EINVAL;
     return launch_dequant(*m, 0, m->rows, out, ld, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int64_t altxs_prefill_workspace_bytes(const altxs_model_desc *desc, int T) {
+    TD D{};
+    if (!desc || T < 1 || fill(*desc, T, D, true)) return -1;
+    const int64_t lo_total = D.r > 0 ? lora_offsets(*desc).total : 1;
+    int64_t a_n, b_n;
+    tc_scratch(D, &a_n, &b_n);
+    return carve(D, nullptr, nullptr) + align_up(lo_total * 4, 256) + kSplitkFloats * 4 + align_up(a_n * 2, 256) +
+           align_up(b_n * 2, 256);
+}
+
+int altxs_prefill(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
+                  const int32_t *tokens, int T, const float *lora, uint8_t *kv, void *workspace,
+                  int64_t workspace_bytes, altxs_stream_t stream) {
+    if (!desc || !w || !kv || T < 0) return ALTXS_EINVAL;
+    if (T == 0) return ALTXS_OK;
+    if (!tokens || !workspace) return ALTXS_EINVAL;
+    Run R{};
+    TRY(fill(*desc, T, R.D, true));
+    if (desc->ctx < 1 || w->rope_positions < T) return ALTXS_EINVAL;
+    if (R.D.r > 0 && !lora) return ALTXS_EINVAL;
+    if (dense && (!dense->emb || !dense->qkv || !dense->o || !dense->up || !dense->down)) return ALTXS_EINVAL;
+    if (workspace_bytes < altxs_prefill_workspace_bytes(desc, T)) return ALTXS_EINVAL;
+    R.desc = desc;
+    R.w = w;
+    R.dw = dense;
+    R.no_lora = R.D.r == 0 || !lora;
+    R.st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t tape_bytes = carve(R.D, workspace, &R.tp);
+    const LoraOff lo = lora_offsets(*desc);
+    R.splitk = reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + tape_bytes +
+                                         align_up((R.no_lora ? 1 : lo.total) * 4, 256));
+    R.splitk_floats = kSplitkFloats;
+    R.sp = w->split;
+    if (R.sp) {
+        tc_scratch(R.D, &R.tca_n, &R.tcb_n);
+        R.tca = reinterpret_cast<uint16_t *>(R.splitk + kSplitkFloats);
+        R.tcb = R.tca + align_up(R.tca_n, 128);
+    }
+    TRY(forward(R, tokens, nullptr, lora, nullptr, false));
+    ALTXS_LAUNCH(kKTtt, R.st, t_kv_write<<<dim3(T, R.D.L), 128, 0, R.st>>>(R.D, R.tp, kv, desc->ctx));
+    return ALTXS_OK;
 }
 
 int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,

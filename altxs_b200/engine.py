@@ -94,7 +94,7 @@ class DeviceModel:
         self.desc = _lib.ModelDesc(
             vocab=cfg.vocab_size, n_layers=L, d_model=cfg.model_dim, n_heads=cfg.num_heads,
             n_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, mlp_hidden=cfg.mlp_hidden,
-            ctx=cfg.ctx, rope_dims=cfg.rope_dims, skip_gates=int(cfg.skip_gates_enabled),
+            ctx=cfg.kv_len, rope_dims=cfg.rope_dims, skip_gates=int(cfg.skip_gates_enabled),
             lora_rank=cfg.ttt_lora_rank if cfg.lora_enabled else 0, lora_mask=lora_mask(cfg),
             cdf_mode=_lib.CDF_FIXED if cfg.cdf_mode == "fixed" else _lib.CDF_REF, cdf_bits=cfg.cdf_bits,
             logit_softcap=cfg.logit_softcap, lora_scale=cfg.lora_scale if cfg.lora_enabled else 0.0,
@@ -200,7 +200,8 @@ class StreamBatch:
         self.pos = torch.zeros(n, dtype=torch.int64, device=dev)
         self.active = torch.ones(n, dtype=torch.uint8, device=dev)
         # sliding-window ring, rows in the 24-bit split format (3 bytes/value)
-        self.kv = torch.zeros((n, L, 2, Hkv, cfg.ctx, 3 * hd), dtype=torch.uint8, device=dev)
+        self.kv = torch.zeros((n, L, 2, Hkv, cfg.kv_len, 3 * hd), dtype=torch.uint8, device=dev)
+        self.pos_base = torch.zeros(n, dtype=torch.int64, device=dev)  # absolute index of position 0
         self.ac = torch.zeros((n, 8), dtype=torch.int64, device=dev)
         self.bits = torch.zeros((n, self.words_per_stream), dtype=torch.int32, device=dev)
         self.sym = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -222,6 +223,7 @@ class StreamBatch:
             lora_stride=dm.lora_floats, ac=self.ac.data_ptr(), bits=self.bits.data_ptr(),
             words_per_stream=self.words_per_stream, sym=self.sym.data_ptr(),
             hist=self.hist.data_ptr() if self.hist is not None else None, hist_len=self.hist_len,
+            pos_base=self.pos_base.data_ptr(),
             logits_out=self.logits.data_ptr() if self.logits is not None else None,
             workspace=self.workspace.data_ptr(), workspace_bytes=wsb,
         )
@@ -404,6 +406,47 @@ class StreamResult:
     n_symbols: int
 
 
+class ContextReset:
+    """Segment-reset context (``context_mode="reset"``): at a boundary
+    ``start`` (after the update) each row's context becomes its last
+    ``n = min(block_size, start)`` symbols at positions 0..n-1 (reference
+    ``reset_segment`` with ``_chunk_ctx_start``, incremental.py:858-897,
+    compress.py:122-125).  ``altxs_prefill`` writes the K/V rows of the first
+    n-1 of them with the row's adapters; the row's pending token is already
+    the n-th, so the next step at position n-1 gives the segment's first
+    distribution.  ``pos_base`` keeps the symbol ring in absolute order."""
+
+    def __init__(self, dm: DeviceModel):
+        self.dm = dm
+        self.t_max = max(1, int(dm.cfg.block_size) - 1)
+        self.ws_bytes = int(_lib.lib().altxs_prefill_workspace_bytes(C.byref(dm.desc), self.t_max))
+        if self.ws_bytes < 0:
+            raise ValueError("model shape not supported by the prefill kernels")
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dm.device)
+        self.dense = None if dm.tensor_cores else dm.dense_weights()
+
+    def __call__(self, b: StreamBatch, rows, start: int) -> None:
+        if b.hist is None:
+            raise RuntimeError("the batch was built without a symbol ring")
+        n = min(int(self.dm.cfg.block_size), int(start))
+        if n < 1:
+            return
+        dev = self.dm.device
+        idx = torch.arange(start - n, start, device=dev) % b.hist_len
+        L = _lib.lib()
+        for r in rows:
+            ctx = b.hist[r].index_select(0, idx).contiguous()
+            lora = b.lora[r].data_ptr() if b.lora is not None else None
+            rc = L.altxs_prefill(
+                C.byref(self.dm.desc), C.byref(self.dm.weights_struct),
+                C.byref(self.dense) if self.dense is not None else None, ctx.data_ptr(), n - 1, lora,
+                b.kv[r].data_ptr(), self.ws.data_ptr(), self.ws_bytes, _stream_handle(dev))
+            _lib.check(rc, "altxs_prefill")
+        ri = torch.as_tensor(list(rows), dtype=torch.int64, device=dev)
+        b.pos.index_fill_(0, ri, n - 1)
+        b.pos_base.index_fill_(0, ri, int(start) - n)
+
+
 class Engine:
     """Encode / decode many independent streams in lockstep on one GPU."""
 
@@ -411,11 +454,12 @@ class Engine:
         self.dm = dm
         self.cfg = dm.cfg
         self.ttt = ttt  # optional callable(batch, rows, hist_end) for the boundary update
+        self.reset = ContextReset(dm) if dm.cfg.context_mode == "reset" else None
 
     def _new_batch(self, n: int, max_len: int) -> StreamBatch:
         cfg = self.cfg
         self.dm.ensure_rope(max_len + 2)
-        hist = cfg.ctx + 2 if self.ttt is not None else 0
+        hist = cfg.ctx + 2 if (self.ttt is not None or self.reset is not None) else 0
         return StreamBatch(self.dm, n, words_per_stream=words_for_segment(cfg.online_retrain_every, cfg.cdf_bits),
                            hist_len=hist)
 
@@ -464,6 +508,8 @@ class Engine:
         b.ac_init(rows)
         if self.ttt is not None:
             self.ttt(b, rows, t)
+        if self.reset is not None:
+            self.reset(b, rows, t)
 
     def decode(self, payloads: list[bytes], n_symbols: list[int]) -> list[np.ndarray]:
         cfg, dev = self.cfg, self.dm.device
@@ -488,6 +534,8 @@ class Engine:
                     b.set_active(None)
                     if self.ttt is not None:
                         self.ttt(b, rows, t)
+                    if self.reset is not None:
+                        self.reset(b, rows, t)
                     b.begin_decode({i: segs[i][t // every] for i in rows})
             active = lens > t
             if not active.all():

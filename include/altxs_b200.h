@@ -193,6 +193,9 @@ typedef struct altxs_batch {
     float *logits_out;      /* [n][V] final logits copy, or NULL */
     void *workspace;        /* >= altxs_workspace_bytes(desc, n) bytes, 256-aligned */
     int64_t workspace_bytes;
+    const int64_t *pos_base; /* [n] absolute index of position 0 for the hist ring, or NULL
+                                (= 0).  Segment-reset context (positions restart at every
+                                segment) keeps hist in absolute symbol order with it. */
 } altxs_batch;
 
 /* Allocation-free altxs_step for callers that cannot allocate device memory
@@ -204,7 +207,7 @@ typedef struct altxs_batch {
  * is a fixed 16 MiB array inside the library's device image (held on every
  * GPU that loads the library until exit; altxs_step_noalloc_max_bytes()).
  * Batches whose scratch would exceed it return ALTXS_ENOSPC (at the 33M
- * shapes, about 120 streams fit).  The first call on a device resolves the
+ * shapes, 133 streams fit).  The first call on a device resolves the
  * array's device address with that device current; make that first call
  * before any stream capture.  All calls share the array: calls that overlap
  * on one GPU race, so issue them one after another.  Nothing in the scratch
@@ -276,6 +279,19 @@ int altxs_gemm(int M, int N, int K, const float *A, int64_t lda, int64_t sA, int
 int64_t altxs_linear_workspace_bytes(int M, int K);
 int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo, int row0, int N, const float *X,
                  int M, float *Y, void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+
+/* Segment-reset context (the reference's reset_segment, altxs
+ * src/xsa_ttt/incremental.py:858-897, with _chunk_ctx_start, compress.py:122-125):
+ * after a boundary update the stream's context is rebuilt from its last
+ * block_size symbols at positions 0..  This writes the key and value rows of
+ * tokens[0..T) at positions 0..T-1 (slots 0..T-1) of one stream's ring
+ * kv ([L][2][Hkv][desc->ctx][3*hd]), computed with the stream's adapters;
+ * the caller then steps the context's last token at position T.  lora may be
+ * NULL when desc->lora_rank is 0. */
+int64_t altxs_prefill_workspace_bytes(const altxs_model_desc *desc, int T);
+int altxs_prefill(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
+                  const int32_t *tokens, int T, const float *lora, uint8_t *kv, void *workspace,
+                  int64_t workspace_bytes, altxs_stream_t stream);
 
 /* Workspace for one update over a T-token window (bytes). */
 int64_t altxs_ttt_workspace_bytes(const altxs_model_desc *desc, int T);

@@ -214,7 +214,7 @@ class OracleModel:
         cfg = self.cfg
         pos = st["pos"]
         x_pos = torch.tensor([pos])
-        keep = cfg.ctx - 1  # the current key makes the window ``ctx`` wide
+        keep = cfg.kv_len - 1  # the current key makes the window ``kv_len`` wide
         prefixes = []
         for kv in st["kv"]:
             if kv is None or keep == 0:
@@ -238,12 +238,24 @@ class OracleModel:
             raise ValueError("prefill starts from an empty stream")
         toks = torch.as_tensor(np.asarray(tokens, dtype=np.int64))
         T = toks.shape[0]
-        if T > self.cfg.ctx:
+        if T > self.cfg.kv_len:
             raise ValueError("prefill longer than the window is not a sliding-window pass")
         logits, new_kv = self._stack(toks, torch.arange(T), [None] * self.cfg.num_layers, lora, causal=True)
         st["kv"] = list(new_kv)
         st["pos"] = T
         return logits[-1]
+
+    def reset_segment(self, arr, start: int, lora: OracleLoRA | None = None):
+        """Segment-reset context (reference reset_segment + _chunk_ctx_start,
+        incremental.py:858-897, compress.py:122-125): a fresh stream holding
+        the first n-1 of the last n = min(block_size, start) symbols before
+        ``start`` at positions 0..n-2.  Stepping arr[start-1] next gives the
+        distribution of symbol ``start``.  Returns the stream."""
+        st = self.new_stream()
+        n = min(int(self.cfg.block_size), int(start))
+        if n > 1:
+            self.prefill(st, np.asarray(arr[start - n: start - 1]), lora)
+        return st
 
     # ---- teacher-forced window (training forward) --------------------------
     def window_logits(self, tokens: torch.Tensor, lora: OracleLoRA | None) -> torch.Tensor:
