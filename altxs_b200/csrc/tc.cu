@@ -276,6 +276,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Per 32-column block: lane = tile row on the way out of tensor
         // memory, lane = column on the way to global memory.
         float(*eb)[33] = ebuf[warp];
+        // 16-byte stores and loads need 4-float row strides and 16-byte (8 for planes) bases
+        auto al = [](const void *p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
+        const bool vec = ((g.ldc | g.ldr | g.ldy2 | g.ldp | g.sC) & 3) == 0 && al(g.C, 15) && al(g.R, 15) &&
+                         al(g.Y2, 15) && al(g.colscale, 15) && al(g.p_hi, 7) && al(g.p_lo, 7);
         int j = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
             const Tile T = tile_of(g, t, mt, ntl, nk, BN);
@@ -306,46 +310,117 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
                 __syncwarp();
-                // this lane's column of the block: all reads first (the residual
-                // input may be the output array itself), then the stores
-                float col[32];
+                // lane -> 4 consecutive columns (c4) of rows it*4 + sub: one
+                // 16-byte store per lane covers 4 rows x 32 columns per warp
+                // instruction.  All reads of a block come before its stores (the
+                // residual input may be the output array itself).
+                const int sub = lane >> 3, c4 = (lane & 7) * 4;
+                float4 vv[8];
 #pragma unroll
-                for (int rr = 0; rr < 32; ++rr) col[rr] = eb[rr][lane];
-                const int n = T.n0 + c0 + lane;
-                const int mb = T.m0 + warp * 32;
-                const int nr = g.M - mb < 32 ? g.M - mb : 32;
-                if (n >= g.N || nr <= 0) continue;
-                if (g.epi == kEpiResid) {
-                    const float cs = g.colscale[n];
-                    float rv[32];
-#pragma unroll
-                    for (int rr = 0; rr < 32; ++rr) rv[rr] = rr < nr ? g.R[(int64_t)(mb + rr) * g.ldr + n] : 0.0f;
-#pragma unroll
-                    for (int rr = 0; rr < 32; ++rr) col[rr] = __fadd_rn(rv[rr], __fmul_rn(cs, col[rr]));
-                } else {
-                    if (g.alpha != 1.0f) {
-#pragma unroll
-                        for (int rr = 0; rr < 32; ++rr) col[rr] = __fmul_rn(g.alpha, col[rr]);
-                    }
-                    if (g.beta != 0.0f) {
-                        float cv[32];
-#pragma unroll
-                        for (int rr = 0; rr < 32; ++rr) cv[rr] = rr < nr ? Cb[(int64_t)(mb + rr) * g.ldc + n] : 0.0f;
-#pragma unroll
-                        for (int rr = 0; rr < 32; ++rr) col[rr] = __fadd_rn(col[rr], __fmul_rn(g.beta, cv[rr]));
-                    }
-                    if (g.epi == kEpiLeaky2) {
-#pragma unroll
-                        for (int rr = 0; rr < 32; ++rr) col[rr] = leaky2(col[rr]);
-                    }
+                for (int it = 0; it < 8; ++it) {
+                    const float *e = eb[it * 4 + sub] + c4;
+                    vv[it] = make_float4(e[0], e[1], e[2], e[3]);
                 }
+                const int n = T.n0 + c0 + c4;
+                const int mb = T.m0 + warp * 32;
+                if (n >= g.N) continue;
+                if (vec && n + 3 < g.N) {
+                    if (g.epi == kEpiResid) {
+                        const float4 cs = *reinterpret_cast<const float4 *>(g.colscale + n);
+                        float4 rv[8];
 #pragma unroll
-                for (int rr = 0; rr < 32; ++rr) {
-                    if (rr >= nr) break;
-                    const int64_t m = mb + rr;
-                    if (Cb) Cb[m * g.ldc + n] = col[rr];
-                    if (g.Y2) g.Y2[m * g.ldy2 + n] = col[rr];
-                    if (g.p_hi) split_store(g.p_hi, g.p_lo, m * g.ldp + n, col[rr]);
+                        for (int it = 0; it < 8; ++it) {
+                            const int m = mb + it * 4 + sub;
+                            rv[it] = m < g.M ? *reinterpret_cast<const float4 *>(g.R + (int64_t)m * g.ldr + n)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int it = 0; it < 8; ++it) {
+                            vv[it].x = __fadd_rn(rv[it].x, __fmul_rn(cs.x, vv[it].x));
+                            vv[it].y = __fadd_rn(rv[it].y, __fmul_rn(cs.y, vv[it].y));
+                            vv[it].z = __fadd_rn(rv[it].z, __fmul_rn(cs.z, vv[it].z));
+                            vv[it].w = __fadd_rn(rv[it].w, __fmul_rn(cs.w, vv[it].w));
+                        }
+                    } else {
+                        if (g.alpha != 1.0f) {
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                vv[it].x = __fmul_rn(g.alpha, vv[it].x);
+                                vv[it].y = __fmul_rn(g.alpha, vv[it].y);
+                                vv[it].z = __fmul_rn(g.alpha, vv[it].z);
+                                vv[it].w = __fmul_rn(g.alpha, vv[it].w);
+                            }
+                        }
+                        if (g.beta != 0.0f) {
+                            float4 cv[8];
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                const int m = mb + it * 4 + sub;
+                                cv[it] = m < g.M ? *reinterpret_cast<const float4 *>(Cb + (int64_t)m * g.ldc + n)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                vv[it].x = __fadd_rn(vv[it].x, __fmul_rn(g.beta, cv[it].x));
+                                vv[it].y = __fadd_rn(vv[it].y, __fmul_rn(g.beta, cv[it].y));
+                                vv[it].z = __fadd_rn(vv[it].z, __fmul_rn(g.beta, cv[it].z));
+                                vv[it].w = __fadd_rn(vv[it].w, __fmul_rn(g.beta, cv[it].w));
+                            }
+                        }
+                        if (g.epi == kEpiLeaky2) {
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                vv[it].x = leaky2(vv[it].x);
+                                vv[it].y = leaky2(vv[it].y);
+                                vv[it].z = leaky2(vv[it].z);
+                                vv[it].w = leaky2(vv[it].w);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const int64_t m = mb + it * 4 + sub;
+                        if (m >= g.M) continue;
+                        if (Cb) *reinterpret_cast<float4 *>(Cb + m * g.ldc + n) = vv[it];
+                        if (g.Y2) *reinterpret_cast<float4 *>(g.Y2 + m * g.ldy2 + n) = vv[it];
+                        if (g.p_hi) {
+                            const float f[4] = {vv[it].x, vv[it].y, vv[it].z, vv[it].w};
+                            uint32_t h2[2], l2[2];
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * u]), h1 = __float2bfloat16_rn(f[2 * u + 1]);
+                                const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(f[2 * u], __bfloat162float(h0)));
+                                const __nv_bfloat16 l1 =
+                                    __float2bfloat16_rn(__fsub_rn(f[2 * u + 1], __bfloat162float(h1)));
+                                h2[u] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+                                l2[u] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+                            }
+                            *reinterpret_cast<uint2 *>(g.p_hi + m * g.ldp + n) = make_uint2(h2[0], h2[1]);
+                            *reinterpret_cast<uint2 *>(g.p_lo + m * g.ldp + n) = make_uint2(l2[0], l2[1]);
+                        }
+                    }
+                } else {
+                    // ragged or unaligned edge: element by element, same arithmetic
+                    for (int it = 0; it < 8; ++it) {
+                        const int64_t m = mb + it * 4 + sub;
+                        if (m >= g.M) continue;
+                        const float f4[4] = {vv[it].x, vv[it].y, vv[it].z, vv[it].w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (n + u >= g.N) break;
+                            float x = f4[u];
+                            if (g.epi == kEpiResid) {
+                                x = __fadd_rn(g.R[m * g.ldr + n + u], __fmul_rn(g.colscale[n + u], x));
+                            } else {
+                                if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
+                                if (g.beta != 0.0f) x = __fadd_rn(x, __fmul_rn(g.beta, Cb[m * g.ldc + n + u]));
+                                if (g.epi == kEpiLeaky2) x = leaky2(x);
+                            }
+                            if (Cb) Cb[m * g.ldc + n + u] = x;
+                            if (g.Y2) g.Y2[m * g.ldy2 + n + u] = x;
+                            if (g.p_hi) split_store(g.p_hi, g.p_lo, m * g.ldp + n + u, x);
+                        }
+                    }
                 }
             }
         }
