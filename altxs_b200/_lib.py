@@ -25,7 +25,7 @@ EXPORTS = (
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
     "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
-    "altxs_prefill_workspace_bytes",
+    "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -120,6 +120,8 @@ def lib():
             "altxs_launch_count": (i64, []),
             "altxs_profile": (C.c_int, [C.c_int]),
             "altxs_profile_mask": (C.c_int, [C.c_uint32]),
+            "altxs_set_wait_limit": (C.c_int, [C.c_uint32]),
+            "altxs_default_wait_limit": (C.c_uint32, []),
             "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
             "altxs_step_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int,
                                              vp]),

@@ -159,6 +159,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return false;
 }
 constexpr uint32_t kWaitLimit = 1u << 22;
+// Polls of the first wait of every pipeline stage (the data the kernel is
+// waiting for).  A wait that gives up records ALTXS_ST_TIMEOUT; the drain
+// waits that follow (the kernel's own copies and MMAs) keep kWaitLimit, so
+// nothing is left in flight when a CTA exits.  One copy per translation unit,
+// set for all of them by altxs_set_wait_limit (tests use 0: give up at once).
+static __device__ uint32_t g_wait_limit = kWaitLimit;
+__device__ __forceinline__ uint32_t wait_limit() { return *(volatile uint32_t *)&g_wait_limit; }
 
 // fp16 bits -> float
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }

@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int
         }
         const int nch = (it.nvalid + kRingChunk - 1) / kRingChunk;
         for (int cc = 0; cc < nch; ++cc) {
-            const bool ok = __all_sync(FULL, mbar_wait_bounded(&bar[slot], (par >> slot) & 1u, kWaitLimit));
+            const bool ok = __all_sync(FULL, mbar_wait_bounded(&bar[slot], (par >> slot) & 1u, wait_limit()));
             if (!ok) {  // a copy did not land in time: record it, let this warp's copies drain, leave
                 if (lane == 0) atomicOr(&c.b.ac[it.i].status, ALTXS_ST_TIMEOUT);
                 for (int s = 0; s < slots; ++s)
@@ -777,6 +777,13 @@ int fill_dims(const altxs_model_desc *dsc, int n, Dims &D) {
 }  // namespace
 
 extern "C" {
+
+int altxs_set_wait_limit(uint32_t limit) {
+    if (cudaMemcpyToSymbol(g_wait_limit, &limit, sizeof(limit)) != cudaSuccess) return ALTXS_ECUDA;
+    return altxs::set_wait_limit_tc(limit);
+}
+
+uint32_t altxs_default_wait_limit(void) { return altxs::kWaitLimit; }
 
 int64_t altxs_workspace_bytes(const altxs_model_desc *desc, int n_streams) {
     Dims D{};

@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int ab = op_batch(g.a, T.b), bb = op_batch(g.b, T.b);
                 for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
                     const int s = q % S, r = q / S;
-                    if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, kWaitLimit)) {
+                    if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, wait_limit())) {
                         abort_sh = 1;
                         break;
                     }
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (T.skip) continue;
                 const int buf = j & 1, use = j >> 1;
                 ++j;
-                if (use > 0 && !mbar_wait_bounded(&tempty[buf], (use - 1) & 1, kWaitLimit)) {
+                if (use > 0 && !mbar_wait_bounded(&tempty[buf], (use - 1) & 1, wait_limit())) {
                     ok = false;
                     break;
                 }
@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t acc = tmem + buf * Cfg::kTmemCols;
                 for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
                     const int s = q % S, r = q / S;
-                    if (!mbar_wait_bounded(&full[s], r & 1, kWaitLimit)) {
+                    if (!mbar_wait_bounded(&full[s], r & 1, wait_limit())) {
                         ok = false;
                         break;
                     }
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int buf = j & 1, use = j >> 1;
             ++j;
             const bool gave_up = __any_sync(kFull, abort_sh != 0);  // warp-uniform
-            const bool ok = !gave_up && __all_sync(kFull, mbar_wait_bounded(&tfull[buf], use & 1, kWaitLimit));
+            const bool ok = !gave_up && __all_sync(kFull, mbar_wait_bounded(&tfull[buf], use & 1, wait_limit()));
             if (!ok) {
                 const int row = T.m0 + warp * 32 + lane;
                 if (g.status && row < g.M) atomicOr(g.status + (int64_t)row * g.status_stride, ALTXS_ST_TIMEOUT);
@@ -597,6 +597,10 @@ int launch_tc(const TcArgs &a, cudaStream_t st) {
     g.status = a.status;
     g.status_stride = a.status_stride;
     return launch_tc_gemm(g, st);
+}
+
+int set_wait_limit_tc(uint32_t limit) {
+    return cudaMemcpyToSymbol(g_wait_limit, &limit, sizeof(limit)) == cudaSuccess ? ALTXS_OK : ALTXS_ECUDA;
 }
 
 int launch_split_weights(const altxs_qmat &W, uint16_t *hi, uint16_t *lo, cudaStream_t st) {

@@ -102,6 +102,9 @@ void tc_f32_scratch(const GemmArgs &g, int64_t *a_elems, int64_t *b_elems);
 int tc_gemm_f32(const GemmArgs &g, uint16_t *a_scr, int64_t a_elems, uint16_t *b_scr, int64_t b_elems,
                 cudaStream_t stream, int kernel_class);
 
+// The first-wait poll limit of this translation unit's kernels (altxs_set_wait_limit).
+int set_wait_limit_tc(uint32_t limit);
+
 // Expand rows [0, rows) of a mixed-bit matrix into hi/lo bf16 planes [rows][cols].
 int launch_split_weights(const altxs_qmat &W, uint16_t *hi, uint16_t *lo, cudaStream_t stream);
 

@@ -310,6 +310,19 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
                      float *adam_v, int step, float *loss_out, void *workspace, int64_t workspace_bytes,
                      altxs_stream_t stream);
 
+/* ---- failure detection ------------------------------------------------------
+ * No counterpart in the reference (its device waits do not exist; its coder
+ * drops bits silently).  Every device wait of this library is bounded: the
+ * first wait of a pipeline stage polls at most `limit` times
+ * (altxs_default_wait_limit() unless changed), then the kernel records
+ * ALTXS_ST_TIMEOUT in the affected streams' status words, lets its own
+ * copies and tensor-core operations finish (with the default bound) and
+ * returns.  Setting the limit to 0 makes every such wait give up at once:
+ * tests use it to exercise the timeout path on a real step without faulting
+ * or hanging the GPU.  Applies to later launches on the current device. */
+int altxs_set_wait_limit(uint32_t limit);
+uint32_t altxs_default_wait_limit(void);
+
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these
  * give the benchmark per-kernel device time measured live on the launch
