@@ -293,6 +293,7 @@ def default_small(cfg: ModelConfig) -> dict[str, np.ndarray]:
     L, d, H, S = cfg.num_layers, cfg.model_dim, cfg.num_heads, cfg.num_skip_weights
     rm = np.zeros((L, 2, d), dtype=np.float32)
     rm[:, 0, :] = 1.0
+    gw = cfg.gate_window
     return {
         "q_gain": np.full((L, H), cfg.qk_gain_init, dtype=np.float32),
         "attn_scale": np.ones((L, d), dtype=np.float32),
@@ -300,6 +301,13 @@ def default_small(cfg: ModelConfig) -> dict[str, np.ndarray]:
         "resid_mix": rm,
         "skip_weights": np.ones((S, d), dtype=np.float32),
         "skip_gates": np.zeros((S, d), dtype=np.float32),
+        # motifs (model.py:994-996, 1087-1105, 753-758): zero-initialised gates, unit lambdas
+        "smear_gate": np.zeros((gw,), dtype=np.float32),
+        "smear_lambda": np.zeros((1,), dtype=np.float32),
+        "attn_gate_w": np.zeros((L, H, gw), dtype=np.float32),
+        "softcap": np.array([cfg.logit_softcap, cfg.logit_softcap], dtype=np.float32),  # positive, negative
+        "parallel_post": np.ones((L, 2, 2), dtype=np.float32),
+        "parallel_resid": np.full((L, 2), 1.1, dtype=np.float32),
     }
 
 
@@ -344,6 +352,16 @@ def dense_weights(cfg: ModelConfig, tensors: dict[str, Any]) -> ModelWeights:
         small["mlp_scale"][i] = t(f"blocks.{i}.mlp_scale")
         small["resid_mix"][i] = t(f"blocks.{i}.resid_mix")
         small["q_gain"][i] = t(f"blocks.{i}.attn.q_gain")
+        if cfg.sparse_attn_gate_enabled:
+            small["attn_gate_w"][i] = t(f"blocks.{i}.attn.attn_gate_w")
+    if cfg.smear_gate_enabled:
+        small["smear_gate"] = t("smear_gate.weight").reshape(-1)
+        small["smear_lambda"] = t("smear_lambda").reshape(1)
+    if cfg.asym_logit_rescale:
+        small["softcap"] = np.array([float(t("softcap_pos")), float(t("softcap_neg"))], dtype=np.float32)
+    if "parallel_post_lambdas" in tensors:
+        small["parallel_post"] = t("parallel_post_lambdas")
+        small["parallel_resid"] = t("parallel_resid_lambdas")
     gm = GroupMatrix.from_dense
     return ModelWeights(
         cfg,

@@ -62,6 +62,20 @@ class ModelConfig:
     ttt_mlp_lora: bool = False
     ttt_use_rslora: bool = False
     grad_clip: float = 1.0
+    # reference model motifs (model.py:982-1110; all off = the plain GPT).  The
+    # step and the oracle run them with frozen weights; the test-time LoRA
+    # update covers the plain GPT only.
+    smear_gate_enabled: bool = False      # previous-token smear on the raw embedding
+    gate_window: int = 12                 # input width of the smear / attention gates
+    xsa_last_n: int = 0                   # XSA (value-direction removal) on the last n layers
+    sparse_attn_gate_enabled: bool = False  # per-head sigmoid gate on the attention output
+    sparse_attn_gate_scale: float = 0.5
+    asym_logit_rescale: bool = False      # learned positive / negative softcaps
+    num_loops: int = 0                    # depth recurrence over layers loop_start..loop_end
+    loop_start: int = 3
+    loop_end: int = 5
+    parallel_start_layer: int = 0         # parallel attention / MLP lanes from this layer (0 = off)
+    parallel_final_lane: str = "mean"     # "mean" | "attn" | "mlp"
     # framework CDF rule: "fixed" (integer fixed-point softmax, total
     # <= 2^cdf_bits) or "ref" (reference max(1, floor(p*1e6+0.5)) masses)
     cdf_mode: str = "fixed"
@@ -81,12 +95,35 @@ class ModelConfig:
         return int(self.mlp_mult * self.model_dim)
 
     @property
+    def layer_schedule(self) -> tuple[list[int], list[int]]:
+        """Physical layer of every encoder and decoder application (model.py:1065-1077):
+        with depth loops the segment loop_start..loop_end runs num_loops+1 times."""
+        L = self.num_layers
+        if self.num_loops > 0:
+            seg = list(range(self.loop_start, self.loop_end + 1))
+            order = list(range(self.loop_start)) + seg * (self.num_loops + 1) + list(range(self.loop_end + 1, L))
+            n_enc = len(order) // 2
+            return order[:n_enc], order[n_enc:]
+        return list(range(L // 2)), list(range(L // 2, L))
+
+    @property
+    def num_virtual_layers(self) -> int:
+        enc, dec = self.layer_schedule
+        return len(enc) + len(dec)
+
+    @property
     def num_encoder_layers(self) -> int:
-        return self.num_layers // 2
+        return len(self.layer_schedule[0])
 
     @property
     def num_skip_weights(self) -> int:
-        return min(self.num_encoder_layers, self.num_layers - self.num_encoder_layers)
+        enc, dec = self.layer_schedule
+        return min(len(enc), len(dec))
+
+    @property
+    def motifs(self) -> bool:
+        return bool(self.smear_gate_enabled or self.xsa_last_n > 0 or self.sparse_attn_gate_enabled
+                    or self.asym_logit_rescale or self.num_loops > 0 or self.parallel_start_layer > 0)
 
     @property
     def ctx(self) -> int:
@@ -134,6 +171,14 @@ class ModelConfig:
             raise ValueError("retrain_mode must be 'lora' or 'none'")
         if self.context_mode not in ("sliding", "reset"):
             raise ValueError("context_mode must be 'sliding' or 'reset'")
+        if self.parallel_final_lane not in ("mean", "attn", "mlp"):
+            raise ValueError("parallel_final_lane must be 'mean', 'attn' or 'mlp'")
+        if self.num_loops > 0 and not (0 <= self.loop_start <= self.loop_end < self.num_layers):
+            raise ValueError("loop_start..loop_end must be layers of the model")
+        if (self.smear_gate_enabled or self.sparse_attn_gate_enabled) and not 0 < self.gate_window <= self.model_dim:
+            raise ValueError("gate_window must be in 1..model_dim")
+        if self.motifs and self.lora_enabled:
+            raise ValueError("the test-time LoRA update covers the plain GPT; use retrain_mode='none' with motifs")
 
     def to_dict(self) -> dict[str, Any]:
         return dataclasses.asdict(self)
@@ -155,14 +200,8 @@ class ModelConfig:
             lambda k, dflt=None: getattr(ref, k, dflt)
         )
         unsupported = {
-            "xsa_last_n": get("xsa_last_n", 0) > 0,
-            "smear_gate_enabled": bool(get("smear_gate_enabled", False)),
-            "sparse_attn_gate_enabled": bool(get("sparse_attn_gate_enabled", False)),
             "attn_out_gate_enabled": bool(get("attn_out_gate_enabled", False)),
             "gated_attn_enabled": bool(get("gated_attn_enabled", False)),
-            "num_loops": get("num_loops", 0) > 0,
-            "parallel_start_layer": get("parallel_start_layer", 0) > 0,
-            "asym_logit_rescale": bool(get("asym_logit_rescale", False)),
             "rope_yarn": bool(get("rope_yarn", False)),
             "tie_embeddings": not bool(get("tie_embeddings", True)),
         }

@@ -21,6 +21,11 @@ Restated from the altxs reference (paths inside that project):
   * LoRA A init order and seed              src/xsa_ttt/ttt_lora.py:67-105,
                                             src/xsa_ttt/compress.py:1965-1974
   * training window (last block_size)       src/xsa_ttt/compress.py:301-320
+  * motifs: smear gate                       src/xsa_ttt/model.py:1350-1362
+            XSA, sparse attention gate       src/xsa_ttt/model.py:760-768, 845-862
+            depth-loop layer schedule        src/xsa_ttt/model.py:1064-1077, 1377-1436
+            parallel lanes                   src/xsa_ttt/model.py:1293-1348, 1404-1443
+            asymmetric softcap               src/xsa_ttt/model.py:1478-1500
 
 Context semantics.  The reference re-prefills a context at each segment
 boundary; this engine instead keeps a sliding window of the last
@@ -146,6 +151,7 @@ class OracleModel:
         q = _rope(q, cos, sin, rd)
         k = _rope(k, cos, sin, rd)
         q = q * w.small["q_gain"][i][None, :, None]
+        v_new = v
         if kv_prefix is not None:
             pk, pv = kv_prefix
             k_all = torch.cat([pk, k], 0)
@@ -159,6 +165,15 @@ class OracleModel:
             q.transpose(0, 1)[None], ke.transpose(0, 1)[None], ve.transpose(0, 1)[None],
             is_causal=causal,
         )[0].transpose(0, 1)
+        if cfg.xsa_last_n > 0 and i >= cfg.num_layers - cfg.xsa_last_n:
+            # remove each head's component along its own token's value direction
+            vn = F.normalize(v_new, dim=-1)[:, :, None, :]  # [T, Hkv, 1, D]
+            yg = y.reshape(T, Hkv, rep, D)
+            y = (yg - (yg * vn).sum(-1, keepdim=True) * vn).reshape(T, H, D)
+        if cfg.sparse_attn_gate_enabled:
+            gw = cfg.gate_window
+            g = torch.sigmoid(cfg.sparse_attn_gate_scale * (n[:, :gw] @ w.small["attn_gate_w"][i].T))  # [T, H]
+            y = y * g[:, :, None]
         y = y.reshape(T, H * D)
         out = y @ w.o[i].T
         if lora is not None and f"o{i}" in lora.A:
@@ -177,36 +192,77 @@ class OracleModel:
         x_out = x_out + sm["mlp_scale"][i][None, :] * (h @ self.w.down[i].T)
         return x_out, kv_new
 
-    def _stack(self, tokens, x_pos, kv_prefixes, lora, causal):
+    def _parallel_block(self, i, lane0, lane1, x0, x_pos, kv_prefix, causal):
         cfg, sm = self.cfg, self.w.small
-        x = _rms(self.w.emb[tokens])
+        ln = 1.0 / math.sqrt(i + 1) if cfg.ln_scale else 1.0
+        mix = sm["resid_mix"][i]
+        n = _rms(mix[0][None, :] * lane0 + mix[1][None, :] * x0) * ln
+        attn_out, kv_new = self._attn(i, n, x_pos, kv_prefix, None, causal)
+        attn_out = sm["attn_scale"][i][None, :] * attn_out
+        h = F.leaky_relu(_rms(lane1) * ln @ self.w.up[i].T, negative_slope=0.5).square()
+        mlp_out = sm["mlp_scale"][i][None, :] * (h @ self.w.down[i].T)
+        pr, pp = sm["parallel_resid"][i], sm["parallel_post"][i]
+        lane0 = pr[0] * lane0 + pp[0][0] * attn_out + pp[1][0] * mlp_out
+        lane1 = pr[1] * lane1 + pp[0][1] * attn_out + pp[1][1] * mlp_out
+        return lane0, lane1, kv_new
+
+    def _embed(self, tokens, prev_tok):
+        cfg, sm = self.cfg, self.w.small
+        raw = self.w.emb[tokens]
+        if not cfg.smear_gate_enabled:
+            return raw
+        prev = torch.cat([self.w.emb[[prev_tok]] if prev_tok is not None else torch.zeros_like(raw[:1]), raw[:-1]])
+        g = sm["smear_lambda"][0] * torch.sigmoid(raw[:, : cfg.gate_window] @ sm["smear_gate"])
+        return raw + g[:, None] * prev
+
+    def _stack(self, tokens, x_pos, kv_prefixes, lora, causal, prev_tok=None):
+        cfg, sm = self.cfg, self.w.small
+        x = _rms(self._embed(tokens, prev_tok))
         x0 = x
-        L, enc = cfg.num_layers, cfg.num_encoder_layers
+        enc, dec = cfg.layer_schedule
         skips, new_kv = [], []
-        for i in range(enc):
-            x, kv = self._block(i, x, x0, x_pos, kv_prefixes[i], lora, causal)
+        for i in enc:
+            x, kv = self._block(i, x, x0, x_pos, kv_prefixes[len(new_kv)], lora, causal)
             new_kv.append(kv)
             skips.append(x)
-        for skip_idx, i in enumerate(range(enc, L)):
+        psl = cfg.parallel_start_layer
+        lane0 = lane1 = None
+
+        def skip_into(dest, skip_idx):
             if skip_idx < cfg.num_skip_weights and skips:
                 scaled = sm["skip_weights"][skip_idx][None, :] * skips.pop()
                 if cfg.skip_gates_enabled:
-                    g = torch.sigmoid(sm["skip_gates"][skip_idx])[None, :]
-                    x = torch.lerp(scaled, x, g)
-                else:
-                    x = x + scaled
-            x, kv = self._block(i, x, x0, x_pos, kv_prefixes[i], lora, causal)
+                    return torch.lerp(scaled, dest, torch.sigmoid(sm["skip_gates"][skip_idx])[None, :])
+                return dest + scaled
+            return dest
+
+        for skip_idx, i in enumerate(dec):
+            if psl > 0 and i >= psl:
+                if lane0 is None:
+                    lane0 = lane1 = x
+                lane0 = skip_into(lane0, skip_idx)
+                lane0, lane1, kv = self._parallel_block(i, lane0, lane1, x0, x_pos,
+                                                        kv_prefixes[len(new_kv)], causal)
+            else:
+                x = skip_into(x, skip_idx)
+                x, kv = self._block(i, x, x0, x_pos, kv_prefixes[len(new_kv)], lora, causal)
             new_kv.append(kv)
+        if lane0 is not None:
+            fl = cfg.parallel_final_lane
+            x = lane1 if fl == "mlp" else lane0 if fl == "attn" else 0.5 * (lane0 + lane1)
         h = _rms(x)
         logits = h @ self.w.emb.T
         if lora is not None:
             logits = logits + lora.delta("lm", h, cfg.lora_scale)
+        if cfg.asym_logit_rescale:
+            sp, sn = sm["softcap"][0], sm["softcap"][1]
+            return torch.where(logits >= 0, sp * torch.tanh(logits / sp), sn * torch.tanh(logits / sn)), new_kv
         c = cfg.logit_softcap
         return c * torch.tanh(logits / c), new_kv
 
     # ---- sliding-window decode ----------------------------------------------
     def new_stream(self):
-        return {"pos": 0, "kv": [None] * self.cfg.num_layers}
+        return {"pos": 0, "kv": [None] * self.cfg.num_virtual_layers, "prev": None}
 
     @torch.no_grad()
     def step(self, st, tok: int, lora: OracleLoRA | None = None) -> torch.Tensor:
@@ -221,7 +277,9 @@ class OracleModel:
                 prefixes.append(None)
             else:
                 prefixes.append((kv[0][-keep:], kv[1][-keep:]))
-        logits, new_kv = self._stack(torch.tensor([tok]), x_pos, prefixes, lora, causal=False)
+        logits, new_kv = self._stack(torch.tensor([tok]), x_pos, prefixes, lora, causal=False,
+                                     prev_tok=st.get("prev"))
+        st["prev"] = int(tok)
         for i, (k, v) in enumerate(new_kv):
             if prefixes[i] is None:
                 st["kv"][i] = (k, v)
@@ -240,9 +298,11 @@ class OracleModel:
         T = toks.shape[0]
         if T > self.cfg.kv_len:
             raise ValueError("prefill longer than the window is not a sliding-window pass")
-        logits, new_kv = self._stack(toks, torch.arange(T), [None] * self.cfg.num_layers, lora, causal=True)
+        logits, new_kv = self._stack(toks, torch.arange(T), [None] * self.cfg.num_virtual_layers, lora,
+                                     causal=True)
         st["kv"] = list(new_kv)
         st["pos"] = T
+        st["prev"] = int(toks[-1])
         return logits[-1]
 
     def reset_segment(self, arr, start: int, lora: OracleLoRA | None = None):
@@ -260,7 +320,7 @@ class OracleModel:
     # ---- teacher-forced window (training forward) --------------------------
     def window_logits(self, tokens: torch.Tensor, lora: OracleLoRA | None) -> torch.Tensor:
         T = tokens.shape[0]
-        logits, _ = self._stack(tokens, torch.arange(T), [None] * self.cfg.num_layers, lora, causal=True)
+        logits, _ = self._stack(tokens, torch.arange(T), [None] * self.cfg.num_virtual_layers, lora, causal=True)
         return logits
 
 

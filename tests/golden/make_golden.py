@@ -258,6 +258,68 @@ def gen_lora() -> None:
     np.savez_compressed(HERE / "lora_small.npz", **out)
 
 
+MOTIFS = dict(
+    vocab_size=256, num_layers=6, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0,
+    rope_dims=16, block_size=64, online_retrain_every=128, seed=3, retrain_mode="none",
+    smear_gate_enabled=True, xsa_last_n=3, sparse_attn_gate_enabled=True, asym_logit_rescale=True,
+    num_loops=1, loop_start=1, loop_end=2, parallel_start_layer=4, parallel_final_lane="mean",
+)
+
+
+def gen_model_motifs() -> None:
+    """The reference GPT with its motifs on (smear gate, XSA on the last 3
+    layers, sparse attention gate, asymmetric softcap, one depth loop over
+    layers 1-2, parallel lanes from layer 4), random weights rounded to fp16
+    (stored as fp16, loaded exactly), full-forward logits of one sequence."""
+    h = XsaTttConfig(seed=MOTIFS["seed"])
+    for k, v in MOTIFS.items():
+        setattr(h, k, v)
+    h.rope_base = 1e4
+    h.qk_gain_init = 5.0
+    h.logit_softcap = 30.0
+    h.ln_scale = True
+    h.skip_gates_enabled = True
+    h.attn_out_gate_enabled = False
+    h.gated_attn_enabled = False
+    h.rope_yarn = False
+    h.tie_embeddings = True
+    h.gradient_checkpointing = False
+    torch.manual_seed(0)
+    m = GPT(h)
+    m.enable_looping(True)
+    g = torch.Generator().manual_seed(11)
+    sd = m.state_dict()
+    for k, v in sd.items():
+        if v.dtype != torch.float32:
+            continue
+        if v.ndim >= 2 and v.numel() > 64:  # weight banks / embedding: fresh random
+            v = torch.randn(v.shape, generator=g) * (0.5 / v.shape[-1] ** 0.5 if "emb" not in k else 0.3)
+        elif k in ("smear_lambda",):
+            v = torch.full_like(v, 0.7)
+        elif k.startswith("smear_gate") or k.endswith("attn_gate_w"):
+            v = torch.randn(v.shape, generator=g) * 0.5
+        elif k.startswith("parallel_"):
+            v = v + 0.1 * torch.randn(v.shape, generator=g)
+        elif k == "softcap_pos":
+            v = torch.tensor(25.0)
+        elif k == "softcap_neg":
+            v = torch.tensor(35.0)
+        elif "skip_gates" in k or "resid_mix" in k or k.endswith("q_gain") or "scale" in k:
+            v = v + 0.05 * torch.randn(v.shape, generator=g)
+        sd[k] = v.half().float()
+    m.load_state_dict(sd, strict=True)
+    m.eval()
+    rng = np.random.default_rng(8)
+    T = 48
+    toks = rng.integers(0, h.vocab_size, size=T).astype(np.int64)
+    with torch.no_grad():
+        logits = m.forward_logits(torch.tensor(toks)[None])[0].float().numpy()
+    out = {"tokens": toks.astype(np.int32), "logits": logits.astype(np.float32),
+           "config": np.frombuffer(json.dumps(MOTIFS).encode(), dtype=np.uint8)}
+    out.update({f"w/{k}": v.half().numpy() for k, v in sd.items()})
+    np.savez_compressed(HERE / "model_motifs.npz", **out)
+
+
 def gen_zipf() -> None:
     from altxs_b200.synth import zipf_markov
 
@@ -271,6 +333,7 @@ if __name__ == "__main__":
     print(gen_codec())
     gen_model()
     gen_lora()
+    gen_model_motifs()
     gen_zipf()
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
         print(f.name, f.stat().st_size)

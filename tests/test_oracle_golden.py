@@ -146,3 +146,34 @@ def test_oracle_coder_roundtrip_edge(vocab):
     # empty input: flush only
     cum0 = np.zeros((0, vocab + 1), dtype=np.uint64)
     assert len(oc.encode_cum(cum0, np.zeros(0, np.int32))) == 1
+
+
+def _motif_model(g):
+    import json
+
+    from altxs_b200 import codec as C
+    from altxs_b200.config import ModelConfig
+
+    cfg = ModelConfig(**json.loads(bytes(g["config"])))
+    tensors = {k[2:]: g[k].astype(np.float32) for k in g.files if k.startswith("w/")}
+    return cfg, C.dense_weights(cfg, tensors)
+
+
+def test_oracle_motifs_match_reference(golden):
+    """Step-by-step oracle logits of the reference GPT with every supported
+    motif on (smear, XSA, sparse gate, asymmetric softcap, depth loop,
+    parallel lanes) against the reference's own full forward."""
+    from oracle.model import OracleModel, OracleWeights
+
+    g = golden("model_motifs.npz")
+    cfg, w = _motif_model(g)
+    assert cfg.num_virtual_layers == 8 and cfg.motifs
+    om = OracleModel(OracleWeights.from_model_weights(w))
+    st = om.new_stream()
+    got = np.stack([om.step(st, int(t)).numpy() for t in g["tokens"]])
+    err = float(np.abs(got - g["logits"]).max())
+    assert err < 1e-4, err
+    # one causal pass gives the same last row
+    st2 = om.new_stream()
+    last = om.prefill(st2, g["tokens"]).numpy()
+    assert float(np.abs(last - g["logits"][-1]).max()) < 1e-4
