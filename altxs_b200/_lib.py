@@ -53,6 +53,10 @@ class ModelDesc(C.Structure):
         ("ctx", C.c_int32), ("rope_dims", C.c_int32), ("skip_gates", C.c_int32),
         ("lora_rank", C.c_int32), ("lora_mask", C.c_int32), ("cdf_mode", C.c_int32),
         ("cdf_bits", C.c_int32), ("logit_softcap", C.c_float), ("lora_scale", C.c_float),
+        ("n_virtual", C.c_int32), ("n_encoder", C.c_int32), ("schedule", C.c_void_p),
+        ("smear_gate", C.c_int32), ("gate_window", C.c_int32), ("xsa_last_n", C.c_int32),
+        ("sparse_gate", C.c_int32), ("sparse_gate_scale", C.c_float), ("asym_softcap", C.c_int32),
+        ("parallel_start", C.c_int32), ("parallel_final", C.c_int32),
     ]
 
 
@@ -67,6 +71,8 @@ class Weights(C.Structure):
         ("resid_mix", C.c_void_p), ("ln_scale", C.c_void_p), ("skip_weights", C.c_void_p),
         ("skip_gates", C.c_void_p), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
         ("rope_positions", C.c_int64), ("split", C.POINTER(SplitPlanes)),
+        ("smear_gate", C.c_void_p), ("smear_lambda", C.c_void_p), ("attn_gate_w", C.c_void_p),
+        ("softcap", C.c_void_p), ("parallel_post", C.c_void_p), ("parallel_resid", C.c_void_p),
     ]
 
 
@@ -87,6 +93,7 @@ class Batch(C.Structure):
         ("bits", C.c_void_p), ("words_per_stream", C.c_int64), ("sym", C.c_void_p),
         ("hist", C.c_void_p), ("hist_len", C.c_int32), ("logits_out", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64), ("pos_base", C.c_void_p),
+        ("prev_tok", C.c_void_p),
     ]
 
 

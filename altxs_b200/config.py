@@ -177,8 +177,12 @@ class ModelConfig:
             raise ValueError("loop_start..loop_end must be layers of the model")
         if (self.smear_gate_enabled or self.sparse_attn_gate_enabled) and not 0 < self.gate_window <= self.model_dim:
             raise ValueError("gate_window must be in 1..model_dim")
+        if self.sparse_attn_gate_enabled and self.gate_window > self.head_dim:
+            raise ValueError("the sparse attention gate needs gate_window <= head_dim")
         if self.motifs and self.lora_enabled:
             raise ValueError("the test-time LoRA update covers the plain GPT; use retrain_mode='none' with motifs")
+        if self.motifs and self.context_mode == "reset":
+            raise ValueError("the segment-reset prefill covers the plain GPT; use context_mode='sliding' with motifs")
 
     def to_dict(self) -> dict[str, Any]:
         return dataclasses.asdict(self)

@@ -30,7 +30,21 @@ constexpr int kCdfThreads = 512;
 struct Dims {
     int n, V, L, d, H, Hkv, hd, F, ctx, rd, r, nsplit, enc, nskip, qkv_n, kvd;
     int64_t lora_stride;
+    int Lv;        // layer applications (KV sets): L, or more with depth loops
+    int xsa_from;  // physical layers >= xsa_from run XSA (L = none)
+    int par;       // some decoder applications run the two parallel lanes
+    int gw;        // gate window of the smear and sparse attention gates
 };
+
+// Per-application layout: which physical layer's weights run, at which KV set.
+struct LayerApp {
+    int p;     // physical layer
+    int v;     // application index (KV set, skip slots)
+    int mode;  // kAppPlain, kAppPar, kAppParFirst
+};
+constexpr int kAppPlain = 0;     // one residual stream
+constexpr int kAppPar = 1;       // two lanes: attention reads lane 0, the MLP lane 1
+constexpr int kAppParFirst = 2;  // first two-lane application: lane 1 starts as a copy of x
 
 struct StepCtx {
     altxs_model_desc dsc;
@@ -40,6 +54,7 @@ struct StepCtx {
     LoraOff lo;
     // workspace
     float *x, *x0, *nrm, *nrm2, *skip, *qkv, *q, *part, *y, *ao, *hid, *logits, *lt;
+    float *lane1, *mo;  // parallel lanes: the MLP lane and the MLP output
     // tensor-core path: hi/lo bf16 planes of the linear layers' inputs
     int tc;
     uint16_t *nrm_h, *nrm_l, *y_h, *y_l, *nrm2_h, *nrm2_l, *hid_h, *hid_l;
@@ -49,8 +64,11 @@ __device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return
 
 // ---------------------------------------------------------------------------
 
+// Embedding row, the smear gate when on (model.py:1350-1362: raw +=
+// lambda * sigmoid(g . raw[:gate_window]) * raw of the previous token), RMSNorm.
 __global__ void k_embed(StepCtx c) {
     __shared__ float red[32];
+    __shared__ float gate;
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, tok = c.b.tok[i];
@@ -59,9 +77,22 @@ __global__ void k_embed(StepCtx c) {
         for (int k = threadIdx.x; k < d; k += blockDim.x) x[k] = x0[k] = 0.0f;
         return;
     }
+    int prev = -1;
+    if (c.dsc.smear_gate) {
+        prev = c.b.prev_tok[i];
+        if (threadIdx.x < 32) {
+            float g = 0.0f;
+            for (int k = threadIdx.x; k < c.D.gw; k += 32) g = __fmaf_rn(qmat_elem(c.w.emb, tok, k), c.w.smear_gate[k], g);
+            g = warp_sum(g);
+            if (threadIdx.x == 0) gate = __fmul_rn(c.w.smear_lambda[0], sigmoidf_(g));
+        }
+        __syncthreads();
+    }
+    const bool smear = prev >= 0 && prev < c.D.V;
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
-        const float v = qmat_elem(c.w.emb, tok, k);
+        float v = qmat_elem(c.w.emb, tok, k);
+        if (smear) v = __fadd_rn(v, __fmul_rn(gate, qmat_elem(c.w.emb, prev, k)));
         x[k] = v;
         ss = __fmaf_rn(v, v, ss);
     }
@@ -74,38 +105,53 @@ __global__ void k_embed(StepCtx c) {
     }
 }
 
-// skip lerp (decoder layers) + resid_mix + rms * ln  -> x (= x_in), nrm
-__global__ void k_prenorm(StepCtx c, int l) {
+// Skip lerp (decoder applications) + resid_mix + rms * ln -> x (= x_in), nrm.
+// Two-lane applications (model.py:1293-1348) keep x as lane 0 after the skip
+// (the lanes' residuals start from it, not from x_in) and also norm lane 1
+// into nrm2 for the MLP, which reads lane 1 instead of the attention output.
+__global__ void k_prenorm(StepCtx c, LayerApp a) {
     __shared__ float red[32];
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
-    const int d = c.D.d, n = c.D.n;
+    const int d = c.D.d, n = c.D.n, l = a.p;
     float *x = c.x + (int64_t)i * d;
     const float *x0 = c.x0 + (int64_t)i * d;
     const float *mix = c.w.resid_mix + (int64_t)l * 2 * d;
-    const int j = l - c.D.enc;  // decoder skip index
+    const int j = a.v - c.D.enc;  // decoder skip index
     const bool skip = j >= 0 && j < c.D.nskip;
-    const float *sk = skip ? c.skip + ((int64_t)(c.D.enc - 1 - j) * n + i) * d : nullptr;
-    float ss = 0.0f;
+    const float *sk = skip ? c.skip + ((int64_t)(c.D.nskip - 1 - j) * n + i) * d : nullptr;
+    const bool par = a.mode != kAppPlain;
+    float *l1 = par ? c.lane1 + (int64_t)i * d : nullptr;
+    float ss = 0.0f, ss1 = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
         float xv = x[k];
+        if (a.mode == kAppParFirst) l1[k] = xv;
+        if (par) ss1 = __fmaf_rn(l1[k], l1[k], ss1);
         if (skip) {
             const float scaled = __fmul_rn(c.w.skip_weights[(int64_t)j * d + k], sk[k]);
             if (c.dsc.skip_gates) xv = lerp_t(scaled, xv, sigmoidf_(c.w.skip_gates[(int64_t)j * d + k]));
             else xv = __fadd_rn(xv, scaled);
         }
         const float xin = __fadd_rn(__fmul_rn(mix[k], xv), __fmul_rn(mix[d + k], x0[k]));
-        x[k] = xin;
+        x[k] = par ? xv : xin;
         ss = __fmaf_rn(xin, xin, ss);
     }
     const float inv = rms_inv(block_sum(ss, red), d);
+    const float inv1 = par ? rms_inv(block_sum(ss1, red), d) : 0.0f;
     const float ln = c.w.ln_scale[l];
     __syncthreads();
     float *nr = c.nrm + (int64_t)i * d;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(x[k], inv), ln);
+        // x_in again from its parts (x now holds lane 0 on two-lane applications)
+        const float xin = par ? __fadd_rn(__fmul_rn(mix[k], x[k]), __fmul_rn(mix[d + k], x0[k])) : x[k];
+        const float v = __fmul_rn(__fmul_rn(xin, inv), ln);
         nr[k] = v;
         if (c.tc) split_store(c.nrm_h, c.nrm_l, (int64_t)i * d + k, v);
+        if (par) {
+            const float v1 = __fmul_rn(__fmul_rn(l1[k], inv1), ln);
+            c.nrm2[(int64_t)i * d + k] = v1;
+            if (c.tc) split_store(c.nrm2_h, c.nrm2_l, (int64_t)i * d + k, v1);
+        }
     }
 }
 
@@ -159,14 +205,15 @@ __device__ __forceinline__ float lora_u(const float *B, const float *t, int rank
 }
 
 // LoRA on q/k/v, per-head RMSNorm, partial RoPE, q_gain, KV ring write.
-__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, int l) {
+// Layers that run XSA get their new V rows (fp32, after LoRA) back in qkv.
+__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) {
     extern __shared__ __align__(16) float sm[];
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
     const int tok = c.b.tok[i];
     if (tok < 0) return;
     const Dims &D = c.D;
-    const int d = D.d, kvd = D.kvd, hd = D.hd, R = D.r;
+    const int d = D.d, kvd = D.kvd, hd = D.hd, R = D.r, l = a.p;
     float *v = sm;                   // [qkv_n]
     float *tq = sm + D.qkv_n;        // [3][R]
     float *nx = tq + 3 * (R > 0 ? R : 1);  // [d]
@@ -195,6 +242,10 @@ __global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, int l) {
         }
     }
     __syncthreads();
+    if (l >= D.xsa_from && R > 0 && c.b.lora) {
+        float *dst = c.qkv + (int64_t)i * D.qkv_n;
+        for (int k = d + kvd + threadIdx.x; k < D.qkv_n; k += blockDim.x) dst[k] = v[k];
+    }
     const int64_t pos = c.b.pos[i];
     if (pos < 0 || pos >= c.w.rope_positions) {
         if (threadIdx.x == 0) atomicOr(&c.b.ac[i].status, ALTXS_ST_BAD_POS);
@@ -207,7 +258,7 @@ __global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, int l) {
     // heads: 0..H-1 q, H..H+Hkv-1 k (normed + rope), H+Hkv.. v (copy)
     const int nhead = D.H + 2 * D.Hkv;
     const int64_t rb = 3 * (int64_t)hd;  // bytes per KV row
-    uint8_t *kvbase = c.b.kv + ((int64_t)i * D.L + l) * 2 * D.Hkv * D.ctx * rb;
+    uint8_t *kvbase = c.b.kv + ((int64_t)i * D.Lv + a.v) * 2 * D.Hkv * D.ctx * rb;
     for (int h = wid; h < nhead; h += nw) {
         float *e = v + h * hd;  // q heads, then k heads, then v heads are contiguous
         if (h >= D.H + D.Hkv) {
@@ -315,6 +366,7 @@ __device__ __forceinline__ RingItem ring_item(const StepCtx &c, int t) {
     return it;
 }
 
+// l: the application's KV set
 template <int LPK, int G>
 __global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int l, int n_items, int slots) {
     constexpr int KPP = 32 / LPK;  // keys per pass
@@ -360,7 +412,7 @@ __global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int
             const int rows = min(kRingChunk, lit.nvalid - lc * kRingChunk);
             const uint32_t bytes = (uint32_t)rows * RB;
             const int64_t k0 = (int64_t)lit.sp * kSplit + lc * kRingChunk;
-            const uint8_t *kvb = c.b.kv + ((int64_t)lit.i * D.L + l) * 2 * D.Hkv * D.ctx * RB;
+            const uint8_t *kvb = c.b.kv + ((int64_t)lit.i * D.Lv + l) * 2 * D.Hkv * D.ctx * RB;
             uint8_t *dst = wbuf + (int64_t)s * 2 * kChunkBytes;
             mbar_expect_tx(&bar[s], 2 * bytes);
             bulk_g2s(dst, kvb + ((int64_t)lit.kvh * D.ctx + k0) * RB, bytes, &bar[s]);
@@ -566,11 +618,15 @@ cudaError_t launch_attn(const StepCtx &c, int l, cudaStream_t st) {
 #undef ALTXS_RING_G
 }
 
-// Fixed-order merge of the split partials -> y [n][H*hd]
-__global__ void k_attn_merge(StepCtx c) {
+// Fixed-order merge of the split partials -> y [n][H*hd], then on XSA layers
+// y -= (y . v^) v^ with v^ = v/max(|v|, 1e-12) of the head's own new V row,
+// and with the sparse attention gate y *= sigmoid(scale * w_h . n[:gate_window])
+// (model.py:760-768, 845-862).  One CTA of hd threads per (stream, head).
+__global__ void k_attn_merge(StepCtx c, int p) {
+    __shared__ float red[32];
     const Dims &D = c.D;
     const int i = blockIdx.x / D.H, h = blockIdx.x % D.H, k = threadIdx.x;
-    if (!row_active(c.b, i) || c.b.tok[i] < 0 || k >= D.hd) return;
+    if (!row_active(c.b, i) || c.b.tok[i] < 0) return;
     const float *pp = c.part + ((int64_t)i * D.H + h) * D.nsplit * (D.hd + 2);
     float M = -INFINITY;
     for (int s = 0; s < D.nsplit; ++s)
@@ -584,7 +640,21 @@ __global__ void k_attn_merge(StepCtx c) {
             a = __fmaf_rn(q[k], f, a);
         }
     }
-    const float yv = l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
+    float yv = l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
+    if (p >= D.xsa_from) {
+        const float vn = c.qkv[(int64_t)i * D.qkv_n + D.d + D.kvd + (h / (D.H / D.Hkv)) * D.hd + k];
+        const float nv = fmaxf(__fsqrt_rn(block_sum(__fmul_rn(vn, vn), red)), 1e-12f);
+        const float vh = __fdiv_rn(vn, nv);
+        const float dot = block_sum(__fmul_rn(yv, vh), red);
+        yv = __fsub_rn(yv, __fmul_rn(dot, vh));
+    }
+    if (c.dsc.sparse_gate) {
+        const float *gw = c.w.attn_gate_w + ((int64_t)p * D.H + h) * D.gw;
+        const float *nr = c.nrm + (int64_t)i * D.d;
+        // gate_window <= head_dim (checked on the host): thread k takes n[k]
+        const float g = block_sum(k < D.gw ? __fmul_rn(nr[k], gw[k]) : 0.0f, red);
+        yv = __fmul_rn(yv, sigmoidf_(__fmul_rn(c.dsc.sparse_gate_scale, g)));
+    }
     c.y[(int64_t)i * D.d + h * D.hd + k] = yv;
     if (c.tc) split_store(c.y_h, c.y_l, (int64_t)i * D.d + h * D.hd + k, yv);
 }
@@ -623,20 +693,46 @@ __global__ void k_post_attn(StepCtx c, int l) {
     }
 }
 
-// final RMSNorm (+ lm_head LoRA t)
-__global__ void k_final(StepCtx c) {
+// Two-lane residual update (model.py:1293-1348):
+//   a = attn_scale*ao ; m = mlp_scale*mo
+//   lane0 = r0*lane0 + p00*a + p10*m ; lane1 = r1*lane1 + p01*a + p11*m
+__global__ void k_par_combine(StepCtx c, int l) {
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int d = c.D.d;
+    const float *pp = c.w.parallel_post + (int64_t)l * 4, *pr = c.w.parallel_resid + (int64_t)l * 2;
+    const float p00 = pp[0], p01 = pp[1], p10 = pp[2], p11 = pp[3], r0 = pr[0], r1 = pr[1];
+    float *x = c.x + (int64_t)i * d, *l1 = c.lane1 + (int64_t)i * d;
+    const float *ao = c.ao + (int64_t)i * d, *mo = c.mo + (int64_t)i * d;
+    const float *as = c.w.attn_scale + (int64_t)l * d, *ms = c.w.mlp_scale + (int64_t)l * d;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float a = __fmul_rn(as[k], ao[k]), m = __fmul_rn(ms[k], mo[k]);
+        x[k] = __fadd_rn(__fadd_rn(__fmul_rn(r0, x[k]), __fmul_rn(p00, a)), __fmul_rn(p10, m));
+        l1[k] = __fadd_rn(__fadd_rn(__fmul_rn(r1, l1[k]), __fmul_rn(p01, a)), __fmul_rn(p11, m));
+    }
+}
+
+// final RMSNorm (+ lm_head LoRA t).  lanes: -1 one residual stream; after
+// two-lane applications 0 the lanes' mean, 1 lane 0, 2 lane 1 (model.py:1437-1443).
+__global__ void k_final(StepCtx c, int lanes) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, R = c.D.r;
-    const float *x = c.x + (int64_t)i * d;
+    const float *x = lanes == 2 ? c.lane1 + (int64_t)i * d : c.x + (int64_t)i * d;
+    const float *x1 = c.lane1 + (int64_t)i * d;
     float *nr = c.nrm + (int64_t)i * d;
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) ss = __fmaf_rn(x[k], x[k], ss);
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float v = x[k];
+        if (lanes == 0) v = __fmul_rn(0.5f, __fadd_rn(v, x1[k]));
+        sm[k] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
     const float inv = rms_inv(block_sum(ss, red), d);
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
-        const float v = __fmul_rn(x[k], inv);
+        const float v = __fmul_rn(sm[k], inv);
         nr[k] = v;
         sm[k] = v;
         if (c.tc) split_store(c.nrm_h, c.nrm_l, (int64_t)i * d + k, v);
@@ -663,12 +759,16 @@ __global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
     if (has_lm && threadIdx.x < R) tl[threadIdx.x] = c.lt[(int64_t)i * R + threadIdx.x];
     __syncthreads();
     const float *raw = c.logits + (int64_t)i * V;
+    // asymmetric softcap (model.py:1478-1500): separate caps above and below zero
+    const float cap_n = c.dsc.asym_softcap ? c.w.softcap[1] : cap;
+    const float cap_p = c.dsc.asym_softcap ? c.w.softcap[0] : cap;
     for (int k = threadIdx.x; k < V; k += blockDim.x) {
         float lg = 0.0f;
         if (tok >= 0) {
             float v = raw[k];
             if (has_lm) v = __fadd_rn(v, lora_u(P, tl, R, k, c.dsc.lora_scale));
-            lg = __fmul_rn(cap, tanhf(__fdiv_rn(v, cap)));
+            const float cp = v >= 0.0f ? cap_p : cap_n;
+            lg = __fmul_rn(cp, tanhf(__fdiv_rn(v, cp)));
         }
         buf[k] = lg;
         if (c.b.logits_out) c.b.logits_out[(int64_t)i * V + k] = lg;
@@ -721,6 +821,7 @@ __global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
         if (tok >= 0) p += 1;
         c.b.pos[i] = p;
         c.b.tok[i] = sym;
+        if (c.b.prev_tok && tok >= 0) c.b.prev_tok[i] = tok;
         if (c.b.hist) {
             const int64_t ap = p + (c.b.pos_base ? c.b.pos_base[i] : 0);  // absolute symbol index
             c.b.hist[(int64_t)i * c.b.hist_len + (ap % c.b.hist_len)] = sym;
@@ -743,6 +844,7 @@ inline int64_t ws_size(const Dims &D) {
     s += A((int64_t)D.n * D.V);                       // logits
     s += A((int64_t)D.n * (D.r > 0 ? D.r : 1));       // lm LoRA t
     s += 3 * A((int64_t)D.n * D.d);                   // hi/lo bf16 planes of nrm, y, nrm2
+    if (D.par) s += 2 * A((int64_t)D.n * D.d);        // lane 1, MLP output
     return s;
 }
 
@@ -769,8 +871,27 @@ int fill_dims(const altxs_model_desc *dsc, int n, Dims &D) {
     D.kvd = D.Hkv * D.hd;
     D.qkv_n = D.d + 2 * D.kvd;
     D.nsplit = (D.ctx + kSplit - 1) / kSplit;
-    D.enc = D.L / 2;
-    D.nskip = D.enc < D.L - D.enc ? D.enc : D.L - D.enc;
+    D.Lv = dsc->n_virtual > 0 ? dsc->n_virtual : D.L;
+    if (D.Lv != D.L && !dsc->schedule) return ALTXS_EINVAL;
+    if (D.Lv > 4 * D.L + 64) return ALTXS_EINVAL;
+    if (dsc->schedule)
+        for (int v = 0; v < D.Lv; ++v)
+            if (dsc->schedule[v] < 0 || dsc->schedule[v] >= D.L) return ALTXS_EINVAL;
+    D.enc = dsc->n_encoder > 0 ? dsc->n_encoder : D.Lv / 2;
+    if (D.enc > D.Lv) return ALTXS_EINVAL;
+    D.nskip = D.enc < D.Lv - D.enc ? D.enc : D.Lv - D.enc;
+    if (dsc->xsa_last_n < 0 || dsc->xsa_last_n > D.L || dsc->parallel_start < 0) return ALTXS_EINVAL;
+    D.xsa_from = D.L - dsc->xsa_last_n;
+    D.par = 0;
+    if (dsc->parallel_start > 0)
+        for (int v = D.enc; v < D.Lv; ++v)
+            if ((dsc->schedule ? dsc->schedule[v] : v) >= dsc->parallel_start) D.par = 1;
+    if (dsc->parallel_final < 0 || dsc->parallel_final > 2) return ALTXS_EINVAL;
+    D.gw = 0;
+    if (dsc->smear_gate || dsc->sparse_gate) {
+        D.gw = dsc->gate_window;
+        if (D.gw < 1 || D.gw > D.d || (dsc->sparse_gate && D.gw > D.hd)) return ALTXS_EINVAL;
+    }
     return ALTXS_OK;
 }
 
@@ -817,6 +938,10 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         w->o.rows != D.L * D.d || w->o.cols != D.d || w->up.rows != D.L * D.F || w->up.cols != D.d ||
         w->down.rows != D.L * D.d || w->down.cols != D.F)
         return ALTXS_EINVAL;
+    if ((desc->smear_gate && (!w->smear_gate || !w->smear_lambda || !b->prev_tok)) ||
+        (desc->sparse_gate && !w->attn_gate_w) || (desc->asym_softcap && !w->softcap) ||
+        (D.par && (!w->parallel_post || !w->parallel_resid)))
+        return ALTXS_EINVAL;
     c.lo = lora_offsets(*desc);
     if (D.r > 0 && b->lora && b->lora_stride < c.lo.total) return ALTXS_EINVAL;
     D.lora_stride = b->lora_stride;
@@ -852,6 +977,10 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         // the MLP hidden planes take the place of the fp32 hidden buffer (unused on this path)
         c.hid_h = reinterpret_cast<uint16_t *>(c.hid);
         c.hid_l = c.hid_h + (int64_t)D.n * D.F;
+    }
+    if (D.par) {
+        c.lane1 = take((int64_t)D.n * D.d);
+        c.mo = take((int64_t)D.n * D.d);
     }
     const altxs_split_planes *sp = w->split;
     c.tc = sp != nullptr;
@@ -902,8 +1031,18 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         }
     }
     const size_t qkv_sm = ((size_t)D.qkv_n + 3 * (D.r > 0 ? D.r : 1) + D.d) * 4;
-    for (int l = 0; l < D.L; ++l) {
-        ALTXS_LAUNCH(::altxs::kKPrenorm, st, k_prenorm<<<D.n, 128, 0, st>>>(c, l));
+    // applications in schedule order: weights by physical layer p, KV set and
+    // skip slot by application v (model.py:1064-1077, 1377-1436)
+    bool lanes_on = false;
+    for (int v = 0; v < D.Lv; ++v) {
+        const int l = desc->schedule ? desc->schedule[v] : v;
+        LayerApp app{l, v, kAppPlain};
+        if (v >= D.enc && desc->parallel_start > 0 && l >= desc->parallel_start) {
+            app.mode = lanes_on ? kAppPar : kAppParFirst;
+            lanes_on = true;
+        }
+        const bool par = app.mode != kAppPlain;
+        ALTXS_LAUNCH(::altxs::kKPrenorm, st, k_prenorm<<<D.n, 128, 0, st>>>(c, app));
         QmmArgs a{};
         a.X = c.nrm;
         a.ldx = D.d;
@@ -916,13 +1055,13 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.ldy = D.qkv_n;
         a.epi = kEpiStore;
         if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->qkv_hi : nullptr, c.tc ? sp->qkv_lo : nullptr, nullptr, nullptr))) return rc;
-        ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, l));
+        ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, app));
         {
             cudaError_t ae = cudaSuccess;
-            ALTXS_LAUNCH(::altxs::kKAttn, st, ae = launch_attn(c, l, st));
+            ALTXS_LAUNCH(::altxs::kKAttn, st, ae = launch_attn(c, v, st));
             if (ae != cudaSuccess) return ALTXS_ECUDA;
         }
-        ALTXS_LAUNCH(::altxs::kKAttnMerge, st, k_attn_merge<<<D.n * D.H, D.hd, 0, st>>>(c));
+        ALTXS_LAUNCH(::altxs::kKAttnMerge, st, k_attn_merge<<<D.n * D.H, D.hd, 0, st>>>(c, l));
         a.X = c.y;
         a.W = w->o;
         a.row0 = l * D.d;
@@ -930,7 +1069,9 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.Y = c.ao;
         a.ldy = D.d;
         if ((rc = linear(a, c.y_h, c.y_l, c.tc ? sp->o_hi : nullptr, c.tc ? sp->o_lo : nullptr, nullptr, nullptr))) return rc;
-        ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l));
+        // two-lane applications normed lane 1 for the MLP in k_prenorm
+        if (!par)
+            ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l));
         a.X = c.nrm2;
         a.W = w->up;
         a.row0 = l * D.F;
@@ -945,17 +1086,26 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.row0 = l * D.d;
         a.N = D.d;
         a.K = D.F;
-        a.Y = c.x;
         a.ldy = D.d;
-        a.epi = kEpiResid;
-        a.R = c.x;
-        a.ldr = D.d;
-        a.colscale = w->mlp_scale + (int64_t)l * D.d;
-        a.Y2 = l < D.enc ? c.skip + (int64_t)l * D.n * D.d : nullptr;
-        a.ldy2 = D.d;
+        if (par) {
+            a.Y = c.mo;
+            a.epi = kEpiStore;
+        } else {
+            a.Y = c.x;
+            a.epi = kEpiResid;
+            a.R = c.x;
+            a.ldr = D.d;
+            a.colscale = w->mlp_scale + (int64_t)l * D.d;
+            // encoder outputs the decoder's skips read (the last nskip of them)
+            const int slot = v - (D.enc - D.nskip);
+            a.Y2 = v < D.enc && slot >= 0 ? c.skip + (int64_t)slot * D.n * D.d : nullptr;
+            a.ldy2 = D.d;
+        }
         if ((rc = linear(a, c.hid_h, c.hid_l, c.tc ? sp->down_hi : nullptr, c.tc ? sp->down_lo : nullptr, nullptr, nullptr))) return rc;
+        if (par) ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_par_combine<<<D.n, 128, 0, st>>>(c, l));
     }
-    ALTXS_LAUNCH(::altxs::kKFinal, st, k_final<<<D.n, 128, D.d * 4, st>>>(c));
+    const int lanes = lanes_on ? desc->parallel_final : -1;
+    ALTXS_LAUNCH(::altxs::kKFinal, st, k_final<<<D.n, 128, D.d * 4, st>>>(c, lanes));
     QmmArgs a{};
     a.X = c.nrm;
     a.ldx = D.d;

@@ -57,6 +57,10 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, bool prefill = false) {
     if (T < (prefill ? 1 : 2) || D.r < (prefill ? 0 : 1) || D.r > 64) return ALTXS_EINVAL;
     if (D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
     if (D.hd > 128 || D.rd > D.hd || D.rd % 2) return ALTXS_EINVAL;
+    // the window forward here is the plain GPT stack: one application per layer, no motifs
+    if ((dsc.n_virtual > 0 && dsc.n_virtual != D.L) || dsc.schedule || dsc.smear_gate || dsc.xsa_last_n ||
+        dsc.sparse_gate || dsc.asym_softcap || dsc.parallel_start)
+        return ALTXS_ENOTSUP;
     return ALTXS_OK;
 }
 

@@ -89,6 +89,19 @@ class DeviceModel:
             "skip_weights": f32(s["skip_weights"] if s["skip_weights"].size else np.zeros((1, cfg.model_dim))),
             "skip_gates": f32(s["skip_gates"] if s["skip_gates"].size else np.zeros((1, cfg.model_dim))),
         }
+        # reference motifs: parameters uploaded only for the motifs that are on
+        motif_on = {
+            "smear_gate": cfg.smear_gate_enabled, "smear_lambda": cfg.smear_gate_enabled,
+            "attn_gate_w": cfg.sparse_attn_gate_enabled, "softcap": cfg.asym_logit_rescale,
+            "parallel_post": cfg.parallel_start_layer > 0, "parallel_resid": cfg.parallel_start_layer > 0,
+        }
+        for k, on in motif_on.items():
+            if on:
+                self.small[k] = f32(s[k])
+        enc, dec = cfg.layer_schedule
+        sched = enc + dec
+        self._schedule = (C.c_int32 * len(sched))(*sched)
+        self.n_virtual = len(sched)
         self.rope_positions = 0
         self.ensure_rope(rope_positions)
         self.desc = _lib.ModelDesc(
@@ -98,6 +111,12 @@ class DeviceModel:
             lora_rank=cfg.ttt_lora_rank if cfg.lora_enabled else 0, lora_mask=lora_mask(cfg),
             cdf_mode=_lib.CDF_FIXED if cfg.cdf_mode == "fixed" else _lib.CDF_REF, cdf_bits=cfg.cdf_bits,
             logit_softcap=cfg.logit_softcap, lora_scale=cfg.lora_scale if cfg.lora_enabled else 0.0,
+            n_virtual=self.n_virtual, n_encoder=len(enc),
+            schedule=C.cast(self._schedule, C.c_void_p) if cfg.num_loops > 0 else None,
+            smear_gate=int(cfg.smear_gate_enabled), gate_window=cfg.gate_window, xsa_last_n=cfg.xsa_last_n,
+            sparse_gate=int(cfg.sparse_attn_gate_enabled), sparse_gate_scale=cfg.sparse_attn_gate_scale,
+            asym_softcap=int(cfg.asym_logit_rescale), parallel_start=cfg.parallel_start_layer,
+            parallel_final={"mean": 0, "attn": 1, "mlp": 2}[cfg.parallel_final_lane],
         )
         self.lora_floats = int(_lib.lib().altxs_lora_floats(C.byref(self.desc)))
         self.tensor_cores = bool(tensor_cores)
@@ -174,6 +193,8 @@ class DeviceModel:
                 skip_gates=s["skip_gates"].data_ptr(), rope_cos=self.rope_cos.data_ptr(),
                 rope_sin=self.rope_sin.data_ptr(), rope_positions=self.rope_positions,
                 split=C.pointer(self._split) if self._split is not None else None,
+                **{k: s[k].data_ptr() for k in ("smear_gate", "smear_lambda", "attn_gate_w", "softcap",
+                                                "parallel_post", "parallel_resid") if k in s},
             )
         return self._weights_struct
 
@@ -195,13 +216,15 @@ class StreamBatch:
         self.replays = 0
         self.dm, self.n, self.cfg = dm, int(n), cfg
         self.words_per_stream = int(words_per_stream)
-        L, Hkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
+        L, Hkv, hd = dm.n_virtual, cfg.num_kv_heads, cfg.head_dim
         self.tok = torch.full((n,), -1, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(n, dtype=torch.int64, device=dev)
         self.active = torch.ones(n, dtype=torch.uint8, device=dev)
         # sliding-window ring, rows in the 24-bit split format (3 bytes/value)
         self.kv = torch.zeros((n, L, 2, Hkv, cfg.kv_len, 3 * hd), dtype=torch.uint8, device=dev)
         self.pos_base = torch.zeros(n, dtype=torch.int64, device=dev)  # absolute index of position 0
+        # smear gate: the token each stream consumed last (-1: none yet)
+        self.prev_tok = torch.full((n,), -1, dtype=torch.int32, device=dev) if cfg.smear_gate_enabled else None
         self.ac = torch.zeros((n, 8), dtype=torch.int64, device=dev)
         self.bits = torch.zeros((n, self.words_per_stream), dtype=torch.int32, device=dev)
         self.sym = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -224,6 +247,7 @@ class StreamBatch:
             words_per_stream=self.words_per_stream, sym=self.sym.data_ptr(),
             hist=self.hist.data_ptr() if self.hist is not None else None, hist_len=self.hist_len,
             pos_base=self.pos_base.data_ptr(),
+            prev_tok=self.prev_tok.data_ptr() if self.prev_tok is not None else None,
             logits_out=self.logits.data_ptr() if self.logits is not None else None,
             workspace=self.workspace.data_ptr(), workspace_bytes=wsb,
         )

@@ -133,6 +133,20 @@ typedef struct altxs_model_desc {
     int32_t lora_mask;  /* bit0 q, bit1 k, bit2 v, bit3 o, bit4 lm_head */
     int32_t cdf_mode, cdf_bits;
     float logit_softcap, lora_scale;
+    /* Reference motifs (altxs src/xsa_ttt/model.py:760-768, 845-862, 1064-1077,
+     * 1293-1362, 1404-1500); all zero = the plain GPT.  The test-time update
+     * (altxs_ttt_update, altxs_prefill) covers the plain GPT only. */
+    int32_t n_virtual;          /* layer applications (depth loops repeat layers); 0 = n_layers */
+    int32_t n_encoder;          /* encoder applications (the U-Net skips' sources); 0 = n_virtual/2 */
+    const int32_t *schedule;    /* host [n_virtual]: physical layer of each application, or NULL */
+    int32_t smear_gate;         /* raw embedding += lambda*sigmoid(g . raw[:gate_window]) * previous raw */
+    int32_t gate_window;
+    int32_t xsa_last_n;         /* on the last n physical layers: y_h -= (y_h . v^) v^, v^ = v/|v| */
+    int32_t sparse_gate;        /* y_h *= sigmoid(sparse_gate_scale * w_h . n[:gate_window]) */
+    float sparse_gate_scale;
+    int32_t asym_softcap;       /* logits: sp*tanh(l/sp) for l >= 0, sn*tanh(l/sn) below */
+    int32_t parallel_start;     /* decoder applications of layers >= this run two lanes; 0 = off */
+    int32_t parallel_final;     /* final hidden: 0 mean of the lanes, 1 attention lane, 2 MLP lane */
 } altxs_model_desc;
 
 /* Tensor-core operand form of the five mixed-bit matrices: every dequantised
@@ -170,6 +184,13 @@ typedef struct altxs_weights {
      * Either way results do not depend on the batch; an encoder and its
      * decoder must make the same choice. */
     const altxs_split_planes *split;
+    /* motif parameters (device; NULL when the motif is off) */
+    const float *smear_gate;     /* [gate_window] */
+    const float *smear_lambda;   /* [1] */
+    const float *attn_gate_w;    /* [L][H][gate_window] */
+    const float *softcap;        /* [2]: positive, negative */
+    const float *parallel_post;  /* [L][2][2]: (attention, MLP) output into (lane 0, lane 1) */
+    const float *parallel_resid; /* [L][2]: lane 0, lane 1 residual scales */
 } altxs_weights;
 
 /* Per-stream state and scratch of a batch of n streams.  Stream i of the
@@ -179,7 +200,7 @@ typedef struct altxs_batch {
     int32_t *tok;           /* [n] token consumed this step (<0: none, uniform row) */
     int64_t *pos;           /* [n] position tok is written at (tokens consumed) */
     const uint8_t *active;  /* [n] 0 = leave the stream untouched (NULL = all) */
-    uint8_t *kv;            /* [n][L][2 (K,V)][Hkv][ctx][3*hd] sliding-window ring, rows in
+    uint8_t *kv;            /* [n][n_virtual][2 (K,V)][Hkv][ctx][3*hd] sliding-window ring, rows in
                                24-bit split format: hd x u16 (bf16 high half of the
                                round-to-nearest 24-bit value) then hd x u8 (low byte) */
     float *lora;            /* [n][lora_floats] adapters (NULL if lora_rank = 0) */
@@ -196,6 +217,9 @@ typedef struct altxs_batch {
     const int64_t *pos_base; /* [n] absolute index of position 0 for the hist ring, or NULL
                                 (= 0).  Segment-reset context (positions restart at every
                                 segment) keeps hist in absolute symbol order with it. */
+    int32_t *prev_tok;       /* [n] token consumed by the previous step (-1: none), read by
+                                the smear gate and advanced with pos by the encode and
+                                decode modes; NULL when the gate is off */
 } altxs_batch;
 
 /* Allocation-free altxs_step for callers that cannot allocate device memory
