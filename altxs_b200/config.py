@@ -3,9 +3,10 @@
 ``ModelConfig`` mirrors the subset of the reference ``XsaTttConfig``
 (altxs ``src/xsa_ttt/config.py:20-189``) that the per-symbol loop reads.  The
 reference motifs that sit on top of the plain GPT (XSA, SmearGate,
-SparseAttnGate, depth loops, parallel residual lanes, asymmetric softcap) are
-not part of this engine; ``from_reference_cfg`` refuses configs that enable
-them instead of silently computing a different model.
+SparseAttnGate, depth loops, parallel residual lanes, asymmetric softcap) run
+in the decode step with frozen weights; ``from_reference_cfg`` refuses the
+ones this engine does not compute (output gates, YaRN, untied heads) instead
+of silently computing a different model.
 
 The always-on pieces of the reference block are kept: QK-RMSNorm, per-head
 ``q_gain``, partial RoPE over ``rope_dims``, ``resid_mix`` against ``x0``,
@@ -50,7 +51,7 @@ class ModelConfig:
     context_mode: str = "sliding"
     seed: int = 1337
     # test-time LoRA (reference ttt_* fields, config.py:144-165)
-    retrain_mode: str = "lora"  # "lora" or "none"
+    retrain_mode: str = "lora"  # "lora", "replenish" (every parameter, see below) or "none"
     ttt_lora_rank: int = 8
     ttt_lora_alpha: float = 144.0
     ttt_lora_lr: float = 1e-3
@@ -62,6 +63,30 @@ class ModelConfig:
     ttt_mlp_lora: bool = False
     ttt_use_rslora: bool = False
     grad_clip: float = 1.0
+    # full-parameter replenish (reference config.py:59-138, compress.py:363-482,
+    # 611-720, 816-1146): AdamW over every weight of the model on the chunk just
+    # coded (with the preceding block as context), optionally Forward-XM over
+    # update scales scored on held-out probe chunks
+    online_retrain_steps: int = 1
+    online_retrain_replay: bool = True
+    ttt_bootstrap_symbols: int = 0
+    ttt_bootstrap_steps: int = 0
+    ttt_replenish_ramp: int = 0
+    ttt_replenish_anneal: str = "exp"
+    ttt_replenish_lr_half_mb: float = 0.0
+    ttt_replenish_lr_min: float = 4e-5
+    ttt_replenish_steps_min: int = 1
+    ttt_replenish_warmup_steps: int = 16
+    ttt_replenish_total_bytes: int = 0
+    ttt_replenish_accum: bool = False
+    ttt_replenish_replay_lr_scale: float = 1.0
+    ttt_replenish_replay_recent_mb: float = 1.0
+    ttt_replenish_anchor: str = ""         # safetensors of per-weight stiffness masks ("" = none)
+    ttt_replenish_anchor_rate: float = 0.05
+    ttt_replenish_xm_k: int = 3
+    ttt_replenish_xm_probe_chunks: int = 1
+    ttt_replenish_xm_4x_until_bytes: int = 100 * 1024 * 1024
+    ttt_burst_schedule: str = ""           # "pos:steps,..." extra steps at the first boundary >= pos
     # reference model motifs (model.py:982-1110; all off = the plain GPT).  The
     # step and the oracle run them with frozen weights; the test-time LoRA
     # update covers the plain GPT only.
@@ -167,8 +192,12 @@ class ModelConfig:
             raise ValueError("cdf_bits must satisfy vocab < 2^cdf_bits <= 2^30")
         if self.ttt_mlp_lora:
             raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
-        if self.retrain_mode not in ("lora", "none"):
-            raise ValueError("retrain_mode must be 'lora' or 'none'")
+        if self.retrain_mode not in ("lora", "replenish", "none"):
+            raise ValueError("retrain_mode must be 'lora', 'replenish' or 'none'")
+        if self.retrain_mode == "replenish" and self.motifs:
+            raise ValueError("the replenish update covers the plain GPT; turn the motifs off")
+        if self.retrain_mode == "replenish" and self.context_mode == "reset":
+            raise ValueError("replenish runs with the sliding context")
         if self.context_mode not in ("sliding", "reset"):
             raise ValueError("context_mode must be 'sliding' or 'reset'")
         if self.parallel_final_lane not in ("mean", "attn", "mlp"):

@@ -320,6 +320,73 @@ def gen_model_motifs() -> None:
     np.savez_compressed(HERE / "model_motifs.npz", **out)
 
 
+REPLENISH = dict(
+    vocab_size=64, num_layers=2, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0,
+    rope_dims=8, block_size=16, online_retrain_every=24, seed=13, retrain_mode="none",
+)
+# reference replenish scenarios: (name, XsaTttConfig overrides, boundaries)
+REPLENISH_CASES = [
+    ("xm", dict(ttt_replenish_xm_k=3, ttt_replenish_warmup_steps=1, ttt_replenish_xm_4x_until_bytes=60,
+                ttt_weight_decay=0.01, ttt_lora_lr=2e-3), [24, 48, 72, 96]),
+    ("xm_probe2_anchor", dict(ttt_replenish_xm_k=2, ttt_replenish_warmup_steps=0, ttt_replenish_xm_probe_chunks=2,
+                              ttt_replenish_xm_4x_until_bytes=0, ttt_replenish_anneal="exp",
+                              ttt_replenish_lr_half_mb=1e-4, ttt_replenish_lr_min=1e-4, ttt_lora_lr=3e-3,
+                              ttt_replenish_anchor_rate=0.3), [24, 48, 72, 96]),
+    ("replay", dict(ttt_replenish_xm_k=0, ttt_replenish_warmup_steps=0, online_retrain_steps=2,
+                    online_retrain_replay=True, ttt_replenish_replay_recent_mb=0.0, ttt_lora_lr=2e-3,
+                    ttt_beta1=0.9), [24, 48, 72, 96]),
+]
+
+
+def gen_replenish() -> None:
+    """Full-parameter replenish boundaries of the reference (online_retrain in
+    retrain_mode="replenish", Forward-XM, anchor, anneal, replay) on a tiny
+    GPT: the returned loss and the XM scores/choice at every boundary and the
+    weights after the last one, from the reference's own code on CPU."""
+    import copy
+    import tempfile
+
+    from safetensors.torch import save_file
+    from xsa_ttt.compress import _init_online_state, online_retrain
+
+    cfg = ModelConfig(**REPLENISH)
+    w = C.synth_weights(cfg, seed=21)
+    base = ref_model(cfg, w)
+    rng = np.random.default_rng(5)
+    arr = rng.integers(0, cfg.vocab_size, size=100).astype(np.int64)
+    out = {"arr": arr.astype(np.int32), "config": np.frombuffer(json.dumps(REPLENISH).encode(), dtype=np.uint8)}
+    out.update({f"w0/{k}": v.detach().numpy() for k, v in base.state_dict().items()})
+    tmp = Path(tempfile.mkdtemp())
+    masks = {"qo_bank": torch.rand(base.qo_bank.shape, generator=torch.Generator().manual_seed(3)),
+             "blocks.0.attn_scale": torch.ones(base.blocks[0].attn_scale.shape)}
+    save_file(masks, str(tmp / "anchor.safetensors"))
+    out.update({f"anchor/{k}": v.numpy() for k, v in masks.items()})
+    for name, over, ends in REPLENISH_CASES:
+        m = copy.deepcopy(base)
+        h = ref_cfg(cfg)
+        h.retrain_mode = "replenish"
+        for k, v in over.items():
+            setattr(h, k, v)
+        if "anchor" in name:
+            h.ttt_replenish_anchor = str(tmp / "anchor.safetensors")
+        dev = torch.device("cpu")
+        _, opt = _init_online_state(m, h, dev, True)
+        out[f"{name}/over"] = np.frombuffer(json.dumps(over).encode(), dtype=np.uint8)
+        for end in ends:
+            m.train()
+            loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=None, seed=h.seed,
+                                  n_total=len(arr))
+            xm = getattr(m, "_xm_last", None)
+            out[f"{name}/{end}/loss"] = np.float64(loss)
+            if xm is not None and int(xm["end"]) == end:
+                out[f"{name}/{end}/xm_chosen"] = np.int32(xm["chosen"])
+                out[f"{name}/{end}/xm_scores"] = np.asarray(xm["scores"], dtype=np.float64)
+        # the per-boundary losses and scores pin the trajectory; the weights are kept at its end
+        for k, v in m.state_dict().items():
+            out[f"{name}/w/{k}"] = v.detach().numpy().copy()
+    np.savez_compressed(HERE / "replenish.npz", **out)
+
+
 def gen_zipf() -> None:
     from altxs_b200.synth import zipf_markov
 
@@ -334,6 +401,7 @@ if __name__ == "__main__":
     gen_model()
     gen_lora()
     gen_model_motifs()
+    gen_replenish()
     gen_zipf()
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
         print(f.name, f.stat().st_size)

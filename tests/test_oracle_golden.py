@@ -177,3 +177,42 @@ def test_oracle_motifs_match_reference(golden):
     st2 = om.new_stream()
     last = om.prefill(st2, g["tokens"]).numpy()
     assert float(np.abs(last - g["logits"][-1]).max()) < 1e-4
+
+
+def replenish_case(g, name):
+    """Config, initial state and anchor masks of one golden replenish scenario."""
+    import json
+
+    from altxs_b200.config import ModelConfig
+
+    base = json.loads(bytes(g["config"]))
+    over = json.loads(bytes(g[f"{name}/over"]))
+    cfg = ModelConfig(**{**base, "retrain_mode": "replenish", **over})
+    w0 = {k[3:]: g[k] for k in g.files if k.startswith("w0/")}
+    masks = {k[7:]: g[k] for k in g.files if k.startswith("anchor/")} if "anchor" in name else None
+    if masks:
+        cfg.ttt_replenish_anchor = "anchor.safetensors"
+    return cfg, w0, masks
+
+
+@pytest.mark.parametrize("name", ["xm", "xm_probe2_anchor", "replay"])
+def test_oracle_replenish_matches_reference(golden, name):
+    """Full-parameter replenish boundaries (Forward-XM with a 4x head and a
+    warmup boundary; XM over two probe chunks with anchor masks and an
+    annealed lr; plain replenish with replay draws) against the reference's
+    own online_retrain: loss and XM scores/choice per boundary, weights at the end."""
+    from oracle.replenish import OracleReplenish
+
+    g = golden("replenish.npz")
+    cfg, w0, masks = replenish_case(g, name)
+    o = OracleReplenish(cfg, w0, masks)
+    arr = g["arr"].astype(np.int64)
+    for end in (24, 48, 72, 96):
+        loss = o.boundary(arr, end, n_total=len(arr))
+        assert abs(loss - float(g[f"{name}/{end}/loss"])) < 1e-5, (end, loss)
+        if f"{name}/{end}/xm_chosen" in g.files:
+            assert o.xm_last["chosen"] == int(g[f"{name}/{end}/xm_chosen"])
+            assert np.abs(np.array(o.xm_last["scores"]) - g[f"{name}/{end}/xm_scores"]).max() < 1e-5
+    st = o.state()
+    err = max(float(np.abs(st[k] - g[f"{name}/w/{k}"]).max()) for k in st)
+    assert err < 1e-6, err
