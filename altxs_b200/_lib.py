@@ -26,6 +26,8 @@ EXPORTS = (
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
     "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
     "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit",
+    "altxs_param_layout_of", "altxs_full_workspace_bytes", "altxs_full_loss_grad", "altxs_adamw",
+    "altxs_params_axpy", "altxs_params_anchor", "altxs_split_params",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -73,7 +75,15 @@ class Weights(C.Structure):
         ("rope_positions", C.c_int64), ("split", C.POINTER(SplitPlanes)),
         ("smear_gate", C.c_void_p), ("smear_lambda", C.c_void_p), ("attn_gate_w", C.c_void_p),
         ("softcap", C.c_void_p), ("parallel_post", C.c_void_p), ("parallel_resid", C.c_void_p),
+        ("emb_dense", C.c_void_p),
     ]
+
+
+class ParamLayout(C.Structure):
+    """Segments (floats) of a full parameter arena (altxs_param_layout)."""
+
+    _fields_ = [(k, C.c_int64) for k in ("emb", "qkv", "o", "up", "down", "q_gain", "attn_scale", "mlp_scale",
+                                         "resid_mix", "skip_weights", "skip_gates", "total")]
 
 
 class TttHparams(C.Structure):
@@ -145,6 +155,14 @@ def lib():
             "altxs_linear_workspace_bytes": (i64, [C.c_int, C.c_int]),
             "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
             "altxs_gemm_workspace_bytes": (i64, [C.c_int] * 6),
+            "altxs_param_layout_of": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(ParamLayout)]),
+            "altxs_full_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.c_int]),
+            "altxs_full_loss_grad": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(DenseWeights), vp,
+                                               C.c_int, C.c_int, vp, vp, vp, i64, vp]),
+            "altxs_adamw": (C.c_int, [i64, vp, vp, vp, vp, C.POINTER(TttHparams), C.c_int, vp, vp]),
+            "altxs_params_axpy": (C.c_int, [i64, vp, C.c_float, vp, vp, vp]),
+            "altxs_params_anchor": (C.c_int, [i64, vp, vp, vp, vp]),
+            "altxs_split_params": (C.c_int, [C.POINTER(ModelDesc), vp, C.POINTER(SplitPlanes), vp]),
             "altxs_gemm": (C.c_int, [C.c_int, C.c_int, C.c_int, vp, i64, i64, C.c_int, vp, i64, i64, C.c_int, vp, i64,
                                      i64, C.c_int, C.c_float, C.c_float, C.c_int, vp, i64, vp]),
         }

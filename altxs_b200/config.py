@@ -196,8 +196,6 @@ class ModelConfig:
             raise ValueError("retrain_mode must be 'lora', 'replenish' or 'none'")
         if self.retrain_mode == "replenish" and self.motifs:
             raise ValueError("the replenish update covers the plain GPT; turn the motifs off")
-        if self.retrain_mode == "replenish" and self.context_mode == "reset":
-            raise ValueError("replenish runs with the sliding context")
         if self.context_mode not in ("sliding", "reset"):
             raise ValueError("context_mode must be 'sliding' or 'reset'")
         if self.parallel_final_lane not in ("mean", "attn", "mlp"):

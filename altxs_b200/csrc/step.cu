@@ -82,17 +82,20 @@ __global__ void k_embed(StepCtx c) {
         prev = c.b.prev_tok[i];
         if (threadIdx.x < 32) {
             float g = 0.0f;
-            for (int k = threadIdx.x; k < c.D.gw; k += 32) g = __fmaf_rn(qmat_elem(c.w.emb, tok, k), c.w.smear_gate[k], g);
+            for (int k = threadIdx.x; k < c.D.gw; k += 32)
+                g = __fmaf_rn(c.w.emb_dense ? c.w.emb_dense[(int64_t)tok * d + k] : qmat_elem(c.w.emb, tok, k),
+                              c.w.smear_gate[k], g);
             g = warp_sum(g);
             if (threadIdx.x == 0) gate = __fmul_rn(c.w.smear_lambda[0], sigmoidf_(g));
         }
         __syncthreads();
     }
     const bool smear = prev >= 0 && prev < c.D.V;
+    const float *ed = c.w.emb_dense;
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
-        float v = qmat_elem(c.w.emb, tok, k);
-        if (smear) v = __fadd_rn(v, __fmul_rn(gate, qmat_elem(c.w.emb, prev, k)));
+        float v = ed ? ed[(int64_t)tok * d + k] : qmat_elem(c.w.emb, tok, k);
+        if (smear) v = __fadd_rn(v, __fmul_rn(gate, ed ? ed[(int64_t)prev * d + k] : qmat_elem(c.w.emb, prev, k)));
         x[k] = v;
         ss = __fmaf_rn(v, v, ss);
     }

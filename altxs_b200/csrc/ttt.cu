@@ -22,7 +22,11 @@ namespace {
 
 struct TD {
     int T, V, L, d, H, Hkv, hd, kvd, F, qn, r, enc, nskip, G, rd;
+    int first;  // first scored position of the loss (rows before it are context only)
+    int full;   // full-parameter gradient (replenish): extra tape, P recomputed per layer
 };
+
+enum FillMode { kFillLora, kFillPrefill, kFillFull };
 
 struct Tape {
     // forward state
@@ -35,9 +39,16 @@ struct Tape {
     float *invf, *hf, *logits, *tlm, *rowloss;
     // backward
     float *dx, *dskip, *dd, *dh, *dn, *dn2, *dqkv, *dqr, *dkr, *dy, *dao, *dS, *dt, *grad, *red;
+    // full-parameter gradient only: layer inputs before skip and mix, attention
+    // outputs, o- and down-projection outputs [L][T][d]; raw embedding rows and
+    // their inverse rms; d(x0); per-row products [T][4d] and their column partials
+    float *xraw, *yl, *aol, *doutl, *eraw, *inv0, *dx0, *colbuf, *cpart;
 };
 
-int fill(const altxs_model_desc &dsc, int T, TD &D, bool prefill = false) {
+constexpr int kColChunks = 64;  // row chunks of a column sum (summed in order)
+
+int fill(const altxs_model_desc &dsc, int T, TD &D, FillMode mode = kFillLora) {
+    const bool prefill = mode == kFillPrefill;
     D.T = T;
     D.V = dsc.vocab;
     D.L = dsc.n_layers;
@@ -53,8 +64,16 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, bool prefill = false) {
     D.nskip = D.enc < D.L - D.enc ? D.enc : D.L - D.enc;
     D.G = D.H / (D.Hkv > 0 ? D.Hkv : 1);
     D.rd = dsc.rope_dims;
-    // an update trains adapters over >= 2 positions; a context prefill needs neither
-    if (T < (prefill ? 1 : 2) || D.r < (prefill ? 0 : 1) || D.r > 64) return ALTXS_EINVAL;
+    D.first = 0;
+    D.full = mode == kFillFull;
+    // an adapter update trains over >= 2 positions; a context prefill needs neither;
+    // the full-parameter gradient trains the base itself (no adapters)
+    if (mode == kFillFull) {
+        if (T < 1 || D.r != 0) return ALTXS_EINVAL;
+        if (D.d > 1024) return ALTXS_ENOTSUP;  // embedding scatter: 8 columns per thread of 128
+    } else if (T < (prefill ? 1 : 2) || D.r < (prefill ? 0 : 1) || D.r > 64) {
+        return ALTXS_EINVAL;
+    }
     if (D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
     if (D.hd > 128 || D.rd > D.hd || D.rd % 2) return ALTXS_EINVAL;
     // the window forward here is the plain GPT stack: one application per layer, no motifs
@@ -84,7 +103,9 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.hinv = take(L * T * (D.H + D.Hkv));
     t.qr = take(L * T * d);
     t.kr = take(L * T * D.kvd);
-    t.P = take(L * D.H * T * align_up(T, 8));  // fp32 [H][T][T], or bf16 hi/lo planes [2][H][T][align8(T)]
+    // fp32 [H][T][T], or bf16 hi/lo planes [2][H][T][align8(T)], per layer; one layer
+    // (recomputed in the backward) for the full-parameter gradient
+    t.P = take((D.full ? 1 : L) * D.H * T * align_up(T, 8));
     t.tq = take(L * T * D.r);
     t.tk = take(L * T * D.r);
     t.tv = take(L * T * D.r);
@@ -116,23 +137,40 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.dt = take(T * D.r);
     t.grad = nullptr;  // set by caller (lora_floats)
     t.red = take(1024);
+    if (D.full) {
+        t.xraw = take(L * T * d);
+        t.yl = take(L * T * d);
+        t.aol = take(L * T * d);
+        t.doutl = take(L * T * d);
+        t.eraw = take(T * d);
+        t.inv0 = take(T);
+        t.dx0 = take(T * d);
+        const int64_t cw = 4 * d > D.H ? 4 * d : D.H;
+        t.colbuf = take(T * cw);
+        t.cpart = take((int64_t)kColChunks * cw);
+    }
     if (tp) *tp = t;
     return off;
 }
 
 // ---- forward row kernels -------------------------------------------------
 
-__global__ void t_embed(TD D, const int32_t *tok, altxs_qmat emb, float *x0, float *x) {
+// embedding rows (dense fp32 copy when given, else the mixed-bit codes) + RMSNorm;
+// the full-parameter gradient keeps the raw rows and their inverse rms
+__global__ void t_embed(TD D, const int32_t *tok, altxs_qmat emb, const float *embd, float *x0, float *x, Tape tp) {
     __shared__ float red[32];
     const int t = blockIdx.x;
     const int tk = tok[t];
     float ss = 0.0f;
     for (int k = threadIdx.x; k < D.d; k += blockDim.x) {
-        const float v = (tk >= 0 && tk < D.V) ? qmat_elem(emb, tk, k) : 0.0f;
+        float v = 0.0f;
+        if (tk >= 0 && tk < D.V) v = embd ? embd[(int64_t)tk * D.d + k] : qmat_elem(emb, tk, k);
         x0[(int64_t)t * D.d + k] = v;
+        if (tp.eraw) tp.eraw[(int64_t)t * D.d + k] = v;
         ss = __fmaf_rn(v, v, ss);
     }
     const float inv = rms_inv(block_sum(ss, red), D.d);
+    if (tp.inv0 && threadIdx.x == 0) tp.inv0[t] = inv;
     __syncthreads();
     for (int k = threadIdx.x; k < D.d; k += blockDim.x) {
         const float v = __fmul_rn(x0[(int64_t)t * D.d + k], inv);
@@ -151,9 +189,11 @@ __global__ void t_prenorm(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
     const bool skip = j >= 0 && j < D.nskip;
     const float *sk = skip ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
     float *xin = tp.xin + ((int64_t)l * D.T + t) * d;
+    float *xr = tp.xraw ? tp.xraw + ((int64_t)l * D.T + t) * d : nullptr;
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
         float xv = x[k];
+        if (xr) xr[k] = xv;
         if (skip) {
             const float scaled = __fmul_rn(w.skip_weights[(int64_t)j * d + k], sk[k]);
             xv = skip_gates ? lerp_t(scaled, xv, sigmoidf_(w.skip_gates[(int64_t)j * d + k])) : __fadd_rn(xv, scaled);
@@ -228,11 +268,11 @@ __global__ void t_softmax(TD D, float *P) {
     for (int j = threadIdx.x; j < D.T; j += blockDim.x) s[j] = __fmul_rn(s[j], inv);
 }
 
-__global__ void t_post_attn(TD D, int l, Tape tp, altxs_weights w) {
+__global__ void t_post_attn(TD D, int l, Tape tp, altxs_weights w, const float *aob) {
     __shared__ float red[32];
     const int t = blockIdx.x, d = D.d;
     const float *xin = tp.xin + ((int64_t)l * D.T + t) * d;
-    const float *ao = tp.ao + (int64_t)t * d;
+    const float *ao = aob + (int64_t)t * d;
     const float *as = w.attn_scale + (int64_t)l * d;
     float *xm = tp.xmid + ((int64_t)l * D.T + t) * d;
     float ss = 0.0f;
@@ -273,6 +313,11 @@ __global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap) {
     __shared__ float red[32];
     const int t = blockIdx.x;
     float *l = tp.logits + (int64_t)t * D.V;
+    if (t < D.first) {  // context row: not scored
+        for (int j = threadIdx.x; j < D.V; j += blockDim.x) l[j] = 0.0f;
+        if (threadIdx.x == 0) tp.rowloss[t] = 0.0f;
+        return;
+    }
     const int y = tgt[t];
     float m = -INFINITY;
     for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
@@ -289,7 +334,7 @@ __global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap) {
     s = block_sum(s, red);
     __syncthreads();
     const float lse = __fadd_rn(m, logf(s));
-    const float invT = __fdiv_rn(1.0f, (float)D.T);
+    const float invT = __fdiv_rn(1.0f, (float)(D.T - D.first));
     for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
         const float th = tanhf(__fdiv_rn(l[j], cap));
         const float z = __fmul_rn(cap, th);
@@ -300,12 +345,13 @@ __global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap) {
     }
 }
 
-__global__ void t_loss_sum(int T, const float *rowloss, float *out) {
+// mean of the scored rows' losses (rows before `first` hold 0)
+__global__ void t_loss_sum(int T, int first, const float *rowloss, float *out) {
     __shared__ float red[32];
     float s = 0.0f;
     for (int t = threadIdx.x; t < T; t += blockDim.x) s = __fadd_rn(s, rowloss[t]);
     s = block_sum(s, red);
-    if (threadIdx.x == 0 && out) *out = __fdiv_rn(s, (float)T);
+    if (threadIdx.x == 0 && out) *out = __fdiv_rn(s, (float)(T - first));
 }
 
 // ---- backward row kernels -----------------------------------------------
@@ -458,6 +504,22 @@ __global__ void t_qk_bwd(TD D, int l, Tape tp, altxs_weights w) {
             ga[u] = v;
         }
         dot = warp_sum(dot);
+        if (D.full && h < D.H) {  // d q_gain[h] = sum_k dout_k * (roped, normed q)_k
+            float gd = 0.0f;
+            for (int k = lane; k < hd; k += 32) {
+                const float a = __fmul_rn(e[k], inv);
+                float r = a;
+                if (k < D.rd) {
+                    if (k < half)
+                        r = __fadd_rn(__fmul_rn(a, cs[k]), __fmul_rn(__fmul_rn(e[k + half], inv), sn[k]));
+                    else
+                        r = __fadd_rn(__fmul_rn(__fmul_rn(e[k - half], inv), -sn[k - half]), __fmul_rn(a, cs[k - half]));
+                }
+                gd = __fmaf_rn(gsrc[k], r, gd);
+            }
+            gd = warp_sum(gd);
+            if (lane == 0) tp.colbuf[(int64_t)t * D.H + h] = gd;
+        }
         const float c = __fdiv_rn(__fmul_rn(__fmul_rn(inv, inv), __fmul_rn(inv, dot)), (float)hd);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -467,7 +529,10 @@ __global__ void t_qk_bwd(TD D, int l, Tape tp, altxs_weights w) {
     }
 }
 
-// residual mix and skip lerp backward: dx <- d(loss)/d(layer input)
+// residual mix and skip lerp backward: dx <- d(loss)/d(layer input).  The
+// full-parameter gradient also adds mix1 * d(x_in) into d(x0) and leaves per-row
+// products for the column sums: [0,d) d(mix0), [d,2d) d(mix1), [2d,3d)
+// d(skip_weights), [3d,4d) d(skip_gates).
 __global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates) {
     const int t = blockIdx.x, d = D.d;
     const float *mix = w.resid_mix + (int64_t)l * 2 * d;
@@ -475,7 +540,37 @@ __global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
     const bool skip = j >= 0 && j < D.nskip;
     float *dx = tp.dx + (int64_t)t * d;
     float *ds = skip ? tp.dskip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
+    const float *sk = skip ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        if (D.full) {
+            const float gin = dx[k];
+            const float xr = tp.xraw[((int64_t)l * D.T + t) * d + k];
+            float xv = xr, scaled = 0.0f, gg = 0.0f;
+            if (skip) {
+                scaled = __fmul_rn(w.skip_weights[(int64_t)j * d + k], sk[k]);
+                if (skip_gates) {
+                    gg = sigmoidf_(w.skip_gates[(int64_t)j * d + k]);
+                    xv = lerp_t(scaled, xr, gg);
+                } else {
+                    xv = __fadd_rn(xr, scaled);
+                }
+            }
+            float *cb = tp.colbuf + (int64_t)t * 4 * d;
+            cb[k] = __fmul_rn(gin, xv);
+            cb[d + k] = __fmul_rn(gin, tp.x0[(int64_t)t * d + k]);
+            float *g0 = tp.dx0 + (int64_t)t * d + k;
+            *g0 = __fadd_rn(*g0, __fmul_rn(mix[d + k], gin));
+            if (skip) {
+                const float gv = __fmul_rn(gin, mix[k]);
+                if (skip_gates) {
+                    cb[2 * d + k] = __fmul_rn(__fmul_rn(gv, __fsub_rn(1.0f, gg)), sk[k]);
+                    cb[3 * d + k] = __fmul_rn(__fmul_rn(gv, __fsub_rn(xr, scaled)), __fmul_rn(gg, __fsub_rn(1.0f, gg)));
+                } else {
+                    cb[2 * d + k] = __fmul_rn(gv, sk[k]);
+                    cb[3 * d + k] = 0.0f;
+                }
+            }
+        }
         const float gx = __fmul_rn(dx[k], mix[k]);
         if (skip) {
             const float sw = w.skip_weights[(int64_t)j * d + k];
@@ -496,6 +591,77 @@ __global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
 __global__ void t_add(int64_t n, float *a, const float *b) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) a[i] = __fadd_rn(a[i], b[i]);
+}
+
+// Column sums over rows t < T of A[t][c] (times B[t][c] when B is given), in a
+// fixed order: each of the gridDim.y row chunks sums its rows in order, then
+// t_colsum_fin adds the chunk partials in order.
+__global__ void t_colsum_part(int T, int ncol, const float *A, int64_t lda, const float *B, int64_t ldb,
+                              float *part) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= ncol) return;
+    const int per = (T + gridDim.y - 1) / gridDim.y;
+    const int t0 = blockIdx.y * per, t1 = t0 + per < T ? t0 + per : T;
+    float s = 0.0f;
+    for (int t = t0; t < t1; ++t)
+        s = B ? __fmaf_rn(A[(int64_t)t * lda + c], B[(int64_t)t * ldb + c], s) : __fadd_rn(s, A[(int64_t)t * lda + c]);
+    part[(int64_t)blockIdx.y * ncol + c] = s;
+}
+__global__ void t_colsum_fin(int ncol, int nch, const float *part, float *out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= ncol) return;
+    float s = 0.0f;
+    for (int i = 0; i < nch; ++i) s = __fadd_rn(s, part[(int64_t)i * ncol + c]);
+    out[c] = s;
+}
+
+// Input-embedding gradient of the tied table: gemb[v] += sum over positions t
+// with tok[t] == v of draw[t], in increasing t.  Each warp finds the matching
+// positions 32 at a time with a ballot; thread k owns columns k, k+128, ..
+// (d <= 1024, 128 threads).
+__global__ void __launch_bounds__(128) t_emb_scatter(int T, int d, int V, const int32_t *tok, const float *draw,
+                                                     float *gemb) {
+    constexpr unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    for (int v = blockIdx.x; v < V; v += gridDim.x) {
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
+        bool hit = false;
+        for (int base = 0; base < T; base += 32) {
+            const int t = base + lane;
+            unsigned m = __ballot_sync(FULL, t < T && tok[t] == v);
+            hit |= m != 0u;
+            while (m) {
+                const int b = __ffs(m) - 1;
+                m &= m - 1u;
+                const float *row = draw + (int64_t)(base + b) * d;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int k = threadIdx.x + 128 * u;
+                    if (k < d) acc[u] = __fadd_rn(acc[u], row[k]);
+                }
+            }
+        }
+        if (hit) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int k = threadIdx.x + 128 * u;
+                if (k < d) gemb[(int64_t)v * d + k] = __fadd_rn(gemb[(int64_t)v * d + k], acc[u]);
+            }
+        }
+    }
+}
+
+// out = a + s * b (two roundings, as the reference's w + s * dw)
+__global__ void t_axpy(int64_t n, const float *a, float s, const float *b, float *out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = __fadd_rn(a[i], __fmul_rn(s, b[i]));
+}
+// p -= (p - w0) * pull
+__global__ void t_anchor(int64_t n, float *p, const float *w0, const float *pull) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = __fsub_rn(p[i], __fmul_rn(__fsub_rn(p[i], w0[i]), pull[i]));
 }
 
 // global grad norm: partial sums over fixed chunks, then a single-block sum
@@ -558,8 +724,12 @@ struct Run {
     const altxs_split_planes *sp;
     uint16_t *tca, *tcb;
     int64_t tca_n, tcb_n;
-    bool no_lora;  // context prefill of a model without adapters
+    bool no_lora;  // context prefill of a model without adapters, or the full-parameter gradient
     cudaStream_t st;
+    // full-parameter gradient: the window's tokens, the gradient arena and its layout
+    const int32_t *tok;
+    float *fg;
+    altxs_param_layout lay;
 };
 
 // Batched/causal GEMMs of the update: tensor cores when the model carries
@@ -704,6 +874,7 @@ int lora_fwd(const Run &R, const float *X, int din, const float *A, const float 
 // LoRA backward: grads dA, dB (written), dX += dt A (if dX)
 int lora_bwd(const Run &R, const float *X, int din, const float *A, const float *B, int dout, float s,
              const float *t, const float *Gy, int64_t ldg, float *dA, float *dB, float *dX) {
+    if (R.no_lora) return ALTXS_OK;
     const int T = R.D.T, r = R.D.r;
     float *dt = R.tp.dt;
     TRY(launch_gemm(G(R, Gy, ldg, 1, t, r, 0, dB, r, dout, r, T, s), R.st));  // dB = s G^T t
@@ -716,6 +887,41 @@ int lora_bwd(const Run &R, const float *X, int din, const float *A, const float 
 // the weight planes of matrix field f (NULL on the CUDA-core path)
 #define PL(f) (R.sp ? R.sp->f : nullptr)
 
+// attention probabilities of layer l (causal softmax of q k^T / sqrt(hd)): fp32
+// [H][T][T], or hi/lo planes [2][H][T][align8(T)] on the tensor-core path.  The
+// full-parameter gradient keeps one layer's worth and recomputes it in the backward.
+float *p_f32(const Run &R, int l) {
+    return R.tp.P + (R.D.full ? 0 : (int64_t)l * R.D.H * R.D.T * R.D.T);
+}
+uint16_t *p_planes(const Run &R, int l) {
+    return reinterpret_cast<uint16_t *>(R.tp.P + (R.D.full ? 0 : (int64_t)l * R.D.H * R.D.T * align_up(R.D.T, 8)));
+}
+int attn_probs(const Run &R, int l) {
+    const TD &D = R.D;
+    const Tape &tp = R.tp;
+    const int Tn = D.T, d = D.d;
+    cudaStream_t st = R.st;
+    const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
+    const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+    const int64_t ldp = align_up(Tn, 8);
+    float *S = R.sp ? tp.dS : p_f32(R, l);  // tensor cores: S in fp32 scratch, P leaves as planes
+    GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, S, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
+    g.batch = D.H;
+    g.sA = D.hd;
+    g.sB = D.hd;
+    g.bdiv = D.G;
+    g.sC = (int64_t)Tn * Tn;
+    g.causal = 1;
+    TRY(gemm(R, g));
+    if (R.sp) {
+        uint16_t *Ph = p_planes(R, l), *Pl = Ph + D.H * Tn * ldp;
+        ALTXS_LAUNCH(kKTtt, st, t_softmax_pl<<<D.H * Tn, 256, 0, st>>>(D, tp.dS, Ph, Pl, ldp));
+    } else {
+        ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, S));
+    }
+    return ALTXS_OK;
+}
+
 int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out,
             bool head = true) {
     const TD &D = R.D;
@@ -726,9 +932,8 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
     const int mask = R.desc->lora_mask;
     const float s = R.desc->lora_scale;
     const int Tn = D.T, d = D.d, r = D.r;
-    const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
     cudaStream_t st = R.st;
-    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, tp.x0, tp.x));
+    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, dw ? dw->emb : w->emb_dense, tp.x0, tp.x, tp));
     for (int l = 0; l < D.L; ++l) {
         ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
         const float *n = tp.n + (int64_t)l * Tn * d;
@@ -742,34 +947,18 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         TRY(lora_fwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
                      tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
         ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, tp, *w));
-        float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
-        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        TRY(attn_probs(R, l));
+        // the full-parameter gradient keeps every layer's attention output and projections
+        float *yb = D.full ? tp.yl + (int64_t)l * Tn * d : tp.y;
+        float *aob = D.full ? tp.aol + (int64_t)l * Tn * d : tp.ao;
         const int64_t ldp = align_up(Tn, 8);
-        uint16_t *Ph = reinterpret_cast<uint16_t *>(tp.P + (int64_t)l * D.H * Tn * ldp), *Pl = Ph + D.H * Tn * ldp;
-        if (R.sp) {  // tensor cores: S in fp32 scratch, P kept as planes for y = P v and the backward
-            GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, tp.dS, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
-            g.batch = D.H;
-            g.sA = D.hd;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = (int64_t)Tn * Tn;
-            g.causal = 1;
-            TRY(gemm(R, g));
-            ALTXS_LAUNCH(kKTtt, st, t_softmax_pl<<<D.H * Tn, 256, 0, st>>>(D, tp.dS, Ph, Pl, ldp));
+        if (R.sp) {
+            const uint16_t *Ph = p_planes(R, l), *Pl = Ph + D.H * Tn * ldp;
             TcOp a{Ph, Pl, 0, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, 1, 0}, b{};
             TRY(split_b(R, qkv + d + D.kvd, Tn, D.hd, D.qn, D.Hkv, D.hd, 1, D.G, 1, 0, b));  // v, [n=c][k=t']
-            TRY(tc_att(R, a, b, Tn, D.hd, Tn, D.H, 2, 0.0f, tp.y, d, D.hd));                 // y = P v
+            TRY(tc_att(R, a, b, Tn, D.hd, Tn, D.H, 2, 0.0f, yb, d, D.hd));                   // y = P v
         } else {
-            GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, P, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
-            g.batch = D.H;
-            g.sA = D.hd;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = (int64_t)Tn * Tn;
-            g.causal = 1;
-            TRY(gemm(R, g));
-            ALTXS_LAUNCH(kKTtt, st, t_softmax<<<D.H * Tn, 256, 0, st>>>(D, P));
-            g = G(R, P, Tn, 0, qkv + d + D.kvd, D.qn, 0, tp.y, d, Tn, D.hd, Tn);  // y = P v
+            GemmArgs g = G(R, p_f32(R, l), Tn, 0, qkv + d + D.kvd, D.qn, 0, yb, d, Tn, D.hd, Tn);  // y = P v
             g.batch = D.H;
             g.sA = (int64_t)Tn * Tn;
             g.sB = D.hd;
@@ -778,20 +967,21 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             g.causal = 2;
             TRY(gemm(R, g));
         }
-        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, tp.y, d, tp.ao, d));
+        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, yb, d, aob, d));
         if (mask & 8)
             TRY(lora_fwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
-                         tp.to + (int64_t)l * Tn * r, tp.ao, d));
-        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w));
+                         tp.to + (int64_t)l * Tn * r, aob, d));
+        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w, aob));
         float *u = tp.u + (int64_t)l * Tn * D.F;
         TRY(lin_fwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), l * D.F, D.F, d, tp.n2 + (int64_t)l * Tn * d, d, u, D.F));
         ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
         float *sk = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
         const float *xm = tp.xmid + (int64_t)l * Tn * d;
         if (dw || R.sp) {
-            TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.hbuf, D.F, tp.dd, d));
+            float *db = D.full ? tp.doutl + (int64_t)l * Tn * d : tp.dd;
+            TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.hbuf, D.F, db, d));
             ALTXS_LAUNCH(kKTtt, st, t_resid<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                        (int64_t)Tn * d, d, xm, w->mlp_scale + (int64_t)l * d, tp.dd, tp.x, sk));
+                                        (int64_t)Tn * d, d, xm, w->mlp_scale + (int64_t)l * d, db, tp.x, sk));
         } else {
             QmmArgs a{};
             a.X = tp.hbuf;
@@ -817,10 +1007,12 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
     TRY(lin_fwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.hf, d, tp.logits, D.V));
     if (mask & 16) TRY(lora_fwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V));
     ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, R.desc->logit_softcap));
-    ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, tp.rowloss, loss_out));
+    ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, D.first, tp.rowloss, loss_out));
     return ALTXS_OK;
 }
 
+// Backward of the window loss: into the adapters (grad in the LoRA arena
+// layout), or with R.fg into every parameter (the full arena layout R.lay).
 int backward(const Run &R, const float *lora, float *grad) {
     const TD &D = R.D;
     const Tape &tp = R.tp;
@@ -832,6 +1024,24 @@ int backward(const Run &R, const float *lora, float *grad) {
     const int Tn = D.T, d = D.d, r = D.r;
     const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
     cudaStream_t st = R.st;
+    const bool full = D.full;
+    float *FG = R.fg;
+    const altxs_param_layout &lay = R.lay;
+    // out[c] = sum over rows of A[t][c] (* B[t][c])
+    auto colsum = [&](const float *A, int64_t lda, const float *B, int64_t ldb, int ncol, float *out) -> int {
+        ALTXS_LAUNCH(kKTtt, st, t_colsum_part<<<dim3(g1(ncol, 128), kColChunks), 128, 0, st>>>(Tn, ncol, A, lda, B,
+                                                                                                 ldb, tp.cpart));
+        ALTXS_LAUNCH(kKTtt, st, t_colsum_fin<<<g1(ncol, 128), 128, 0, st>>>(ncol, kColChunks, tp.cpart, out));
+        return ALTXS_OK;
+    };
+    // weight gradient out[N][K] = dY^T X (dY [T][N], X [T][K]): the reduction runs over positions
+    auto wgrad = [&](const float *dY, int N, const float *X, int K, float *out) -> int {
+        return gemm(R, G(R, dY, N, 1, X, K, 0, out, K, N, K, Tn));
+    };
+    if (full) {
+        cudaMemsetAsync(tp.dx0, 0, (size_t)Tn * d * 4, st);
+        TRY(wgrad(tp.logits, D.V, tp.hf, d, FG + lay.emb));  // the tied table as the LM head
+    }
     // LM head: dhf = dlogits E (+ LoRA)
     TRY(lin_bwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.logits, D.V, tp.dn, d, 0.0f));
     if (mask & 16)
@@ -845,13 +1055,21 @@ int backward(const Run &R, const float *lora, float *grad) {
         // MLP
         ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
                                     (int64_t)Tn * d, d, tp.dx, w->mlp_scale + (int64_t)l * d, tp.dd));
+        if (full) {
+            TRY(colsum(tp.dx, d, tp.doutl + (int64_t)l * Tn * d, d, d, FG + lay.mlp_scale + (int64_t)l * d));
+            ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
+                                        (int64_t)Tn * D.F, tp.u + (int64_t)l * Tn * D.F, tp.hbuf));
+            TRY(wgrad(tp.dd, d, tp.hbuf, D.F, FG + lay.down + (int64_t)l * d * D.F));
+        }
         TRY(lin_bwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.dd, d, tp.dh, D.F, 0.0f));
         ALTXS_LAUNCH(kKTtt, st, t_leaky_bwd<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
                                     (int64_t)Tn * D.F, tp.dh, tp.u + (int64_t)l * Tn * D.F, tp.dh));
+        if (full) TRY(wgrad(tp.dh, D.F, tp.n2 + (int64_t)l * Tn * d, d, FG + lay.up + (int64_t)l * D.F * d));
         TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), l * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
         ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Tn * d,
                                                              tp.inv2 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
                                                              tp.dx));
+        if (full) TRY(colsum(tp.dx, d, tp.aol + (int64_t)l * Tn * d, d, d, FG + lay.attn_scale + (int64_t)l * d));
         ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
                                     (int64_t)Tn * d, d, tp.dx, w->attn_scale + (int64_t)l * d, tp.dao));
         const float *n = tp.n + (int64_t)l * Tn * d;
@@ -860,14 +1078,16 @@ int backward(const Run &R, const float *lora, float *grad) {
             TRY(lora_bwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
                          grad + lo.oB + l * lo.o_stride, tp.dn));
+        if (full) TRY(wgrad(tp.dao, d, tp.yl + (int64_t)l * Tn * d, d, FG + lay.o + (int64_t)l * d * d));
         TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
         // attention backward
-        const float *P = tp.P + (int64_t)l * D.H * Tn * Tn;
+        if (full) TRY(attn_probs(R, l));
+        const float *P = p_f32(R, l);
         const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
         const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
         if (R.sp) {  // tensor cores: P and dS as planes, K-major or read transposed (MN-major)
             const int64_t ldp = align_up(Tn, 8);
-            const uint16_t *Ph = reinterpret_cast<const uint16_t *>(tp.P + (int64_t)l * D.H * Tn * ldp);
+            const uint16_t *Ph = p_planes(R, l);
             const uint16_t *Pl = Ph + D.H * Tn * ldp;
             GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
             g.batch = D.H;
@@ -899,49 +1119,50 @@ int backward(const Run &R, const float *lora, float *grad) {
                            gi ? 1.0f : 0.0f, tp.dkr, D.kvd, D.hd));
             }
         } else {
-        {
-            GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
-            g.batch = D.H;
-            g.sA = D.hd;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = (int64_t)Tn * Tn;
-            g.causal = 1;
-            TRY(gemm(R, g));
-        }
-        for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
-            GemmArgs g = G(R, P + (int64_t)gi * Tn * Tn, Tn, 1, tp.dy + gi * D.hd, d, 0, tp.dqkv + d + D.kvd,
-                           D.qn, Tn, D.hd, Tn, 1.0f, gi ? 1.0f : 0.0f);
-            g.batch = D.Hkv;
-            g.sA = (int64_t)D.G * Tn * Tn;
-            g.sB = (int64_t)D.G * D.hd;
-            g.sC = D.hd;
-            g.causal = 3;
-            TRY(gemm(R, g));
-        }
-        ALTXS_LAUNCH(kKTtt, st, t_softmax_bwd<<<D.H * Tn, 256, 0, st>>>(D, P, tp.dS, att_scale));
-        {
-            GemmArgs g = G(R, tp.dS, Tn, 0, kr, D.kvd, 0, tp.dqr, d, Tn, D.hd, Tn);  // dq = dS k
-            g.batch = D.H;
-            g.sA = (int64_t)Tn * Tn;
-            g.sB = D.hd;
-            g.bdiv = D.G;
-            g.sC = D.hd;
-            g.causal = 2;
-            TRY(gemm(R, g));
-        }
-        for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
-            GemmArgs g = G(R, tp.dS + (int64_t)gi * Tn * Tn, Tn, 1, qr + gi * D.hd, d, 0, tp.dkr, D.kvd, Tn, D.hd,
-                           Tn, 1.0f, gi ? 1.0f : 0.0f);
-            g.batch = D.Hkv;
-            g.sA = (int64_t)D.G * Tn * Tn;
-            g.sB = (int64_t)D.G * D.hd;
-            g.sC = D.hd;
-            g.causal = 3;
-            TRY(gemm(R, g));
-        }
+            {
+                GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
+                g.batch = D.H;
+                g.sA = D.hd;
+                g.sB = D.hd;
+                g.bdiv = D.G;
+                g.sC = (int64_t)Tn * Tn;
+                g.causal = 1;
+                TRY(gemm(R, g));
+            }
+            for (int gi = 0; gi < D.G; ++gi) {  // dv = sum over the group's heads of P^T dy
+                GemmArgs g = G(R, P + (int64_t)gi * Tn * Tn, Tn, 1, tp.dy + gi * D.hd, d, 0, tp.dqkv + d + D.kvd,
+                               D.qn, Tn, D.hd, Tn, 1.0f, gi ? 1.0f : 0.0f);
+                g.batch = D.Hkv;
+                g.sA = (int64_t)D.G * Tn * Tn;
+                g.sB = (int64_t)D.G * D.hd;
+                g.sC = D.hd;
+                g.causal = 3;
+                TRY(gemm(R, g));
+            }
+            ALTXS_LAUNCH(kKTtt, st, t_softmax_bwd<<<D.H * Tn, 256, 0, st>>>(D, P, tp.dS, att_scale));
+            {
+                GemmArgs g = G(R, tp.dS, Tn, 0, kr, D.kvd, 0, tp.dqr, d, Tn, D.hd, Tn);  // dq = dS k
+                g.batch = D.H;
+                g.sA = (int64_t)Tn * Tn;
+                g.sB = D.hd;
+                g.bdiv = D.G;
+                g.sC = D.hd;
+                g.causal = 2;
+                TRY(gemm(R, g));
+            }
+            for (int gi = 0; gi < D.G; ++gi) {  // dk = sum over the group's heads of dS^T q
+                GemmArgs g = G(R, tp.dS + (int64_t)gi * Tn * Tn, Tn, 1, qr + gi * D.hd, d, 0, tp.dkr, D.kvd, Tn, D.hd,
+                               Tn, 1.0f, gi ? 1.0f : 0.0f);
+                g.batch = D.Hkv;
+                g.sA = (int64_t)D.G * Tn * Tn;
+                g.sB = (int64_t)D.G * D.hd;
+                g.sC = D.hd;
+                g.causal = 3;
+                TRY(gemm(R, g));
+            }
         }
         ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, tp, *w));
+        if (full) TRY(colsum(tp.colbuf, D.H, nullptr, 0, D.H, FG + lay.q_gain + (int64_t)l * D.H));
         TRY(lora_bwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
                      tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, grad + lo.qA + l * lo.q_stride,
                      grad + lo.qB + l * lo.q_stride, tp.dn));
@@ -952,11 +1173,26 @@ int backward(const Run &R, const float *lora, float *grad) {
         TRY(lora_bwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
                      tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, grad + lo.vA + l * lo.v_stride,
                      grad + lo.vB + l * lo.v_stride, tp.dn));
+        if (full) TRY(wgrad(tp.dqkv, D.qn, n, d, FG + lay.qkv + (int64_t)l * D.qn * d));
         TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), l * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
         ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Tn * d,
                                                              tp.inv1 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
                                                              tp.dx));
         ALTXS_LAUNCH(kKTtt, st, t_mix_bwd<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
+        if (full) {
+            TRY(colsum(tp.colbuf, 4 * d, nullptr, 0, 2 * d, FG + lay.resid_mix + (int64_t)l * 2 * d));
+            const int j = l - D.enc;
+            if (j >= 0 && j < D.nskip) {
+                TRY(colsum(tp.colbuf + 2 * d, 4 * d, nullptr, 0, d, FG + lay.skip_weights + (int64_t)j * d));
+                TRY(colsum(tp.colbuf + 3 * d, 4 * d, nullptr, 0, d, FG + lay.skip_gates + (int64_t)j * d));
+            }
+        }
+    }
+    if (full) {  // embedding: d(x0) over every use, through x0 = rms(raw), into the rows of the tied table
+        ALTXS_LAUNCH(kKTtt, st, t_add<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>((int64_t)Tn * d, tp.dx0, tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dx0, d, tp.eraw, tp.inv0, nullptr, nullptr, tp.dn));
+        ALTXS_LAUNCH(kKTtt, st, t_emb_scatter<<<D.V < 148 * 16 ? D.V : 148 * 16, 128, 0, st>>>(Tn, d, D.V, R.tok,
+                                                                                             tp.dn, FG + lay.emb));
     }
     return ALTXS_OK;
 }
@@ -973,7 +1209,36 @@ void tc_scratch(const TD &D, int64_t *a_n, int64_t *b_n) {
     a = a > T * align_up(D.F, 8) ? a : T * align_up(D.F, 8);
     a = a > T * align_up(D.qn, 8) ? a : T * align_up(D.qn, 8);
     *a_n = 2 * align_up(a, 128);
-    *b_n = 2 * align_up(T * align_up(D.hd, 8) * (D.H > D.Hkv ? D.H : D.Hkv), 128);
+    int64_t b = T * align_up(D.hd, 8) * (D.H > D.Hkv ? D.H : D.Hkv);
+    if (D.full) b = b > T * align_up(D.F, 8) ? b : T * align_up(D.F, 8);  // weight-gradient inputs [T][F]
+    *b_n = 2 * align_up(b, 128);
+}
+
+// Segments of the full parameter arena (floats, each 64-aligned).
+altxs_param_layout param_layout(const altxs_model_desc &dsc) {
+    const int64_t V = dsc.vocab, L = dsc.n_layers, d = dsc.d_model, H = dsc.n_heads, F = dsc.mlp_hidden;
+    const int64_t qn = d + 2 * (int64_t)dsc.n_kv_heads * dsc.head_dim;
+    const int64_t S = L / 2 < L - L / 2 ? L / 2 : L - L / 2;
+    altxs_param_layout o{};
+    int64_t off = 0;
+    auto seg = [&](int64_t n) {
+        const int64_t r = off;
+        off += align_up(n, 64);
+        return r;
+    };
+    o.emb = seg(V * d);
+    o.qkv = seg(L * qn * d);
+    o.o = seg(L * d * d);
+    o.up = seg(L * F * d);
+    o.down = seg(L * d * F);
+    o.q_gain = seg(L * H);
+    o.attn_scale = seg(L * d);
+    o.mlp_scale = seg(L * d);
+    o.resid_mix = seg(L * 2 * d);
+    o.skip_weights = seg(S * d);
+    o.skip_gates = seg(S * d);
+    o.total = off;
+    return o;
 }
 
 }  // namespace
@@ -996,7 +1261,7 @@ int altxs_dequant(const altxs_qmat *m, float *out, int64_t ld, altxs_stream_t st
 
 int64_t altxs_prefill_workspace_bytes(const altxs_model_desc *desc, int T) {
     TD D{};
-    if (!desc || T < 1 || fill(*desc, T, D, true)) return -1;
+    if (!desc || T < 1 || fill(*desc, T, D, kFillPrefill)) return -1;
     const int64_t lo_total = D.r > 0 ? lora_offsets(*desc).total : 1;
     int64_t a_n, b_n;
     tc_scratch(D, &a_n, &b_n);
@@ -1011,7 +1276,7 @@ int altxs_prefill(const altxs_model_desc *desc, const altxs_weights *w, const al
     if (T == 0) return ALTXS_OK;
     if (!tokens || !workspace) return ALTXS_EINVAL;
     Run R{};
-    TRY(fill(*desc, T, R.D, true));
+    TRY(fill(*desc, T, R.D, kFillPrefill));
     if (desc->ctx < 1 || w->rope_positions < T) return ALTXS_EINVAL;
     if (R.D.r > 0 && !lora) return ALTXS_EINVAL;
     if (dense && (!dense->emb || !dense->qkv || !dense->o || !dense->up || !dense->down)) return ALTXS_EINVAL;
@@ -1072,6 +1337,110 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
     ALTXS_LAUNCH(kKTtt, st, t_sqsum_part<<<nparts, 256, 0, st>>>(lo.total, grad, R.tp.red));
     ALTXS_LAUNCH(kKTtt, st, t_adam<<<g1(lo.total, 1024), 1024, 0, st>>>(lo.total, lora, grad, adam_m, adam_v,
                                                                          R.tp.red, nparts, *hp, step));
+    return ALTXS_OK;
+}
+
+int altxs_param_layout_of(const altxs_model_desc *desc, altxs_param_layout *out) {
+    TD D{};
+    if (!desc || !out) return ALTXS_EINVAL;
+    TRY(fill(*desc, 1, D, kFillFull));
+    *out = param_layout(*desc);
+    return ALTXS_OK;
+}
+
+int64_t altxs_full_workspace_bytes(const altxs_model_desc *desc, int n) {
+    TD D{};
+    if (!desc || n < 2 || fill(*desc, n - 1, D, kFillFull)) return -1;
+    int64_t a_n, b_n;
+    tc_scratch(D, &a_n, &b_n);
+    return carve(D, nullptr, nullptr) + kSplitkFloats * 4 + align_up(a_n * 2, 256) + align_up(b_n * 2, 256);
+}
+
+int altxs_full_loss_grad(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
+                         const int32_t *tokens, int n, int first, float *loss_out, float *grad, void *workspace,
+                         int64_t workspace_bytes, altxs_stream_t stream) {
+    if (!desc || !w || !dense || !tokens || !workspace || n < 2 || first < 0 || first >= n - 1) return ALTXS_EINVAL;
+    if (!dense->emb || !dense->qkv || !dense->o || !dense->up || !dense->down) return ALTXS_EINVAL;
+    Run R{};
+    TRY(fill(*desc, n - 1, R.D, kFillFull));
+    R.D.first = first;
+    if (workspace_bytes < altxs_full_workspace_bytes(desc, n)) return ALTXS_EINVAL;
+    if (w->rope_positions < n - 1) return ALTXS_EINVAL;
+    R.desc = desc;
+    R.w = w;
+    R.dw = dense;
+    R.no_lora = true;
+    R.st = reinterpret_cast<cudaStream_t>(stream);
+    R.tok = tokens;
+    R.fg = grad;
+    R.lay = param_layout(*desc);
+    const int64_t tape_bytes = carve(R.D, workspace, &R.tp);
+    R.splitk = reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) + tape_bytes);
+    R.splitk_floats = kSplitkFloats;
+    R.sp = w->split;
+    if (R.sp) {
+        tc_scratch(R.D, &R.tca_n, &R.tcb_n);
+        R.tca = reinterpret_cast<uint16_t *>(R.splitk + kSplitkFloats);
+        R.tcb = R.tca + align_up(R.tca_n, 128);
+    }
+    TRY(forward(R, tokens, tokens + 1, nullptr, loss_out));
+    if (grad) {
+        cudaMemsetAsync(grad, 0, (size_t)R.lay.total * 4, R.st);
+        TRY(backward(R, nullptr, nullptr));
+    }
+    return cudaGetLastError() == cudaSuccess ? ALTXS_OK : ALTXS_ECUDA;
+}
+
+int altxs_adamw(int64_t n, float *params, const float *grad, float *m, float *v, const altxs_ttt_hparams *hp, int step,
+                float *partials, altxs_stream_t stream) {
+    if (n < 0 || !hp || step < 1) return ALTXS_EINVAL;
+    if (n == 0) return ALTXS_OK;
+    if (!params || !grad || !m || !v || !partials) return ALTXS_EINVAL;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int nparts = 256;
+    ALTXS_LAUNCH(kKTtt, st, t_sqsum_part<<<nparts, 256, 0, st>>>(n, grad, partials));
+    const int64_t blocks = (n + 1023) / 1024;
+    ALTXS_LAUNCH(kKTtt, st, t_adam<<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), 1024, 0, st>>>(
+                                n, params, grad, m, v, partials, nparts, *hp, step));
+    return ALTXS_OK;
+}
+
+int altxs_params_axpy(int64_t n, const float *a, float s, const float *b, float *out, altxs_stream_t stream) {
+    if (n < 0 || (n && (!a || !b || !out))) return ALTXS_EINVAL;
+    if (n == 0) return ALTXS_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t blocks = (n + 255) / 256;
+    ALTXS_LAUNCH(kKTtt, st, t_axpy<<<(unsigned)(blocks < 148 * 64 ? blocks : 148 * 64), 256, 0, st>>>(n, a, s, b, out));
+    return ALTXS_OK;
+}
+
+int altxs_params_anchor(int64_t n, float *p, const float *w0, const float *pull, altxs_stream_t stream) {
+    if (n < 0 || (n && (!p || !w0 || !pull))) return ALTXS_EINVAL;
+    if (n == 0) return ALTXS_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t blocks = (n + 255) / 256;
+    ALTXS_LAUNCH(kKTtt, st, t_anchor<<<(unsigned)(blocks < 148 * 64 ? blocks : 148 * 64), 256, 0, st>>>(n, p, w0, pull));
+    return ALTXS_OK;
+}
+
+int altxs_split_params(const altxs_model_desc *desc, const float *params, const altxs_split_planes *planes,
+                       altxs_stream_t stream) {
+    TD D{};
+    if (!desc || !params || !planes) return ALTXS_EINVAL;
+    TRY(fill(*desc, 1, D, kFillFull));
+    const altxs_param_layout lay = param_layout(*desc);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    struct M {
+        int64_t off, rows, cols;
+        uint16_t *hi, *lo;
+    } ms[5] = {
+        {lay.emb, D.V, D.d, const_cast<uint16_t *>(planes->emb_hi), const_cast<uint16_t *>(planes->emb_lo)},
+        {lay.qkv, (int64_t)D.L * D.qn, D.d, const_cast<uint16_t *>(planes->qkv_hi), const_cast<uint16_t *>(planes->qkv_lo)},
+        {lay.o, (int64_t)D.L * D.d, D.d, const_cast<uint16_t *>(planes->o_hi), const_cast<uint16_t *>(planes->o_lo)},
+        {lay.up, (int64_t)D.L * D.F, D.d, const_cast<uint16_t *>(planes->up_hi), const_cast<uint16_t *>(planes->up_lo)},
+        {lay.down, (int64_t)D.L * D.d, D.F, const_cast<uint16_t *>(planes->down_hi), const_cast<uint16_t *>(planes->down_lo)},
+    };
+    for (const M &m : ms) TRY(launch_split_f32(params + m.off, m.rows, m.cols, m.cols, 1, 0, m.hi, m.lo, st, kKTtt));
     return ALTXS_OK;
 }
 

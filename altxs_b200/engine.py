@@ -64,7 +64,12 @@ class DeviceModel:
     """
 
     def __init__(self, weights: ModelWeights, device: torch.device | str, *, rope_positions: int = 1 << 16,
-                 tensor_cores: bool = True):
+                 tensor_cores: bool = True, full_params: bool = False):
+        """``full_params=True`` keeps every parameter in one fp32 arena
+        (``self.params``, layout ``self.layout``) that the step reads — the
+        embedding rows, the small parameters and the tensor-core planes
+        (re-split by ``refresh()``) — so that a full-parameter update
+        (``replenish.ReplenishTTT``) can change the model between segments."""
         self.cfg = cfg = weights.cfg
         cfg.validate()
         self.device = device = torch.device(device)
@@ -120,7 +125,55 @@ class DeviceModel:
         )
         self.lora_floats = int(_lib.lib().altxs_lora_floats(C.byref(self.desc)))
         self.tensor_cores = bool(tensor_cores)
+        self.full_params = bool(full_params)
+        self.params = None
+        if self.full_params:
+            self._build_arena()
         self._split = self._split_planes() if self.tensor_cores else None
+
+    def _build_arena(self) -> None:
+        """Every parameter in one device arena: the five matrices dequantised
+        exactly, the small parameters copied; ``small`` then views the arena."""
+        L = _lib.lib()
+        lay = _lib.ParamLayout()
+        _lib.check(L.altxs_param_layout_of(C.byref(self.desc), C.byref(lay)), "altxs_param_layout_of")
+        self.layout = lay
+        self.params = torch.zeros(lay.total, dtype=torch.float32, device=self.device)
+        base = self.params.data_ptr()
+        st = _stream_handle(self.device)
+        for name in ("emb", "qkv", "o", "up", "down"):
+            q = self.q[name]
+            _lib.check(L.altxs_dequant(C.byref(q), base + 4 * getattr(lay, name), q.cols, st), "altxs_dequant")
+        for name in ("q_gain", "attn_scale", "mlp_scale", "resid_mix", "skip_weights", "skip_gates"):
+            src = self.small[name].reshape(-1)
+            off = getattr(lay, name)
+            if name.startswith("skip") and not self.cfg.num_skip_weights:
+                continue
+            view = self.params[off: off + src.numel()]
+            view.copy_(src)
+            self.small[name] = view
+        self._weights_struct = None
+
+    def arena(self, name: str) -> torch.Tensor:
+        """The segment ``name`` of the parameter arena (a view)."""
+        lay, cfg = self.layout, self.cfg
+        sizes = {"emb": cfg.vocab_size * cfg.model_dim,
+                 "qkv": cfg.num_layers * (cfg.model_dim + 2 * cfg.kv_dim) * cfg.model_dim,
+                 "o": cfg.num_layers * cfg.model_dim ** 2, "up": cfg.num_layers * cfg.mlp_hidden * cfg.model_dim,
+                 "down": cfg.num_layers * cfg.model_dim * cfg.mlp_hidden, "q_gain": cfg.num_layers * cfg.num_heads,
+                 "attn_scale": cfg.num_layers * cfg.model_dim, "mlp_scale": cfg.num_layers * cfg.model_dim,
+                 "resid_mix": cfg.num_layers * 2 * cfg.model_dim,
+                 "skip_weights": cfg.num_skip_weights * cfg.model_dim,
+                 "skip_gates": cfg.num_skip_weights * cfg.model_dim}
+        off = getattr(lay, name)
+        return self.params[off: off + sizes[name]]
+
+    def refresh(self) -> None:
+        """After the arena changed: rewrite the step's tensor-core planes."""
+        if self.full_params and self._split is not None:
+            _lib.check(_lib.lib().altxs_split_params(C.byref(self.desc), self.params.data_ptr(),
+                                                     C.byref(self._split), _stream_handle(self.device)),
+                       "altxs_split_params")
 
     def _up(self, a: np.ndarray) -> torch.Tensor:
         t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
@@ -148,11 +201,16 @@ class DeviceModel:
             q = self.q[name]
             hi = torch.empty((q.rows, q.cols), dtype=torch.bfloat16, device=self.device)
             lo = torch.empty_like(hi)
-            _lib.check(L.altxs_split_weights(C.byref(q), hi.data_ptr(), lo.data_ptr(), _stream_handle(self.device)),
-                       "altxs_split_weights")
+            if not self.full_params:
+                _lib.check(L.altxs_split_weights(C.byref(q), hi.data_ptr(), lo.data_ptr(),
+                                                 _stream_handle(self.device)), "altxs_split_weights")
             self._split_bufs += [hi, lo]
             fields[f"{name}_hi"], fields[f"{name}_lo"] = hi.data_ptr(), lo.data_ptr()
-        return _lib.SplitPlanes(**fields)
+        planes = _lib.SplitPlanes(**fields)
+        if self.full_params:
+            _lib.check(L.altxs_split_params(C.byref(self.desc), self.params.data_ptr(), C.byref(planes),
+                                            _stream_handle(self.device)), "altxs_split_params")
+        return planes
 
     def ensure_rope(self, n_pos: int) -> None:
         """RoPE tables must cover every absolute position a stream reaches."""
@@ -168,6 +226,9 @@ class DeviceModel:
     def dense_weights(self) -> _lib.DenseWeights:
         """Dense fp32 copies of the frozen base for the test-time update
         (built once on first use, exact values; 4 bytes per weight)."""
+        if getattr(self, "_dense", None) is None and self.full_params:
+            base, lay = self.params.data_ptr(), self.layout
+            self._dense = _lib.DenseWeights(**{k: base + 4 * getattr(lay, k) for k in ("emb", "qkv", "o", "up", "down")})
         if getattr(self, "_dense", None) is None:
             L = _lib.lib()
             bufs = {}
@@ -195,6 +256,7 @@ class DeviceModel:
                 split=C.pointer(self._split) if self._split is not None else None,
                 **{k: s[k].data_ptr() for k in ("smear_gate", "smear_lambda", "attn_gate_w", "softcap",
                                                 "parallel_post", "parallel_resid") if k in s},
+                emb_dense=self.params.data_ptr() + 4 * self.layout.emb if self.full_params else None,
             )
         return self._weights_struct
 
@@ -487,7 +549,26 @@ class Engine:
         return StreamBatch(self.dm, n, words_per_stream=words_for_segment(cfg.online_retrain_every, cfg.cdf_bits),
                            hist_len=hist)
 
+    def _per_stream(self) -> bool:
+        """A full-parameter update changes the model itself: one stream at a time."""
+        return bool(getattr(self.ttt, "per_stream_model", False))
+
+    def _update(self, b: StreamBatch, rows, t: int, prefix: torch.Tensor) -> None:
+        if getattr(self.ttt, "needs_prefix", False):
+            self.ttt(b, rows, t, prefix=prefix)
+        else:
+            self.ttt(b, rows, t)
+
     def encode(self, streams: list[np.ndarray]) -> list[StreamResult]:
+        if self._per_stream():
+            out = []
+            for s in streams:
+                self.ttt.reset()
+                out += self._encode(list([s]))
+            return out
+        return self._encode(streams)
+
+    def _encode(self, streams: list[np.ndarray]) -> list[StreamResult]:
         cfg, dev = self.cfg, self.dm.device
         n = len(streams)
         lens = np.array([len(s) for s in streams], dtype=np.int64)
@@ -504,7 +585,7 @@ class Engine:
         for t in range(T):
             if t > 0 and t % every == 0:
                 rows = [i for i in range(n) if lens[i] > t]
-                self._boundary_encode(b, rows, segs, t)
+                self._boundary_encode(b, rows, segs, t, symsT_d[:, 0])
             active = lens > t
             if not active.all():
                 b.set_active(active)
@@ -524,18 +605,27 @@ class Engine:
             out.append(StreamResult(payload=payload, segments=segs[i], n_symbols=int(lens[i])))
         return out
 
-    def _boundary_encode(self, b: StreamBatch, rows, segs, t: int) -> None:
+    def _boundary_encode(self, b: StreamBatch, rows, segs, t: int, prefix: torch.Tensor) -> None:
         b.set_active(None)
         b.ac_flush(rows)
         for r, p in b.segment_bytes(rows).items():
             segs[r].append(p)
         b.ac_init(rows)
         if self.ttt is not None:
-            self.ttt(b, rows, t)
+            self._update(b, rows, t, prefix)
         if self.reset is not None:
             self.reset(b, rows, t)
 
     def decode(self, payloads: list[bytes], n_symbols: list[int]) -> list[np.ndarray]:
+        if self._per_stream():
+            out = []
+            for p, k in zip(payloads, n_symbols):
+                self.ttt.reset()
+                out += self._decode([p], [k])
+            return out
+        return self._decode(payloads, n_symbols)
+
+    def _decode(self, payloads: list[bytes], n_symbols: list[int]) -> list[np.ndarray]:
         cfg, dev = self.cfg, self.dm.device
         n = len(payloads)
         lens = np.asarray(n_symbols, dtype=np.int64)
@@ -557,7 +647,7 @@ class Engine:
                 if rows:
                     b.set_active(None)
                     if self.ttt is not None:
-                        self.ttt(b, rows, t)
+                        self._update(b, rows, t, out[:, 0])
                     if self.reset is not None:
                         self.reset(b, rows, t)
                     b.begin_decode({i: segs[i][t // every] for i in rows})

@@ -191,6 +191,10 @@ typedef struct altxs_weights {
     const float *softcap;        /* [2]: positive, negative */
     const float *parallel_post;  /* [L][2][2]: (attention, MLP) output into (lane 0, lane 1) */
     const float *parallel_resid; /* [L][2]: lane 0, lane 1 residual scales */
+    /* dense fp32 embedding [V][d] for the step's input rows, or NULL (rows from
+     * the emb codes).  A model whose weights change (full-parameter replenish)
+     * points it at its parameter arena and refreshes split with altxs_split_params. */
+    const float *emb_dense;
 } altxs_weights;
 
 /* Per-stream state and scratch of a batch of n streams.  Stream i of the
@@ -333,6 +337,58 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
                      const altxs_ttt_hparams *hp, const int32_t *tokens, int T, float *lora, float *adam_m,
                      float *adam_v, int step, float *loss_out, void *workspace, int64_t workspace_bytes,
                      altxs_stream_t stream);
+
+/* ---- full-parameter replenish -------------------------------------------------
+ * The reference's production update trains every weight of the model
+ * (online_retrain with retrain_mode "replenish", altxs src/xsa_ttt/compress.py:
+ * 816-1073, and its Forward-XM boundary :611-718).  One stream's parameters
+ * live in a single fp32 arena whose segments (floats from its start, each
+ * 64-aligned) altxs_param_layout_of gives:
+ *   emb [V][d] (the tied table), qkv [L][d+2*kvd][d] (each layer's q, k, v
+ *   rows), o [L][d][d], up [L][F][d], down [L][d][F], q_gain [L][H],
+ *   attn_scale [L][d], mlp_scale [L][d], resid_mix [L][2][d],
+ *   skip_weights [S][d], skip_gates [S][d]   (S = L/2)
+ * The gradient and the AdamW moments use the same layout.  The host keeps the
+ * boundary schedule (anneal, warmup, replay draws, XM candidates and probe
+ * windows), which is integer and float arithmetic of a few values. */
+typedef struct altxs_param_layout {
+    int64_t emb, qkv, o, up, down, q_gain, attn_scale, mlp_scale, resid_mix, skip_weights, skip_gates, total;
+} altxs_param_layout;
+int altxs_param_layout_of(const altxs_model_desc *desc, altxs_param_layout *out);
+
+/* Workspace of one altxs_full_loss_grad call over windows of up to n tokens. */
+int64_t altxs_full_workspace_bytes(const altxs_model_desc *desc, int n);
+
+/* Teacher-forced forward over tokens[0..n-1) (positions 0.., causal) and the
+ * mean cross-entropy of targets tokens[first+1..n) — the chunk loss of
+ * chunk_tf_train_loss (compress.py:128-170; tokens = arr[ctx_start:chunk_end],
+ * first = p0 - ctx_start - 1) and of the XM probes (_xm_probe_ce, :523-583).
+ * With grad non-NULL, also d(loss)/d(every parameter) into grad
+ * [layout.total] (all entries written).  The forward reads the five matrices
+ * from dense (tensor cores from w->split when set) and the small parameters
+ * from w; the caller points both into its parameter arena.  desc->lora_rank
+ * must be 0; the plain GPT only.  loss_out: device float or NULL. */
+int altxs_full_loss_grad(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
+                         const int32_t *tokens, int n, int first, float *loss_out, float *grad, void *workspace,
+                         int64_t workspace_bytes, altxs_stream_t stream);
+
+/* clip_grad_norm_(grad, hp->grad_clip) then AdamW step `step` (1-based) over
+ * n floats, as torch.optim.AdamW (decoupled decay, bias corrections, eps
+ * outside the square root).  partials: device scratch of >= 256 floats. */
+int altxs_adamw(int64_t n, float *params, const float *grad, float *m, float *v, const altxs_ttt_hparams *hp, int step,
+                float *partials, altxs_stream_t stream);
+
+/* out[i] = a[i] + s * b[i]: ΔW = W - W0 (s = -1) and the XM candidates W0 + s ΔW. */
+int altxs_params_axpy(int64_t n, const float *a, float s, const float *b, float *out, altxs_stream_t stream);
+
+/* Anchor pull toward the first boundary's weights: p[i] -= (p[i] - w0[i]) * pull[i]
+ * (_apply_replenish_anchor, compress.py:439-445; pull = mask * rate). */
+int altxs_params_anchor(int64_t n, float *p, const float *w0, const float *pull, altxs_stream_t stream);
+
+/* Rewrites the step's tensor-core planes (written through planes' pointers)
+ * from the five matrices of a parameter arena. */
+int altxs_split_params(const altxs_model_desc *desc, const float *params, const altxs_split_planes *planes,
+                       altxs_stream_t stream);
 
 /* ---- failure detection ------------------------------------------------------
  * No counterpart in the reference (its device waits do not exist; its coder
