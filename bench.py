@@ -61,6 +61,10 @@ def parse_args():
                     help="how the windows are filled before timing: code the preceding 2048 symbols "
                          "(default) or write seeded random K/V rows (profiling runs: same per-step work, "
                          "no 2048-step warm-up)")
+    ap.add_argument("--replenish", action="store_true",
+                    help="instead of the decode benchmark: one full-parameter replenish boundary of the 33M "
+                         "model (Forward-XM: gradient of every weight over an 18,432-token window, AdamW, "
+                         "four candidate updates each scored on an 18,432-token probe window), one JSON line")
     ap.add_argument("--c2", action="store_true",
                     help="instead of the decode benchmark: the linear-layer microbenchmark (the C3 layer "
                          "shapes K x N at M = 1, 16, 128, 512 rows, tensor-core and CUDA-core paths), one "
@@ -244,6 +248,102 @@ def run_c2(args) -> None:
                                   "frac": achieved / peak, "peak_source": f"{kind}"}), flush=True)
 
 
+def run_replenish(args) -> None:
+    """One Forward-XM replenish boundary of the 33M model at its own shapes
+    (block 2048, segments of 16,384 symbols) on one GPU.  The boundary at
+    position 3 x 16,384 trains on the previous segment with its 2048-symbol
+    context (18,432 tokens), then scores the candidates W0 + s dW, s in
+    0.5, 1, 2, 4, on the just-coded segment (18,432 tokens each).  Timed with
+    CUDA events on the launch stream after one warm-up boundary, over --steps
+    boundaries (each restarting from the same weights and optimizer state).
+    Tensor roofline: algorithmic FLOPs of the four passes (3 x forward for the
+    gradient pass, 1 x forward per probe; forward = 2 x parameters x tokens
+    + 2 x T^2 x d x layers for causal attention) over the bf16 dense peak;
+    the hi/lo operand split issues three MMAs per product, so its ceiling is a
+    third of that."""
+    import ctypes
+
+    from altxs_b200 import _lib
+    from altxs_b200 import codec as C
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import DeviceModel
+    from altxs_b200.replenish import ReplenishTTT
+    from altxs_b200.synth import zipf_markov
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = c3_config()
+    cfg.retrain_mode = "replenish"
+    cfg.ttt_replenish_warmup_steps = 0
+    cfg.ttt_lora_lr = 8e-5
+    every, block = cfg.online_retrain_every, cfg.block_size
+    dm = DeviceModel(C.synth_weights(cfg, seed=WEIGHT_SEED), dev, full_params=True)
+    arr = zipf_markov(3 * every, cfg.vocab_size, [11])[0].astype(np.int32)
+    prefix = torch.as_tensor(arr, device=dev)
+    ttt = ReplenishTTT(dm, n_total=len(arr))
+    peaks, kind = load_peaks()
+    L = _lib.lib()
+    n_tok = every + block
+    T = n_tok - 1
+    P = dm.layout.total
+    fwd = 2.0 * P * T + 2.0 * T * T * cfg.model_dim * cfg.num_layers
+    # time the parts: the gradient pass and one probe forward
+    st = torch.cuda.current_stream().cuda_stream
+    toks = prefix[every - block: 2 * every].contiguous()
+
+    def call(grad: bool):
+        rc = L.altxs_full_loss_grad(ctypes.byref(dm.desc), ctypes.byref(dm.weights_struct),
+                                    ctypes.byref(dm.dense_weights()), toks.data_ptr(), n_tok, block - 1,
+                                    ttt.loss.data_ptr(), ttt.grad.data_ptr() if grad else None, ttt.ws.data_ptr(),
+                                    ttt.ws_bytes, st)
+        _lib.check(rc, "altxs_full_loss_grad")
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        out = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            out.append(e0.elapsed_time(e1) / 1000.0)
+        return statistics.median(out)
+
+    reps = max(1, min(args.steps, 5))
+    t_grad = timed(lambda: call(True), reps)
+    t_fwd = timed(lambda: call(False), reps)
+    p0, m0, v0 = dm.params.clone(), ttt.m.clone(), ttt.v.clone()
+
+    def boundary():
+        dm.params.copy_(p0)
+        ttt.m.copy_(m0)
+        ttt.v.copy_(v0)
+        ttt.step = 0
+        dm.refresh()
+        ttt.boundary(prefix, 3 * every)
+
+    sampler = ClockSampler(0)
+    t_b = timed(boundary, reps)
+    clocks = sampler.stop()
+    n_cand = len(ttt.xm_last["candidates"])
+    flops = 3 * fwd + n_cand * fwd
+    tf = flops / t_b / 1e12
+    print(json.dumps({
+        "replenish": True, "workload": "33M model (8L/512d/8h, MLP 2048, V 16384), block 2048, segment 16384: "
+                                       "one Forward-XM boundary, 4 candidates, 1 probe window",
+        "tokens_per_window": n_tok, "params": P, "boundary_ms": t_b * 1e3, "grad_pass_ms": t_grad * 1e3,
+        "forward_ms": t_fwd * 1e3, "candidates": n_cand, "xm_chosen": ttt.xm_last["chosen"],
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tf / peaks["bf16_tflops"], "peak_source": f"{kind} bf16_tflops",
+                     "note": "hi/lo bf16 split: 3 MMAs per product, ceiling 1/3 of peak"},
+        "grad_pass_tflops": 3 * fwd / t_grad / 1e12, "forward_tflops": fwd / t_fwd / 1e12,
+        "workspace_gib": ttt.ws_bytes / 2 ** 30, "clocks": clocks, "dtype": "f32 math, hi/lo bf16 tensor-core products",
+        "data": "synthetic: seeded Zipf-Markov stream, seeded random mixed-bit weights",
+    }), flush=True)
+
+
 def config_block(world: int, streams: int) -> dict:
     return {
         "workload": "box-scale sharded decode: 2048 independent streams split over N GPUs, 33M model "
@@ -282,6 +382,10 @@ def main():
     if args.c2:
         if rank == 0:
             run_c2(args)
+        return
+    if args.replenish:
+        if rank == 0:
+            run_replenish(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
