@@ -331,6 +331,113 @@ def synth_weights(cfg: ModelConfig, seed: int = 0) -> ModelWeights:
     return ModelWeights(cfg, emb, q, k, v, o, up, down, default_small(cfg))
 
 
+def small_from_state(cfg: ModelConfig, tensors: dict[str, Any]) -> dict[str, np.ndarray]:
+    """The engine's small parameters from reference-named tensors; names that
+    are absent keep the reference's initial values."""
+    L = cfg.num_layers
+
+    def t(name):
+        x = tensors[name]
+        return np.asarray(x.detach().cpu().numpy() if hasattr(x, "detach") else x, dtype=np.float32)
+
+    small = default_small(cfg)
+    for name in ("skip_weights", "skip_gates"):
+        if name in tensors and np.size(tensors[name]):
+            small[name] = t(name).reshape(-1, cfg.model_dim)
+    for i in range(L):
+        for field, key in (("attn_scale", "attn_scale"), ("mlp_scale", "mlp_scale"), ("resid_mix", "resid_mix"),
+                           ("q_gain", "attn.q_gain"), ("attn_gate_w", "attn.attn_gate_w")):
+            name = f"blocks.{i}.{key}"
+            if name in tensors:
+                small[field][i] = t(name).reshape(small[field][i].shape)
+    if "smear_gate.weight" in tensors:
+        small["smear_gate"] = t("smear_gate.weight").reshape(-1)
+    if "smear_lambda" in tensors:
+        small["smear_lambda"] = t("smear_lambda").reshape(1)
+    if "softcap_pos" in tensors:
+        small["softcap"] = np.array([float(t("softcap_pos")), float(t("softcap_neg"))], dtype=np.float32)
+    if "parallel_post_lambdas" in tensors:
+        small["parallel_post"] = t("parallel_post_lambdas").reshape(L, 2, 2)
+    if "parallel_resid_lambdas" in tensors:
+        small["parallel_resid"] = t("parallel_resid_lambdas").reshape(L, 2)
+    return small
+
+
+def reference_init(cfg: ModelConfig, seed: int) -> dict[str, np.ndarray]:
+    """The reference's deterministic ``Init(seed)`` (``build_model`` after
+    ``enable_deterministic``: ``torch.manual_seed(seed)``, then ``GPT.__init__``
+    and ``_init_weights``, altxs src/xsa_ttt/model.py:985-1163,
+    src/model/deterministic_mode.py:50-62), as reference-named fp32 arrays.
+
+    The draws from torch's CPU generator are replayed in construction order:
+    ``nn.Embedding`` N(0,1); per block the sparse attention gate
+    N(0, init_std) when that std is positive; the smear gate's ``nn.Linear``
+    Kaiming-uniform draw (then zeroed); in ``_init_weights`` the tied table
+    N(0, tied_embed_init_std), per layer orthogonal q, k, v (o zero), then per
+    layer orthogonal up (down zero).  ``orthogonal_`` is torch's QR recipe with
+    the same generator, so the values are torch's own."""
+    import math as _m
+
+    import torch
+
+    V, L, d, H, kv, F = (cfg.vocab_size, cfg.num_layers, cfg.model_dim, cfg.num_heads, cfg.kv_dim,
+                         cfg.mlp_hidden)
+    g = torch.Generator().manual_seed(int(seed))
+
+    def orthogonal(rows: int, cols: int) -> torch.Tensor:
+        flat = torch.empty(rows, cols).normal_(0.0, 1.0, generator=g)
+        if rows < cols:
+            flat = flat.t()
+        q, r = torch.linalg.qr(flat)
+        q = q * torch.diag(r, 0).sign()
+        if rows < cols:
+            q = q.t()
+        return q.contiguous()
+
+    emb = torch.empty(V, d).normal_(0.0, 1.0, generator=g)
+    gate_w = torch.zeros(L, H, cfg.gate_window)
+    for i in range(L):
+        if cfg.sparse_attn_gate_enabled and cfg.sparse_attn_gate_init_std > 0:
+            gate_w[i] = torch.empty(H, cfg.gate_window).normal_(0.0, float(cfg.sparse_attn_gate_init_std),
+                                                                 generator=g)
+    if cfg.smear_gate_enabled:  # nn.Linear(gate_window, 1).reset_parameters, later zero-initialised
+        bound = 1.0 / _m.sqrt(cfg.gate_window)
+        torch.empty(1, cfg.gate_window).uniform_(-bound, bound, generator=g)
+    emb.normal_(0.0, float(cfg.tied_embed_init_std), generator=g)
+    qo = torch.zeros(2 * L, d, d)
+    kvb = torch.zeros(2 * L, kv, d)
+    up = torch.zeros(L, F, d)
+    for i in range(L):
+        qo[i] = orthogonal(d, d)
+        kvb[i] = orthogonal(kv, d)
+        kvb[L + i] = orthogonal(kv, d)
+    for i in range(L):
+        up[i] = orthogonal(F, d)
+    out = {"tok_emb.weight": emb, "qo_bank": qo, "kv_bank": kvb, "mlp_up_bank": up,
+           "mlp_down_bank": torch.zeros(L, d, F)}
+    small = default_small(cfg)
+    S = cfg.num_skip_weights
+    out["skip_weights"] = torch.ones(S, d)
+    if cfg.skip_gates_enabled:
+        out["skip_gates"] = torch.zeros(S, d)
+    for i in range(L):
+        out[f"blocks.{i}.attn_scale"] = torch.from_numpy(small["attn_scale"][i])
+        out[f"blocks.{i}.mlp_scale"] = torch.from_numpy(small["mlp_scale"][i])
+        out[f"blocks.{i}.resid_mix"] = torch.from_numpy(small["resid_mix"][i])
+        out[f"blocks.{i}.attn.q_gain"] = torch.from_numpy(small["q_gain"][i])
+        if cfg.sparse_attn_gate_enabled:
+            out[f"blocks.{i}.attn.attn_gate_w"] = gate_w[i]
+    if cfg.smear_gate_enabled:
+        out["smear_gate.weight"] = torch.zeros(1, cfg.gate_window)
+        out["smear_lambda"] = torch.zeros(1)
+    if cfg.asym_logit_rescale:
+        out["softcap_pos"] = torch.tensor(float(cfg.logit_softcap))
+        out["softcap_neg"] = torch.tensor(float(cfg.logit_softcap))
+    out["parallel_post_lambdas"] = torch.ones(L, 2, 2)
+    out["parallel_resid_lambdas"] = torch.full((L, 2), 1.1)
+    return {k: v.numpy().astype(np.float32) for k, v in out.items()}
+
+
 def dense_weights(cfg: ModelConfig, tensors: dict[str, Any]) -> ModelWeights:
     """Wrap dense fp32 reference-named tensors (e.g. a reference GPT state
     dict) as 32-bit groups, so the kernels run a dense model exactly."""
@@ -343,25 +450,7 @@ def dense_weights(cfg: ModelConfig, tensors: dict[str, Any]) -> ModelWeights:
 
     qo, kvb = t("qo_bank"), t("kv_bank")
     up, down = t("mlp_up_bank"), t("mlp_down_bank")
-    small = default_small(cfg)
-    small["skip_weights"] = t("skip_weights")
-    if "skip_gates" in tensors:
-        small["skip_gates"] = t("skip_gates")
-    for i in range(L):
-        small["attn_scale"][i] = t(f"blocks.{i}.attn_scale")
-        small["mlp_scale"][i] = t(f"blocks.{i}.mlp_scale")
-        small["resid_mix"][i] = t(f"blocks.{i}.resid_mix")
-        small["q_gain"][i] = t(f"blocks.{i}.attn.q_gain")
-        if cfg.sparse_attn_gate_enabled:
-            small["attn_gate_w"][i] = t(f"blocks.{i}.attn.attn_gate_w")
-    if cfg.smear_gate_enabled:
-        small["smear_gate"] = t("smear_gate.weight").reshape(-1)
-        small["smear_lambda"] = t("smear_lambda").reshape(1)
-    if cfg.asym_logit_rescale:
-        small["softcap"] = np.array([float(t("softcap_pos")), float(t("softcap_neg"))], dtype=np.float32)
-    if "parallel_post_lambdas" in tensors:
-        small["parallel_post"] = t("parallel_post_lambdas")
-        small["parallel_resid"] = t("parallel_resid_lambdas")
+    small = small_from_state(cfg, tensors)
     gm = GroupMatrix.from_dense
     return ModelWeights(
         cfg,
@@ -529,11 +618,9 @@ def read_codec(path: str | Path) -> ModelWeights:
         raise ValueError(f"not a mixed-bit delta codec: {path}")
     if int(meta.get("format_version", -1)) not in (3, 4, 5):
         raise ValueError(f"unsupported format_version {meta.get('format_version')}")
-    if meta.get("delta_base", "init") != "zero":
-        raise ValueError(
-            "codec is a residual over Init(seed); rebuilding that dense base is not "
-            "supported by this engine (set delta_base='zero' codecs only)"
-        )
+    residual = meta.get("delta_base", "init") != "zero"
+    if meta.get("global_lora"):
+        raise ValueError("this codec has a global-LoRA residual; the reference ships no decoder for it")
     if meta.get("compact"):
         raise ValueError("zlib-compacted codecs are not supported")
     mode = str(meta.get("codebook_mode", "lloyd")).lower()
@@ -541,7 +628,8 @@ def read_codec(path: str | Path) -> ModelWeights:
         raise ValueError(f"codebook_mode {mode!r} not supported")
     axis = meta.get("channel_axis", "ref")
     cfg_d = meta.get("cfg") or {}
-    cfg = ModelConfig.from_dict(cfg_d) if "retrain_mode" in cfg_d else ModelConfig.from_reference_cfg(cfg_d)
+    # this engine's own configs carry its CDF rule; anything else is a reference XsaTttConfig
+    cfg = ModelConfig.from_dict(cfg_d) if "cdf_mode" in cfg_d else ModelConfig.from_reference_cfg(cfg_d)
     cfg.validate()
     st = load_file(str(path))
     L = int(meta["n_layers"])
@@ -584,6 +672,18 @@ def read_codec(path: str | Path) -> ModelWeights:
             return lut, np.arange(sel.size, dtype=np.int64)
 
         banks[name] = _channels_to_groups(name, bits, codes_of, lut_of, scale_of, width, shape, axis)
+    if residual:
+        # the reference's load_codec: Init(seed) + dequantised delta for the banks,
+        # the listed small parameters replace their initial values (mixed_bit_delta.py:232-305,
+        # train_hyperflow.py:8-19)
+        state = reference_init(cfg, int(meta["seed"]))
+        for name, mats in banks.items():
+            delta = np.concatenate([m.dequant() for m in mats]).reshape(state[name].shape)
+            state[name] = (state[name] + delta).astype(np.float32)
+        for k in meta["small_params"]:
+            if f"small/{k}" in st:
+                state[k] = st[f"small/{k}"].astype(np.float32).reshape(np.shape(state.get(k, st[f"small/{k}"])))
+        return dense_weights(cfg, state)
     small = default_small(cfg)
     for k in meta["small_params"]:
         key = f"small/{k}"

@@ -95,6 +95,7 @@ class ModelConfig:
     xsa_last_n: int = 0                   # XSA (value-direction removal) on the last n layers
     sparse_attn_gate_enabled: bool = False  # per-head sigmoid gate on the attention output
     sparse_attn_gate_scale: float = 0.5
+    sparse_attn_gate_init_std: float = 0.0  # init draw of the gate weights (Init(seed) of residual codecs)
     asym_logit_rescale: bool = False      # learned positive / negative softcaps
     num_loops: int = 0                    # depth recurrence over layers loop_start..loop_end
     loop_start: int = 3
@@ -190,7 +191,7 @@ class ModelConfig:
             raise ValueError("cdf_mode must be 'fixed' or 'ref'")
         if self.cdf_mode == "fixed" and not (self.vocab_size < (1 << self.cdf_bits) <= (1 << 30)):
             raise ValueError("cdf_bits must satisfy vocab < 2^cdf_bits <= 2^30")
-        if self.ttt_mlp_lora:
+        if self.ttt_mlp_lora and self.lora_enabled:
             raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
         if self.retrain_mode not in ("lora", "replenish", "none"):
             raise ValueError("retrain_mode must be 'lora', 'replenish' or 'none'")
@@ -244,6 +245,10 @@ class ModelConfig:
             v = get(f.name, None)
             if v is not None:
                 setattr(out, f.name, v)
+        if out.retrain_mode not in ("lora", "replenish", "none"):
+            out.retrain_mode = "none"  # the "full" mode's window retrain is not part of this engine
+        if out.motifs and out.lora_enabled:
+            out.retrain_mode = "none"  # adapters cover the plain GPT only
         return out
 
 

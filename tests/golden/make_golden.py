@@ -387,6 +387,87 @@ def gen_replenish() -> None:
     np.savez_compressed(HERE / "replenish.npz", **out)
 
 
+CODEC_REF = dict(
+    vocab_size=256, num_layers=4, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0, rope_dims=16,
+    block_size=64, online_retrain_every=128, seed=77, smear_gate_enabled=True, xsa_last_n=2,
+    sparse_attn_gate_enabled=True, sparse_attn_gate_init_std=0.02, asym_logit_rescale=True, num_loops=1,
+    loop_start=1, loop_end=2, parallel_start_layer=3, parallel_final_lane="mean",
+)
+
+
+def gen_codec_ref() -> None:
+    """A reference-format codec as the reference ships them: residual over
+    Init(seed), channels along the reference layout (rows; o and mlp_down as
+    columns), lloyd codebooks (2^b fp16 centroids per channel), some 0-bit
+    channels, the motif small parameters; decoded by the reference's own
+    load_codec (its deterministic Init(seed) + delta) and run by its GPT."""
+    import dataclasses
+
+    from hyperflow_distillation.mixed_bit_delta import load_codec
+    from safetensors.numpy import save_file
+
+    h = XsaTttConfig(seed=CODEC_REF["seed"])
+    for k, v in CODEC_REF.items():
+        setattr(h, k, v)
+    h.tie_embeddings = True
+    h.attn_out_gate_enabled = False
+    h.gated_attn_enabled = False
+    h.rope_yarn = False
+    h.gradient_checkpointing = False
+    L, d, V = h.num_layers, h.model_dim, h.vocab_size
+    kv = h.num_kv_heads * (d // h.num_heads)
+    F = int(h.mlp_mult * d)
+    shapes = {"qo_bank": [2 * L, d, d], "kv_bank": [2 * L, kv, d], "mlp_up_bank": [L, F, d],
+              "mlp_down_bank": [L, d, F], "tok_emb.weight": [V, d]}
+    rng = np.random.default_rng(19)
+    tensors, layouts = {}, {}
+    for name, shape in shapes.items():
+        n_ch = int(np.prod(shape)) // d
+        bits = rng.choice([0, 2, 3, 4], size=n_ch, p=[0.05, 0.3, 0.35, 0.3]).astype(np.uint8)
+        tensors[f"bits/{name}"] = bits
+        for b in (2, 3, 4):
+            idx = np.flatnonzero(bits == b)
+            codes = rng.integers(0, 1 << b, size=(idx.size, d)).astype(np.uint8)
+            tensors[f"packed/{name}/b{b}"] = C._pack_lsb(codes, b).reshape(-1) if idx.size else np.zeros(0, np.uint8)
+            cb = np.sort(rng.normal(0, 0.01, size=(idx.size, 1 << b)), axis=1).astype(np.float16)
+            tensors[f"codebook/{name}/b{b}"] = cb
+        layouts[name] = {"shape": shape, "channels": n_ch, "channel_width": d}
+    small = {}
+    for i in range(L):
+        small[f"blocks.{i}.attn_scale"] = (1 + 0.1 * rng.normal(size=d)).astype(np.float16)
+        small[f"blocks.{i}.mlp_scale"] = (1 + 0.1 * rng.normal(size=d)).astype(np.float32)
+        small[f"blocks.{i}.resid_mix"] = np.stack([1 + 0.1 * rng.normal(size=d), 0.1 * rng.normal(size=d)]).astype(np.float16)
+        small[f"blocks.{i}.attn.q_gain"] = (5 + rng.normal(size=h.num_heads)).astype(np.float32)
+        if i:  # layer 0 keeps the gate weights Init(seed) drew
+            small[f"blocks.{i}.attn.attn_gate_w"] = (0.5 * rng.normal(size=(h.num_heads, h.gate_window))).astype(np.float32)
+    S = min(len(range(4)) // 2, 3)
+    small["skip_weights"] = (1 + 0.1 * rng.normal(size=(3, d))).astype(np.float32)
+    small["skip_gates"] = (0.3 * rng.normal(size=(3, d))).astype(np.float32)
+    small["smear_gate.weight"] = (0.5 * rng.normal(size=(1, h.gate_window))).astype(np.float32)
+    small["smear_lambda"] = np.array([0.6], dtype=np.float32)
+    small["softcap_pos"] = np.array(22.0, dtype=np.float32)
+    small["softcap_neg"] = np.array(33.0, dtype=np.float32)
+    small["parallel_post_lambdas"] = (1 + 0.1 * rng.normal(size=(L, 2, 2))).astype(np.float32)
+    small["parallel_resid_lambdas"] = (1.1 + 0.1 * rng.normal(size=(L, 2))).astype(np.float32)
+    del S
+    for k, v in small.items():
+        tensors[f"small/{k}"] = v
+    path = HERE / "codec_ref_v256.safetensors"
+    save_file(tensors, str(path))
+    cfg_d = {k: v for k, v in dataclasses.asdict(h).items() if isinstance(v, (int, float, str, bool)) or v is None}
+    meta = {"format": "hope_mixed_bit_delta", "format_version": 5, "codebook_mode": "lloyd", "seed": h.seed,
+            "cfg": cfg_d, "n_layers": L, "layouts": layouts, "small_params": sorted(small)}
+    path.with_suffix(".json").write_text(json.dumps(meta, indent=1) + "\n")
+    model, _, _ = load_codec(path, device=torch.device("cpu"))
+    model.eval()
+    toks = np.random.default_rng(3).integers(0, V, size=40).astype(np.int64)
+    with torch.no_grad():
+        logits = model.forward_logits(torch.tensor(toks)[None])[0].float().numpy()
+    out = {"tokens": toks.astype(np.int32), "logits": logits.astype(np.float32)}
+    out.update({f"w/{k}": v.detach().float().numpy() for k, v in model.state_dict().items()})
+    np.savez_compressed(HERE / "codec_ref_v256.npz", **out)
+
+
 def gen_zipf() -> None:
     from altxs_b200.synth import zipf_markov
 
@@ -402,6 +483,7 @@ if __name__ == "__main__":
     gen_lora()
     gen_model_motifs()
     gen_replenish()
+    gen_codec_ref()
     gen_zipf()
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
         print(f.name, f.stat().st_size)

@@ -183,3 +183,26 @@ def test_motif_desc_refused_by_update_and_prefill():
     L = _lib.lib()
     assert L.altxs_prefill_workspace_bytes(ctypes.byref(dm.desc), 8) == -1
     assert L.altxs_ttt_workspace_bytes(ctypes.byref(dm.desc), 8) == -1
+
+
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_shipped_format_codec_runs_on_the_step(golden, tensor_cores):
+    """The reference-format V=256 codec (residual over Init(seed), lloyd
+    codebooks, motifs) loaded by read_codec and run by the CUDA step: logits
+    within 2e-3 of the reference GPT's; encode -> decode round trip."""
+    from altxs_b200.engine import DeviceModel, Engine
+    from tests.conftest import GOLDEN
+
+    g = golden("codec_ref_v256.npz")
+    w = C.read_codec(GOLDEN / "codec_ref_v256.safetensors")
+    dm = DeviceModel(w, DEV, tensor_cores=tensor_cores)
+    got = _logits_mode(dm, [g["tokens"]])[0]
+    err = float(np.abs(got - g["logits"]).max())
+    assert err < TOL, err
+    rng = np.random.default_rng(2)
+    streams = [rng.integers(0, 256, size=n).astype(np.int32) for n in (300, 77)]
+    eng = Engine(dm)
+    res = eng.encode(streams)
+    back = eng.decode([r.payload for r in res], [len(s) for s in streams])
+    for s, d in zip(streams, back):
+        assert np.array_equal(s, d)

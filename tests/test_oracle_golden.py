@@ -216,3 +216,30 @@ def test_oracle_replenish_matches_reference(golden, name):
     st = o.state()
     err = max(float(np.abs(st[k] - g[f"{name}/w/{k}"]).max()) for k in st)
     assert err < 1e-6, err
+
+
+def test_reference_codec_decodes_like_the_reference(golden):
+    """A reference-format V=256 codec as shipped (residual over Init(seed),
+    reference channel layout with o / mlp_down as columns, lloyd codebooks,
+    0-bit channels, motif small parameters): read_codec rebuilds the
+    reference's deterministic Init(seed) and adds the decoded delta, giving the
+    reference load_codec's weights bit for bit; the oracle then reproduces the
+    reference GPT's logits."""
+    from altxs_b200 import codec as C
+    from tests.conftest import GOLDEN
+
+    g = golden("codec_ref_v256.npz")
+    w = C.read_codec(GOLDEN / "codec_ref_v256.safetensors")
+    assert w.cfg.vocab_size == 256 and w.cfg.motifs and w.cfg.num_virtual_layers == 6
+    dense = w.dense()
+    for k in ("tok_emb.weight", "qo_bank", "kv_bank", "mlp_up_bank", "mlp_down_bank"):
+        assert np.array_equal(dense[k], g["w/" + k]), k
+    sm = w.small
+    for i in range(w.cfg.num_layers):
+        assert np.array_equal(sm["attn_gate_w"][i], g[f"w/blocks.{i}.attn.attn_gate_w"])  # layer 0: Init draw
+        assert np.array_equal(sm["resid_mix"][i], g[f"w/blocks.{i}.resid_mix"])
+    assert np.array_equal(sm["smear_gate"], g["w/smear_gate.weight"].reshape(-1))
+    om = OracleModel(OracleWeights.from_model_weights(w))
+    st = om.new_stream()
+    got = np.stack([om.step(st, int(t)).numpy() for t in g["tokens"]])
+    assert float(np.abs(got - g["logits"]).max()) < 1e-4
