@@ -133,7 +133,7 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.dkr = take(T * D.kvd);
     t.dy = take(T * d);
     t.dao = take(T * d);
-    t.dS = take((int64_t)D.H * T * T);
+    t.dS = take((int64_t)D.H * T * align_up(T, 8));  // fp32 scores / dP, rows of stride align8(T) on the tensor-core path
     t.dt = take(T * D.r);
     t.grad = nullptr;  // set by caller (lora_floats)
     t.red = take(1024);
@@ -403,41 +403,105 @@ __global__ void t_softmax_bwd(TD D, const float *P, float *dS, float scale) {
         g[j] = j <= t ? __fmul_rn(__fmul_rn(p[j], __fsub_rn(g[j], s)), scale) : 0.0f;
 }
 
-// Plane forms of the two softmax kernels (tensor-core path): the scores S
-// come in fp32 (row stride T), P leaves as hi/lo bf16 planes [H][T][ldp]
-// (zero above the diagonal); the backward reads P from its planes and writes
-// dS as planes.
-__global__ void t_softmax_pl(TD D, const float *S, uint16_t *ph, uint16_t *pl, int64_t ldp) {
+// Plane forms of the two softmax kernels (tensor-core path).  The scores S
+// (and dP) come in fp32 rows of stride ldp = align8(T); P (and dS) leave as
+// hi/lo bf16 planes [H][T][ldp].  Row t is written only up to the end of its
+// 128-column diagonal tile (zero past t): the products that read the planes
+// (P v and dS k with k < m0 + 128, P^T dy and dS^T q with k >= m0) never read
+// further.  Each thread takes 8 consecutive columns per pass with 16-byte loads
+// and stores; one CTA per (head, t) row.
+__device__ __forceinline__ void load8(const float *p, float *v) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void store8_planes(uint16_t *hi, uint16_t *lo, int64_t idx, const float *v) {
+    uint16_t h[8], l[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(v[u]);
+        h[u] = __bfloat16_as_ushort(b);
+        l[u] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(v[u], __bfloat162float(b))));
+    }
+    *reinterpret_cast<uint4 *>(hi + idx) = *reinterpret_cast<const uint4 *>(h);
+    *reinterpret_cast<uint4 *>(lo + idx) = *reinterpret_cast<const uint4 *>(l);
+}
+__device__ __forceinline__ void load8_planes(const uint16_t *hi, const uint16_t *lo, int64_t idx, float *v) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(hi + idx), b = *reinterpret_cast<const uint4 *>(lo + idx);
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(&a), *l = reinterpret_cast<const uint16_t *>(&b);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+        v[u] = __fadd_rn(__bfloat162float(__ushort_as_bfloat16(h[u])), __bfloat162float(__ushort_as_bfloat16(l[u])));
+}
+__device__ __forceinline__ int64_t diag_end(int n, int64_t ldp) {
+    const int64_t e = ((int64_t)n + 127) / 128 * 128;
+    return e < ldp ? e : ldp;
+}
+
+__global__ void __launch_bounds__(256) t_softmax_pl(TD D, const float *S, uint16_t *ph, uint16_t *pl, int64_t ldp) {
     __shared__ float red[32];
     const int row = blockIdx.x;  // h * T + t
-    const int t = row % D.T;
-    const float *s = S + (int64_t)row * D.T;
+    const int n = row % D.T + 1;  // scores 0..t
+    const float *s = S + (int64_t)row * ldp;
+    const int nc = (n + 7) / 8;
+    float v[8];
     float m = -INFINITY;
-    for (int j = threadIdx.x; j <= t; j += blockDim.x) m = fmaxf(m, s[j]);
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        load8(s + 8 * c, v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (8 * c + u < n) m = fmaxf(m, v[u]);
+    }
     m = block_max(m, red);
-    __syncthreads();
     float sum = 0.0f;
-    for (int j = threadIdx.x; j <= t; j += blockDim.x) sum = __fadd_rn(sum, expf(__fsub_rn(s[j], m)));
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        load8(s + 8 * c, v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (8 * c + u < n) sum = __fadd_rn(sum, expf(__fsub_rn(v[u], m)));
+    }
     sum = block_sum(sum, red);
     const float inv = __fdiv_rn(1.0f, sum);
     const int64_t o = (int64_t)row * ldp;
-    for (int j = threadIdx.x; j < ldp; j += blockDim.x)
-        split_store(ph, pl, o + j, j <= t ? __fmul_rn(expf(__fsub_rn(s[j], m)), inv) : 0.0f);
+    const int wc = (int)(diag_end(n, ldp) / 8);
+    for (int c = threadIdx.x; c < wc; c += blockDim.x) {
+        if (c < nc) load8(s + 8 * c, v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = 8 * c + u < n ? __fmul_rn(expf(__fsub_rn(v[u], m)), inv) : 0.0f;
+        store8_planes(ph, pl, o + 8 * c, v);
+    }
 }
 
-__global__ void t_softmax_bwd_pl(TD D, const uint16_t *ph, const uint16_t *pl, int64_t ldp, const float *dP,
-                                 uint16_t *gh, uint16_t *gl, float scale) {
+// dS = P * (dP - sum_j dP P) * scale over j <= t (dP above the diagonal is never computed)
+__global__ void __launch_bounds__(256) t_softmax_bwd_pl(TD D, const uint16_t *ph, const uint16_t *pl, int64_t ldp,
+                                                        const float *dP, uint16_t *gh, uint16_t *gl, float scale) {
     __shared__ float red[32];
     const int row = blockIdx.x;
-    const int t = row % D.T;
+    const int n = row % D.T + 1;
     const int64_t o = (int64_t)row * ldp;
-    const float *g = dP + (int64_t)row * D.T;
-    float s = 0.0f;
-    for (int j = threadIdx.x; j <= t; j += blockDim.x) s = __fmaf_rn(g[j], split_load(ph, pl, o + j), s);
-    s = block_sum(s, red);
-    for (int j = threadIdx.x; j < ldp; j += blockDim.x)
-        split_store(gh, gl, o + j,
-                    j <= t ? __fmul_rn(__fmul_rn(split_load(ph, pl, o + j), __fsub_rn(g[j], s)), scale) : 0.0f);
+    const float *g = dP + o;
+    const int nc = (n + 7) / 8;
+    float pv[8], gv[8];
+    float sdot = 0.0f;
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        load8_planes(ph, pl, o + 8 * c, pv);
+        load8(g + 8 * c, gv);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (8 * c + u < n) sdot = __fmaf_rn(gv[u], pv[u], sdot);
+    }
+    sdot = block_sum(sdot, red);
+    const int wc = (int)(diag_end(n, ldp) / 8);
+    for (int c = threadIdx.x; c < wc; c += blockDim.x) {
+        float out[8];
+        if (c < nc) {
+            load8_planes(ph, pl, o + 8 * c, pv);
+            load8(g + 8 * c, gv);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            out[u] = 8 * c + u < n ? __fmul_rn(__fmul_rn(pv[u], __fsub_rn(gv[u], sdot)), scale) : 0.0f;
+        store8_planes(gh, gl, o + 8 * c, out);
+    }
 }
 
 // context prefill: K (normed, roped) and V rows of position t, layer l into
@@ -904,13 +968,15 @@ int attn_probs(const Run &R, int l) {
     const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
     const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
     const int64_t ldp = align_up(Tn, 8);
-    float *S = R.sp ? tp.dS : p_f32(R, l);  // tensor cores: S in fp32 scratch, P leaves as planes
-    GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, S, Tn, Tn, Tn, D.hd, att_scale);  // S = q k^T
+    // tensor cores: S in fp32 scratch (rows of stride ldp), P leaves as planes
+    float *S = R.sp ? tp.dS : p_f32(R, l);
+    const int64_t lds = R.sp ? ldp : Tn;
+    GemmArgs g = G(R, qr, D.H * D.hd, 0, kr, D.kvd, 1, S, lds, Tn, Tn, D.hd, att_scale);  // S = q k^T
     g.batch = D.H;
     g.sA = D.hd;
     g.sB = D.hd;
     g.bdiv = D.G;
-    g.sC = (int64_t)Tn * Tn;
+    g.sC = (int64_t)Tn * lds;
     g.causal = 1;
     TRY(gemm(R, g));
     if (R.sp) {
@@ -1089,12 +1155,12 @@ int backward(const Run &R, const float *lora, float *grad) {
             const int64_t ldp = align_up(Tn, 8);
             const uint16_t *Ph = p_planes(R, l);
             const uint16_t *Pl = Ph + D.H * Tn * ldp;
-            GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, Tn, Tn, Tn, D.hd);  // dP = dy v^T
+            GemmArgs g = G(R, tp.dy, d, 0, qkv + d + D.kvd, D.qn, 1, tp.dS, ldp, Tn, Tn, D.hd);  // dP = dy v^T
             g.batch = D.H;
             g.sA = D.hd;
             g.sB = D.hd;
             g.bdiv = D.G;
-            g.sC = (int64_t)Tn * Tn;
+            g.sC = (int64_t)Tn * ldp;
             g.causal = 1;
             TRY(gemm(R, g));
             TcOp b{};
