@@ -42,7 +42,8 @@ struct TcCfg {
     static constexpr int kBTile = BN * kBK * 2;   // bytes of one B plane tile
     static constexpr int kStage = 2 * kATile + 2 * kBTile;
     static constexpr int kStages = (192 * 1024) / kStage;  // BN 64: 4, 128: 3
-    static constexpr int kSmem = kStages * kStage + 1024;  // + alignment slack
+    static constexpr int kStore = 4 * 32 * 32 * 4;          // one 32 x 32 fp32 store block per epilogue warp
+    static constexpr int kSmem = kStages * kStage + kStore + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
     // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B,
     // A/B major-ness, M = 128, N = BN
@@ -58,6 +59,19 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+
+// TMA tensor store of one [32 rows][32 fp32] box (128-byte swizzle) from shared
+// memory; completion is tracked per thread with bulk groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z), "r"(smem_u32(src))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Shared-memory matrix descriptors of tiles written by TMA with the 128-byte
 // swizzle (8-row x 128-byte atoms).  K-major: rows are MN, 128 bytes of K per
@@ -146,7 +160,8 @@ __device__ __forceinline__ int op_batch(const TcOp &o, int b) { return (b / o.di
 template <int BN, int AMN, int BMN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
-              const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo, TcGemm g) {
+              const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+              const __grid_constant__ CUtensorMap tc_map, TcGemm g) {
     using Cfg = TcCfg<BN, AMN, BMN>;
     constexpr int S = Cfg::kStages;
     extern __shared__ unsigned char tc_smem_raw[];
@@ -276,6 +291,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Per 32-column block: lane = tile row on the way out of tensor
         // memory, lane = column on the way to global memory.
         float(*eb)[33] = ebuf[warp];
+        // TMA store path: this warp's [32 rows][32 fp32] box, 1024-byte aligned after the stages
+        float *sb = reinterpret_cast<float *>(sm + S * Cfg::kStage) + warp * 32 * 32;
         // 16-byte stores and loads need 4-float row strides and 16-byte (8 for planes) bases
         auto al = [](const void *p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
         const bool vec = ((g.ldc | g.ldr | g.ldy2 | g.ldp | g.sC) & 3) == 0 && al(g.C, 15) && al(g.R, 15) &&
@@ -306,6 +323,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[buf]);
+                }
+                if (g.tma_c) {
+                    // lane = tile row: its 32 columns become row `lane` of the box
+                    // (16-byte chunk j stored at j ^ (row & 7): the 128-byte swizzle),
+                    // then one asynchronous tensor store; the map clips rows >= M and
+                    // columns >= N.  The box is rewritten only after the previous
+                    // store has finished reading it.
+                    const int n0 = T.n0 + c0, mrow = T.m0 + warp * 32;
+                    if (n0 >= g.N || mrow >= g.M) continue;
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                    char *rowp = reinterpret_cast<char *>(sb) + lane * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        float q[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const float x = no_k ? 0.0f : v[4 * c + u];
+                            q[u] = g.alpha != 1.0f ? __fmul_rn(g.alpha, x) : x;
+                        }
+                        *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) = make_float4(q[0], q[1], q[2], q[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tma_store_3d(&tc_map, sb, n0, mrow, T.b);
+                    continue;
                 }
 #pragma unroll
                 for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
@@ -424,6 +467,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         }
+        if (g.tma_c && lane == 0) bulk_wait_all();  // every tensor store of this warp has landed
     }
     tc_fence_before();
     __syncthreads();
@@ -493,6 +537,24 @@ bool make_map(CUtensorMap *m, const uint16_t *p, const TcOp &o, int box_rows) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Tensor map of C ([batch][M][ldc] fp32, boxes of 32 x 32, 128-byte swizzle)
+// when the epilogue is a plain store that TMA can take: no accumulation into
+// C, no residual, second output or planes, 16-byte aligned base and strides.
+bool make_c_map(CUtensorMap *m, const TcGemm &g) {
+    if (!g.C || g.epi != kEpiStore || g.beta != 0.0f || g.Y2 || g.p_hi || g.R) return false;
+    if (!aligned16(g.C) || g.ldc % 4 || g.ldc < g.N || (g.batch > 1 && (g.sC % 4 || g.sC < g.ldc * g.M))) return false;
+    auto enc = encoder();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)g.N, (cuuint64_t)g.M, (cuuint64_t)g.batch};
+    const int64_t bs = g.batch > 1 ? g.sC : g.ldc * (int64_t)g.M;
+    cuuint64_t strides[2] = {(cuuint64_t)(g.ldc * 4), (cuuint64_t)(bs * 4)};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, g.C, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool op_ok(const TcOp &o) {
     if (!o.hi || !o.lo || !aligned16(o.hi) || !aligned16(o.lo)) return false;
     if (o.ld % 8 || o.ld < o.cols || o.rows < 1 || o.cols < 1 || o.div < 1 || o.mul < 0 || o.add < 0) return false;
@@ -513,16 +575,19 @@ int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
             return ALTXS_ECUDA;
         attr_done[dev] = true;
     }
-    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo, tc_map;
     const int abox = AMN ? 64 : kBM, bbox = BMN ? 64 : BN;
     if (!make_map(&ta_hi, g.a.hi, g.a, abox) || !make_map(&ta_lo, g.a.lo, g.a, abox) ||
         !make_map(&tb_hi, g.b.hi, g.b, bbox) || !make_map(&tb_lo, g.b.lo, g.b, bbox))
         return ALTXS_EINVAL;
+    TcGemm gk = g;
+    gk.tma_c = make_c_map(&tc_map, g) ? 1 : 0;
+    if (!gk.tma_c) tc_map = ta_hi;  // unused
     // persistent: at most one CTA per SM walks the tiles
     const int64_t tiles = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch;
     const int grid = (int)(tiles < sms ? tiles : sms);
     ALTXS_LAUNCH(::altxs::kKQmm, st,
-                 k_tc_gemm<BN, AMN, BMN><<<grid, kTcThreads, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, g));
+                 k_tc_gemm<BN, AMN, BMN><<<grid, kTcThreads, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, tc_map, gk));
     return ALTXS_OK;
 }
 

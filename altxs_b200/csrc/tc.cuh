@@ -63,6 +63,7 @@ struct TcGemm {
     int64_t ldp;
     uint32_t *status;       // optional per-row status word (ALTXS_ST_TIMEOUT on a wait that gave up)
     int64_t status_stride;  // in uint32 units
+    int tma_c;              // set by launch_tc_gemm: C is written by TMA tensor stores
 };
 
 // 0 on success.  K and the operands' K extents must be multiples of 8, plane
