@@ -51,7 +51,7 @@ class ModelConfig:
     context_mode: str = "sliding"
     seed: int = 1337
     # test-time LoRA (reference ttt_* fields, config.py:144-165)
-    retrain_mode: str = "lora"  # "lora", "replenish" (every parameter, see below) or "none"
+    retrain_mode: str = "lora"  # "lora", "replenish" / "full" (every parameter, see below) or "none"
     ttt_lora_rank: int = 8
     ttt_lora_alpha: float = 144.0
     ttt_lora_lr: float = 1e-3
@@ -87,6 +87,13 @@ class ModelConfig:
     ttt_replenish_xm_probe_chunks: int = 1
     ttt_replenish_xm_4x_until_bytes: int = 100 * 1024 * 1024
     ttt_burst_schedule: str = ""           # "pos:steps,..." extra steps at the first boundary >= pos
+    # "full" mode (the reference's default, compress.py:923-1146): the window loss
+    # of the last block_size symbols, replay windows, and burst steps on their own
+    # AdamW that walk the segment boundaries oldest -> newest
+    ttt_burst_lr: float = 3e-4
+    ttt_burst_beta1: float = 0.9
+    ttt_burst_beta2: float = 0.999
+    ttt_burst_weight_decay: float = 0.01
     # reference model motifs (model.py:982-1110; all off = the plain GPT).  The
     # step and the oracle run them with frozen weights; the test-time LoRA
     # update covers the plain GPT only.
@@ -193,10 +200,10 @@ class ModelConfig:
             raise ValueError("cdf_bits must satisfy vocab < 2^cdf_bits <= 2^30")
         if self.ttt_mlp_lora and self.lora_enabled:
             raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
-        if self.retrain_mode not in ("lora", "replenish", "none"):
-            raise ValueError("retrain_mode must be 'lora', 'replenish' or 'none'")
-        if self.retrain_mode == "replenish" and self.motifs:
-            raise ValueError("the replenish update covers the plain GPT; turn the motifs off")
+        if self.retrain_mode not in ("lora", "replenish", "full", "none"):
+            raise ValueError("retrain_mode must be 'lora', 'replenish', 'full' or 'none'")
+        if self.retrain_mode in ("replenish", "full") and self.motifs:
+            raise ValueError("the full-parameter updates cover the plain GPT; turn the motifs off")
         if self.context_mode not in ("sliding", "reset"):
             raise ValueError("context_mode must be 'sliding' or 'reset'")
         if self.parallel_final_lane not in ("mean", "attn", "mlp"):
@@ -245,10 +252,10 @@ class ModelConfig:
             v = get(f.name, None)
             if v is not None:
                 setattr(out, f.name, v)
-        if out.retrain_mode not in ("lora", "replenish", "none"):
-            out.retrain_mode = "none"  # the "full" mode's window retrain is not part of this engine
-        if out.motifs and out.lora_enabled:
-            out.retrain_mode = "none"  # adapters cover the plain GPT only
+        if out.retrain_mode not in ("lora", "replenish", "full", "none"):
+            out.retrain_mode = "none"
+        if out.motifs and out.retrain_mode != "none":
+            out.retrain_mode = "none"  # the updates cover the plain GPT only
         return out
 
 

@@ -114,6 +114,24 @@ def probe_windows(cfg: ModelConfig, end: int) -> list[tuple[int, int, int]]:
     return out
 
 
+def window_start(end: int, block_size: int) -> int | None:
+    """First index of the "full" mode's window arr[start:end] (its last block_size
+    positions, compress.py:301-320), or None when it holds fewer than 2."""
+    if end < 2:
+        return None
+    t = min(int(block_size), int(end) - 1)
+    return None if t < 2 else int(end) - t - 1
+
+
+def replay_window_end(cfg: ModelConfig, end: int, step_index: int) -> int:
+    """Older window end for the "full" mode's replay steps (compress.py:343-360)."""
+    lo = int(min(end, int(cfg.block_size) + 1))
+    if step_index <= 0 or lo >= end:
+        return int(end)
+    mix = (int(cfg.seed) * 1_000_003 + int(end) * 31) ^ (int(step_index) * 0x9E3779B1)
+    return int(np.random.default_rng(mix & 0x7FFF_FFFF_FFFF).integers(lo, int(end) + 1))
+
+
 def replay_end(cfg: ModelConfig, end: int, step_index: int) -> int:
     every = max(1, int(cfg.online_retrain_every))
     n_chunks = max(1, int(end) // every)
@@ -197,7 +215,9 @@ class ReplenishTTT:
         if not dm.full_params:
             raise ValueError("replenish needs DeviceModel(full_params=True)")
         if cfg.lora_enabled or cfg.motifs:
-            raise ValueError("replenish trains the plain GPT without adapters")
+            raise ValueError("the full-parameter updates train the plain GPT without adapters")
+        if cfg.retrain_mode not in ("replenish", "full"):
+            raise ValueError("ReplenishTTT runs retrain_mode 'replenish' or 'full'")
         self.dm, self.cfg = dm, cfg
         self.n_total = n_total
         self.L = _lib.lib()
@@ -223,6 +243,8 @@ class ReplenishTTT:
         self._anchor = None
         self.w0 = self.delta = self.acc = None
         self.step = 0
+        self.bm = self.bv = None  # "full" mode: the burst steps' own AdamW moments
+        self.bstep = 0
         self.boundaries = 0
         self.xm_last = None
         self.xm_counts: dict[int, int] = {}
@@ -234,6 +256,8 @@ class ReplenishTTT:
         self.m.zero_()
         self.v.zero_()
         self.step = 0
+        self.bm = self.bv = None
+        self.bstep = 0
         self._anchor = None
         self.xm_last = None
         self.dm.refresh()
@@ -328,8 +352,55 @@ class ReplenishTTT:
             raise ValueError("replenish needs the stream's symbols (prefix)")
         self.boundary(prefix, int(end))
 
+    def _burst_adam(self) -> None:
+        """One step of the burst optimizer (lr, betas and decay ttt_burst_*)."""
+        c = self.cfg
+        if self.bm is None:
+            self.bm, self.bv = torch.zeros_like(self.m), torch.zeros_like(self.v)
+        self.bstep += 1
+        hp = _lib.TttHparams(lr=c.ttt_burst_lr, beta1=c.ttt_burst_beta1, beta2=c.ttt_burst_beta2, eps=1e-8,
+                             weight_decay=c.ttt_burst_weight_decay, grad_clip=c.grad_clip)
+        _lib.check(self.L.altxs_adamw(self.dm.layout.total, self.dm.params.data_ptr(), self.grad.data_ptr(),
+                                      self.bm.data_ptr(), self.bv.data_ptr(), C.byref(hp), self.bstep,
+                                      self.partials.data_ptr(), self._stream()), "altxs_adamw")
+
+    def _full(self, prefix: torch.Tensor, end: int) -> None:
+        """The reference's "full" mode (online_retrain without its replenish
+        branch, compress.py:923-1146): mean CE over the last block window; replay
+        windows after the first step; at burst boundaries every step runs on the
+        burst optimizer and walks the segment boundaries oldest -> newest, the
+        last one on the newest window."""
+        cfg = self.cfg
+        every = max(1, int(cfg.online_retrain_every))
+        steps = steps_at(cfg, end)
+        if steps == 0 or window_start(end, cfg.block_size) is None:
+            return
+        replay = bool(cfg.online_retrain_replay) and steps > 1
+        burst = steps > max(1, int(cfg.online_retrain_steps)) and bool(str(cfg.ttt_burst_schedule or ""))
+        bounds = list(range(every, int(end) + 1, every)) or [int(end)]
+        cur = int(end)
+        self.boundaries += 1
+        for si in range(steps):
+            if burst:
+                end_k = int(end) if si == steps - 1 else bounds[si % len(bounds)]
+                if end_k != cur and window_start(end_k, cfg.block_size) is not None:
+                    cur = end_k
+            elif replay and si > 0:
+                end_k = replay_window_end(cfg, end, si)
+                if window_start(end_k, cfg.block_size) is not None:
+                    cur = end_k
+            self._loss_grad(prefix, window_start(cur, cfg.block_size), cur, 0, 0, True)
+            if burst:
+                self._burst_adam()
+            else:
+                self._adam(float(cfg.ttt_lora_lr))
+            self.dm.refresh()  # the next step's forward reads the tensor-core planes
+
     def boundary(self, prefix: torch.Tensor, end: int) -> None:
         cfg = self.cfg
+        if cfg.retrain_mode == "full":
+            self._full(prefix, int(end))
+            return
         every = max(1, int(cfg.online_retrain_every))
         steps = steps_at(cfg, end)
         if steps == 0 or end < 2 or min(int(cfg.block_size), end - 1) < 2:

@@ -20,6 +20,13 @@ over every parameter, lr ``ttt_lora_lr``, betas ``ttt_beta1/2``,
 ``ttt_weight_decay``, global-norm clip ``grad_clip``; burst steps from
 ``parse_burst_schedule`` (config.py:454-473).
 
+The "full" mode (the reference's default ``retrain_mode``; ``online_retrain``
+:923-1146 without the replenish branch) is restated too: the window loss of
+the last ``block_size`` symbols (``_window_xy`` :301-320, ``GPT.forward``
+model.py:1502-1510), replay windows (``_replay_window_end`` :343-360) and
+burst steps on a second AdamW (``ttt_burst_*``) that walk the segment
+boundaries oldest -> newest.
+
 The serial XM fallback (compress.py:721-802) is unreachable: every candidate
 trains on the same window, which always holds >= 2 symbols past ``end >= 2``.
 Pinned against the reference's own ``online_retrain`` (tests/golden/replenish.npz).
@@ -118,6 +125,22 @@ def xm_probe_windows(end: int, every: int, n_probe: int, block_size: int) -> lis
     return out
 
 
+def window_start(end: int, block_size: int) -> int | None:
+    """First index of the last-block window ``arr[start:end]`` (x = [:-1], y = [1:])."""
+    if end < 2:
+        return None
+    t = min(int(block_size), end - 1)
+    return None if t < 2 else end - t - 1
+
+
+def replay_window_end(end: int, step_index: int, seed: int, block_size: int) -> int:
+    lo = int(min(end, int(block_size) + 1))
+    if step_index <= 0 or lo >= end:
+        return int(end)
+    mix = (int(seed) * 1_000_003 + int(end) * 31) ^ (int(step_index) * 0x9E3779B1)
+    return int(np.random.default_rng(mix & 0x7FFF_FFFF_FFFF).integers(lo, int(end) + 1))
+
+
 def replay_chunk_end(cfg: ModelConfig, seed: int, end: int, step_index: int) -> int:
     """Chunk end drawn for replay step ``step_index`` (compress.py:1012-1037)."""
     every = max(1, int(cfg.online_retrain_every))
@@ -152,6 +175,7 @@ class OracleReplenish:
         self.anchor_masks = anchor_masks
         self.anchor = None
         self.xm_last = None
+        self.burst_opt = None
 
     # ---- forward ---------------------------------------------------------------
     def weights(self) -> OracleWeights:
@@ -235,8 +259,10 @@ class OracleReplenish:
 
     # ---- one boundary ----------------------------------------------------------
     def boundary(self, arr: np.ndarray, end: int, n_total: int | None = None) -> float:
-        """Reference ``online_retrain`` in replenish mode at position ``end``."""
+        """Reference ``online_retrain`` in replenish (or full) mode at position ``end``."""
         cfg = self.cfg
+        if cfg.retrain_mode == "full":
+            return self._full(arr, end)
         every = max(1, int(cfg.online_retrain_every))
         steps = online_steps_at(end, cfg, every)
         if steps == 0 or end < 2 or min(int(cfg.block_size), end - 1) < 2:
@@ -283,6 +309,40 @@ class OracleReplenish:
                     self._set_lr(lr_eff if si == steps - 1 else lr_eff * cfg.ttt_replenish_replay_lr_scale)
                 self._step(loss)
             self._apply_anchor(anchor)
+            last = float(loss.detach())
+        return last
+
+    def _full(self, arr: np.ndarray, end: int) -> float:
+        cfg = self.cfg
+        every = max(1, int(cfg.online_retrain_every))
+        steps = online_steps_at(end, cfg, every)
+        if steps == 0 or end < 2 or window_start(end, cfg.block_size) is None:
+            return float("nan")
+        replay = bool(cfg.online_retrain_replay) and steps > 1
+        is_burst = steps > max(1, int(cfg.online_retrain_steps)) and bool(str(cfg.ttt_burst_schedule or ""))
+        if is_burst and self.burst_opt is None:
+            self.burst_opt = torch.optim.AdamW(self.params, lr=cfg.ttt_burst_lr,
+                                               betas=(cfg.ttt_burst_beta1, cfg.ttt_burst_beta2),
+                                               weight_decay=cfg.ttt_burst_weight_decay)
+        bounds = list(range(every, int(end) + 1, every)) or [int(end)]
+        cur = int(end)
+        last = float("nan")
+        for si in range(steps):
+            if is_burst:
+                end_k = int(end) if si == steps - 1 else bounds[si % len(bounds)]
+                if end_k != cur and window_start(end_k, cfg.block_size) is not None:
+                    cur = end_k
+            elif replay and si > 0:
+                end_k = replay_window_end(end, si, cfg.seed, cfg.block_size)
+                if window_start(end_k, cfg.block_size) is not None:
+                    cur = end_k
+            opt = self.burst_opt if is_burst else self.opt
+            opt.zero_grad(set_to_none=True)
+            with torch.enable_grad():
+                loss = self.window_ce(arr[window_start(cur, cfg.block_size): cur], 0)
+                loss.backward()
+            torch.nn.utils.clip_grad_norm_(self.params, cfg.grad_clip)
+            opt.step()
             last = float(loss.detach())
         return last
 

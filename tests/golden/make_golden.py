@@ -387,6 +387,49 @@ def gen_replenish() -> None:
     np.savez_compressed(HERE / "replenish.npz", **out)
 
 
+FULL_CASES = [
+    ("full_plain", dict(ttt_lora_lr=2e-3, ttt_weight_decay=0.01)),
+    ("full_replay", dict(online_retrain_steps=3, online_retrain_replay=True, ttt_lora_lr=1e-3, ttt_beta1=0.9)),
+    ("full_burst", dict(ttt_burst_schedule="50:3", ttt_burst_lr=1e-3, ttt_lora_lr=2e-3)),
+]
+
+
+def gen_full() -> None:
+    """The reference's default retrain mode ("full": every weight on the last
+    block window, replay windows, burst steps on their own AdamW) through its
+    own online_retrain, driven like its stream driver (steps from
+    _online_steps_at, one persistent burst state): per-boundary loss, final weights."""
+    import copy
+
+    from xsa_ttt.compress import _init_online_state, _online_steps_at, online_retrain
+
+    cfg = ModelConfig(**REPLENISH)
+    w = C.synth_weights(cfg, seed=21)
+    base = ref_model(cfg, w)
+    arr = np.random.default_rng(5).integers(0, cfg.vocab_size, size=100).astype(np.int64)
+    out = {"arr": arr.astype(np.int32), "config": np.frombuffer(json.dumps(REPLENISH).encode(), dtype=np.uint8)}
+    out.update({f"w0/{k}": v.detach().numpy() for k, v in base.state_dict().items()})
+    dev = torch.device("cpu")
+    for name, over in FULL_CASES:
+        m = copy.deepcopy(base)
+        h = ref_cfg(cfg)
+        h.retrain_mode = "full"
+        for k, v in over.items():
+            setattr(h, k, v)
+        _, opt = _init_online_state(m, h, dev, True)
+        burst: dict = {}
+        out[f"{name}/over"] = np.frombuffer(json.dumps(over).encode(), dtype=np.uint8)
+        for end in (24, 48, 72, 96):
+            steps = _online_steps_at(end, h, int(h.online_retrain_every))
+            m.train()
+            loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=None, seed=h.seed,
+                                  steps_override=steps, burst_state=burst, n_total=len(arr))
+            out[f"{name}/{end}/loss"] = np.float64(loss)
+        for k, v in m.state_dict().items():
+            out[f"{name}/w/{k}"] = v.detach().numpy().copy()
+    np.savez_compressed(HERE / "full_retrain.npz", **out)
+
+
 CODEC_REF = dict(
     vocab_size=256, num_layers=4, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0, rope_dims=16,
     block_size=64, online_retrain_every=128, seed=77, smear_gate_enabled=True, xsa_last_n=2,
@@ -483,6 +526,7 @@ if __name__ == "__main__":
     gen_lora()
     gen_model_motifs()
     gen_replenish()
+    gen_full()
     gen_codec_ref()
     gen_zipf()
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):

@@ -137,3 +137,28 @@ def test_replenish_engine_round_trip(tensor_cores):
     assert torch.equal(p_enc, dec_dm.params)
     assert enc.ttt.boundaries >= 5 and enc.ttt.xm_counts
     assert not torch.equal(p_enc, enc.ttt.initial)  # the updates did change the model
+
+
+@pytest.mark.parametrize("tensor_cores", [False, True])
+@pytest.mark.parametrize("case", ["full_plain", "full_replay", "full_burst"])
+def test_full_retrain_matches_reference(golden, case, tensor_cores):
+    """The reference's default "full" retrain mode through the device kernels
+    (window loss of the last block, replay windows, burst steps on their own
+    AdamW): final weights against the reference's online_retrain."""
+    from altxs_b200.replenish import ReplenishTTT, state_from_arena
+    from tests.test_oracle_golden import full_case
+
+    g = golden("full_retrain.npz")
+    cfg, w0 = full_case(g, case)
+    dm = _model(cfg, w0, tensor_cores)
+    ttt = ReplenishTTT(dm, n_total=len(g["arr"]))
+    prefix = torch.as_tensor(g["arr"].astype(np.int32), device=DEV)
+    for end in (24, 48, 72, 96):
+        ttt.boundary(prefix, end)
+    torch.cuda.synchronize()
+    got = state_from_arena(dm)
+    ref = {k[len(case) + 3:]: g[k] for k in g.files if k.startswith(f"{case}/w/")}
+    ref = {k: v for k, v in ref.items() if k in got}
+    lr = min(cfg.ttt_lora_lr, cfg.ttt_burst_lr)
+    worst = max(float(np.abs(got[k] - v).max()) for k, v in ref.items())
+    assert worst < (0.5 if tensor_cores else 0.1) * lr, (worst, lr)

@@ -243,3 +243,38 @@ def test_reference_codec_decodes_like_the_reference(golden):
     st = om.new_stream()
     got = np.stack([om.step(st, int(t)).numpy() for t in g["tokens"]])
     assert float(np.abs(got - g["logits"]).max()) < 1e-4
+
+
+def full_case(g, name):
+    """Config and initial state of one golden full-mode scenario."""
+    import json
+
+    from altxs_b200.config import ModelConfig
+
+    base = json.loads(bytes(g["config"]))
+    over = json.loads(bytes(g[f"{name}/over"]))
+    cfg = ModelConfig(**{**base, "retrain_mode": "full", **over})
+    return cfg, {k[3:]: g[k] for k in g.files if k.startswith("w0/")}
+
+
+@pytest.mark.parametrize("name", ["full_plain", "full_replay", "full_burst"])
+def test_oracle_full_retrain_matches_reference(golden, name):
+    """The reference's default retrain mode ("full": every weight on the last
+    block window; replay windows; burst steps on their own AdamW walking the
+    boundaries) against its own online_retrain: loss per boundary, final weights."""
+    from oracle.replenish import OracleReplenish
+
+    g = golden("full_retrain.npz")
+    cfg, w0 = full_case(g, name)
+    o = OracleReplenish(cfg, w0)
+    arr = g["arr"].astype(np.int64)
+    for end in (24, 48, 72, 96):
+        loss = o.boundary(arr, end, n_total=len(arr))
+        assert abs(loss - float(g[f"{name}/{end}/loss"])) < 1e-5, (end, loss)
+    st = o.state()
+    err = max(float(np.abs(st[k] - g[f"{name}/w/{k}"]).max()) for k in st)
+    # Adam moves an entry by about lr per step whatever its gradient's size, so
+    # rounding on entries whose gradient is ~0 (they do not move the loss: the
+    # losses above agree to 1e-5) shows up as a fraction of a step
+    lr = min(cfg.ttt_lora_lr, cfg.ttt_burst_lr)
+    assert err < 0.1 * lr, (err, lr)

@@ -37,5 +37,8 @@ def test_schedule_matches_oracle():
                     end, e, cfg.ttt_replenish_xm_probe_chunks, cfg.block_size)
                 for si in range(3):
                     assert R.replay_end(cfg, end, si) == O.replay_chunk_end(cfg, cfg.seed, end, si)
+                    assert R.replay_window_end(cfg, end, si) == O.replay_window_end(end, si, cfg.seed,
+                                                                                    cfg.block_size)
+            assert R.window_start(end, cfg.block_size) == O.window_start(end, cfg.block_size)
             n += 1
     assert n > 1000
