@@ -144,7 +144,12 @@ def test_replenish_engine_round_trip(tensor_cores):
 def test_full_retrain_matches_reference(golden, case, tensor_cores):
     """The reference's default "full" retrain mode through the device kernels
     (window loss of the last block, replay windows, burst steps on their own
-    AdamW): final weights against the reference's online_retrain."""
+    AdamW) against the reference's online_retrain: the loss of every
+    boundary's last step, and the final weights in units of an optimizer step.
+    A burst's first AdamW step (beta1 0.9, bias-corrected) moves every weight
+    by about +-lr whatever its gradient's size, and it replays windows the
+    model has already trained on, where many gradients are ~0 and their signs
+    follow summation order; the losses pin the model itself."""
     from altxs_b200.replenish import ReplenishTTT, state_from_arena
     from tests.test_oracle_golden import full_case
 
@@ -155,10 +160,12 @@ def test_full_retrain_matches_reference(golden, case, tensor_cores):
     prefix = torch.as_tensor(g["arr"].astype(np.int32), device=DEV)
     for end in (24, 48, 72, 96):
         ttt.boundary(prefix, end)
+        loss = float(ttt.loss[0])
+        assert abs(loss - float(g[f"{case}/{end}/loss"])) < (2e-4 if tensor_cores else 2e-5), (end, loss)
     torch.cuda.synchronize()
     got = state_from_arena(dm)
     ref = {k[len(case) + 3:]: g[k] for k in g.files if k.startswith(f"{case}/w/")}
     ref = {k: v for k, v in ref.items() if k in got}
-    lr = min(cfg.ttt_lora_lr, cfg.ttt_burst_lr)
+    lr = max(cfg.ttt_lora_lr, cfg.ttt_burst_lr if cfg.ttt_burst_schedule else 0.0)
     worst = max(float(np.abs(got[k] - v).max()) for k, v in ref.items())
-    assert worst < (0.5 if tensor_cores else 0.1) * lr, (worst, lr)
+    assert worst < (1.5 if tensor_cores else 0.5) * lr, (worst, lr)
