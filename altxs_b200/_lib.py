@@ -13,6 +13,7 @@ _HERE = Path(__file__).resolve().parent
 LIB_PATH = _HERE / "libaltxs_b200.so"
 
 ALTXS_OK = 0
+ALTXS_EINVAL, ALTXS_ENOSPC, ALTXS_ENOTSUP, ALTXS_ECUDA, ALTXS_ENOMEM = -22, -28, -95, -5, -12
 ST_OVERFLOW, ST_BAD_SYMBOL, ST_BAD_TOTAL, ST_NONFINITE, ST_TIMEOUT, ST_BAD_POS = 1, 2, 4, 8, 16, 32
 CDF_FIXED, CDF_REF = 0, 1
 STEP_LOGITS, STEP_ENCODE, STEP_DECODE = 0, 1, 2
@@ -28,6 +29,9 @@ EXPORTS = (
     "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit",
     "altxs_param_layout_of", "altxs_full_workspace_bytes", "altxs_full_loss_grad", "altxs_adamw",
     "altxs_params_axpy", "altxs_params_anchor", "altxs_split_params",
+    "altxs_create", "altxs_load_weights", "altxs_set_adapters", "altxs_set_ttt", "altxs_set_segment",
+    "altxs_streams_init", "altxs_step_encode", "altxs_step_decode", "altxs_ttt_boundary", "altxs_flush",
+    "altxs_begin_decode", "altxs_get_status", "altxs_ctx_words_per_stream", "altxs_destroy",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
                   "final_norm", "cdf_code", "coder", "ttt")
@@ -156,6 +160,20 @@ def lib():
             "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
             "altxs_gemm_workspace_bytes": (i64, [C.c_int] * 6),
             "altxs_param_layout_of": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(ParamLayout)]),
+            "altxs_create": (vp, [C.POINTER(ModelDesc), C.c_int, C.POINTER(C.c_int)]),
+            "altxs_load_weights": (C.c_int, [vp, C.POINTER(Weights), C.c_int]),
+            "altxs_set_adapters": (C.c_int, [vp, vp]),
+            "altxs_set_ttt": (C.c_int, [vp, C.POINTER(TttHparams)]),
+            "altxs_set_segment": (C.c_int, [vp, i64]),
+            "altxs_streams_init": (C.c_int, [vp, C.c_int, vp]),
+            "altxs_step_encode": (C.c_int, [vp, vp, vp]),
+            "altxs_step_decode": (C.c_int, [vp, vp, vp]),
+            "altxs_ttt_boundary": (C.c_int, [vp, vp]),
+            "altxs_flush": (C.c_int, [vp, vp, vp, vp]),
+            "altxs_begin_decode": (C.c_int, [vp, vp, vp, vp]),
+            "altxs_get_status": (C.c_int, [vp, vp]),
+            "altxs_ctx_words_per_stream": (i64, [vp]),
+            "altxs_destroy": (None, [vp]),
             "altxs_full_workspace_bytes": (i64, [C.POINTER(ModelDesc), C.c_int]),
             "altxs_full_loss_grad": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(DenseWeights), vp,
                                                C.c_int, C.c_int, vp, vp, vp, i64, vp]),

@@ -61,6 +61,9 @@ def parse_args():
                     help="how the windows are filled before timing: code the preceding 2048 symbols "
                          "(default) or write seeded random K/V rows (profiling runs: same per-step work, "
                          "no 2048-step warm-up)")
+    ap.add_argument("--cuda-cores", action="store_true",
+                    help="run the step's linear layers on CUDA cores from the packed codes (the few-stream "
+                         "choice: 0.43 bytes per weight read per step instead of the 4-byte tensor-core planes)")
     ap.add_argument("--replenish", action="store_true",
                     help="instead of the decode benchmark: one full-parameter replenish boundary of the 33M "
                          "model (Forward-XM: gradient of every weight over an 18,432-token window, AdamW, "
@@ -169,7 +172,7 @@ def run_reference(args, rank, world):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic Zipf-Markov (alpha 1.1), seeded random mixed-bit weights",
-        "config": config_block(world, GLOBAL_STREAMS),
+        "config": config_block(world, args.streams, args.cuda_cores),
         "cpu_baseline": {"value": value, "unit": "sym/s", "cores": res["cores"], "kind": res["kind"],
                          "sample": res["sample"]},
         "e2e": {"value": value, "unit": "sym/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -344,10 +347,12 @@ def run_replenish(args) -> None:
     }), flush=True)
 
 
-def config_block(world: int, streams: int) -> dict:
+def config_block(world: int, streams: int, cuda_cores: bool = False) -> dict:
     return {
-        "workload": "box-scale sharded decode: 2048 independent streams split over N GPUs, 33M model "
-                    "(8L/512d/8h, MLP 2048, V 16384) at mixed 2/3/4-bit 3.15 bpw, ctx 2048 window full",
+        "workload": f"{'box-scale sharded' if streams > 1 else 'single-stream'} decode: {streams} independent "
+                    f"stream(s) split over N GPUs, 33M model (8L/512d/8h, MLP 2048, V 16384) at mixed 2/3/4-bit "
+                    f"3.15 bpw, ctx 2048 window full",
+        "linear": "CUDA cores from the packed codes" if cuda_cores else "tensor cores (hi/lo bf16 planes)",
         "global_streams": streams,
         "streams_per_gpu": streams // max(1, world),
         "ctx": 2048,
@@ -414,7 +419,7 @@ def main():
     chunk = W + K
     every = cfg.online_retrain_every
     w = C.synth_weights(cfg, seed=WEIGHT_SEED)
-    dm = DeviceModel(w, dev, rope_positions=cfg.ctx + chunk + 8)
+    dm = DeviceModel(w, dev, rope_positions=cfg.ctx + chunk + 8, tensor_cores=not args.cuda_cores)
     gids = np.arange(rank * n_local, (rank + 1) * n_local)
     data = zipf_markov(cfg.ctx + chunk, cfg.vocab_size, 1000 + gids)  # [n][T]
     symsT = torch.from_numpy(np.ascontiguousarray(data.T)).to(dev)     # [T][n]
@@ -680,7 +685,7 @@ def main():
         "vs_baseline": None,
         "dtype": "f32 math; weights 2/3/4-bit + fp16 scales; KV 24-bit",
         "data": "synthetic: seeded Zipf-Markov streams (alpha 1.1), seeded random mixed-bit weights",
-        "config": config_block(world, n_global),
+        "config": config_block(world, n_global, args.cuda_cores),
         "bits_per_symbol": bits_total / (n_local * chunk),
         "roundtrip_ok": bool(ok and ok_e2e),
         "ttt_updates_timed": timed_boundaries,

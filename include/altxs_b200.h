@@ -29,6 +29,7 @@ extern "C" {
 #define ALTXS_ENOSPC (-28)
 #define ALTXS_ENOTSUP (-95)
 #define ALTXS_ECUDA (-5)
+#define ALTXS_ENOMEM (-12)
 
 /* per-stream device status bits (altxs_ac_state.status) */
 #define ALTXS_ST_OVERFLOW 1u    /* bit buffer full: further bits dropped */
@@ -389,6 +390,52 @@ int altxs_params_anchor(int64_t n, float *p, const float *w0, const float *pull,
  * from the five matrices of a parameter arena. */
 int altxs_split_params(const altxs_model_desc *desc, const float *params, const altxs_split_planes *planes,
                        altxs_stream_t stream);
+
+/* ---- runtime context ----------------------------------------------------------
+ * A handle over the calls above for callers that want the engine's state kept
+ * for them: the reference's compress_full_sha_incremental /
+ * decompress_full_sha_incremental drivers (altxs src/xsa_ttt/incremental.py:
+ * 1561-1976) call create / load_weights / streams_init once, then per symbol
+ * step_encode or step_decode, and at every segment boundary flush (encoder) or
+ * begin_decode (decoder) around ttt_boundary (online_retrain, lora branch,
+ * compress.py:1104-1137); the device coder module xsa_gpu_ac (gpu_ac.py:
+ * 26-365) and StaticACEngine's state (incremental.py:203-1218) are what it
+ * replaces.  All allocation happens in create, load_weights and streams_init;
+ * the per-symbol and boundary calls allocate nothing and never synchronise the
+ * host (get_status does).  Errors: negative return codes for arguments, device
+ * errors per stream in the status words.  Not thread-safe per context. */
+typedef struct altxs_ctx altxs_ctx;
+
+/* NULL on failure (*status = error code). */
+altxs_ctx *altxs_create(const altxs_model_desc *desc, int device, int *status);
+/* Device views of the weights (caller-owned, kept alive by the caller); with
+ * tensor_cores the context builds the hi/lo planes (4 bytes per weight),
+ * without it and with adapters, dense fp32 copies for the update. */
+int altxs_load_weights(altxs_ctx *ctx, const altxs_weights *view, int tensor_cores);
+/* The adapters every stream starts from (device, altxs_lora_floats floats:
+ * the reference's seeded initial A matrices, B = 0). */
+int altxs_set_adapters(altxs_ctx *ctx, const float *d_init);
+/* Hyperparameters of the boundary update (no update when never set). */
+int altxs_set_ttt(altxs_ctx *ctx, const altxs_ttt_hparams *hp);
+/* Symbols per segment (online_retrain_every): sizes the bit buffers. */
+int altxs_set_segment(altxs_ctx *ctx, int64_t segment_symbols);
+/* Allocate and reset n streams (ids unused: streams are independent). */
+int altxs_streams_init(altxs_ctx *ctx, int n_streams, const uint64_t *ids);
+/* One symbol per stream: d_tokens [n] device (encode input / decode output). */
+int altxs_step_encode(altxs_ctx *ctx, const int32_t *d_tokens, altxs_stream_t stream);
+int altxs_step_decode(altxs_ctx *ctx, int32_t *d_tokens_out, altxs_stream_t stream);
+/* One AdamW step of every stream's adapters on its last window of coded symbols. */
+int altxs_ttt_boundary(altxs_ctx *ctx, altxs_stream_t stream);
+/* Finish the segments: d_bits [n][altxs_ctx_words_per_stream], d_nbits [n]
+ * (device, segment k of stream i = the first nbits[i] bits of row i, MSB-first);
+ * the coders restart for the next segment. */
+int altxs_flush(altxs_ctx *ctx, uint32_t *d_bits, uint64_t *d_nbits, altxs_stream_t stream);
+/* Load one segment per stream and seed the decoders. */
+int altxs_begin_decode(altxs_ctx *ctx, const uint32_t *d_bits, const uint64_t *d_nbits, altxs_stream_t stream);
+/* Waits; status (host [n] or NULL) gets each stream's status word; returns their OR. */
+int altxs_get_status(altxs_ctx *ctx, int32_t *status);
+int64_t altxs_ctx_words_per_stream(const altxs_ctx *ctx);
+void altxs_destroy(altxs_ctx *ctx);
 
 /* ---- failure detection ------------------------------------------------------
  * No counterpart in the reference (its device waits do not exist; its coder

@@ -14,7 +14,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def _declared() -> list[str]:
     text = (ROOT / "include" / "altxs_b200.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|int64_t|uint32_t|const char \*)\s*(altxs_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|uint32_t|void|const char \*|altxs_ctx \*)\s*(altxs_\w+)\s*\(", text, re.M)))
 
 
 @pytest.fixture(scope="module")
