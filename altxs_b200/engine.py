@@ -585,7 +585,7 @@ class Engine:
         for t in range(T):
             if t > 0 and t % every == 0:
                 rows = [i for i in range(n) if lens[i] > t]
-                self._boundary_encode(b, rows, segs, t, symsT_d[:, 0])
+                self._boundary_encode(b, rows, segs, t, symsT_d)
             active = lens > t
             if not active.all():
                 b.set_active(active)
@@ -647,7 +647,7 @@ class Engine:
                 if rows:
                     b.set_active(None)
                     if self.ttt is not None:
-                        self._update(b, rows, t, out[:, 0])
+                        self._update(b, rows, t, out)
                     if self.reset is not None:
                         self.reset(b, rows, t)
                     b.begin_decode({i: segs[i][t // every] for i in rows})

@@ -43,11 +43,14 @@ def chunk_ctx_start(chunk_start: int, block_size: int) -> tuple[int, int]:
     return p0, max(0, p0 - int(block_size))
 
 
-def steps_at(cfg: ModelConfig, position: int) -> int:
+def steps_at(cfg: ModelConfig, position: int, gate: bool = True) -> int:
+    """Steps of the update at ``position`` (_online_steps_at, compress.py:323-341);
+    ``gate=False`` for callers that decide the boundaries themselves (streams on
+    shifted segment clocks)."""
     every = max(1, int(cfg.online_retrain_every))
     if position > 0 and cfg.ttt_bootstrap_steps > 0 and position == cfg.ttt_bootstrap_symbols:
         return int(cfg.ttt_bootstrap_steps)
-    if position <= 0 or position % every:
+    if position <= 0 or (gate and position % every):
         return 0
     steps = int(cfg.online_retrain_steps)
     for entry in str(cfg.ttt_burst_schedule or "").split(","):
@@ -348,8 +351,11 @@ class ReplenishTTT:
 
     # ---- one boundary ----------------------------------------------------------
     def __call__(self, b, rows, end: int, prefix: torch.Tensor | None = None) -> None:
+        """``prefix``: the stream's symbols on the device, [>= end] or [>= end][1]."""
         if prefix is None:
             raise ValueError("replenish needs the stream's symbols (prefix)")
+        if prefix.dim() == 2:
+            prefix = prefix[:, 0].contiguous()
         self.boundary(prefix, int(end))
 
     def _burst_adam(self) -> None:

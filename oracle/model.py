@@ -353,16 +353,29 @@ class OracleTTT:
         )
 
     def update(self, arr: np.ndarray, end: int) -> float:
+        """The lora branch of online_retrain at boundary ``end``
+        (compress.py:923-1146): ``_online_steps_at`` steps, the first on the
+        newest window, later ones on replay windows (``_replay_window_end``)."""
+        from oracle.replenish import online_steps_at, replay_window_end
+
         cfg = self.model.cfg
+        steps = online_steps_at(end, cfg, max(1, int(cfg.online_retrain_every)))
         xy = window_xy(arr, end, cfg.block_size)
-        if xy is None:
+        if steps == 0 or xy is None:
             return float("nan")
         x, y = xy
-        self.opt.zero_grad(set_to_none=True)
-        with torch.enable_grad():
-            logits = self.model.window_logits(x, self.lora)
-            loss = F.cross_entropy(logits.float(), y, reduction="mean")
-            loss.backward()
-        torch.nn.utils.clip_grad_norm_(self.params, cfg.grad_clip)
-        self.opt.step()
+        replay = bool(cfg.online_retrain_replay) and steps > 1
+        loss = None
+        for si in range(steps):
+            if replay and si > 0:
+                xy_k = window_xy(arr, replay_window_end(end, si, cfg.seed, cfg.block_size), cfg.block_size)
+                if xy_k is not None:
+                    x, y = xy_k
+            self.opt.zero_grad(set_to_none=True)
+            with torch.enable_grad():
+                logits = self.model.window_logits(x, self.lora)
+                loss = F.cross_entropy(logits.float(), y, reduction="mean")
+                loss.backward()
+            torch.nn.utils.clip_grad_norm_(self.params, cfg.grad_clip)
+            self.opt.step()
         return float(loss.detach())

@@ -258,6 +258,34 @@ def gen_lora() -> None:
     np.savez_compressed(HERE / "lora_small.npz", **out)
 
 
+def gen_lora_steps() -> None:
+    """The reference's online_retrain in lora mode with several steps per
+    boundary (replay windows after the first, _replay_window_end) driven like
+    its stream driver: adapters after two boundaries, the losses."""
+    from xsa_ttt.compress import _init_online_state, _online_steps_at, online_retrain
+
+    cfg = small_cfg()
+    w = C.synth_weights(cfg, seed=7)
+    m = ref_model(cfg, w)
+    h = m.cfg
+    h.online_retrain_steps = 3
+    h.online_retrain_replay = True
+    dev = torch.device("cpu")
+    lora, opt = _init_online_state(m, h, dev, True)
+    init = {k: v.detach().clone().numpy() for k, v in lora.state_dict().items()}
+    arr = np.random.default_rng(10).integers(0, cfg.vocab_size, size=200).astype(np.int64)
+    every = int(h.online_retrain_every)
+    out = {"arr": arr.astype(np.int32)}
+    for end in (every, 2 * every):
+        steps = _online_steps_at(end, h, every)
+        loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=lora, seed=h.seed,
+                              steps_override=steps, n_total=len(arr))
+        out[f"{end}/loss"] = np.float64(loss)
+    out.update({f"init/{k}": v for k, v in init.items()})
+    out.update({f"final/{k}": v.detach().clone().numpy() for k, v in lora.state_dict().items()})
+    np.savez_compressed(HERE / "lora_steps.npz", **out)
+
+
 MOTIFS = dict(
     vocab_size=256, num_layers=6, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0,
     rope_dims=16, block_size=64, online_retrain_every=128, seed=3, retrain_mode="none",
@@ -524,6 +552,7 @@ if __name__ == "__main__":
     print(gen_codec())
     gen_model()
     gen_lora()
+    gen_lora_steps()
     gen_model_motifs()
     gen_replenish()
     gen_full()

@@ -121,3 +121,39 @@ def test_engine_roundtrip_with_ttt(n_streams):
     # the adapters moved (updates happened)
     no = Engine(dm).encode(streams)
     assert any(a.payload != b.payload for a, b in zip(enc, no))
+
+
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_lora_steps_with_replay_match_reference(golden, tensor_cores):
+    """LoraTTT with three steps per boundary (replay windows after the first,
+    read from the stream's symbols) against the reference's own online_retrain
+    in lora mode: the adapters after two boundaries."""
+    from altxs_b200.engine import DeviceModel, StreamBatch
+    from altxs_b200.lora import lora_shapes
+    from altxs_b200.ttt import LoraTTT
+
+    g = golden("lora_steps.npz")
+    cfg = ModelConfig(**{**SMALL, "online_retrain_steps": 3, "online_retrain_replay": True})
+    dm = DeviceModel(C_.synth_weights(cfg, seed=7), DEV, tensor_cores=tensor_cores)
+    ttt = LoraTTT(dm)
+    b = StreamBatch(dm, 1, words_per_stream=8, hist_len=cfg.ctx + 2)
+    arr = g["arr"].astype(np.int32)
+    prefix = torch.as_tensor(arr[:, None].copy(), device=DEV)
+    every = cfg.online_retrain_every
+    for end in (every, 2 * every):
+        pos = torch.arange(max(0, end - b.hist_len), end, device=DEV)  # the ring holds the last hist_len symbols
+        b.hist[0].index_copy_(0, pos % b.hist_len, prefix[pos, 0])
+        ttt(b, [0], end, prefix=prefix)
+    torch.cuda.synchronize()
+    ref = []
+    names = {"lm": "lm_head_lora"}
+    for i in range(cfg.num_layers):
+        for t in ("q", "k", "v", "o"):
+            names[f"{t}{i}"] = f"{t}_loras.{i}"
+    for name in lora_shapes(cfg):
+        ref += [g[f"final/{names[name]}.A"].reshape(-1), g[f"final/{names[name]}.B"].reshape(-1)]
+    ref = np.concatenate(ref)
+    got = b.lora[0].cpu().numpy()
+    # Adam steps of lr per entry: agreement within a small fraction of one step
+    err = float(np.abs(got - ref).max())
+    assert err < (0.3 if tensor_cores else 0.05) * cfg.ttt_lora_lr, err

@@ -278,3 +278,26 @@ def test_oracle_full_retrain_matches_reference(golden, name):
     # losses above agree to 1e-5) shows up as a fraction of a step
     lr = min(cfg.ttt_lora_lr, cfg.ttt_burst_lr)
     assert err < 0.1 * lr, (err, lr)
+
+
+def test_oracle_lora_steps_match_reference(golden):
+    """Three LoRA steps per boundary (replay windows after the first) against
+    the reference's own online_retrain in lora mode: losses and adapters."""
+    g = golden("lora_steps.npz")
+    cfg = ModelConfig(**{**SMALL, "online_retrain_steps": 3, "online_retrain_replay": True})
+    m = OracleModel(OracleWeights.from_model_weights(C.synth_weights(cfg, seed=7)))
+    ttt = OracleTTT(m)
+    names = {"lm": "lm_head_lora"}
+    for i in range(cfg.num_layers):
+        for t in ("q", "k", "v", "o"):
+            names[f"{t}{i}"] = f"{t}_loras.{i}"
+    for ours, ref in names.items():
+        assert torch.equal(ttt.lora.A[ours], torch.from_numpy(g[f"init/{ref}.A"])), ours
+    arr = g["arr"].astype(np.int64)
+    every = cfg.online_retrain_every
+    for end in (every, 2 * every):
+        loss = ttt.update(arr, end)
+        assert abs(loss - float(g[f"{end}/loss"])) < 1e-5, (end, loss)
+    for ours, ref in names.items():
+        np.testing.assert_allclose(ttt.lora.A[ours].detach().numpy(), g[f"final/{ref}.A"], atol=1e-6)
+        np.testing.assert_allclose(ttt.lora.B[ours].detach().numpy(), g[f"final/{ref}.B"], atol=1e-6)
