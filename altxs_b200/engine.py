@@ -152,6 +152,7 @@ class DeviceModel:
             view = self.params[off: off + src.numel()]
             view.copy_(src)
             self.small[name] = view
+        self.params_initial = self.params.clone()  # the shipped weights: every stream starts from them
         self._weights_struct = None
 
     def arena(self, name: str) -> torch.Tensor:

@@ -54,16 +54,26 @@ def _resolve(model, cfg, device) -> tuple[DeviceModel, ModelConfig]:
         if cfg is not None:
             c = cfg if isinstance(cfg, ModelConfig) else ModelConfig.from_reference_cfg(cfg)
             model.cfg = c
-        dm = DeviceModel(model, device)
+        # the full-parameter updates train the model itself: every weight in one arena
+        dm = DeviceModel(model, device, full_params=model.cfg.retrain_mode in ("replenish", "full"))
     return dm, dm.cfg
 
 
-def _make_engine(dm: DeviceModel, online_retrain_enabled: bool) -> Engine:
+def _make_engine(dm: DeviceModel, online_retrain_enabled: bool, n_total: int | None = None) -> Engine:
+    """Engine with the configured update: LoRA adapters, or every weight
+    ("replenish" / "full", one stream at a time from the shipped weights)."""
     ttt = None
+    mode = dm.cfg.retrain_mode
     if online_retrain_enabled and dm.cfg.lora_enabled:
         from .ttt import LoraTTT
 
         ttt = LoraTTT(dm)
+    elif online_retrain_enabled and mode in ("replenish", "full"):
+        from .replenish import ReplenishTTT
+
+        if not dm.full_params:
+            raise ValueError(f"retrain_mode={mode!r} needs DeviceModel(full_params=True)")
+        ttt = ReplenishTTT(dm, n_total=n_total)
     return Engine(dm, ttt=ttt)
 
 
@@ -100,7 +110,7 @@ def compress_full_sha_incremental(
     n = int(arr.shape[0])
     every = max(1, int(cfg.online_retrain_every))
     t0 = time.time()
-    eng = _make_engine(dm, online_retrain_enabled)
+    eng = _make_engine(dm, online_retrain_enabled, n_total=n)
     res = eng.encode([arr])[0]
     src_sha = hashlib.sha256(_symbols_for_hash(arr)).hexdigest()
     rows = []
@@ -110,7 +120,7 @@ def compress_full_sha_incremental(
     dec_sha = sha_ok = first_mismatch = None
     decoded_bytes = None
     if do_verify:
-        eng2 = _make_engine(dm, online_retrain_enabled)
+        eng2 = _make_engine(dm, online_retrain_enabled, n_total=n)
         dec = eng2.decode([res.payload], [n])[0].astype(arr.dtype)
         blob = _symbols_for_hash(dec)
         dec_sha = hashlib.sha256(blob).hexdigest()
@@ -126,7 +136,8 @@ def compress_full_sha_incremental(
     if progress:
         dt = time.time() - t0
         print(f"[AC b200] {n:,} sym in {dt:.1f}s ({n / max(dt, 1e-9):,.0f} sym/s), bpb={bpb:.4f}", flush=True)
-    retrains = (n - 1) // every if (online_retrain_enabled and cfg.lora_enabled and n > 0) else 0
+    updates = cfg.lora_enabled or cfg.retrain_mode in ("replenish", "full")
+    retrains = (n - 1) // every if (online_retrain_enabled and updates and n > 0) else 0
     ce = getattr(eng.ttt, "ce_history", []) if eng.ttt is not None else []
     return {
         "payload": res.payload,
@@ -168,7 +179,7 @@ def decompress_full_sha_incremental(
     n = int(n_symbols)
     every = max(1, int(cfg.online_retrain_every))
     t0 = time.time()
-    eng = _make_engine(dm, online_retrain_enabled)
+    eng = _make_engine(dm, online_retrain_enabled, n_total=n)
     dec = eng.decode([payload], [n])[0]
     arr = dec.astype(np.uint8 if cfg.vocab_size <= 256 else np.uint16)
     blob = _symbols_for_hash(arr)
@@ -178,7 +189,8 @@ def decompress_full_sha_incremental(
     if progress:
         dt = time.time() - t0
         print(f"[AC b200 decode] {n:,} sym in {dt:.1f}s ({n / max(dt, 1e-9):,.0f} sym/s)", flush=True)
-    retrains = (n - 1) // every if (online_retrain_enabled and cfg.lora_enabled and n > 0) else 0
+    updates = cfg.lora_enabled or cfg.retrain_mode in ("replenish", "full")
+    retrains = (n - 1) // every if (online_retrain_enabled and updates and n > 0) else 0
     return {
         "n_symbols": n,
         "payload_bytes": len(payload),

@@ -241,7 +241,7 @@ class ReplenishTTT:
         # slot 0: the training chunk's loss; then one per (candidate, probe window)
         self.loss = torch.zeros(1 + 4 * max(1, int(cfg.ttt_replenish_xm_probe_chunks)), dtype=torch.float32,
                                 device=dev)
-        self.initial = dm.params.detach().clone()
+        self.initial = dm.params_initial
         self.anchor_masks = anchor_masks
         self._anchor = None
         self.w0 = self.delta = self.acc = None

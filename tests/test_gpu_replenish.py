@@ -169,3 +169,23 @@ def test_full_retrain_matches_reference(golden, case, tensor_cores):
     lr = max(cfg.ttt_lora_lr, cfg.ttt_burst_lr if cfg.ttt_burst_schedule else 0.0)
     worst = max(float(np.abs(got[k] - v).max()) for k, v in ref.items())
     assert worst < (1.5 if tensor_cores else 0.5) * lr, (worst, lr)
+
+
+@pytest.mark.parametrize("mode", ["full", "replenish"])
+def test_entry_points_with_full_parameter_update(mode):
+    """The reference-mirroring entry points in the reference's default "full"
+    mode and in replenish mode: the update trains every weight of the model at
+    each boundary on both sides; verify_decode restores the input and a
+    separate decompress call does too (both start from the shipped weights)."""
+    from altxs_b200.config import ModelConfig
+    from altxs_b200.incremental import compress_full_sha_incremental, decompress_full_sha_incremental
+
+    cfg = ModelConfig(vocab_size=64, num_layers=2, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0,
+                      rope_dims=8, block_size=16, online_retrain_every=40, retrain_mode=mode, ttt_lora_lr=2e-3,
+                      online_retrain_steps=2, ttt_replenish_warmup_steps=1)
+    w = C.synth_weights(cfg, seed=6)
+    data = np.random.default_rng(2).integers(0, 64, size=170).astype(np.uint8)
+    res = compress_full_sha_incremental(w, data, cfg=cfg, device=DEV, progress=False, verify_decode=True)
+    assert res["sha256_ok"] and res["roundtrip_ok"] and res["retrain_count"] == 4
+    dec = decompress_full_sha_incremental(w, res["payload"], len(data), cfg=cfg, device=DEV, progress=False)
+    assert dec["decoded_sha256"] == res["sha256"]
