@@ -153,6 +153,20 @@ class DeviceModel:
             view.copy_(src)
             self.small[name] = view
         self.params_initial = self.params.clone()  # the shipped weights: every stream starts from them
+        if not self.tensor_cores:
+            # the CUDA-core step reads the live arena as 32-bit groups (raw fp32
+            # values, scale 1): the same group-order dot products, on the updated weights
+            for name in ("emb", "qkv", "o", "up", "down"):
+                q = self.q[name]
+                rows, cols = q.rows, q.cols
+                G = cols // 64
+                row_off8 = (np.arange(rows, dtype=np.int64) * (cols // 2)).astype(np.uint32)
+                gd = (np.uint32(0x3C00) | np.uint32(4 << 16)
+                      | (np.arange(G, dtype=np.uint32) * np.uint32(32)) << np.uint32(20))
+                gdesc = np.broadcast_to(gd, (rows, G)).astype(np.uint32)
+                ro, gdt = self._up(_i32(row_off8)), self._up(_i32(gdesc))
+                self.q[name] = _lib.QMat(codes=base + 4 * getattr(lay, name), row_off8=ro.data_ptr(),
+                                         gdesc=gdt.data_ptr(), lut=None, glut=None, rows=rows, cols=cols)
         self._weights_struct = None
 
     def arena(self, name: str) -> torch.Tensor:

@@ -189,3 +189,31 @@ def test_entry_points_with_full_parameter_update(mode):
     assert res["sha256_ok"] and res["roundtrip_ok"] and res["retrain_count"] == 4
     dec = decompress_full_sha_incremental(w, res["payload"], len(data), cfg=cfg, device=DEV, progress=False)
     assert dec["decoded_sha256"] == res["sha256"]
+
+
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_step_reads_the_updated_weights(golden, tensor_cores):
+    """After a full-parameter boundary the decode step runs the updated model:
+    its logits equal the oracle's on the arena's weights (both linear paths;
+    the CUDA-core path reads the arena as dense groups)."""
+    from altxs_b200.replenish import ReplenishTTT, state_from_arena
+    from oracle.model import OracleModel
+    from tests.test_gpu_step import _run_logits
+
+    g = golden("replenish.npz")
+    cfg, w0, _ = replenish_case(g, "xm")
+    dm = _model(cfg, w0, tensor_cores)
+    ttt = ReplenishTTT(dm, n_total=100)
+    prefix = torch.as_tensor(g["arr"].astype(np.int32), device=DEV)
+    for end in (24, 48):
+        ttt.boundary(prefix, end)
+    torch.cuda.synchronize()
+    st = state_from_arena(dm)
+    assert float(np.abs(st["qo_bank"] - w0["qo_bank"]).max()) > 1e-4  # the update moved the weights
+    om = OracleReplenish(cfg, st).model()
+    toks = g["arr"][:30]
+    got = _run_logits(dm, [toks])[0]
+    ref_st = om.new_stream()
+    ref = np.stack([om.step(ref_st, int(t)).numpy() for t in toks])
+    assert float(np.abs(got - ref).max()) < 2e-3
+    del OracleModel
