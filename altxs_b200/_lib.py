@@ -87,7 +87,8 @@ class ParamLayout(C.Structure):
     """Segments (floats) of a full parameter arena (altxs_param_layout)."""
 
     _fields_ = [(k, C.c_int64) for k in ("emb", "qkv", "o", "up", "down", "q_gain", "attn_scale", "mlp_scale",
-                                         "resid_mix", "skip_weights", "skip_gates", "total")]
+                                         "resid_mix", "skip_weights", "skip_gates", "smear_gate", "smear_lambda",
+                                         "attn_gate_w", "softcap", "parallel_post", "parallel_resid", "total")]
 
 
 class TttHparams(C.Structure):

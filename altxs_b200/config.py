@@ -4,7 +4,7 @@
 (altxs ``src/xsa_ttt/config.py:20-189``) that the per-symbol loop reads.  The
 reference motifs that sit on top of the plain GPT (XSA, SmearGate,
 SparseAttnGate, depth loops, parallel residual lanes, asymmetric softcap) run
-in the decode step with frozen weights; ``from_reference_cfg`` refuses the
+in the decode step and in the full-parameter updates; ``from_reference_cfg`` refuses the
 ones this engine does not compute (output gates, YaRN, untied heads) instead
 of silently computing a different model.
 
@@ -95,8 +95,8 @@ class ModelConfig:
     ttt_burst_beta2: float = 0.999
     ttt_burst_weight_decay: float = 0.01
     # reference model motifs (model.py:982-1110; all off = the plain GPT).  The
-    # step and the oracle run them with frozen weights; the test-time LoRA
-    # update covers the plain GPT only.
+    # step, the oracle and the full-parameter updates (replenish, full) run
+    # them; the test-time LoRA update covers the plain GPT only.
     smear_gate_enabled: bool = False      # previous-token smear on the raw embedding
     gate_window: int = 12                 # input width of the smear / attention gates
     xsa_last_n: int = 0                   # XSA (value-direction removal) on the last n layers
@@ -202,8 +202,12 @@ class ModelConfig:
             raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
         if self.retrain_mode not in ("lora", "replenish", "full", "none"):
             raise ValueError("retrain_mode must be 'lora', 'replenish', 'full' or 'none'")
-        if self.retrain_mode in ("replenish", "full") and self.motifs:
-            raise ValueError("the full-parameter updates cover the plain GPT; turn the motifs off")
+        if self.retrain_mode in ("replenish", "full") and self.parallel_start_layer > 0:
+            dec = self.layer_schedule[1]
+            par = [i >= self.parallel_start_layer for i in dec]
+            if any(p and not q for p, q in zip(par, par[1:])):
+                raise ValueError("the full-parameter update needs every decoder application after the first "
+                                 "parallel one to run parallel lanes")
         if self.context_mode not in ("sliding", "reset"):
             raise ValueError("context_mode must be 'sliding' or 'reset'")
         if self.parallel_final_lane not in ("mean", "attn", "mlp"):
@@ -254,8 +258,8 @@ class ModelConfig:
                 setattr(out, f.name, v)
         if out.retrain_mode not in ("lora", "replenish", "full", "none"):
             out.retrain_mode = "none"
-        if out.motifs and out.retrain_mode != "none":
-            out.retrain_mode = "none"  # the updates cover the plain GPT only
+        if out.motifs and out.retrain_mode == "lora":
+            out.retrain_mode = "none"  # the LoRA update covers the plain GPT only
         return out
 
 

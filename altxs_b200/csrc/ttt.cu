@@ -20,18 +20,27 @@ using namespace altxs;
 
 namespace {
 
+// Per-application tape entries are indexed by the layer application a (depth
+// loops apply a physical layer i more than once); weights by i.
 struct TD {
-    int T, V, L, d, H, Hkv, hd, kvd, F, qn, r, enc, nskip, G, rd;
-    int first;  // first scored position of the loss (rows before it are context only)
-    int full;   // full-parameter gradient (replenish): extra tape, P recomputed per layer
+    int T, V, L, d, H, Hkv, hd, kvd, F, qn, r, G, rd;
+    int A;          // layer applications (= L without depth loops)
+    int enc, nskip; // encoder applications (the skips' sources); skips taken by the decoder
+    int first;      // first scored position of the loss (rows before it are context only)
+    int full;       // full-parameter gradient (replenish): extra tape, P recomputed per layer
+    // motifs (full-parameter gradient only)
+    int smear, gw, xsa_from, sgate, asym, par, pfinal;
+    float sgs;
 };
+
+constexpr int kMaxApps = 64;
 
 enum FillMode { kFillLora, kFillPrefill, kFillFull };
 
 struct Tape {
     // forward state
     float *x0, *x, *skip;  // skip [enc][T][d]
-    // per layer [L][...]
+    // per layer application [A][...]
     float *xin, *inv1, *n, *qkv, *hinv, *qr, *kr, *P, *tq, *tk, *tv, *to, *xmid, *inv2, *n2, *u;
     // scratch
     float *y, *ao, *hbuf;
@@ -43,6 +52,10 @@ struct Tape {
     // outputs, o- and down-projection outputs [L][T][d]; raw embedding rows and
     // their inverse rms; d(x0); per-row products [T][4d] and their column partials
     float *xraw, *yl, *aol, *doutl, *eraw, *inv0, *dx0, *colbuf, *cpart;
+    // motifs: smeared embedding rows before the norm [T][d]; attention outputs
+    // before XSA and the gate [A][T][d]; the second lane and its gradient, the
+    // gradient of the attention read of a parallel block [T][d]; XSA's d(v) [T][kvd]
+    float *esm, *yraw, *lane1, *dl1, *dread, *dvx;
 };
 
 constexpr int kColChunks = 64;  // row chunks of a column sum (summed in order)
@@ -60,8 +73,6 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, FillMode mode = kFillLora) {
     D.F = dsc.mlp_hidden;
     D.qn = D.d + 2 * D.kvd;
     D.r = dsc.lora_rank;
-    D.enc = D.L / 2;
-    D.nskip = D.enc < D.L - D.enc ? D.enc : D.L - D.enc;
     D.G = D.H / (D.Hkv > 0 ? D.Hkv : 1);
     D.rd = dsc.rope_dims;
     D.first = 0;
@@ -76,12 +87,49 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, FillMode mode = kFillLora) {
     }
     if (D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
     if (D.hd > 128 || D.rd > D.hd || D.rd % 2) return ALTXS_EINVAL;
-    // the window forward here is the plain GPT stack: one application per layer, no motifs
-    if ((dsc.n_virtual > 0 && dsc.n_virtual != D.L) || dsc.schedule || dsc.smear_gate || dsc.xsa_last_n ||
-        dsc.sparse_gate || dsc.asym_softcap || dsc.parallel_start)
-        return ALTXS_ENOTSUP;
+    D.A = dsc.n_virtual > 0 ? dsc.n_virtual : D.L;
+    if (D.A != D.L && !dsc.schedule) return ALTXS_EINVAL;
+    if (D.A > kMaxApps || D.L > kMaxApps) return ALTXS_ENOTSUP;
+    if (dsc.schedule)
+        for (int a = 0; a < D.A; ++a)
+            if (dsc.schedule[a] < 0 || dsc.schedule[a] >= D.L) return ALTXS_EINVAL;
+    D.enc = dsc.n_encoder > 0 ? dsc.n_encoder : D.A / 2;
+    if (D.enc > D.A) return ALTXS_EINVAL;
+    D.nskip = D.enc < D.A - D.enc ? D.enc : D.A - D.enc;
+    if (dsc.xsa_last_n < 0 || dsc.xsa_last_n > D.L || dsc.parallel_start < 0) return ALTXS_EINVAL;
+    if (dsc.parallel_final < 0 || dsc.parallel_final > 2) return ALTXS_EINVAL;
+    D.smear = dsc.smear_gate != 0;
+    D.sgate = dsc.sparse_gate != 0;
+    D.sgs = dsc.sparse_gate_scale;
+    D.xsa_from = dsc.xsa_last_n > 0 ? D.L - dsc.xsa_last_n : D.L;
+    D.asym = dsc.asym_softcap != 0;
+    D.par = dsc.parallel_start;
+    D.pfinal = dsc.parallel_final;
+    D.gw = 0;
+    if (D.smear || D.sgate) {
+        D.gw = dsc.gate_window;
+        if (D.gw < 1 || D.gw > D.d || (D.sgate && (D.gw > D.hd || D.H > 128))) return ALTXS_EINVAL;
+    }
+    // parallel lanes: once a decoder application runs two lanes, every later one
+    // must (the reference would run a plain block on its stale single stream)
+    if (D.par > 0) {
+        bool on = false;
+        for (int a = D.enc; a < D.A; ++a) {
+            const bool p = (dsc.schedule ? dsc.schedule[a] : a) >= D.par;
+            if (on && !p) return ALTXS_ENOTSUP;
+            on = on || p;
+        }
+    }
+    const bool motif = D.A != D.L || dsc.schedule || D.smear || dsc.xsa_last_n || D.sgate || D.asym || D.par;
+    // the LoRA update and the context prefill run the plain GPT stack
+    if (motif && mode != kFillFull) return ALTXS_ENOTSUP;
     return ALTXS_OK;
 }
+
+// the layer application a runs two lanes (a decoder application of a layer >= parallel_start)
+inline bool par_app(const TD &D, const int *sched, int a) { return D.par > 0 && a >= D.enc && sched[a] >= D.par; }
+// attention output rewritten before the o-projection (XSA on this layer, or the sparse gate)
+inline bool ymotif(const TD &D, int i) { return i >= D.xsa_from || D.sgate; }
 
 int64_t carve(const TD &D, void *base, Tape *tp) {
     unsigned char *p = static_cast<unsigned char *>(base);
@@ -91,7 +139,7 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
         off += align_up(nfl * 4, 256);
         return r;
     };
-    const int64_t T = D.T, L = D.L, d = D.d;
+    const int64_t T = D.T, L = D.A, d = D.d;  // per-application arrays
     Tape t{};
     t.x0 = take(T * d);
     t.x = take(T * d);
@@ -145,9 +193,19 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
         t.eraw = take(T * d);
         t.inv0 = take(T);
         t.dx0 = take(T * d);
-        const int64_t cw = 4 * d > D.H ? 4 * d : D.H;
+        int64_t cw = 4 * d > D.H ? 4 * d : D.H;
+        cw = cw > (int64_t)D.H * D.gw ? cw : (int64_t)D.H * D.gw;  // sparse gate weights
+        cw = cw > D.gw + 1 ? cw : D.gw + 1;                          // smear gate, lambda
         t.colbuf = take(T * cw);
         t.cpart = take((int64_t)kColChunks * cw);
+        if (D.smear) t.esm = take(T * d);
+        if (D.xsa_from < D.L || D.sgate) t.yraw = take(L * T * d);
+        if (D.par) {
+            t.lane1 = take(T * d);
+            t.dl1 = take(T * d);
+            t.dread = take(T * d);
+        }
+        if (D.xsa_from < D.L) t.dvx = take(T * D.kvd);
     }
     if (tp) *tp = t;
     return off;
@@ -156,17 +214,33 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
 // ---- forward row kernels -------------------------------------------------
 
 // embedding rows (dense fp32 copy when given, else the mixed-bit codes) + RMSNorm;
-// the full-parameter gradient keeps the raw rows and their inverse rms
-__global__ void t_embed(TD D, const int32_t *tok, altxs_qmat emb, const float *embd, float *x0, float *x, Tape tp) {
+// the full-parameter gradient keeps the raw rows and their inverse rms.  Smear
+// gate (model.py:1364-1375): row t >= 1 adds lambda*sigmoid(raw_t[:gw] . g) times
+// row t-1; the window's first row is left alone.
+__device__ __forceinline__ float emb_row_elem(const TD &D, altxs_qmat emb, const float *embd, int tk, int k) {
+    if (tk < 0 || tk >= D.V) return 0.0f;
+    return embd ? embd[(int64_t)tk * D.d + k] : qmat_elem(emb, tk, k);
+}
+__global__ void t_embed(TD D, const int32_t *tok, altxs_qmat emb, const float *embd, float *x0, float *x, Tape tp,
+                        altxs_weights w) {
     __shared__ float red[32];
     const int t = blockIdx.x;
     const int tk = tok[t];
+    float gate = 0.0f;
+    if (D.smear && t > 0) {
+        float z = 0.0f;
+        for (int k = threadIdx.x; k < D.gw; k += blockDim.x) z = __fmaf_rn(emb_row_elem(D, emb, embd, tk, k), w.smear_gate[k], z);
+        z = block_sum(z, red);
+        gate = __fmul_rn(w.smear_lambda[0], sigmoidf_(z));
+        __syncthreads();
+    }
     float ss = 0.0f;
     for (int k = threadIdx.x; k < D.d; k += blockDim.x) {
-        float v = 0.0f;
-        if (tk >= 0 && tk < D.V) v = embd ? embd[(int64_t)tk * D.d + k] : qmat_elem(emb, tk, k);
-        x0[(int64_t)t * D.d + k] = v;
+        float v = emb_row_elem(D, emb, embd, tk, k);
         if (tp.eraw) tp.eraw[(int64_t)t * D.d + k] = v;
+        if (D.smear && t > 0) v = __fadd_rn(v, __fmul_rn(gate, emb_row_elem(D, emb, embd, tok[t - 1], k)));
+        if (tp.esm) tp.esm[(int64_t)t * D.d + k] = v;
+        x0[(int64_t)t * D.d + k] = v;
         ss = __fmaf_rn(v, v, ss);
     }
     const float inv = rms_inv(block_sum(ss, red), D.d);
@@ -179,14 +253,17 @@ __global__ void t_embed(TD D, const int32_t *tok, altxs_qmat emb, const float *e
     }
 }
 
-__global__ void t_prenorm(TD D, int l, Tape tp, altxs_weights w, int skip_gates) {
+// application a of layer i: the skip of decoder application j (-1: none) into
+// the stream, then x_in = mix0 * x + mix1 * x0 and its normed, ln-scaled form.
+// A parallel application (par) keeps lane 0 (after the skip) as its stream and
+// x_in only as the attention's read (model.py:1310-1317).
+__global__ void t_prenorm(TD D, int a, int i, int j, int par, Tape tp, altxs_weights w, int skip_gates) {
     __shared__ float red[32];
-    const int t = blockIdx.x, d = D.d;
+    const int t = blockIdx.x, d = D.d, l = a;
     float *x = tp.x + (int64_t)t * d;
     const float *x0 = tp.x0 + (int64_t)t * d;
-    const float *mix = w.resid_mix + (int64_t)l * 2 * d;
-    const int j = l - D.enc;
-    const bool skip = j >= 0 && j < D.nskip;
+    const float *mix = w.resid_mix + (int64_t)i * 2 * d;
+    const bool skip = j >= 0;
     const float *sk = skip ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
     float *xin = tp.xin + ((int64_t)l * D.T + t) * d;
     float *xr = tp.xraw ? tp.xraw + ((int64_t)l * D.T + t) * d : nullptr;
@@ -200,11 +277,11 @@ __global__ void t_prenorm(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
         }
         const float v = __fadd_rn(__fmul_rn(mix[k], xv), __fmul_rn(mix[d + k], x0[k]));
         xin[k] = v;
-        x[k] = v;
+        x[k] = par ? xv : v;
         ss = __fmaf_rn(v, v, ss);
     }
     const float inv = rms_inv(block_sum(ss, red), d);
-    const float ln = w.ln_scale[l];
+    const float ln = w.ln_scale[i];
     if (threadIdx.x == 0) tp.inv1[(int64_t)l * D.T + t] = inv;
     __syncthreads();
     float *nr = tp.n + ((int64_t)l * D.T + t) * d;
@@ -212,7 +289,7 @@ __global__ void t_prenorm(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
 }
 
 // per-head RMSNorm + RoPE (positions 0..T-1) + q_gain; one warp per head
-__global__ void t_qk(TD D, int l, Tape tp, altxs_weights w) {
+__global__ void t_qk(TD D, int l, int i, Tape tp, altxs_weights w) {
     const int t = blockIdx.x, hd = D.hd, half = D.rd / 2;
     const float *qkv = tp.qkv + ((int64_t)l * D.T + t) * D.qn;
     const float *cs = w.rope_cos + (int64_t)t * half, *sn = w.rope_sin + (int64_t)t * half;
@@ -227,7 +304,7 @@ __global__ void t_qk(TD D, int l, Tape tp, altxs_weights w) {
         float g = 1.0f;
         if (h < D.H) {
             dst = tp.qr + ((int64_t)l * D.T + t) * D.d + (int64_t)h * hd;
-            g = w.q_gain[(int64_t)l * D.H + h];
+            g = w.q_gain[(int64_t)i * D.H + h];
         } else {
             dst = tp.kr + ((int64_t)l * D.T + t) * D.kvd + (int64_t)(h - D.H) * hd;
         }
@@ -268,21 +345,23 @@ __global__ void t_softmax(TD D, float *P) {
     for (int j = threadIdx.x; j < D.T; j += blockDim.x) s[j] = __fmul_rn(s[j], inv);
 }
 
-__global__ void t_post_attn(TD D, int l, Tape tp, altxs_weights w, const float *aob) {
+// MLP input of application l (layer i): x_in + attn_scale * attention output, or
+// in a parallel application lane 1 (model.py:1337-1339); kept with its inverse rms
+__global__ void t_post_attn(TD D, int l, int i, Tape tp, altxs_weights w, const float *aob, int par) {
     __shared__ float red[32];
     const int t = blockIdx.x, d = D.d;
     const float *xin = tp.xin + ((int64_t)l * D.T + t) * d;
     const float *ao = aob + (int64_t)t * d;
-    const float *as = w.attn_scale + (int64_t)l * d;
+    const float *as = w.attn_scale + (int64_t)i * d;
     float *xm = tp.xmid + ((int64_t)l * D.T + t) * d;
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
-        const float v = __fadd_rn(xin[k], __fmul_rn(as[k], ao[k]));
+        const float v = par ? tp.lane1[(int64_t)t * d + k] : __fadd_rn(xin[k], __fmul_rn(as[k], ao[k]));
         xm[k] = v;
         ss = __fmaf_rn(v, v, ss);
     }
     const float inv = rms_inv(block_sum(ss, red), d);
-    const float ln = w.ln_scale[l];
+    const float ln = w.ln_scale[i];
     if (threadIdx.x == 0) tp.inv2[(int64_t)l * D.T + t] = inv;
     __syncthreads();
     float *n2 = tp.n2 + ((int64_t)l * D.T + t) * d;
@@ -297,10 +376,18 @@ __global__ void t_leaky(int64_t n, const float *u, float *h) {
     h[i] = __fmul_rn(a, a);
 }
 
-__global__ void t_final(TD D, Tape tp) {
+// final RMSNorm; after parallel lanes the hidden state is first their mean,
+// lane 0 or lane 1 (model.py:1357-1362), written back into the stream
+__global__ void t_final(TD D, Tape tp, int lanes) {
     __shared__ float red[32];
     const int t = blockIdx.x, d = D.d;
-    const float *x = tp.x + (int64_t)t * d;
+    float *x = tp.x + (int64_t)t * d;
+    if (lanes) {
+        const float *l1 = tp.lane1 + (int64_t)t * d;
+        for (int k = threadIdx.x; k < d; k += blockDim.x)
+            x[k] = D.pfinal == 0 ? __fmul_rn(0.5f, __fadd_rn(x[k], l1[k])) : D.pfinal == 1 ? x[k] : l1[k];
+        __syncthreads();
+    }
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) ss = __fmaf_rn(x[k], x[k], ss);
     const float inv = rms_inv(block_sum(ss, red), d);
@@ -308,41 +395,130 @@ __global__ void t_final(TD D, Tape tp) {
     for (int k = threadIdx.x; k < d; k += blockDim.x) tp.hf[(int64_t)t * d + k] = __fmul_rn(x[k], inv);
 }
 
-// softcap + cross-entropy; logits row -> d(loss)/d(raw logits) in place
-__global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap) {
+// softcap + cross-entropy; logits row -> d(loss)/d(raw logits) in place.  With
+// the asymmetric softcap (sc = {positive, negative} caps, model.py:1478-1493) the
+// row's contributions to d(cap) go to scrow[t][2].
+__global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap, const float *sc, float *scrow) {
     __shared__ float red[32];
     const int t = blockIdx.x;
     float *l = tp.logits + (int64_t)t * D.V;
     if (t < D.first) {  // context row: not scored
         for (int j = threadIdx.x; j < D.V; j += blockDim.x) l[j] = 0.0f;
         if (threadIdx.x == 0) tp.rowloss[t] = 0.0f;
+        if (scrow && threadIdx.x < 2) scrow[2 * t + threadIdx.x] = 0.0f;
         return;
     }
+    const float cp = sc ? sc[0] : cap, cn = sc ? sc[1] : cap;
     const int y = tgt[t];
     float m = -INFINITY;
     for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
-        const float z = __fmul_rn(cap, tanhf(__fdiv_rn(l[j], cap)));
+        const float c = l[j] >= 0.0f ? cp : cn;
+        const float z = __fmul_rn(c, tanhf(__fdiv_rn(l[j], c)));
         m = fmaxf(m, z);
     }
     m = block_max(m, red);
     __syncthreads();
     float s = 0.0f;
     for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
-        const float z = __fmul_rn(cap, tanhf(__fdiv_rn(l[j], cap)));
+        const float c = l[j] >= 0.0f ? cp : cn;
+        const float z = __fmul_rn(c, tanhf(__fdiv_rn(l[j], c)));
         s = __fadd_rn(s, expf(__fsub_rn(z, m)));
     }
     s = block_sum(s, red);
     __syncthreads();
     const float lse = __fadd_rn(m, logf(s));
     const float invT = __fdiv_rn(1.0f, (float)(D.T - D.first));
+    float gp = 0.0f, gn = 0.0f;
     for (int j = threadIdx.x; j < D.V; j += blockDim.x) {
-        const float th = tanhf(__fdiv_rn(l[j], cap));
-        const float z = __fmul_rn(cap, th);
+        const float lj = l[j];
+        const bool pos = lj >= 0.0f;
+        const float c = pos ? cp : cn;
+        const float u = __fdiv_rn(lj, c);
+        const float th = tanhf(u);
+        const float z = __fmul_rn(c, th);
         if (j == y) tp.rowloss[t] = __fsub_rn(lse, z);
         float p = __fdiv_rn(expf(__fsub_rn(z, m)), s);
         if (j == y) p = __fsub_rn(p, 1.0f);
-        l[j] = __fmul_rn(__fmul_rn(p, invT), __fsub_rn(1.0f, __fmul_rn(th, th)));
+        const float dz = __fmul_rn(p, invT);
+        const float sech2 = __fsub_rn(1.0f, __fmul_rn(th, th));
+        l[j] = __fmul_rn(dz, sech2);
+        if (scrow) {  // d(c tanh(l/c))/dc = tanh(u) - u (1 - tanh(u)^2)
+            const float dc = __fmul_rn(dz, __fsub_rn(th, __fmul_rn(u, sech2)));
+            if (pos) gp = __fadd_rn(gp, dc);
+            else gn = __fadd_rn(gn, dc);
+        }
     }
+    if (scrow) {
+        gp = block_sum(gp, red);
+        gn = block_sum(gn, red);
+        if (threadIdx.x == 0) {
+            scrow[2 * t] = gp;
+            scrow[2 * t + 1] = gn;
+        }
+    }
+}
+
+// XSA and the sparse attention gate on one row of application l, layer i
+// (model.py:760-768, 845-862): per head, y -= (y . v^) v^ with v^ the head's KV
+// group value at the same position over its norm (floored at 1e-12), when
+// layer i is one of the last xsa_last_n; then y *= sigmoid(scale * w_h . n[:gw])
+// with n the block's normed attention input.  yraw -> yl; one warp per head.
+__global__ void t_xsa_gate(TD D, int l, int i, Tape tp, altxs_weights w) {
+    const int t = blockIdx.x, hd = D.hd, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int64_t row = (int64_t)l * D.T + t;
+    const float *yr = tp.yraw + row * D.d, *nr = tp.n + row * D.d;
+    const float *vr = tp.qkv + row * D.qn + D.d + D.kvd;
+    float *yo = tp.yl + row * D.d;
+    const bool xsa = i >= D.xsa_from;
+    for (int h = wid; h < D.H; h += nw) {
+        float y[4], v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = lane + 32 * u;
+            y[u] = k < hd ? yr[(int64_t)h * hd + k] : 0.0f;
+            v[u] = k < hd ? vr[(int64_t)(h / D.G) * hd + k] : 0.0f;
+        }
+        if (xsa) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) ss = __fmaf_rn(v[u], v[u], ss);
+            const float den = fmaxf(__fsqrt_rn(warp_sum(ss)), 1e-12f);
+            float dot = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                v[u] = __fdiv_rn(v[u], den);
+                dot = __fmaf_rn(y[u], v[u], dot);
+            }
+            dot = warp_sum(dot);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) y[u] = __fsub_rn(y[u], __fmul_rn(dot, v[u]));
+        }
+        if (D.sgate) {
+            const float *gwr = w.attn_gate_w + ((int64_t)i * D.H + h) * D.gw;
+            float z = 0.0f;
+            for (int k = lane; k < D.gw; k += 32) z = __fmaf_rn(nr[k], gwr[k], z);
+            const float g = sigmoidf_(__fmul_rn(D.sgs, warp_sum(z)));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) y[u] = __fmul_rn(y[u], g);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (lane + 32 * u < hd) yo[(int64_t)h * hd + lane + 32 * u] = y[u];
+    }
+}
+
+// parallel lanes after application l of layer i (model.py:1336-1351):
+// lane0 = r0 lane0 + p00 a + p10 m, lane1 = r1 lane1 + p01 a + p11 m with
+// a = attn_scale * (o-projection), m = mlp_scale * (down-projection)
+__global__ void t_par_combine(int64_t n, int d, int l, int i, Tape tp, altxs_weights w, int T) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    const int k = (int)(e % d);
+    const float A = __fmul_rn(w.attn_scale[(int64_t)i * d + k], tp.aol[(int64_t)l * T * d + e]);
+    const float M = __fmul_rn(w.mlp_scale[(int64_t)i * d + k], tp.doutl[(int64_t)l * T * d + e]);
+    const float *pr = w.parallel_resid + 2 * i, *pp = w.parallel_post + 4 * i;
+    tp.x[e] = __fadd_rn(__fadd_rn(__fmul_rn(pr[0], tp.x[e]), __fmul_rn(pp[0], A)), __fmul_rn(pp[2], M));
+    tp.lane1[e] = __fadd_rn(__fadd_rn(__fmul_rn(pr[1], tp.lane1[e]), __fmul_rn(pp[1], A)), __fmul_rn(pp[3], M));
 }
 
 // mean of the scored rows' losses (rows before `first` hold 0)
@@ -529,7 +705,7 @@ __global__ void t_resid(int64_t n, int d, const float *r, const float *col, cons
 }
 
 // q/k: undo gain, RoPE transpose, per-head RMSNorm backward -> dqkv
-__global__ void t_qk_bwd(TD D, int l, Tape tp, altxs_weights w) {
+__global__ void t_qk_bwd(TD D, int l, int i, Tape tp, altxs_weights w) {
     const int t = blockIdx.x, hd = D.hd, half = D.rd / 2;
     const float *qkv = tp.qkv + ((int64_t)l * D.T + t) * D.qn;
     const float *cs = w.rope_cos + (int64_t)t * half, *sn = w.rope_sin + (int64_t)t * half;
@@ -542,7 +718,7 @@ __global__ void t_qk_bwd(TD D, int l, Tape tp, altxs_weights w) {
         float g = 1.0f;
         if (h < D.H) {
             gsrc = tp.dqr + (int64_t)t * D.d + (int64_t)h * hd;
-            g = w.q_gain[(int64_t)l * D.H + h];
+            g = w.q_gain[(int64_t)i * D.H + h];
         } else {
             gsrc = tp.dkr + (int64_t)t * D.kvd + (int64_t)(h - D.H) * hd;
         }
@@ -593,21 +769,26 @@ __global__ void t_qk_bwd(TD D, int l, Tape tp, altxs_weights w) {
     }
 }
 
-// residual mix and skip lerp backward: dx <- d(loss)/d(layer input).  The
-// full-parameter gradient also adds mix1 * d(x_in) into d(x0) and leaves per-row
-// products for the column sums: [0,d) d(mix0), [d,2d) d(mix1), [2d,3d)
+// residual mix and skip lerp backward of application l (layer i, skip of
+// decoder application j or -1): dx <- d(loss)/d(input of the application).  In
+// a sequential block dx holds d(x_in); in a parallel one d(x_in) (the
+// attention read) comes in tp.dread and dx holds the residual lane's r0 * d(lane0).
+// The full-parameter gradient also adds mix1 * d(x_in) into d(x0) and leaves
+// per-row products for the column sums: [0,d) d(mix0), [d,2d) d(mix1), [2d,3d)
 // d(skip_weights), [3d,4d) d(skip_gates).
-__global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates) {
+__global__ void t_mix_bwd(TD D, int l, int i, int j, int par, Tape tp, altxs_weights w, int skip_gates) {
     const int t = blockIdx.x, d = D.d;
-    const float *mix = w.resid_mix + (int64_t)l * 2 * d;
-    const int j = l - D.enc;
-    const bool skip = j >= 0 && j < D.nskip;
+    const float *mix = w.resid_mix + (int64_t)i * 2 * d;
+    const bool skip = j >= 0;
     float *dx = tp.dx + (int64_t)t * d;
+    const float *gread = par ? tp.dread + (int64_t)t * d : dx;
     float *ds = skip ? tp.dskip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
     const float *sk = skip ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float gin = gread[k];
+        // d(stream after the skip): through the mix, plus the parallel lane's residual
+        const float gx = par ? __fadd_rn(__fmul_rn(gin, mix[k]), dx[k]) : __fmul_rn(gin, mix[k]);
         if (D.full) {
-            const float gin = dx[k];
             const float xr = tp.xraw[((int64_t)l * D.T + t) * d + k];
             float xv = xr, scaled = 0.0f, gg = 0.0f;
             if (skip) {
@@ -625,7 +806,7 @@ __global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
             float *g0 = tp.dx0 + (int64_t)t * d + k;
             *g0 = __fadd_rn(*g0, __fmul_rn(mix[d + k], gin));
             if (skip) {
-                const float gv = __fmul_rn(gin, mix[k]);
+                const float gv = gx;
                 if (skip_gates) {
                     cb[2 * d + k] = __fmul_rn(__fmul_rn(gv, __fsub_rn(1.0f, gg)), sk[k]);
                     cb[3 * d + k] = __fmul_rn(__fmul_rn(gv, __fsub_rn(xr, scaled)), __fmul_rn(gg, __fsub_rn(1.0f, gg)));
@@ -635,7 +816,6 @@ __global__ void t_mix_bwd(TD D, int l, Tape tp, altxs_weights w, int skip_gates)
                 }
             }
         }
-        const float gx = __fmul_rn(dx[k], mix[k]);
         if (skip) {
             const float sw = w.skip_weights[(int64_t)j * d + k];
             if (skip_gates) {
@@ -671,12 +851,209 @@ __global__ void t_colsum_part(int T, int ncol, const float *A, int64_t lda, cons
         s = B ? __fmaf_rn(A[(int64_t)t * lda + c], B[(int64_t)t * ldb + c], s) : __fadd_rn(s, A[(int64_t)t * lda + c]);
     part[(int64_t)blockIdx.y * ncol + c] = s;
 }
+// adds into out: a layer applied several times (depth loops) sums its applications
 __global__ void t_colsum_fin(int ncol, int nch, const float *part, float *out) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= ncol) return;
     float s = 0.0f;
     for (int i = 0; i < nch; ++i) s = __fadd_rn(s, part[(int64_t)i * ncol + c]);
-    out[c] = s;
+    out[c] = __fadd_rn(out[c], s);
+}
+
+// Backward of t_xsa_gate for one row: tp.dy (d of the o-projection input) is
+// rewritten in place as d of the attention output; d(v) of XSA goes to tp.dvx,
+// d(n[:gw]) of the gate is added into tp.dn, and the gate-weight products
+// dz_h * n[k] to colbuf [t][H*gw].  One warp per KV group, heads in order.
+__global__ void t_xsa_gate_bwd(TD D, int l, int i, Tape tp, altxs_weights w) {
+    __shared__ float dzs[128];
+    const int t = blockIdx.x, hd = D.hd, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int64_t row = (int64_t)l * D.T + t;
+    const float *yr = tp.yraw + row * D.d, *nr = tp.n + row * D.d;
+    const float *vr = tp.qkv + row * D.qn + D.d + D.kvd;
+    float *dy = tp.dy + (int64_t)t * D.d;
+    const bool xsa = i >= D.xsa_from;
+    for (int g = wid; g < D.Hkv; g += nw) {
+        float vn[4], dvn[4];
+        float nrm = 0.0f, den = 1.0f;
+        if (xsa) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = lane + 32 * u;
+                vn[u] = k < hd ? vr[(int64_t)g * hd + k] : 0.0f;
+                ss = __fmaf_rn(vn[u], vn[u], ss);
+            }
+            nrm = __fsqrt_rn(warp_sum(ss));
+            den = fmaxf(nrm, 1e-12f);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) vn[u] = __fdiv_rn(vn[u], den);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) dvn[u] = 0.0f;
+        for (int h = g * D.G; h < (g + 1) * D.G; ++h) {
+            float y0[4], y1[4], gy[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = lane + 32 * u;
+                y0[u] = k < hd ? yr[(int64_t)h * hd + k] : 0.0f;
+                gy[u] = k < hd ? dy[(int64_t)h * hd + k] : 0.0f;
+            }
+            float c = 0.0f;
+            if (xsa) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) c = __fmaf_rn(y0[u], vn[u], c);
+                c = warp_sum(c);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) y1[u] = xsa ? __fsub_rn(y0[u], __fmul_rn(c, vn[u])) : y0[u];
+            if (D.sgate) {
+                const float *gwr = w.attn_gate_w + ((int64_t)i * D.H + h) * D.gw;
+                float z = 0.0f;
+                for (int k = lane; k < D.gw; k += 32) z = __fmaf_rn(nr[k], gwr[k], z);
+                const float gt = sigmoidf_(__fmul_rn(D.sgs, warp_sum(z)));
+                float dg = 0.0f;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) dg = __fmaf_rn(gy[u], y1[u], dg);
+                dg = warp_sum(dg);
+                if (lane == 0) dzs[h] = __fmul_rn(__fmul_rn(dg, __fmul_rn(gt, __fsub_rn(1.0f, gt))), D.sgs);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) gy[u] = __fmul_rn(gy[u], gt);
+            }
+            if (xsa) {  // y1 = y0 - (y0 . vn) vn: d y0 = P d y1, d vn -= (d y1 . vn) y0 + c d y1
+                float e = 0.0f;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) e = __fmaf_rn(gy[u], vn[u], e);
+                e = warp_sum(e);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    dvn[u] = __fsub_rn(dvn[u], __fadd_rn(__fmul_rn(e, y0[u]), __fmul_rn(c, gy[u])));
+                    gy[u] = __fsub_rn(gy[u], __fmul_rn(e, vn[u]));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (lane + 32 * u < hd) dy[(int64_t)h * hd + lane + 32 * u] = gy[u];
+        }
+        if (xsa) {  // vn = v / max(|v|, eps)
+            float pd = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) pd = __fmaf_rn(dvn[u], vn[u], pd);
+            pd = warp_sum(pd);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = lane + 32 * u;
+                const float dv = nrm > 1e-12f ? __fdiv_rn(__fsub_rn(dvn[u], __fmul_rn(pd, vn[u])), den)
+                                              : __fdiv_rn(dvn[u], den);
+                if (k < hd) tp.dvx[(int64_t)t * D.kvd + (int64_t)g * hd + k] = dv;
+            }
+        }
+    }
+    if (!D.sgate) return;
+    __syncthreads();
+    float *dn = tp.dn + (int64_t)t * D.d;
+    for (int k = threadIdx.x; k < D.gw; k += blockDim.x) {
+        float acc = 0.0f;
+        for (int h = 0; h < D.H; ++h) acc = __fmaf_rn(dzs[h], w.attn_gate_w[((int64_t)i * D.H + h) * D.gw + k], acc);
+        dn[k] = __fadd_rn(dn[k], acc);
+    }
+    float *cb = tp.colbuf + (int64_t)t * D.H * D.gw;
+    for (int e = threadIdx.x; e < D.H * D.gw; e += blockDim.x) cb[e] = __fmul_rn(dzs[e / D.gw], nr[e % D.gw]);
+}
+
+// d(v part of qkv) += XSA's d(v)
+__global__ void t_add_v(int64_t n, int kvd, int qn, int voff, float *dqkv, const float *dvx) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    const int64_t t = e / kvd;
+    float *p = dqkv + t * qn + voff + (e - t * kvd);
+    *p = __fadd_rn(*p, dvx[e]);
+}
+
+// Backward of t_par_combine for application l (layer i, skip j) per row: from
+// d(lane0') in tp.dx and d(lane1') in tp.dl1 to d(o-projection) (tp.dao),
+// d(down-projection) (tp.dd), the lanes' residual parts (tp.dx = r0 d lane0',
+// tp.dl1 = r1 d lane1') and per-row products: [0,d) d(attn_scale), [d,2d)
+// d(mlp_scale), [2d,2d+2) d(parallel_resid[i]), [2d+2,2d+6) d(parallel_post[i]).
+__global__ void t_par_bwd(TD D, int l, int i, int j, Tape tp, altxs_weights w, int skip_gates) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, d = D.d;
+    const int64_t row = ((int64_t)l * D.T + t) * d;
+    const float *pr = w.parallel_resid + 2 * i, *pp = w.parallel_post + 4 * i;
+    const float *sk = j >= 0 ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
+    float *dx = tp.dx + (int64_t)t * d, *dl1 = tp.dl1 + (int64_t)t * d;
+    float *cb = tp.colbuf + (int64_t)t * 4 * d;
+    float s[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        const float g0 = dx[k], g1 = dl1[k];
+        const float as = w.attn_scale[(int64_t)i * d + k], ms = w.mlp_scale[(int64_t)i * d + k];
+        const float ao = tp.aol[row + k], mo = tp.doutl[row + k];
+        const float A = __fmul_rn(as, ao), M = __fmul_rn(ms, mo);
+        float l0 = tp.xraw[row + k];  // lane 0 after the skip
+        if (sk) {
+            const float scaled = __fmul_rn(w.skip_weights[(int64_t)j * d + k], sk[k]);
+            l0 = skip_gates ? lerp_t(scaled, l0, sigmoidf_(w.skip_gates[(int64_t)j * d + k])) : __fadd_rn(l0, scaled);
+        }
+        const float da = __fadd_rn(__fmul_rn(pp[0], g0), __fmul_rn(pp[1], g1));
+        const float dm = __fadd_rn(__fmul_rn(pp[2], g0), __fmul_rn(pp[3], g1));
+        tp.dao[(int64_t)t * d + k] = __fmul_rn(as, da);
+        tp.dd[(int64_t)t * d + k] = __fmul_rn(ms, dm);
+        cb[k] = __fmul_rn(da, ao);
+        cb[d + k] = __fmul_rn(dm, mo);
+        s[0] = __fmaf_rn(g0, l0, s[0]);
+        s[1] = __fmaf_rn(g1, tp.xmid[row + k], s[1]);
+        s[2] = __fmaf_rn(g0, A, s[2]);
+        s[3] = __fmaf_rn(g1, A, s[3]);
+        s[4] = __fmaf_rn(g0, M, s[4]);
+        s[5] = __fmaf_rn(g1, M, s[5]);
+        dx[k] = __fmul_rn(pr[0], g0);
+        dl1[k] = __fmul_rn(pr[1], g1);
+    }
+#pragma unroll
+    for (int q = 0; q < 6; ++q) {
+        const float v = block_sum(s[q], red);
+        if (threadIdx.x == 0) cb[2 * d + q] = v;
+    }
+}
+
+// d(final hidden) -> the two lanes (mean, lane 0 or lane 1)
+__global__ void t_lane_split(int64_t n, int pfinal, float *dx, float *dl1) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    const float g = dx[e];
+    dx[e] = pfinal == 0 ? __fmul_rn(0.5f, g) : pfinal == 1 ? g : 0.0f;
+    dl1[e] = pfinal == 0 ? __fmul_rn(0.5f, g) : pfinal == 2 ? g : 0.0f;
+}
+
+// Smear gate backward per row t: dxs = d(smeared rows) -> draw = d(raw rows)
+// (x_t = raw_t + lambda*sig(z_t)*raw_{t-1}, z_t = raw_t[:gw] . g), and per-row
+// products [0] d(lambda), [1, 1+gw) d(g) into colbuf [t][1+gw].
+__global__ void t_smear_bwd(TD D, Tape tp, altxs_weights w, const float *dxs, float *draw) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, d = D.d, gw = D.gw;
+    const float *raw = tp.eraw + (int64_t)t * d;
+    const float lam = w.smear_lambda[0];
+    float z = 0.0f, zn = 0.0f, dg = 0.0f;
+    for (int k = threadIdx.x; k < gw; k += blockDim.x) {
+        z = __fmaf_rn(raw[k], w.smear_gate[k], z);
+        if (t + 1 < D.T) zn = __fmaf_rn(raw[d + k], w.smear_gate[k], zn);
+    }
+    if (t > 0)
+        for (int k = threadIdx.x; k < d; k += blockDim.x) dg = __fmaf_rn(dxs[(int64_t)t * d + k], raw[k - d], dg);
+    z = block_sum(z, red);
+    zn = block_sum(zn, red);
+    dg = block_sum(dg, red);
+    const float sg = sigmoidf_(z);
+    const float gn = t + 1 < D.T ? __fmul_rn(lam, sigmoidf_(zn)) : 0.0f;
+    const float dz = t > 0 ? __fmul_rn(__fmul_rn(dg, lam), __fmul_rn(sg, __fsub_rn(1.0f, sg))) : 0.0f;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float v = dxs[(int64_t)t * d + k];
+        if (t + 1 < D.T) v = __fadd_rn(v, __fmul_rn(gn, dxs[(int64_t)(t + 1) * d + k]));
+        if (k < gw) v = __fadd_rn(v, __fmul_rn(dz, w.smear_gate[k]));
+        draw[(int64_t)t * d + k] = v;
+    }
+    float *cb = tp.colbuf + (int64_t)t * (gw + 1);
+    if (threadIdx.x == 0) cb[0] = t > 0 ? __fmul_rn(dg, sg) : 0.0f;
+    for (int k = threadIdx.x; k < gw; k += blockDim.x) cb[1 + k] = __fmul_rn(dz, raw[k]);
 }
 
 // Input-embedding gradient of the tied table: gemb[v] += sum over positions t
@@ -794,7 +1171,15 @@ struct Run {
     const int32_t *tok;
     float *fg;
     altxs_param_layout lay;
+    // physical layer of every application
+    int sched[kMaxApps];
 };
+
+void plan(Run &R) {
+    for (int a = 0; a < R.D.A; ++a) R.sched[a] = R.desc->schedule ? R.desc->schedule[a] : a;
+}
+// skip slot taken by application a (a decoder application), or -1
+inline int skip_of(const TD &D, int a) { return a >= D.enc && a - D.enc < D.nskip ? a - D.enc : -1; }
 
 // Batched/causal GEMMs of the update: tensor cores when the model carries
 // bf16 planes, CUDA cores otherwise (the two differ in the last bits; the
@@ -999,12 +1384,20 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
     const float s = R.desc->lora_scale;
     const int Tn = D.T, d = D.d, r = D.r;
     cudaStream_t st = R.st;
-    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, dw ? dw->emb : w->emb_dense, tp.x0, tp.x, tp));
-    for (int l = 0; l < D.L; ++l) {
-        ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
+    ALTXS_LAUNCH(kKTtt, st, t_embed<<<Tn, 128, 0, st>>>(D, tok, w->emb, dw ? dw->emb : w->emb_dense, tp.x0, tp.x, tp, *w));
+    bool lanes = false;
+    // l: the layer application (tape index; the LoRA update has one per layer), i: its layer
+    for (int l = 0; l < D.A; ++l) {
+        const int i = R.sched[l];
+        const bool par = par_app(D, R.sched, l);
+        if (par && !lanes) {  // the stream splits into two lanes (model.py:1404-1407)
+            cudaMemcpyAsync(tp.lane1, tp.x, (size_t)Tn * d * 4, cudaMemcpyDeviceToDevice, st);
+            lanes = true;
+        }
+        ALTXS_LAUNCH(kKTtt, st, t_prenorm<<<Tn, 128, 0, st>>>(D, l, i, skip_of(D, l), par, tp, *w, R.desc->skip_gates));
         const float *n = tp.n + (int64_t)l * Tn * d;
         float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
-        TRY(lin_fwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), l * D.qn, D.qn, d, n, d, qkv, D.qn));
+        TRY(lin_fwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), i * D.qn, D.qn, d, n, d, qkv, D.qn));
         TRY(lora_fwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
                      tp.tq + (int64_t)l * Tn * r, qkv, D.qn));
         if (mask & 2)
@@ -1012,19 +1405,21 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
                          tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn));
         TRY(lora_fwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
                      tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
-        ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, tp, *w));
+        ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
         TRY(attn_probs(R, l));
-        // the full-parameter gradient keeps every layer's attention output and projections
+        // the full-parameter gradient keeps every application's attention output and projections
         float *yb = D.full ? tp.yl + (int64_t)l * Tn * d : tp.y;
         float *aob = D.full ? tp.aol + (int64_t)l * Tn * d : tp.ao;
+        const bool ym = D.full && ymotif(D, i);
+        float *ya = ym ? tp.yraw + (int64_t)l * Tn * d : yb;  // P v, before XSA and the gate
         const int64_t ldp = align_up(Tn, 8);
         if (R.sp) {
             const uint16_t *Ph = p_planes(R, l), *Pl = Ph + D.H * Tn * ldp;
             TcOp a{Ph, Pl, 0, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, 1, 0}, b{};
             TRY(split_b(R, qkv + d + D.kvd, Tn, D.hd, D.qn, D.Hkv, D.hd, 1, D.G, 1, 0, b));  // v, [n=c][k=t']
-            TRY(tc_att(R, a, b, Tn, D.hd, Tn, D.H, 2, 0.0f, yb, d, D.hd));                   // y = P v
+            TRY(tc_att(R, a, b, Tn, D.hd, Tn, D.H, 2, 0.0f, ya, d, D.hd));                   // y = P v
         } else {
-            GemmArgs g = G(R, p_f32(R, l), Tn, 0, qkv + d + D.kvd, D.qn, 0, yb, d, Tn, D.hd, Tn);  // y = P v
+            GemmArgs g = G(R, p_f32(R, l), Tn, 0, qkv + d + D.kvd, D.qn, 0, ya, d, Tn, D.hd, Tn);  // y = P v
             g.batch = D.H;
             g.sA = (int64_t)Tn * Tn;
             g.sB = D.hd;
@@ -1033,28 +1428,33 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             g.causal = 2;
             TRY(gemm(R, g));
         }
-        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, yb, d, aob, d));
+        if (ym) ALTXS_LAUNCH(kKTtt, st, t_xsa_gate<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
+        TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), i * d, d, d, yb, d, aob, d));
         if (mask & 8)
             TRY(lora_fwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, aob, d));
-        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, tp, *w, aob));
+        ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, i, tp, *w, aob, par));
         float *u = tp.u + (int64_t)l * Tn * D.F;
-        TRY(lin_fwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), l * D.F, D.F, d, tp.n2 + (int64_t)l * Tn * d, d, u, D.F));
+        TRY(lin_fwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), i * D.F, D.F, d, tp.n2 + (int64_t)l * Tn * d, d, u, D.F));
         ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
         float *sk = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
         const float *xm = tp.xmid + (int64_t)l * Tn * d;
         if (dw || R.sp) {
             float *db = D.full ? tp.doutl + (int64_t)l * Tn * d : tp.dd;
-            TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.hbuf, D.F, db, d));
-            ALTXS_LAUNCH(kKTtt, st, t_resid<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                        (int64_t)Tn * d, d, xm, w->mlp_scale + (int64_t)l * d, db, tp.x, sk));
+            TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), i * d, d, D.F, tp.hbuf, D.F, db, d));
+            if (par)
+                ALTXS_LAUNCH(kKTtt, st, t_par_combine<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>((int64_t)Tn * d, d, l,
+                                                                                                 i, tp, *w, Tn));
+            else
+                ALTXS_LAUNCH(kKTtt, st, t_resid<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
+                                            (int64_t)Tn * d, d, xm, w->mlp_scale + (int64_t)i * d, db, tp.x, sk));
         } else {
             QmmArgs a{};
             a.X = tp.hbuf;
             a.ldx = D.F;
             a.M = Tn;
             a.W = w->down;
-            a.row0 = l * d;
+            a.row0 = i * d;
             a.N = d;
             a.K = D.F;
             a.Y = tp.x;
@@ -1062,23 +1462,26 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             a.epi = kEpiResid;
             a.R = xm;
             a.ldr = d;
-            a.colscale = w->mlp_scale + (int64_t)l * d;
+            a.colscale = w->mlp_scale + (int64_t)i * d;
             a.Y2 = sk;
             a.ldy2 = d;
             TRY(launch_qmm(a, st));
         }
     }
     if (!head) return ALTXS_OK;  // context prefill: the layers' K/V rows are all it needs
-    ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp));
+    ALTXS_LAUNCH(kKTtt, st, t_final<<<Tn, 128, 0, st>>>(D, tp, lanes ? 1 : 0));
     TRY(lin_fwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.hf, d, tp.logits, D.V));
     if (mask & 16) TRY(lora_fwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V));
-    ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, R.desc->logit_softcap));
+    const float *sc = D.asym ? w->softcap : nullptr;
+    ALTXS_LAUNCH(kKTtt, st, t_ce<<<Tn, 512, 0, st>>>(D, tgt, tp, R.desc->logit_softcap, sc,
+                                                     D.asym && D.full ? tp.colbuf : nullptr));
     ALTXS_LAUNCH(kKTtt, st, t_loss_sum<<<1, 1024, 0, st>>>(Tn, D.first, tp.rowloss, loss_out));
     return ALTXS_OK;
 }
 
 // Backward of the window loss: into the adapters (grad in the LoRA arena
-// layout), or with R.fg into every parameter (the full arena layout R.lay).
+// layout), or with R.fg into every parameter (the full arena layout R.lay,
+// zeroed by the caller: a layer's applications add up).
 int backward(const Run &R, const float *lora, float *grad) {
     const TD &D = R.D;
     const Tape &tp = R.tp;
@@ -1088,25 +1491,31 @@ int backward(const Run &R, const float *lora, float *grad) {
     const int mask = R.desc->lora_mask;
     const float s = R.desc->lora_scale;
     const int Tn = D.T, d = D.d, r = D.r;
+    const int64_t Td = (int64_t)Tn * d;
     const float att_scale = 1.0f / __builtin_sqrtf((float)D.hd);
     cudaStream_t st = R.st;
     const bool full = D.full;
     float *FG = R.fg;
     const altxs_param_layout &lay = R.lay;
-    // out[c] = sum over rows of A[t][c] (* B[t][c])
+    // out[c] += sum over rows of A[t][c] (* B[t][c])
     auto colsum = [&](const float *A, int64_t lda, const float *B, int64_t ldb, int ncol, float *out) -> int {
         ALTXS_LAUNCH(kKTtt, st, t_colsum_part<<<dim3(g1(ncol, 128), kColChunks), 128, 0, st>>>(Tn, ncol, A, lda, B,
                                                                                                  ldb, tp.cpart));
         ALTXS_LAUNCH(kKTtt, st, t_colsum_fin<<<g1(ncol, 128), 128, 0, st>>>(ncol, kColChunks, tp.cpart, out));
         return ALTXS_OK;
     };
-    // weight gradient out[N][K] = dY^T X (dY [T][N], X [T][K]): the reduction runs over positions
-    auto wgrad = [&](const float *dY, int N, const float *X, int K, float *out) -> int {
-        return gemm(R, G(R, dY, N, 1, X, K, 0, out, K, N, K, Tn));
+    // weight gradient out[N][K] (+)= dY^T X (dY [T][N], X [T][K]): the reduction runs over positions
+    auto wgrad = [&](const float *dY, int N, const float *X, int K, float *out, bool acc) -> int {
+        return gemm(R, G(R, dY, N, 1, X, K, 0, out, K, N, K, Tn, 1.0f, acc ? 1.0f : 0.0f));
     };
+    bool seen[kMaxApps] = {};  // layer i already has gradient from a later application
+    int first_par = -1;
+    for (int l = 0; l < D.A; ++l)
+        if (first_par < 0 && par_app(D, R.sched, l)) first_par = l;
     if (full) {
-        cudaMemsetAsync(tp.dx0, 0, (size_t)Tn * d * 4, st);
-        TRY(wgrad(tp.logits, D.V, tp.hf, d, FG + lay.emb));  // the tied table as the LM head
+        cudaMemsetAsync(tp.dx0, 0, (size_t)Td * 4, st);
+        if (D.asym) TRY(colsum(tp.colbuf, 2, nullptr, 0, 2, FG + lay.softcap));  // rows left by t_ce
+        TRY(wgrad(tp.logits, D.V, tp.hf, d, FG + lay.emb, false));  // the tied table as the LM head
     }
     // LM head: dhf = dlogits E (+ LoRA)
     TRY(lin_bwd(R, w->emb, dw ? dw->emb : nullptr, PL(emb_hi), PL(emb_lo), 0, D.V, d, tp.logits, D.V, tp.dn, d, 0.0f));
@@ -1114,43 +1523,65 @@ int backward(const Run &R, const float *lora, float *grad) {
         TRY(lora_bwd(R, tp.hf, d, lora + lo.lmA, lora + lo.lmB, D.V, s, tp.tlm, tp.logits, D.V, grad + lo.lmA,
                      grad + lo.lmB, tp.dn));
     ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.x, tp.invf, nullptr, nullptr, tp.dx));
-    for (int l = D.L - 1; l >= 0; --l) {
+    if (first_par >= 0)
+        ALTXS_LAUNCH(kKTtt, st, t_lane_split<<<g1(Td, 256), 256, 0, st>>>(Td, D.pfinal, tp.dx, tp.dl1));
+    for (int l = D.A - 1; l >= 0; --l) {
+        const int i = R.sched[l], j = skip_of(D, l);
+        const bool par = par_app(D, R.sched, l);
+        const bool acc = seen[i];
+        seen[i] = true;
         if (l < D.enc)
-            ALTXS_LAUNCH(kKTtt, st, t_add<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                        (int64_t)Tn * d, tp.dx, tp.dskip + (int64_t)l * Tn * d));
-        // MLP
-        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                    (int64_t)Tn * d, d, tp.dx, w->mlp_scale + (int64_t)l * d, tp.dd));
+            ALTXS_LAUNCH(kKTtt, st, t_add<<<g1(Td, 256), 256, 0, st>>>(Td, tp.dx, tp.dskip + (int64_t)l * Td));
+        // MLP: d(down-projection output) into dd
+        if (par) {  // both lanes' gradients -> the two branches, the residual parts, the lane products
+            ALTXS_LAUNCH(kKTtt, st, t_par_bwd<<<Tn, 128, 0, st>>>(D, l, i, j, tp, *w, R.desc->skip_gates));
+            TRY(colsum(tp.colbuf, 4 * d, nullptr, 0, d, FG + lay.attn_scale + (int64_t)i * d));
+            TRY(colsum(tp.colbuf + d, 4 * d, nullptr, 0, d, FG + lay.mlp_scale + (int64_t)i * d));
+            TRY(colsum(tp.colbuf + 2 * d, 4 * d, nullptr, 0, 2, FG + lay.parallel_resid + 2 * i));
+            TRY(colsum(tp.colbuf + 2 * d + 2, 4 * d, nullptr, 0, 4, FG + lay.parallel_post + 4 * i));
+        } else {
+            ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1(Td, 256), 256, 0, st>>>(Td, d, tp.dx, w->mlp_scale + (int64_t)i * d,
+                                                                             tp.dd));
+            if (full) TRY(colsum(tp.dx, d, tp.doutl + (int64_t)l * Td, d, d, FG + lay.mlp_scale + (int64_t)i * d));
+        }
         if (full) {
-            TRY(colsum(tp.dx, d, tp.doutl + (int64_t)l * Tn * d, d, d, FG + lay.mlp_scale + (int64_t)l * d));
             ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
                                         (int64_t)Tn * D.F, tp.u + (int64_t)l * Tn * D.F, tp.hbuf));
-            TRY(wgrad(tp.dd, d, tp.hbuf, D.F, FG + lay.down + (int64_t)l * d * D.F));
+            TRY(wgrad(tp.dd, d, tp.hbuf, D.F, FG + lay.down + (int64_t)i * d * D.F, acc));
         }
-        TRY(lin_bwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), l * d, d, D.F, tp.dd, d, tp.dh, D.F, 0.0f));
+        TRY(lin_bwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), i * d, d, D.F, tp.dd, d, tp.dh, D.F, 0.0f));
         ALTXS_LAUNCH(kKTtt, st, t_leaky_bwd<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>(
                                     (int64_t)Tn * D.F, tp.dh, tp.u + (int64_t)l * Tn * D.F, tp.dh));
-        if (full) TRY(wgrad(tp.dh, D.F, tp.n2 + (int64_t)l * Tn * d, d, FG + lay.up + (int64_t)l * D.F * d));
-        TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), l * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
-        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Tn * d,
-                                                             tp.inv2 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
-                                                             tp.dx));
-        if (full) TRY(colsum(tp.dx, d, tp.aol + (int64_t)l * Tn * d, d, d, FG + lay.attn_scale + (int64_t)l * d));
-        ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>(
-                                    (int64_t)Tn * d, d, tp.dx, w->attn_scale + (int64_t)l * d, tp.dao));
-        const float *n = tp.n + (int64_t)l * Tn * d;
-        cudaMemsetAsync(tp.dn, 0, (size_t)Tn * d * 4, st);
+        if (full) TRY(wgrad(tp.dh, D.F, tp.n2 + (int64_t)l * Td, d, FG + lay.up + (int64_t)i * D.F * d, acc));
+        TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), i * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
+        // the MLP read: x_mid (sequential) or lane 1 (parallel)
+        float *dmid = par ? tp.dl1 : tp.dx;
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Td,
+                                                             tp.inv2 + (int64_t)l * Tn, w->ln_scale + i, dmid, dmid));
+        if (!par) {
+            if (full) TRY(colsum(tp.dx, d, tp.aol + (int64_t)l * Td, d, d, FG + lay.attn_scale + (int64_t)i * d));
+            ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1(Td, 256), 256, 0, st>>>(Td, d, tp.dx,
+                                                                             w->attn_scale + (int64_t)i * d, tp.dao));
+        }
+        const float *n = tp.n + (int64_t)l * Td;
+        cudaMemsetAsync(tp.dn, 0, (size_t)Td * 4, st);
         if (mask & 8)
             TRY(lora_bwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
                          grad + lo.oB + l * lo.o_stride, tp.dn));
-        if (full) TRY(wgrad(tp.dao, d, tp.yl + (int64_t)l * Tn * d, d, FG + lay.o + (int64_t)l * d * d));
-        TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), l * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
+        if (full) TRY(wgrad(tp.dao, d, tp.yl + (int64_t)l * Td, d, FG + lay.o + (int64_t)i * d * d, acc));
+        TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), i * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
+        const bool ym = full && ymotif(D, i);
+        if (ym) {  // XSA / sparse gate: dy becomes d(P v); d(v) and d(n[:gw]) on the side
+            ALTXS_LAUNCH(kKTtt, st, t_xsa_gate_bwd<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
+            if (D.sgate) TRY(colsum(tp.colbuf, (int64_t)D.H * D.gw, nullptr, 0, D.H * D.gw,
+                                    FG + lay.attn_gate_w + (int64_t)i * D.H * D.gw));
+        }
         // attention backward
         if (full) TRY(attn_probs(R, l));
         const float *P = p_f32(R, l);
         const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
-        const float *qr = tp.qr + (int64_t)l * Tn * d, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
+        const float *qr = tp.qr + (int64_t)l * Td, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
         if (R.sp) {  // tensor cores: P and dS as planes, K-major or read transposed (MN-major)
             const int64_t ldp = align_up(Tn, 8);
             const uint16_t *Ph = p_planes(R, l);
@@ -1227,8 +1658,11 @@ int backward(const Run &R, const float *lora, float *grad) {
                 TRY(gemm(R, g));
             }
         }
-        ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, tp, *w));
-        if (full) TRY(colsum(tp.colbuf, D.H, nullptr, 0, D.H, FG + lay.q_gain + (int64_t)l * D.H));
+        if (ym && i >= D.xsa_from)
+            ALTXS_LAUNCH(kKTtt, st, t_add_v<<<g1((int64_t)Tn * D.kvd, 256), 256, 0, st>>>(
+                                        (int64_t)Tn * D.kvd, D.kvd, D.qn, d + D.kvd, tp.dqkv, tp.dvx));
+        ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
+        if (full) TRY(colsum(tp.colbuf, D.H, nullptr, 0, D.H, FG + lay.q_gain + (int64_t)i * D.H));
         TRY(lora_bwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
                      tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, grad + lo.qA + l * lo.q_stride,
                      grad + lo.qB + l * lo.q_stride, tp.dn));
@@ -1239,26 +1673,36 @@ int backward(const Run &R, const float *lora, float *grad) {
         TRY(lora_bwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
                      tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, grad + lo.vA + l * lo.v_stride,
                      grad + lo.vB + l * lo.v_stride, tp.dn));
-        if (full) TRY(wgrad(tp.dqkv, D.qn, n, d, FG + lay.qkv + (int64_t)l * D.qn * d));
-        TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), l * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
-        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Tn * d,
-                                                             tp.inv1 + (int64_t)l * Tn, w->ln_scale + l, tp.dx,
-                                                             tp.dx));
-        ALTXS_LAUNCH(kKTtt, st, t_mix_bwd<<<Tn, 128, 0, st>>>(D, l, tp, *w, R.desc->skip_gates));
+        if (full) TRY(wgrad(tp.dqkv, D.qn, n, d, FG + lay.qkv + (int64_t)i * D.qn * d, acc));
+        TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), i * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
+        // d(x_in): added to the stream's gradient (sequential), or the attention read alone (parallel)
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn, d, tp.xin + (int64_t)l * Td,
+                                                             tp.inv1 + (int64_t)l * Tn, w->ln_scale + i,
+                                                             par ? nullptr : tp.dx, par ? tp.dread : tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_mix_bwd<<<Tn, 128, 0, st>>>(D, l, i, j, par, tp, *w, R.desc->skip_gates));
         if (full) {
-            TRY(colsum(tp.colbuf, 4 * d, nullptr, 0, 2 * d, FG + lay.resid_mix + (int64_t)l * 2 * d));
-            const int j = l - D.enc;
-            if (j >= 0 && j < D.nskip) {
+            TRY(colsum(tp.colbuf, 4 * d, nullptr, 0, 2 * d, FG + lay.resid_mix + (int64_t)i * 2 * d));
+            if (j >= 0) {
                 TRY(colsum(tp.colbuf + 2 * d, 4 * d, nullptr, 0, d, FG + lay.skip_weights + (int64_t)j * d));
                 TRY(colsum(tp.colbuf + 3 * d, 4 * d, nullptr, 0, d, FG + lay.skip_gates + (int64_t)j * d));
             }
         }
+        if (l == first_par)  // before the split both lanes were the one stream
+            ALTXS_LAUNCH(kKTtt, st, t_add<<<g1(Td, 256), 256, 0, st>>>(Td, tp.dx, tp.dl1));
     }
-    if (full) {  // embedding: d(x0) over every use, through x0 = rms(raw), into the rows of the tied table
-        ALTXS_LAUNCH(kKTtt, st, t_add<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>((int64_t)Tn * d, tp.dx0, tp.dx));
-        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dx0, d, tp.eraw, tp.inv0, nullptr, nullptr, tp.dn));
+    if (full) {  // embedding: d(x0) over every use, through x0 = rms(raw or smeared), into the tied table's rows
+        ALTXS_LAUNCH(kKTtt, st, t_add<<<g1(Td, 256), 256, 0, st>>>(Td, tp.dx0, tp.dx));
+        ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dx0, d, D.smear ? tp.esm : tp.eraw, tp.inv0,
+                                                             nullptr, nullptr, tp.dn));
+        const float *draw = tp.dn;
+        if (D.smear) {
+            ALTXS_LAUNCH(kKTtt, st, t_smear_bwd<<<Tn, 128, 0, st>>>(D, tp, *w, tp.dn, tp.dd));
+            TRY(colsum(tp.colbuf, D.gw + 1, nullptr, 0, 1, FG + lay.smear_lambda));
+            TRY(colsum(tp.colbuf + 1, D.gw + 1, nullptr, 0, D.gw, FG + lay.smear_gate));
+            draw = tp.dd;
+        }
         ALTXS_LAUNCH(kKTtt, st, t_emb_scatter<<<D.V < 148 * 16 ? D.V : 148 * 16, 128, 0, st>>>(Tn, d, D.V, R.tok,
-                                                                                             tp.dn, FG + lay.emb));
+                                                                                             draw, FG + lay.emb));
     }
     return ALTXS_OK;
 }
@@ -1284,7 +1728,9 @@ void tc_scratch(const TD &D, int64_t *a_n, int64_t *b_n) {
 altxs_param_layout param_layout(const altxs_model_desc &dsc) {
     const int64_t V = dsc.vocab, L = dsc.n_layers, d = dsc.d_model, H = dsc.n_heads, F = dsc.mlp_hidden;
     const int64_t qn = d + 2 * (int64_t)dsc.n_kv_heads * dsc.head_dim;
-    const int64_t S = L / 2 < L - L / 2 ? L / 2 : L - L / 2;
+    const int64_t A = dsc.n_virtual > 0 ? dsc.n_virtual : L, E = dsc.n_encoder > 0 ? dsc.n_encoder : A / 2;
+    const int64_t S = E < A - E ? E : A - E;
+    const int64_t gw = (dsc.smear_gate || dsc.sparse_gate) ? dsc.gate_window : 0;
     altxs_param_layout o{};
     int64_t off = 0;
     auto seg = [&](int64_t n) {
@@ -1303,6 +1749,12 @@ altxs_param_layout param_layout(const altxs_model_desc &dsc) {
     o.resid_mix = seg(L * 2 * d);
     o.skip_weights = seg(S * d);
     o.skip_gates = seg(S * d);
+    o.smear_gate = seg(dsc.smear_gate ? gw : 0);
+    o.smear_lambda = seg(dsc.smear_gate ? 1 : 0);
+    o.attn_gate_w = seg(dsc.sparse_gate ? L * H * gw : 0);
+    o.softcap = seg(dsc.asym_softcap ? 2 : 0);
+    o.parallel_post = seg(dsc.parallel_start > 0 ? L * 4 : 0);
+    o.parallel_resid = seg(dsc.parallel_start > 0 ? L * 2 : 0);
     o.total = off;
     return o;
 }
@@ -1348,6 +1800,7 @@ int altxs_prefill(const altxs_model_desc *desc, const altxs_weights *w, const al
     if (dense && (!dense->emb || !dense->qkv || !dense->o || !dense->up || !dense->down)) return ALTXS_EINVAL;
     if (workspace_bytes < altxs_prefill_workspace_bytes(desc, T)) return ALTXS_EINVAL;
     R.desc = desc;
+    plan(R);
     R.w = w;
     R.dw = dense;
     R.no_lora = R.D.r == 0 || !lora;
@@ -1379,6 +1832,7 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
     if (w->rope_positions < T) return ALTXS_EINVAL;
     if (dense && (!dense->emb || !dense->qkv || !dense->o || !dense->up || !dense->down)) return ALTXS_EINVAL;
     R.desc = desc;
+    plan(R);
     R.w = w;
     R.dw = dense;
     R.st = reinterpret_cast<cudaStream_t>(stream);
@@ -1433,6 +1887,7 @@ int altxs_full_loss_grad(const altxs_model_desc *desc, const altxs_weights *w, c
     if (workspace_bytes < altxs_full_workspace_bytes(desc, n)) return ALTXS_EINVAL;
     if (w->rope_positions < n - 1) return ALTXS_EINVAL;
     R.desc = desc;
+    plan(R);
     R.w = w;
     R.dw = dense;
     R.no_lora = true;

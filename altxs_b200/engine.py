@@ -53,6 +53,11 @@ def lora_mask(cfg: ModelConfig) -> int:
     return m
 
 
+# small parameters held in the arena (segment names of altxs_param_layout)
+_ARENA_SMALL = ("q_gain", "attn_scale", "mlp_scale", "resid_mix", "skip_weights", "skip_gates", "smear_gate",
+                "smear_lambda", "attn_gate_w", "softcap", "parallel_post", "parallel_resid")
+
+
 class DeviceModel:
     """One model resident on one GPU.
 
@@ -144,11 +149,11 @@ class DeviceModel:
         for name in ("emb", "qkv", "o", "up", "down"):
             q = self.q[name]
             _lib.check(L.altxs_dequant(C.byref(q), base + 4 * getattr(lay, name), q.cols, st), "altxs_dequant")
-        for name in ("q_gain", "attn_scale", "mlp_scale", "resid_mix", "skip_weights", "skip_gates"):
+        for name in _ARENA_SMALL:
+            if name not in self.small or self._arena_size(name) == 0:
+                continue  # no skips, or a motif that is off
             src = self.small[name].reshape(-1)
             off = getattr(lay, name)
-            if name.startswith("skip") and not self.cfg.num_skip_weights:
-                continue
             view = self.params[off: off + src.numel()]
             view.copy_(src)
             self.small[name] = view
@@ -169,19 +174,25 @@ class DeviceModel:
                                          gdesc=gdt.data_ptr(), lut=None, glut=None, rows=rows, cols=cols)
         self._weights_struct = None
 
+    def _arena_size(self, name: str) -> int:
+        cfg, L, d = self.cfg, self.cfg.num_layers, self.cfg.model_dim
+        gw = cfg.gate_window
+        sizes = {"emb": cfg.vocab_size * d, "qkv": L * (d + 2 * cfg.kv_dim) * d, "o": L * d * d,
+                 "up": L * cfg.mlp_hidden * d, "down": L * d * cfg.mlp_hidden, "q_gain": L * cfg.num_heads,
+                 "attn_scale": L * d, "mlp_scale": L * d, "resid_mix": L * 2 * d,
+                 "skip_weights": cfg.num_skip_weights * d, "skip_gates": cfg.num_skip_weights * d,
+                 "smear_gate": gw if cfg.smear_gate_enabled else 0,
+                 "smear_lambda": 1 if cfg.smear_gate_enabled else 0,
+                 "attn_gate_w": L * cfg.num_heads * gw if cfg.sparse_attn_gate_enabled else 0,
+                 "softcap": 2 if cfg.asym_logit_rescale else 0,
+                 "parallel_post": L * 4 if cfg.parallel_start_layer > 0 else 0,
+                 "parallel_resid": L * 2 if cfg.parallel_start_layer > 0 else 0}
+        return sizes[name]
+
     def arena(self, name: str) -> torch.Tensor:
         """The segment ``name`` of the parameter arena (a view)."""
-        lay, cfg = self.layout, self.cfg
-        sizes = {"emb": cfg.vocab_size * cfg.model_dim,
-                 "qkv": cfg.num_layers * (cfg.model_dim + 2 * cfg.kv_dim) * cfg.model_dim,
-                 "o": cfg.num_layers * cfg.model_dim ** 2, "up": cfg.num_layers * cfg.mlp_hidden * cfg.model_dim,
-                 "down": cfg.num_layers * cfg.model_dim * cfg.mlp_hidden, "q_gain": cfg.num_layers * cfg.num_heads,
-                 "attn_scale": cfg.num_layers * cfg.model_dim, "mlp_scale": cfg.num_layers * cfg.model_dim,
-                 "resid_mix": cfg.num_layers * 2 * cfg.model_dim,
-                 "skip_weights": cfg.num_skip_weights * cfg.model_dim,
-                 "skip_gates": cfg.num_skip_weights * cfg.model_dim}
-        off = getattr(lay, name)
-        return self.params[off: off + sizes[name]]
+        off = getattr(self.layout, name)
+        return self.params[off: off + self._arena_size(name)]
 
     def refresh(self) -> None:
         """After the arena changed: rewrite the step's tensor-core planes."""

@@ -165,7 +165,7 @@ def state_from_arena(dm: DeviceModel, flat: torch.Tensor | None = None) -> dict[
     src = dm if flat is None else _ArenaOf(dm, flat)
     a = {k: src.arena(k).detach().cpu().numpy() for k in
          ("emb", "qkv", "o", "up", "down", "q_gain", "attn_scale", "mlp_scale", "resid_mix", "skip_weights",
-          "skip_gates")}
+          "skip_gates", "smear_gate", "smear_lambda", "attn_gate_w", "softcap", "parallel_post", "parallel_resid")}
     qkv = a["qkv"].reshape(L, d + 2 * kv, d)
     out = {
         "tok_emb.weight": a["emb"].reshape(cfg.vocab_size, d),
@@ -182,6 +182,17 @@ def state_from_arena(dm: DeviceModel, flat: torch.Tensor | None = None) -> dict[
         out[f"blocks.{i}.mlp_scale"] = a["mlp_scale"].reshape(L, d)[i]
         out[f"blocks.{i}.resid_mix"] = a["resid_mix"].reshape(L, 2, d)[i]
         out[f"blocks.{i}.attn.q_gain"] = a["q_gain"].reshape(L, cfg.num_heads)[i]
+        if cfg.sparse_attn_gate_enabled:
+            out[f"blocks.{i}.attn.attn_gate_w"] = a["attn_gate_w"].reshape(L, cfg.num_heads, cfg.gate_window)[i]
+    if cfg.smear_gate_enabled:  # model.py:1101-1105
+        out["smear_gate.weight"] = a["smear_gate"].reshape(1, cfg.gate_window)
+        out["smear_lambda"] = a["smear_lambda"].reshape(1)
+    if cfg.asym_logit_rescale:
+        out["softcap_pos"] = a["softcap"][0].copy()
+        out["softcap_neg"] = a["softcap"][1].copy()
+    if cfg.parallel_start_layer > 0:
+        out["parallel_post_lambdas"] = a["parallel_post"].reshape(L, 2, 2)
+        out["parallel_resid_lambdas"] = a["parallel_resid"].reshape(L, 2)
     return out
 
 
@@ -190,13 +201,17 @@ def arena_slices(dm: DeviceModel, name: str, shape) -> torch.Tensor:
     (None where the tensor is not one contiguous segment: qo_bank, kv_bank)."""
     cfg, L, d = dm.cfg, dm.cfg.num_layers, dm.cfg.model_dim
     direct = {"tok_emb.weight": "emb", "mlp_up_bank": "up", "mlp_down_bank": "down", "skip_weights": "skip_weights",
-              "skip_gates": "skip_gates"}
+              "skip_gates": "skip_gates", "smear_gate.weight": "smear_gate", "smear_lambda": "smear_lambda",
+              "parallel_post_lambdas": "parallel_post", "parallel_resid_lambdas": "parallel_resid"}
     if name in direct:
         return dm.arena(direct[name]).view(*shape)
+    if name in ("softcap_pos", "softcap_neg"):
+        k = 0 if name == "softcap_pos" else 1
+        return dm.arena("softcap")[k: k + 1].view(*shape)
     if name.startswith("blocks."):
         i, field = int(name.split(".")[1]), name.split(".", 2)[2]
         seg = {"attn_scale": "attn_scale", "mlp_scale": "mlp_scale", "resid_mix": "resid_mix",
-               "attn.q_gain": "q_gain"}[field]
+               "attn.q_gain": "q_gain", "attn.attn_gate_w": "attn_gate_w"}[field]
         per = int(np.prod(shape))
         return dm.arena(seg)[i * per: (i + 1) * per].view(*shape)
     return None
@@ -217,8 +232,8 @@ class ReplenishTTT:
         cfg = dm.cfg
         if not dm.full_params:
             raise ValueError("replenish needs DeviceModel(full_params=True)")
-        if cfg.lora_enabled or cfg.motifs:
-            raise ValueError("the full-parameter updates train the plain GPT without adapters")
+        if cfg.lora_enabled:
+            raise ValueError("the full-parameter updates train the model without adapters")
         if cfg.retrain_mode not in ("replenish", "full"):
             raise ValueError("ReplenishTTT runs retrain_mode 'replenish' or 'full'")
         self.dm, self.cfg = dm, cfg

@@ -135,8 +135,10 @@ typedef struct altxs_model_desc {
     int32_t cdf_mode, cdf_bits;
     float logit_softcap, lora_scale;
     /* Reference motifs (altxs src/xsa_ttt/model.py:760-768, 845-862, 1064-1077,
-     * 1293-1362, 1404-1500); all zero = the plain GPT.  The test-time update
-     * (altxs_ttt_update, altxs_prefill) covers the plain GPT only. */
+     * 1293-1362, 1404-1500); all zero = the plain GPT.  The step and the
+     * full-parameter gradient (altxs_full_loss_grad) compute them; the LoRA
+     * update and the context prefill (altxs_ttt_update, altxs_prefill) cover
+     * the plain GPT only. */
     int32_t n_virtual;          /* layer applications (depth loops repeat layers); 0 = n_layers */
     int32_t n_encoder;          /* encoder applications (the U-Net skips' sources); 0 = n_virtual/2 */
     const int32_t *schedule;    /* host [n_virtual]: physical layer of each application, or NULL */
@@ -348,12 +350,18 @@ int altxs_ttt_update(const altxs_model_desc *desc, const altxs_weights *w, const
  *   emb [V][d] (the tied table), qkv [L][d+2*kvd][d] (each layer's q, k, v
  *   rows), o [L][d][d], up [L][F][d], down [L][d][F], q_gain [L][H],
  *   attn_scale [L][d], mlp_scale [L][d], resid_mix [L][2][d],
- *   skip_weights [S][d], skip_gates [S][d]   (S = L/2)
+ *   skip_weights [S][d], skip_gates [S][d]   (S = min(encoder, decoder)
+ *   applications), and the motif parameters of the model (empty segments when
+ *   a motif is off): smear_gate [gate_window], smear_lambda [1], attn_gate_w
+ *   [L][H][gate_window], softcap [2] (positive, negative), parallel_post
+ *   [L][2][2], parallel_resid [L][2]
  * The gradient and the AdamW moments use the same layout.  The host keeps the
  * boundary schedule (anneal, warmup, replay draws, XM candidates and probe
  * windows), which is integer and float arithmetic of a few values. */
 typedef struct altxs_param_layout {
-    int64_t emb, qkv, o, up, down, q_gain, attn_scale, mlp_scale, resid_mix, skip_weights, skip_gates, total;
+    int64_t emb, qkv, o, up, down, q_gain, attn_scale, mlp_scale, resid_mix, skip_weights, skip_gates;
+    int64_t smear_gate, smear_lambda, attn_gate_w, softcap, parallel_post, parallel_resid;
+    int64_t total;
 } altxs_param_layout;
 int altxs_param_layout_of(const altxs_model_desc *desc, altxs_param_layout *out);
 
@@ -368,7 +376,11 @@ int64_t altxs_full_workspace_bytes(const altxs_model_desc *desc, int n);
  * [layout.total] (all entries written).  The forward reads the five matrices
  * from dense (tensor cores from w->split when set) and the small parameters
  * from w; the caller points both into its parameter arena.  desc->lora_rank
- * must be 0; the plain GPT only.  loss_out: device float or NULL. */
+ * must be 0.  The motifs of desc run in the forward and the backward as in the
+ * reference's training forward (GPT._forward_hidden, model.py:1377-1476, with
+ * the depth-loop schedule): the smear gate from the window's first position,
+ * XSA, the sparse attention gate, parallel lanes, the asymmetric softcap; their
+ * parameters get gradients like every other.  loss_out: device float or NULL. */
 int altxs_full_loss_grad(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
                          const int32_t *tokens, int n, int first, float *loss_out, float *grad, void *workspace,
                          int64_t workspace_bytes, altxs_stream_t stream);

@@ -45,6 +45,9 @@ from oracle.model import OracleModel, OracleWeights
 
 # reference names of the five weight banks (model.py:997-1011)
 BANKS = ("tok_emb.weight", "qo_bank", "kv_bank", "mlp_up_bank", "mlp_down_bank")
+# model-level motif parameters (the per-block sparse gate is blocks.{i}.attn.attn_gate_w)
+MOTIF_PARAMS = ("smear_gate.weight", "smear_lambda", "softcap_pos", "softcap_neg", "parallel_post_lambdas",
+                "parallel_resid_lambdas")
 
 
 def chunk_ctx_start(chunk_start: int, block_size: int) -> tuple[int, int]:
@@ -167,8 +170,13 @@ class OracleReplenish:
             if name in state and np.asarray(state[name]).size:
                 self.p[name] = t(state[name])
         for i in range(L):
-            for k in ("attn_scale", "mlp_scale", "resid_mix", "attn.q_gain"):
-                self.p[f"blocks.{i}.{k}"] = t(state[f"blocks.{i}.{k}"])
+            for k in ("attn_scale", "mlp_scale", "resid_mix", "attn.q_gain", "attn.attn_gate_w"):
+                if f"blocks.{i}.{k}" in state:
+                    self.p[f"blocks.{i}.{k}"] = t(state[f"blocks.{i}.{k}"])
+        # motif parameters (model.py:753-758, 994-996, 1092-1105): trained like every other
+        for name in MOTIF_PARAMS:
+            if name in state:
+                self.p[name] = t(state[name])
         self.params = list(self.p.values())
         self.opt = torch.optim.AdamW(self.params, lr=cfg.ttt_lora_lr, betas=(cfg.ttt_beta1, cfg.ttt_beta2),
                                      weight_decay=cfg.ttt_weight_decay)
@@ -188,6 +196,16 @@ class OracleReplenish:
             "skip_weights": p.get("skip_weights", torch.zeros(0, cfg.model_dim)),
             "skip_gates": p.get("skip_gates", torch.zeros(0, cfg.model_dim)),
         }
+        if "smear_gate.weight" in p:
+            small["smear_gate"] = p["smear_gate.weight"].reshape(-1)
+            small["smear_lambda"] = p["smear_lambda"].reshape(1)
+        if "blocks.0.attn.attn_gate_w" in p:
+            small["attn_gate_w"] = torch.stack([p[f"blocks.{i}.attn.attn_gate_w"] for i in range(L)])
+        if "softcap_pos" in p:
+            small["softcap"] = torch.stack([p["softcap_pos"].reshape(()), p["softcap_neg"].reshape(())])
+        if "parallel_post_lambdas" in p:
+            small["parallel_post"] = p["parallel_post_lambdas"]
+            small["parallel_resid"] = p["parallel_resid_lambdas"]
         return OracleWeights(
             cfg=cfg, emb=p["tok_emb.weight"],
             q=[p["qo_bank"][i] for i in range(L)], o=[p["qo_bank"][L + i] for i in range(L)],

@@ -458,6 +458,96 @@ def gen_full() -> None:
     np.savez_compressed(HERE / "full_retrain.npz", **out)
 
 
+MOTIF_RETRAIN = dict(
+    vocab_size=64, num_layers=4, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0, rope_dims=8,
+    block_size=16, online_retrain_every=24, seed=17, retrain_mode="none", smear_gate_enabled=True, gate_window=8,
+    xsa_last_n=2, sparse_attn_gate_enabled=True, sparse_attn_gate_scale=0.5, asym_logit_rescale=True, num_loops=1,
+    loop_start=1, loop_end=2, parallel_start_layer=3, parallel_final_lane="mean",
+)
+MOTIF_RETRAIN_CASES = [
+    ("m_full", "full", dict(online_retrain_steps=2, online_retrain_replay=True, ttt_lora_lr=2e-3, ttt_beta1=0.9)),
+    ("m_xm", "replenish", dict(ttt_replenish_xm_k=3, ttt_replenish_warmup_steps=1,
+                               ttt_replenish_xm_4x_until_bytes=60, ttt_lora_lr=2e-3, ttt_weight_decay=0.01)),
+]
+
+
+def gen_motif_retrain() -> None:
+    """Both full-parameter retrain modes of the reference ("full" with replay
+    windows; replenish with Forward-XM) through its own online_retrain on a
+    GPT with every supported motif on (smear gate, XSA on the last 2 layers,
+    sparse attention gate, asymmetric softcap, one depth loop over layers 1-2
+    with looping active as at compression, parallel lanes from layer 3), random
+    weights: per-boundary loss, XM choice and scores, final weights."""
+    import copy
+
+    from xsa_ttt.compress import _init_online_state, _online_steps_at, online_retrain
+
+    h0 = XsaTttConfig(seed=MOTIF_RETRAIN["seed"])
+    for k, v in MOTIF_RETRAIN.items():
+        setattr(h0, k, v)
+    h0.rope_base = 1e4
+    h0.qk_gain_init = 5.0
+    h0.logit_softcap = 30.0
+    h0.ln_scale = True
+    h0.skip_gates_enabled = True
+    h0.attn_out_gate_enabled = False
+    h0.gated_attn_enabled = False
+    h0.rope_yarn = False
+    h0.tie_embeddings = True
+    h0.gradient_checkpointing = False
+    h0.ttt_lora_rank = 0
+    torch.manual_seed(0)
+    base = GPT(h0)
+    base.enable_looping(True)
+    g = torch.Generator().manual_seed(23)
+    sd = base.state_dict()
+    for k, v in sd.items():
+        if v.dtype != torch.float32:
+            continue
+        if v.ndim >= 2 and v.numel() > 64:
+            v = torch.randn(v.shape, generator=g) * (0.5 / v.shape[-1] ** 0.5 if "emb" not in k else 0.3)
+        elif k == "smear_lambda":
+            v = torch.full_like(v, 0.6)
+        elif k.startswith("smear_gate") or k.endswith("attn_gate_w"):
+            v = torch.randn(v.shape, generator=g) * 0.5
+        elif k.startswith("parallel_"):
+            v = v + 0.1 * torch.randn(v.shape, generator=g)
+        elif k == "softcap_pos":
+            v = torch.tensor(12.0)
+        elif k == "softcap_neg":
+            v = torch.tensor(18.0)
+        elif "skip_gates" in k or "resid_mix" in k or k.endswith("q_gain") or "scale" in k:
+            v = v + 0.05 * torch.randn(v.shape, generator=g)
+        sd[k] = v
+    base.load_state_dict(sd, strict=True)
+    arr = np.random.default_rng(6).integers(0, h0.vocab_size, size=100).astype(np.int64)
+    out = {"arr": arr.astype(np.int32), "config": np.frombuffer(json.dumps(MOTIF_RETRAIN).encode(), dtype=np.uint8)}
+    out.update({f"w0/{k}": v.detach().numpy().copy() for k, v in base.state_dict().items()})
+    dev = torch.device("cpu")
+    for name, mode, over in MOTIF_RETRAIN_CASES:
+        m = copy.deepcopy(base)
+        h = copy.deepcopy(h0)
+        h.retrain_mode = mode
+        for k, v in over.items():
+            setattr(h, k, v)
+        _, opt = _init_online_state(m, h, dev, True)
+        burst: dict = {}
+        out[f"{name}/over"] = np.frombuffer(json.dumps({"retrain_mode": mode, **over}).encode(), dtype=np.uint8)
+        for end in (24, 48, 72, 96):
+            steps = _online_steps_at(end, h, int(h.online_retrain_every))
+            m.train()
+            loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=None, seed=h.seed,
+                                  steps_override=steps, burst_state=burst, n_total=len(arr))
+            out[f"{name}/{end}/loss"] = np.float64(loss)
+            xm = getattr(m, "_xm_last", None)
+            if xm is not None and int(xm["end"]) == end:
+                out[f"{name}/{end}/xm_chosen"] = np.int32(xm["chosen"])
+                out[f"{name}/{end}/xm_scores"] = np.asarray(xm["scores"], dtype=np.float64)
+        for k, v in m.state_dict().items():
+            out[f"{name}/w/{k}"] = v.detach().numpy().copy()
+    np.savez_compressed(HERE / "motif_retrain.npz", **out)
+
+
 CODEC_REF = dict(
     vocab_size=256, num_layers=4, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0, rope_dims=16,
     block_size=64, online_retrain_every=128, seed=77, smear_gate_enabled=True, xsa_last_n=2,
@@ -556,6 +646,7 @@ if __name__ == "__main__":
     gen_model_motifs()
     gen_replenish()
     gen_full()
+    gen_motif_retrain()
     gen_codec_ref()
     gen_zipf()
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):

@@ -172,8 +172,9 @@ def test_motif_round_trip_and_batch_independence(tensor_cores):
 
 
 def test_motif_desc_refused_by_update_and_prefill():
-    """The window forward of the update and the reset prefill is the plain
-    GPT: a desc with motifs is refused there (ENOTSUP), not run wrong."""
+    """The LoRA update and the reset prefill run the plain GPT: a desc with
+    motifs is refused there, not run wrong (the full-parameter gradient
+    computes the motifs)."""
     import ctypes
 
     from altxs_b200.engine import DeviceModel
@@ -183,6 +184,7 @@ def test_motif_desc_refused_by_update_and_prefill():
     L = _lib.lib()
     assert L.altxs_prefill_workspace_bytes(ctypes.byref(dm.desc), 8) == -1
     assert L.altxs_ttt_workspace_bytes(ctypes.byref(dm.desc), 8) == -1
+    assert L.altxs_full_workspace_bytes(ctypes.byref(dm.desc), 8) > 0
 
 
 @pytest.mark.parametrize("tensor_cores", [True, False])
@@ -206,3 +208,19 @@ def test_shipped_format_codec_runs_on_the_step(golden, tensor_cores):
     back = eng.decode([r.payload for r in res], [len(s) for s in streams])
     for s, d in zip(streams, back):
         assert np.array_equal(s, d)
+
+
+def test_shipped_format_codec_with_its_retrain_mode(golden):
+    """The reference-format codec keeps its config's retrain mode ("full", the
+    reference default) and the entry points run it: every weight, the motifs'
+    own included, updated at each boundary on both sides; round trip exact."""
+    from altxs_b200.incremental import compress_full_sha_incremental, decompress_full_sha_incremental
+    from tests.conftest import GOLDEN
+
+    w = C.read_codec(GOLDEN / "codec_ref_v256.safetensors")
+    assert w.cfg.retrain_mode == "full" and w.cfg.motifs
+    data = np.random.default_rng(4).integers(0, 256, size=300).astype(np.uint8)
+    res = compress_full_sha_incremental(w, data, cfg=w.cfg, device=DEV, progress=False, verify_decode=True)
+    assert res["sha256_ok"] and res["roundtrip_ok"] and res["retrain_count"] == 2
+    dec = decompress_full_sha_incremental(w, res["payload"], len(data), cfg=w.cfg, device=DEV, progress=False)
+    assert dec["decoded_sha256"] == res["sha256"]

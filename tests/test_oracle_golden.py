@@ -280,6 +280,41 @@ def test_oracle_full_retrain_matches_reference(golden, name):
     assert err < 0.1 * lr, (err, lr)
 
 
+def motif_case(g, name):
+    """Config and initial state of one golden retrain scenario on the motif model."""
+    import json
+
+    base = json.loads(bytes(g["config"]))
+    over = json.loads(bytes(g[f"{name}/over"]))
+    cfg = ModelConfig(**{**base, **over})
+    return cfg, {k[3:]: g[k] for k in g.files if k.startswith("w0/")}
+
+
+@pytest.mark.parametrize("name", ["m_full", "m_xm"])
+def test_oracle_motif_retrain_matches_reference(golden, name):
+    """Both full-parameter retrain modes on a model with every supported motif
+    on (smear gate, XSA, sparse attention gate, asymmetric softcap, a depth
+    loop, parallel lanes) against the reference's own online_retrain: loss and
+    XM choice per boundary, every parameter (the motifs' own included) at the end."""
+    from oracle.replenish import OracleReplenish
+
+    g = golden("motif_retrain.npz")
+    cfg, w0 = motif_case(g, name)
+    o = OracleReplenish(cfg, w0)
+    assert {"smear_gate.weight", "softcap_pos", "parallel_post_lambdas", "blocks.1.attn.attn_gate_w"} <= set(o.p)
+    arr = g["arr"].astype(np.int64)
+    for end in (24, 48, 72, 96):
+        loss = o.boundary(arr, end, n_total=len(arr))
+        assert abs(loss - float(g[f"{name}/{end}/loss"])) < 1e-5, (end, loss)
+        if f"{name}/{end}/xm_chosen" in g.files:
+            assert o.xm_last["chosen"] == int(g[f"{name}/{end}/xm_chosen"])
+            assert np.abs(np.array(o.xm_last["scores"]) - g[f"{name}/{end}/xm_scores"]).max() < 1e-5
+    st = o.state()
+    assert set(st) == {k[len(name) + 3:] for k in g.files if k.startswith(f"{name}/w/")}
+    err = max(float(np.abs(st[k] - g[f"{name}/w/{k}"]).max()) for k in st)
+    assert err < 0.1 * cfg.ttt_lora_lr, err
+
+
 def test_oracle_lora_steps_match_reference(golden):
     """Three LoRA steps per boundary (replay windows after the first) against
     the reference's own online_retrain in lora mode: losses and adapters."""
