@@ -170,12 +170,19 @@ class OracleReplenish:
             if name in state and np.asarray(state[name]).size:
                 self.p[name] = t(state[name])
         for i in range(L):
-            for k in ("attn_scale", "mlp_scale", "resid_mix", "attn.q_gain", "attn.attn_gate_w"):
-                if f"blocks.{i}.{k}" in state:
-                    self.p[f"blocks.{i}.{k}"] = t(state[f"blocks.{i}.{k}"])
-        # motif parameters (model.py:753-758, 994-996, 1092-1105): trained like every other
+            for k in ("attn_scale", "mlp_scale", "resid_mix", "attn.q_gain"):
+                self.p[f"blocks.{i}.{k}"] = t(state[f"blocks.{i}.{k}"])
+            if cfg.sparse_attn_gate_enabled:
+                self.p[f"blocks.{i}.attn.attn_gate_w"] = t(state[f"blocks.{i}.attn.attn_gate_w"])
+        # motif parameters (model.py:753-758, 994-996, 1092-1105), trained like every
+        # other when their motif is on; the reference model always holds the
+        # parallel lambdas, which get no gradient (AdamW skips them) with the lanes off
+        on = {"smear_gate.weight": cfg.smear_gate_enabled, "smear_lambda": cfg.smear_gate_enabled,
+              "softcap_pos": cfg.asym_logit_rescale, "softcap_neg": cfg.asym_logit_rescale,
+              "parallel_post_lambdas": cfg.parallel_start_layer > 0,
+              "parallel_resid_lambdas": cfg.parallel_start_layer > 0}
         for name in MOTIF_PARAMS:
-            if name in state:
+            if on[name]:
                 self.p[name] = t(state[name])
         self.params = list(self.p.values())
         self.opt = torch.optim.AdamW(self.params, lr=cfg.ttt_lora_lr, betas=(cfg.ttt_beta1, cfg.ttt_beta2),
