@@ -60,7 +60,8 @@ class ModelConfig:
     ttt_weight_decay: float = 0.0
     ttt_k_lora: bool = True
     ttt_o_lora: bool = True
-    ttt_mlp_lora: bool = False
+    ttt_mlp_lora: bool = False   # MLP adapter (d -> d on the MLP's normed input); reference default on
+    ttt_o_lora_on_y: bool = False  # the o adapter reads the attention output instead of the normed input
     ttt_use_rslora: bool = False
     grad_clip: float = 1.0
     # full-parameter replenish (reference config.py:59-138, compress.py:363-482,
@@ -198,8 +199,8 @@ class ModelConfig:
             raise ValueError("cdf_mode must be 'fixed' or 'ref'")
         if self.cdf_mode == "fixed" and not (self.vocab_size < (1 << self.cdf_bits) <= (1 << 30)):
             raise ValueError("cdf_bits must satisfy vocab < 2^cdf_bits <= 2^30")
-        if self.ttt_mlp_lora and self.lora_enabled:
-            raise ValueError("MLP LoRA is not part of this engine (q/k/v/o + lm_head only)")
+        if self.lora_enabled and not 1 <= self.ttt_lora_rank <= 128:
+            raise ValueError("ttt_lora_rank must be in 1..128")
         if self.retrain_mode not in ("lora", "replenish", "full", "none"):
             raise ValueError("retrain_mode must be 'lora', 'replenish', 'full' or 'none'")
         if self.retrain_mode in ("replenish", "full") and self.parallel_start_layer > 0:

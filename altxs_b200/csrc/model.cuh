@@ -5,16 +5,18 @@
 
 namespace altxs {
 
-// LoRA arena offsets (floats) in TTTLoRA.parameters() order: lm, q_i, v_i, k_i, o_i.
+// LoRA arena offsets (floats) in TTTLoRA.parameters() order (its module
+// registration order, ttt_lora.py:67-105): lm, q_s, v_s, k_s, mlp_s, o_s over
+// the slots s (one per layer application).
 struct LoraOff {
-    int64_t lmA, lmB, qA, qB, vA, vB, kA, kB, oA, oB;  // per-layer blocks start; stride below
-    int64_t q_stride, v_stride, k_stride, o_stride, total;
+    int64_t lmA, lmB, qA, qB, vA, vB, kA, kB, mA, mB, oA, oB;  // per-slot blocks start; stride below
+    int64_t q_stride, v_stride, k_stride, m_stride, o_stride, total;
 };
 
 __host__ __device__ inline LoraOff lora_offsets(const altxs_model_desc &dsc) {
     LoraOff o{};
     const int64_t r = dsc.lora_rank, d = dsc.d_model, kvd = (int64_t)dsc.n_kv_heads * dsc.head_dim;
-    const int64_t V = dsc.vocab, L = dsc.n_layers;
+    const int64_t V = dsc.vocab, L = dsc.n_virtual > 0 ? dsc.n_virtual : dsc.n_layers;
     int64_t cur = 0;
     if (r <= 0) return o;
     o.lmA = cur;
@@ -34,6 +36,12 @@ __host__ __device__ inline LoraOff lora_offsets(const altxs_model_desc &dsc) {
         o.kA = cur;
         o.kB = cur + r * d;
         cur += L * o.k_stride;
+    }
+    if (dsc.lora_mask & 32) {  // MLP adapter: d -> d on the MLP's normed input
+        o.m_stride = r * d + d * r;
+        o.mA = cur;
+        o.mB = cur + r * d;
+        cur += L * o.m_stride;
     }
     if (dsc.lora_mask & 8) {
         o.o_stride = r * d + d * r;

@@ -34,6 +34,7 @@ struct Dims {
     int xsa_from;  // physical layers >= xsa_from run XSA (L = none)
     int par;       // some decoder applications run the two parallel lanes
     int gw;        // gate window of the smear and sparse attention gates
+    int mlora;     // MLP adapters (lora_mask bit 5)
 };
 
 // Per-application layout: which physical layer's weights run, at which KV set.
@@ -54,7 +55,8 @@ struct StepCtx {
     LoraOff lo;
     // workspace
     float *x, *x0, *nrm, *nrm2, *skip, *qkv, *q, *part, *y, *ao, *hid, *logits, *lt;
-    float *lane1, *mo;  // parallel lanes: the MLP lane and the MLP output
+    float *lane1, *mo;  // parallel lanes: the MLP lane; the MLP output (also with MLP adapters)
+    float *lt2;         // MLP adapter: t = A n2 per stream [n][r]
     // tensor-core path: hi/lo bf16 planes of the linear layers' inputs
     int tc;
     uint16_t *nrm_h, *nrm_l, *y_h, *y_l, *nrm2_h, *nrm2_l, *hid_h, *hid_l;
@@ -674,8 +676,11 @@ __global__ void k_post_attn(StepCtx c, int l) {
     const float *as = c.w.attn_scale + (int64_t)l * d;
     float *t = sm;  // [R]
     const bool has_o = R > 0 && c.b.lora && (c.dsc.lora_mask & 8);
-    const float *P = has_o ? c.b.lora + (int64_t)i * c.b.lora_stride : nullptr;
-    if (has_o) lora_t(P + c.lo.oA + l * c.lo.o_stride, c.nrm + (int64_t)i * d, R, d, t);
+    const float *P = R > 0 && c.b.lora ? c.b.lora + (int64_t)i * c.b.lora_stride : nullptr;
+    // the o adapter reads the block's normed input, or with lora_mask bit 6 the
+    // attention output y (ttt_o_lora_on_y, ttt_lora.py:168-170)
+    const float *o_in = (c.dsc.lora_mask & 64) ? c.y + (int64_t)i * d : c.nrm + (int64_t)i * d;
+    if (has_o) lora_t(P + c.lo.oA + l * c.lo.o_stride, o_in, R, d, t);
     __syncthreads();
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
@@ -693,6 +698,30 @@ __global__ void k_post_attn(StepCtx c, int l) {
         const float v = __fmul_rn(__fmul_rn(x[k], inv), ln);
         nr[k] = v;
         if (c.tc) split_store(c.nrm2_h, c.nrm2_l, (int64_t)i * d + k, v);
+    }
+    if (c.D.mlora && P) {  // MLP adapter's t = A n2 (the row is read back after the barrier)
+        __syncthreads();
+        lora_t(P + c.lo.mA + l * c.lo.m_stride, nr, R, d, c.lt2 + (int64_t)i * R);
+    }
+}
+
+// MLP output with its adapter, then the residual (ttt_lora.py:171-175):
+// x = x_mid + mlp_scale * (down + s * B t); encoder applications also keep the
+// result as a skip source.
+__global__ void k_mlp_resid(StepCtx c, int l, float *skip) {
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const int d = c.D.d, R = c.D.r;
+    const float *P = c.b.lora ? c.b.lora + (int64_t)i * c.b.lora_stride + c.lo.mB + l * c.lo.m_stride : nullptr;
+    const float *t = c.lt2 + (int64_t)i * R;
+    float *x = c.x + (int64_t)i * d;
+    const float *mo = c.mo + (int64_t)i * d, *ms = c.w.mlp_scale + (int64_t)l * d;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        float m = mo[k];
+        if (P) m = __fadd_rn(m, lora_u(P, t, R, k, c.dsc.lora_scale));
+        const float v = __fadd_rn(x[k], __fmul_rn(ms[k], m));
+        x[k] = v;
+        if (skip) skip[(int64_t)i * d + k] = v;
     }
 }
 
@@ -751,7 +780,7 @@ __global__ void k_final(StepCtx c, int lanes) {
 __global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
     extern __shared__ __align__(16) float buf[];  // [V]
     __shared__ CdfScratch sc;
-    __shared__ float tl[64];
+    __shared__ float tl[128];
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
     const Dims &D = c.D;
@@ -847,7 +876,9 @@ inline int64_t ws_size(const Dims &D) {
     s += A((int64_t)D.n * D.V);                       // logits
     s += A((int64_t)D.n * (D.r > 0 ? D.r : 1));       // lm LoRA t
     s += 3 * A((int64_t)D.n * D.d);                   // hi/lo bf16 planes of nrm, y, nrm2
-    if (D.par) s += 2 * A((int64_t)D.n * D.d);        // lane 1, MLP output
+    if (D.par) s += A((int64_t)D.n * D.d);            // lane 1
+    if (D.par || D.mlora) s += A((int64_t)D.n * D.d);  // MLP output
+    if (D.mlora) s += A((int64_t)D.n * D.r);          // MLP adapter t
     return s;
 }
 
@@ -866,7 +897,8 @@ int fill_dims(const altxs_model_desc *dsc, int n, Dims &D) {
     D.r = dsc->lora_rank;
     if (D.V < 2 || D.L < 1 || D.d % 64 || D.F % 64 || D.H < 1 || D.Hkv < 1 || D.H % D.Hkv) return ALTXS_EINVAL;
     if (D.hd * D.H != D.d || D.hd % 16 || D.hd > 128 || 32 % (D.hd / 8) || D.H / D.Hkv > 4) return ALTXS_ENOTSUP;
-    if (D.rd % 2 || D.rd > D.hd || D.ctx < 1 || D.r < 0 || D.r > 64) return ALTXS_EINVAL;
+    if (D.rd % 2 || D.rd > D.hd || D.ctx < 1 || D.r < 0 || D.r > 128) return ALTXS_EINVAL;
+    D.mlora = D.r > 0 && (dsc->lora_mask & 32) != 0;
     if ((int64_t)D.V * 4 > 160 * 1024) return ALTXS_ENOTSUP;
     if (dsc->cdf_mode != ALTXS_CDF_FIXED && dsc->cdf_mode != ALTXS_CDF_REF) return ALTXS_EINVAL;
     if (dsc->cdf_mode == ALTXS_CDF_FIXED && (dsc->cdf_bits > 30 || (1ll << dsc->cdf_bits) <= D.V))
@@ -981,10 +1013,9 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         c.hid_h = reinterpret_cast<uint16_t *>(c.hid);
         c.hid_l = c.hid_h + (int64_t)D.n * D.F;
     }
-    if (D.par) {
-        c.lane1 = take((int64_t)D.n * D.d);
-        c.mo = take((int64_t)D.n * D.d);
-    }
+    if (D.par) c.lane1 = take((int64_t)D.n * D.d);
+    if (D.par || D.mlora) c.mo = take((int64_t)D.n * D.d);
+    if (D.mlora) c.lt2 = take((int64_t)D.n * D.r);
     const altxs_split_planes *sp = w->split;
     c.tc = sp != nullptr;
     if (sp && (!sp->emb_hi || !sp->emb_lo || !sp->qkv_hi || !sp->qkv_lo || !sp->o_hi || !sp->o_lo || !sp->up_hi ||
@@ -1090,7 +1121,11 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.N = D.d;
         a.K = D.F;
         a.ldy = D.d;
-        if (par) {
+        // encoder outputs the decoder's skips read (the last nskip of them)
+        const int skip_slot = v - (D.enc - D.nskip);
+        float *skip_out = v < D.enc && skip_slot >= 0 ? c.skip + (int64_t)skip_slot * D.n * D.d : nullptr;
+        const bool mres = !par && D.mlora && b->lora;  // MLP adapter: the residual in k_mlp_resid
+        if (par || mres) {
             a.Y = c.mo;
             a.epi = kEpiStore;
         } else {
@@ -1099,13 +1134,12 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
             a.R = c.x;
             a.ldr = D.d;
             a.colscale = w->mlp_scale + (int64_t)l * D.d;
-            // encoder outputs the decoder's skips read (the last nskip of them)
-            const int slot = v - (D.enc - D.nskip);
-            a.Y2 = v < D.enc && slot >= 0 ? c.skip + (int64_t)slot * D.n * D.d : nullptr;
+            a.Y2 = skip_out;
             a.ldy2 = D.d;
         }
         if ((rc = linear(a, c.hid_h, c.hid_l, c.tc ? sp->down_hi : nullptr, c.tc ? sp->down_lo : nullptr, nullptr, nullptr))) return rc;
         if (par) ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_par_combine<<<D.n, 128, 0, st>>>(c, l));
+        if (mres) ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_mlp_resid<<<D.n, 128, 0, st>>>(c, l, skip_out));
     }
     const int lanes = lanes_on ? desc->parallel_final : -1;
     ALTXS_LAUNCH(::altxs::kKFinal, st, k_final<<<D.n, 128, D.d * 4, st>>>(c, lanes));

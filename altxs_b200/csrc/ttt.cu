@@ -27,6 +27,7 @@ struct TD {
     int A;          // layer applications (= L without depth loops)
     int enc, nskip; // encoder applications (the skips' sources); skips taken by the decoder
     int first;      // first scored position of the loss (rows before it are context only)
+    int omask;      // lora_mask
     int full;       // full-parameter gradient (replenish): extra tape, P recomputed per layer
     // motifs (full-parameter gradient only)
     int smear, gw, xsa_from, sgate, asym, par, pfinal;
@@ -41,7 +42,7 @@ struct Tape {
     // forward state
     float *x0, *x, *skip;  // skip [enc][T][d]
     // per layer application [A][...]
-    float *xin, *inv1, *n, *qkv, *hinv, *qr, *kr, *P, *tq, *tk, *tv, *to, *xmid, *inv2, *n2, *u;
+    float *xin, *inv1, *n, *qkv, *hinv, *qr, *kr, *P, *tq, *tk, *tv, *to, *tm, *xmid, *inv2, *n2, *u;
     // scratch
     float *y, *ao, *hbuf;
     // head
@@ -77,12 +78,13 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, FillMode mode = kFillLora) {
     D.rd = dsc.rope_dims;
     D.first = 0;
     D.full = mode == kFillFull;
+    D.omask = dsc.lora_mask;
     // an adapter update trains over >= 2 positions; a context prefill needs neither;
     // the full-parameter gradient trains the base itself (no adapters)
     if (mode == kFillFull) {
         if (T < 1 || D.r != 0) return ALTXS_EINVAL;
         if (D.d > 1024) return ALTXS_ENOTSUP;  // embedding scatter: 8 columns per thread of 128
-    } else if (T < (prefill ? 1 : 2) || D.r < (prefill ? 0 : 1) || D.r > 64) {
+    } else if (T < (prefill ? 1 : 2) || D.r < (prefill ? 0 : 1) || D.r > 128) {
         return ALTXS_EINVAL;
     }
     if (D.d % 64 || D.F % 64 || D.H % D.Hkv || D.hd * D.H != D.d) return ALTXS_EINVAL;
@@ -158,6 +160,7 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.tk = take(L * T * D.r);
     t.tv = take(L * T * D.r);
     t.to = take(L * T * D.r);
+    t.tm = take(L * T * D.r);
     t.xmid = take(L * T * d);
     t.inv2 = take(L * T);
     t.n2 = take(L * T * d);
@@ -185,6 +188,8 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.dt = take(T * D.r);
     t.grad = nullptr;  // set by caller (lora_floats)
     t.red = take(1024);
+    const bool o_on_y = D.r > 0 && (D.omask & 64);
+    if (o_on_y && !D.full) t.yl = take(L * T * d);  // the o adapter's input, per layer
     if (D.full) {
         t.xraw = take(L * T * d);
         t.yl = take(L * T * d);
@@ -1408,7 +1413,8 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
         TRY(attn_probs(R, l));
         // the full-parameter gradient keeps every application's attention output and projections
-        float *yb = D.full ? tp.yl + (int64_t)l * Tn * d : tp.y;
+        const bool o_on_y = r > 0 && (mask & 64);
+        float *yb = D.full || o_on_y ? tp.yl + (int64_t)l * Tn * d : tp.y;
         float *aob = D.full ? tp.aol + (int64_t)l * Tn * d : tp.ao;
         const bool ym = D.full && ymotif(D, i);
         float *ya = ym ? tp.yraw + (int64_t)l * Tn * d : yb;  // P v, before XSA and the gate
@@ -1431,7 +1437,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         if (ym) ALTXS_LAUNCH(kKTtt, st, t_xsa_gate<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
         TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), i * d, d, d, yb, d, aob, d));
         if (mask & 8)
-            TRY(lora_fwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
+            TRY(lora_fwd(R, o_on_y ? yb : n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, aob, d));
         ALTXS_LAUNCH(kKTtt, st, t_post_attn<<<Tn, 128, 0, st>>>(D, l, i, tp, *w, aob, par));
         float *u = tp.u + (int64_t)l * Tn * D.F;
@@ -1439,9 +1445,12 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
         float *sk = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
         const float *xm = tp.xmid + (int64_t)l * Tn * d;
-        if (dw || R.sp) {
+        if (dw || R.sp || (mask & 32)) {
             float *db = D.full ? tp.doutl + (int64_t)l * Tn * d : tp.dd;
             TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), i * d, d, D.F, tp.hbuf, D.F, db, d));
+            if (mask & 32)  // MLP adapter on the MLP's normed input, added to its output
+                TRY(lora_fwd(R, tp.n2 + (int64_t)l * Tn * d, d, lora + lo.mA + l * lo.m_stride,
+                             lora + lo.mB + l * lo.m_stride, d, s, tp.tm + (int64_t)l * Tn * r, db, d));
             if (par)
                 ALTXS_LAUNCH(kKTtt, st, t_par_combine<<<g1((int64_t)Tn * d, 256), 256, 0, st>>>((int64_t)Tn * d, d, l,
                                                                                                  i, tp, *w, Tn));
@@ -1554,6 +1563,10 @@ int backward(const Run &R, const float *lora, float *grad) {
                                     (int64_t)Tn * D.F, tp.dh, tp.u + (int64_t)l * Tn * D.F, tp.dh));
         if (full) TRY(wgrad(tp.dh, D.F, tp.n2 + (int64_t)l * Td, d, FG + lay.up + (int64_t)i * D.F * d, acc));
         TRY(lin_bwd(R, w->up, dw ? dw->up : nullptr, PL(up_hi), PL(up_lo), i * D.F, D.F, d, tp.dh, D.F, tp.dn2, d, 0.0f));
+        if (mask & 32)
+            TRY(lora_bwd(R, tp.n2 + (int64_t)l * Td, d, lora + lo.mA + l * lo.m_stride, lora + lo.mB + l * lo.m_stride,
+                         d, s, tp.tm + (int64_t)l * Tn * r, tp.dd, d, grad + lo.mA + l * lo.m_stride,
+                         grad + lo.mB + l * lo.m_stride, tp.dn2));
         // the MLP read: x_mid (sequential) or lane 1 (parallel)
         float *dmid = par ? tp.dl1 : tp.dx;
         ALTXS_LAUNCH(kKTtt, st, t_rms_bwd<<<Tn, 128, 0, st>>>(d, tp.dn2, d, tp.xmid + (int64_t)l * Td,
@@ -1565,12 +1578,17 @@ int backward(const Run &R, const float *lora, float *grad) {
         }
         const float *n = tp.n + (int64_t)l * Td;
         cudaMemsetAsync(tp.dn, 0, (size_t)Td * 4, st);
-        if (mask & 8)
+        const bool o_on_y = r > 0 && (mask & 64);
+        if ((mask & 8) && !o_on_y)
             TRY(lora_bwd(R, n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
                          tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
                          grad + lo.oB + l * lo.o_stride, tp.dn));
         if (full) TRY(wgrad(tp.dao, d, tp.yl + (int64_t)l * Td, d, FG + lay.o + (int64_t)i * d * d, acc));
         TRY(lin_bwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), i * d, d, d, tp.dao, d, tp.dy, d, 0.0f));
+        if ((mask & 8) && o_on_y)  // the o adapter read y: its d(input) joins d(y)
+            TRY(lora_bwd(R, tp.yl + (int64_t)l * Td, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride,
+                         d, s, tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
+                         grad + lo.oB + l * lo.o_stride, tp.dy));
         const bool ym = full && ymotif(D, i);
         if (ym) {  // XSA / sparse gate: dy becomes d(P v); d(v) and d(n[:gw]) on the side
             ALTXS_LAUNCH(kKTtt, st, t_xsa_gate_bwd<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));

@@ -50,6 +50,10 @@ def lora_mask(cfg: ModelConfig) -> int:
         m |= 2
     if cfg.ttt_o_lora:
         m |= 8
+    if cfg.ttt_mlp_lora:
+        m |= 32
+    if cfg.ttt_o_lora and cfg.ttt_o_lora_on_y:
+        m |= 64
     return m
 
 

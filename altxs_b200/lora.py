@@ -6,7 +6,10 @@ LoRA adapters follow the reference ``TTTLoRA`` (altxs
 zero, the delta is ``(x @ A.T @ B.T) * alpha / rank``, and an ``lm_head``
 adapter is always present.  The initial ``A`` matrices come from one CPU
 generator seeded with ``seed ^ 0xA5A51070`` (compress.py:1965-1968) in the
-reference's creation order: lm_head, q (per layer), v, k, o.
+reference's creation order: lm_head, q (per layer), v, k, mlp, o.  The MLP
+adapter maps the MLP's normed input (d -> d) and adds to the MLP output; the
+o adapter reads the block's normed input, or the attention output with
+``ttt_o_lora_on_y`` (ttt_lora.py:161-175).
 
 RoPE tables use the reference ``Rotary`` rule (model.py:130-190): fp32
 ``inv_freq = 1 / base ** (arange(0, rd, 2) / rd)``, ``freqs = outer(t,
@@ -38,6 +41,9 @@ def lora_shapes(cfg: ModelConfig) -> "OrderedDict[str, tuple[tuple[int, int], tu
     if cfg.ttt_k_lora:
         for i in range(L):
             out[f"k{i}"] = ((r, d), (kv, r))
+    if cfg.ttt_mlp_lora:
+        for i in range(L):
+            out[f"mlp{i}"] = ((r, d), (d, r))
     if cfg.ttt_o_lora:
         for i in range(L):
             out[f"o{i}"] = ((r, d), (d, r))

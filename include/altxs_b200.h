@@ -131,7 +131,9 @@ typedef struct altxs_model_desc {
     int32_t rope_dims;  /* partial RoPE width */
     int32_t skip_gates; /* sigmoid-gated U-Net skips */
     int32_t lora_rank;  /* 0 = no adapters */
-    int32_t lora_mask;  /* bit0 q, bit1 k, bit2 v, bit3 o, bit4 lm_head */
+    int32_t lora_mask;  /* bit0 q, bit1 k, bit2 v, bit3 o, bit4 lm_head, bit5 MLP (d -> d on the
+                           MLP's normed input, added to the MLP output), bit6 the o adapter
+                           reads the attention output y instead of the block's normed input */
     int32_t cdf_mode, cdf_bits;
     float logit_softcap, lora_scale;
     /* Reference motifs (altxs src/xsa_ttt/model.py:760-768, 845-862, 1064-1077,

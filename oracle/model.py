@@ -176,8 +176,8 @@ class OracleModel:
             y = y * g[:, :, None]
         y = y.reshape(T, H * D)
         out = y @ w.o[i].T
-        if lora is not None and f"o{i}" in lora.A:
-            out = out + lora.delta(f"o{i}", n, cfg.lora_scale)
+        if lora is not None and f"o{i}" in lora.A:  # ttt_lora.py:168-170
+            out = out + lora.delta(f"o{i}", y if cfg.ttt_o_lora_on_y else n, cfg.lora_scale)
         return out, (k, v)
 
     def _block(self, i, x, x0, x_pos, kv_prefix, lora, causal):
@@ -188,8 +188,12 @@ class OracleModel:
         n = _rms(x_in) * ln
         attn_out, kv_new = self._attn(i, n, x_pos, kv_prefix, lora, causal)
         x_out = x_in + sm["attn_scale"][i][None, :] * attn_out
-        h = F.leaky_relu(_rms(x_out) * ln @ self.w.up[i].T, negative_slope=0.5).square()
-        x_out = x_out + sm["mlp_scale"][i][None, :] * (h @ self.w.down[i].T)
+        mlp_n = _rms(x_out) * ln
+        h = F.leaky_relu(mlp_n @ self.w.up[i].T, negative_slope=0.5).square()
+        mlp_out = h @ self.w.down[i].T
+        if lora is not None and f"mlp{i}" in lora.A:  # ttt_lora.py:171-174
+            mlp_out = mlp_out + lora.delta(f"mlp{i}", mlp_n, cfg.lora_scale)
+        x_out = x_out + sm["mlp_scale"][i][None, :] * mlp_out
         return x_out, kv_new
 
     def _parallel_block(self, i, lane0, lane1, x0, x_pos, kv_prefix, causal):

@@ -286,6 +286,45 @@ def gen_lora_steps() -> None:
     np.savez_compressed(HERE / "lora_steps.npz", **out)
 
 
+LORA_DEFAULTS = [  # the reference's LoRA defaults: rank 80, k off, o and MLP adapters on
+    ("base", dict(ttt_lora_rank=80, ttt_k_lora=False, ttt_o_lora=True, ttt_mlp_lora=True, ttt_lora_lr=1e-3,
+                  online_retrain_steps=2, online_retrain_replay=True)),
+    ("o_on_y", dict(ttt_lora_rank=80, ttt_k_lora=False, ttt_o_lora=True, ttt_mlp_lora=True, ttt_o_lora_on_y=True,
+                    ttt_lora_lr=1e-3, online_retrain_steps=2, online_retrain_replay=True)),
+]
+
+
+def gen_lora_defaults() -> None:
+    """The reference's online_retrain in lora mode with its default adapter set
+    (rank 80, q/v/o + MLP + lm_head adapters, k off), with the o adapter on the
+    normed input and on the attention output: per-boundary losses, adapters
+    after two boundaries of two steps (replay window on the second)."""
+    from xsa_ttt.compress import _init_online_state, _online_steps_at, online_retrain
+
+    arr = np.random.default_rng(12).integers(0, SMALL["vocab_size"], size=200).astype(np.int64)
+    out = {"arr": arr.astype(np.int32)}
+    for name, over in LORA_DEFAULTS:
+        cfg = ModelConfig(**{**SMALL, **over})
+        w = C.synth_weights(cfg, seed=7)
+        m = ref_model(cfg, w)
+        h = m.cfg
+        h.ttt_o_lora_on_y = bool(over.get("ttt_o_lora_on_y", False))
+        h.online_retrain_steps = over["online_retrain_steps"]
+        h.online_retrain_replay = over["online_retrain_replay"]
+        dev = torch.device("cpu")
+        lora, opt = _init_online_state(m, h, dev, True)
+        out.update({f"{name}/init/{k}": v.detach().clone().numpy() for k, v in lora.state_dict().items()})
+        every = int(h.online_retrain_every)
+        for end in (every, 2 * every):
+            steps = _online_steps_at(end, h, every)
+            loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=lora, seed=h.seed,
+                                  steps_override=steps, n_total=len(arr))
+            out[f"{name}/{end}/loss"] = np.float64(loss)
+        out.update({f"{name}/final/{k}": v.detach().clone().numpy() for k, v in lora.state_dict().items()})
+        out[f"{name}/over"] = np.frombuffer(json.dumps(over).encode(), dtype=np.uint8)
+    np.savez_compressed(HERE / "lora_defaults.npz", **out)
+
+
 MOTIFS = dict(
     vocab_size=256, num_layers=6, model_dim=64, num_heads=4, num_kv_heads=2, mlp_mult=2.0,
     rope_dims=16, block_size=64, online_retrain_every=128, seed=3, retrain_mode="none",
@@ -643,6 +682,7 @@ if __name__ == "__main__":
     gen_model()
     gen_lora()
     gen_lora_steps()
+    gen_lora_defaults()
     gen_model_motifs()
     gen_replenish()
     gen_full()

@@ -315,6 +315,43 @@ def test_oracle_motif_retrain_matches_reference(golden, name):
     assert err < 0.1 * cfg.ttt_lora_lr, err
 
 
+def lora_ref_names(cfg) -> dict:
+    """Our adapter names -> the reference TTTLoRA module names."""
+    names = {"lm": "lm_head_lora"}
+    for i in range(cfg.num_layers):
+        for t, mod in (("q", "q_loras"), ("k", "k_loras"), ("v", "v_loras"), ("o", "o_loras"), ("mlp", "mlp_loras")):
+            names[f"{t}{i}"] = f"{mod}.{i}"
+    return names
+
+
+@pytest.mark.parametrize("name", ["base", "o_on_y"])
+def test_oracle_lora_defaults_match_reference(golden, name):
+    """The reference's default adapter set (rank 80, MLP adapters, k off; the o
+    adapter on the normed input or on the attention output) through its own
+    online_retrain in lora mode: initial A bit-identical, losses per boundary,
+    adapters after two boundaries of two steps."""
+    import json
+
+    g = golden("lora_defaults.npz")
+    cfg = ModelConfig(**{**SMALL, **json.loads(bytes(g[f"{name}/over"]))})
+    m = OracleModel(OracleWeights.from_model_weights(C.synth_weights(cfg, seed=7)))
+    ttt = OracleTTT(m)
+    names = lora_ref_names(cfg)
+    for ours in ttt.lora.A:
+        assert torch.equal(ttt.lora.A[ours], torch.from_numpy(g[f"{name}/init/{names[ours]}.A"])), ours
+    assert any(k.startswith("mlp") for k in ttt.lora.A)
+    arr = g["arr"].astype(np.int64)
+    every = cfg.online_retrain_every
+    for end in (every, 2 * every):
+        loss = ttt.update(arr, end)
+        assert abs(loss - float(g[f"{name}/{end}/loss"])) < 1e-5, (end, loss)
+    err = 0.0
+    for ours in ttt.lora.A:
+        for part, t in (("A", ttt.lora.A[ours]), ("B", ttt.lora.B[ours])):
+            err = max(err, float(np.abs(t.detach().numpy() - g[f"{name}/final/{names[ours]}.{part}"]).max()))
+    assert err < 0.05 * cfg.ttt_lora_lr, err
+
+
 def test_oracle_lora_steps_match_reference(golden):
     """Three LoRA steps per boundary (replay windows after the first) against
     the reference's own online_retrain in lora mode: losses and adapters."""
