@@ -42,8 +42,8 @@ def _golden_arena(g, case, cfg, part="final"):
 @pytest.mark.parametrize("case", CASES)
 def test_lora_defaults_update_matches_reference(golden, case, tensor_cores):
     """LoraTTT with the default adapter set, two steps per boundary (replay on
-    the second), against the reference's online_retrain: adapters after two
-    boundaries within a fraction of one Adam step."""
+    the second), against the reference's online_retrain: every boundary's loss,
+    and the adapters after two boundaries."""
     from altxs_b200.engine import DeviceModel, StreamBatch
     from altxs_b200.ttt import LoraTTT
 
@@ -61,10 +61,20 @@ def test_lora_defaults_update_matches_reference(golden, case, tensor_cores):
         pos = torch.arange(max(0, end - b.hist_len), end, device=DEV)
         b.hist[0].index_copy_(0, pos % b.hist_len, prefix[pos, 0])
         ttt(b, [0], end, prefix=prefix)
+        # the loss of the boundary's last step, as the reference's online_retrain returns it
+        loss = float(ttt.loss.item())
+        assert abs(loss - float(g[f"{case}/{end}/loss"])) < (2e-4 if tensor_cores else 2e-5), (end, loss)
     torch.cuda.synchronize()
-    got = b.lora[0].cpu().numpy()
-    err = float(np.abs(got - _golden_arena(g, case, cfg)).max())
-    assert err < (0.3 if tensor_cores else 0.05) * cfg.ttt_lora_lr, err
+    lr = cfg.ttt_lora_lr
+    diff = np.abs(b.lora[0].cpu().numpy() - _golden_arena(g, case, cfg))
+    # From the second step on every A entry gets gradient through B != 0; a few
+    # dozen of the rank-80 A entries have gradients near zero whose sign follows
+    # summation order, and Adam with beta1 = 0 turns a sign into a step of up to
+    # lr * sqrt((1 - beta2^t) / (1 - beta2)) at step t (1, 1.41, 1.72, 1.98 lr over
+    # the four steps).  The bulk agrees to a tenth of a step; the worst entry stays
+    # inside the largest displacement four steps can make.
+    assert (diff <= 0.1 * lr).mean() > 0.999, ((diff > 0.1 * lr).sum(), diff.size)
+    assert diff.max() < 6.2 * lr, diff.max()
 
 
 @pytest.mark.parametrize("tensor_cores", [True, False])
