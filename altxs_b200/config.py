@@ -219,8 +219,6 @@ class ModelConfig:
             raise ValueError("gate_window must be in 1..model_dim")
         if self.sparse_attn_gate_enabled and self.gate_window > self.head_dim:
             raise ValueError("the sparse attention gate needs gate_window <= head_dim")
-        if self.motifs and self.lora_enabled:
-            raise ValueError("the test-time LoRA update covers the plain GPT; use retrain_mode='none' with motifs")
         if self.motifs and self.context_mode == "reset":
             raise ValueError("the segment-reset prefill covers the plain GPT; use context_mode='sliding' with motifs")
 
@@ -259,8 +257,6 @@ class ModelConfig:
                 setattr(out, f.name, v)
         if out.retrain_mode not in ("lora", "replenish", "full", "none"):
             out.retrain_mode = "none"
-        if out.motifs and out.retrain_mode == "lora":
-            out.retrain_mode = "none"  # the LoRA update covers the plain GPT only
         return out
 
 

@@ -230,19 +230,20 @@ __global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) {
         __syncthreads();
         const float *P = c.b.lora + (int64_t)i * c.b.lora_stride;
         const LoraOff &o = c.lo;
-        lora_t(P + o.qA + l * o.q_stride, nx, R, d, tq);
-        if (c.dsc.lora_mask & 2) lora_t(P + o.kA + l * o.k_stride, nx, R, d, tq + R);
-        lora_t(P + o.vA + l * o.v_stride, nx, R, d, tq + 2 * R);
+        const int s = a.v;  // adapter slot: one per layer application (ttt_lora.py:73-77)
+        lora_t(P + o.qA + s * o.q_stride, nx, R, d, tq);
+        if (c.dsc.lora_mask & 2) lora_t(P + o.kA + s * o.k_stride, nx, R, d, tq + R);
+        lora_t(P + o.vA + s * o.v_stride, nx, R, d, tq + 2 * R);
         __syncthreads();
         const float sc = c.dsc.lora_scale;
         for (int k = threadIdx.x; k < D.qkv_n; k += blockDim.x) {
             if (k < d) {
-                v[k] = __fadd_rn(v[k], lora_u(P + o.qB + l * o.q_stride, tq, R, k, sc));
+                v[k] = __fadd_rn(v[k], lora_u(P + o.qB + s * o.q_stride, tq, R, k, sc));
             } else if (k < d + kvd) {
                 if (c.dsc.lora_mask & 2)
-                    v[k] = __fadd_rn(v[k], lora_u(P + o.kB + l * o.k_stride, tq + R, R, k - d, sc));
+                    v[k] = __fadd_rn(v[k], lora_u(P + o.kB + s * o.k_stride, tq + R, R, k - d, sc));
             } else {
-                v[k] = __fadd_rn(v[k], lora_u(P + o.vB + l * o.v_stride, tq + 2 * R, R, k - d - kvd, sc));
+                v[k] = __fadd_rn(v[k], lora_u(P + o.vB + s * o.v_stride, tq + 2 * R, R, k - d - kvd, sc));
             }
         }
     }
@@ -664,8 +665,9 @@ __global__ void k_attn_merge(StepCtx c, int p) {
     if (c.tc) split_store(c.y_h, c.y_l, (int64_t)i * D.d + h * D.hd + k, yv);
 }
 
-// o-LoRA on the pre-attention normed input, residual, rms*ln for the MLP.
-__global__ void k_post_attn(StepCtx c, int l) {
+// o-LoRA on the pre-attention normed input, residual, rms*ln for the MLP
+// (layer l, adapter slot s).
+__global__ void k_post_attn(StepCtx c, int l, int s) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
     const int i = blockIdx.x;
@@ -680,12 +682,12 @@ __global__ void k_post_attn(StepCtx c, int l) {
     // the o adapter reads the block's normed input, or with lora_mask bit 6 the
     // attention output y (ttt_o_lora_on_y, ttt_lora.py:168-170)
     const float *o_in = (c.dsc.lora_mask & 64) ? c.y + (int64_t)i * d : c.nrm + (int64_t)i * d;
-    if (has_o) lora_t(P + c.lo.oA + l * c.lo.o_stride, o_in, R, d, t);
+    if (has_o) lora_t(P + c.lo.oA + s * c.lo.o_stride, o_in, R, d, t);
     __syncthreads();
     float ss = 0.0f;
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
         float o = ao[k];
-        if (has_o) o = __fadd_rn(o, lora_u(P + c.lo.oB + l * c.lo.o_stride, t, R, k, c.dsc.lora_scale));
+        if (has_o) o = __fadd_rn(o, lora_u(P + c.lo.oB + s * c.lo.o_stride, t, R, k, c.dsc.lora_scale));
         const float xv = __fadd_rn(x[k], __fmul_rn(as[k], o));
         x[k] = xv;
         ss = __fmaf_rn(xv, xv, ss);
@@ -701,18 +703,18 @@ __global__ void k_post_attn(StepCtx c, int l) {
     }
     if (c.D.mlora && P) {  // MLP adapter's t = A n2 (the row is read back after the barrier)
         __syncthreads();
-        lora_t(P + c.lo.mA + l * c.lo.m_stride, nr, R, d, c.lt2 + (int64_t)i * R);
+        lora_t(P + c.lo.mA + s * c.lo.m_stride, nr, R, d, c.lt2 + (int64_t)i * R);
     }
 }
 
 // MLP output with its adapter, then the residual (ttt_lora.py:171-175):
 // x = x_mid + mlp_scale * (down + s * B t); encoder applications also keep the
 // result as a skip source.
-__global__ void k_mlp_resid(StepCtx c, int l, float *skip) {
+__global__ void k_mlp_resid(StepCtx c, int l, int s, float *skip) {
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, R = c.D.r;
-    const float *P = c.b.lora ? c.b.lora + (int64_t)i * c.b.lora_stride + c.lo.mB + l * c.lo.m_stride : nullptr;
+    const float *P = c.b.lora ? c.b.lora + (int64_t)i * c.b.lora_stride + c.lo.mB + s * c.lo.m_stride : nullptr;
     const float *t = c.lt2 + (int64_t)i * R;
     float *x = c.x + (int64_t)i * d;
     const float *mo = c.mo + (int64_t)i * d, *ms = c.w.mlp_scale + (int64_t)l * d;
@@ -725,20 +727,33 @@ __global__ void k_mlp_resid(StepCtx c, int l, float *skip) {
     }
 }
 
-// Two-lane residual update (model.py:1293-1348):
-//   a = attn_scale*ao ; m = mlp_scale*mo
+// Two-lane residual update (model.py:1293-1348; ttt_lora.py:181-250 with adapters):
+//   a = attn_scale*(ao + o-adapter) ; m = mlp_scale*(mo + MLP adapter)
 //   lane0 = r0*lane0 + p00*a + p10*m ; lane1 = r1*lane1 + p01*a + p11*m
-__global__ void k_par_combine(StepCtx c, int l) {
+// (layer l, adapter slot s)
+__global__ void k_par_combine(StepCtx c, int l, int s) {
+    extern __shared__ __align__(16) float tsm[];  // [2][R]: o- and MLP-adapter t
     const int i = blockIdx.x;
     if (!row_active(c.b, i)) return;
-    const int d = c.D.d;
+    const int d = c.D.d, R = c.D.r;
     const float *pp = c.w.parallel_post + (int64_t)l * 4, *pr = c.w.parallel_resid + (int64_t)l * 2;
     const float p00 = pp[0], p01 = pp[1], p10 = pp[2], p11 = pp[3], r0 = pr[0], r1 = pr[1];
     float *x = c.x + (int64_t)i * d, *l1 = c.lane1 + (int64_t)i * d;
     const float *ao = c.ao + (int64_t)i * d, *mo = c.mo + (int64_t)i * d;
     const float *as = c.w.attn_scale + (int64_t)l * d, *ms = c.w.mlp_scale + (int64_t)l * d;
+    const float *P = R > 0 && c.b.lora ? c.b.lora + (int64_t)i * c.b.lora_stride : nullptr;
+    const bool has_o = P && (c.dsc.lora_mask & 8), has_m = P && c.D.mlora;
+    if (has_o) {
+        const float *o_in = (c.dsc.lora_mask & 64) ? c.y + (int64_t)i * d : c.nrm + (int64_t)i * d;
+        lora_t(P + c.lo.oA + s * c.lo.o_stride, o_in, R, d, tsm);
+    }
+    if (has_m) lora_t(P + c.lo.mA + s * c.lo.m_stride, c.nrm2 + (int64_t)i * d, R, d, tsm + R);
+    __syncthreads();
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
-        const float a = __fmul_rn(as[k], ao[k]), m = __fmul_rn(ms[k], mo[k]);
+        float ov = ao[k], mv = mo[k];
+        if (has_o) ov = __fadd_rn(ov, lora_u(P + c.lo.oB + s * c.lo.o_stride, tsm, R, k, c.dsc.lora_scale));
+        if (has_m) mv = __fadd_rn(mv, lora_u(P + c.lo.mB + s * c.lo.m_stride, tsm + R, R, k, c.dsc.lora_scale));
+        const float a = __fmul_rn(as[k], ov), m = __fmul_rn(ms[k], mv);
         x[k] = __fadd_rn(__fadd_rn(__fmul_rn(r0, x[k]), __fmul_rn(p00, a)), __fmul_rn(p10, m));
         l1[k] = __fadd_rn(__fadd_rn(__fmul_rn(r1, l1[k]), __fmul_rn(p01, a)), __fmul_rn(p11, m));
     }
@@ -1105,7 +1120,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         if ((rc = linear(a, c.y_h, c.y_l, c.tc ? sp->o_hi : nullptr, c.tc ? sp->o_lo : nullptr, nullptr, nullptr))) return rc;
         // two-lane applications normed lane 1 for the MLP in k_prenorm
         if (!par)
-            ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l));
+            ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l, v));
         a.X = c.nrm2;
         a.W = w->up;
         a.row0 = l * D.F;
@@ -1138,8 +1153,10 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
             a.ldy2 = D.d;
         }
         if ((rc = linear(a, c.hid_h, c.hid_l, c.tc ? sp->down_hi : nullptr, c.tc ? sp->down_lo : nullptr, nullptr, nullptr))) return rc;
-        if (par) ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_par_combine<<<D.n, 128, 0, st>>>(c, l));
-        if (mres) ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_mlp_resid<<<D.n, 128, 0, st>>>(c, l, skip_out));
+        if (par)
+            ALTXS_LAUNCH(::altxs::kKPostAttn, st,
+                         k_par_combine<<<D.n, 128, 2 * (D.r > 0 ? D.r : 1) * 4, st>>>(c, l, v));
+        if (mres) ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_mlp_resid<<<D.n, 128, 0, st>>>(c, l, v, skip_out));
     }
     const int lanes = lanes_on ? desc->parallel_final : -1;
     ALTXS_LAUNCH(::altxs::kKFinal, st, k_final<<<D.n, 128, D.d * 4, st>>>(c, lanes));

@@ -123,8 +123,8 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, FillMode mode = kFillLora) {
         }
     }
     const bool motif = D.A != D.L || dsc.schedule || D.smear || dsc.xsa_last_n || D.sgate || D.asym || D.par;
-    // the LoRA update and the context prefill run the plain GPT stack
-    if (motif && mode != kFillFull) return ALTXS_ENOTSUP;
+    // the context prefill runs the plain GPT stack
+    if (motif && mode == kFillPrefill) return ALTXS_ENOTSUP;
     return ALTXS_OK;
 }
 
@@ -190,6 +190,17 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.red = take(1024);
     const bool o_on_y = D.r > 0 && (D.omask & 64);
     if (o_on_y && !D.full) t.yl = take(L * T * d);  // the o adapter's input, per layer
+    if (D.par && !D.full) {  // the lanes' combine and its backward read each application's outputs
+        t.aol = take(L * T * d);
+        t.doutl = take(L * T * d);
+    }
+    if (D.xsa_from < D.L || D.sgate) t.yraw = take(L * T * d);
+    if (D.par) {
+        t.lane1 = take(T * d);
+        t.dl1 = take(T * d);
+        t.dread = take(T * d);
+    }
+    if (D.xsa_from < D.L) t.dvx = take(T * D.kvd);
     if (D.full) {
         t.xraw = take(L * T * d);
         t.yl = take(L * T * d);
@@ -204,13 +215,6 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
         t.colbuf = take(T * cw);
         t.cpart = take((int64_t)kColChunks * cw);
         if (D.smear) t.esm = take(T * d);
-        if (D.xsa_from < D.L || D.sgate) t.yraw = take(L * T * d);
-        if (D.par) {
-            t.lane1 = take(T * d);
-            t.dl1 = take(T * d);
-            t.dread = take(T * d);
-        }
-        if (D.xsa_from < D.L) t.dvx = take(T * D.kvd);
     }
     if (tp) *tp = t;
     return off;
@@ -468,12 +472,12 @@ __global__ void t_ce(TD D, const int32_t *tgt, Tape tp, float cap, const float *
 // group value at the same position over its norm (floored at 1e-12), when
 // layer i is one of the last xsa_last_n; then y *= sigmoid(scale * w_h . n[:gw])
 // with n the block's normed attention input.  yraw -> yl; one warp per head.
-__global__ void t_xsa_gate(TD D, int l, int i, Tape tp, altxs_weights w) {
+__global__ void t_xsa_gate(TD D, int l, int i, Tape tp, altxs_weights w, float *yout) {
     const int t = blockIdx.x, hd = D.hd, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int64_t row = (int64_t)l * D.T + t;
     const float *yr = tp.yraw + row * D.d, *nr = tp.n + row * D.d;
     const float *vr = tp.qkv + row * D.qn + D.d + D.kvd;
-    float *yo = tp.yl + row * D.d;
+    float *yo = yout + (int64_t)t * D.d;
     const bool xsa = i >= D.xsa_from;
     for (int h = wid; h < D.H; h += nw) {
         float y[4], v[4];
@@ -961,6 +965,7 @@ __global__ void t_xsa_gate_bwd(TD D, int l, int i, Tape tp, altxs_weights w) {
         for (int h = 0; h < D.H; ++h) acc = __fmaf_rn(dzs[h], w.attn_gate_w[((int64_t)i * D.H + h) * D.gw + k], acc);
         dn[k] = __fadd_rn(dn[k], acc);
     }
+    if (!tp.colbuf) return;  // gate-weight products: the full-parameter gradient only
     float *cb = tp.colbuf + (int64_t)t * D.H * D.gw;
     for (int e = threadIdx.x; e < D.H * D.gw; e += blockDim.x) cb[e] = __fmul_rn(dzs[e / D.gw], nr[e % D.gw]);
 }
@@ -986,15 +991,15 @@ __global__ void t_par_bwd(TD D, int l, int i, int j, Tape tp, altxs_weights w, i
     const float *pr = w.parallel_resid + 2 * i, *pp = w.parallel_post + 4 * i;
     const float *sk = j >= 0 ? tp.skip + ((int64_t)(D.enc - 1 - j) * D.T + t) * d : nullptr;
     float *dx = tp.dx + (int64_t)t * d, *dl1 = tp.dl1 + (int64_t)t * d;
-    float *cb = tp.colbuf + (int64_t)t * 4 * d;
+    float *cb = tp.colbuf ? tp.colbuf + (int64_t)t * 4 * d : nullptr;  // parameter products (full gradient)
     float s[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
     for (int k = threadIdx.x; k < d; k += blockDim.x) {
         const float g0 = dx[k], g1 = dl1[k];
         const float as = w.attn_scale[(int64_t)i * d + k], ms = w.mlp_scale[(int64_t)i * d + k];
         const float ao = tp.aol[row + k], mo = tp.doutl[row + k];
         const float A = __fmul_rn(as, ao), M = __fmul_rn(ms, mo);
-        float l0 = tp.xraw[row + k];  // lane 0 after the skip
-        if (sk) {
+        float l0 = cb ? tp.xraw[row + k] : 0.0f;  // lane 0 after the skip
+        if (cb && sk) {
             const float scaled = __fmul_rn(w.skip_weights[(int64_t)j * d + k], sk[k]);
             l0 = skip_gates ? lerp_t(scaled, l0, sigmoidf_(w.skip_gates[(int64_t)j * d + k])) : __fadd_rn(l0, scaled);
         }
@@ -1002,8 +1007,10 @@ __global__ void t_par_bwd(TD D, int l, int i, int j, Tape tp, altxs_weights w, i
         const float dm = __fadd_rn(__fmul_rn(pp[2], g0), __fmul_rn(pp[3], g1));
         tp.dao[(int64_t)t * d + k] = __fmul_rn(as, da);
         tp.dd[(int64_t)t * d + k] = __fmul_rn(ms, dm);
-        cb[k] = __fmul_rn(da, ao);
-        cb[d + k] = __fmul_rn(dm, mo);
+        if (cb) {
+            cb[k] = __fmul_rn(da, ao);
+            cb[d + k] = __fmul_rn(dm, mo);
+        }
         s[0] = __fmaf_rn(g0, l0, s[0]);
         s[1] = __fmaf_rn(g1, tp.xmid[row + k], s[1]);
         s[2] = __fmaf_rn(g0, A, s[2]);
@@ -1013,6 +1020,7 @@ __global__ void t_par_bwd(TD D, int l, int i, int j, Tape tp, altxs_weights w, i
         dx[k] = __fmul_rn(pr[0], g0);
         dl1[k] = __fmul_rn(pr[1], g1);
     }
+    if (!cb) return;
 #pragma unroll
     for (int q = 0; q < 6; ++q) {
         const float v = block_sum(s[q], red);
@@ -1415,8 +1423,8 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         // the full-parameter gradient keeps every application's attention output and projections
         const bool o_on_y = r > 0 && (mask & 64);
         float *yb = D.full || o_on_y ? tp.yl + (int64_t)l * Tn * d : tp.y;
-        float *aob = D.full ? tp.aol + (int64_t)l * Tn * d : tp.ao;
-        const bool ym = D.full && ymotif(D, i);
+        float *aob = tp.aol ? tp.aol + (int64_t)l * Tn * d : tp.ao;
+        const bool ym = ymotif(D, i);
         float *ya = ym ? tp.yraw + (int64_t)l * Tn * d : yb;  // P v, before XSA and the gate
         const int64_t ldp = align_up(Tn, 8);
         if (R.sp) {
@@ -1434,7 +1442,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             g.causal = 2;
             TRY(gemm(R, g));
         }
-        if (ym) ALTXS_LAUNCH(kKTtt, st, t_xsa_gate<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
+        if (ym) ALTXS_LAUNCH(kKTtt, st, t_xsa_gate<<<Tn, 256, 0, st>>>(D, l, i, tp, *w, yb));
         TRY(lin_fwd(R, w->o, dw ? dw->o : nullptr, PL(o_hi), PL(o_lo), i * d, d, d, yb, d, aob, d));
         if (mask & 8)
             TRY(lora_fwd(R, o_on_y ? yb : n, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride, d, s,
@@ -1445,8 +1453,8 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         ALTXS_LAUNCH(kKTtt, st, t_leaky<<<g1((int64_t)Tn * D.F, 256), 256, 0, st>>>((int64_t)Tn * D.F, u, tp.hbuf));
         float *sk = l < D.enc ? tp.skip + (int64_t)l * Tn * d : nullptr;
         const float *xm = tp.xmid + (int64_t)l * Tn * d;
-        if (dw || R.sp || (mask & 32)) {
-            float *db = D.full ? tp.doutl + (int64_t)l * Tn * d : tp.dd;
+        if (dw || R.sp || (mask & 32) || par) {
+            float *db = tp.doutl ? tp.doutl + (int64_t)l * Tn * d : tp.dd;
             TRY(lin_fwd(R, w->down, dw ? dw->down : nullptr, PL(down_hi), PL(down_lo), i * d, d, D.F, tp.hbuf, D.F, db, d));
             if (mask & 32)  // MLP adapter on the MLP's normed input, added to its output
                 TRY(lora_fwd(R, tp.n2 + (int64_t)l * Tn * d, d, lora + lo.mA + l * lo.m_stride,
@@ -1544,10 +1552,12 @@ int backward(const Run &R, const float *lora, float *grad) {
         // MLP: d(down-projection output) into dd
         if (par) {  // both lanes' gradients -> the two branches, the residual parts, the lane products
             ALTXS_LAUNCH(kKTtt, st, t_par_bwd<<<Tn, 128, 0, st>>>(D, l, i, j, tp, *w, R.desc->skip_gates));
-            TRY(colsum(tp.colbuf, 4 * d, nullptr, 0, d, FG + lay.attn_scale + (int64_t)i * d));
-            TRY(colsum(tp.colbuf + d, 4 * d, nullptr, 0, d, FG + lay.mlp_scale + (int64_t)i * d));
-            TRY(colsum(tp.colbuf + 2 * d, 4 * d, nullptr, 0, 2, FG + lay.parallel_resid + 2 * i));
-            TRY(colsum(tp.colbuf + 2 * d + 2, 4 * d, nullptr, 0, 4, FG + lay.parallel_post + 4 * i));
+            if (full) {
+                TRY(colsum(tp.colbuf, 4 * d, nullptr, 0, d, FG + lay.attn_scale + (int64_t)i * d));
+                TRY(colsum(tp.colbuf + d, 4 * d, nullptr, 0, d, FG + lay.mlp_scale + (int64_t)i * d));
+                TRY(colsum(tp.colbuf + 2 * d, 4 * d, nullptr, 0, 2, FG + lay.parallel_resid + 2 * i));
+                TRY(colsum(tp.colbuf + 2 * d + 2, 4 * d, nullptr, 0, 4, FG + lay.parallel_post + 4 * i));
+            }
         } else {
             ALTXS_LAUNCH(kKTtt, st, t_scale_cols<<<g1(Td, 256), 256, 0, st>>>(Td, d, tp.dx, w->mlp_scale + (int64_t)i * d,
                                                                              tp.dd));
@@ -1589,10 +1599,10 @@ int backward(const Run &R, const float *lora, float *grad) {
             TRY(lora_bwd(R, tp.yl + (int64_t)l * Td, d, lora + lo.oA + l * lo.o_stride, lora + lo.oB + l * lo.o_stride,
                          d, s, tp.to + (int64_t)l * Tn * r, tp.dao, d, grad + lo.oA + l * lo.o_stride,
                          grad + lo.oB + l * lo.o_stride, tp.dy));
-        const bool ym = full && ymotif(D, i);
+        const bool ym = ymotif(D, i);
         if (ym) {  // XSA / sparse gate: dy becomes d(P v); d(v) and d(n[:gw]) on the side
             ALTXS_LAUNCH(kKTtt, st, t_xsa_gate_bwd<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
-            if (D.sgate) TRY(colsum(tp.colbuf, (int64_t)D.H * D.gw, nullptr, 0, D.H * D.gw,
+            if (full && D.sgate) TRY(colsum(tp.colbuf, (int64_t)D.H * D.gw, nullptr, 0, D.H * D.gw,
                                     FG + lay.attn_gate_w + (int64_t)i * D.H * D.gw));
         }
         // attention backward

@@ -28,8 +28,10 @@ from .config import ModelConfig
 
 
 def lora_shapes(cfg: ModelConfig) -> "OrderedDict[str, tuple[tuple[int, int], tuple[int, int]]]":
-    """name -> ((rank, in), (out, rank)) in TTTLoRA.parameters() order."""
-    r, d, kv, V, L = cfg.ttt_lora_rank, cfg.model_dim, cfg.kv_dim, cfg.vocab_size, cfg.num_layers
+    """name -> ((rank, in), (out, rank)) in TTTLoRA.parameters() order; one
+    adapter slot per layer application (depth loops repeat layers, each
+    application with its own adapters: ttt_lora.py:73-77)."""
+    r, d, kv, V, L = cfg.ttt_lora_rank, cfg.model_dim, cfg.kv_dim, cfg.vocab_size, cfg.num_virtual_layers
     out: OrderedDict = OrderedDict()
     if not cfg.lora_enabled:
         return out

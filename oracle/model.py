@@ -131,7 +131,9 @@ class OracleModel:
         return self.cos[pos][:, None, :], self.sin[pos][:, None, :]
 
     # ---- one block over rows x [T, d] with queries at positions qpos ---------
-    def _attn(self, i, n, x_pos, kv_prefix, lora, causal):
+    def _attn(self, i, n, x_pos, kv_prefix, lora, causal, slot=None):
+        """Attention of layer i; adapters of slot ``slot`` (the application index)."""
+        s = i if slot is None else slot
         cfg, w = self.cfg, self.w
         H, Hkv, D, rd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.rope_dims
         T = n.shape[0]
@@ -139,11 +141,11 @@ class OracleModel:
         k = n @ w.k[i].T
         v = n @ w.v[i].T
         if lora is not None:
-            s = cfg.lora_scale
-            q = q + lora.delta(f"q{i}", n, s)
-            if f"k{i}" in lora.A:
-                k = k + lora.delta(f"k{i}", n, s)
-            v = v + lora.delta(f"v{i}", n, s)
+            sc = cfg.lora_scale
+            q = q + lora.delta(f"q{s}", n, sc)
+            if f"k{s}" in lora.A:
+                k = k + lora.delta(f"k{s}", n, sc)
+            v = v + lora.delta(f"v{s}", n, sc)
         q = _rms(q.view(T, H, D))
         k = _rms(k.view(T, Hkv, D))
         v = v.view(T, Hkv, D)
@@ -176,35 +178,42 @@ class OracleModel:
             y = y * g[:, :, None]
         y = y.reshape(T, H * D)
         out = y @ w.o[i].T
-        if lora is not None and f"o{i}" in lora.A:  # ttt_lora.py:168-170
-            out = out + lora.delta(f"o{i}", y if cfg.ttt_o_lora_on_y else n, cfg.lora_scale)
+        if lora is not None and f"o{s}" in lora.A:  # ttt_lora.py:168-170
+            out = out + lora.delta(f"o{s}", y if cfg.ttt_o_lora_on_y else n, cfg.lora_scale)
         return out, (k, v)
 
-    def _block(self, i, x, x0, x_pos, kv_prefix, lora, causal):
+    def _block(self, i, x, x0, x_pos, kv_prefix, lora, causal, slot=None):
         cfg, sm = self.cfg, self.w.small
+        s = i if slot is None else slot
         ln = 1.0 / math.sqrt(i + 1) if cfg.ln_scale else 1.0
         mix = sm["resid_mix"][i]
         x_in = mix[0][None, :] * x + mix[1][None, :] * x0
         n = _rms(x_in) * ln
-        attn_out, kv_new = self._attn(i, n, x_pos, kv_prefix, lora, causal)
+        attn_out, kv_new = self._attn(i, n, x_pos, kv_prefix, lora, causal, s)
         x_out = x_in + sm["attn_scale"][i][None, :] * attn_out
         mlp_n = _rms(x_out) * ln
         h = F.leaky_relu(mlp_n @ self.w.up[i].T, negative_slope=0.5).square()
         mlp_out = h @ self.w.down[i].T
-        if lora is not None and f"mlp{i}" in lora.A:  # ttt_lora.py:171-174
-            mlp_out = mlp_out + lora.delta(f"mlp{i}", mlp_n, cfg.lora_scale)
+        if lora is not None and f"mlp{s}" in lora.A:  # ttt_lora.py:171-174
+            mlp_out = mlp_out + lora.delta(f"mlp{s}", mlp_n, cfg.lora_scale)
         x_out = x_out + sm["mlp_scale"][i][None, :] * mlp_out
         return x_out, kv_new
 
-    def _parallel_block(self, i, lane0, lane1, x0, x_pos, kv_prefix, causal):
+    def _parallel_block(self, i, lane0, lane1, x0, x_pos, kv_prefix, causal, lora=None, slot=None):
+        """Two-lane block (model.py:1293-1351; with adapters ttt_lora.py:181-250)."""
         cfg, sm = self.cfg, self.w.small
+        s = i if slot is None else slot
         ln = 1.0 / math.sqrt(i + 1) if cfg.ln_scale else 1.0
         mix = sm["resid_mix"][i]
         n = _rms(mix[0][None, :] * lane0 + mix[1][None, :] * x0) * ln
-        attn_out, kv_new = self._attn(i, n, x_pos, kv_prefix, None, causal)
+        attn_out, kv_new = self._attn(i, n, x_pos, kv_prefix, lora, causal, s)
         attn_out = sm["attn_scale"][i][None, :] * attn_out
-        h = F.leaky_relu(_rms(lane1) * ln @ self.w.up[i].T, negative_slope=0.5).square()
-        mlp_out = sm["mlp_scale"][i][None, :] * (h @ self.w.down[i].T)
+        mlp_n = _rms(lane1) * ln
+        h = F.leaky_relu(mlp_n @ self.w.up[i].T, negative_slope=0.5).square()
+        mlp_raw = h @ self.w.down[i].T
+        if lora is not None and f"mlp{s}" in lora.A:
+            mlp_raw = mlp_raw + lora.delta(f"mlp{s}", mlp_n, cfg.lora_scale)
+        mlp_out = sm["mlp_scale"][i][None, :] * mlp_raw
         pr, pp = sm["parallel_resid"][i], sm["parallel_post"][i]
         lane0 = pr[0] * lane0 + pp[0][0] * attn_out + pp[1][0] * mlp_out
         lane1 = pr[1] * lane1 + pp[0][1] * attn_out + pp[1][1] * mlp_out
@@ -225,8 +234,8 @@ class OracleModel:
         x0 = x
         enc, dec = cfg.layer_schedule
         skips, new_kv = [], []
-        for i in enc:
-            x, kv = self._block(i, x, x0, x_pos, kv_prefixes[len(new_kv)], lora, causal)
+        for i in enc:  # the application index is the adapter slot
+            x, kv = self._block(i, x, x0, x_pos, kv_prefixes[len(new_kv)], lora, causal, len(new_kv))
             new_kv.append(kv)
             skips.append(x)
         psl = cfg.parallel_start_layer
@@ -246,10 +255,10 @@ class OracleModel:
                     lane0 = lane1 = x
                 lane0 = skip_into(lane0, skip_idx)
                 lane0, lane1, kv = self._parallel_block(i, lane0, lane1, x0, x_pos,
-                                                        kv_prefixes[len(new_kv)], causal)
+                                                        kv_prefixes[len(new_kv)], causal, lora, len(new_kv))
             else:
                 x = skip_into(x, skip_idx)
-                x, kv = self._block(i, x, x0, x_pos, kv_prefixes[len(new_kv)], lora, causal)
+                x, kv = self._block(i, x, x0, x_pos, kv_prefixes[len(new_kv)], lora, causal, len(new_kv))
             new_kv.append(kv)
         if lane0 is not None:
             fl = cfg.parallel_final_lane

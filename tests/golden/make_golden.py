@@ -507,16 +507,19 @@ MOTIF_RETRAIN_CASES = [
     ("m_full", "full", dict(online_retrain_steps=2, online_retrain_replay=True, ttt_lora_lr=2e-3, ttt_beta1=0.9)),
     ("m_xm", "replenish", dict(ttt_replenish_xm_k=3, ttt_replenish_warmup_steps=1,
                                ttt_replenish_xm_4x_until_bytes=60, ttt_lora_lr=2e-3, ttt_weight_decay=0.01)),
+    ("m_lora", "lora", dict(ttt_lora_rank=8, ttt_k_lora=True, ttt_o_lora=True, ttt_mlp_lora=True, ttt_lora_lr=2e-3,
+                            online_retrain_steps=2, online_retrain_replay=True)),
 ]
 
 
 def gen_motif_retrain() -> None:
-    """Both full-parameter retrain modes of the reference ("full" with replay
-    windows; replenish with Forward-XM) through its own online_retrain on a
-    GPT with every supported motif on (smear gate, XSA on the last 2 layers,
+    """The reference's retrain modes ("full" with replay windows; replenish
+    with Forward-XM; lora with an adapter slot per layer application, MLP
+    adapters, replay) through its own online_retrain on a GPT with every
+    supported motif on (smear gate, XSA on the last 2 layers,
     sparse attention gate, asymmetric softcap, one depth loop over layers 1-2
     with looping active as at compression, parallel lanes from layer 3), random
-    weights: per-boundary loss, XM choice and scores, final weights."""
+    weights: per-boundary loss, XM choice and scores, final weights (adapters in lora mode)."""
     import copy
 
     from xsa_ttt.compress import _init_online_state, _online_steps_at, online_retrain
@@ -569,19 +572,23 @@ def gen_motif_retrain() -> None:
         h.retrain_mode = mode
         for k, v in over.items():
             setattr(h, k, v)
-        _, opt = _init_online_state(m, h, dev, True)
+        lora, opt = _init_online_state(m, h, dev, True)
+        if lora is not None:
+            out.update({f"{name}/init/{k}": v.detach().clone().numpy() for k, v in lora.state_dict().items()})
         burst: dict = {}
         out[f"{name}/over"] = np.frombuffer(json.dumps({"retrain_mode": mode, **over}).encode(), dtype=np.uint8)
         for end in (24, 48, 72, 96):
             steps = _online_steps_at(end, h, int(h.online_retrain_every))
             m.train()
-            loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=None, seed=h.seed,
+            loss = online_retrain(m, arr, end=end, cfg=h, device=dev, optimizer=opt, lora=lora, seed=h.seed,
                                   steps_override=steps, burst_state=burst, n_total=len(arr))
             out[f"{name}/{end}/loss"] = np.float64(loss)
             xm = getattr(m, "_xm_last", None)
             if xm is not None and int(xm["end"]) == end:
                 out[f"{name}/{end}/xm_chosen"] = np.int32(xm["chosen"])
                 out[f"{name}/{end}/xm_scores"] = np.asarray(xm["scores"], dtype=np.float64)
+        if lora is not None:
+            out.update({f"{name}/final/{k}": v.detach().clone().numpy() for k, v in lora.state_dict().items()})
         for k, v in m.state_dict().items():
             out[f"{name}/w/{k}"] = v.detach().numpy().copy()
     np.savez_compressed(HERE / "motif_retrain.npz", **out)

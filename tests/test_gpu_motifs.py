@@ -63,12 +63,15 @@ def _case_model(name: str):
     return cfg, w
 
 
-def _logits_mode(dm, toks_by_stream):
-    """LOGITS mode (the stream is not advanced: the test moves pos and prev_tok)."""
+def _logits_mode(dm, toks_by_stream, lora=None):
+    """LOGITS mode (the stream is not advanced: the test moves pos and prev_tok);
+    ``lora``: one adapter vector for every stream."""
     from altxs_b200.engine import StreamBatch
 
     n, T = len(toks_by_stream), len(toks_by_stream[0])
     b = StreamBatch(dm, n, words_per_stream=8, keep_logits=True)
+    if lora is not None:
+        b.lora.copy_(lora.expand_as(b.lora))
     toks = torch.as_tensor(np.stack(toks_by_stream).astype(np.int32), device=DEV)
     out = np.zeros((n, T, dm.cfg.vocab_size), dtype=np.float32)
     for t in range(T):

@@ -352,6 +352,46 @@ def test_oracle_lora_defaults_match_reference(golden, name):
     assert err < 0.05 * cfg.ttt_lora_lr, err
 
 
+def motif_lora_model(cfg, w0):
+    """OracleModel of a reference state (detached fp32 tensors)."""
+    import dataclasses
+
+    from oracle.replenish import OracleReplenish
+
+    w = OracleReplenish(cfg, w0).weights()
+    det = lambda v: [t.detach() for t in v] if isinstance(v, list) else v.detach()  # noqa: E731
+    w = dataclasses.replace(w, **{f.name: det(getattr(w, f.name)) for f in dataclasses.fields(w)
+                                  if f.name not in ("cfg", "small")},
+                            small={k: v.detach() for k, v in w.small.items()})
+    return OracleModel(w)
+
+
+def test_oracle_motif_lora_matches_reference(golden):
+    """The reference's lora mode on its motif model (one adapter slot per layer
+    application with the depth loop active, MLP adapters, replay steps) through
+    its own online_retrain: initial A bit-identical, loss per boundary, adapters."""
+    g = golden("motif_retrain.npz")
+    cfg, w0 = motif_case(g, "m_lora")
+    assert cfg.num_virtual_layers == 6 and cfg.lora_enabled
+    ttt = OracleTTT(motif_lora_model(cfg, w0))
+    names = {"lm": "lm_head_lora"}
+    for sl in range(cfg.num_virtual_layers):
+        for t, mod in (("q", "q_loras"), ("k", "k_loras"), ("v", "v_loras"), ("o", "o_loras"), ("mlp", "mlp_loras")):
+            names[f"{t}{sl}"] = f"{mod}.{sl}"
+    assert len([k for k in ttt.lora.A if k.startswith("q")]) == 6
+    for ours in ttt.lora.A:
+        assert torch.equal(ttt.lora.A[ours], torch.from_numpy(g[f"m_lora/init/{names[ours]}.A"])), ours
+    arr = g["arr"].astype(np.int64)
+    for end in (24, 48, 72, 96):
+        loss = ttt.update(arr, end)
+        assert abs(loss - float(g[f"m_lora/{end}/loss"])) < 1e-5, (end, loss)
+    err = 0.0
+    for ours in ttt.lora.A:
+        for part, t in (("A", ttt.lora.A[ours]), ("B", ttt.lora.B[ours])):
+            err = max(err, float(np.abs(t.detach().numpy() - g[f"m_lora/final/{names[ours]}.{part}"]).max()))
+    assert err < 0.05 * cfg.ttt_lora_lr, err
+
+
 def test_oracle_lora_steps_match_reference(golden):
     """Three LoRA steps per boundary (replay windows after the first) against
     the reference's own online_retrain in lora mode: losses and adapters."""
