@@ -13,7 +13,6 @@ from altxs_b200 import codec as C
 from altxs_b200.config import ModelConfig
 from oracle.model import OracleModel, OracleWeights
 from tests.test_gpu_motifs import BASE, CASES, _logits_mode
-from tests.test_gpu_replenish import _model
 from tests.test_gpu_step import _lora_vec
 from tests.test_oracle_golden import motif_case
 
@@ -70,15 +69,17 @@ def test_motif_lora_update_matches_reference(golden, tensor_cores):
     """LoraTTT on the reference's motif model (depth loop active: six adapter
     slots for four layers), two steps per boundary with replay, against the
     reference's online_retrain in lora mode: every boundary's loss, and the
-    adapters (the bulk within a tenth of an Adam step; the worst entry within
-    the displacement eight steps with beta1 = 0 can make)."""
+    adapters in units of an Adam step."""
     from altxs_b200.engine import StreamBatch
     from altxs_b200.lora import lora_shapes
     from altxs_b200.ttt import LoraTTT
 
+    from altxs_b200.engine import DeviceModel
+
     g = golden("motif_retrain.npz")
     cfg, w0 = motif_case(g, "m_lora")
-    dm = _model(cfg, w0, tensor_cores)
+    dm = DeviceModel(C.dense_weights(cfg, {k: np.asarray(v, np.float32) for k, v in w0.items()}), DEV,
+                     tensor_cores=tensor_cores)
     names = {"lm": "lm_head_lora"}
     for sl in range(cfg.num_virtual_layers):
         for t, mod in (("q", "q_loras"), ("k", "k_loras"), ("v", "v_loras"), ("o", "o_loras"), ("mlp", "mlp_loras")):
@@ -93,18 +94,24 @@ def test_motif_lora_update_matches_reference(golden, tensor_cores):
     assert np.array_equal(b.lora[0].cpu().numpy(), arena("init"))
     arr = g["arr"].astype(np.int32)
     prefix = torch.as_tensor(arr[:, None].copy(), device=DEV)
+    diffs = []
     for end in (24, 48, 72, 96):
         pos = torch.arange(max(0, end - b.hist_len), end, device=DEV)
         b.hist[0].index_copy_(0, pos % b.hist_len, prefix[pos, 0])
         ttt(b, [0], end, prefix=prefix)
-        loss = float(ttt.loss.item())
-        assert abs(loss - float(g[f"m_lora/{end}/loss"])) < (3e-4 if tensor_cores else 3e-5), (end, loss)
+        diffs.append(abs(float(ttt.loss.item()) - float(g[f"m_lora/{end}/loss"])))
+    # the first boundary pins the model; later ones carry the earlier steps' drift
+    assert diffs[0] < (2e-4 if tensor_cores else 2e-5), diffs
+    assert max(diffs) < (1e-3 if tensor_cores else 1e-4), diffs
     lr = cfg.ttt_lora_lr
     diff = np.abs(b.lora[0].cpu().numpy() - arena("final"))
-    assert (diff <= 0.1 * lr).mean() > 0.999, ((diff > 0.1 * lr).sum(), diff.size)
-    b2 = cfg.ttt_beta2
-    reach = sum(((1 - b2 ** t) / (1 - b2)) ** 0.5 for t in range(1, 9)) * lr  # eight steps, one entry
-    assert diff.max() < reach, (diff.max(), reach)
+    # fp32 agrees to a few percent of a step everywhere; the tensor cores' 2^-16
+    # products flip the signs of some near-zero gradients over the eight steps,
+    # and Adam (beta1 = 0) turns each into part of a step: 99.9 % of entries
+    # within half a step, every entry within one (measured worst 0.78 lr)
+    frac = 0.5 if tensor_cores else 0.1
+    assert (diff <= frac * lr).mean() > 0.999, ((diff > frac * lr).sum(), diff.size)
+    assert diff.max() < (1.0 if tensor_cores else 0.1) * lr, diff.max() / lr
 
 
 @pytest.mark.parametrize("tensor_cores", [True, False])

@@ -174,20 +174,23 @@ def test_motif_round_trip_and_batch_independence(tensor_cores):
     assert alone.payload == res[1].payload
 
 
-def test_motif_desc_refused_by_update_and_prefill():
-    """The LoRA update and the reset prefill run the plain GPT: a desc with
-    motifs is refused there, not run wrong (the full-parameter gradient
-    computes the motifs)."""
+def test_motif_desc_refused_by_prefill_only():
+    """The reset prefill runs the plain GPT: a desc with motifs is refused
+    there, not run wrong; the LoRA update and the full-parameter gradient
+    compute the motifs."""
     import ctypes
+    import dataclasses
 
     from altxs_b200.engine import DeviceModel
 
     cfg, w = _case_model("xsa")
+    cfg = dataclasses.replace(cfg, retrain_mode="lora", ttt_lora_rank=4)
+    w.cfg = cfg
     dm = DeviceModel(w, DEV)
     L = _lib.lib()
     assert L.altxs_prefill_workspace_bytes(ctypes.byref(dm.desc), 8) == -1
-    assert L.altxs_ttt_workspace_bytes(ctypes.byref(dm.desc), 8) == -1
-    assert L.altxs_full_workspace_bytes(ctypes.byref(dm.desc), 8) > 0
+    assert L.altxs_ttt_workspace_bytes(ctypes.byref(dm.desc), 8) > 0
+    assert L.altxs_full_workspace_bytes(ctypes.byref(dm.desc), 8) == -1  # the full gradient trains no adapters
 
 
 @pytest.mark.parametrize("tensor_cores", [True, False])
