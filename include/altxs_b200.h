@@ -253,7 +253,8 @@ int64_t altxs_step_noalloc_max_bytes(void);
 int64_t altxs_workspace_bytes(const altxs_model_desc *desc, int n_streams);
 
 /* Floats per stream in the LoRA arena: adapters in the reference
- * TTTLoRA.parameters() order lm(A,B), q_i(A,B).., v_i.., k_i.., o_i..
+ * TTTLoRA.parameters() order lm(A,B), q_s(A,B).., v_s.., k_s.., mlp_s.., o_s..
+ * over the slots s = 0..n_virtual-1, one per layer application
  * (ttt_lora.py:67-105), A [r][in] then B [out][r]. */
 int64_t altxs_lora_floats(const altxs_model_desc *desc);
 
