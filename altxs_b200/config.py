@@ -219,8 +219,6 @@ class ModelConfig:
             raise ValueError("gate_window must be in 1..model_dim")
         if self.sparse_attn_gate_enabled and self.gate_window > self.head_dim:
             raise ValueError("the sparse attention gate needs gate_window <= head_dim")
-        if self.motifs and self.context_mode == "reset":
-            raise ValueError("the segment-reset prefill covers the plain GPT; use context_mode='sliding' with motifs")
 
     def to_dict(self) -> dict[str, Any]:
         return dataclasses.asdict(self)

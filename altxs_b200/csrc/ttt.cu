@@ -122,9 +122,6 @@ int fill(const altxs_model_desc &dsc, int T, TD &D, FillMode mode = kFillLora) {
             on = on || p;
         }
     }
-    const bool motif = D.A != D.L || dsc.schedule || D.smear || dsc.xsa_last_n || D.sgate || D.asym || D.par;
-    // the context prefill runs the plain GPT stack
-    if (motif && mode == kFillPrefill) return ALTXS_ENOTSUP;
     return ALTXS_OK;
 }
 
@@ -689,8 +686,9 @@ __global__ void __launch_bounds__(256) t_softmax_bwd_pl(TD D, const uint16_t *ph
     }
 }
 
-// context prefill: K (normed, roped) and V rows of position t, layer l into
-// slot t % ctx of one stream's ring [L][2][Hkv][ctx][3*hd] (24-bit rows)
+// context prefill: K (normed, roped) and V rows of position t, layer
+// application l into slot t % ctx of one stream's ring [A][2][Hkv][ctx][3*hd]
+// (24-bit rows; depth loops give each application its own K/V set)
 __global__ void t_kv_write(TD D, Tape tp, uint8_t *kv, int64_t ctx) {
     const int t = blockIdx.x, l = blockIdx.y, hd = D.hd;
     const int64_t rb = 3 * (int64_t)hd, slot = t % ctx;
@@ -1845,7 +1843,7 @@ int altxs_prefill(const altxs_model_desc *desc, const altxs_weights *w, const al
         R.tcb = R.tca + align_up(R.tca_n, 128);
     }
     TRY(forward(R, tokens, nullptr, lora, nullptr, false));
-    ALTXS_LAUNCH(kKTtt, R.st, t_kv_write<<<dim3(T, R.D.L), 128, 0, R.st>>>(R.D, R.tp, kv, desc->ctx));
+    ALTXS_LAUNCH(kKTtt, R.st, t_kv_write<<<dim3(T, R.D.A), 128, 0, R.st>>>(R.D, R.tp, kv, desc->ctx));
     return ALTXS_OK;
 }
 

@@ -137,10 +137,9 @@ typedef struct altxs_model_desc {
     int32_t cdf_mode, cdf_bits;
     float logit_softcap, lora_scale;
     /* Reference motifs (altxs src/xsa_ttt/model.py:760-768, 845-862, 1064-1077,
-     * 1293-1362, 1404-1500); all zero = the plain GPT.  The step and the
-     * full-parameter gradient (altxs_full_loss_grad) compute them; the LoRA
-     * update and the context prefill (altxs_ttt_update, altxs_prefill) cover
-     * the plain GPT only. */
+     * 1293-1362, 1404-1500); all zero = the plain GPT.  The step, the
+     * updates (altxs_ttt_update, altxs_full_loss_grad) and the context
+     * prefill (altxs_prefill) compute them. */
     int32_t n_virtual;          /* layer applications (depth loops repeat layers); 0 = n_layers */
     int32_t n_encoder;          /* encoder applications (the U-Net skips' sources); 0 = n_virtual/2 */
     const int32_t *schedule;    /* host [n_virtual]: physical layer of each application, or NULL */
@@ -319,9 +318,11 @@ int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo
  * after a boundary update the stream's context is rebuilt from its last
  * block_size symbols at positions 0..  This writes the key and value rows of
  * tokens[0..T) at positions 0..T-1 (slots 0..T-1) of one stream's ring
- * kv ([L][2][Hkv][desc->ctx][3*hd]), computed with the stream's adapters;
- * the caller then steps the context's last token at position T.  lora may be
- * NULL when desc->lora_rank is 0. */
+ * kv ([n_virtual][2][Hkv][desc->ctx][3*hd]: one K/V set per layer
+ * application), computed with the stream's adapters and the model's motifs
+ * (the smear gate leaves tokens[0] alone, as at a sequence start); the caller
+ * then steps the context's last token at position T with the previous token
+ * tokens[T-1] for the smear gate.  lora may be NULL when desc->lora_rank is 0. */
 int64_t altxs_prefill_workspace_bytes(const altxs_model_desc *desc, int T);
 int altxs_prefill(const altxs_model_desc *desc, const altxs_weights *w, const altxs_dense_weights *dense,
                   const int32_t *tokens, int T, const float *lora, uint8_t *kv, void *workspace,

@@ -23,15 +23,35 @@ SMALL = dict(
 )
 
 
+def _motif_cfg_weights():
+    """Every motif on (with a depth loop and parallel lanes), q/k/v/o/MLP adapters."""
+    from tests.test_gpu_lora_motifs import _cfg, _weights
+
+    cfg = _cfg("all", context_mode="reset", ttt_lora_rank=4, ttt_lora_lr=1e-3)
+    return cfg, _weights(cfg, seed=21)
+
+
+@pytest.mark.parametrize("tensor_cores", [True, False])
+@pytest.mark.parametrize("with_updates", [False, True])
+def test_reset_with_motifs_matches_oracle(with_updates, tensor_cores):
+    """The reset prefill on a motif model (one K/V set per layer application,
+    smear gate from the context's first token, XSA, gate, lanes, adapters)."""
+    cfg, w = _motif_cfg_weights()
+    _check_reset(cfg, w, with_updates, tensor_cores)
+
+
 @pytest.mark.parametrize("with_updates", [False, True])
 def test_reset_logits_match_oracle(with_updates):
+    cfg = ModelConfig(**SMALL)
+    _check_reset(cfg, C.synth_weights(cfg, seed=21), with_updates, True)
+
+
+def _check_reset(cfg, w, with_updates, tensor_cores):
     from altxs_b200 import _lib
     from altxs_b200.engine import ContextReset, DeviceModel, StreamBatch
     from altxs_b200.ttt import LoraTTT
 
-    cfg = ModelConfig(**SMALL)
-    w = C.synth_weights(cfg, seed=21)
-    dm = DeviceModel(w, DEV)
+    dm = DeviceModel(w, DEV, tensor_cores=tensor_cores)
     om = OracleModel(OracleWeights.from_model_weights(w))
     ottt = OracleTTT(om)
     rng = np.random.default_rng(5)
@@ -53,6 +73,8 @@ def test_reset_logits_match_oracle(with_updates):
             st = om.reset_segment(s, t, ottt.lora if with_updates else None)
         tok = -1 if t == 0 else int(s[t - 1])
         b.tok.fill_(tok)
+        if b.prev_tok is not None:  # LOGITS mode leaves the smear gate's previous token to the caller
+            b.prev_tok.fill_(int(s[t - 2]) if t >= 2 else -1)
         b.step(_lib.STEP_LOGITS)
         got = b.logits[0].cpu().numpy()
         if tok >= 0:
@@ -61,6 +83,20 @@ def test_reset_logits_match_oracle(with_updates):
             errs.append(float(np.abs(got - ref).max()))
     assert max(errs) < TOL, max(errs)
     assert int(b.pos.item()) == cfg.block_size - 1 + (T - 128)  # positions restarted at the last boundary
+
+
+def test_reset_engine_roundtrip_with_motifs():
+    from altxs_b200.engine import DeviceModel, Engine
+    from altxs_b200.ttt import LoraTTT
+
+    cfg, w = _motif_cfg_weights()
+    dm = DeviceModel(w, DEV)
+    rng = np.random.default_rng(8)
+    streams = [rng.integers(0, cfg.vocab_size, size=k).astype(np.int32) for k in (200, 131)]
+    enc = Engine(dm, ttt=LoraTTT(dm)).encode(streams)
+    dec = Engine(dm, ttt=LoraTTT(dm)).decode([r.payload for r in enc], [len(x) for x in streams])
+    for a, d in zip(streams, dec):
+        assert np.array_equal(a, d)
 
 
 @pytest.mark.parametrize("n_streams", [1, 3])
