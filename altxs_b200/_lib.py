@@ -26,7 +26,7 @@ EXPORTS = (
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
     "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
-    "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit",
+    "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit", "altxs_set_step_fusion",
     "altxs_param_layout_of", "altxs_full_workspace_bytes", "altxs_full_loss_grad", "altxs_adamw",
     "altxs_params_axpy", "altxs_params_anchor", "altxs_split_params",
     "altxs_create", "altxs_load_weights", "altxs_set_adapters", "altxs_set_ttt", "altxs_set_segment",
@@ -34,7 +34,7 @@ EXPORTS = (
     "altxs_begin_decode", "altxs_get_status", "altxs_ctx_words_per_stream", "altxs_destroy",
 )
 KERNEL_CLASSES = ("embed", "prenorm", "linear", "qkv_post", "attn_partial", "attn_merge", "post_attn",
-                  "final_norm", "cdf_code", "coder", "ttt")
+                  "final_norm", "cdf_code", "coder", "ttt", "fused_step")
 
 
 class AcState(C.Structure):
@@ -144,6 +144,7 @@ def lib():
             "altxs_profile_mask": (C.c_int, [C.c_uint32]),
             "altxs_set_wait_limit": (C.c_int, [C.c_uint32]),
             "altxs_default_wait_limit": (C.c_uint32, []),
+            "altxs_set_step_fusion": (C.c_int, [C.c_int]),
             "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
             "altxs_step_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int,
                                              vp]),

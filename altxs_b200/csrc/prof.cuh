@@ -20,6 +20,7 @@ enum KernelClass : int {
     kKCdfCode,
     kKCoder,
     kKTtt,
+    kKFused,
     kKNumClasses
 };
 

@@ -11,158 +11,18 @@
 // reference computes the same dot products from pre-multiplied dense weights
 // (mixed_bit_delta.py:147-213 then F.linear); dequantised values are exact in
 // fp32, so the two differ only in rounding order.
-#include "qmm.cuh"
+#include "qmm_body.cuh"
 #include "prof.cuh"
 
 namespace altxs {
 namespace {
 
-__device__ __forceinline__ int width_of(uint32_t d) {
-    const int c = (d >> 16) & 15;
-    return c == 0 ? 0 : c == 1 ? 2 : c == 2 ? 3 : c == 3 ? 4 : 32;
-}
-
-__device__ __forceinline__ float leaky2(float v) {
-    const float t = v >= 0.0f ? v : __fmul_rn(v, 0.5f);
-    return __fmul_rn(t, t);
-}
-
-__device__ __forceinline__ void epilogue_store(const QmmArgs &a, int m, int n, float acc) {
-    float v = acc;
-    if (a.epi == kEpiLeaky2) {
-        v = leaky2(acc);
-    } else if (a.epi == kEpiResid) {
-        v = __fadd_rn(a.R[(int64_t)m * a.ldr + n], __fmul_rn(a.colscale[n], acc));
-        if (a.Y2) a.Y2[(int64_t)m * a.ldy2 + n] = v;
-    }
-    a.Y[(int64_t)m * a.ldy + n] = v;
-}
-
-// Extract NC consecutive codes (LSB-first, width B) starting at bit sh0 of w[0].
-template <int B, int NC>
-__device__ __forceinline__ void unpack_codes(const uint32_t *w, int sh0, uint32_t *codes) {
-#pragma unroll
-    for (int j = 0; j < NC; ++j) {
-        const int bp = sh0 + j * B, wi = bp >> 5, sh = bp & 31;
-        uint32_t v = w[wi] >> sh;
-        if (sh + B > 32) v |= w[wi + 1] << (32 - sh);
-        codes[j] = v & ((1u << B) - 1u);
-    }
-}
-
-// Levels of NC codes starting at code index c0 (multiple of NC) of one group.
-template <int NC>
-__device__ __forceinline__ void group_levels(const altxs_qmat &W, int row, int g, int G, uint32_t d, int c0,
-                                             float *lev) {
-    const int b = width_of(d);
-    const uint8_t *gp = W.codes + 8ull * ((uint64_t)W.row_off8[row] + (d >> 20));
-    if (b == 0) {
-#pragma unroll
-        for (int j = 0; j < NC; ++j) lev[j] = 0.0f;
-        return;
-    }
-    if (b == 32) {
-        const float2 *f = reinterpret_cast<const float2 *>(gp) + (c0 >> 1);
-#pragma unroll
-        for (int j = 0; j < NC / 2; ++j) {
-            const float2 v = f[j];
-            lev[2 * j] = v.x;
-            lev[2 * j + 1] = v.y;
-        }
-        return;
-    }
-    constexpr int kMaxW = (NC * 4 + 31) / 32 + 1;
-    uint32_t words[kMaxW];
-    uint32_t codes[NC];
-    const int bit0 = c0 * b;
-    const uint32_t *wp = reinterpret_cast<const uint32_t *>(gp) + (bit0 >> 5);
-    const int sh0 = bit0 & 31;
-    const int nw = (sh0 + NC * b + 31) >> 5;
-#pragma unroll
-    for (int i = 0; i < kMaxW; ++i) words[i] = i < nw ? wp[i] : 0u;
-    if (b == 2) unpack_codes<2, NC>(words, sh0, codes);
-    else if (b == 3) unpack_codes<3, NC>(words, sh0, codes);
-    else unpack_codes<4, NC>(words, sh0, codes);
-    if (W.lut) {
-        const uint16_t *lut = W.lut + 16ull * W.glut[(int64_t)row * G + g];
-#pragma unroll
-        for (int j = 0; j < NC; ++j) lev[j] = h2f(lut[codes[j]]);
-    } else {
-        const float center = (float)((1 << b) - 1) * 0.5f;
-#pragma unroll
-        for (int j = 0; j < NC; ++j) lev[j] = __fsub_rn((float)codes[j], center);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// GEMV path: one lane computes one (row, group) partial p_g for every m; the
-// lanes of a row then chain y = fma(s_g, p_g, y) in group order.
-constexpr int kGemvThreads = 128;
-constexpr int kGemvMaxM = 16;
-
 template <int MM>
 __global__ void __launch_bounds__(kGemvThreads) k_qgemv(QmmArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][K + K/64]: one pad float per group
-    const int K = a.K, G = K / 64, M = a.M;
-    const int kp = K + G;
-    for (int idx = threadIdx.x; idx < M * K; idx += blockDim.x) {
-        const int m = idx / K, k = idx - m * K;
-        xs[m * kp + k + (k >> 6)] = a.X[(int64_t)m * a.ldx + k];
-    }
+    qgemv_stage_x(a, xs, blockDim.x);
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // lanes per row: the power of two >= G, capped at 32 (then lanes loop over groups)
-    int lpr = 1;
-    while (lpr < G && lpr < 32) lpr <<= 1;
-    const int rows_per_warp = 32 / lpr;
-    const int warps = blockDim.x >> 5;
-    const int row_local = lane / lpr, sub = lane % lpr;
-    const int n = (blockIdx.x * warps + warp) * rows_per_warp + row_local;
-    const bool valid = n < a.N;
-    const int row = a.row0 + (valid ? n : 0);
-    float y[MM];
-#pragma unroll
-    for (int m = 0; m < MM; ++m) y[m] = 0.0f;
-    for (int g0 = 0; g0 < G; g0 += lpr) {
-        const int g = g0 + sub;
-        float p[MM];
-#pragma unroll
-        for (int m = 0; m < MM; ++m) p[m] = 0.0f;
-        float s = 0.0f;
-        if (valid && g < G) {
-            const uint32_t d = a.W.gdesc[(int64_t)row * G + g];
-            s = h2f((uint16_t)(d & 0xffffu));
-#pragma unroll 1
-            for (int c = 0; c < 64; c += 16) {
-                float lev[16];
-                group_levels<16>(a.W, row, g, G, d, c, lev);
-#pragma unroll
-                for (int m = 0; m < MM; ++m) {
-                    if (m < M) {
-                        const float *xr = xs + m * kp + g * 65 + c;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) p[m] = __fmaf_rn(lev[j], xr[j], p[m]);
-                    }
-                }
-            }
-        }
-        // chain this round's groups in group order
-        const int gl = min(lpr, G - g0);
-        for (int j = 0; j < gl; ++j) {
-            const int src = row_local * lpr + j;
-            const float sj = __shfl_sync(0xffffffffu, s, src);
-#pragma unroll
-            for (int m = 0; m < MM; ++m) {
-                const float pj = __shfl_sync(0xffffffffu, p[m], src);
-                y[m] = __fmaf_rn(sj, pj, y[m]);
-            }
-        }
-    }
-    if (valid && sub == 0) {
-#pragma unroll
-        for (int m = 0; m < MM; ++m)
-            if (m < M) epilogue_store(a, m, n, y[m]);
-    }
+    qgemv_rows<MM>(a, xs, blockIdx.x, blockDim.x >> 5, threadIdx.x >> 5);
 }
 
 // ---------------------------------------------------------------------------
@@ -218,7 +78,7 @@ __global__ void __launch_bounds__(kTThreads) k_qgemm(QmmArgs a) {
             uint32_t d = 0;
             if (wn < a.N) {
                 d = a.W.gdesc[(int64_t)wrow * G + g];
-                group_levels<16>(a.W, wrow, g, G, d, lc, lev);
+                qmm_group_levels<16>(a.W, wrow, g, G, d, lc, lev);
             } else {
 #pragma unroll
                 for (int q = 0; q < 16; ++q) lev[q] = 0.0f;
@@ -258,7 +118,7 @@ __global__ void __launch_bounds__(kTThreads) k_qgemm(QmmArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int n = n0 + tx * 4 + j;
-            if (n < a.N) epilogue_store(a, m, n, y[i][j]);
+            if (n < a.N) qmm_epilogue_store(a, m, n, y[i][j]);
         }
     }
 }
@@ -272,8 +132,7 @@ int launch_qmm_path(const QmmArgs &a, cudaStream_t stream, int force_path) {
     if (gemv) {
         if (a.M > kGemvMaxM) return ALTXS_EINVAL;
         const int G = a.K / 64;
-        int lpr = 1;
-        while (lpr < G && lpr < 32) lpr <<= 1;
+        const int lpr = qgemv_lanes_per_row(a.K);
         const int rows_per_cta = (kGemvThreads / 32) * (32 / lpr);
         const size_t sm = (size_t)a.M * (a.K + G) * sizeof(float);
         if (sm > 200 * 1024) return ALTXS_ENOTSUP;

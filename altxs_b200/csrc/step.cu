@@ -15,6 +15,7 @@
 #include "model.cuh"
 #include "prof.cuh"
 #include "qmm.cuh"
+#include "qmm_body.cuh"
 #include "tc.cuh"
 
 using namespace altxs;
@@ -64,19 +65,25 @@ struct StepCtx {
 
 __device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return !b.active || b.active[i]; }
 
+// Kernel bodies take the block's item (bi, in place of blockIdx.x) and the
+// thread count their arithmetic is written for (nt, in place of blockDim.x):
+// the fused step runs them in larger blocks, where threads >= nt only join
+// the barriers (their zero partials leave the block reductions unchanged).
+#define ALTXS_TLOOP(k, lim) for (int k = (int)threadIdx.x < nt ? (int)threadIdx.x : (lim); k < (lim); k += nt)
+
 // ---------------------------------------------------------------------------
 
 // Embedding row, the smear gate when on (model.py:1350-1362: raw +=
 // lambda * sigmoid(g . raw[:gate_window]) * raw of the previous token), RMSNorm.
-__global__ void k_embed(StepCtx c) {
+__device__ void embed_body(const StepCtx &c, int bi, int nt) {
     __shared__ float red[32];
     __shared__ float gate;
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, tok = c.b.tok[i];
     float *x = c.x + (int64_t)i * d, *x0 = c.x0 + (int64_t)i * d;
     if (tok < 0 || tok >= c.D.V) {
-        for (int k = threadIdx.x; k < d; k += blockDim.x) x[k] = x0[k] = 0.0f;
+        ALTXS_TLOOP(k, d) x[k] = x0[k] = 0.0f;
         return;
     }
     int prev = -1;
@@ -95,7 +102,7 @@ __global__ void k_embed(StepCtx c) {
     const bool smear = prev >= 0 && prev < c.D.V;
     const float *ed = c.w.emb_dense;
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         float v = ed ? ed[(int64_t)tok * d + k] : qmat_elem(c.w.emb, tok, k);
         if (smear) v = __fadd_rn(v, __fmul_rn(gate, ed ? ed[(int64_t)prev * d + k] : qmat_elem(c.w.emb, prev, k)));
         x[k] = v;
@@ -103,20 +110,21 @@ __global__ void k_embed(StepCtx c) {
     }
     const float inv = rms_inv(block_sum(ss, red), d);
     __syncthreads();
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         const float v = __fmul_rn(x[k], inv);
         x[k] = v;
         x0[k] = v;
     }
 }
+__global__ void k_embed(StepCtx c) { embed_body(c, blockIdx.x, blockDim.x); }
 
 // Skip lerp (decoder applications) + resid_mix + rms * ln -> x (= x_in), nrm.
 // Two-lane applications (model.py:1293-1348) keep x as lane 0 after the skip
 // (the lanes' residuals start from it, not from x_in) and also norm lane 1
 // into nrm2 for the MLP, which reads lane 1 instead of the attention output.
-__global__ void k_prenorm(StepCtx c, LayerApp a) {
+__device__ void prenorm_body(const StepCtx &c, const LayerApp &a, int bi, int nt) {
     __shared__ float red[32];
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, n = c.D.n, l = a.p;
     float *x = c.x + (int64_t)i * d;
@@ -128,7 +136,7 @@ __global__ void k_prenorm(StepCtx c, LayerApp a) {
     const bool par = a.mode != kAppPlain;
     float *l1 = par ? c.lane1 + (int64_t)i * d : nullptr;
     float ss = 0.0f, ss1 = 0.0f;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         float xv = x[k];
         if (a.mode == kAppParFirst) l1[k] = xv;
         if (par) ss1 = __fmaf_rn(l1[k], l1[k], ss1);
@@ -146,7 +154,7 @@ __global__ void k_prenorm(StepCtx c, LayerApp a) {
     const float ln = c.w.ln_scale[l];
     __syncthreads();
     float *nr = c.nrm + (int64_t)i * d;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         // x_in again from its parts (x now holds lane 0 on two-lane applications)
         const float xin = par ? __fadd_rn(__fmul_rn(mix[k], x[k]), __fmul_rn(mix[d + k], x0[k])) : x[k];
         const float v = __fmul_rn(__fmul_rn(xin, inv), ln);
@@ -159,6 +167,7 @@ __global__ void k_prenorm(StepCtx c, LayerApp a) {
         }
     }
 }
+__global__ void k_prenorm(StepCtx c, LayerApp a) { prenorm_body(c, a, blockIdx.x, blockDim.x); }
 
 // t[r] = A[r] . x  (warp per rank row; each lane sums its 16-byte chunks of
 // the row in order, then a fixed warp tree; the chunk loads of a row are
@@ -211,9 +220,10 @@ __device__ __forceinline__ float lora_u(const float *B, const float *t, int rank
 
 // LoRA on q/k/v, per-head RMSNorm, partial RoPE, q_gain, KV ring write.
 // Layers that run XSA get their new V rows (fp32, after LoRA) back in qkv.
-__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) {
+// (no block-wide reductions: its arithmetic does not depend on the block size)
+__device__ void qkv_post_body(const StepCtx &c, const LayerApp &a, int bi) {
     extern __shared__ __align__(16) float sm[];
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int tok = c.b.tok[i];
     if (tok < 0) return;
@@ -321,6 +331,8 @@ __device__ __forceinline__ void unpack24x2(uint32_t h, uint32_t lo2, float &f0, 
     f0 = __uint_as_float(__byte_perm(h, lo2, 0x1046));
     f1 = __uint_as_float(__byte_perm(h, lo2, 0x3256));
 }
+__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) { qkv_post_body(c, a, blockIdx.x); }
+
 
 // ---------------------------------------------------------------------------
 // Warp-pipelined split attention.  Item t of a layer (stream, kv head, split
@@ -372,21 +384,21 @@ __device__ __forceinline__ RingItem ring_item(const StepCtx &c, int t) {
     return it;
 }
 
-// l: the application's KV set
-template <int LPK, int G>
-__global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int l, int n_items, int slots) {
+// One warp's share of a layer's items: warp gw of GW takes items gw, gw+GW, ..
+// with its slots in wbuf and its mbarriers in bar (l: the application's KV set).
+// False when a copy did not land in time (the barriers are then left as they
+// are).  kReuse: the caller initialises the same barriers again later (the
+// fused step), so they are invalidated at the end.
+template <int LPK, int G, bool kReuse = false>
+__device__ bool attn_ring_warp(const StepCtx &c, int l, int n_items, int slots, int gw, int GW, uint8_t *wbuf,
+                               uint64_t *bar) {
     constexpr int KPP = 32 / LPK;  // keys per pass
     constexpr int HD = LPK * 8, RB = 3 * HD;
     constexpr uint32_t kChunkBytes = (uint32_t)kRingChunk * RB;  // K (or V) rows of one chunk
     constexpr unsigned FULL = 0xffffffffu;
-    extern __shared__ __align__(128) unsigned char smraw[];
-    __shared__ __align__(8) uint64_t bars[kRingMaxWarps * kRingMaxSlots];
     const Dims &D = c.D;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
     const int ds = lane % LPK, kl = lane / LPK;
-    const int GW = gridDim.x * W, gw = blockIdx.x * W + w;
-    uint8_t *wbuf = smraw + (int64_t)w * slots * 2 * kChunkBytes;
-    uint64_t *bar = bars + w * kRingMaxSlots;
     if (lane == 0) {
         for (int s = 0; s < slots; ++s) mbar_init(&bar[s], 1);
         fence_mbar_init();
@@ -470,7 +482,7 @@ __global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int
                 if (lane == 0) atomicOr(&c.b.ac[it.i].status, ALTXS_ST_TIMEOUT);
                 for (int s = 0; s < slots; ++s)
                     if (pend & (1u << s)) mbar_wait_bounded(&bar[s], (par >> s) & 1u, kWaitLimit);
-                return;
+                return false;
             }
             par ^= 1u << slot;
             pend &= ~(1u << slot);
@@ -575,6 +587,22 @@ __global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int
             }
         }
     }
+    if (kReuse) {  // every copy this warp issued has been waited for: release the barriers
+        __syncwarp();
+        if (lane == 0)
+            for (int s = 0; s < slots; ++s) mbar_inval(&bar[s]);
+    }
+    return true;
+}
+
+template <int LPK, int G>
+__global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int l, int n_items, int slots) {
+    constexpr uint32_t kChunkBytes = (uint32_t)kRingChunk * 3 * (LPK * 8);
+    extern __shared__ __align__(128) unsigned char smraw[];
+    __shared__ __align__(8) uint64_t bars[kRingMaxWarps * kRingMaxSlots];
+    const int w = threadIdx.x >> 5, W = blockDim.x >> 5;
+    attn_ring_warp<LPK, G>(c, l, n_items, slots, blockIdx.x * W + w, gridDim.x * W,
+                           smraw + (int64_t)w * slots * 2 * kChunkBytes, bars + w * kRingMaxSlots);
 }
 
 // Launch of the ring kernel for this model's head size and group size:
@@ -628,10 +656,13 @@ cudaError_t launch_attn(const StepCtx &c, int l, cudaStream_t st) {
 // y -= (y . v^) v^ with v^ = v/max(|v|, 1e-12) of the head's own new V row,
 // and with the sparse attention gate y *= sigmoid(scale * w_h . n[:gate_window])
 // (model.py:760-768, 845-862).  One CTA of hd threads per (stream, head).
-__global__ void k_attn_merge(StepCtx c, int p) {
+// (item bi = stream * H + head; nt = hd threads, one element each)
+__device__ void merge_body(const StepCtx &c, int p, int bi, int nt) {
     __shared__ float red[32];
     const Dims &D = c.D;
-    const int i = blockIdx.x / D.H, h = blockIdx.x % D.H, k = threadIdx.x;
+    const int i = bi / D.H, h = bi % D.H;
+    const bool act = (int)threadIdx.x < nt;
+    const int k = act ? (int)threadIdx.x : 0;
     if (!row_active(c.b, i) || c.b.tok[i] < 0) return;
     const float *pp = c.part + ((int64_t)i * D.H + h) * D.nsplit * (D.hd + 2);
     float M = -INFINITY;
@@ -646,9 +677,9 @@ __global__ void k_attn_merge(StepCtx c, int p) {
             a = __fmaf_rn(q[k], f, a);
         }
     }
-    float yv = l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
+    float yv = act && l > 0.0f ? __fdiv_rn(a, l) : 0.0f;
     if (p >= D.xsa_from) {
-        const float vn = c.qkv[(int64_t)i * D.qkv_n + D.d + D.kvd + (h / (D.H / D.Hkv)) * D.hd + k];
+        const float vn = act ? c.qkv[(int64_t)i * D.qkv_n + D.d + D.kvd + (h / (D.H / D.Hkv)) * D.hd + k] : 0.0f;
         const float nv = fmaxf(__fsqrt_rn(block_sum(__fmul_rn(vn, vn), red)), 1e-12f);
         const float vh = __fdiv_rn(vn, nv);
         const float dot = block_sum(__fmul_rn(yv, vh), red);
@@ -658,19 +689,21 @@ __global__ void k_attn_merge(StepCtx c, int p) {
         const float *gw = c.w.attn_gate_w + ((int64_t)p * D.H + h) * D.gw;
         const float *nr = c.nrm + (int64_t)i * D.d;
         // gate_window <= head_dim (checked on the host): thread k takes n[k]
-        const float g = block_sum(k < D.gw ? __fmul_rn(nr[k], gw[k]) : 0.0f, red);
+        const float g = block_sum(act && k < D.gw ? __fmul_rn(nr[k], gw[k]) : 0.0f, red);
         yv = __fmul_rn(yv, sigmoidf_(__fmul_rn(c.dsc.sparse_gate_scale, g)));
     }
+    if (!act) return;
     c.y[(int64_t)i * D.d + h * D.hd + k] = yv;
     if (c.tc) split_store(c.y_h, c.y_l, (int64_t)i * D.d + h * D.hd + k, yv);
 }
+__global__ void k_attn_merge(StepCtx c, int p) { merge_body(c, p, blockIdx.x, blockDim.x); }
 
 // o-LoRA on the pre-attention normed input, residual, rms*ln for the MLP
 // (layer l, adapter slot s).
-__global__ void k_post_attn(StepCtx c, int l, int s) {
+__device__ void post_attn_body(const StepCtx &c, int l, int s, int bi, int nt) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, R = c.D.r;
     float *x = c.x + (int64_t)i * d;
@@ -685,7 +718,7 @@ __global__ void k_post_attn(StepCtx c, int l, int s) {
     if (has_o) lora_t(P + c.lo.oA + s * c.lo.o_stride, o_in, R, d, t);
     __syncthreads();
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         float o = ao[k];
         if (has_o) o = __fadd_rn(o, lora_u(P + c.lo.oB + s * c.lo.o_stride, t, R, k, c.dsc.lora_scale));
         const float xv = __fadd_rn(x[k], __fmul_rn(as[k], o));
@@ -696,7 +729,7 @@ __global__ void k_post_attn(StepCtx c, int l, int s) {
     const float ln = c.w.ln_scale[l];
     __syncthreads();
     float *nr = c.nrm2 + (int64_t)i * d;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         const float v = __fmul_rn(__fmul_rn(x[k], inv), ln);
         nr[k] = v;
         if (c.tc) split_store(c.nrm2_h, c.nrm2_l, (int64_t)i * d + k, v);
@@ -706,19 +739,20 @@ __global__ void k_post_attn(StepCtx c, int l, int s) {
         lora_t(P + c.lo.mA + s * c.lo.m_stride, nr, R, d, c.lt2 + (int64_t)i * R);
     }
 }
+__global__ void k_post_attn(StepCtx c, int l, int s) { post_attn_body(c, l, s, blockIdx.x, blockDim.x); }
 
 // MLP output with its adapter, then the residual (ttt_lora.py:171-175):
 // x = x_mid + mlp_scale * (down + s * B t); encoder applications also keep the
 // result as a skip source.
-__global__ void k_mlp_resid(StepCtx c, int l, int s, float *skip) {
-    const int i = blockIdx.x;
+__device__ void mlp_resid_body(const StepCtx &c, int l, int s, float *skip, int bi, int nt) {
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, R = c.D.r;
     const float *P = c.b.lora ? c.b.lora + (int64_t)i * c.b.lora_stride + c.lo.mB + s * c.lo.m_stride : nullptr;
     const float *t = c.lt2 + (int64_t)i * R;
     float *x = c.x + (int64_t)i * d;
     const float *mo = c.mo + (int64_t)i * d, *ms = c.w.mlp_scale + (int64_t)l * d;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         float m = mo[k];
         if (P) m = __fadd_rn(m, lora_u(P, t, R, k, c.dsc.lora_scale));
         const float v = __fadd_rn(x[k], __fmul_rn(ms[k], m));
@@ -726,14 +760,15 @@ __global__ void k_mlp_resid(StepCtx c, int l, int s, float *skip) {
         if (skip) skip[(int64_t)i * d + k] = v;
     }
 }
+__global__ void k_mlp_resid(StepCtx c, int l, int s, float *skip) { mlp_resid_body(c, l, s, skip, blockIdx.x, blockDim.x); }
 
 // Two-lane residual update (model.py:1293-1348; ttt_lora.py:181-250 with adapters):
 //   a = attn_scale*(ao + o-adapter) ; m = mlp_scale*(mo + MLP adapter)
 //   lane0 = r0*lane0 + p00*a + p10*m ; lane1 = r1*lane1 + p01*a + p11*m
 // (layer l, adapter slot s)
-__global__ void k_par_combine(StepCtx c, int l, int s) {
+__device__ void par_combine_body(const StepCtx &c, int l, int s, int bi, int nt) {
     extern __shared__ __align__(16) float tsm[];  // [2][R]: o- and MLP-adapter t
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, R = c.D.r;
     const float *pp = c.w.parallel_post + (int64_t)l * 4, *pr = c.w.parallel_resid + (int64_t)l * 2;
@@ -749,7 +784,7 @@ __global__ void k_par_combine(StepCtx c, int l, int s) {
     }
     if (has_m) lora_t(P + c.lo.mA + s * c.lo.m_stride, c.nrm2 + (int64_t)i * d, R, d, tsm + R);
     __syncthreads();
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         float ov = ao[k], mv = mo[k];
         if (has_o) ov = __fadd_rn(ov, lora_u(P + c.lo.oB + s * c.lo.o_stride, tsm, R, k, c.dsc.lora_scale));
         if (has_m) mv = __fadd_rn(mv, lora_u(P + c.lo.mB + s * c.lo.m_stride, tsm + R, R, k, c.dsc.lora_scale));
@@ -758,27 +793,28 @@ __global__ void k_par_combine(StepCtx c, int l, int s) {
         l1[k] = __fadd_rn(__fadd_rn(__fmul_rn(r1, l1[k]), __fmul_rn(p01, a)), __fmul_rn(p11, m));
     }
 }
+__global__ void k_par_combine(StepCtx c, int l, int s) { par_combine_body(c, l, s, blockIdx.x, blockDim.x); }
 
 // final RMSNorm (+ lm_head LoRA t).  lanes: -1 one residual stream; after
 // two-lane applications 0 the lanes' mean, 1 lane 0, 2 lane 1 (model.py:1437-1443).
-__global__ void k_final(StepCtx c, int lanes) {
+__device__ void final_body(const StepCtx &c, int lanes, int bi, int nt) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float red[32];
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const int d = c.D.d, R = c.D.r;
     const float *x = lanes == 2 ? c.lane1 + (int64_t)i * d : c.x + (int64_t)i * d;
     const float *x1 = c.lane1 + (int64_t)i * d;
     float *nr = c.nrm + (int64_t)i * d;
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         float v = x[k];
         if (lanes == 0) v = __fmul_rn(0.5f, __fadd_rn(v, x1[k]));
         sm[k] = v;
         ss = __fmaf_rn(v, v, ss);
     }
     const float inv = rms_inv(block_sum(ss, red), d);
-    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+    ALTXS_TLOOP(k, d) {
         const float v = __fmul_rn(sm[k], inv);
         nr[k] = v;
         sm[k] = v;
@@ -790,13 +826,15 @@ __global__ void k_final(StepCtx c, int lanes) {
         lora_t(P + c.lo.lmA, sm, R, d, c.lt + (int64_t)i * R);
     }
 }
+__global__ void k_final(StepCtx c, int lanes) { final_body(c, lanes, blockIdx.x, blockDim.x); }
 
-// logits (+ lm LoRA) -> softcap -> integer CDF -> encode / decode
-__global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
+// logits (+ lm LoRA) -> softcap -> integer CDF -> encode / decode; written for
+// (and called only with) blocks of kCdfThreads threads
+__device__ void cdf_code_body(const StepCtx &c, int mode, int bi) {
     extern __shared__ __align__(16) float buf[];  // [V]
     __shared__ CdfScratch sc;
     __shared__ float tl[128];
-    const int i = blockIdx.x;
+    const int i = bi;
     if (!row_active(c.b, i)) return;
     const Dims &D = c.D;
     const int V = D.V, R = D.r, tok = c.b.tok[i];
@@ -875,6 +913,277 @@ __global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) {
         }
     }
 }
+__global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) { cdf_code_body(c, mode, blockIdx.x); }
+
+
+// ---------------------------------------------------------------------------
+// Fused step for a few streams on the CUDA-core path: one persistent,
+// cooperatively launched kernel runs the whole step (every layer application,
+// the logits, the CDF and the coder) as the same sequence of phases that
+// altxs_step launches one kernel each, calling the same bodies with the same
+// thread counts and item order, with a grid-wide barrier between phases.  Its
+// results are therefore bit-identical to the multi-launch step; what goes
+// away is the ~76 launches per symbol.  Every barrier wait is bounded: a wait
+// that gives up (or a block that saw a TMA copy time out) marks every stream
+// ALTXS_ST_TIMEOUT and all blocks return.
+
+constexpr int kFusedThreads = 512;  // = kCdfThreads: the CDF body runs at its own width
+// Attention in the fused step: few streams give few items (n * Hkv * splits),
+// so each warp keeps all chunks of its item in flight (8 slots of 32 rows =
+// one 256-key split) instead of 2; 2 warps per block hold 2 x 8 slots.
+constexpr int kFusedAttnWarps = 2;
+constexpr int kFusedAttnSlots = 8;
+constexpr int kFusedMaxApps = 64;
+constexpr uint32_t kGridWaitLimit = 1u << 24;  // polls of one barrier wait (~0.2 us each: a few seconds)
+
+struct GridSync {
+    unsigned count, err, pad0, pad1;
+};
+
+struct FusedProg {
+    GridSync *sync;
+    int mode;
+    int sched[kFusedMaxApps];  // physical layer of each application
+};
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// All blocks meet; ok = 0 from any thread of any block aborts the kernel.
+// One arrival word: every block adds 1 except block 0, which adds
+// 0x80000000 - (blocks - 1), so the word's top bit flips when the last block
+// arrives; a block waits for the flip relative to the value it saw.  Release
+// before the arrive, a fence after the wait: the next phase's loads see every
+// block's stores of this one.
+__device__ bool grid_sync(GridSync *g, int ok) {
+    __shared__ int res;
+    ok = __syncthreads_and(ok);
+    if (threadIdx.x == 0) {
+        if (!ok) atomicOr(&g->err, 1u);
+        const unsigned add = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u;
+        __threadfence();
+        const unsigned old = atomicAdd(&g->count, add);
+        bool flipped = false;
+        for (uint32_t spins = 0;; ++spins) {
+            if ((old ^ *(volatile unsigned *)&g->count) & 0x80000000u) {
+                flipped = true;
+                break;
+            }
+            if ((spins & 255u) == 255u && (spins > kGridWaitLimit || *(volatile unsigned *)&g->err)) break;
+        }
+        if (!flipped) atomicOr(&g->err, 1u);
+        __threadfence();
+        res = flipped && !*(volatile unsigned *)&g->err;
+    }
+    __syncthreads();
+    return res != 0;
+}
+
+// One linear layer on the CUDA-core GEMV: the same rows, the same per-row
+// arithmetic as k_qgemv; a block stages X once and takes row blocks rb =
+// blockIdx.x, + gridDim.x, ..
+__device__ void fused_gemv(const QmmArgs &a, float *xs) {
+    const int warps = kFusedThreads / 32;
+    const int rows_per_block = warps * (32 / qgemv_lanes_per_row(a.K));
+    const int nrb = (a.N + rows_per_block - 1) / rows_per_block;
+    if ((int)blockIdx.x >= nrb) return;
+    qgemv_stage_x(a, xs, kFusedThreads);
+    __syncthreads();
+    for (int rb = blockIdx.x; rb < nrb; rb += gridDim.x) {
+        if (a.M <= 1) qgemv_rows<1>(a, xs, rb, warps, threadIdx.x >> 5);
+        else qgemv_rows<4>(a, xs, rb, warps, threadIdx.x >> 5);  // the fused step takes <= 4 streams
+    }
+    __syncthreads();
+}
+
+__device__ QmmArgs fused_lin(const float *X, int64_t ldx, int M, const altxs_qmat &W, int row0, int N, int K, float *Y,
+                             int64_t ldy, int epi) {
+    QmmArgs a{};
+    a.X = X;
+    a.ldx = ldx;
+    a.M = M;
+    a.W = W;
+    a.row0 = row0;
+    a.N = N;
+    a.K = K;
+    a.Y = Y;
+    a.ldy = ldy;
+    a.epi = epi;
+    return a;
+}
+
+template <int LPK, int G>
+__global__ void __launch_bounds__(kFusedThreads, 1) k_step_fused(StepCtx c, FusedProg fp) {
+    constexpr uint32_t kChunkBytes = (uint32_t)kRingChunk * 3 * (LPK * 8);
+    extern __shared__ __align__(128) unsigned char fsm[];
+    __shared__ __align__(8) uint64_t fbars[kFusedAttnWarps * kFusedAttnSlots];
+    const Dims &D = c.D;
+    const int nb = gridDim.x, w = threadIdx.x >> 5;
+    float *xs = reinterpret_cast<float *>(fsm);
+    int ok = 1;
+#define ALTXS_FUSED_SYNC()                                                              \
+    do {                                                                                \
+        if (!grid_sync(fp.sync, ok)) {                                                  \
+            if (blockIdx.x == 0 && c.b.ac)                                              \
+                for (int i_ = threadIdx.x; i_ < D.n; i_ += blockDim.x)                  \
+                    atomicOr(&c.b.ac[i_].status, ALTXS_ST_TIMEOUT);                     \
+            return;                                                                     \
+        }                                                                               \
+    } while (0)
+#define ALTXS_FUSED_ITEMS(cnt, ...)                                        \
+    do {                                                                   \
+        for (int it = blockIdx.x; it < (cnt); it += nb) {                  \
+            __VA_ARGS__;                                                   \
+            __syncthreads();                                               \
+        }                                                                  \
+    } while (0)
+
+    ALTXS_FUSED_ITEMS(D.n, embed_body(c, it, 128));
+    ALTXS_FUSED_SYNC();
+    bool lanes_on = false;
+    for (int v = 0; v < D.Lv; ++v) {
+        const int l = fp.sched[v];
+        LayerApp app{l, v, kAppPlain};
+        if (v >= D.enc && c.dsc.parallel_start > 0 && l >= c.dsc.parallel_start) {
+            app.mode = lanes_on ? kAppPar : kAppParFirst;
+            lanes_on = true;
+        }
+        const bool par = app.mode != kAppPlain;
+        ALTXS_FUSED_ITEMS(D.n, prenorm_body(c, app, it, 128));
+        ALTXS_FUSED_SYNC();
+        fused_gemv(fused_lin(c.nrm, D.d, D.n, c.w.qkv, l * D.qkv_n, D.qkv_n, D.d, c.qkv, D.qkv_n, kEpiStore), xs);
+        ALTXS_FUSED_SYNC();
+        ALTXS_FUSED_ITEMS(D.n, qkv_post_body(c, app, it));
+        fence_proxy_async_global();  // the new K/V rows, read next by TMA bulk copies on other SMs
+        ALTXS_FUSED_SYNC();
+        fence_proxy_async_global();
+        if (w < kFusedAttnWarps)
+            ok &= attn_ring_warp<LPK, G, true>(c, v, D.n * D.Hkv * D.nsplit, kFusedAttnSlots,
+                                               blockIdx.x * kFusedAttnWarps + w, nb * kFusedAttnWarps,
+                                               fsm + (int64_t)w * kFusedAttnSlots * 2 * kChunkBytes,
+                                               fbars + w * kFusedAttnSlots)
+                      ? 1
+                      : 0;
+        ALTXS_FUSED_SYNC();
+        ALTXS_FUSED_ITEMS(D.n * D.H, merge_body(c, l, it, D.hd));
+        ALTXS_FUSED_SYNC();
+        fused_gemv(fused_lin(c.y, D.d, D.n, c.w.o, l * D.d, D.d, D.d, c.ao, D.d, kEpiStore), xs);
+        ALTXS_FUSED_SYNC();
+        if (!par) {
+            ALTXS_FUSED_ITEMS(D.n, post_attn_body(c, l, v, it, 128));
+            ALTXS_FUSED_SYNC();
+        }
+        fused_gemv(fused_lin(c.nrm2, D.d, D.n, c.w.up, l * D.F, D.F, D.d, c.hid, D.F, kEpiLeaky2), xs);
+        ALTXS_FUSED_SYNC();
+        const int skip_slot = v - (D.enc - D.nskip);
+        float *skip_out = v < D.enc && skip_slot >= 0 ? c.skip + (int64_t)skip_slot * D.n * D.d : nullptr;
+        const bool mres = !par && D.mlora && c.b.lora;
+        QmmArgs dn = fused_lin(c.hid, D.F, D.n, c.w.down, l * D.d, D.d, D.F, par || mres ? c.mo : c.x, D.d,
+                               par || mres ? kEpiStore : kEpiResid);
+        if (!(par || mres)) {
+            dn.R = c.x;
+            dn.ldr = D.d;
+            dn.colscale = c.w.mlp_scale + (int64_t)l * D.d;
+            dn.Y2 = skip_out;
+            dn.ldy2 = D.d;
+        }
+        fused_gemv(dn, xs);
+        ALTXS_FUSED_SYNC();
+        if (par) {
+            ALTXS_FUSED_ITEMS(D.n, par_combine_body(c, l, v, it, 128));
+            ALTXS_FUSED_SYNC();
+        }
+        if (mres) {
+            ALTXS_FUSED_ITEMS(D.n, mlp_resid_body(c, l, v, skip_out, it, 128));
+            ALTXS_FUSED_SYNC();
+        }
+    }
+    const int lanes = lanes_on ? c.dsc.parallel_final : -1;
+    ALTXS_FUSED_ITEMS(D.n, final_body(c, lanes, it, 128));
+    ALTXS_FUSED_SYNC();
+    fused_gemv(fused_lin(c.nrm, D.d, D.n, c.w.emb, 0, D.V, D.d, c.logits, D.V, kEpiStore), xs);
+    ALTXS_FUSED_SYNC();
+    ALTXS_FUSED_ITEMS(D.n, cdf_code_body(c, fp.mode, it));
+#undef ALTXS_FUSED_SYNC
+#undef ALTXS_FUSED_ITEMS
+}
+
+// Dynamic shared memory of the fused step: the largest phase (the attention
+// slots of kFusedAttnWarps warps, the CDF row, a staged GEMV input, the
+// qkv_post row).
+inline size_t fused_smem(const Dims &D) {
+    size_t s = (size_t)kFusedAttnWarps * kFusedAttnSlots * 2 * kRingChunk * 3 * D.hd;
+    auto mx = [&](size_t v) { s = v > s ? v : s; };
+    mx((size_t)D.V * 4);
+    mx((size_t)D.n * (D.F + D.F / 64) * 4);
+    mx((size_t)D.n * (D.d + D.d / 64) * 4);
+    mx(((size_t)D.qkv_n + 3 * (D.r > 0 ? D.r : 1) + D.d) * 4);
+    mx((size_t)2 * (D.r > 0 ? D.r : 1) * 4);
+    return s;
+}
+
+// altxs_set_step_fusion; off by default: on a B200 the 33M single-stream step
+// measured 0.75 ms fused against 0.56 ms for the CUDA-graph replay of the
+// launch-per-phase step (each phase costs inside the kernel what it costs as
+// its own launch, and the grid barrier eats the launch gap it saves)
+int g_fused_max_streams = 0;
+
+template <int LPK, int G>
+int launch_fused_t(const StepCtx &c, const FusedProg &fp, cudaStream_t st) {
+    static int blocks[64] = {};
+    static size_t smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return ALTXS_ENOTSUP;
+    const size_t smem = fused_smem(c.D);
+    if (smem_set[dev] < smem) {
+        if (cudaFuncSetAttribute(k_step_fused<LPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return ALTXS_ENOTSUP;
+        smem_set[dev] = smem;
+        int per_sm = 0, sms = 0, coop = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_fused<LPK, G>, kFusedThreads, smem) !=
+            cudaSuccess)
+            return ALTXS_ENOTSUP;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+        blocks[dev] = coop && per_sm > 0 ? sms : 0;  // one block per SM: all co-resident
+    }
+    if (blocks[dev] <= 0) return ALTXS_ENOTSUP;
+    cudaMemsetAsync(fp.sync, 0, sizeof(GridSync), st);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(blocks[dev]);
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaSuccess;
+    ALTXS_LAUNCH(::altxs::kKFused, st, e = cudaLaunchKernelEx(&cfg, k_step_fused<LPK, G>, c, fp));
+    return e == cudaSuccess ? ALTXS_OK : ALTXS_ECUDA;
+}
+
+// ENOTSUP: not a shape the fused step covers (the caller launches the phases one by one)
+int launch_fused(const StepCtx &c, const altxs_model_desc *desc, int mode, GridSync *sync, cudaStream_t st) {
+    const Dims &D = c.D;
+    if (c.tc || D.n < 1 || D.n > g_fused_max_streams || D.n > 4 || D.Lv > kFusedMaxApps) return ALTXS_ENOTSUP;
+    FusedProg fp{};
+    fp.sync = sync;
+    fp.mode = mode;
+    for (int v = 0; v < D.Lv; ++v) fp.sched[v] = desc->schedule ? desc->schedule[v] : v;
+    const int G = D.H / D.Hkv;
+    if (D.hd == 64 && G == 1) return launch_fused_t<8, 1>(c, fp, st);
+    if (D.hd == 64 && G == 2) return launch_fused_t<8, 2>(c, fp, st);
+    if (D.hd == 32 && G == 1) return launch_fused_t<4, 1>(c, fp, st);
+    if (D.hd == 32 && G == 2) return launch_fused_t<4, 2>(c, fp, st);
+    return ALTXS_ENOTSUP;
+}
 
 // ---------------------------------------------------------------------------
 
@@ -894,6 +1203,7 @@ inline int64_t ws_size(const Dims &D) {
     if (D.par) s += A((int64_t)D.n * D.d);            // lane 1
     if (D.par || D.mlora) s += A((int64_t)D.n * D.d);  // MLP output
     if (D.mlora) s += A((int64_t)D.n * D.r);          // MLP adapter t
+    s += 256;                                         // grid barrier words of the fused step
     return s;
 }
 
@@ -955,6 +1265,12 @@ int altxs_set_wait_limit(uint32_t limit) {
 }
 
 uint32_t altxs_default_wait_limit(void) { return altxs::kWaitLimit; }
+
+int altxs_set_step_fusion(int max_streams) {
+    if (max_streams < 0) return ALTXS_EINVAL;
+    g_fused_max_streams = max_streams;
+    return ALTXS_OK;
+}
 
 int64_t altxs_workspace_bytes(const altxs_model_desc *desc, int n_streams) {
     Dims D{};
@@ -1031,11 +1347,18 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     if (D.par) c.lane1 = take((int64_t)D.n * D.d);
     if (D.par || D.mlora) c.mo = take((int64_t)D.n * D.d);
     if (D.mlora) c.lt2 = take((int64_t)D.n * D.r);
+    GridSync *gsync = reinterpret_cast<GridSync *>(p);
+    p += 256;
     const altxs_split_planes *sp = w->split;
     c.tc = sp != nullptr;
     if (sp && (!sp->emb_hi || !sp->emb_lo || !sp->qkv_hi || !sp->qkv_lo || !sp->o_hi || !sp->o_lo || !sp->up_hi ||
                !sp->up_lo || !sp->down_hi || !sp->down_lo))
         return ALTXS_EINVAL;
+    // a few streams on the CUDA-core path: the whole step as one fused launch
+    if (!c.tc) {
+        rc = launch_fused(c, desc, mode, gsync, st);
+        if (rc != ALTXS_ENOTSUP) return rc;
+    }
     // one linear layer: tensor cores from the bf16 planes, or CUDA cores from the packed codes
     auto linear = [&](const QmmArgs &q, const uint16_t *xh, const uint16_t *xl, const uint16_t *wh, const uint16_t *wl,
                       uint16_t *ph, uint16_t *pl) -> int {

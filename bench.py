@@ -64,6 +64,9 @@ def parse_args():
     ap.add_argument("--cuda-cores", action="store_true",
                     help="run the step's linear layers on CUDA cores from the packed codes (the few-stream "
                          "choice: 0.43 bytes per weight read per step instead of the 4-byte tensor-core planes)")
+    ap.add_argument("--fusion", action="store_true",
+                    help="with --cuda-cores and at most 4 streams per GPU: run each step as one fused "
+                         "persistent kernel instead of a kernel per phase (same bits; measured slower)")
     ap.add_argument("--replenish", action="store_true",
                     help="instead of the decode benchmark: one full-parameter replenish boundary of the 33M "
                          "model (Forward-XM: gradient of every weight over an 18,432-token window, AdamW, "
@@ -347,12 +350,14 @@ def run_replenish(args) -> None:
     }), flush=True)
 
 
-def config_block(world: int, streams: int, cuda_cores: bool = False) -> dict:
+def config_block(world: int, streams: int, cuda_cores: bool = False, fusion: bool = False) -> dict:
     return {
         "workload": f"{'box-scale sharded' if streams > 1 else 'single-stream'} decode: {streams} independent "
                     f"stream(s) split over N GPUs, 33M model (8L/512d/8h, MLP 2048, V 16384) at mixed 2/3/4-bit "
                     f"3.15 bpw, ctx 2048 window full",
         "linear": "CUDA cores from the packed codes" if cuda_cores else "tensor cores (hi/lo bf16 planes)",
+        "step": ("one fused persistent kernel per step" if cuda_cores and fusion and -(-streams // world) <= 4
+                 else "one kernel per phase (CUDA-graph replay)"),
         "global_streams": streams,
         "streams_per_gpu": streams // max(1, world),
         "ctx": 2048,
@@ -420,6 +425,8 @@ def main():
     every = cfg.online_retrain_every
     w = C.synth_weights(cfg, seed=WEIGHT_SEED)
     dm = DeviceModel(w, dev, rope_positions=cfg.ctx + chunk + 8, tensor_cores=not args.cuda_cores)
+    if args.fusion:
+        _lib.check(_lib.lib().altxs_set_step_fusion(4), "altxs_set_step_fusion")
     gids = np.arange(rank * n_local, (rank + 1) * n_local)
     data = zipf_markov(cfg.ctx + chunk, cfg.vocab_size, 1000 + gids)  # [n][T]
     symsT = torch.from_numpy(np.ascontiguousarray(data.T)).to(dev)     # [T][n]
@@ -685,7 +692,7 @@ def main():
         "vs_baseline": None,
         "dtype": "f32 math; weights 2/3/4-bit + fp16 scales; KV 24-bit",
         "data": "synthetic: seeded Zipf-Markov streams (alpha 1.1), seeded random mixed-bit weights",
-        "config": config_block(world, n_global, args.cuda_cores),
+        "config": config_block(world, n_global, args.cuda_cores, args.fusion),
         "bits_per_symbol": bits_total / (n_local * chunk),
         "roundtrip_ok": bool(ok and ok_e2e),
         "ttt_updates_timed": timed_boundaries,

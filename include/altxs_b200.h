@@ -466,6 +466,18 @@ void altxs_destroy(altxs_ctx *ctx);
 int altxs_set_wait_limit(uint32_t limit);
 uint32_t altxs_default_wait_limit(void);
 
+/* ---- fused step -------------------------------------------------------------
+ * Counterpart of the reference's W=1 fused paths (persistent_step.py,
+ * mega_step.py) for a few streams: on the CUDA-core path (weights->split
+ * NULL) with 1 <= n_streams <= max_streams (at most 4), head_dim 32 or 64 and
+ * n_heads/n_kv_heads 1 or 2, altxs_step runs the whole step as one persistent
+ * cooperative kernel: the same phases and arithmetic as the launch-per-phase
+ * step, so results are bit-identical, with a grid-wide barrier (bounded wait,
+ * ALTXS_ST_TIMEOUT on giving up) instead of each launch.  Off by default
+ * (max_streams 0): measured slower than the CUDA-graph replay of the
+ * launch-per-phase step on a B200.  Process-wide. */
+int altxs_set_step_fusion(int max_streams);
+
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these
  * give the benchmark per-kernel device time measured live on the launch
