@@ -96,8 +96,8 @@ class ModelConfig:
     ttt_burst_beta2: float = 0.999
     ttt_burst_weight_decay: float = 0.01
     # reference model motifs (model.py:982-1110; all off = the plain GPT).  The
-    # step, the oracle and the full-parameter updates (replenish, full) run
-    # them; the test-time LoRA update covers the plain GPT only.
+    # step, the oracle, every test-time update (lora, replenish, full) and the
+    # segment-reset prefill run them.
     smear_gate_enabled: bool = False      # previous-token smear on the raw embedding
     gate_window: int = 12                 # input width of the smear / attention gates
     xsa_last_n: int = 0                   # XSA (value-direction removal) on the last n layers

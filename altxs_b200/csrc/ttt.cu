@@ -1,13 +1,17 @@
-// Test-time LoRA update of one stream over its last window (sm_100a).
+// Test-time updates of one stream over a window (sm_100a): the LoRA update,
+// the full-parameter gradient of replenish / "full", and the context prefill.
 //
 // Restates the reference online update in lora mode (altxs
-// src/xsa_ttt/compress.py:1104-1137 with ttt_lora.py:124-179, 258-374):
+// src/xsa_ttt/compress.py:1104-1137 with ttt_lora.py:124-250, 258-374):
 // teacher-forced forward over x = window[0..T), targets window[1..T] with
 // positions 0..T-1 and causal attention, LoRA deltas (x A^T B^T) * alpha/r on
-// q/k/v/o (o on the block's normed input) and on the tied LM head, tanh
-// softcap, mean cross-entropy; backward into the adapters only (frozen
-// mixed-bit base); global-norm clip; AdamW step.  Every reduction runs in a
-// fixed order (no atomics), so encoder and decoder compute identical updates.
+// q/k/v/o/MLP (o on the block's normed input or on y) per layer application
+// and on the tied LM head, softcap, mean cross-entropy; backward into the
+// adapters only (frozen mixed-bit base); global-norm clip; AdamW step.  The
+// full-parameter gradient (compress.py:611-1146) trains every parameter of the
+// same forward.  The reference motifs (model.py:760-868, 1293-1500) run in
+// both.  Every reduction runs in a fixed order (no atomics), so encoder and
+// decoder compute identical updates.
 #include <math.h>
 
 #include "gemm.cuh"
