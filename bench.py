@@ -53,7 +53,9 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--impl", choices=("b200", "reference", "reference-triton"), default="b200")
+    ap.add_argument("--ref-symbols", type=int, default=REF_TRITON_SYMBOLS,
+                    help="stream length of the reference-triton arm")
     ap.add_argument("--streams", type=int, default=GLOBAL_STREAMS, help="global stream count")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -181,6 +183,131 @@ def run_reference(args, rank, world):
         "e2e": {"value": value, "unit": "sym/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "bits_per_symbol": res["bits_per_symbol"],
         "wall_s": time.perf_counter() - t0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+REF_INSTALL = ROOT / "baseline" / "_ref"
+REF_TRITON_SYMBOLS = 4096
+
+
+def _ref_xsa_config(cfg, XsaTttConfig):
+    """The reference's config for the same model: plain GPT, every motif off,
+    tied embeddings (src/xsa_ttt/config.py field names)."""
+    h = XsaTttConfig(seed=cfg.seed)
+    for k in ("vocab_size", "num_layers", "model_dim", "num_heads", "num_kv_heads", "mlp_mult",
+              "rope_base", "rope_dims", "qk_gain_init", "logit_softcap", "ln_scale",
+              "skip_gates_enabled", "block_size", "online_retrain_every", "grad_clip"):
+        setattr(h, k, getattr(cfg, k))
+    for k in ("xsa_last_n", "num_loops", "parallel_start_layer"):
+        setattr(h, k, 0)
+    for k in ("smear_gate_enabled", "sparse_attn_gate_enabled", "attn_out_gate_enabled",
+              "gated_attn_enabled", "asym_logit_rescale", "rope_yarn", "gradient_checkpointing"):
+        setattr(h, k, False)
+    h.tie_embeddings = True
+    return h
+
+
+def run_reference_triton(args, rank, world):
+    """The reference's own GPU decode on one B200, through its public entry
+    points from the offline install in baseline/_ref: the 33M model (dense
+    fp32 copy of the same seeded mixed-bit weights), one stream of
+    REF_TRITON_SYMBOLS Zipf-Markov symbols encoded with
+    ``compress_full_sha_incremental`` and decoded with
+    ``decompress_full_sha_incremental`` (src/xsa_ttt/incremental.py:1561,
+    :1799) in its stock GPU configuration (Triton fused step, GPU range
+    coder, CUDA graphs).  The reference's context
+    grows within a segment, so positions 0..4095 attend on average 2048 keys,
+    the bench's window.  Updates are off (the reference's lockstep update
+    would only lower its rate).  Each step is one full decode call, timed with
+    a device synchronize on both sides; the first decode call (Triton
+    compilation, graph capture) is a warm-up.  The reference's window switch
+    is set to one symbol (``XSA_AC_WINDOW=1``, unless the caller sets it):
+    decode steps one row either way, and with it the encoder runs the
+    decoder's exact op sequence, so the round trip holds (with 64-symbol
+    encode windows the reference's encoder and decoder part within a few
+    symbols on this model).  A failure inside the reference prints an
+    ``unavailable`` line with the error."""
+    if rank != 0:
+        return
+    os.environ.setdefault("XSA_AC_WINDOW", "1")
+    try:
+        _run_reference_triton(args)
+    except Exception as e:  # the reference's own code failed on this box
+        print(json.dumps({"impl": "reference-triton",
+                          "unavailable": f"reference GPU decode failed: {type(e).__name__}: {e}"[:400]}))
+
+
+def _run_reference_triton(args):
+    if not (REF_INSTALL / "xsa_ttt").is_dir():
+        print(json.dumps({"impl": "reference-triton", "unavailable": "baseline/_ref is not installed"}))
+        return
+    for p in (REF_INSTALL, REF_INSTALL / "model"):
+        sys.path.insert(0, str(p))
+    from xsa_ttt.config import XsaTttConfig
+    from xsa_ttt.incremental import compress_full_sha_incremental, decompress_full_sha_incremental
+    from xsa_ttt.model import GPT
+
+    from altxs_b200 import codec as C
+    from altxs_b200.config import c3_config
+    from altxs_b200.synth import zipf_markov
+
+    cfg = c3_config()
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    n_sym = args.ref_symbols
+    w = C.synth_weights(cfg, seed=WEIGHT_SEED)
+    h = _ref_xsa_config(cfg, XsaTttConfig)
+    torch.manual_seed(0)
+    model = GPT(h)
+    sd = model.state_dict()
+    for k, v in w.dense().items():
+        sd[k] = torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32))
+    model.load_state_dict(sd, strict=True)
+    model = model.to(dev).eval()
+    data = zipf_markov(n_sym, cfg.vocab_size, np.array([1000]))[0].astype(np.uint16)
+
+    def sync():
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+
+    t0 = time.perf_counter()
+    enc = compress_full_sha_incremental(model, data, cfg=h, device=dev, online_retrain_enabled=False,
+                                        progress=False)
+    sync()
+    enc_s = time.perf_counter() - t0
+    times, ok = [], True
+    for i in range(max(1, args.warmup) + max(1, min(args.steps, 3))):
+        sync()
+        t1 = time.perf_counter()
+        dec = decompress_full_sha_incremental(model, enc["payload"], n_sym, cfg=h, device=dev,
+                                              online_retrain_enabled=False, progress=False)
+        sync()
+        if i >= max(1, args.warmup):
+            times.append(time.perf_counter() - t1)
+        ok = ok and bool(dec.get("decoded_sha256") == enc.get("sha256"))
+    s = float(statistics.median(times))
+    value = n_sym / s
+    line = {
+        "impl": "reference-triton",
+        "metric": METRIC,
+        "value": value,
+        "unit": "sym/s",
+        "n_gpus": 1,
+        "steps": len(times),
+        "warmup": max(1, args.warmup),
+        "ms_per_step": 1000.0 * s,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16/f32 (reference stock)",
+        "data": "synthetic Zipf-Markov (alpha 1.1), dense copy of the seeded random mixed-bit weights",
+        "config": {"workload": f"reference stock GPU decode, 1 stream x {n_sym} symbols, 33M model, "
+                               "context grows 0..n (mean 2048 at 4096), updates off, XSA_AC_WINDOW="
+                               + os.environ.get("XSA_AC_WINDOW", ""),
+                   "streams": 1, "symbols": n_sym, "device": str(dev)},
+        "encode_s": enc_s,
+        "bits_per_symbol": 8.0 * float(enc["payload_bytes"]) / n_sym,
+        "roundtrip_ok": ok,
     }
     print(json.dumps(line), flush=True)
 
@@ -399,6 +526,9 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.impl == "reference-triton":
+        run_reference_triton(args, rank, world)
         return
     import ctypes
 
