@@ -22,7 +22,11 @@ inputs from HBM.  The per-kernel breakdown and the attention roofline come
 from re-running the same K steps launch by launch with CUDA events around
 every launch.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference|reference-triton]
+
+--impl reference times the CPU port of the reference's eager decode on the host
+cores; --impl reference-triton times the reference's own GPU decode (its Triton
+megakernel and GPU coder, from the offline install in baseline/_ref) on one GPU.
 """
 
 from __future__ import annotations
