@@ -12,6 +12,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -40,15 +41,29 @@ def nvcc() -> str:
     return cand
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> Path:
+    """Compile each ``csrc/*.cu`` to an object in parallel, then link the .so."""
     if not force and not _stale():
         return LIB
+    obj_dir = HERE / "_build"
+    obj_dir.mkdir(exist_ok=True)
+    compile_flags = [f for f in FLAGS if f != "-shared"]
+    cmds = []
+    for src in sources():
+        cmd = [nvcc(), *ARCH, *compile_flags, "-c", "-o", str(obj_dir / (src.stem + ".o")), str(src)]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd), file=sys.stderr)
+        cmds.append(cmd)
+    jobs = jobs or max(1, min(len(cmds), os.cpu_count() or 1))
+    with ThreadPoolExecutor(jobs) as ex:
+        procs = list(ex.map(lambda c: subprocess.run(c, cwd=str(CSRC)), cmds))
+    bad = [c[-1] for c, p in zip(cmds, procs) if p.returncode]
+    if bad:
+        raise RuntimeError(f"nvcc failed on {', '.join(bad)}")
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-o", str(tmp), *map(str, sources())]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True, cwd=str(CSRC))
+    objs = [str(obj_dir / (src.stem + ".o")) for src in sources()]
+    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs], check=True, cwd=str(CSRC))
     os.replace(tmp, LIB)
     return LIB
 

@@ -1133,29 +1133,37 @@ int g_fused_max_streams = 0;
 
 template <int LPK, int G>
 int launch_fused_t(const StepCtx &c, const FusedProg &fp, cudaStream_t st) {
+    // per-device launch shape, set up once per (device, shared-memory size);
+    // the lock keeps a second host thread from reading a half-written entry
+    static std::mutex mu;
     static int blocks[64] = {};
     static size_t smem_set[64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
+    if (cudaGetDevice(&dev) != cudaSuccess) return ALTXS_ECUDA;
     if (dev < 0 || dev >= 64) return ALTXS_ENOTSUP;
     const size_t smem = fused_smem(c.D);
-    if (smem_set[dev] < smem) {
-        if (cudaFuncSetAttribute(k_step_fused<LPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-            return ALTXS_ENOTSUP;
-        smem_set[dev] = smem;
-        int per_sm = 0, sms = 0, coop = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_fused<LPK, G>, kFusedThreads, smem) !=
-            cudaSuccess)
-            return ALTXS_ENOTSUP;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
-        blocks[dev] = coop && per_sm > 0 ? sms : 0;  // one block per SM: all co-resident
+    int nblk = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (smem_set[dev] < smem) {
+            if (cudaFuncSetAttribute(k_step_fused<LPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem) != cudaSuccess)
+                return ALTXS_ENOTSUP;
+            int per_sm = 0, sms = 0, coop = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_fused<LPK, G>, kFusedThreads, smem) !=
+                cudaSuccess)
+                return ALTXS_ENOTSUP;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+            blocks[dev] = coop && per_sm > 0 ? sms : 0;  // one block per SM: all co-resident
+            smem_set[dev] = smem;
+        }
+        nblk = blocks[dev];
     }
-    if (blocks[dev] <= 0) return ALTXS_ENOTSUP;
-    cudaMemsetAsync(fp.sync, 0, sizeof(GridSync), st);
+    if (nblk <= 0) return ALTXS_ENOTSUP;
+    if (cudaMemsetAsync(fp.sync, 0, sizeof(GridSync), st) != cudaSuccess) return ALTXS_ECUDA;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(blocks[dev]);
+    cfg.gridDim = dim3(nblk);
     cfg.blockDim = dim3(kFusedThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;

@@ -241,7 +241,10 @@ typedef struct altxs_batch {
  * Batches whose scratch would exceed it return ALTXS_ENOSPC (at the 33M
  * shapes, 133 streams fit).  The first call on a device resolves the
  * array's device address with that device current; make that first call
- * before any stream capture.  All calls share the array: calls that overlap
+ * before any stream capture.  The address is kept for the life of the
+ * process, so do not call this entry point again on a device after
+ * cudaDeviceReset (the library's device image, and with it the array, is
+ * reloaded at a new address).  All calls share the array: calls that overlap
  * on one GPU race, so issue them one after another.  Nothing in the scratch
  * needs to start at zero. */
 int altxs_step_noalloc(const altxs_model_desc *desc, const altxs_weights *w, const altxs_batch *b, int mode,
