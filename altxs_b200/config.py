@@ -259,11 +259,14 @@ class ModelConfig:
 
 
 def c1_config() -> ModelConfig:
-    """CPU plumbing config: 2L/128d/4h, ctx 256, V 4096, rank-4 q/v LoRA."""
+    """CPU plumbing config: 2L/128d/4h, ctx 256, V 4096, rank-4 q/v LoRA
+    (plus the lm_head adapter) updated every 4096 symbols at lr 1e-3, 16-bit
+    CDF precision.  Its weights are the reference's seed-0 init
+    (``codec.reference_init(cfg, 0)``)."""
     return ModelConfig(
         vocab_size=4096, num_layers=2, model_dim=128, num_heads=4, num_kv_heads=4,
         mlp_mult=4.0, block_size=256, online_retrain_every=4096, seed=0,
-        ttt_lora_rank=4, ttt_lora_lr=1e-3, ttt_k_lora=False, ttt_o_lora=False,
+        ttt_lora_rank=4, ttt_lora_lr=1e-3, ttt_k_lora=False, ttt_o_lora=False, cdf_bits=16,
     )
 
 

@@ -566,18 +566,21 @@ class ContextReset:
 class Engine:
     """Encode / decode many independent streams in lockstep on one GPU."""
 
-    def __init__(self, dm: DeviceModel, *, ttt=None):
+    def __init__(self, dm: DeviceModel, *, ttt=None, on_logits=None):
         self.dm = dm
         self.cfg = dm.cfg
         self.ttt = ttt  # optional callable(batch, rows, hist_end) for the boundary update
         self.reset = ContextReset(dm) if dm.cfg.context_mode == "reset" else None
+        # optional callable(t, logits [n, V] on the device) after each encode step:
+        # the logits every stream's symbol t was coded with (before the CDF rule)
+        self.on_logits = on_logits
 
     def _new_batch(self, n: int, max_len: int) -> StreamBatch:
         cfg = self.cfg
         self.dm.ensure_rope(max_len + 2)
         hist = cfg.ctx + 2 if (self.ttt is not None or self.reset is not None) else 0
         return StreamBatch(self.dm, n, words_per_stream=words_for_segment(cfg.online_retrain_every, cfg.cdf_bits),
-                           hist_len=hist)
+                           hist_len=hist, keep_logits=self.on_logits is not None)
 
     def _per_stream(self) -> bool:
         """A full-parameter update changes the model itself: one stream at a time."""
@@ -621,6 +624,8 @@ class Engine:
                 b.set_active(active)
             b.sym.copy_(symsT_d[t])
             b.step(_lib.STEP_ENCODE)
+            if self.on_logits is not None:
+                self.on_logits(t, b.logits)
         rows = [i for i in range(n) if lens[i] > 0]
         if rows:
             b.set_active(None)

@@ -148,44 +148,50 @@ class ClockSampler:
         }
 
 
+def cpu_parallel(args, stream_seeds, n_symbols: int, target_s: float) -> dict:
+    """Aggregate CPU decode rate over the host cores (one single-threaded
+    process per core, each decoding whole streams of the benchmark workload):
+    the reference's own eager CPU path from the offline install when it is
+    there, else the port under oracle/."""
+    from altxs_b200.config import c3_config
+    from oracle.baseline import parallel_decode_baseline
+
+    ref_root = str(REF_INSTALL) if (REF_INSTALL / "xsa_ttt").is_dir() else None
+    return parallel_decode_baseline(weight_seed=WEIGHT_SEED, stream_seeds=stream_seeds, start=c3_config().ctx,
+                                    n_symbols=n_symbols, target_s=target_s, ref_root=ref_root,
+                                    repo_root=str(ROOT))
+
+
 def run_reference(args, rank, world):
-    """CPU reference arm: the reference's eager decode path (oracle port)."""
+    """CPU reference arm: the reference's eager decode on every host core
+    (one process per core, each decoding its own streams of the workload:
+    window full, the chunk of W + K symbols each stream decodes in the GPU
+    arm).  Rank 0 runs it; other ranks exit."""
     if rank != 0:
         return
-    from altxs_b200 import codec as C
-    from altxs_b200.config import c3_config
-    from oracle.baseline import cpu_decode_baseline
-
-    cfg = c3_config()
-    w = C.synth_weights(cfg, seed=WEIGHT_SEED)
-    per_step = []
-    for _ in range(max(1, args.warmup)):
-        cpu_decode_baseline(w, target_s=min(2.0, args.cpu_seconds), seed=1)
     t0 = time.perf_counter()
-    res = None
-    for k in range(max(1, min(args.steps, 3))):
-        res = cpu_decode_baseline(w, target_s=args.cpu_seconds, seed=1 + k)
-        per_step.append(res["value"])
-    value = float(statistics.median(per_step))
+    chunk = max(3, args.warmup) + max(1, args.steps)
+    res = cpu_parallel(args, list(range(1000, 1000 + args.streams)), chunk, args.cpu_seconds)
+    value = float(res["value"])
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": "sym/s",
         "n_gpus": world,
-        "steps": len(per_step),
-        "warmup": args.warmup,
-        "ms_per_step": 1000.0 / value,
+        "steps": max(1, args.steps),
+        "warmup": max(3, args.warmup),
+        "ms_per_step": 1000.0 * res["cores"] / value,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic Zipf-Markov (alpha 1.1), seeded random mixed-bit weights",
         "config": config_block(world, args.streams, args.cuda_cores),
-        "cpu_baseline": {"value": value, "unit": "sym/s", "cores": res["cores"], "kind": res["kind"],
-                         "sample": res["sample"]},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": value, "unit": "sym/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "bits_per_symbol": res["bits_per_symbol"],
+        "streams_decoded": len(res["stream_bytes"]),
         "wall_s": time.perf_counter() - t0,
     }
     print(json.dumps(line), flush=True)
@@ -806,12 +812,24 @@ def main():
                 "peak_source": f"{peak_kind} hbm_gbs",
                 "timing": "CUDA events around each attention launch on its stream, over the same K "
                           "steps re-run launch by launch after the graph-replayed timed pass"}
-    cpu = None
+    cpu = same = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from oracle.baseline import cpu_decode_baseline
-
-        r = cpu_decode_baseline(w, target_s=args.cpu_seconds, seed=1)
-        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        # the host cores decode some of this GPU's own streams (those without a
+        # segment boundary in the chunk: one segment each on both sides), so
+        # both bits/symbol figures below describe the same symbols
+        crossing = set(brows)
+        plain = [int(g) for g in gids if int(g) - rank * n_local not in crossing]
+        r = cpu_parallel(args, [1000 + g for g in plain], chunk, args.cpu_seconds)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "bits_per_symbol")}
+        done = [s - 1000 - rank * n_local for s in r["stream_bytes"]]
+        gpu_bytes = sum(len(p) for i in done for p in segs[i])
+        cpu_bytes = sum(r["stream_bytes"].values())
+        same = {"streams": len(done), "symbols": len(done) * chunk,
+                "gpu": 8.0 * gpu_bytes / (len(done) * chunk), "cpu": 8.0 * cpu_bytes / (len(done) * chunk),
+                "delta_pct": 100.0 * (gpu_bytes / cpu_bytes - 1.0),
+                "note": "GPU: this engine's fixed-point CDF rule, sliding window; CPU: the "
+                        + ("reference's masses and segment-reset context" if r["kind"] == "reference"
+                           else "port's CDF rule and sliding window")}
     h2d = int(stage_h.numel() * 4 + nbits_h.numel() * 8)
     line = {
         "metric": METRIC,
@@ -832,6 +850,7 @@ def main():
         "ttt_updates_timed": timed_boundaries,
         "roofline": roof,
         "cpu_baseline": cpu,
+        "bits_same_symbols": same,
         "e2e": {"value": n_global * chunk / (e2e_ms / 1000.0), "unit": "sym/s",
                 "h2d_bytes_per_step": h2d // chunk, "d2h_bytes_per_step": int(b.n * 4),
                 "path": "StreamBatch steps + LoraTTT with pinned host segments in, host symbols out"},

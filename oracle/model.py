@@ -122,6 +122,9 @@ class OracleModel:
         cfg = w.cfg
         self.cfg = cfg
         self.cos, self.sin = (torch.from_numpy(a) for a in rope_tables(cfg, 1 << 12))
+        # optional rounding of every stored K/V value (a callable on fp32
+        # tensors): emulates a KV-cache storage format in precision studies
+        self.kv_round = None
 
     def _tables(self, pos: torch.Tensor):
         need = int(pos.max()) + 1
@@ -153,6 +156,8 @@ class OracleModel:
         q = _rope(q, cos, sin, rd)
         k = _rope(k, cos, sin, rd)
         q = q * w.small["q_gain"][i][None, :, None]
+        if self.kv_round is not None:
+            k, v = self.kv_round(k), self.kv_round(v)
         v_new = v
         if kv_prefix is not None:
             pk, pv = kv_prefix

@@ -682,19 +682,147 @@ def gen_zipf() -> None:
     np.savez_compressed(HERE / "zipf_markov.npz", seeds=np.array([1, 2, 3]), streams=s)
 
 
+# positions whose reference probability rows the C1 fixture keeps (both
+# segment sides of several boundaries, the stream start and end)
+C1_ROWS = (1, 2, 3, 255, 256, 257, 4095, 4096, 4097, 4100, 8191, 8192, 8193, 20000, 32767, 32768,
+           32769, 61439, 61440, 61441, 65534, 65535)
+
+
+C1_BANKS = ("tok_emb.weight", "qo_bank", "kv_bank", "mlp_up_bank", "mlp_down_bank")
+
+
+def gen_c1_stream() -> None:
+    """BASELINE config C1 through the reference's own coder path.
+
+    Model: the reference ``GPT`` at the C1 shapes from ``torch.manual_seed(0)``
+    (its own random init).  Stream: 65,536 symbols of the order-2 Zipf-Markov
+    source, seed 1.  Run: ``compress_bytes`` (compress.py:1363) with rank-4
+    q/v LoRA, lr 1e-3, an update at every multiple of 4096 (``online_retrain``
+    lora branch), probability rows from the chunked teacher-forced forward
+    (``_chunk_tf_probs``: each segment with the previous block as context at
+    positions from 0), masses ``max(1, round(p*1e6))``.  Kept: bits/symbol,
+    payload size and hash, and the log-probability rows at ``C1_ROWS``."""
+    import time
+
+    import xsa_ttt.compress as rc
+
+    from altxs_b200.config import c1_config
+    from altxs_b200.synth import zipf_markov
+
+    cfg = c1_config()
+    h = ref_cfg(cfg)
+    torch.manual_seed(0)
+    m = GPT(h)
+    m.eval()
+    sd = {k: v.detach().float().numpy() for k, v in m.state_dict().items()}
+    mine = C.reference_init(cfg, 0)
+    for k in C1_BANKS:
+        assert np.array_equal(sd[k], mine[k]), k
+    wsha = hashlib.sha256()
+    for k in C1_BANKS:
+        wsha.update(np.ascontiguousarray(sd[k], dtype=np.float32).tobytes())
+    arr = zipf_markov(65536, cfg.vocab_size, [1])[0].astype(np.uint16)
+    cache: dict = {}
+    t0 = time.time()
+    res = rc.compress_bytes(m, arr, cfg=h, device=torch.device("cpu"), online_retrain_enabled=True,
+                            progress=False, prob_cache=cache)
+    t_enc = time.time() - t0
+    rows = []
+    for p in C1_ROWS:
+        st = (p // 4096) * 4096
+        r = cache[(st, min(65536, st + 4096))][p - st].astype(np.float64)
+        rows.append(np.log(np.maximum(r, 1e-45)))
+    out = dict(
+        stream_sha=np.frombuffer(hashlib.sha256(arr.astype("<u2").tobytes()).digest(), np.uint8),
+        bank_sha=np.frombuffer(wsha.digest(), np.uint8),
+        bits_per_symbol=np.float64(res["bits_per_symbol"]),
+        payload_bytes=np.int64(res["payload_bytes"]),
+        payload_sha=np.frombuffer(hashlib.sha256(res["payload"]).digest(), np.uint8),
+        retrain_count=np.int64(res["retrain_count"]),
+        chunk_bits=np.array([r["bpb"] for r in res["chunk_bpb_rows"]]),
+        row_pos=np.array(C1_ROWS, dtype=np.int64),
+        row_logp=np.stack(rows).astype(np.float32),
+    )
+    np.savez_compressed(HERE / "c1_stream.npz", **out)
+    print(f"c1: {res['bits_per_symbol']:.5f} bits/sym, {res['payload_bytes']} B, "
+          f"{res['retrain_count']} updates, encode {t_enc:.1f} s")
+
+
+def gen_incr_stream() -> None:
+    """Bits/symbol and probability rows of the reference's own incremental
+    entry point, ``compress_full_sha_incremental`` (incremental.py:1561), run
+    eagerly on the CPU (``XSA_AC_FUSED=0 XSA_AC_GPU_AC=0 XSA_AC_GRAPH=0``).
+
+    Same stream as C1 (65,536 Zipf-Markov symbols, seed 1) and the C1 shapes.
+    The weights are this framework's seeded mixed-bit synthetic model at those
+    shapes (seed 3; dense fp32 in the reference ``GPT``): the reference's own
+    seed-0 init has zero output and down projections and stays at log2(V)
+    bits under every update, which would not tell a right update from a wrong
+    one.  Two runs: no update (the reference engine's segment reset and
+    prefill alone), and ``retrain_mode="replenish"`` (its production update;
+    this entry point refuses LoRA, incremental.py:1553) with an update every
+    4096 symbols, 2 steps per boundary (replay on), lr 1e-3, no warmup.  Each
+    run keeps bits/symbol, payload size and hash, and the log-probabilities
+    the reference engine coded with at ``C1_ROWS`` (from its
+    ``_segment_rows_tf``, which runs ``reset_segment`` then the W-windows)."""
+    import time
+
+    os.environ.update(XSA_AC_FUSED="0", XSA_AC_GPU_AC="0", XSA_AC_GRAPH="0")
+    import xsa_ttt.incremental as inc
+
+    from altxs_b200.config import c1_config
+    from altxs_b200.synth import zipf_markov
+
+    cfg = c1_config()
+    arr = zipf_markov(65536, cfg.vocab_size, [1])[0].astype(np.uint16)
+    out = {"row_pos": np.array(C1_ROWS, dtype=np.int64)}
+    orig = inc._segment_rows_tf
+    for tag, online in (("none", False), ("replenish", True)):
+        w = C.synth_weights(cfg, seed=3)
+        m = ref_model(cfg, w)
+        h = m.cfg
+        h.retrain_mode = "replenish"
+        h.online_retrain_every = 4096
+        h.online_retrain_steps = 2
+        h.ttt_lora_lr = 1e-3
+        h.ttt_replenish_warmup_steps = 0
+        got: dict[int, np.ndarray] = {}
+
+        def rec(engine, a, seg, *, start):
+            rows = orig(engine, a, seg, start=start)
+            for p in C1_ROWS:
+                if start <= p < start + len(seg):
+                    got[p] = np.log(np.maximum(rows[p - start].astype(np.float64), 1e-45))
+            return rows
+
+        inc._segment_rows_tf = rec
+        try:
+            t0 = time.time()
+            res = inc.compress_full_sha_incremental(m, arr, cfg=h, device=torch.device("cpu"),
+                                                    online_retrain_enabled=online, progress=False)
+        finally:
+            inc._segment_rows_tf = orig
+        out[f"{tag}_bits_per_symbol"] = np.float64(res["bits_per_symbol"])
+        out[f"{tag}_payload_bytes"] = np.int64(res["payload_bytes"])
+        out[f"{tag}_payload_sha"] = np.frombuffer(hashlib.sha256(res["payload"]).digest(), np.uint8)
+        out[f"{tag}_retrain_count"] = np.int64(res["retrain_count"])
+        out[f"{tag}_segment_bits"] = np.array([r["bpb"] for r in res["chunk_bpb_rows"]])
+        out[f"{tag}_row_logp"] = np.stack([got[p] for p in C1_ROWS]).astype(np.float32)
+        print(f"incr {tag}: {res['bits_per_symbol']:.5f} bits/sym, {res['payload_bytes']} B, "
+              f"{res['retrain_count']} updates, {time.time() - t0:.1f} s")
+    np.savez_compressed(HERE / "incr_stream.npz", **out)
+
+
 if __name__ == "__main__":
-    gen_coder_probs()
-    gen_coder_cum()
-    print(gen_codec())
-    gen_model()
-    gen_lora()
-    gen_lora_steps()
-    gen_lora_defaults()
-    gen_model_motifs()
-    gen_replenish()
-    gen_full()
-    gen_motif_retrain()
-    gen_codec_ref()
-    gen_zipf()
+    GEN = [gen_coder_probs, gen_coder_cum, gen_codec, gen_model, gen_lora, gen_lora_steps, gen_lora_defaults,
+           gen_model_motifs, gen_replenish, gen_full, gen_motif_retrain, gen_codec_ref, gen_zipf, gen_c1_stream,
+           gen_incr_stream]
+    # no argument: every fixture; otherwise only the named generators (e.g. gen_c1_stream)
+    pick = sys.argv[1:]
+    for fn in GEN:
+        if not pick or fn.__name__ in pick:
+            r = fn()
+            if r is not None:
+                print(r)
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
         print(f.name, f.stat().st_size)

@@ -193,6 +193,31 @@ def test_c3_shape_step_runs_and_is_batch_independent():
     assert float(np.abs(one - ref).max()) < TOL
 
 
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_c3_full_window_logits_match_oracle(tensor_cores):
+    """The 33M model with the window full: 2100 symbols of one stream, so the
+    KV ring wraps and every fixed 256-key attention split is full; every
+    position from 2040 on against the fp32 oracle (one causal prefill of the
+    first 2040 symbols, then sliding-window steps), on both linear paths."""
+    from altxs_b200.engine import DeviceModel
+    from altxs_b200.synth import zipf_markov
+
+    cfg = c3_config()
+    w = C.synth_weights(cfg, seed=1)
+    T, first = 2100, 2040
+    toks = zipf_markov(T, cfg.vocab_size, [5])[0]
+    dm = DeviceModel(w, DEV, tensor_cores=tensor_cores)
+    got = _run_logits(dm, [toks[: T - 1]])[0]
+    om = OracleModel(OracleWeights.from_model_weights(w))
+    st = om.new_stream()
+    ref = [om.prefill(st, toks[:first]).numpy()]
+    for t in range(first, T - 1):
+        ref.append(om.step(st, int(toks[t])).numpy())
+    err = np.abs(got[first - 1:] - np.stack(ref)).max(axis=1)
+    print(f"33M full window, tensor_cores={tensor_cores}: max |logit - oracle| = {err.max():.2e}")
+    assert float(err.max()) < TOL
+
+
 def test_graph_replay_matches_launches():
     """StreamBatch(graphs=True) replays captured steps: same symbols, same bytes."""
     from altxs_b200 import _lib
