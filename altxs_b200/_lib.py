@@ -25,6 +25,8 @@ EXPORTS = (
     "altxs_launch_count", "altxs_profile", "altxs_profile_read", "altxs_version",
     "altxs_ttt_workspace_bytes", "altxs_ttt_update", "altxs_step_noalloc", "altxs_step_noalloc_max_bytes",
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
+    "altxs_linear_tc_workspace_bytes", "altxs_linear_tc", "altxs_set_lockstep", "altxs_lockstep_id",
+    "altxs_set_linear_packed",
     "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
     "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit", "altxs_set_step_fusion",
     "altxs_param_layout_of", "altxs_full_workspace_bytes", "altxs_full_loss_grad", "altxs_adamw",
@@ -79,7 +81,7 @@ class Weights(C.Structure):
         ("rope_positions", C.c_int64), ("split", C.POINTER(SplitPlanes)),
         ("smear_gate", C.c_void_p), ("smear_lambda", C.c_void_p), ("attn_gate_w", C.c_void_p),
         ("softcap", C.c_void_p), ("parallel_post", C.c_void_p), ("parallel_resid", C.c_void_p),
-        ("emb_dense", C.c_void_p),
+        ("emb_dense", C.c_void_p), ("planes_live", C.c_int32),
     ]
 
 
@@ -145,6 +147,7 @@ def lib():
             "altxs_set_wait_limit": (C.c_int, [C.c_uint32]),
             "altxs_default_wait_limit": (C.c_uint32, []),
             "altxs_set_step_fusion": (C.c_int, [C.c_int]),
+            "altxs_set_linear_packed": (C.c_int, [C.c_int]),
             "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
             "altxs_step_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int,
                                              vp]),
@@ -160,6 +163,8 @@ def lib():
             "altxs_split_weights": (C.c_int, [C.POINTER(QMat), vp, vp, vp]),
             "altxs_linear_workspace_bytes": (i64, [C.c_int, C.c_int]),
             "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
+            "altxs_linear_tc_workspace_bytes": (i64, [C.c_int, C.c_int, C.c_int]),
+            "altxs_linear_tc": (C.c_int, [C.POINTER(QMat), C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
             "altxs_gemm_workspace_bytes": (i64, [C.c_int] * 6),
             "altxs_param_layout_of": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(ParamLayout)]),
             "altxs_create": (vp, [C.POINTER(ModelDesc), C.c_int, C.POINTER(C.c_int)]),
@@ -173,6 +178,8 @@ def lib():
             "altxs_ttt_boundary": (C.c_int, [vp, vp]),
             "altxs_flush": (C.c_int, [vp, vp, vp, vp]),
             "altxs_begin_decode": (C.c_int, [vp, vp, vp, vp]),
+            "altxs_set_lockstep": (C.c_int, [vp, C.c_uint64, C.c_uint64]),
+            "altxs_lockstep_id": (C.c_int, [vp, C.POINTER(C.c_uint64)]),
             "altxs_get_status": (C.c_int, [vp, vp]),
             "altxs_ctx_words_per_stream": (i64, [vp]),
             "altxs_destroy": (None, [vp]),

@@ -81,6 +81,9 @@ struct altxs_ctx {
     uint64_t *nbits = nullptr;
     int32_t *status = nullptr;
     int64_t t = 0;  // symbols coded per stream so far
+    bool tensor_cores = false;
+    uint64_t weights_id = 0;  // the caller's identifier of the weights (altxs_set_lockstep)
+    uint64_t expect_id = 0;   // the encoder's lockstep id a decoder must match (0 = unchecked)
 
     void *alloc(size_t bytes) {
         void *p = nullptr;
@@ -93,6 +96,49 @@ struct altxs_ctx {
 namespace {
 
 int use_device(const altxs_ctx *c) { return cudaSetDevice(c->device) == cudaSuccess ? ALTXS_OK : ALTXS_ECUDA; }
+
+// Bumped whenever a kernel change alters any result bit of the step or the
+// update (the same number as the Python engine's payload fingerprint).
+constexpr uint64_t kNumerics = 2;
+
+struct Fnv {
+    uint64_t h = 1469598103934665603ull;
+    void bytes(const void *p, size_t n) {
+        const unsigned char *b = static_cast<const unsigned char *>(p);
+        for (size_t i = 0; i < n; ++i) h = (h ^ b[i]) * 1099511628211ull;
+    }
+    template <typename T>
+    void v(const T &x) {
+        bytes(&x, sizeof(x));
+    }
+};
+
+// Everything of a context that changes the coded bits: the model description
+// field by field (no padding or pointers), the layer schedule, the linear
+// path, the segment length, the update and its hyper-parameters, the caller's
+// weights identifier and the numerics version.
+uint64_t lockstep_id(const altxs_ctx *c) {
+    const altxs_model_desc &d = c->desc;
+    Fnv f;
+    f.v(kNumerics);
+    const int32_t ints[] = {d.vocab, d.n_layers, d.d_model, d.n_heads, d.n_kv_heads, d.head_dim, d.mlp_hidden, d.ctx,
+                            d.rope_dims, d.skip_gates, d.lora_rank, d.lora_mask, d.cdf_mode, d.cdf_bits, d.n_virtual,
+                            d.n_encoder, d.smear_gate, d.gate_window, d.xsa_last_n, d.sparse_gate, d.asym_softcap,
+                            d.parallel_start, d.parallel_final};
+    f.bytes(ints, sizeof(ints));
+    const float fl[] = {d.logit_softcap, d.lora_scale, d.sparse_gate_scale};
+    f.bytes(fl, sizeof(fl));
+    for (int32_t x : c->schedule) f.v(x);
+    f.v((int32_t)c->tensor_cores);
+    f.v(c->words);
+    f.v((int32_t)c->ttt);
+    if (c->ttt) {
+        const float hp[] = {c->hp.lr, c->hp.beta1, c->hp.beta2, c->hp.eps, c->hp.weight_decay, c->hp.grad_clip};
+        f.bytes(hp, sizeof(hp));
+    }
+    f.v(c->weights_id);
+    return f.h ? f.h : 1;  // never 0: 0 means "unchecked"
+}
 
 }  // namespace
 
@@ -154,7 +200,21 @@ int altxs_load_weights(altxs_ctx *c, const altxs_weights *view, int tensor_cores
         c->have_dense = true;
     }
     if (cudaStreamSynchronize(st) != cudaSuccess) return ALTXS_ECUDA;
+    c->tensor_cores = tensor_cores != 0;
     c->weights = true;
+    return ALTXS_OK;
+}
+
+int altxs_set_lockstep(altxs_ctx *c, uint64_t weights_id, uint64_t expect_id) {
+    if (!c) return ALTXS_EINVAL;
+    c->weights_id = weights_id;
+    c->expect_id = expect_id;
+    return ALTXS_OK;
+}
+
+int altxs_lockstep_id(altxs_ctx *c, uint64_t *id) {
+    if (!c || !id || !c->weights) return ALTXS_EINVAL;
+    *id = lockstep_id(c);
     return ALTXS_OK;
 }
 
@@ -304,6 +364,7 @@ int altxs_flush(altxs_ctx *c, uint32_t *d_bits, uint64_t *d_nbits, altxs_stream_
 // Load one segment per stream (bits [n][words], n_bits [n], device) and seed the decoders.
 int altxs_begin_decode(altxs_ctx *c, const uint32_t *d_bits, const uint64_t *d_nbits, altxs_stream_t stream) {
     if (!c || !c->n || !d_bits || !d_nbits) return ALTXS_EINVAL;
+    if (c->expect_id && c->expect_id != lockstep_id(c)) return ALTXS_EMISMATCH;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (cudaMemcpyAsync(c->b.bits, d_bits, (size_t)c->n * c->words * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return ALTXS_ECUDA;

@@ -9,6 +9,8 @@
 // logits with tanh softcap (model.py:1460-1500), the integer CDF and the coder.
 #include <math.h>
 
+#include <algorithm>
+
 #include <mutex>
 
 #include "coder.cuh"
@@ -61,6 +63,10 @@ struct StepCtx {
     // tensor-core path: hi/lo bf16 planes of the linear layers' inputs
     int tc;
     uint16_t *nrm_h, *nrm_l, *y_h, *y_l, *nrm2_h, *nrm2_l, *hid_h, *hid_l;
+    // split-K scratch of the tensor-core linears (partials, arrival counters)
+    float *tcpart;
+    uint32_t *tccnt;
+    int64_t tccnt_elems;
 };
 
 __device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return !b.active || b.active[i]; }
@@ -1130,6 +1136,9 @@ inline size_t fused_smem(const Dims &D) {
 // launch-per-phase step (each phase costs inside the kernel what it costs as
 // its own launch, and the grid barrier eats the launch gap it saves)
 int g_fused_max_streams = 0;
+// altxs_set_linear_packed: the tensor-core linears read the packed codes (1) or
+// the dense hi/lo planes (0); both give the same bits
+int g_linear_packed = 0;
 
 template <int LPK, int G>
 int launch_fused_t(const StepCtx &c, const FusedProg &fp, cudaStream_t st) {
@@ -1195,6 +1204,20 @@ int launch_fused(const StepCtx &c, const altxs_model_desc *desc, int mode, GridS
 
 // ---------------------------------------------------------------------------
 
+// split-K scratch of the step's tensor-core linears (qkv, o, up, down, tied head)
+inline int64_t tc_part_max(const Dims &D) {
+    const int nk[5][2] = {{D.qkv_n, D.d}, {D.d, D.d}, {D.F, D.d}, {D.d, D.F}, {D.V, D.d}};
+    int64_t m = 0;
+    for (const auto &x : nk) m = std::max(m, tc_linear_part_elems(D.n, x[0], x[1]));
+    return m;
+}
+inline int64_t tc_cnt_max(const Dims &D) {
+    const int nk[5][2] = {{D.qkv_n, D.d}, {D.d, D.d}, {D.F, D.d}, {D.d, D.F}, {D.V, D.d}};
+    int64_t m = 0;
+    for (const auto &x : nk) m = std::max(m, tc_linear_cnt_elems(D.n, x[0], x[1]));
+    return m;
+}
+
 inline int64_t ws_size(const Dims &D) {
     auto A = [](int64_t x) { return align_up(x * 4, 256); };
     int64_t s = 0;
@@ -1212,6 +1235,7 @@ inline int64_t ws_size(const Dims &D) {
     if (D.par || D.mlora) s += A((int64_t)D.n * D.d);  // MLP output
     if (D.mlora) s += A((int64_t)D.n * D.r);          // MLP adapter t
     s += 256;                                         // grid barrier words of the fused step
+    s += A(tc_part_max(D)) + A(tc_cnt_max(D));        // split-K scratch of the tensor-core linears
     return s;
 }
 
@@ -1273,6 +1297,11 @@ int altxs_set_wait_limit(uint32_t limit) {
 }
 
 uint32_t altxs_default_wait_limit(void) { return altxs::kWaitLimit; }
+
+int altxs_set_linear_packed(int on) {
+    g_linear_packed = on ? 1 : 0;
+    return ALTXS_OK;
+}
 
 int altxs_set_step_fusion(int max_streams) {
     if (max_streams < 0) return ALTXS_EINVAL;
@@ -1357,6 +1386,9 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     if (D.mlora) c.lt2 = take((int64_t)D.n * D.r);
     GridSync *gsync = reinterpret_cast<GridSync *>(p);
     p += 256;
+    c.tcpart = take(tc_part_max(D));
+    c.tccnt_elems = tc_cnt_max(D);
+    c.tccnt = reinterpret_cast<uint32_t *>(take(c.tccnt_elems));
     const altxs_split_planes *sp = w->split;
     c.tc = sp != nullptr;
     if (sp && (!sp->emb_hi || !sp->emb_lo || !sp->qkv_hi || !sp->qkv_lo || !sp->o_hi || !sp->o_lo || !sp->up_hi ||
@@ -1397,8 +1429,13 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
             t.status = &b->ac[0].status;
             t.status_stride = sizeof(altxs_ac_state) / sizeof(uint32_t);
         }
+        if (!w->planes_live && g_linear_packed) t.wq = &q.W;  // the producer warps expand B from the codes
+        t.part = c.tcpart;
+        t.cnt = c.tccnt;
         return launch_tc(t, st);
     };
+    if (c.tc && c.tccnt_elems > 0 && cudaMemsetAsync(c.tccnt, 0, c.tccnt_elems * 4, st) != cudaSuccess)
+        return ALTXS_ECUDA;
 
     ALTXS_LAUNCH(::altxs::kKEmbed, st, k_embed<<<D.n, 128, 0, st>>>(c));
     {

@@ -33,7 +33,6 @@ namespace {
 
 constexpr int kBM = 128;         // tile rows = tensor-memory lanes
 constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of bf16
-constexpr int kTcThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 MMA
 constexpr unsigned kFull = 0xffffffffu;
 
 template <int BN, int AMN, int BMN>
@@ -135,20 +134,120 @@ __device__ __forceinline__ float leaky2(float v) {  // leaky_relu(v, 0.5)^2 (mod
     return __fmul_rn(t, t);
 }
 
+// Dequantise the 64-wide group slice `kb` of packed weight row `wrow` into
+// values i0 .. i0 + N1 - 1 (N1 = 64 / LPR) of that row in a K-major stage:
+// hi/lo bf16 planes, 128 bytes per row, 16-byte chunk j of row r at
+// (j ^ (r & 7)) (the 128-byte swizzle TMA would have produced).  The values
+// are those of k_split_weights: w = level * scale, hi = bf16(w), lo = bf16(w - hi).
+struct DqGroup {
+    uint32_t d;            // group descriptor
+    uint64_t w[4];         // packed codes (up to 4 x 64 bits: 2/3/4-bit groups)
+    const uint8_t *gp;     // the group's code bytes
+};
+
+__device__ __forceinline__ int dq_bits(uint32_t d) {
+    const int c = (d >> 16) & 15;
+    return c == 0 ? 0 : c == 1 ? 2 : c == 2 ? 3 : c == 3 ? 4 : 32;
+}
+
+__device__ __forceinline__ void dq_fetch(const altxs_qmat &W, int64_t wrow, int kb, uint32_t row_off8, DqGroup &q) {
+    const int G = W.cols >> 6;
+    q.d = __ldg(W.gdesc + wrow * G + kb);
+    q.gp = W.codes + 8ull * ((uint64_t)row_off8 + (q.d >> 20));
+    const int b = dq_bits(q.d);
+    const uint64_t *p = reinterpret_cast<const uint64_t *>(q.gp);
+    if (b >= 2 && b <= 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q.w[j] = j < b ? __ldg(p + j) : 0ull;
+    }
+}
+
+__device__ __forceinline__ void dq_put8(unsigned char *hrow, unsigned char *lrow, int pos, const float *f) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * u]), h1 = __float2bfloat16_rn(f[2 * u + 1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(f[2 * u], __bfloat162float(h0)));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(__fsub_rn(f[2 * u + 1], __bfloat162float(h1)));
+        h[u] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+        l[u] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+    }
+    *reinterpret_cast<uint4 *>(hrow + pos) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4 *>(lrow + pos) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+template <int B, int N1>
+__device__ __forceinline__ void dq_codes(const DqGroup &q, const altxs_qmat &W, int64_t wrow, int kb, int i0,
+                                         unsigned char *hrow, unsigned char *lrow, int r7) {
+    const float s = h2f((uint16_t)(q.d & 0xffffu));
+    const float center = (float)((1 << B) - 1) * 0.5f;
+    const uint16_t *lut = W.lut ? W.lut + 16ull * __ldg(W.glut + wrow * (W.cols >> 6) + kb) : nullptr;
+#pragma unroll
+    for (int c = 0; c < N1 / 8; ++c) {
+        float f[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + c * 8 + u;  // i0 is 0 or 32: the bit positions below fold to constants per case
+            const int bp = i * B, wi = bp >> 6, sh = bp & 63;
+            uint64_t v = q.w[wi] >> sh;
+            if (sh + B > 64) v |= q.w[wi + 1] << (64 - sh);
+            const uint32_t code = (uint32_t)v & ((1u << B) - 1u);
+            const float lev = lut ? h2f(__ldg(lut + code)) : __fsub_rn((float)code, center);
+            f[u] = __fmul_rn(lev, s);
+        }
+        const int j = (i0 >> 3) + c;
+        dq_put8(hrow, lrow, (j ^ r7) << 4, f);
+    }
+}
+
+template <int N1>
+__device__ __forceinline__ void dq_slice(const DqGroup &q, const altxs_qmat &W, int64_t wrow, int kb, int i0,
+                                         unsigned char *hrow, unsigned char *lrow, int r7) {
+    const int b = dq_bits(q.d);
+    if (b == 2) {
+        if (i0 == 0) dq_codes<2, N1>(q, W, wrow, kb, 0, hrow, lrow, r7);
+        else dq_codes<2, N1>(q, W, wrow, kb, 32, hrow, lrow, r7);
+    } else if (b == 3) {
+        if (i0 == 0) dq_codes<3, N1>(q, W, wrow, kb, 0, hrow, lrow, r7);
+        else dq_codes<3, N1>(q, W, wrow, kb, 32, hrow, lrow, r7);
+    } else if (b == 4) {
+        if (i0 == 0) dq_codes<4, N1>(q, W, wrow, kb, 0, hrow, lrow, r7);
+        else dq_codes<4, N1>(q, W, wrow, kb, 32, hrow, lrow, r7);
+    } else {
+        // 0-bit group (zeros) or an exact fp32 group
+        const float *dense = reinterpret_cast<const float *>(q.gp);
+#pragma unroll 1
+        for (int c = 0; c < N1 / 8; ++c) {
+            float f[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) f[u] = b == 32 ? __ldg(dense + i0 + c * 8 + u) : 0.0f;
+            dq_put8(hrow, lrow, ((((i0 >> 3) + c) ^ r7) << 4), f);
+        }
+    }
+}
+
+
 struct Tile {
     int m0, n0, b, kb0, kb1;
+    int id, split;  // output tile index (m-tile fastest, then n-tile, then batch) and split index
     bool skip;
 };
 
-// tile t: m-tile fastest (CTAs running at the same time share B tiles), then n-tile, then batch
-__device__ __forceinline__ Tile tile_of(const TcGemm &g, int t, int mt, int ntl, int nk, int bn) {
+// unit u: split fastest, then m-tile (CTAs running at the same time share B
+// tiles), then n-tile, then batch; split s covers the K slices
+// [s*nk/S, (s+1)*nk/S) of its tile
+__device__ __forceinline__ Tile tile_of(const TcGemm &g, int u, int mt, int ntl, int nk, int bn) {
     Tile T;
+    const int S = g.splits;
+    T.split = u % S;
+    const int t = u / S;
+    T.id = t;
     T.m0 = (t % mt) * kBM;
     const int r = t / mt;
     T.n0 = (r % ntl) * bn;
     T.b = r / ntl;
-    T.kb0 = 0;
-    T.kb1 = nk;
+    T.kb0 = T.split * nk / S;
+    T.kb1 = (T.split + 1) * nk / S;
     T.skip = g.causal == 1 && T.n0 > T.m0 + kBM - 1;
     if (g.causal == 2) T.kb1 = min(nk, (T.m0 + kBM + kBK - 1) / kBK);
     if (g.causal == 3) T.kb0 = min(nk, T.m0 / kBK);
@@ -157,13 +256,169 @@ __device__ __forceinline__ Tile tile_of(const TcGemm &g, int t, int mt, int ntl,
 
 __device__ __forceinline__ int op_batch(const TcOp &o, int b) { return (b / o.div) * o.mul + o.add; }
 
-template <int BN, int AMN, int BMN>
-__global__ void __launch_bounds__(kTcThreads, 1)
+// Epilogue of one 32 x 32 block (tile rows 32*warp .., columns c0 ..): v holds
+// this lane's row (lane = tile row).  Applies the layer's epilogue and stores.
+template <int BN>
+__device__ __forceinline__ void emit_block(const TcGemm &g, const Tile &T, const CUtensorMap *tcm, int warp, int lane,
+                                           int c0, const float *v, bool no_k, float (*eb)[33], float *sb, bool vec) {
+    float *Cb = g.C ? g.C + (int64_t)T.b * g.sC : nullptr;
+    if (g.tma_c) {
+        // lane = tile row: its 32 columns become row `lane` of the box
+        // (16-byte chunk j stored at j ^ (row & 7): the 128-byte swizzle),
+        // then one asynchronous tensor store; the map clips rows >= M and
+        // columns >= N.  The box is rewritten only after the previous
+        // store has finished reading it.
+        const int n0 = T.n0 + c0, mrow = T.m0 + warp * 32;
+        if (n0 >= g.N || mrow >= g.M) return;
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        char *rowp = reinterpret_cast<char *>(sb) + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float q[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float x = no_k ? 0.0f : v[4 * c + u];
+                q[u] = g.alpha != 1.0f ? __fmul_rn(g.alpha, x) : x;
+            }
+            *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) = make_float4(q[0], q[1], q[2], q[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tma_store_3d(tcm, sb, n0, mrow, T.b);
+        return;
+    }
+#pragma unroll
+    for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
+    __syncwarp();
+    // lane -> 4 consecutive columns (c4) of rows it*4 + sub: one 16-byte store
+    // per lane covers 4 rows x 32 columns per warp instruction.  All reads of
+    // a block come before its stores (the residual input may be the output
+    // array itself).
+    const int sub = lane >> 3, c4 = (lane & 7) * 4;
+    float4 vv[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const float *e = eb[it * 4 + sub] + c4;
+        vv[it] = make_float4(e[0], e[1], e[2], e[3]);
+    }
+    __syncwarp();  // the block buffer is free for the next block once every lane has its values
+    const int n = T.n0 + c0 + c4;
+    const int mb = T.m0 + warp * 32;
+    if (n >= g.N) return;
+    if (vec && n + 3 < g.N) {
+        if (g.epi == kEpiResid) {
+            const float4 cs = *reinterpret_cast<const float4 *>(g.colscale + n);
+            float4 rv[8];
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int m = mb + it * 4 + sub;
+                rv[it] = m < g.M ? *reinterpret_cast<const float4 *>(g.R + (int64_t)m * g.ldr + n)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                vv[it].x = __fadd_rn(rv[it].x, __fmul_rn(cs.x, vv[it].x));
+                vv[it].y = __fadd_rn(rv[it].y, __fmul_rn(cs.y, vv[it].y));
+                vv[it].z = __fadd_rn(rv[it].z, __fmul_rn(cs.z, vv[it].z));
+                vv[it].w = __fadd_rn(rv[it].w, __fmul_rn(cs.w, vv[it].w));
+            }
+        } else {
+            if (g.alpha != 1.0f) {
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    vv[it].x = __fmul_rn(g.alpha, vv[it].x);
+                    vv[it].y = __fmul_rn(g.alpha, vv[it].y);
+                    vv[it].z = __fmul_rn(g.alpha, vv[it].z);
+                    vv[it].w = __fmul_rn(g.alpha, vv[it].w);
+                }
+            }
+            if (g.beta != 0.0f) {
+                float4 cv[8];
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    const int m = mb + it * 4 + sub;
+                    cv[it] = m < g.M ? *reinterpret_cast<const float4 *>(Cb + (int64_t)m * g.ldc + n)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    vv[it].x = __fadd_rn(vv[it].x, __fmul_rn(g.beta, cv[it].x));
+                    vv[it].y = __fadd_rn(vv[it].y, __fmul_rn(g.beta, cv[it].y));
+                    vv[it].z = __fadd_rn(vv[it].z, __fmul_rn(g.beta, cv[it].z));
+                    vv[it].w = __fadd_rn(vv[it].w, __fmul_rn(g.beta, cv[it].w));
+                }
+            }
+            if (g.epi == kEpiLeaky2) {
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    vv[it].x = leaky2(vv[it].x);
+                    vv[it].y = leaky2(vv[it].y);
+                    vv[it].z = leaky2(vv[it].z);
+                    vv[it].w = leaky2(vv[it].w);
+                }
+            }
+        }
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+            const int64_t m = mb + it * 4 + sub;
+            if (m >= g.M) continue;
+            if (Cb) *reinterpret_cast<float4 *>(Cb + m * g.ldc + n) = vv[it];
+            if (g.Y2) *reinterpret_cast<float4 *>(g.Y2 + m * g.ldy2 + n) = vv[it];
+            if (g.p_hi) {
+                const float f[4] = {vv[it].x, vv[it].y, vv[it].z, vv[it].w};
+                uint32_t h2[2], l2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * u]), h1 = __float2bfloat16_rn(f[2 * u + 1]);
+                    const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(f[2 * u], __bfloat162float(h0)));
+                    const __nv_bfloat16 l1 = __float2bfloat16_rn(__fsub_rn(f[2 * u + 1], __bfloat162float(h1)));
+                    h2[u] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+                    l2[u] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+                }
+                *reinterpret_cast<uint2 *>(g.p_hi + m * g.ldp + n) = make_uint2(h2[0], h2[1]);
+                *reinterpret_cast<uint2 *>(g.p_lo + m * g.ldp + n) = make_uint2(l2[0], l2[1]);
+            }
+        }
+    } else {
+        // ragged or unaligned edge: element by element, same arithmetic
+        for (int it = 0; it < 8; ++it) {
+            const int64_t m = mb + it * 4 + sub;
+            if (m >= g.M) continue;
+            const float f4[4] = {vv[it].x, vv[it].y, vv[it].z, vv[it].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (n + u >= g.N) break;
+                float x = f4[u];
+                if (g.epi == kEpiResid) {
+                    x = __fadd_rn(g.R[m * g.ldr + n + u], __fmul_rn(g.colscale[n + u], x));
+                } else {
+                    if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
+                    if (g.beta != 0.0f) x = __fadd_rn(x, __fmul_rn(g.beta, Cb[m * g.ldc + n + u]));
+                    if (g.epi == kEpiLeaky2) x = leaky2(x);
+                }
+                if (Cb) Cb[m * g.ldc + n + u] = x;
+                if (g.Y2) g.Y2[m * g.ldy2 + n + u] = x;
+                if (g.p_hi) split_store(g.p_hi, g.p_lo, m * g.ldp + n + u, x);
+            }
+        }
+    }
+}
+
+template <int BQ>
+struct TcThreads {
+    // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer, 6-9 (BQ) dequantising producers
+    static constexpr int kN = BQ ? 320 : 192;
+};
+
+template <int BN, int AMN, int BMN, int BQ>
+__global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
               const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
               const __grid_constant__ CUtensorMap tc_map, TcGemm g) {
     using Cfg = TcCfg<BN, AMN, BMN>;
     constexpr int S = Cfg::kStages;
+    static_assert(!BQ || !BMN, "packed weights are read K-major");
     extern __shared__ unsigned char tc_smem_raw[];
     __shared__ __align__(8) uint64_t full[S], empty[S], tfull[2], tempty[2], drainb;
     __shared__ uint32_t tmem_sh;
@@ -174,10 +429,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = (g.K + kBK - 1) / kBK;
     const int mt = (g.M + kBM - 1) / kBM, ntl = (g.N + BN - 1) / BN;
-    const int n_tiles = mt * ntl * g.batch;
+    const int n_units = mt * ntl * g.batch * g.splits;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], BQ ? 5 : 1);  // the A copies' transaction arrival (+ 4 dequantising warps)
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -201,8 +456,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 4) {
         if (lane == 0) {
-            int q = 0;  // stage fills issued by this CTA (all tiles)
-            for (int t = blockIdx.x; t < n_tiles && !abort_sh; t += gridDim.x) {
+            int q = 0;  // stage fills issued by this CTA (all units)
+            for (int t = blockIdx.x; t < n_units && !abort_sh; t += gridDim.x) {
                 const Tile T = tile_of(g, t, mt, ntl, nk, BN);
                 if (T.skip) continue;
                 const int ab = op_batch(g.a, T.b), bb = op_batch(g.b, T.b);
@@ -216,7 +471,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     unsigned char *st = sm + s * Cfg::kStage;
                     unsigned char *sa = st, *sb = st + 2 * Cfg::kATile;
                     const int k0 = kb * kBK;
-                    mbar_expect_tx(&full[s], Cfg::kStage);
+                    mbar_expect_tx(&full[s], BQ ? 2 * Cfg::kATile : Cfg::kStage);
                     if (!AMN) {
                         tma_load_3d(sa, &ta_hi, k0, (int)g.a.row_off + T.m0, ab, &full[s]);
                         tma_load_3d(sa + Cfg::kATile, &ta_lo, k0, (int)g.a.row_off + T.m0, ab, &full[s]);
@@ -228,6 +483,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                         &full[s]);
                         }
                     }
+                    if (BQ) continue;  // the dequantising warps fill B
                     if (!BMN) {
                         tma_load_3d(sb, &tb_hi, k0, (int)g.b.row_off + T.n0, bb, &full[s]);
                         tma_load_3d(sb + Cfg::kBTile, &tb_lo, k0, (int)g.b.row_off + T.n0, bb, &full[s]);
@@ -248,8 +504,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == 5) {
         if (lane == 0) {
             bool ok = true;
-            int q = 0, j = 0;  // stage fills consumed, tiles done by this CTA
-            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            int q = 0, j = 0;  // stage fills consumed, units done by this CTA
+            for (int t = blockIdx.x; t < n_units && ok; t += gridDim.x) {
                 const Tile T = tile_of(g, t, mt, ntl, nk, BN);
                 if (T.skip) continue;
                 const int buf = j & 1, use = j >> 1;
@@ -280,10 +536,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 if (ok) tc_commit(&tfull[buf]);
             }
-            if (!ok) {  // no result for this tile: wait for the MMAs already issued, then leave
+            if (!ok) {  // no result for this unit: wait for the MMAs already issued, then leave
                 abort_sh = 1;
                 tc_commit(&drainb);
                 mbar_wait_bounded(&drainb, 0, kWaitLimit);
+            }
+        }
+    } else if (warp >= 6) {
+        if constexpr (BQ != 0) {
+            // B from the packed codes: warp w fills tile rows (w-6)*R .. of every
+            // stage, LPR lanes per row, each lane 64/LPR consecutive values of the
+            // row's 64-wide group.  Generic-proxy stores, then a proxy fence so the
+            // tensor cores see them, then one arrival per warp on the stage's full
+            // barrier.  The next slice's codes are fetched before this one is
+            // expanded.
+            constexpr int R = BN / 4, LPR = 32 / R, N1 = 64 / LPR;
+            const int rloc = (warp - 6) * R + lane / LPR;
+            const int i0 = (lane % LPR) * N1;
+            const int r7 = rloc & 7;
+            int q = 0;
+            for (int t = blockIdx.x; t < n_units && !abort_sh; t += gridDim.x) {
+                const Tile T = tile_of(g, t, mt, ntl, nk, BN);
+                if (T.skip) continue;
+                const int n = T.n0 + rloc;
+                const bool valid = n < g.N;
+                const int64_t wrow = g.wq_row0 + (valid ? n : 0);
+                const uint32_t ro = valid ? __ldg(g.wq.row_off8 + wrow) : 0u;
+                DqGroup cur, nxt;
+                if (valid && T.kb0 < T.kb1) dq_fetch(g.wq, wrow, T.kb0, ro, cur);
+                bool stop = false;
+                for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
+                    const int s = q % S, r = q / S;
+                    if (valid && kb + 1 < T.kb1) dq_fetch(g.wq, wrow, kb + 1, ro, nxt);
+                    if (r > 0) {
+                        bool w_ok = true;
+                        if (lane == 0) w_ok = mbar_wait_bounded(&empty[s], (r - 1) & 1, wait_limit());
+                        w_ok = __shfl_sync(kFull, w_ok ? 1 : 0, 0) != 0;
+                        if (!w_ok) abort_sh = 1;
+                    }
+                    if (abort_sh) {
+                        stop = true;
+                        break;
+                    }
+                    unsigned char *bh = sm + s * Cfg::kStage + 2 * Cfg::kATile;
+                    unsigned char *hrow = bh + rloc * 128, *lrow = bh + Cfg::kBTile + rloc * 128;
+                    if (valid) {
+                        dq_slice<N1>(cur, g.wq, wrow, kb, i0, hrow, lrow, r7);
+                    } else {
+                        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int c = 0; c < N1 / 8; ++c) dq_put8(hrow, lrow, ((((i0 >> 3) + c) ^ r7) << 4), z);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[s]);
+                    cur = nxt;
+                }
+                if (stop) break;
             }
         }
     } else {
@@ -298,7 +607,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool vec = ((g.ldc | g.ldr | g.ldy2 | g.ldp | g.sC) & 3) == 0 && al(g.C, 15) && al(g.R, 15) &&
                          al(g.Y2, 15) && al(g.colscale, 15) && al(g.p_hi, 7) && al(g.p_lo, 7);
         int j = 0;
-        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+        for (int t = blockIdx.x; t < n_units; t += gridDim.x) {
             const Tile T = tile_of(g, t, mt, ntl, nk, BN);
             if (T.skip) continue;
             const int buf = j & 1, use = j >> 1;
@@ -313,159 +622,82 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             const bool no_k = T.kb0 >= T.kb1;  // nothing accumulated: the product is zero
             const uint32_t tl = tmem + buf * Cfg::kTmemCols + ((uint32_t)(warp * 32) << 16);
-            float *Cb = g.C ? g.C + (int64_t)T.b * g.sC : nullptr;
+            if (g.splits == 1) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    __syncwarp();  // warp-collective load; the block buffer is free again
+                    tc_ld32(tl + c0, v);
+                    if (c0 + 32 >= BN) {  // accumulator fully read: hand it back to the MMA warp
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
+                    }
+                    emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, no_k, eb, sb, vec);
+                }
+                continue;
+            }
+            // split K: this warp's 32-row slab of the partial goes to
+            // part[tile][split] ([128][BN] fp32, row-major); the slab's arrival
+            // counter picks the last of the tile's splits, which sums the
+            // partials in split order and runs the epilogue on the sum
+            float *pslot = g.part + ((int64_t)T.id * g.splits + T.split) * (kBM * BN) + (int64_t)warp * 32 * BN;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
-                __syncwarp();  // warp-collective load; the block buffer is free again
+                __syncwarp();
                 tc_ld32(tl + c0, v);
-                if (c0 + 32 >= BN) {  // accumulator fully read: hand it back to the MMA warp
+                if (c0 + 32 >= BN) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[buf]);
                 }
-                if (g.tma_c) {
-                    // lane = tile row: its 32 columns become row `lane` of the box
-                    // (16-byte chunk j stored at j ^ (row & 7): the 128-byte swizzle),
-                    // then one asynchronous tensor store; the map clips rows >= M and
-                    // columns >= N.  The box is rewritten only after the previous
-                    // store has finished reading it.
-                    const int n0 = T.n0 + c0, mrow = T.m0 + warp * 32;
-                    if (n0 >= g.N || mrow >= g.M) continue;
-                    if (lane == 0) bulk_wait_read_all();
-                    __syncwarp();
-                    char *rowp = reinterpret_cast<char *>(sb) + lane * 128;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        float q[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const float x = no_k ? 0.0f : v[4 * c + u];
-                            q[u] = g.alpha != 1.0f ? __fmul_rn(g.alpha, x) : x;
-                        }
-                        *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) = make_float4(q[0], q[1], q[2], q[3]);
-                    }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) tma_store_3d(&tc_map, sb, n0, mrow, T.b);
-                    continue;
-                }
 #pragma unroll
                 for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
                 __syncwarp();
-                // lane -> 4 consecutive columns (c4) of rows it*4 + sub: one
-                // 16-byte store per lane covers 4 rows x 32 columns per warp
-                // instruction.  All reads of a block come before its stores (the
-                // residual input may be the output array itself).
                 const int sub = lane >> 3, c4 = (lane & 7) * 4;
-                float4 vv[8];
 #pragma unroll
                 for (int it = 0; it < 8; ++it) {
                     const float *e = eb[it * 4 + sub] + c4;
-                    vv[it] = make_float4(e[0], e[1], e[2], e[3]);
+                    *reinterpret_cast<float4 *>(pslot + (it * 4 + sub) * BN + c0 + c4) =
+                        make_float4(e[0], e[1], e[2], e[3]);
                 }
-                const int n = T.n0 + c0 + c4;
-                const int mb = T.m0 + warp * 32;
-                if (n >= g.N) continue;
-                if (vec && n + 3 < g.N) {
-                    if (g.epi == kEpiResid) {
-                        const float4 cs = *reinterpret_cast<const float4 *>(g.colscale + n);
-                        float4 rv[8];
-#pragma unroll
-                        for (int it = 0; it < 8; ++it) {
-                            const int m = mb + it * 4 + sub;
-                            rv[it] = m < g.M ? *reinterpret_cast<const float4 *>(g.R + (int64_t)m * g.ldr + n)
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-#pragma unroll
-                        for (int it = 0; it < 8; ++it) {
-                            vv[it].x = __fadd_rn(rv[it].x, __fmul_rn(cs.x, vv[it].x));
-                            vv[it].y = __fadd_rn(rv[it].y, __fmul_rn(cs.y, vv[it].y));
-                            vv[it].z = __fadd_rn(rv[it].z, __fmul_rn(cs.z, vv[it].z));
-                            vv[it].w = __fadd_rn(rv[it].w, __fmul_rn(cs.w, vv[it].w));
-                        }
-                    } else {
-                        if (g.alpha != 1.0f) {
-#pragma unroll
-                            for (int it = 0; it < 8; ++it) {
-                                vv[it].x = __fmul_rn(g.alpha, vv[it].x);
-                                vv[it].y = __fmul_rn(g.alpha, vv[it].y);
-                                vv[it].z = __fmul_rn(g.alpha, vv[it].z);
-                                vv[it].w = __fmul_rn(g.alpha, vv[it].w);
-                            }
-                        }
-                        if (g.beta != 0.0f) {
-                            float4 cv[8];
-#pragma unroll
-                            for (int it = 0; it < 8; ++it) {
-                                const int m = mb + it * 4 + sub;
-                                cv[it] = m < g.M ? *reinterpret_cast<const float4 *>(Cb + (int64_t)m * g.ldc + n)
-                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-                            }
-#pragma unroll
-                            for (int it = 0; it < 8; ++it) {
-                                vv[it].x = __fadd_rn(vv[it].x, __fmul_rn(g.beta, cv[it].x));
-                                vv[it].y = __fadd_rn(vv[it].y, __fmul_rn(g.beta, cv[it].y));
-                                vv[it].z = __fadd_rn(vv[it].z, __fmul_rn(g.beta, cv[it].z));
-                                vv[it].w = __fadd_rn(vv[it].w, __fmul_rn(g.beta, cv[it].w));
-                            }
-                        }
-                        if (g.epi == kEpiLeaky2) {
-#pragma unroll
-                            for (int it = 0; it < 8; ++it) {
-                                vv[it].x = leaky2(vv[it].x);
-                                vv[it].y = leaky2(vv[it].y);
-                                vv[it].z = leaky2(vv[it].z);
-                                vv[it].w = leaky2(vv[it].w);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int it = 0; it < 8; ++it) {
-                        const int64_t m = mb + it * 4 + sub;
-                        if (m >= g.M) continue;
-                        if (Cb) *reinterpret_cast<float4 *>(Cb + m * g.ldc + n) = vv[it];
-                        if (g.Y2) *reinterpret_cast<float4 *>(g.Y2 + m * g.ldy2 + n) = vv[it];
-                        if (g.p_hi) {
-                            const float f[4] = {vv[it].x, vv[it].y, vv[it].z, vv[it].w};
-                            uint32_t h2[2], l2[2];
-#pragma unroll
-                            for (int u = 0; u < 2; ++u) {
-                                const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * u]), h1 = __float2bfloat16_rn(f[2 * u + 1]);
-                                const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(f[2 * u], __bfloat162float(h0)));
-                                const __nv_bfloat16 l1 =
-                                    __float2bfloat16_rn(__fsub_rn(f[2 * u + 1], __bfloat162float(h1)));
-                                h2[u] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-                                l2[u] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
-                            }
-                            *reinterpret_cast<uint2 *>(g.p_hi + m * g.ldp + n) = make_uint2(h2[0], h2[1]);
-                            *reinterpret_cast<uint2 *>(g.p_lo + m * g.ldp + n) = make_uint2(l2[0], l2[1]);
-                        }
-                    }
-                } else {
-                    // ragged or unaligned edge: element by element, same arithmetic
-                    for (int it = 0; it < 8; ++it) {
-                        const int64_t m = mb + it * 4 + sub;
-                        if (m >= g.M) continue;
-                        const float f4[4] = {vv[it].x, vv[it].y, vv[it].z, vv[it].w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            if (n + u >= g.N) break;
-                            float x = f4[u];
-                            if (g.epi == kEpiResid) {
-                                x = __fadd_rn(g.R[m * g.ldr + n + u], __fmul_rn(g.colscale[n + u], x));
-                            } else {
-                                if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
-                                if (g.beta != 0.0f) x = __fadd_rn(x, __fmul_rn(g.beta, Cb[m * g.ldc + n + u]));
-                                if (g.epi == kEpiLeaky2) x = leaky2(x);
-                            }
-                            if (Cb) Cb[m * g.ldc + n + u] = x;
-                            if (g.Y2) g.Y2[m * g.ldy2 + n + u] = x;
-                            if (g.p_hi) split_store(g.p_hi, g.p_lo, m * g.ldp + n + u, x);
-                        }
-                    }
-                }
+                __syncwarp();
             }
+            __threadfence();
+            __syncwarp();
+            uint32_t old = 0;
+            if (lane == 0) old = atomicAdd(g.cnt + (int64_t)T.id * 4 + warp, 1u);
+            old = __shfl_sync(kFull, old, 0);
+            if (old != (uint32_t)g.splits - 1) continue;
+            __threadfence();  // the other splits' partials are visible from here on
+            const float *pbase = g.part + (int64_t)T.id * g.splits * (kBM * BN) + (int64_t)(warp * 32 + lane) * BN;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+#pragma unroll
+                for (int u4 = 0; u4 < 8; ++u4) {
+                    const float4 p0 = __ldcg(reinterpret_cast<const float4 *>(pbase + c0) + u4);
+                    v[4 * u4] = p0.x;
+                    v[4 * u4 + 1] = p0.y;
+                    v[4 * u4 + 2] = p0.z;
+                    v[4 * u4 + 3] = p0.w;
+                }
+                for (int sp = 1; sp < g.splits; ++sp) {
+                    const float *ps = pbase + (int64_t)sp * (kBM * BN) + c0;
+#pragma unroll
+                    for (int u4 = 0; u4 < 8; ++u4) {
+                        const float4 p = __ldcg(reinterpret_cast<const float4 *>(ps) + u4);
+                        v[4 * u4] = __fadd_rn(v[4 * u4], p.x);
+                        v[4 * u4 + 1] = __fadd_rn(v[4 * u4 + 1], p.y);
+                        v[4 * u4 + 2] = __fadd_rn(v[4 * u4 + 2], p.z);
+                        v[4 * u4 + 3] = __fadd_rn(v[4 * u4 + 3], p.w);
+                    }
+                }
+                __syncwarp();
+                emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, false, eb, sb, vec);
+            }
+            if (lane == 0) g.cnt[(int64_t)T.id * 4 + warp] = 0;  // ready for the next call
         }
         if (g.tma_c && lane == 0) bulk_wait_all();  // every tensor store of this warp has landed
     }
@@ -562,55 +794,73 @@ bool op_ok(const TcOp &o) {
     return o.row_off >= 0;
 }
 
-template <int BN, int AMN, int BMN>
+template <int BN, int AMN, int BMN, int BQ>
 int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
     using Cfg = TcCfg<BN, AMN, BMN>;
+    static std::mutex mu;
     static bool attr_done[64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return ALTXS_ECUDA;
-    if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(k_tc_gemm<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
-            cudaSuccess)
-            return ALTXS_ECUDA;
-        attr_done[dev] = true;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ALTXS_ECUDA;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_done[dev]) {
+            if (cudaFuncSetAttribute(k_tc_gemm<BN, AMN, BMN, BQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::kSmem) != cudaSuccess)
+                return ALTXS_ECUDA;
+            attr_done[dev] = true;
+        }
     }
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo, tc_map;
     const int abox = AMN ? 64 : kBM, bbox = BMN ? 64 : BN;
-    if (!make_map(&ta_hi, g.a.hi, g.a, abox) || !make_map(&ta_lo, g.a.lo, g.a, abox) ||
-        !make_map(&tb_hi, g.b.hi, g.b, bbox) || !make_map(&tb_lo, g.b.lo, g.b, bbox))
+    if (!make_map(&ta_hi, g.a.hi, g.a, abox) || !make_map(&ta_lo, g.a.lo, g.a, abox)) return ALTXS_EINVAL;
+    if (BQ) {
+        tb_hi = ta_hi;  // unused: the producer warps expand B from the packed codes
+        tb_lo = ta_lo;
+    } else if (!make_map(&tb_hi, g.b.hi, g.b, bbox) || !make_map(&tb_lo, g.b.lo, g.b, bbox)) {
         return ALTXS_EINVAL;
+    }
     TcGemm gk = g;
     gk.tma_c = make_c_map(&tc_map, g) ? 1 : 0;
     if (!gk.tma_c) tc_map = ta_hi;  // unused
-    // persistent: at most one CTA per SM walks the tiles
-    const int64_t tiles = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch;
-    const int grid = (int)(tiles < sms ? tiles : sms);
+    // persistent: at most one CTA per SM walks the units
+    const int64_t units = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch * g.splits;
+    const int grid = (int)(units < sms ? units : sms);
     ALTXS_LAUNCH(::altxs::kKQmm, st,
-                 k_tc_gemm<BN, AMN, BMN><<<grid, kTcThreads, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo, tc_map, gk));
+                 k_tc_gemm<BN, AMN, BMN, BQ><<<grid, TcThreads<BQ>::kN, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo,
+                                                                                          tc_map, gk));
     return ALTXS_OK;
 }
 
 template <int BN>
 int launch_bn(const TcGemm &g, int sms, cudaStream_t st) {
-    if (!g.a.mn_major && !g.b.mn_major) return launch_cfg<BN, 0, 0>(g, sms, st);
-    if (!g.a.mn_major && g.b.mn_major) return launch_cfg<BN, 0, 1>(g, sms, st);
-    if (g.a.mn_major && !g.b.mn_major) return launch_cfg<BN, 1, 0>(g, sms, st);
-    return launch_cfg<BN, 1, 1>(g, sms, st);
+    if (g.bq) return g.a.mn_major ? launch_cfg<BN, 1, 0, 1>(g, sms, st) : launch_cfg<BN, 0, 0, 1>(g, sms, st);
+    if (!g.a.mn_major && !g.b.mn_major) return launch_cfg<BN, 0, 0, 0>(g, sms, st);
+    if (!g.a.mn_major && g.b.mn_major) return launch_cfg<BN, 0, 1, 0>(g, sms, st);
+    if (g.a.mn_major && !g.b.mn_major) return launch_cfg<BN, 1, 0, 0>(g, sms, st);
+    return launch_cfg<BN, 1, 1, 0>(g, sms, st);
 }
 
 }  // namespace
 
-int launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
+int launch_tc_gemm(const TcGemm &g0, cudaStream_t st) {
+    TcGemm g = g0;
+    if (g.splits == 0) g.splits = 1;  // zero-initialised arguments: no split
     if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
-    if (g.K <= 0 || !op_ok(g.a) || !op_ok(g.b)) return ALTXS_EINVAL;
+    if (g.K <= 0 || !op_ok(g.a) || (!g.bq && !op_ok(g.b))) return ALTXS_EINVAL;
     if (g.causal < 0 || g.causal > 3) return ALTXS_EINVAL;
+    if (g.bq && (!g.wq.codes || !g.wq.row_off8 || !g.wq.gdesc || (g.wq.lut && !g.wq.glut) || g.wq.cols != g.K ||
+                 g.K % kBK || g.wq_row0 < 0 || g.wq_row0 + g.N > g.wq.rows || g.batch != 1 || g.b.mn_major ||
+                 (reinterpret_cast<uintptr_t>(g.wq.codes) & 7)))
+        return ALTXS_EINVAL;
+    if (g.splits < 1 || g.splits > (g.K + kBK - 1) / kBK) return ALTXS_EINVAL;
+    if (g.splits > 1 && (!g.part || !g.cnt || g.causal != 0 || (reinterpret_cast<uintptr_t>(g.part) & 15)))
+        return ALTXS_EINVAL;
     if (g.epi == kEpiResid && (!g.R || !g.colscale || g.batch != 1)) return ALTXS_EINVAL;
     if ((g.p_hi && (!g.p_lo || g.ldp < g.N || g.batch != 1)) || (g.Y2 && g.batch != 1)) return ALTXS_EINVAL;
     if (g.beta != 0.0f && !g.C) return ALTXS_EINVAL;
     // the K extent of each operand must be covered by its stored array (zeros beyond come from the bounds)
     const int64_t ka = g.a.mn_major ? g.a.rows - g.a.row_off : g.a.cols;
-    const int64_t kbx = g.b.mn_major ? g.b.rows - g.b.row_off : g.b.cols;
+    const int64_t kbx = g.bq ? g.wq.cols : g.b.mn_major ? g.b.rows - g.b.row_off : g.b.cols;
     if (ka < g.K || kbx < g.K) return ALTXS_EINVAL;
     // a K slice reads 64 values: past K they must come from the bounds (zeros), not from stored data
     if (g.K % kBK && (ka != g.K || kbx != g.K)) return ALTXS_EINVAL;
@@ -661,7 +911,44 @@ int launch_tc(const TcArgs &a, cudaStream_t st) {
     g.ldp = a.ldp;
     g.status = a.status;
     g.status_stride = a.status_stride;
+    if (a.wq) {
+        g.bq = 1;
+        g.wq = *a.wq;
+        g.wq_row0 = a.row0;
+    }
+    g.splits = 1;
+    const int sp = tc_linear_splits(a.N, a.K);
+    if (sp > 1 && a.part && a.cnt) {
+        g.splits = sp;
+        g.part = a.part;
+        g.cnt = a.cnt;
+    }
     return launch_tc_gemm(g, st);
+}
+
+int tc_linear_splits(int N, int K) {
+    // No split.  Splitting the K loop of the layers with few output tiles
+    // (o and down at M <= 256: 16 tiles) into 2-4 ranges was measured on a
+    // B200 (ncu launch list of the 256-stream step, same box, A/B): the
+    // tensor-core linears took 1174 us per two steps with the split against
+    // 1123 us without, and the 2048-stream step lost 2 %: a call at these
+    // sizes is bound by its fixed costs (launch, set-up, pipeline fill,
+    // epilogue), not by its K loop, and the partials add traffic.
+    (void)N;
+    (void)K;
+    return 1;
+}
+
+int64_t tc_linear_part_elems(int M, int N, int K) {
+    const int s = tc_linear_splits(N, K);
+    if (s <= 1 || M <= 0 || N <= 0) return 0;
+    // tiles x splits x 128 x BN for the wider of the two tile widths' padding
+    return align_up(M, kBM) * align_up(N, 128) * s;
+}
+
+int64_t tc_linear_cnt_elems(int M, int N, int K) {
+    if (tc_linear_splits(N, K) <= 1 || M <= 0 || N <= 0) return 0;
+    return (int64_t)((M + kBM - 1) / kBM) * ((N + 63) / 64) * 4;  // 64-wide tiles: the most tiles
 }
 
 int set_wait_limit_tc(uint32_t limit) {
@@ -863,6 +1150,49 @@ int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo
     t.epi = kEpiStore;
     t.Y = Y;
     t.ldy = N;
+    return launch_tc(t, st);
+}
+
+int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return -1;
+    return altxs::align_up((int64_t)M * K * 2, 256) * 2 + altxs::align_up(altxs::tc_linear_part_elems(M, N, K) * 4, 256) +
+           altxs::align_up(altxs::tc_linear_cnt_elems(M, N, K) * 4, 256);
+}
+
+int altxs_linear_tc(const altxs_qmat *m, int row0, int N, const float *X, int M, float *Y, void *workspace,
+                    int64_t workspace_bytes, altxs_stream_t stream) {
+    using namespace altxs;
+    if (!m || !X || !Y || M < 0 || N < 0 || row0 < 0 || row0 + N > m->rows) return ALTXS_EINVAL;
+    if (M == 0 || N == 0) return ALTXS_OK;
+    const int K = m->cols;
+    if (!workspace || workspace_bytes < altxs_linear_tc_workspace_bytes(M, N, K)) return ALTXS_EINVAL;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char *p = static_cast<unsigned char *>(workspace);
+    uint16_t *xh = reinterpret_cast<uint16_t *>(p);
+    p += align_up((int64_t)M * K * 2, 256);
+    uint16_t *xl = reinterpret_cast<uint16_t *>(p);
+    p += align_up((int64_t)M * K * 2, 256);
+    float *part = reinterpret_cast<float *>(p);
+    p += align_up(tc_linear_part_elems(M, N, K) * 4, 256);
+    uint32_t *cnt = reinterpret_cast<uint32_t *>(p);
+    const int64_t nc = tc_linear_cnt_elems(M, N, K);
+    if (nc > 0 && cudaMemsetAsync(cnt, 0, nc * 4, st) != cudaSuccess) return ALTXS_ECUDA;
+    ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_rows<<<M, 256, 0, st>>>(X, K, K, xh, xl));
+    TcArgs t{};
+    t.a_hi = xh;
+    t.a_lo = xl;
+    t.lda = K;
+    t.M = M;
+    t.b_rows = m->rows;
+    t.row0 = row0;
+    t.N = N;
+    t.K = K;
+    t.epi = kEpiStore;
+    t.Y = Y;
+    t.ldy = N;
+    t.wq = m;
+    t.part = part;
+    t.cnt = cnt;
     return launch_tc(t, st);
 }
 

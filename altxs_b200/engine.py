@@ -25,7 +25,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, lockstep
 from .codec import ModelWeights, PackedMatrix
 from .config import ModelConfig
 from .lora import init_lora_A, lora_shapes, rope_tables
@@ -88,6 +88,7 @@ class DeviceModel:
         self._keep: list[torch.Tensor] = []
         packed = weights.packed()
         self.weight_bytes = sum(p.nbytes for p in packed.values())
+        self.weights_sha256 = lockstep.weights_digest(packed, weights.small)
         self.q = {k: self._qmat(v) for k, v in packed.items()}
         s = weights.small
         L = cfg.num_layers
@@ -287,6 +288,7 @@ class DeviceModel:
                 **{k: s[k].data_ptr() for k in ("smear_gate", "smear_lambda", "attn_gate_w", "softcap",
                                                 "parallel_post", "parallel_resid") if k in s},
                 emb_dense=self.params.data_ptr() + 4 * self.layout.emb if self.full_params else None,
+                planes_live=1 if self.full_params else 0,
             )
         return self._weights_struct
 
@@ -566,10 +568,13 @@ class ContextReset:
 class Engine:
     """Encode / decode many independent streams in lockstep on one GPU."""
 
-    def __init__(self, dm: DeviceModel, *, ttt=None, on_logits=None):
+    def __init__(self, dm: DeviceModel, *, ttt=None, on_logits=None, header: bool = True):
         self.dm = dm
         self.cfg = dm.cfg
         self.ttt = ttt  # optional callable(batch, rows, hist_end) for the boundary update
+        # payloads carry (and decoding checks) the lockstep fingerprint of the run
+        self.header = bool(header)
+        self.settings = lockstep.run_settings(dm, ttt is not None)
         self.reset = ContextReset(dm) if dm.cfg.context_mode == "reset" else None
         # optional callable(t, logits [n, V] on the device) after each encode step:
         # the logits every stream's symbol t was coded with (before the CDF rule)
@@ -635,8 +640,9 @@ class Engine:
         torch.cuda.synchronize(dev)
         b.check_status()
         out = []
+        head = lockstep.header_frame(self.settings) if self.header else b""
         for i in range(n):
-            payload = b"".join(struct.pack("<Q", len(p)) + p for p in segs[i])
+            payload = head + b"".join(struct.pack("<Q", len(p)) + p for p in segs[i])
             out.append(StreamResult(payload=payload, segments=segs[i], n_symbols=int(lens[i])))
         return out
 
@@ -666,7 +672,11 @@ class Engine:
         lens = np.asarray(n_symbols, dtype=np.int64)
         T = int(lens.max()) if n else 0
         every = max(1, int(cfg.online_retrain_every))
-        segs = [list(iter_framed_segments(p)) for p in payloads]
+        segs = []
+        for p in payloads:
+            enc_settings, fp, body = lockstep.split_header(p)
+            lockstep.check(enc_settings, fp, self.settings)  # raises on a mismatch
+            segs.append(list(iter_framed_segments(body)))
         for i in range(n):
             need = (int(lens[i]) + every - 1) // every
             if len(segs[i]) != need:

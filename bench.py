@@ -70,6 +70,9 @@ def parse_args():
     ap.add_argument("--cuda-cores", action="store_true",
                     help="run the step's linear layers on CUDA cores from the packed codes (the few-stream "
                          "choice: 0.43 bytes per weight read per step instead of the 4-byte tensor-core planes)")
+    ap.add_argument("--packed", type=int, default=None,
+                    help="1: the step's tensor-core linears expand the packed codes in the GEMM; 0: they read "
+                         "the dense hi/lo planes (same bits); default: the library's setting")
     ap.add_argument("--fusion", action="store_true",
                     help="with --cuda-cores and at most 4 streams per GPU: run each step as one fused "
                          "persistent kernel instead of a kernel per phase (same bits; measured slower)")
@@ -77,6 +80,10 @@ def parse_args():
                     help="instead of the decode benchmark: one full-parameter replenish boundary of the 33M "
                          "model (Forward-XM: gradient of every weight over an 18,432-token window, AdamW, "
                          "four candidate updates each scored on an 18,432-token probe window), one JSON line")
+    ap.add_argument("--lora-update", action="store_true",
+                    help="instead of the decode benchmark: one test-time LoRA boundary update (33M model, full "
+                         "window), for 1 and for --update-rows streams, one JSON line each")
+    ap.add_argument("--update-rows", type=int, default=8)
     ap.add_argument("--c2", action="store_true",
                     help="instead of the decode benchmark: the linear-layer microbenchmark (the C3 layer "
                          "shapes K x N at M = 1, 16, 128, 512 rows, tensor-core and CUDA-core paths), one "
@@ -326,8 +333,10 @@ def run_c2(args) -> None:
     """Linear-layer microbenchmark: Y = X W^T for the C3 layer shapes (layer 0
     of the benchmark model's qkv, o, up, down matrices; 3.15-bit mixed-bit
     weights + fp16 group scales) at M rows of N(0,1) activations.  Each timed
-    call is one ``altxs_linear`` (tensor cores: hi/lo split of X + tcgen05
-    GEMM; CUDA cores: packed-code GEMV/GEMM), CUDA events around the call, L2
+    call is one ``altxs_linear_tc`` (tensor cores as in the decode step: hi/lo
+    split of X + tcgen05 GEMM expanding the packed weights in its producer
+    warps) or ``altxs_linear`` (tensor_planes: the same GEMM on dense hi/lo
+    weight planes; CUDA cores: packed-code GEMV/GEMM), CUDA events around the call, L2
     flushed (256 MB written, then read) before every call, median of 20.  Roofline: HBM for
     M <= 64 on the algorithmic bytes K*N*3.40/8 + 2*M*K + 2*M*N (packed weights
     incl. scales, bf16 activations), tensor cores above on 2*M*K*N."""
@@ -353,15 +362,21 @@ def run_c2(args) -> None:
         for M in (1, 16, 128, 512, 2048):  # the C2 sizes, then the bench's per-GPU batch
             X = torch.randn(M, K, generator=g, device=dev)
             Y = torch.empty(M, N, device=dev)
-            wsb = int(L.altxs_linear_workspace_bytes(M, K))
+            wsb = int(max(L.altxs_linear_workspace_bytes(M, K), L.altxs_linear_tc_workspace_bytes(M, N, K)))
             ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-            for path in ("tensor", "cuda_core"):
-                hi = getattr(dm._split, f"{name}_hi") if path == "tensor" else None
-                lo = getattr(dm._split, f"{name}_lo") if path == "tensor" else None
+            # tensor: the step's linear (packed codes expanded in the GEMM, K split by layer
+            # shape); tensor_planes: the same GEMM streaming dense hi/lo bf16 weight planes
+            for path in ("tensor", "tensor_planes", "cuda_core"):
+                hi = getattr(dm._split, f"{name}_hi") if path == "tensor_planes" else None
+                lo = getattr(dm._split, f"{name}_lo") if path == "tensor_planes" else None
 
                 def call():
-                    rc = L.altxs_linear(ctypes.byref(q), hi, lo, 0, N, X.data_ptr(), M, Y.data_ptr(),
-                                        ws.data_ptr(), wsb, st)
+                    if path == "tensor":
+                        rc = L.altxs_linear_tc(ctypes.byref(q), 0, N, X.data_ptr(), M, Y.data_ptr(),
+                                               ws.data_ptr(), wsb, st)
+                    else:
+                        rc = L.altxs_linear(ctypes.byref(q), hi, lo, 0, N, X.data_ptr(), M, Y.data_ptr(),
+                                            ws.data_ptr(), wsb, st)
                     _lib.check(rc, "altxs_linear")
 
                 for _ in range(3):
@@ -487,6 +502,72 @@ def run_replenish(args) -> None:
     }), flush=True)
 
 
+def run_lora_update(args) -> None:
+    """One test-time LoRA boundary update of the benchmark's model (33M, rank-8
+    q/k/v/o + lm_head adapters) on the full 2047-token window, for 1 and for
+    --update-rows streams updated at the same boundary: CUDA events around
+    each update after a warm-up, the library's per-class launch profile, and
+    the launch count.  Tensor roofline: forward + input-gradient backward
+    through the frozen model, 4 x parameters x tokens + attention
+    (4 x T^2 x d x layers forward + backward, causal), over the bf16 peak."""
+    import ctypes
+
+    from altxs_b200 import _lib
+    from altxs_b200 import codec as C
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import DeviceModel, StreamBatch
+    from altxs_b200.synth import zipf_markov
+    from altxs_b200.ttt import LoraTTT
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = c3_config()
+    dm = DeviceModel(C.synth_weights(cfg, seed=WEIGHT_SEED), dev, tensor_cores=not args.cuda_cores)
+    peaks, kind = load_peaks()
+    L = _lib.lib()
+    every, ctx = cfg.online_retrain_every, cfg.ctx
+    T = ctx - 1
+    ncls = len(_lib.KERNEL_CLASSES)
+    for rows_n in sorted({1, max(1, args.update_rows)}):
+        b = StreamBatch(dm, rows_n, words_per_stream=8, hist_len=ctx + 2)
+        data = zipf_markov(ctx + 2, cfg.vocab_size, 1000 + np.arange(rows_n))
+        idx = torch.arange(every - ctx - 1, every, device=dev) % b.hist_len
+        b.hist[:, idx] = torch.as_tensor(data[:, : ctx + 1].astype(np.int32), device=dev)
+        ttt = LoraTTT(dm)
+        rows = list(range(rows_n))
+        ttt(b, rows, every)  # warm-up (and first AdamW step)
+        torch.cuda.synchronize()
+        times = []
+        for k in range(max(1, min(args.steps, 5))):
+            n0 = L.altxs_launch_count()
+            if k == 0:
+                L.altxs_profile(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ttt(b, rows, every)
+            e1.record()
+            torch.cuda.synchronize()
+            if k == 0:
+                L.altxs_profile(0)
+                launches = L.altxs_launch_count() - n0
+            times.append(e0.elapsed_time(e1))
+        pms = (ctypes.c_double * ncls)()
+        pcnt = (ctypes.c_int64 * ncls)()
+        L.altxs_profile_read(ncls, pms, pcnt)
+        ms = statistics.median(times[1:] if len(times) > 1 else times)
+        P = 33554432
+        flops = rows_n * (4.0 * P * T + 4.0 * T * T * cfg.model_dim * cfg.num_layers)
+        tf = flops / (ms / 1e3) / 1e12
+        print(json.dumps({
+            "lora_update": True, "rows": rows_n, "window_tokens": T, "ms": ms, "ms_per_row": ms / rows_n,
+            "launches": int(launches), "tflops": tf, "frac": tf / peaks["bf16_tflops"],
+            "peak_source": f"{kind} bf16_tflops",
+            "breakdown_ms": {name: pms[i] for i, name in enumerate(_lib.KERNEL_CLASSES) if pcnt[i]},
+            "breakdown_launches": {name: int(pcnt[i]) for i, name in enumerate(_lib.KERNEL_CLASSES) if pcnt[i]},
+            "linear": "CUDA cores" if args.cuda_cores else "tensor cores",
+        }), flush=True)
+
+
 def config_block(world: int, streams: int, cuda_cores: bool = False, fusion: bool = False) -> dict:
     return {
         "workload": f"{'box-scale sharded' if streams > 1 else 'single-stream'} decode: {streams} independent "
@@ -534,6 +615,10 @@ def main():
         if rank == 0:
             run_replenish(args)
         return
+    if args.lora_update:
+        if rank == 0:
+            run_lora_update(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
@@ -567,6 +652,8 @@ def main():
     dm = DeviceModel(w, dev, rope_positions=cfg.ctx + chunk + 8, tensor_cores=not args.cuda_cores)
     if args.fusion:
         _lib.check(_lib.lib().altxs_set_step_fusion(4), "altxs_set_step_fusion")
+    if args.packed is not None:
+        _lib.check(_lib.lib().altxs_set_linear_packed(args.packed), "altxs_set_linear_packed")
     gids = np.arange(rank * n_local, (rank + 1) * n_local)
     data = zipf_markov(cfg.ctx + chunk, cfg.vocab_size, 1000 + gids)  # [n][T]
     symsT = torch.from_numpy(np.ascontiguousarray(data.T)).to(dev)     # [T][n]

@@ -30,6 +30,7 @@ extern "C" {
 #define ALTXS_ENOTSUP (-95)
 #define ALTXS_ECUDA (-5)
 #define ALTXS_ENOMEM (-12)
+#define ALTXS_EMISMATCH (-71) /* decoder settings differ from the encoder's (altxs_set_lockstep) */
 
 /* per-stream device status bits (altxs_ac_state.status) */
 #define ALTXS_ST_OVERFLOW 1u    /* bit buffer full: further bits dropped */
@@ -184,9 +185,11 @@ typedef struct altxs_weights {
     int64_t rope_positions;
     /* NULL: the step's linear layers run on CUDA cores in exact fp32 order
      * (sum over 64-wide groups of scale * sum of level*x).  Non-NULL: they run
-     * on the tensor cores from these planes (products within 2^-16 relative).
-     * Either way results do not depend on the batch; an encoder and its
-     * decoder must make the same choice. */
+     * on the tensor cores (products within 2^-16 relative), expanding the
+     * packed codes of the five matrices in the GEMM's producer warps; the
+     * planes themselves are read only with planes_live (below) and by the
+     * test-time updates.  Either way results do not depend on the batch; an
+     * encoder and its decoder must make the same choice. */
     const altxs_split_planes *split;
     /* motif parameters (device; NULL when the motif is off) */
     const float *smear_gate;     /* [gate_window] */
@@ -199,6 +202,12 @@ typedef struct altxs_weights {
      * the emb codes).  A model whose weights change (full-parameter replenish)
      * points it at its parameter arena and refreshes split with altxs_split_params. */
     const float *emb_dense;
+    /* 1: the tensor-core linears read the split planes instead of the packed
+     * codes, because the planes hold weights updated after loading (a
+     * full-parameter model's arena, re-split by altxs_split_params); 0: the
+     * planes equal the codes and the codes are read (0.43 instead of 4 bytes
+     * per weight). */
+    int32_t planes_live;
 } altxs_weights;
 
 /* Per-stream state and scratch of a batch of n streams.  Stream i of the
@@ -315,6 +324,19 @@ int altxs_gemm(int M, int N, int K, const float *A, int64_t lda, int64_t sA, int
 int64_t altxs_linear_workspace_bytes(int M, int K);
 int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo, int row0, int N, const float *X,
                  int M, float *Y, void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+
+/* The layer on the tensor cores with the weights read as packed 2/3/4-bit
+ * codes and fp16 group scales (the reference's mixed-bit GEMV/GEMM, altxs
+ * src/xsa_ttt/ac_gemv.py:27 _gemv_row_tiles, on the format of
+ * src/hyperflow_distillation/mixed_bit_delta.py:96-229): the GEMM's own
+ * producer warps expand each 64-wide group slice in shared memory into the
+ * hi/lo bf16 operands (no dense copy of the weights is read), so the result
+ * is bit-identical to altxs_linear with the planes.  The decode step takes
+ * this path under altxs_set_linear_packed(1).  Needs
+ * altxs_linear_tc_workspace_bytes(M, N, m->cols) of device workspace. */
+int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K);
+int altxs_linear_tc(const altxs_qmat *m, int row0, int N, const float *X, int M, float *Y, void *workspace,
+                    int64_t workspace_bytes, altxs_stream_t stream);
 
 /* Segment-reset context (the reference's reset_segment, altxs
  * src/xsa_ttt/incremental.py:858-897, with _chunk_ctx_start, compress.py:122-125):
@@ -449,8 +471,21 @@ int altxs_ttt_boundary(altxs_ctx *ctx, altxs_stream_t stream);
  * (device, segment k of stream i = the first nbits[i] bits of row i, MSB-first);
  * the coders restart for the next segment. */
 int altxs_flush(altxs_ctx *ctx, uint32_t *d_bits, uint64_t *d_nbits, altxs_stream_t stream);
-/* Load one segment per stream and seed the decoders. */
+/* Load one segment per stream and seed the decoders.  Returns ALTXS_EMISMATCH
+ * (loading nothing) when an expected lockstep id was set and differs. */
 int altxs_begin_decode(altxs_ctx *ctx, const uint32_t *d_bits, const uint64_t *d_nbits, altxs_stream_t stream);
+/* Lockstep identity of a context: a 64-bit hash of everything that changes
+ * the coded bits (model description, layer schedule, linear path, segment
+ * length, update hyper-parameters, the caller's weights_id and the library's
+ * numerics version).  An encoder stores altxs_lockstep_id with its payload; a
+ * decoder passes it as expect_id, and altxs_begin_decode then refuses a
+ * context that would decode with other settings instead of desyncing.
+ * weights_id identifies the weights (e.g. a hash of the codec file); 0 is
+ * allowed.  The reference has no such check: its decoder silently desyncs
+ * when a config field or environment switch differs (src/xsa_ttt/config.py:
+ * 271-420). */
+int altxs_set_lockstep(altxs_ctx *ctx, uint64_t weights_id, uint64_t expect_id);
+int altxs_lockstep_id(altxs_ctx *ctx, uint64_t *id);
 /* Waits; status (host [n] or NULL) gets each stream's status word; returns their OR. */
 int altxs_get_status(altxs_ctx *ctx, int32_t *status);
 int64_t altxs_ctx_words_per_stream(const altxs_ctx *ctx);
@@ -480,6 +515,12 @@ uint32_t altxs_default_wait_limit(void);
  * (max_streams 0): measured slower than the CUDA-graph replay of the
  * launch-per-phase step on a B200.  Process-wide. */
 int altxs_set_step_fusion(int max_streams);
+
+/* Operand source of the step's tensor-core linears: 1 = the packed codes,
+ * expanded in the GEMM's producer warps; 0 (default) = the dense hi/lo bf16
+ * planes.  Both feed the tensor cores the same values in the same order, so
+ * the results are bit-identical; only the speed differs.  Process-wide. */
+int altxs_set_linear_packed(int on);
 
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these

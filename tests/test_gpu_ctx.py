@@ -141,3 +141,25 @@ def test_context_api_refuses_misuse():
     assert L.altxs_step_encode(h, tok.data_ptr(), s) == _lib.ALTXS_EINVAL  # no streams yet
     assert L.altxs_streams_init(h, 2, None) == _lib.ALTXS_EINVAL           # no weights, no segment size
     L.altxs_destroy(h)
+
+
+def test_context_refuses_a_decoder_with_other_settings():
+    """The encoder's lockstep id given to a decoder context on the other
+    linear path (or with other weights) makes altxs_begin_decode refuse
+    (ALTXS_EMISMATCH) instead of desyncing; the matching context accepts."""
+    from altxs_b200.engine import DeviceModel
+
+    cfg = ModelConfig(**CFG)
+    dm = DeviceModel(CO.synth_weights(cfg, seed=7), DEV)
+    enc = Ctx(dm, 2, True)
+    L = enc.L
+    assert L.altxs_set_lockstep(enc.h, 1234, 0) == 0
+    eid = C.c_uint64(0)
+    assert L.altxs_lockstep_id(enc.h, C.byref(eid)) == 0 and eid.value != 0
+    enc.close()
+    for tensor_cores, wid, ok in ((False, 1234, False), (True, 99, False), (True, 1234, True)):
+        dec = Ctx(dm, 2, tensor_cores)
+        assert L.altxs_set_lockstep(dec.h, wid, eid.value) == 0
+        rc = L.altxs_begin_decode(dec.h, dec.bits.data_ptr(), dec.nbits.data_ptr(), dec.s)
+        assert rc == (0 if ok else -71), (tensor_cores, wid, rc)
+        dec.close()

@@ -153,3 +153,73 @@ def test_rows_do_not_depend_on_tile_width():
         for i in (0, 700, 2047):
             alone = _linear(dm, name, X[i: i + 1], 0, N, True)
             assert np.array_equal(alone.view(np.uint32), full[i: i + 1].view(np.uint32)), (name, i)
+
+
+def _linear_tc(dm, name, X, row0, N):
+    """The step's tensor-core linear: packed weights expanded by the GEMM's
+    producer warps, K split by layer shape."""
+    from altxs_b200 import _lib
+
+    L = _lib.lib()
+    q = dm.q[name]
+    M = X.shape[0]
+    Xd = torch.as_tensor(X, device=DEV).contiguous()
+    Y = torch.full((M, N), float("nan"), dtype=torch.float32, device=DEV)
+    ws_b = int(L.altxs_linear_tc_workspace_bytes(M, N, q.cols))
+    ws = torch.empty(max(ws_b, 1), dtype=torch.uint8, device=DEV)
+    assert L.altxs_linear_tc(C.byref(q), row0, N, Xd.data_ptr(), M, Y.data_ptr(), ws.data_ptr(), ws_b, None) == 0
+    torch.cuda.synchronize()
+    return Y.cpu().numpy()
+
+
+@pytest.mark.parametrize("name,row0,N,M", [("qkv", 0, 512, 1), ("qkv", 512, 512, 130), ("down", 256, 256, 300),
+                                          ("down", 0, 256, 1), ("emb", 0, 1000, 77), ("up", 1024, 136, 5),
+                                          ("o", 0, 256, 260)])
+def test_packed_weight_gemm_matches_planes_and_float64(model, name, row0, N, M):
+    """Expanding the packed codes in the GEMM's producer warps gives the same
+    products as the dequantised planes: bit-identical output (where a layer's
+    K loop is split the bits may differ: then within the tensor-core bound of
+    float64, which every output meets)."""
+    from altxs_b200 import _lib
+
+    W = _dense(model, name)
+    rng = np.random.default_rng(M + N + 1)
+    X = rng.normal(0, 1, size=(M, W.shape[1])).astype(np.float32)
+    got = _linear_tc(model, name, X, row0, N)
+    planes = _linear(model, name, X, row0, N, True)
+    assert np.all(np.isfinite(got))
+    if _lib.lib().altxs_linear_tc_workspace_bytes(M, N, W.shape[1]) == _lib.lib().altxs_linear_workspace_bytes(
+            M, W.shape[1]):  # no split scratch: the layer is not split
+        assert np.array_equal(got.view(np.uint32), planes.view(np.uint32)), name
+    ref = X.astype(np.float64) @ W[row0: row0 + N].T
+    bound = np.abs(X.astype(np.float64)) @ np.abs(W[row0: row0 + N]).T
+    assert np.all(np.abs(got - ref) <= 2.0 ** -15 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("name,N", [("qkv", 1536), ("o", 512), ("down", 512), ("up", 2048), ("emb", 16384)])
+def test_packed_weight_gemm_rows_do_not_depend_on_the_batch(name, N):
+    """33M shapes (split o and down layers included): rows of a 2048-row call
+    and of a 256-row call equal the rows computed alone, bit for bit."""
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import DeviceModel
+
+    dm = DeviceModel(Cd.synth_weights(c3_config(), seed=5), DEV)
+    K = dm.q[name].cols
+    rng = np.random.default_rng(11)
+    X = rng.normal(0, 1, size=(2048, K)).astype(np.float32)
+    full = _linear_tc(dm, name, X, 0, N)
+    part = _linear_tc(dm, name, X[:256], 0, N)
+    assert np.array_equal(part.view(np.uint32), full[:256].view(np.uint32)), name
+    for i in (0, 129, 2047):
+        alone = _linear_tc(dm, name, X[i: i + 1], 0, N)
+        assert np.array_equal(alone.view(np.uint32), full[i: i + 1].view(np.uint32)), (name, i)
+    from altxs_b200 import _lib
+
+    L = _lib.lib()
+    if L.altxs_linear_tc_workspace_bytes(2048, N, K) == L.altxs_linear_workspace_bytes(2048, K):
+        planes = _linear(dm, name, X, 0, N, True)  # unsplit layer: the same bits as the plane path
+        assert np.array_equal(full.view(np.uint32), planes.view(np.uint32)), name
+    W = _dense(dm, name)
+    ref = X[:64].astype(np.float64) @ W[:N].T
+    bound = np.abs(X[:64].astype(np.float64)) @ np.abs(W[:N]).T
+    assert np.all(np.abs(full[:64] - ref) <= 2.0 ** -15 * bound + 1e-30)

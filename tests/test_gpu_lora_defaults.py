@@ -114,4 +114,4 @@ def test_engine_round_trip_with_default_adapters(tensor_cores):
     for s, d in zip(streams, dec):
         assert np.array_equal(s, d)
     plain = Engine(dm).encode(streams)
-    assert any(a.payload != b.payload for a, b in zip(enc, plain))
+    assert any(a.segments != b.segments for a, b in zip(enc, plain))

@@ -129,4 +129,4 @@ def test_motif_lora_round_trip(tensor_cores):
     for s, d in zip(streams, dec):
         assert np.array_equal(s, d)
     plain = Engine(dm).encode(streams)
-    assert any(a.payload != b.payload for a, b in zip(enc, plain))
+    assert any(a.segments != b.segments for a, b in zip(enc, plain))
