@@ -72,6 +72,14 @@ class SplitPlanes(C.Structure):
     _fields_ = [(f"{m}_{h}", C.c_void_p) for m in ("emb", "qkv", "o", "up", "down") for h in ("hi", "lo")]
 
 
+class QTiles(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("rows", C.c_int32), ("cols", C.c_int32)]
+
+
+class TileWeights(C.Structure):
+    _fields_ = [(k, QTiles) for k in ("emb", "qkv", "o", "up", "down")]
+
+
 class Weights(C.Structure):
     _fields_ = [
         ("emb", QMat), ("qkv", QMat), ("o", QMat), ("up", QMat), ("down", QMat),
@@ -81,7 +89,7 @@ class Weights(C.Structure):
         ("rope_positions", C.c_int64), ("split", C.POINTER(SplitPlanes)),
         ("smear_gate", C.c_void_p), ("smear_lambda", C.c_void_p), ("attn_gate_w", C.c_void_p),
         ("softcap", C.c_void_p), ("parallel_post", C.c_void_p), ("parallel_resid", C.c_void_p),
-        ("emb_dense", C.c_void_p), ("planes_live", C.c_int32),
+        ("emb_dense", C.c_void_p), ("planes_live", C.c_int32), ("tiles", C.POINTER(TileWeights)),
     ]
 
 
@@ -164,7 +172,7 @@ def lib():
             "altxs_linear_workspace_bytes": (i64, [C.c_int, C.c_int]),
             "altxs_linear": (C.c_int, [C.POINTER(QMat), vp, vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
             "altxs_linear_tc_workspace_bytes": (i64, [C.c_int, C.c_int, C.c_int]),
-            "altxs_linear_tc": (C.c_int, [C.POINTER(QMat), C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
+            "altxs_linear_tc": (C.c_int, [C.POINTER(QTiles), C.c_int, C.c_int, vp, C.c_int, vp, vp, i64, vp]),
             "altxs_gemm_workspace_bytes": (i64, [C.c_int] * 6),
             "altxs_param_layout_of": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(ParamLayout)]),
             "altxs_create": (vp, [C.POINTER(ModelDesc), C.c_int, C.POINTER(C.c_int)]),

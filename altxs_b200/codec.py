@@ -219,6 +219,51 @@ def pack_matrix(m: GroupMatrix) -> PackedMatrix:
     )
 
 
+TILE_ROWS = 64
+TILE_SEG = 256 + TILE_ROWS * 32  # 64 group descriptors, then up to 64 groups of <= 32 code bytes
+
+
+def tile_stream(p: PackedMatrix) -> np.ndarray | None:
+    """The packed codes re-laid for the tensor-core GEMM's producer: one
+    fixed-size segment of TILE_SEG bytes per (64-row block, 64-wide group),
+    ``[ceil(rows/64)][cols/64][TILE_SEG]`` uint8, so that a tile's K slice is
+    one bulk copy with no table lookups.  Segment = 64 uint32 descriptors
+    (fp16 scale | width code << 16 | offset of the row's code bytes within the
+    segment's code area, 8-byte units, << 20) followed by the rows' code
+    bytes (8*b each, as in the packed rows).  Rows past the matrix are 0-bit
+    groups.  None when a group is not 0/2/3/4-bit symmetric (codebook or
+    exact fp32 groups): such matrices keep the dense planes."""
+    if p.lut is not None:
+        return None
+    rows, cols = p.rows, p.cols
+    G = cols // GROUP
+    wcode = ((p.gdesc >> 16) & 15).astype(np.int64)
+    if np.any(wcode > 3):
+        return None
+    size = np.array([0, 16, 24, 32], dtype=np.int64)[wcode]  # [rows, G] bytes
+    RB = (rows + TILE_ROWS - 1) // TILE_ROWS
+    pad = RB * TILE_ROWS - rows
+    size_p = np.pad(size, ((0, pad), (0, 0)))
+    desc_p = np.pad(p.gdesc.astype(np.int64), ((0, pad), (0, 0)))
+    # [RB, 64, G] -> offsets of each row's bytes within its (block, group) segment
+    sz = size_p.reshape(RB, TILE_ROWS, G)
+    off = np.cumsum(sz, axis=1) - sz  # exclusive, bytes
+    tdesc = (desc_p.reshape(RB, TILE_ROWS, G) & 0xFFFF) | (np.pad(wcode, ((0, pad), (0, 0))).reshape(
+        RB, TILE_ROWS, G) << 16) | ((off // 8) << 20)
+    out = np.zeros((RB, G, TILE_SEG), dtype=np.uint8)
+    out[:, :, :256] = np.ascontiguousarray(tdesc.transpose(0, 2, 1)).astype("<u4").view(np.uint8).reshape(RB, G, 256)
+    # code bytes: source [row_off8 + goff] * 8 in the packed rows
+    r_idx, g_idx = np.nonzero(size > 0)
+    if r_idx.size:
+        n = size[r_idx, g_idx]
+        src0 = (p.row_off8[r_idx].astype(np.int64) + (p.gdesc[r_idx, g_idx].astype(np.int64) >> 20)) * 8
+        dst0 = ((r_idx // TILE_ROWS) * G + g_idx) * TILE_SEG + 256 + off.reshape(RB * TILE_ROWS, G)[r_idx, g_idx]
+        rep = np.repeat(np.arange(r_idx.size), n)
+        within = np.arange(rep.size) - np.repeat(np.cumsum(n) - n, n)
+        out.reshape(-1)[dst0[rep] + within] = p.codes[src0[rep] + within]
+    return out
+
+
 # ---------------------------------------------------------------------------
 # model weights
 # ---------------------------------------------------------------------------

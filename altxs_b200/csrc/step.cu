@@ -1401,7 +1401,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     }
     // one linear layer: tensor cores from the bf16 planes, or CUDA cores from the packed codes
     auto linear = [&](const QmmArgs &q, const uint16_t *xh, const uint16_t *xl, const uint16_t *wh, const uint16_t *wl,
-                      uint16_t *ph, uint16_t *pl) -> int {
+                      uint16_t *ph, uint16_t *pl, const altxs_qtiles *wt) -> int {
         if (!c.tc) return launch_qmm(q, st);
         TcArgs t{};
         t.a_hi = xh;
@@ -1429,7 +1429,8 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
             t.status = &b->ac[0].status;
             t.status_stride = sizeof(altxs_ac_state) / sizeof(uint32_t);
         }
-        if (!w->planes_live && g_linear_packed) t.wq = &q.W;  // the producer warps expand B from the codes
+        // the producer warps expand B from the packed codes
+        if (!w->planes_live && g_linear_packed && wt && q.row0 % 64 == 0) t.wt = wt;
         t.part = c.tcpart;
         t.cnt = c.tccnt;
         return launch_tc(t, st);
@@ -1471,7 +1472,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.Y = c.qkv;
         a.ldy = D.qkv_n;
         a.epi = kEpiStore;
-        if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->qkv_hi : nullptr, c.tc ? sp->qkv_lo : nullptr, nullptr, nullptr))) return rc;
+        if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->qkv_hi : nullptr, c.tc ? sp->qkv_lo : nullptr, nullptr, nullptr, w->tiles ? &w->tiles->qkv : nullptr))) return rc;
         ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, app));
         {
             cudaError_t ae = cudaSuccess;
@@ -1485,7 +1486,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.N = D.d;
         a.Y = c.ao;
         a.ldy = D.d;
-        if ((rc = linear(a, c.y_h, c.y_l, c.tc ? sp->o_hi : nullptr, c.tc ? sp->o_lo : nullptr, nullptr, nullptr))) return rc;
+        if ((rc = linear(a, c.y_h, c.y_l, c.tc ? sp->o_hi : nullptr, c.tc ? sp->o_lo : nullptr, nullptr, nullptr, w->tiles ? &w->tiles->o : nullptr))) return rc;
         // two-lane applications normed lane 1 for the MLP in k_prenorm
         if (!par)
             ALTXS_LAUNCH(::altxs::kKPostAttn, st, k_post_attn<<<D.n, 128, (D.r > 0 ? D.r : 1) * 4, st>>>(c, l, v));
@@ -1496,7 +1497,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.Y = c.hid;
         a.ldy = D.F;
         a.epi = kEpiLeaky2;
-        if ((rc = linear(a, c.nrm2_h, c.nrm2_l, c.tc ? sp->up_hi : nullptr, c.tc ? sp->up_lo : nullptr, c.tc ? c.hid_h : nullptr, c.tc ? c.hid_l : nullptr))) return rc;
+        if ((rc = linear(a, c.nrm2_h, c.nrm2_l, c.tc ? sp->up_hi : nullptr, c.tc ? sp->up_lo : nullptr, c.tc ? c.hid_h : nullptr, c.tc ? c.hid_l : nullptr, w->tiles ? &w->tiles->up : nullptr))) return rc;
         a.X = c.hid;
         a.ldx = D.F;
         a.W = w->down;
@@ -1520,7 +1521,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
             a.Y2 = skip_out;
             a.ldy2 = D.d;
         }
-        if ((rc = linear(a, c.hid_h, c.hid_l, c.tc ? sp->down_hi : nullptr, c.tc ? sp->down_lo : nullptr, nullptr, nullptr))) return rc;
+        if ((rc = linear(a, c.hid_h, c.hid_l, c.tc ? sp->down_hi : nullptr, c.tc ? sp->down_lo : nullptr, nullptr, nullptr, w->tiles ? &w->tiles->down : nullptr))) return rc;
         if (par)
             ALTXS_LAUNCH(::altxs::kKPostAttn, st,
                          k_par_combine<<<D.n, 128, 2 * (D.r > 0 ? D.r : 1) * 4, st>>>(c, l, v));
@@ -1539,7 +1540,7 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     a.Y = c.logits;
     a.ldy = D.V;
     a.epi = kEpiStore;
-    if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->emb_hi : nullptr, c.tc ? sp->emb_lo : nullptr, nullptr, nullptr))) return rc;
+    if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->emb_hi : nullptr, c.tc ? sp->emb_lo : nullptr, nullptr, nullptr, w->tiles ? &w->tiles->emb : nullptr))) return rc;
     ALTXS_LAUNCH(::altxs::kKCdfCode, st, k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode));
     return ALTXS_OK;
 }

@@ -35,14 +35,21 @@ constexpr int kBM = 128;         // tile rows = tensor-memory lanes
 constexpr int kBK = 64;          // K per stage: one 128-byte swizzle row of bf16
 constexpr unsigned kFull = 0xffffffffu;
 
-template <int BN, int AMN, int BMN>
+constexpr int kSeg = 2304;  // one packed-code segment: 64 descriptors + up to 64 x 32 code bytes
+
+template <int BN, int AMN, int BMN, int BQ = 0>
 struct TcCfg {
     static constexpr int kATile = kBM * kBK * 2;  // bytes of one A plane tile
     static constexpr int kBTile = BN * kBK * 2;   // bytes of one B plane tile
-    static constexpr int kStage = 2 * kATile + 2 * kBTile;
-    static constexpr int kStages = (192 * 1024) / kStage;  // BN 64: 4, 128: 3
-    static constexpr int kStore = 4 * 32 * 32 * 4;          // one 32 x 32 fp32 store block per epilogue warp
+    // packed weights: the tile's code segments (one per 64 rows) land here first
+    static constexpr int kStg = BQ ? (BN / 64) * kSeg : 0;
+    static constexpr int kStage = (2 * kATile + 2 * kBTile + kStg + 1023) / 1024 * 1024;
+    static constexpr int kStages = BQ ? (BN == 64 ? 4 : 3) : (192 * 1024) / kStage;  // BN 64: 4, 128: 3
+    // epilogue buffer: a 32 x 32 fp32 TMA-store box per warp, or the padded
+    // 32 x 33 transpose block of the plain-store path (never both in one launch)
+    static constexpr int kStore = 4 * 32 * 33 * 4;
     static constexpr int kSmem = kStages * kStage + kStore + 1024;  // + alignment slack
+    static_assert(kSmem + 256 <= 227 * 1024, "shared memory");
     static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
     // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B,
     // A/B major-ness, M = 128, N = BN
@@ -140,9 +147,8 @@ __device__ __forceinline__ float leaky2(float v) {  // leaky_relu(v, 0.5)^2 (mod
 // (j ^ (r & 7)) (the 128-byte swizzle TMA would have produced).  The values
 // are those of k_split_weights: w = level * scale, hi = bf16(w), lo = bf16(w - hi).
 struct DqGroup {
-    uint32_t d;            // group descriptor
-    uint64_t w[4];         // packed codes (up to 4 x 64 bits: 2/3/4-bit groups)
-    const uint8_t *gp;     // the group's code bytes
+    uint32_t d;     // group descriptor
+    uint32_t w[8];  // packed codes (up to 8 x 32 bits: 2/3/4-bit groups)
 };
 
 __device__ __forceinline__ int dq_bits(uint32_t d) {
@@ -150,50 +156,57 @@ __device__ __forceinline__ int dq_bits(uint32_t d) {
     return c == 0 ? 0 : c == 1 ? 2 : c == 2 ? 3 : c == 3 ? 4 : 32;
 }
 
-__device__ __forceinline__ void dq_fetch(const altxs_qmat &W, int64_t wrow, int kb, uint32_t row_off8, DqGroup &q) {
-    const int G = W.cols >> 6;
-    q.d = __ldg(W.gdesc + wrow * G + kb);
-    q.gp = W.codes + 8ull * ((uint64_t)row_off8 + (q.d >> 20));
+// the row's descriptor and code words from its staged segment (shared memory)
+__device__ __forceinline__ void dq_load(const unsigned char *seg, int j, DqGroup &q) {
+    q.d = reinterpret_cast<const uint32_t *>(seg)[j];
+    const uint2 *p = reinterpret_cast<const uint2 *>(seg + 256 + 8 * (q.d >> 20));
     const int b = dq_bits(q.d);
-    const uint64_t *p = reinterpret_cast<const uint64_t *>(q.gp);
-    if (b >= 2 && b <= 4) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) q.w[j] = j < b ? __ldg(p + j) : 0ull;
+    for (int w = 0; w < 4; ++w) {
+        const uint2 x = w < b ? p[w] : make_uint2(0u, 0u);
+        q.w[2 * w] = x.x;
+        q.w[2 * w + 1] = x.y;
     }
 }
 
+// 8 values -> one 16-byte chunk of the hi plane and of the lo plane
+// (hi = bf16(v), lo = bf16(v - hi), round to nearest even, two values per cvt)
 __device__ __forceinline__ void dq_put8(unsigned char *hrow, unsigned char *lrow, int pos, const float *f) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-        const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * u]), h1 = __float2bfloat16_rn(f[2 * u + 1]);
-        const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(f[2 * u], __bfloat162float(h0)));
-        const __nv_bfloat16 l1 = __float2bfloat16_rn(__fsub_rn(f[2 * u + 1], __bfloat162float(h1)));
-        h[u] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-        l[u] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(f[2 * u], f[2 * u + 1]);
+        h[u] = *reinterpret_cast<const uint32_t *>(&hb);
+        const float r0 = __fsub_rn(f[2 * u], __uint_as_float(h[u] << 16));
+        const float r1 = __fsub_rn(f[2 * u + 1], __uint_as_float(h[u] & 0xffff0000u));
+        const __nv_bfloat162 lb = __floats2bfloat162_rn(r0, r1);
+        l[u] = *reinterpret_cast<const uint32_t *>(&lb);
     }
     *reinterpret_cast<uint4 *>(hrow + pos) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4 *>(lrow + pos) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// w = (code - (2^B - 1)/2) * scale, exact in fp32 (a <= 4-bit half-integer
+// times an fp16 scale).  The code becomes a float by its bits (2^23 + code),
+// and fma(2^23 + code, s, -2^23 s) = code * s exactly; code * s - c * s is then
+// the same exact value the plane builder forms as (code - c) * s.
 template <int B, int N1>
-__device__ __forceinline__ void dq_codes(const DqGroup &q, const altxs_qmat &W, int64_t wrow, int kb, int i0,
-                                         unsigned char *hrow, unsigned char *lrow, int r7) {
+__device__ __forceinline__ void dq_codes(const DqGroup &q, int i0, unsigned char *hrow, unsigned char *lrow, int r7) {
     const float s = h2f((uint16_t)(q.d & 0xffffu));
-    const float center = (float)((1 << B) - 1) * 0.5f;
-    const uint16_t *lut = W.lut ? W.lut + 16ull * __ldg(W.glut + wrow * (W.cols >> 6) + kb) : nullptr;
+    const float k1 = __fmul_rn(-8388608.0f, s);
+    const float cs = __fmul_rn((float)((1 << B) - 1) * 0.5f, s);
 #pragma unroll
     for (int c = 0; c < N1 / 8; ++c) {
         float f[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            const int i = i0 + c * 8 + u;  // i0 is 0 or 32: the bit positions below fold to constants per case
-            const int bp = i * B, wi = bp >> 6, sh = bp & 63;
-            uint64_t v = q.w[wi] >> sh;
-            if (sh + B > 64) v |= q.w[wi + 1] << (64 - sh);
-            const uint32_t code = (uint32_t)v & ((1u << B) - 1u);
-            const float lev = lut ? h2f(__ldg(lut + code)) : __fsub_rn((float)code, center);
-            f[u] = __fmul_rn(lev, s);
+            const int i = i0 + c * 8 + u;  // i0 is a literal 0 or 32: bit positions fold to constants
+            const int bp = i * B, wi = bp >> 5, sh = bp & 31;
+            uint32_t v;
+            if (sh + B <= 32) v = q.w[wi] >> sh;
+            else v = __funnelshift_r(q.w[wi], q.w[wi + 1], sh);
+            const uint32_t code = v & ((1u << B) - 1u);
+            f[u] = __fsub_rn(__fmaf_rn(__uint_as_float(0x4B000000u | code), s, k1), cs);
         }
         const int j = (i0 >> 3) + c;
         dq_put8(hrow, lrow, (j ^ r7) << 4, f);
@@ -201,31 +214,23 @@ __device__ __forceinline__ void dq_codes(const DqGroup &q, const altxs_qmat &W, 
 }
 
 template <int N1>
-__device__ __forceinline__ void dq_slice(const DqGroup &q, const altxs_qmat &W, int64_t wrow, int kb, int i0,
-                                         unsigned char *hrow, unsigned char *lrow, int r7) {
+__device__ __forceinline__ void dq_slice(const DqGroup &q, int i0, unsigned char *hrow, unsigned char *lrow, int r7) {
     const int b = dq_bits(q.d);
     if (b == 2) {
-        if (i0 == 0) dq_codes<2, N1>(q, W, wrow, kb, 0, hrow, lrow, r7);
-        else dq_codes<2, N1>(q, W, wrow, kb, 32, hrow, lrow, r7);
+        if (i0 == 0) dq_codes<2, N1>(q, 0, hrow, lrow, r7);
+        else dq_codes<2, N1>(q, 32, hrow, lrow, r7);
     } else if (b == 3) {
-        if (i0 == 0) dq_codes<3, N1>(q, W, wrow, kb, 0, hrow, lrow, r7);
-        else dq_codes<3, N1>(q, W, wrow, kb, 32, hrow, lrow, r7);
+        if (i0 == 0) dq_codes<3, N1>(q, 0, hrow, lrow, r7);
+        else dq_codes<3, N1>(q, 32, hrow, lrow, r7);
     } else if (b == 4) {
-        if (i0 == 0) dq_codes<4, N1>(q, W, wrow, kb, 0, hrow, lrow, r7);
-        else dq_codes<4, N1>(q, W, wrow, kb, 32, hrow, lrow, r7);
-    } else {
-        // 0-bit group (zeros) or an exact fp32 group
-        const float *dense = reinterpret_cast<const float *>(q.gp);
-#pragma unroll 1
-        for (int c = 0; c < N1 / 8; ++c) {
-            float f[8];
+        if (i0 == 0) dq_codes<4, N1>(q, 0, hrow, lrow, r7);
+        else dq_codes<4, N1>(q, 32, hrow, lrow, r7);
+    } else {  // 0-bit group: zeros
+        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int u = 0; u < 8; ++u) f[u] = b == 32 ? __ldg(dense + i0 + c * 8 + u) : 0.0f;
-            dq_put8(hrow, lrow, ((((i0 >> 3) + c) ^ r7) << 4), f);
-        }
+        for (int c = 0; c < N1 / 8; ++c) dq_put8(hrow, lrow, ((((i0 >> 3) + c) ^ r7) << 4), z);
     }
 }
-
 
 struct Tile {
     int m0, n0, b, kb0, kb1;
@@ -381,7 +386,9 @@ __device__ __forceinline__ void emit_block(const TcGemm &g, const Tile &T, const
             }
         }
     } else {
-        // ragged or unaligned edge: element by element, same arithmetic
+        // ragged or unaligned edge: element by element, same arithmetic (unrolled,
+        // so that vv stays in registers on every path)
+#pragma unroll
         for (int it = 0; it < 8; ++it) {
             const int64_t m = mb + it * 4 + sub;
             if (m >= g.M) continue;
@@ -416,14 +423,13 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
               const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
               const __grid_constant__ CUtensorMap tc_map, TcGemm g) {
-    using Cfg = TcCfg<BN, AMN, BMN>;
+    using Cfg = TcCfg<BN, AMN, BMN, BQ>;
     constexpr int S = Cfg::kStages;
     static_assert(!BQ || !BMN, "packed weights are read K-major");
     extern __shared__ unsigned char tc_smem_raw[];
-    __shared__ __align__(8) uint64_t full[S], empty[S], tfull[2], tempty[2], drainb;
+    __shared__ __align__(8) uint64_t full[S], empty[S], cfull[S], tfull[2], tempty[2], drainb;
     __shared__ uint32_t tmem_sh;
     __shared__ volatile int abort_sh;
-    __shared__ float ebuf[4][32][33];  // epilogue: one 32 x 32 accumulator block per warp (padded)
     const uint32_t raw_s = smem_u32(tc_smem_raw);
     unsigned char *sm = tc_smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);  // 1024-byte aligned stages
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -434,6 +440,7 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], BQ ? 5 : 1);  // the A copies' transaction arrival (+ 4 dequantising warps)
             mbar_init(&empty[s], 1);
+            mbar_init(&cfull[s], 1);          // packed weights: the code segments' copies
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
@@ -483,7 +490,19 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
                                         &full[s]);
                         }
                     }
-                    if (BQ) continue;  // the dequantising warps fill B
+                    if (BQ) {
+                        // the tile's code segments of this K slice (one bulk copy per 64 rows;
+                        // blocks past the matrix are not copied and read as zeros)
+                        const int G = g.wt.cols / kBK, RB = (g.wt.rows + 63) / 64;
+                        const int64_t rb0 = (g.wq_row0 + T.n0) / 64;
+                        const int nb = (int)max((int64_t)0, min((int64_t)(BN / 64), (int64_t)RB - rb0));
+                        mbar_expect_tx(&cfull[s], (uint32_t)(nb * kSeg));
+                        unsigned char *stg = st + 2 * Cfg::kATile + 2 * Cfg::kBTile;
+                        for (int blk = 0; blk < nb; ++blk)
+                            bulk_g2s(stg + blk * kSeg, g.wt.data + ((rb0 + blk) * G + kb) * (int64_t)kSeg, kSeg,
+                                     &cfull[s]);
+                        continue;  // the dequantising warps fill B
+                    }
                     if (!BMN) {
                         tma_load_3d(sb, &tb_hi, k0, (int)g.b.row_off + T.n0, bb, &full[s]);
                         tma_load_3d(sb + Cfg::kBTile, &tb_lo, k0, (int)g.b.row_off + T.n0, bb, &full[s]);
@@ -498,7 +517,10 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
                 }
             }
             if (abort_sh) {  // let this CTA's copies land before the CTA can exit
-                for (int p = q - S > 0 ? q - S : 0; p < q; ++p) mbar_wait_bounded(&full[p % S], (p / S) & 1, kWaitLimit);
+                for (int p = q - S > 0 ? q - S : 0; p < q; ++p) {
+                    if (BQ) mbar_wait_bounded(&cfull[p % S], (p / S) & 1, kWaitLimit);
+                    mbar_wait_bounded(&full[p % S], (p / S) & 1, kWaitLimit);
+                }
             }
         }
     } else if (warp == 5) {
@@ -554,34 +576,34 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
             const int rloc = (warp - 6) * R + lane / LPR;
             const int i0 = (lane % LPR) * N1;
             const int r7 = rloc & 7;
+            const int blk = rloc / 64, j = rloc % 64;
+            const int RB = (g.wt.rows + 63) / 64;
             int q = 0;
             for (int t = blockIdx.x; t < n_units && !abort_sh; t += gridDim.x) {
                 const Tile T = tile_of(g, t, mt, ntl, nk, BN);
                 if (T.skip) continue;
-                const int n = T.n0 + rloc;
-                const bool valid = n < g.N;
-                const int64_t wrow = g.wq_row0 + (valid ? n : 0);
-                const uint32_t ro = valid ? __ldg(g.wq.row_off8 + wrow) : 0u;
-                DqGroup cur, nxt;
-                if (valid && T.kb0 < T.kb1) dq_fetch(g.wq, wrow, T.kb0, ro, cur);
+                const bool have = (g.wq_row0 + T.n0) / 64 + blk < RB;  // this row's block was copied
                 bool stop = false;
                 for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
                     const int s = q % S, r = q / S;
-                    if (valid && kb + 1 < T.kb1) dq_fetch(g.wq, wrow, kb + 1, ro, nxt);
-                    if (r > 0) {
-                        bool w_ok = true;
-                        if (lane == 0) w_ok = mbar_wait_bounded(&empty[s], (r - 1) & 1, wait_limit());
-                        w_ok = __shfl_sync(kFull, w_ok ? 1 : 0, 0) != 0;
-                        if (!w_ok) abort_sh = 1;
+                    bool w_ok = true;
+                    if (lane == 0) {
+                        if (r > 0) w_ok = mbar_wait_bounded(&empty[s], (r - 1) & 1, wait_limit());
+                        if (w_ok) w_ok = mbar_wait_bounded(&cfull[s], r & 1, wait_limit());
                     }
+                    w_ok = __shfl_sync(kFull, w_ok ? 1 : 0, 0) != 0;
+                    if (!w_ok) abort_sh = 1;
                     if (abort_sh) {
                         stop = true;
                         break;
                     }
-                    unsigned char *bh = sm + s * Cfg::kStage + 2 * Cfg::kATile;
+                    unsigned char *st = sm + s * Cfg::kStage;
+                    unsigned char *bh = st + 2 * Cfg::kATile;
                     unsigned char *hrow = bh + rloc * 128, *lrow = bh + Cfg::kBTile + rloc * 128;
-                    if (valid) {
-                        dq_slice<N1>(cur, g.wq, wrow, kb, i0, hrow, lrow, r7);
+                    if (have) {
+                        DqGroup cur;
+                        dq_load(st + 2 * Cfg::kATile + 2 * Cfg::kBTile + blk * kSeg, j, cur);
+                        dq_slice<N1>(cur, i0, hrow, lrow, r7);
                     } else {
                         const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -590,7 +612,6 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&full[s]);
-                    cur = nxt;
                 }
                 if (stop) break;
             }
@@ -599,9 +620,12 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
         // epilogue: warp w reads tensor-memory lanes 32w .. 32w+31 = tile rows.
         // Per 32-column block: lane = tile row on the way out of tensor
         // memory, lane = column on the way to global memory.
-        float(*eb)[33] = ebuf[warp];
-        // TMA store path: this warp's [32 rows][32 fp32] box, 1024-byte aligned after the stages
-        float *sb = reinterpret_cast<float *>(sm + S * Cfg::kStage) + warp * 32 * 32;
+        // TMA store path: this warp's [32 rows][32 fp32] box (4 KB, 1024-byte aligned:
+        // the 128-byte swizzle); plain-store path: the padded 32 x 33 transpose
+        // block.  One launch uses one of the two, so they share the bytes.
+        float *ebase = reinterpret_cast<float *>(sm + S * Cfg::kStage);
+        float *sb = ebase + warp * 32 * 32;
+        float(*eb)[33] = reinterpret_cast<float(*)[33]>(ebase + warp * 32 * 33);
         // 16-byte stores and loads need 4-float row strides and 16-byte (8 for planes) bases
         auto al = [](const void *p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
         const bool vec = ((g.ldc | g.ldr | g.ldy2 | g.ldp | g.sC) & 3) == 0 && al(g.C, 15) && al(g.R, 15) &&
@@ -796,7 +820,7 @@ bool op_ok(const TcOp &o) {
 
 template <int BN, int AMN, int BMN, int BQ>
 int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
-    using Cfg = TcCfg<BN, AMN, BMN>;
+    using Cfg = TcCfg<BN, AMN, BMN, BQ>;
     static std::mutex mu;
     static bool attr_done[64] = {};
     int dev = 0;
@@ -820,7 +844,8 @@ int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
         return ALTXS_EINVAL;
     }
     TcGemm gk = g;
-    gk.tma_c = make_c_map(&tc_map, g) ? 1 : 0;
+    // (the split epilogue's partials use the transpose buffer the TMA-store box shares)
+    gk.tma_c = g.splits == 1 && make_c_map(&tc_map, g) ? 1 : 0;
     if (!gk.tma_c) tc_map = ta_hi;  // unused
     // persistent: at most one CTA per SM walks the units
     const int64_t units = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch * g.splits;
@@ -848,9 +873,9 @@ int launch_tc_gemm(const TcGemm &g0, cudaStream_t st) {
     if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
     if (g.K <= 0 || !op_ok(g.a) || (!g.bq && !op_ok(g.b))) return ALTXS_EINVAL;
     if (g.causal < 0 || g.causal > 3) return ALTXS_EINVAL;
-    if (g.bq && (!g.wq.codes || !g.wq.row_off8 || !g.wq.gdesc || (g.wq.lut && !g.wq.glut) || g.wq.cols != g.K ||
-                 g.K % kBK || g.wq_row0 < 0 || g.wq_row0 + g.N > g.wq.rows || g.batch != 1 || g.b.mn_major ||
-                 (reinterpret_cast<uintptr_t>(g.wq.codes) & 7)))
+    if (g.bq && (!g.wt.data || g.wt.cols != g.K || g.K % kBK || g.wq_row0 < 0 || g.wq_row0 % 64 ||
+                 g.wq_row0 + g.N > g.wt.rows || g.batch != 1 || g.b.mn_major ||
+                 (reinterpret_cast<uintptr_t>(g.wt.data) & 15)))
         return ALTXS_EINVAL;
     if (g.splits < 1 || g.splits > (g.K + kBK - 1) / kBK) return ALTXS_EINVAL;
     if (g.splits > 1 && (!g.part || !g.cnt || g.causal != 0 || (reinterpret_cast<uintptr_t>(g.part) & 15)))
@@ -860,7 +885,7 @@ int launch_tc_gemm(const TcGemm &g0, cudaStream_t st) {
     if (g.beta != 0.0f && !g.C) return ALTXS_EINVAL;
     // the K extent of each operand must be covered by its stored array (zeros beyond come from the bounds)
     const int64_t ka = g.a.mn_major ? g.a.rows - g.a.row_off : g.a.cols;
-    const int64_t kbx = g.bq ? g.wq.cols : g.b.mn_major ? g.b.rows - g.b.row_off : g.b.cols;
+    const int64_t kbx = g.bq ? g.wt.cols : g.b.mn_major ? g.b.rows - g.b.row_off : g.b.cols;
     if (ka < g.K || kbx < g.K) return ALTXS_EINVAL;
     // a K slice reads 64 values: past K they must come from the bounds (zeros), not from stored data
     if (g.K % kBK && (ka != g.K || kbx != g.K)) return ALTXS_EINVAL;
@@ -911,9 +936,9 @@ int launch_tc(const TcArgs &a, cudaStream_t st) {
     g.ldp = a.ldp;
     g.status = a.status;
     g.status_stride = a.status_stride;
-    if (a.wq) {
+    if (a.wt) {
         g.bq = 1;
-        g.wq = *a.wq;
+        g.wt = *a.wt;
         g.wq_row0 = a.row0;
     }
     g.splits = 1;
@@ -1159,12 +1184,12 @@ int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K) {
            altxs::align_up(altxs::tc_linear_cnt_elems(M, N, K) * 4, 256);
 }
 
-int altxs_linear_tc(const altxs_qmat *m, int row0, int N, const float *X, int M, float *Y, void *workspace,
+int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int M, float *Y, void *workspace,
                     int64_t workspace_bytes, altxs_stream_t stream) {
     using namespace altxs;
-    if (!m || !X || !Y || M < 0 || N < 0 || row0 < 0 || row0 + N > m->rows) return ALTXS_EINVAL;
+    if (!w || !X || !Y || M < 0 || N < 0 || row0 < 0 || row0 + N > w->rows) return ALTXS_EINVAL;
     if (M == 0 || N == 0) return ALTXS_OK;
-    const int K = m->cols;
+    const int K = w->cols;
     if (!workspace || workspace_bytes < altxs_linear_tc_workspace_bytes(M, N, K)) return ALTXS_EINVAL;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char *p = static_cast<unsigned char *>(workspace);
@@ -1183,14 +1208,14 @@ int altxs_linear_tc(const altxs_qmat *m, int row0, int N, const float *X, int M,
     t.a_lo = xl;
     t.lda = K;
     t.M = M;
-    t.b_rows = m->rows;
+    t.b_rows = w->rows;
     t.row0 = row0;
     t.N = N;
     t.K = K;
     t.epi = kEpiStore;
     t.Y = Y;
     t.ldy = N;
-    t.wq = m;
+    t.wt = w;
     t.part = part;
     t.cnt = cnt;
     return launch_tc(t, st);

@@ -64,12 +64,14 @@ struct TcGemm {
     uint32_t *status;       // optional per-row status word (ALTXS_ST_TIMEOUT on a wait that gave up)
     int64_t status_stride;  // in uint32 units
     int tma_c;              // set by launch_tc_gemm: C is written by TMA tensor stores
-    // bq: B is read from packed mixed-bit codes instead of planes: element
-    // (n, k) of B is wq[wq_row0 + n][k] (K-major; batch 1).  Producer warps
-    // expand each 64-wide group slice into the stage as the same hi/lo
-    // planes that k_split_weights writes, so the products are unchanged.
+    // bq: B is read from the packed mixed-bit codes (tile-stream layout,
+    // altxs_qtiles) instead of planes: element (n, k) of B is row wq_row0 + n
+    // of the matrix (K-major; batch 1; wq_row0 a multiple of 64).  Each K
+    // slice's code segments arrive by bulk copy; producer warps expand them
+    // into the stage as the same hi/lo planes k_split_weights writes, so the
+    // products are unchanged.
     int bq;
-    altxs_qmat wq;
+    altxs_qtiles wt;
     int64_t wq_row0;
     // split K: each output tile's K slices are cut into `splits` equal ranges
     // run as separate units; every unit writes its fp32 partial to part
@@ -105,9 +107,9 @@ struct TcArgs {
     int64_t ldp;
     uint32_t *status;
     int64_t status_stride;
-    // optional: the packed weights (B rows from wq instead of the planes) and
+    // optional: the packed weights (B rows from wt instead of the planes) and
     // the split-K scratch (tc_linear_part_elems / tc_linear_cnt_elems for M, N, K)
-    const altxs_qmat *wq;
+    const altxs_qtiles *wt;
     float *part;
     uint32_t *cnt;
 };

@@ -26,7 +26,7 @@ import numpy as np
 import torch
 
 from . import _lib, lockstep
-from .codec import ModelWeights, PackedMatrix
+from .codec import ModelWeights, PackedMatrix, tile_stream
 from .config import ModelConfig
 from .lora import init_lora_A, lora_shapes, rope_tables
 
@@ -90,6 +90,14 @@ class DeviceModel:
         self.weight_bytes = sum(p.nbytes for p in packed.values())
         self.weights_sha256 = lockstep.weights_digest(packed, weights.small)
         self.q = {k: self._qmat(v) for k, v in packed.items()}
+        # the packed codes in the tensor-core GEMM's tile-stream layout (when every
+        # group is 0/2/3/4-bit symmetric), read by the packed tensor-core linears
+        self.tiles = None
+        if tensor_cores:
+            ts = {k: tile_stream(v) for k, v in packed.items()}
+            if all(t is not None for t in ts.values()):
+                self.tiles = _lib.TileWeights(**{k: _lib.QTiles(data=self._up(t).data_ptr(), rows=packed[k].rows,
+                                                                cols=packed[k].cols) for k, t in ts.items()})
         s = weights.small
         L = cfg.num_layers
         f32 = lambda a: self._up(np.ascontiguousarray(a, dtype=np.float32))  # noqa: E731
@@ -289,6 +297,7 @@ class DeviceModel:
                                                 "parallel_post", "parallel_resid") if k in s},
                 emb_dense=self.params.data_ptr() + 4 * self.layout.emb if self.full_params else None,
                 planes_live=1 if self.full_params else 0,
+                tiles=C.pointer(self.tiles) if self.tiles is not None else None,
             )
         return self._weights_struct
 

@@ -372,8 +372,8 @@ def run_c2(args) -> None:
 
                 def call():
                     if path == "tensor":
-                        rc = L.altxs_linear_tc(ctypes.byref(q), 0, N, X.data_ptr(), M, Y.data_ptr(),
-                                               ws.data_ptr(), wsb, st)
+                        rc = L.altxs_linear_tc(ctypes.byref(getattr(dm.tiles, name)), 0, N, X.data_ptr(), M,
+                                               Y.data_ptr(), ws.data_ptr(), wsb, st)
                     else:
                         rc = L.altxs_linear(ctypes.byref(q), hi, lo, 0, N, X.data_ptr(), M, Y.data_ptr(),
                                             ws.data_ptr(), wsb, st)

@@ -126,6 +126,24 @@ typedef struct altxs_qmat {
     int32_t rows, cols;
 } altxs_qmat;
 
+/* The packed codes of one matrix re-laid for the tensor-core GEMM (built
+ * once at load, about 0.56 bytes per weight): fixed-size segments of 2304
+ * bytes, [ceil(rows/64)][cols/64], one per 64-row block and 64-wide group:
+ * 64 uint32 descriptors (fp16 scale | width code << 16 (0:0 1:2 2:3 3:4 bits)
+ * | offset of the row's code bytes within the segment's code area in 8-byte
+ * units << 20), then the rows' code bytes (8*b each, LSB-first as in the
+ * packed rows).  Rows past the matrix are 0-bit.  A tile's K slice is then
+ * one bulk copy per 64 rows with no table lookups.  Only 0/2/3/4-bit
+ * symmetric groups; no counterpart in the reference (its banks are dense). */
+typedef struct altxs_qtiles {
+    const uint8_t *data; /* device, 16-byte aligned */
+    int32_t rows, cols;
+} altxs_qtiles;
+
+typedef struct altxs_tile_weights {
+    altxs_qtiles emb, qkv, o, up, down;
+} altxs_tile_weights;
+
 typedef struct altxs_model_desc {
     int32_t vocab, n_layers, d_model, n_heads, n_kv_heads, head_dim, mlp_hidden;
     int32_t ctx;        /* sliding window (reference block_size) */
@@ -208,6 +226,9 @@ typedef struct altxs_weights {
      * planes equal the codes and the codes are read (0.43 instead of 4 bytes
      * per weight). */
     int32_t planes_live;
+    /* The five matrices in the tile-stream layout for the packed tensor-core
+     * linears (altxs_set_linear_packed), or NULL (planes). */
+    const altxs_tile_weights *tiles;
 } altxs_weights;
 
 /* Per-stream state and scratch of a batch of n streams.  Stream i of the
@@ -332,10 +353,10 @@ int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo
  * producer warps expand each 64-wide group slice in shared memory into the
  * hi/lo bf16 operands (no dense copy of the weights is read), so the result
  * is bit-identical to altxs_linear with the planes.  The decode step takes
- * this path under altxs_set_linear_packed(1).  Needs
- * altxs_linear_tc_workspace_bytes(M, N, m->cols) of device workspace. */
+ * this path under altxs_set_linear_packed(1).  row0 a multiple of 64.  Needs
+ * altxs_linear_tc_workspace_bytes(M, N, w->cols) of device workspace. */
 int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K);
-int altxs_linear_tc(const altxs_qmat *m, int row0, int N, const float *X, int M, float *Y, void *workspace,
+int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int M, float *Y, void *workspace,
                     int64_t workspace_bytes, altxs_stream_t stream);
 
 /* Segment-reset context (the reference's reset_segment, altxs

@@ -161,13 +161,13 @@ def _linear_tc(dm, name, X, row0, N):
     from altxs_b200 import _lib
 
     L = _lib.lib()
-    q = dm.q[name]
+    t = getattr(dm.tiles, name)
     M = X.shape[0]
     Xd = torch.as_tensor(X, device=DEV).contiguous()
     Y = torch.full((M, N), float("nan"), dtype=torch.float32, device=DEV)
-    ws_b = int(L.altxs_linear_tc_workspace_bytes(M, N, q.cols))
+    ws_b = int(L.altxs_linear_tc_workspace_bytes(M, N, t.cols))
     ws = torch.empty(max(ws_b, 1), dtype=torch.uint8, device=DEV)
-    assert L.altxs_linear_tc(C.byref(q), row0, N, Xd.data_ptr(), M, Y.data_ptr(), ws.data_ptr(), ws_b, None) == 0
+    assert L.altxs_linear_tc(C.byref(t), row0, N, Xd.data_ptr(), M, Y.data_ptr(), ws.data_ptr(), ws_b, None) == 0
     torch.cuda.synchronize()
     return Y.cpu().numpy()
 
@@ -223,3 +223,29 @@ def test_packed_weight_gemm_rows_do_not_depend_on_the_batch(name, N):
     ref = X[:64].astype(np.float64) @ W[:N].T
     bound = np.abs(X[:64].astype(np.float64)) @ np.abs(W[:N]).T
     assert np.all(np.abs(full[:64] - ref) <= 2.0 ** -15 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("c3", [False, True])
+def test_step_with_packed_linears_is_bit_identical(model, c3):
+    """The decode step with its tensor-core linears reading the packed codes
+    (altxs_set_linear_packed(1)) gives the same logits, bit for bit, as with
+    the dense planes."""
+    from altxs_b200 import _lib
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import DeviceModel
+    from tests.test_gpu_step import _run_logits
+
+    dm = DeviceModel(Cd.synth_weights(c3_config(), seed=5), DEV) if c3 else model
+    assert dm.tiles is not None
+    rng = np.random.default_rng(4)
+    toks = [rng.integers(0, dm.cfg.vocab_size, size=12) for _ in range(40 if c3 else 7)]
+    L = _lib.lib()
+    try:
+        assert L.altxs_set_linear_packed(0) == 0
+        planes = _run_logits(dm, toks)
+        assert L.altxs_set_linear_packed(1) == 0
+        packed = _run_logits(dm, toks)
+    finally:
+        L.altxs_set_linear_packed(0)
+    assert np.isfinite(packed).all()
+    assert np.array_equal(planes.view(np.uint32), packed.view(np.uint32))
