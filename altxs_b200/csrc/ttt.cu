@@ -186,7 +186,7 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.dy = take(T * d);
     t.dao = take(T * d);
     t.dS = take((int64_t)D.H * T * align_up(T, 8));  // fp32 scores / dP, rows of stride align8(T) on the tensor-core path
-    t.dt = take(T * D.r);
+    t.dt = take(T * 3 * (D.r > 0 ? D.r : 1));  // up to three adapters sharing an input
     t.grad = nullptr;  // set by caller (lora_floats)
     t.red = take(1024);
     const bool o_on_y = D.r > 0 && (D.omask & 64);
@@ -1109,6 +1109,181 @@ __global__ void __launch_bounds__(128) t_emb_scatter(int T, int d, int V, const 
     }
 }
 
+
+// ---- fused LoRA products (rank <= kLoraFused) ---------------------------
+// The adapters that read the same input (q, k and v on the block's normed
+// input) are one launch: a warp per row computes t = X A^T for every adapter
+// (warp reductions over the input in a fixed order) and adds s t B^T to each
+// adapter's output; the backward is a per-row kernel (dt = s G B, dX += dt A)
+// and the two row reductions dB = s G^T t and dA = dt^T X as chunked outer
+// sums added in a fixed chunk order.  Rows are independent, every sum has a
+// fixed order: results do not depend on anything but the window.
+constexpr int kLoraFused = 16;   // largest rank of the fused kernels
+constexpr int kLoraMaxIn = 1024; // largest adapter input width
+constexpr int kOuterChunks = 16; // row chunks of the outer sums
+
+struct LoraJob {
+    const float *A, *B;  // A [r][din], B [dout][r]
+    float *t;            // [T][r]: t = X A^T (forward: written; backward: read)
+    float *Y;            // forward: output columns (ld ldy), += s t B^T
+    const float *G;      // backward: d(output) columns (ld ldg)
+    int64_t ldy, ldg;
+    int dout;
+    float *dA, *dB;      // backward: gradients (written)
+};
+struct LoraGroup {
+    const float *X;
+    int64_t ldx;
+    int din, r, n;  // input width, rank, adapters (<= 3)
+    float s;
+    LoraJob j[3];
+    float *dX;      // backward: += sum_j dt_j A_j (may be NULL)
+    float *dt;      // backward: [T][n * r] scratch
+};
+
+__global__ void __launch_bounds__(256) t_lora_fwd(int T, LoraGroup g) {
+    const int lane = threadIdx.x & 31;
+    const int nw = blockDim.x >> 5;
+    constexpr int E = kLoraMaxIn / 32;
+    for (int row = blockIdx.x * nw + (threadIdx.x >> 5); row < T; row += gridDim.x * nw) {
+        float x[E];
+        const float *xr = g.X + (int64_t)row * g.ldx;
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = lane + 32 * e < g.din ? xr[lane + 32 * e] : 0.0f;
+        for (int a = 0; a < g.n; ++a) {
+            const LoraJob &J = g.j[a];
+            float t[kLoraFused];
+#pragma unroll
+            for (int p = 0; p < kLoraFused; ++p) {
+                float acc = 0.0f;
+                if (p < g.r) {
+                    const float *ar = J.A + (int64_t)p * g.din;
+#pragma unroll
+                    for (int e = 0; e < E; ++e)
+                        if (lane + 32 * e < g.din) acc = __fmaf_rn(x[e], __ldg(ar + lane + 32 * e), acc);
+                }
+                t[p] = warp_sum(acc);
+            }
+            if (lane < g.r) {
+#pragma unroll
+                for (int p = 0; p < kLoraFused; ++p)
+                    if (p == lane) J.t[(int64_t)row * g.r + p] = t[p];
+            }
+            float *yr = J.Y + (int64_t)row * J.ldy;
+            for (int o = lane; o < J.dout; o += 32) {
+                const float *br = J.B + (int64_t)o * g.r;
+                float acc = 0.0f;
+#pragma unroll
+                for (int p = 0; p < kLoraFused; ++p)
+                    if (p < g.r) acc = __fmaf_rn(t[p], __ldg(br + p), acc);
+                yr[o] = __fadd_rn(yr[o], __fmul_rn(g.s, acc));
+            }
+        }
+    }
+}
+
+// backward, per row: dt_j = s G_j B_j (into g.dt), dX += sum_j dt_j A_j
+__global__ void __launch_bounds__(256) t_lora_bwd_rows(int T, LoraGroup g) {
+    const int lane = threadIdx.x & 31;
+    const int nw = blockDim.x >> 5;
+    constexpr int E = kLoraMaxIn / 32;
+    for (int row = blockIdx.x * nw + (threadIdx.x >> 5); row < T; row += gridDim.x * nw) {
+        float dx[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) dx[e] = 0.0f;
+        for (int a = 0; a < g.n; ++a) {
+            const LoraJob &J = g.j[a];
+            float acc[kLoraFused];
+#pragma unroll
+            for (int p = 0; p < kLoraFused; ++p) acc[p] = 0.0f;
+            const float *gr = J.G + (int64_t)row * J.ldg;
+            for (int o = lane; o < J.dout; o += 32) {
+                const float gv = gr[o];
+                const float *br = J.B + (int64_t)o * g.r;
+#pragma unroll
+                for (int p = 0; p < kLoraFused; ++p)
+                    if (p < g.r) acc[p] = __fmaf_rn(gv, __ldg(br + p), acc[p]);
+            }
+            float dt[kLoraFused];
+#pragma unroll
+            for (int p = 0; p < kLoraFused; ++p) dt[p] = __fmul_rn(g.s, warp_sum(acc[p]));
+            if (lane < g.r) {
+#pragma unroll
+                for (int p = 0; p < kLoraFused; ++p)
+                    if (p == lane) g.dt[(int64_t)row * g.n * g.r + a * g.r + p] = dt[p];
+            }
+            if (g.dX) {
+#pragma unroll
+                for (int p = 0; p < kLoraFused; ++p) {
+                    if (p >= g.r) break;
+                    const float *ar = J.A + (int64_t)p * g.din;
+#pragma unroll
+                    for (int e = 0; e < E; ++e)
+                        if (lane + 32 * e < g.din) dx[e] = __fmaf_rn(dt[p], __ldg(ar + lane + 32 * e), dx[e]);
+                }
+            }
+        }
+        if (g.dX) {
+            float *xr = g.dX + (int64_t)row * g.din;
+#pragma unroll
+            for (int e = 0; e < E; ++e)
+                if (lane + 32 * e < g.din) xr[lane + 32 * e] = __fadd_rn(xr[lane + 32 * e], dx[e]);
+        }
+    }
+}
+
+// Outer sums out[p][q] = scale * sum over rows of U[t][p] V[t][q] for the
+// adapter gradients: job 2a is dB_a (U = t_a, V = G_a, stored [q][p] = B's
+// layout), job 2a+1 is dA_a (U = dt_a, V = X, stored [p][q]).  Part: chunk c
+// of the rows, one thread per (job, p, q), partials [c][job][p][qmax].
+__device__ __forceinline__ void lora_outer_job(const LoraGroup &g, int job, const float *&U, int64_t &ldu,
+                                               const float *&V, int64_t &ldv, int &Q) {
+    const LoraJob &J = g.j[job >> 1];
+    if ((job & 1) == 0) {
+        U = J.t;
+        ldu = g.r;
+        V = J.G;
+        ldv = J.ldg;
+        Q = J.dout;
+    } else {
+        U = g.dt + (job >> 1) * g.r;
+        ldu = (int64_t)g.n * g.r;
+        V = g.X;
+        ldv = g.ldx;
+        Q = g.din;
+    }
+}
+
+__global__ void __launch_bounds__(256) t_lora_outer_part(int T, LoraGroup g, int qmax, float *part) {
+    const int job = blockIdx.z / g.r, p = blockIdx.z % g.r, c = blockIdx.y;
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    const float *U, *V;
+    int64_t ldu, ldv;
+    int Q;
+    lora_outer_job(g, job, U, ldu, V, ldv, Q);
+    if (q >= Q) return;
+    const int rows = (T + kOuterChunks - 1) / kOuterChunks;
+    const int t0 = c * rows, t1 = min(T, t0 + rows);
+    float acc = 0.0f;
+    for (int t = t0; t < t1; ++t) acc = __fmaf_rn(U[(int64_t)t * ldu + p], V[(int64_t)t * ldv + q], acc);
+    part[(((int64_t)c * 2 * g.n + job) * g.r + p) * qmax + q] = acc;
+}
+
+__global__ void __launch_bounds__(256) t_lora_outer_fin(LoraGroup g, int qmax, const float *part) {
+    const int job = blockIdx.z / g.r, p = blockIdx.z % g.r;
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    const float *U, *V;
+    int64_t ldu, ldv;
+    int Q;
+    lora_outer_job(g, job, U, ldu, V, ldv, Q);
+    if (q >= Q) return;
+    float acc = 0.0f;
+    for (int c = 0; c < kOuterChunks; ++c) acc = __fadd_rn(acc, part[(((int64_t)c * 2 * g.n + job) * g.r + p) * qmax + q]);
+    const LoraJob &J = g.j[job >> 1];
+    if ((job & 1) == 0) J.dB[(int64_t)q * g.r + p] = __fmul_rn(g.s, acc);
+    else J.dA[(int64_t)p * g.din + q] = acc;
+}
+
 // out = a + s * b (two roundings, as the reference's w + s * dw)
 __global__ void t_axpy(int64_t n, const float *a, float s, const float *b, float *out) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
@@ -1325,11 +1500,84 @@ int lin_bwd(const Run &R, const altxs_qmat &Wq, const float *Wd, const uint16_t 
     return launch_qmm_t(q, R.st);
 }
 
+// fused adapters sharing one input X: forward (t and Y += s t B^T)
+int lora_fwd_group(const Run &R, const LoraGroup &g) {
+    if (R.no_lora || g.n == 0) return ALTXS_OK;
+    const int T = R.D.T;
+    const int grid = (T + 7) / 8 < 148 * 8 ? (T + 7) / 8 : 148 * 8;
+    ALTXS_LAUNCH(kKTtt, R.st, t_lora_fwd<<<grid, 256, 0, R.st>>>(T, g));
+    return ALTXS_OK;
+}
+
+// fused adapters sharing one input X: backward (dt, dX += dt A, dA, dB)
+int lora_bwd_group(const Run &R, const LoraGroup &g) {
+    if (R.no_lora || g.n == 0) return ALTXS_OK;
+    const int T = R.D.T;
+    const int grid = (T + 7) / 8 < 148 * 8 ? (T + 7) / 8 : 148 * 8;
+    ALTXS_LAUNCH(kKTtt, R.st, t_lora_bwd_rows<<<grid, 256, 0, R.st>>>(T, g));
+    int qmax = g.din;
+    for (int a = 0; a < g.n; ++a) qmax = qmax > g.j[a].dout ? qmax : g.j[a].dout;
+    if ((int64_t)kOuterChunks * 2 * g.n * g.r * qmax > R.splitk_floats) return ALTXS_EINVAL;
+    const dim3 grid2((qmax + 255) / 256, kOuterChunks, 2 * g.n * g.r);
+    ALTXS_LAUNCH(kKTtt, R.st, t_lora_outer_part<<<grid2, 256, 0, R.st>>>(T, g, qmax, R.splitk));
+    ALTXS_LAUNCH(kKTtt, R.st,
+                 t_lora_outer_fin<<<dim3((qmax + 255) / 256, 1, 2 * g.n * g.r), 256, 0, R.st>>>(g, qmax, R.splitk));
+    return ALTXS_OK;
+}
+
+// small adapters on the layers' inputs; the LM-head adapter (V outputs) keeps
+// the GEMM path, whose tiles make the T x V read-modify-write of the logits
+// and the V-wide reductions cheaper than a warp per row
+bool lora_fusable(const Run &R, int din, int dout = 0) {
+    return R.D.r > 0 && R.D.r <= kLoraFused && din <= kLoraMaxIn && dout <= kLoraMaxIn;
+}
+
+// one forward adapter job: A, B, the t tape, the output columns
+LoraJob fjob(const float *A, const float *B, float *t, float *Y, int64_t ldy, int dout) {
+    LoraJob j{};
+    j.A = A;
+    j.B = B;
+    j.t = t;
+    j.Y = Y;
+    j.ldy = ldy;
+    j.dout = dout;
+    return j;
+}
+// one backward adapter job: A, B, the t tape, d(output) columns, gradients
+LoraJob bjob(const float *A, const float *B, float *t, const float *Gy, int64_t ldg, int dout, float *dA, float *dB) {
+    LoraJob j{};
+    j.A = A;
+    j.B = B;
+    j.t = t;
+    j.G = Gy;
+    j.ldg = ldg;
+    j.dout = dout;
+    j.dA = dA;
+    j.dB = dB;
+    return j;
+}
+LoraGroup lgroup(const Run &R, const float *X, int din, float *dX = nullptr) {
+    LoraGroup g{};
+    g.X = X;
+    g.ldx = din;
+    g.din = din;
+    g.r = R.D.r;
+    g.s = R.desc->lora_scale;
+    g.dX = dX;
+    g.dt = R.tp.dt;
+    return g;
+}
+
 // LoRA forward for one target: t = X A^T ; Y += s * t B^T
 int lora_fwd(const Run &R, const float *X, int din, const float *A, const float *B, int dout, float s, float *t,
              float *Y, int64_t ldy) {
     if (R.no_lora) return ALTXS_OK;
     const int T = R.D.T, r = R.D.r;
+    if (lora_fusable(R, din, dout) && s == R.desc->lora_scale) {
+        LoraGroup g = lgroup(R, X, din);
+        g.j[g.n++] = fjob(A, B, t, Y, ldy, dout);
+        return lora_fwd_group(R, g);
+    }
     TRY(launch_gemm(G(R, X, din, 0, A, din, 1, t, r, T, r, din), R.st));
     TRY(launch_gemm(G(R, t, r, 0, B, r, 1, Y, ldy, T, dout, r, s, 1.0f), R.st));
     return ALTXS_OK;
@@ -1340,6 +1588,11 @@ int lora_bwd(const Run &R, const float *X, int din, const float *A, const float 
              const float *t, const float *Gy, int64_t ldg, float *dA, float *dB, float *dX) {
     if (R.no_lora) return ALTXS_OK;
     const int T = R.D.T, r = R.D.r;
+    if (lora_fusable(R, din, dout) && s == R.desc->lora_scale) {
+        LoraGroup g = lgroup(R, X, din, dX);
+        g.j[g.n++] = bjob(A, B, const_cast<float *>(t), Gy, ldg, dout, dA, dB);
+        return lora_bwd_group(R, g);
+    }
     float *dt = R.tp.dt;
     TRY(launch_gemm(G(R, Gy, ldg, 1, t, r, 0, dB, r, dout, r, T, s), R.st));  // dB = s G^T t
     TRY(launch_gemm(G(R, Gy, ldg, 0, B, r, 0, dt, r, T, r, dout, s), R.st));  // dt = s G B
@@ -1347,6 +1600,7 @@ int lora_bwd(const Run &R, const float *X, int din, const float *A, const float 
     if (dX) TRY(launch_gemm(G(R, dt, r, 0, A, din, 0, dX, din, T, din, r, 1.0f, 1.0f), R.st));  // dX += dt A
     return ALTXS_OK;
 }
+
 
 // the weight planes of matrix field f (NULL on the CUDA-core path)
 #define PL(f) (R.sp ? R.sp->f : nullptr)
@@ -1413,13 +1667,25 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         const float *n = tp.n + (int64_t)l * Tn * d;
         float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
         TRY(lin_fwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), i * D.qn, D.qn, d, n, d, qkv, D.qn));
-        TRY(lora_fwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
-                     tp.tq + (int64_t)l * Tn * r, qkv, D.qn));
-        if (mask & 2)
-            TRY(lora_fwd(R, n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, s,
-                         tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn));
-        TRY(lora_fwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
-                     tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
+        if (lora_fusable(R, d, d > D.kvd ? d : D.kvd)) {  // q, k, v read the same input: one launch
+            LoraGroup g = lgroup(R, n, d);
+            g.j[g.n++] = fjob(lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride,
+                              tp.tq + (int64_t)l * Tn * r, qkv, D.qn, d);
+            if (mask & 2)
+                g.j[g.n++] = fjob(lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride,
+                                  tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn, D.kvd);
+            g.j[g.n++] = fjob(lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride,
+                              tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn, D.kvd);
+            TRY(lora_fwd_group(R, g));
+        } else {
+            TRY(lora_fwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
+                         tp.tq + (int64_t)l * Tn * r, qkv, D.qn));
+            if (mask & 2)
+                TRY(lora_fwd(R, n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, s,
+                             tp.tk + (int64_t)l * Tn * r, qkv + d, D.qn));
+            TRY(lora_fwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
+                         tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
+        }
         ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
         TRY(attn_probs(R, l));
         // the full-parameter gradient keeps every application's attention output and projections
@@ -1693,16 +1959,31 @@ int backward(const Run &R, const float *lora, float *grad) {
                                         (int64_t)Tn * D.kvd, D.kvd, D.qn, d + D.kvd, tp.dqkv, tp.dvx));
         ALTXS_LAUNCH(kKTtt, st, t_qk_bwd<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
         if (full) TRY(colsum(tp.colbuf, D.H, nullptr, 0, D.H, FG + lay.q_gain + (int64_t)i * D.H));
-        TRY(lora_bwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
-                     tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, grad + lo.qA + l * lo.q_stride,
-                     grad + lo.qB + l * lo.q_stride, tp.dn));
-        if (mask & 2)
-            TRY(lora_bwd(R, n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, s,
-                         tp.tk + (int64_t)l * Tn * r, tp.dqkv + d, D.qn, grad + lo.kA + l * lo.k_stride,
-                         grad + lo.kB + l * lo.k_stride, tp.dn));
-        TRY(lora_bwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
-                     tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, grad + lo.vA + l * lo.v_stride,
-                     grad + lo.vB + l * lo.v_stride, tp.dn));
+        if (lora_fusable(R, d, d > D.kvd ? d : D.kvd) && !R.no_lora) {  // q, k, v read the same input: one group
+            LoraGroup g = lgroup(R, n, d, tp.dn);
+            g.j[g.n++] = bjob(lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride,
+                              tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, d, grad + lo.qA + l * lo.q_stride,
+                              grad + lo.qB + l * lo.q_stride);
+            if (mask & 2)
+                g.j[g.n++] = bjob(lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride,
+                                  tp.tk + (int64_t)l * Tn * r, tp.dqkv + d, D.qn, D.kvd,
+                                  grad + lo.kA + l * lo.k_stride, grad + lo.kB + l * lo.k_stride);
+            g.j[g.n++] = bjob(lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride,
+                              tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, D.kvd,
+                              grad + lo.vA + l * lo.v_stride, grad + lo.vB + l * lo.v_stride);
+            TRY(lora_bwd_group(R, g));
+        } else {
+            TRY(lora_bwd(R, n, d, lora + lo.qA + l * lo.q_stride, lora + lo.qB + l * lo.q_stride, d, s,
+                         tp.tq + (int64_t)l * Tn * r, tp.dqkv, D.qn, grad + lo.qA + l * lo.q_stride,
+                         grad + lo.qB + l * lo.q_stride, tp.dn));
+            if (mask & 2)
+                TRY(lora_bwd(R, n, d, lora + lo.kA + l * lo.k_stride, lora + lo.kB + l * lo.k_stride, D.kvd, s,
+                             tp.tk + (int64_t)l * Tn * r, tp.dqkv + d, D.qn, grad + lo.kA + l * lo.k_stride,
+                             grad + lo.kB + l * lo.k_stride, tp.dn));
+            TRY(lora_bwd(R, n, d, lora + lo.vA + l * lo.v_stride, lora + lo.vB + l * lo.v_stride, D.kvd, s,
+                         tp.tv + (int64_t)l * Tn * r, tp.dqkv + d + D.kvd, D.qn, grad + lo.vA + l * lo.v_stride,
+                         grad + lo.vB + l * lo.v_stride, tp.dn));
+        }
         if (full) TRY(wgrad(tp.dqkv, D.qn, n, d, FG + lay.qkv + (int64_t)i * D.qn * d, acc));
         TRY(lin_bwd(R, w->qkv, dw ? dw->qkv : nullptr, PL(qkv_hi), PL(qkv_lo), i * D.qn, D.qn, d, tp.dqkv, D.qn, tp.dn, d, 1.0f));
         // d(x_in): added to the stream's gradient (sequential), or the attention read alone (parallel)
