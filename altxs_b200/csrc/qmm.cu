@@ -20,9 +20,12 @@ namespace {
 template <int MM>
 __global__ void __launch_bounds__(kGemvThreads) k_qgemv(QmmArgs a) {
     extern __shared__ __align__(16) float xs[];  // [M][K + K/64]: one pad float per group
+    // the lane's first group is fetched while X is staged (independent loads)
+    QgemvPre pre;
+    qgemv_prefetch(a, blockIdx.x, blockDim.x >> 5, threadIdx.x >> 5, pre);
     qgemv_stage_x(a, xs, blockDim.x);
     __syncthreads();
-    qgemv_rows<MM>(a, xs, blockIdx.x, blockDim.x >> 5, threadIdx.x >> 5);
+    qgemv_rows<MM>(a, xs, blockIdx.x, blockDim.x >> 5, threadIdx.x >> 5, &pre);
 }
 
 // ---------------------------------------------------------------------------

@@ -136,10 +136,45 @@ __device__ __forceinline__ void qgemv_stage_x(const QmmArgs &a, float *xs, int n
     }
 }
 
+// A lane's first group (descriptor and packed 2/3/4-bit words), fetched before
+// X is staged so that the two global latencies overlap.
+struct QgemvPre {
+    uint32_t d;
+    uint32_t W[8];
+};
+
+__device__ __forceinline__ void qgemv_prefetch(const QmmArgs &a, int rb, int warps_per_block, int warp,
+                                               QgemvPre &pre) {
+    const int K = a.K, G = K / 64;
+    const int lane = threadIdx.x & 31;
+    const int lpr = qgemv_lanes_per_row(K);
+    const int n = (rb * warps_per_block + warp) * (32 / lpr) + lane / lpr;
+    const int g = lane % lpr;
+    pre.d = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) pre.W[q] = 0u;
+    if (n >= a.N || g >= G) return;
+    const int row = a.row0 + n;
+    pre.d = a.W.gdesc[(int64_t)row * G + g];
+    const int b = qmm_width_of(pre.d);
+    if (b >= 2 && b <= 4) {
+        const uint2 *g2 =
+            reinterpret_cast<const uint2 *>(a.W.codes + 8ull * ((uint64_t)a.W.row_off8[row] + (pre.d >> 20)));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint2 u = q < b ? g2[q] : make_uint2(0u, 0u);
+            pre.W[2 * q] = u.x;
+            pre.W[2 * q + 1] = u.y;
+        }
+    }
+}
+
 // The rows of row block rb (warps_per_block warps of 32 / lpr rows each) from
-// the staged X; warp `warp` of the block takes its rows.
+// the staged X; warp `warp` of the block takes its rows.  `pre` (optional):
+// this lane's first group, already fetched by qgemv_prefetch.
 template <int MM>
-__device__ __forceinline__ void qgemv_rows(const QmmArgs &a, const float *xs, int rb, int warps_per_block, int warp) {
+__device__ __forceinline__ void qgemv_rows(const QmmArgs &a, const float *xs, int rb, int warps_per_block, int warp,
+                                           const QgemvPre *pre = nullptr) {
     const int K = a.K, G = K / 64, M = a.M;
     const int kp = K + G;
     const int lane = threadIdx.x & 31;
@@ -159,19 +194,25 @@ __device__ __forceinline__ void qgemv_rows(const QmmArgs &a, const float *xs, in
         for (int m = 0; m < MM; ++m) p[m] = 0.0f;
         float s = 0.0f;
         if (valid && g < G) {
-            const uint32_t d = a.W.gdesc[(int64_t)row * G + g];
+            const bool have = pre && g0 == 0;
+            const uint32_t d = have ? pre->d : a.W.gdesc[(int64_t)row * G + g];
             s = h2f((uint16_t)(d & 0xffffu));
             const int b = qmm_width_of(d);
             if (b >= 2 && b <= 4) {
                 // the group's packed words in one go (8-byte aligned), then its 64 codes in order
-                const uint2 *g2 =
-                    reinterpret_cast<const uint2 *>(a.W.codes + 8ull * ((uint64_t)a.W.row_off8[row] + (d >> 20)));
                 uint32_t W[8];
+                if (have) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint2 u = q < b ? g2[q] : make_uint2(0u, 0u);
-                    W[2 * q] = u.x;
-                    W[2 * q + 1] = u.y;
+                    for (int q = 0; q < 8; ++q) W[q] = pre->W[q];
+                } else {
+                    const uint2 *g2 = reinterpret_cast<const uint2 *>(
+                        a.W.codes + 8ull * ((uint64_t)a.W.row_off8[row] + (d >> 20)));
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint2 u = q < b ? g2[q] : make_uint2(0u, 0u);
+                        W[2 * q] = u.x;
+                        W[2 * q + 1] = u.y;
+                    }
                 }
                 const uint16_t *lut = a.W.lut ? a.W.lut + 16ull * a.W.glut[(int64_t)row * G + g] : nullptr;
                 const float *xr = xs + g * 65;

@@ -227,7 +227,10 @@ __device__ __forceinline__ float lora_u(const float *B, const float *t, int rank
 // LoRA on q/k/v, per-head RMSNorm, partial RoPE, q_gain, KV ring write.
 // Layers that run XSA get their new V rows (fp32, after LoRA) back in qkv.
 // (no block-wide reductions: its arithmetic does not depend on the block size)
-__device__ void qkv_post_body(const StepCtx &c, const LayerApp &a, int bi) {
+// part/nparts: this block takes heads [part*nh/nparts, (part+1)*nh/nparts) of the
+// row's nh = H + 2 Hkv heads (a few streams spread one row over many blocks);
+// every block computes the adapters' t itself, so the values do not change.
+__device__ void qkv_post_body(const StepCtx &c, const LayerApp &a, int bi, int part = 0, int nparts = 1) {
     extern __shared__ __align__(16) float sm[];
     const int i = bi;
     if (!row_active(c.b, i)) return;
@@ -252,7 +255,9 @@ __device__ void qkv_post_body(const StepCtx &c, const LayerApp &a, int bi) {
         lora_t(P + o.vA + s * o.v_stride, nx, R, d, tq + 2 * R);
         __syncthreads();
         const float sc = c.dsc.lora_scale;
-        for (int k = threadIdx.x; k < D.qkv_n; k += blockDim.x) {
+        const int nh = D.H + 2 * D.Hkv;
+        const int k0 = part * nh / nparts * hd, k1 = (part + 1) * nh / nparts * hd;
+        for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
             if (k < d) {
                 v[k] = __fadd_rn(v[k], lora_u(P + o.qB + s * o.q_stride, tq, R, k, sc));
             } else if (k < d + kvd) {
@@ -264,9 +269,12 @@ __device__ void qkv_post_body(const StepCtx &c, const LayerApp &a, int bi) {
         }
     }
     __syncthreads();
+    const int nhead = D.H + 2 * D.Hkv;
+    const int h0 = part * nhead / nparts, h1 = (part + 1) * nhead / nparts;
     if (l >= D.xsa_from && R > 0 && c.b.lora) {
         float *dst = c.qkv + (int64_t)i * D.qkv_n;
-        for (int k = d + kvd + threadIdx.x; k < D.qkv_n; k += blockDim.x) dst[k] = v[k];
+        const int k0 = max(d + kvd, h0 * hd), k1 = min(D.qkv_n, h1 * hd);
+        for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) dst[k] = v[k];
     }
     const int64_t pos = c.b.pos[i];
     if (pos < 0 || pos >= c.w.rope_positions) {
@@ -278,10 +286,9 @@ __device__ void qkv_post_body(const StepCtx &c, const LayerApp &a, int bi) {
     const float *cs = c.w.rope_cos + pos * half, *sn = c.w.rope_sin + pos * half;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     // heads: 0..H-1 q, H..H+Hkv-1 k (normed + rope), H+Hkv.. v (copy)
-    const int nhead = D.H + 2 * D.Hkv;
     const int64_t rb = 3 * (int64_t)hd;  // bytes per KV row
     uint8_t *kvbase = c.b.kv + ((int64_t)i * D.Lv + a.v) * 2 * D.Hkv * D.ctx * rb;
-    for (int h = wid; h < nhead; h += nw) {
+    for (int h = h0 + wid; h < h1; h += nw) {
         float *e = v + h * hd;  // q heads, then k heads, then v heads are contiguous
         if (h >= D.H + D.Hkv) {
             const int kvh = h - D.H - D.Hkv;
@@ -337,7 +344,9 @@ __device__ __forceinline__ void unpack24x2(uint32_t h, uint32_t lo2, float &f0, 
     f0 = __uint_as_float(__byte_perm(h, lo2, 0x1046));
     f1 = __uint_as_float(__byte_perm(h, lo2, 0x3256));
 }
-__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) { qkv_post_body(c, a, blockIdx.x); }
+__global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) {
+    qkv_post_body(c, a, blockIdx.x, blockIdx.y, gridDim.y);
+}
 
 
 // ---------------------------------------------------------------------------
@@ -359,7 +368,7 @@ __global__ void __launch_bounds__(256, 5) k_qkv_post(StepCtx c, LayerApp a) { qk
 // full score of key kl + (32/LPK)*ds: one score, one exp per lane per chunk.
 constexpr int kRingChunk = 32;     // key rows per TMA chunk
 constexpr int kRingMaxWarps = 8;   // warps per CTA
-constexpr int kRingMaxSlots = 4;   // chunk slots per warp
+constexpr int kRingMaxSlots = 8;   // chunk slots per warp
 #ifndef ALTXS_RING_WARPS
 #define ALTXS_RING_WARPS 2  // 2 warps x 2 slots x 12 KB (hd 64): four CTAs per SM
 #endif
@@ -613,27 +622,44 @@ __global__ void __launch_bounds__(kRingMaxWarps * 32) k_attn_ring(StepCtx c, int
 
 // Launch of the ring kernel for this model's head size and group size:
 // a persistent grid of as many CTAs as fit on the device at once.
+// Few items (a few streams: at most one item per warp of the device) keep every
+// chunk of an item in flight (8 slots = one 256-key split) at one CTA per SM;
+// many items keep 2 slots per warp at four CTAs per SM.  The slot count only
+// changes how far ahead a warp's copies run, not an item's arithmetic.
 template <int LPK, int G>
 cudaError_t launch_ring(const StepCtx &c, int l, cudaStream_t st) {
     const Dims &D = c.D;
-    const int warps = ALTXS_RING_WARPS, slots = ALTXS_RING_SLOTS;
-    const size_t smem = (size_t)warps * slots * 2 * kRingChunk * 3 * (LPK * 8);
-    static int grid_max[64] = {};
+    const int warps = ALTXS_RING_WARPS;
+    static std::mutex mu;
+    static int grid_max[64][2] = {};
+    static int sms_of[64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (grid_max[dev] == 0) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_ring<LPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        int per_sm = 0, sms = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attn_ring<LPK, G>, warps * 32, smem);
-        if (e != cudaSuccess) return e;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        grid_max[dev] = (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 1);
+    const size_t row = (size_t)2 * kRingChunk * 3 * (LPK * 8);  // bytes of one slot (K and V rows)
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (grid_max[dev][0] == 0) {
+            cudaError_t e = cudaFuncSetAttribute(k_attn_ring<LPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)(warps * kRingMaxSlots * row));
+            if (e != cudaSuccess) return e;
+            cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev);
+            for (int k = 0; k < 2; ++k) {
+                const int sl = k ? kRingMaxSlots : ALTXS_RING_SLOTS;
+                int per_sm = 0;
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attn_ring<LPK, G>, warps * 32,
+                                                                  warps * sl * row);
+                if (e != cudaSuccess) return e;
+                grid_max[dev][k] = (per_sm > 0 ? per_sm : 1) * (sms_of[dev] > 0 ? sms_of[dev] : 1);
+            }
+        }
     }
     const int n_items = D.n * D.Hkv * D.nsplit;
+    const int deep = n_items <= warps * (sms_of[dev] > 0 ? sms_of[dev] : 1) ? 1 : 0;
+    const int slots = deep ? kRingMaxSlots : ALTXS_RING_SLOTS;
+    const size_t smem = (size_t)warps * slots * row;
     const int need = (n_items + warps - 1) / warps;
-    const int grid = need < grid_max[dev] ? need : grid_max[dev];
+    const int grid = need < grid_max[dev][deep] ? need : grid_max[dev][deep];
     k_attn_ring<LPK, G><<<grid, warps * 32, smem, st>>>(c, l, n_items, slots);
     return cudaGetLastError();
 }
@@ -836,24 +862,19 @@ __global__ void k_final(StepCtx c, int lanes) { final_body(c, lanes, blockIdx.x,
 
 // logits (+ lm LoRA) -> softcap -> integer CDF -> encode / decode; written for
 // (and called only with) blocks of kCdfThreads threads
-__device__ void cdf_code_body(const StepCtx &c, int mode, int bi) {
-    extern __shared__ __align__(16) float buf[];  // [V]
-    __shared__ CdfScratch sc;
-    __shared__ float tl[128];
-    const int i = bi;
-    if (!row_active(c.b, i)) return;
+// The head's logits of row i, entries [k0, k1): the LM-head adapter's delta,
+// then the (asymmetric) tanh softcap (model.py:1478-1500); into dst (and the
+// caller's logits_out).
+__device__ __forceinline__ void head_logits(const StepCtx &c, int i, int k0, int k1, float *dst, const float *tl) {
     const Dims &D = c.D;
     const int V = D.V, R = D.r, tok = c.b.tok[i];
     const float cap = c.dsc.logit_softcap;
     const bool has_lm = R > 0 && c.b.lora && (c.dsc.lora_mask & 16) && tok >= 0;
     const float *P = has_lm ? c.b.lora + (int64_t)i * c.b.lora_stride + c.lo.lmB : nullptr;
-    if (has_lm && threadIdx.x < R) tl[threadIdx.x] = c.lt[(int64_t)i * R + threadIdx.x];
-    __syncthreads();
     const float *raw = c.logits + (int64_t)i * V;
-    // asymmetric softcap (model.py:1478-1500): separate caps above and below zero
     const float cap_n = c.dsc.asym_softcap ? c.w.softcap[1] : cap;
     const float cap_p = c.dsc.asym_softcap ? c.w.softcap[0] : cap;
-    for (int k = threadIdx.x; k < V; k += blockDim.x) {
+    for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
         float lg = 0.0f;
         if (tok >= 0) {
             float v = raw[k];
@@ -861,8 +882,43 @@ __device__ void cdf_code_body(const StepCtx &c, int mode, int bi) {
             const float cp = v >= 0.0f ? cap_p : cap_n;
             lg = __fmul_rn(cp, tanhf(__fdiv_rn(v, cp)));
         }
-        buf[k] = lg;
+        dst[k - k0] = lg;
         if (c.b.logits_out) c.b.logits_out[(int64_t)i * V + k] = lg;
+    }
+}
+
+// A few streams: the head's logits of each row in parallel over many blocks
+// (part of nparts), written over the raw logits; the CDF kernel then reads them.
+__global__ void k_head_rows(StepCtx c) {
+    __shared__ float tl[128];
+    const int i = blockIdx.x;
+    if (!row_active(c.b, i)) return;
+    const Dims &D = c.D;
+    const int R = D.r;
+    if (R > 0 && c.b.lora && (c.dsc.lora_mask & 16) && c.b.tok[i] >= 0 && threadIdx.x < R)
+        tl[threadIdx.x] = c.lt[(int64_t)i * R + threadIdx.x];
+    __syncthreads();
+    const int k0 = blockIdx.y * D.V / gridDim.y, k1 = (blockIdx.y + 1) * D.V / gridDim.y;
+    head_logits(c, i, k0, k1, c.logits + (int64_t)i * D.V + k0, tl);
+}
+
+// pre: the head's logits are already final in c.logits (k_head_rows)
+__device__ void cdf_code_body(const StepCtx &c, int mode, int bi, int pre = 0) {
+    extern __shared__ __align__(16) float buf[];  // [V]
+    __shared__ CdfScratch sc;
+    __shared__ float tl[128];
+    const int i = bi;
+    if (!row_active(c.b, i)) return;
+    const Dims &D = c.D;
+    const int V = D.V, R = D.r, tok = c.b.tok[i];
+    if (pre) {
+        if (mode == ALTXS_STEP_LOGITS) return;
+        for (int k = threadIdx.x; k < V; k += blockDim.x) buf[k] = c.logits[(int64_t)i * V + k];
+    } else {
+        const bool has_lm = R > 0 && c.b.lora && (c.dsc.lora_mask & 16) && tok >= 0;
+        if (has_lm && threadIdx.x < R) tl[threadIdx.x] = c.lt[(int64_t)i * R + threadIdx.x];
+        __syncthreads();
+        head_logits(c, i, 0, V, buf, tl);
     }
     __syncthreads();
     if (mode == ALTXS_STEP_LOGITS) return;
@@ -919,7 +975,9 @@ __device__ void cdf_code_body(const StepCtx &c, int mode, int bi) {
         }
     }
 }
-__global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode) { cdf_code_body(c, mode, blockIdx.x); }
+__global__ void __launch_bounds__(kCdfThreads) k_cdf_code(StepCtx c, int mode, int pre) {
+    cdf_code_body(c, mode, blockIdx.x, pre);
+}
 
 
 // ---------------------------------------------------------------------------
@@ -1473,7 +1531,12 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         a.ldy = D.qkv_n;
         a.epi = kEpiStore;
         if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->qkv_hi : nullptr, c.tc ? sp->qkv_lo : nullptr, nullptr, nullptr, w->tiles ? &w->tiles->qkv : nullptr))) return rc;
-        ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<D.n, 256, qkv_sm, st>>>(c, app));
+        {
+            // a few streams: one block per head of each row, so the row's heads run in parallel
+            const int nh = D.H + 2 * D.Hkv;
+            const int parts = (int64_t)D.n * nh <= 296 ? nh : 1;
+            ALTXS_LAUNCH(::altxs::kKQkvPost, st, k_qkv_post<<<dim3(D.n, parts), 256, qkv_sm, st>>>(c, app));
+        }
         {
             cudaError_t ae = cudaSuccess;
             ALTXS_LAUNCH(::altxs::kKAttn, st, ae = launch_attn(c, v, st));
@@ -1541,7 +1604,13 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     a.ldy = D.V;
     a.epi = kEpiStore;
     if ((rc = linear(a, c.nrm_h, c.nrm_l, c.tc ? sp->emb_hi : nullptr, c.tc ? sp->emb_lo : nullptr, nullptr, nullptr, w->tiles ? &w->tiles->emb : nullptr))) return rc;
-    ALTXS_LAUNCH(::altxs::kKCdfCode, st, k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode));
+    {
+        // a few streams: the head's logits of each row over many blocks first
+        const int pre = D.n <= 8 ? 1 : 0;
+        if (pre)
+            ALTXS_LAUNCH(::altxs::kKCdfCode, st, k_head_rows<<<dim3(D.n, 32), 256, 0, st>>>(c));
+        ALTXS_LAUNCH(::altxs::kKCdfCode, st, k_cdf_code<<<D.n, kCdfThreads, (size_t)D.V * 4, st>>>(c, mode, pre));
+    }
     return ALTXS_OK;
 }
 

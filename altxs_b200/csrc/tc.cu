@@ -156,14 +156,29 @@ __device__ __forceinline__ int dq_bits(uint32_t d) {
     return c == 0 ? 0 : c == 1 ? 2 : c == 2 ? 3 : c == 3 ? 4 : 32;
 }
 
-// the row's descriptor and code words from its staged segment (shared memory)
-__device__ __forceinline__ void dq_load(const unsigned char *seg, int j, DqGroup &q) {
-    q.d = reinterpret_cast<const uint32_t *>(seg)[j];
-    const uint2 *p = reinterpret_cast<const uint2 *>(seg + 256 + 8 * (q.d >> 20));
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds_u64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+// the row's descriptor and code words from its staged segment (shared-memory
+// address seg: explicit shared loads, not generic ones)
+__device__ __forceinline__ void dq_load(uint32_t seg, int j, DqGroup &q) {
+    q.d = lds_u32(seg + 4 * j);
+    const uint32_t p = seg + 256 + 8 * (q.d >> 20);
     const int b = dq_bits(q.d);
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-        const uint2 x = w < b ? p[w] : make_uint2(0u, 0u);
+        const uint2 x = w < b ? lds_u64(p + 8 * w) : make_uint2(0u, 0u);
         q.w[2 * w] = x.x;
         q.w[2 * w + 1] = x.y;
     }
@@ -171,7 +186,7 @@ __device__ __forceinline__ void dq_load(const unsigned char *seg, int j, DqGroup
 
 // 8 values -> one 16-byte chunk of the hi plane and of the lo plane
 // (hi = bf16(v), lo = bf16(v - hi), round to nearest even, two values per cvt)
-__device__ __forceinline__ void dq_put8(unsigned char *hrow, unsigned char *lrow, int pos, const float *f) {
+__device__ __forceinline__ void dq_put8(uint32_t hrow, uint32_t lrow, int pos, const float *f) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -182,8 +197,8 @@ __device__ __forceinline__ void dq_put8(unsigned char *hrow, unsigned char *lrow
         const __nv_bfloat162 lb = __floats2bfloat162_rn(r0, r1);
         l[u] = *reinterpret_cast<const uint32_t *>(&lb);
     }
-    *reinterpret_cast<uint4 *>(hrow + pos) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4 *>(lrow + pos) = make_uint4(l[0], l[1], l[2], l[3]);
+    sts_v4(hrow + pos, h[0], h[1], h[2], h[3]);
+    sts_v4(lrow + pos, l[0], l[1], l[2], l[3]);
 }
 
 // w = (code - (2^B - 1)/2) * scale, exact in fp32 (a <= 4-bit half-integer
@@ -191,7 +206,7 @@ __device__ __forceinline__ void dq_put8(unsigned char *hrow, unsigned char *lrow
 // and fma(2^23 + code, s, -2^23 s) = code * s exactly; code * s - c * s is then
 // the same exact value the plane builder forms as (code - c) * s.
 template <int B, int N1>
-__device__ __forceinline__ void dq_codes(const DqGroup &q, int i0, unsigned char *hrow, unsigned char *lrow, int r7) {
+__device__ __forceinline__ void dq_codes(const DqGroup &q, int i0, uint32_t hrow, uint32_t lrow, int r7) {
     const float s = h2f((uint16_t)(q.d & 0xffffu));
     const float k1 = __fmul_rn(-8388608.0f, s);
     const float cs = __fmul_rn((float)((1 << B) - 1) * 0.5f, s);
@@ -214,7 +229,7 @@ __device__ __forceinline__ void dq_codes(const DqGroup &q, int i0, unsigned char
 }
 
 template <int N1>
-__device__ __forceinline__ void dq_slice(const DqGroup &q, int i0, unsigned char *hrow, unsigned char *lrow, int r7) {
+__device__ __forceinline__ void dq_slice(const DqGroup &q, int i0, uint32_t hrow, uint32_t lrow, int r7) {
     const int b = dq_bits(q.d);
     if (b == 2) {
         if (i0 == 0) dq_codes<2, N1>(q, 0, hrow, lrow, r7);
@@ -597,9 +612,9 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
                         stop = true;
                         break;
                     }
-                    unsigned char *st = sm + s * Cfg::kStage;
-                    unsigned char *bh = st + 2 * Cfg::kATile;
-                    unsigned char *hrow = bh + rloc * 128, *lrow = bh + Cfg::kBTile + rloc * 128;
+                    const uint32_t st = smem_u32(sm + s * Cfg::kStage);
+                    const uint32_t bh = st + 2 * Cfg::kATile;
+                    const uint32_t hrow = bh + rloc * 128, lrow = bh + Cfg::kBTile + rloc * 128;
                     if (have) {
                         DqGroup cur;
                         dq_load(st + 2 * Cfg::kATile + 2 * Cfg::kBTile + blk * kSeg, j, cur);
