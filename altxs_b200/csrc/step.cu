@@ -63,10 +63,6 @@ struct StepCtx {
     // tensor-core path: hi/lo bf16 planes of the linear layers' inputs
     int tc;
     uint16_t *nrm_h, *nrm_l, *y_h, *y_l, *nrm2_h, *nrm2_l, *hid_h, *hid_l;
-    // split-K scratch of the tensor-core linears (partials, arrival counters)
-    float *tcpart;
-    uint32_t *tccnt;
-    int64_t tccnt_elems;
 };
 
 __device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return !b.active || b.active[i]; }
@@ -1262,20 +1258,6 @@ int launch_fused(const StepCtx &c, const altxs_model_desc *desc, int mode, GridS
 
 // ---------------------------------------------------------------------------
 
-// split-K scratch of the step's tensor-core linears (qkv, o, up, down, tied head)
-inline int64_t tc_part_max(const Dims &D) {
-    const int nk[5][2] = {{D.qkv_n, D.d}, {D.d, D.d}, {D.F, D.d}, {D.d, D.F}, {D.V, D.d}};
-    int64_t m = 0;
-    for (const auto &x : nk) m = std::max(m, tc_linear_part_elems(D.n, x[0], x[1]));
-    return m;
-}
-inline int64_t tc_cnt_max(const Dims &D) {
-    const int nk[5][2] = {{D.qkv_n, D.d}, {D.d, D.d}, {D.F, D.d}, {D.d, D.F}, {D.V, D.d}};
-    int64_t m = 0;
-    for (const auto &x : nk) m = std::max(m, tc_linear_cnt_elems(D.n, x[0], x[1]));
-    return m;
-}
-
 inline int64_t ws_size(const Dims &D) {
     auto A = [](int64_t x) { return align_up(x * 4, 256); };
     int64_t s = 0;
@@ -1293,7 +1275,6 @@ inline int64_t ws_size(const Dims &D) {
     if (D.par || D.mlora) s += A((int64_t)D.n * D.d);  // MLP output
     if (D.mlora) s += A((int64_t)D.n * D.r);          // MLP adapter t
     s += 256;                                         // grid barrier words of the fused step
-    s += A(tc_part_max(D)) + A(tc_cnt_max(D));        // split-K scratch of the tensor-core linears
     return s;
 }
 
@@ -1444,9 +1425,6 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     if (D.mlora) c.lt2 = take((int64_t)D.n * D.r);
     GridSync *gsync = reinterpret_cast<GridSync *>(p);
     p += 256;
-    c.tcpart = take(tc_part_max(D));
-    c.tccnt_elems = tc_cnt_max(D);
-    c.tccnt = reinterpret_cast<uint32_t *>(take(c.tccnt_elems));
     const altxs_split_planes *sp = w->split;
     c.tc = sp != nullptr;
     if (sp && (!sp->emb_hi || !sp->emb_lo || !sp->qkv_hi || !sp->qkv_lo || !sp->o_hi || !sp->o_lo || !sp->up_hi ||
@@ -1489,12 +1467,8 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         }
         // the producer warps expand B from the packed codes
         if (!w->planes_live && g_linear_packed && wt && q.row0 % 64 == 0) t.wt = wt;
-        t.part = c.tcpart;
-        t.cnt = c.tccnt;
         return launch_tc(t, st);
     };
-    if (c.tc && c.tccnt_elems > 0 && cudaMemsetAsync(c.tccnt, 0, c.tccnt_elems * 4, st) != cudaSuccess)
-        return ALTXS_ECUDA;
 
     ALTXS_LAUNCH(::altxs::kKEmbed, st, k_embed<<<D.n, 128, 0, st>>>(c));
     {

@@ -249,25 +249,18 @@ __device__ __forceinline__ void dq_slice(const DqGroup &q, int i0, uint32_t hrow
 
 struct Tile {
     int m0, n0, b, kb0, kb1;
-    int id, split;  // output tile index (m-tile fastest, then n-tile, then batch) and split index
     bool skip;
 };
 
-// unit u: split fastest, then m-tile (CTAs running at the same time share B
-// tiles), then n-tile, then batch; split s covers the K slices
-// [s*nk/S, (s+1)*nk/S) of its tile
-__device__ __forceinline__ Tile tile_of(const TcGemm &g, int u, int mt, int ntl, int nk, int bn) {
+// tile t: m-tile fastest (CTAs running at the same time share B tiles), then n-tile, then batch
+__device__ __forceinline__ Tile tile_of(const TcGemm &g, int t, int mt, int ntl, int nk, int bn) {
     Tile T;
-    const int S = g.splits;
-    T.split = u % S;
-    const int t = u / S;
-    T.id = t;
     T.m0 = (t % mt) * kBM;
     const int r = t / mt;
     T.n0 = (r % ntl) * bn;
     T.b = r / ntl;
-    T.kb0 = T.split * nk / S;
-    T.kb1 = (T.split + 1) * nk / S;
+    T.kb0 = 0;
+    T.kb1 = nk;
     T.skip = g.causal == 1 && T.n0 > T.m0 + kBM - 1;
     if (g.causal == 2) T.kb1 = min(nk, (T.m0 + kBM + kBK - 1) / kBK);
     if (g.causal == 3) T.kb0 = min(nk, T.m0 / kBK);
@@ -450,7 +443,7 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = (g.K + kBK - 1) / kBK;
     const int mt = (g.M + kBM - 1) / kBM, ntl = (g.N + BN - 1) / BN;
-    const int n_units = mt * ntl * g.batch * g.splits;
+    const int n_units = mt * ntl * g.batch;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], BQ ? 5 : 1);  // the A copies' transaction arrival (+ 4 dequantising warps)
@@ -661,82 +654,18 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
             tc_fence_after();
             const bool no_k = T.kb0 >= T.kb1;  // nothing accumulated: the product is zero
             const uint32_t tl = tmem + buf * Cfg::kTmemCols + ((uint32_t)(warp * 32) << 16);
-            if (g.splits == 1) {
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
-                    float v[32];
-                    __syncwarp();  // warp-collective load; the block buffer is free again
-                    tc_ld32(tl + c0, v);
-                    if (c0 + 32 >= BN) {  // accumulator fully read: hand it back to the MMA warp
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[buf]);
-                    }
-                    emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, no_k, eb, sb, vec);
-                }
-                continue;
-            }
-            // split K: this warp's 32-row slab of the partial goes to
-            // part[tile][split] ([128][BN] fp32, row-major); the slab's arrival
-            // counter picks the last of the tile's splits, which sums the
-            // partials in split order and runs the epilogue on the sum
-            float *pslot = g.part + ((int64_t)T.id * g.splits + T.split) * (kBM * BN) + (int64_t)warp * 32 * BN;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
-                __syncwarp();
+                __syncwarp();  // warp-collective load; the block buffer is free again
                 tc_ld32(tl + c0, v);
-                if (c0 + 32 >= BN) {
+                if (c0 + 32 >= BN) {  // accumulator fully read: hand it back to the MMA warp
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[buf]);
                 }
-#pragma unroll
-                for (int u = 0; u < 32; ++u) eb[lane][u] = no_k ? 0.0f : v[u];
-                __syncwarp();
-                const int sub = lane >> 3, c4 = (lane & 7) * 4;
-#pragma unroll
-                for (int it = 0; it < 8; ++it) {
-                    const float *e = eb[it * 4 + sub] + c4;
-                    *reinterpret_cast<float4 *>(pslot + (it * 4 + sub) * BN + c0 + c4) =
-                        make_float4(e[0], e[1], e[2], e[3]);
-                }
-                __syncwarp();
+                emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, no_k, eb, sb, vec);
             }
-            __threadfence();
-            __syncwarp();
-            uint32_t old = 0;
-            if (lane == 0) old = atomicAdd(g.cnt + (int64_t)T.id * 4 + warp, 1u);
-            old = __shfl_sync(kFull, old, 0);
-            if (old != (uint32_t)g.splits - 1) continue;
-            __threadfence();  // the other splits' partials are visible from here on
-            const float *pbase = g.part + (int64_t)T.id * g.splits * (kBM * BN) + (int64_t)(warp * 32 + lane) * BN;
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                float v[32];
-#pragma unroll
-                for (int u4 = 0; u4 < 8; ++u4) {
-                    const float4 p0 = __ldcg(reinterpret_cast<const float4 *>(pbase + c0) + u4);
-                    v[4 * u4] = p0.x;
-                    v[4 * u4 + 1] = p0.y;
-                    v[4 * u4 + 2] = p0.z;
-                    v[4 * u4 + 3] = p0.w;
-                }
-                for (int sp = 1; sp < g.splits; ++sp) {
-                    const float *ps = pbase + (int64_t)sp * (kBM * BN) + c0;
-#pragma unroll
-                    for (int u4 = 0; u4 < 8; ++u4) {
-                        const float4 p = __ldcg(reinterpret_cast<const float4 *>(ps) + u4);
-                        v[4 * u4] = __fadd_rn(v[4 * u4], p.x);
-                        v[4 * u4 + 1] = __fadd_rn(v[4 * u4 + 1], p.y);
-                        v[4 * u4 + 2] = __fadd_rn(v[4 * u4 + 2], p.z);
-                        v[4 * u4 + 3] = __fadd_rn(v[4 * u4 + 3], p.w);
-                    }
-                }
-                __syncwarp();
-                emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, false, eb, sb, vec);
-            }
-            if (lane == 0) g.cnt[(int64_t)T.id * 4 + warp] = 0;  // ready for the next call
         }
         if (g.tma_c && lane == 0) bulk_wait_all();  // every tensor store of this warp has landed
     }
@@ -859,11 +788,10 @@ int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
         return ALTXS_EINVAL;
     }
     TcGemm gk = g;
-    // (the split epilogue's partials use the transpose buffer the TMA-store box shares)
-    gk.tma_c = g.splits == 1 && make_c_map(&tc_map, g) ? 1 : 0;
+    gk.tma_c = make_c_map(&tc_map, g) ? 1 : 0;
     if (!gk.tma_c) tc_map = ta_hi;  // unused
     // persistent: at most one CTA per SM walks the units
-    const int64_t units = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch * g.splits;
+    const int64_t units = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch;
     const int grid = (int)(units < sms ? units : sms);
     ALTXS_LAUNCH(::altxs::kKQmm, st,
                  k_tc_gemm<BN, AMN, BMN, BQ><<<grid, TcThreads<BQ>::kN, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo,
@@ -882,18 +810,13 @@ int launch_bn(const TcGemm &g, int sms, cudaStream_t st) {
 
 }  // namespace
 
-int launch_tc_gemm(const TcGemm &g0, cudaStream_t st) {
-    TcGemm g = g0;
-    if (g.splits == 0) g.splits = 1;  // zero-initialised arguments: no split
+int launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
     if (g.K <= 0 || !op_ok(g.a) || (!g.bq && !op_ok(g.b))) return ALTXS_EINVAL;
     if (g.causal < 0 || g.causal > 3) return ALTXS_EINVAL;
     if (g.bq && (!g.wt.data || g.wt.cols != g.K || g.K % kBK || g.wq_row0 < 0 || g.wq_row0 % 64 ||
                  g.wq_row0 + g.N > g.wt.rows || g.batch != 1 || g.b.mn_major ||
                  (reinterpret_cast<uintptr_t>(g.wt.data) & 15)))
-        return ALTXS_EINVAL;
-    if (g.splits < 1 || g.splits > (g.K + kBK - 1) / kBK) return ALTXS_EINVAL;
-    if (g.splits > 1 && (!g.part || !g.cnt || g.causal != 0 || (reinterpret_cast<uintptr_t>(g.part) & 15)))
         return ALTXS_EINVAL;
     if (g.epi == kEpiResid && (!g.R || !g.colscale || g.batch != 1)) return ALTXS_EINVAL;
     if ((g.p_hi && (!g.p_lo || g.ldp < g.N || g.batch != 1)) || (g.Y2 && g.batch != 1)) return ALTXS_EINVAL;
@@ -956,39 +879,7 @@ int launch_tc(const TcArgs &a, cudaStream_t st) {
         g.wt = *a.wt;
         g.wq_row0 = a.row0;
     }
-    g.splits = 1;
-    const int sp = tc_linear_splits(a.N, a.K);
-    if (sp > 1 && a.part && a.cnt) {
-        g.splits = sp;
-        g.part = a.part;
-        g.cnt = a.cnt;
-    }
     return launch_tc_gemm(g, st);
-}
-
-int tc_linear_splits(int N, int K) {
-    // No split.  Splitting the K loop of the layers with few output tiles
-    // (o and down at M <= 256: 16 tiles) into 2-4 ranges was measured on a
-    // B200 (ncu launch list of the 256-stream step, same box, A/B): the
-    // tensor-core linears took 1174 us per two steps with the split against
-    // 1123 us without, and the 2048-stream step lost 2 %: a call at these
-    // sizes is bound by its fixed costs (launch, set-up, pipeline fill,
-    // epilogue), not by its K loop, and the partials add traffic.
-    (void)N;
-    (void)K;
-    return 1;
-}
-
-int64_t tc_linear_part_elems(int M, int N, int K) {
-    const int s = tc_linear_splits(N, K);
-    if (s <= 1 || M <= 0 || N <= 0) return 0;
-    // tiles x splits x 128 x BN for the wider of the two tile widths' padding
-    return align_up(M, kBM) * align_up(N, 128) * s;
-}
-
-int64_t tc_linear_cnt_elems(int M, int N, int K) {
-    if (tc_linear_splits(N, K) <= 1 || M <= 0 || N <= 0) return 0;
-    return (int64_t)((M + kBM - 1) / kBM) * ((N + 63) / 64) * 4;  // 64-wide tiles: the most tiles
 }
 
 int set_wait_limit_tc(uint32_t limit) {
@@ -1195,8 +1086,7 @@ int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo
 
 int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K) {
     if (M < 0 || N < 0 || K < 0) return -1;
-    return altxs::align_up((int64_t)M * K * 2, 256) * 2 + altxs::align_up(altxs::tc_linear_part_elems(M, N, K) * 4, 256) +
-           altxs::align_up(altxs::tc_linear_cnt_elems(M, N, K) * 4, 256);
+    return altxs::align_up((int64_t)M * K * 2, 256) * 2;
 }
 
 int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int M, float *Y, void *workspace,
@@ -1207,16 +1097,9 @@ int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int 
     const int K = w->cols;
     if (!workspace || workspace_bytes < altxs_linear_tc_workspace_bytes(M, N, K)) return ALTXS_EINVAL;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    unsigned char *p = static_cast<unsigned char *>(workspace);
-    uint16_t *xh = reinterpret_cast<uint16_t *>(p);
-    p += align_up((int64_t)M * K * 2, 256);
-    uint16_t *xl = reinterpret_cast<uint16_t *>(p);
-    p += align_up((int64_t)M * K * 2, 256);
-    float *part = reinterpret_cast<float *>(p);
-    p += align_up(tc_linear_part_elems(M, N, K) * 4, 256);
-    uint32_t *cnt = reinterpret_cast<uint32_t *>(p);
-    const int64_t nc = tc_linear_cnt_elems(M, N, K);
-    if (nc > 0 && cudaMemsetAsync(cnt, 0, nc * 4, st) != cudaSuccess) return ALTXS_ECUDA;
+    uint16_t *xh = static_cast<uint16_t *>(workspace);
+    uint16_t *xl = reinterpret_cast<uint16_t *>(static_cast<unsigned char *>(workspace) +
+                                                align_up((int64_t)M * K * 2, 256));
     ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_rows<<<M, 256, 0, st>>>(X, K, K, xh, xl));
     TcArgs t{};
     t.a_hi = xh;
@@ -1231,8 +1114,6 @@ int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int 
     t.Y = Y;
     t.ldy = N;
     t.wt = w;
-    t.part = part;
-    t.cnt = cnt;
     return launch_tc(t, st);
 }
 

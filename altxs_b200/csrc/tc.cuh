@@ -73,14 +73,6 @@ struct TcGemm {
     int bq;
     altxs_qtiles wt;
     int64_t wq_row0;
-    // split K: each output tile's K slices are cut into `splits` equal ranges
-    // run as separate units; every unit writes its fp32 partial to part
-    // ([tile][split][128][BN]) and the last unit of each 32-row slab (arrival
-    // counters cnt[tile][4], zero on entry and left zero) sums the partials in
-    // split order and runs the epilogue.  1 = no split.
-    int splits;
-    float *part;
-    uint32_t *cnt;
 };
 
 // 0 on success.  K and the operands' K extents must be multiples of 8, plane
@@ -107,22 +99,10 @@ struct TcArgs {
     int64_t ldp;
     uint32_t *status;
     int64_t status_stride;
-    // optional: the packed weights (B rows from wt instead of the planes) and
-    // the split-K scratch (tc_linear_part_elems / tc_linear_cnt_elems for M, N, K)
+    // optional: the packed weights (B rows from wt instead of the planes)
     const altxs_qtiles *wt;
-    float *part;
-    uint32_t *cnt;
 };
 int launch_tc(const TcArgs &a, cudaStream_t stream);
-
-// Split of the K loop of a step's linear layer with N outputs over K inputs.
-// It depends on the layer shape only, never on M, so every row's arithmetic
-// is the same whatever the batch: layers with few output tiles get more
-// units (one per SM-sized share of the device at small M).
-int tc_linear_splits(int N, int K);
-// scratch a launch_tc call with the split needs (0 when the layer is not split)
-int64_t tc_linear_part_elems(int M, int N, int K);
-int64_t tc_linear_cnt_elems(int M, int N, int K);
 
 // An fp32 GEMM with the semantics of GemmArgs (gemm.cuh: C[b] = alpha op(A)
 // op(B) + beta C, batch b reading A batch b / adiv and B batch b / bdiv,
