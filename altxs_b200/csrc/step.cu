@@ -1006,12 +1006,6 @@ struct FusedProg {
     int sched[kFusedMaxApps];  // physical layer of each application
 };
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 // All blocks meet; ok = 0 from any thread of any block aborts the kernel.
 // One arrival word: every block adds 1 except block 0, which adds
 // 0x80000000 - (blocks - 1), so the word's top bit flips when the last block
