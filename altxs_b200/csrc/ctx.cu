@@ -99,7 +99,7 @@ int use_device(const altxs_ctx *c) { return cudaSetDevice(c->device) == cudaSucc
 
 // Bumped whenever a kernel change alters any result bit of the step or the
 // update (the same number as the Python engine's payload fingerprint).
-constexpr uint64_t kNumerics = 2;
+constexpr uint64_t kNumerics = 3;
 
 struct Fnv {
     uint64_t h = 1469598103934665603ull;

@@ -60,9 +60,13 @@ struct StepCtx {
     float *x, *x0, *nrm, *nrm2, *skip, *qkv, *q, *part, *y, *ao, *hid, *logits, *lt;
     float *lane1, *mo;  // parallel lanes: the MLP lane; the MLP output (also with MLP adapters)
     float *lt2;         // MLP adapter: t = A n2 per stream [n][r]
-    // tensor-core path: hi/lo bf16 planes of the linear layers' inputs
+    // tensor-core path: hi/lo bf16 planes of the linear layers' inputs; split-K
+    // scratch of the linears (partials, arrival counters)
     int tc;
     uint16_t *nrm_h, *nrm_l, *y_h, *y_l, *nrm2_h, *nrm2_l, *hid_h, *hid_l;
+    float *tcpart;
+    uint32_t *tccnt;
+    int64_t tccnt_elems;
 };
 
 __device__ __forceinline__ bool row_active(const altxs_batch &b, int i) { return !b.active || b.active[i]; }
@@ -1252,6 +1256,17 @@ int launch_fused(const StepCtx &c, const altxs_model_desc *desc, int mode, GridS
 
 // ---------------------------------------------------------------------------
 
+// split-K scratch of the step's tensor-core linears (qkv, o, up, down, tied head)
+inline int64_t tc_scratch(const Dims &D, bool counters) {
+    const int NK[5][2] = {{D.qkv_n, D.d}, {D.d, D.d}, {D.F, D.d}, {D.d, D.F}, {D.V, D.d}};
+    int64_t m = 0;
+    for (const auto &nk : NK) {
+        const int64_t e = counters ? tc_linear_cnt_elems(D.n, nk[0], nk[1]) : tc_linear_part_elems(D.n, nk[0], nk[1]);
+        m = e > m ? e : m;
+    }
+    return m;
+}
+
 inline int64_t ws_size(const Dims &D) {
     auto A = [](int64_t x) { return align_up(x * 4, 256); };
     int64_t s = 0;
@@ -1268,6 +1283,7 @@ inline int64_t ws_size(const Dims &D) {
     if (D.par) s += A((int64_t)D.n * D.d);            // lane 1
     if (D.par || D.mlora) s += A((int64_t)D.n * D.d);  // MLP output
     if (D.mlora) s += A((int64_t)D.n * D.r);          // MLP adapter t
+    s += A(tc_scratch(D, false)) + A(tc_scratch(D, true));  // split K of the tensor-core linears
     s += 256;                                         // grid barrier words of the fused step
     return s;
 }
@@ -1417,6 +1433,9 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
     if (D.par) c.lane1 = take((int64_t)D.n * D.d);
     if (D.par || D.mlora) c.mo = take((int64_t)D.n * D.d);
     if (D.mlora) c.lt2 = take((int64_t)D.n * D.r);
+    c.tcpart = take(tc_scratch(D, false));
+    c.tccnt_elems = tc_scratch(D, true);
+    c.tccnt = reinterpret_cast<uint32_t *>(take(c.tccnt_elems));
     GridSync *gsync = reinterpret_cast<GridSync *>(p);
     p += 256;
     const altxs_split_planes *sp = w->split;
@@ -1461,9 +1480,16 @@ int altxs_step(const altxs_model_desc *desc, const altxs_weights *w, const altxs
         }
         // the producer warps expand B from the packed codes
         if (!w->planes_live && g_linear_packed && wt && q.row0 % 64 == 0) t.wt = wt;
+        if (c.tccnt_elems > 0) {
+            t.part = c.tcpart;
+            t.cnt = c.tccnt;
+        }
         return launch_tc(t, st);
     };
 
+    // the linears' split-K counters start from zero (each launch also leaves them zero)
+    if (c.tc && c.tccnt_elems > 0 && cudaMemsetAsync(c.tccnt, 0, c.tccnt_elems * 4, st) != cudaSuccess)
+        return ALTXS_ECUDA;
     ALTXS_LAUNCH(::altxs::kKEmbed, st, k_embed<<<D.n, 128, 0, st>>>(c));
     {
         static bool attr_done[64] = {};

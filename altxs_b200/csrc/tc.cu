@@ -50,7 +50,6 @@ struct TcCfg {
     static constexpr int kStore = 4 * 32 * 33 * 4;
     static constexpr int kSmem = kStages * kStage + kStore + 1024;  // + alignment slack
     static_assert(kSmem + 256 <= 227 * 1024, "shared memory");
-    static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
     // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B,
     // A/B major-ness, M = 128, N = BN
     static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)AMN << 15) |
@@ -249,18 +248,40 @@ __device__ __forceinline__ void dq_slice(const DqGroup &q, int i0, uint32_t hrow
 
 struct Tile {
     int m0, n0, b, kb0, kb1;
+    int id;      // output tile (unit without its split)
+    int c0, c1;  // chunked K: the unit's chunks
     bool skip;
 };
 
-// tile t: m-tile fastest (CTAs running at the same time share B tiles), then n-tile, then batch
+__device__ __forceinline__ int n_chunks(int nk) { return (nk + kTcChunkKb - 1) / kTcChunkKb; }
+// chunks per unit (the accumulators a unit keeps in tensor memory)
+__device__ __forceinline__ int unit_chunks(const TcGemm &g, int nk) {
+    return g.chunked ? (n_chunks(nk) + g.splits - 1) / g.splits : 1;
+}
+
+// unit t: split slowest; within a split m-tile fastest (CTAs running at the
+// same time share B tiles), then n-tile, then batch
 __device__ __forceinline__ Tile tile_of(const TcGemm &g, int t, int mt, int ntl, int nk, int bn) {
     Tile T;
+    const int ntiles = mt * ntl * g.batch;
+    const int sp = t / ntiles;
+    t -= sp * ntiles;
+    T.id = t;
     T.m0 = (t % mt) * kBM;
     const int r = t / mt;
     T.n0 = (r % ntl) * bn;
     T.b = r / ntl;
     T.kb0 = 0;
     T.kb1 = nk;
+    T.c0 = 0;
+    T.c1 = 1;
+    if (g.chunked) {
+        const int nch = n_chunks(nk), per = unit_chunks(g, nk);
+        T.c0 = min(nch, sp * per);
+        T.c1 = min(nch, T.c0 + per);
+        T.kb0 = T.c0 * kTcChunkKb;
+        T.kb1 = min(nk, T.c1 * kTcChunkKb);
+    }
     T.skip = g.causal == 1 && T.n0 > T.m0 + kBM - 1;
     if (g.causal == 2) T.kb1 = min(nk, (T.m0 + kBM + kBK - 1) / kBK);
     if (g.causal == 3) T.kb0 = min(nk, T.m0 / kBK);
@@ -443,7 +464,13 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = (g.K + kBK - 1) / kBK;
     const int mt = (g.M + kBM - 1) / kBM, ntl = (g.N + BN - 1) / BN;
-    const int n_units = mt * ntl * g.batch;
+    const int n_units = mt * ntl * g.batch * g.splits;
+    // tensor memory: nbuf tiles in flight, each with `nacc` accumulators of BN columns
+    const int nacc = unit_chunks(g, nk);
+    const uint32_t bufcols = (uint32_t)(nacc * BN);
+    const int nbuf = 2 * bufcols <= 512 ? 2 : 1;
+    uint32_t tcols = 32;
+    while (tcols < nbuf * bufcols) tcols <<= 1;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], BQ ? 5 : 1);  // the A copies' transaction arrival (+ 4 dequantising warps)
@@ -460,7 +487,7 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
     }
     if (warp == 5) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_sh)),
-                     "r"(2 * Cfg::kTmemCols)
+                     "r"(tcols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -538,14 +565,14 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
             for (int t = blockIdx.x; t < n_units && ok; t += gridDim.x) {
                 const Tile T = tile_of(g, t, mt, ntl, nk, BN);
                 if (T.skip) continue;
-                const int buf = j & 1, use = j >> 1;
+                const int buf = j % nbuf, use = j / nbuf;
                 ++j;
                 if (use > 0 && !mbar_wait_bounded(&tempty[buf], (use - 1) & 1, wait_limit())) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t acc = tmem + buf * Cfg::kTmemCols;
+                const uint32_t acc0 = tmem + buf * bufcols;
                 for (int kb = T.kb0; kb < T.kb1; ++kb, ++q) {
                     const int s = q % S, r = q / S;
                     if (!mbar_wait_bounded(&full[s], r & 1, wait_limit())) {
@@ -555,9 +582,13 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
                     tc_fence_after();
                     const uint32_t ah = smem_u32(sm + s * Cfg::kStage);
                     const uint32_t al = ah + Cfg::kATile, bh = ah + 2 * Cfg::kATile, bl = bh + Cfg::kBTile;
+                    // chunked K: each chunk starts its own accumulator from zero
+                    const int ch = g.chunked ? kb / kTcChunkKb - T.c0 : 0;
+                    const bool fresh = g.chunked ? kb % kTcChunkKb == 0 : kb == T.kb0;
+                    const uint32_t acc = acc0 + (uint32_t)(ch * BN);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
-                        const uint32_t first = kb == T.kb0 && kk == 0;
+                        const uint32_t first = fresh && kk == 0;
                         tc_mma(acc, op_desc<AMN>(ah, kk), op_desc<BMN>(bh, kk), Cfg::kIdesc, !first);
                         tc_mma(acc, op_desc<AMN>(ah, kk), op_desc<BMN>(bl, kk), Cfg::kIdesc, 1u);
                         tc_mma(acc, op_desc<AMN>(al, kk), op_desc<BMN>(bh, kk), Cfg::kIdesc, 1u);
@@ -642,7 +673,7 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
         for (int t = blockIdx.x; t < n_units; t += gridDim.x) {
             const Tile T = tile_of(g, t, mt, ntl, nk, BN);
             if (T.skip) continue;
-            const int buf = j & 1, use = j >> 1;
+            const int buf = j % nbuf, use = j / nbuf;
             ++j;
             const bool gave_up = __any_sync(kFull, abort_sh != 0);  // warp-uniform
             const bool ok = !gave_up && __all_sync(kFull, mbar_wait_bounded(&tfull[buf], use & 1, wait_limit()));
@@ -653,19 +684,92 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
             }
             tc_fence_after();
             const bool no_k = T.kb0 >= T.kb1;  // nothing accumulated: the product is zero
-            const uint32_t tl = tmem + buf * Cfg::kTmemCols + ((uint32_t)(warp * 32) << 16);
+            const uint32_t tl = tmem + buf * bufcols + ((uint32_t)(warp * 32) << 16);
+            const int na = T.c1 - T.c0;  // accumulators of this unit
+            if (g.splits == 1) {
+                // the tile's chunk sums added in chunk order (one accumulator unless chunked)
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    __syncwarp();  // warp-collective load; the block buffer is free again
+                    tc_ld32(tl + c0, v);
+#pragma unroll 1
+                    for (int a = 1; a < na; ++a) {
+                        float w[32];
+                        tc_ld32(tl + a * BN + c0, w);
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) v[u] = __fadd_rn(v[u], w[u]);
+                    }
+                    if (c0 + 32 >= BN) {  // accumulators fully read: hand them back to the MMA warp
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
+                    }
+                    emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, no_k, eb, sb, vec);
+                }
+                continue;
+            }
+            // split K: this unit's chunk sums of the warp's 32 rows go to the
+            // partials (float4 j of row `lane` at [j][lane]: every warp store is
+            // 512 contiguous bytes); the slab's arrival counter picks the last
+            // unit, which adds all chunk sums in chunk order and runs the epilogue
+            const int nch = n_chunks(nk);
+            constexpr int kSlab = 32 * BN / 4;  // float4 per warp slab of one chunk
+            float4 *pbase = reinterpret_cast<float4 *>(g.part) + ((int64_t)T.id * nch * 4 + warp) * kSlab;
+#pragma unroll 1
+            for (int a = 0; a < na; ++a) {
+                float4 *pw = pbase + (int64_t)(T.c0 + a) * 4 * kSlab;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    __syncwarp();
+                    tc_ld32(tl + a * BN + c0, v);
+#pragma unroll
+                    for (int u4 = 0; u4 < 8; ++u4)
+                        __stcg(pw + (c0 / 4 + u4) * 32 + lane,
+                               make_float4(v[4 * u4], v[4 * u4 + 1], v[4 * u4 + 2], v[4 * u4 + 3]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            uint32_t old = 0;
+            if (lane == 0) {
+                // release: the warp's partials (ordered before by the warp barrier)
+                // before the arrival; acquire: the other units' partials after it
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                old = atomicAdd(g.cnt + (int64_t)T.id * 4 + warp, 1u);
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            }
+            old = __shfl_sync(kFull, old, 0);
+            if (old != (uint32_t)g.splits - 1) continue;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
-                __syncwarp();  // warp-collective load; the block buffer is free again
-                tc_ld32(tl + c0, v);
-                if (c0 + 32 >= BN) {  // accumulator fully read: hand it back to the MMA warp
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+                for (int u4 = 0; u4 < 8; ++u4) {
+                    const float4 p = __ldcg(pbase + (c0 / 4 + u4) * 32 + lane);
+                    v[4 * u4] = p.x;
+                    v[4 * u4 + 1] = p.y;
+                    v[4 * u4 + 2] = p.z;
+                    v[4 * u4 + 3] = p.w;
                 }
-                emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, no_k, eb, sb, vec);
+#pragma unroll 1
+                for (int c = 1; c < nch; ++c) {
+                    const float4 *pr = pbase + (int64_t)c * 4 * kSlab + c0 / 4 * 32 + lane;
+#pragma unroll
+                    for (int u4 = 0; u4 < 8; ++u4) {
+                        const float4 p = __ldcg(pr + u4 * 32);
+                        v[4 * u4] = __fadd_rn(v[4 * u4], p.x);
+                        v[4 * u4 + 1] = __fadd_rn(v[4 * u4 + 1], p.y);
+                        v[4 * u4 + 2] = __fadd_rn(v[4 * u4 + 2], p.z);
+                        v[4 * u4 + 3] = __fadd_rn(v[4 * u4 + 3], p.w);
+                    }
+                }
+                __syncwarp();
+                emit_block<BN>(g, T, &tc_map, warp, lane, c0, v, false, eb, sb, vec);
             }
+            if (lane == 0) g.cnt[(int64_t)T.id * 4 + warp] = 0;  // ready for the next launch
         }
         if (g.tma_c && lane == 0) bulk_wait_all();  // every tensor store of this warp has landed
     }
@@ -673,7 +777,7 @@ __global__ void __launch_bounds__(TcThreads<BQ>::kN, 1)
     __syncthreads();
     if (warp == 5) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * Cfg::kTmemCols)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols)
                      : "memory");
     }
 }
@@ -791,7 +895,7 @@ int launch_cfg(const TcGemm &g, int sms, cudaStream_t st) {
     gk.tma_c = make_c_map(&tc_map, g) ? 1 : 0;
     if (!gk.tma_c) tc_map = ta_hi;  // unused
     // persistent: at most one CTA per SM walks the units
-    const int64_t units = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch;
+    const int64_t units = (int64_t)((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * g.batch * g.splits;
     const int grid = (int)(units < sms ? units : sms);
     ALTXS_LAUNCH(::altxs::kKQmm, st,
                  k_tc_gemm<BN, AMN, BMN, BQ><<<grid, TcThreads<BQ>::kN, Cfg::kSmem, st>>>(ta_hi, ta_lo, tb_hi, tb_lo,
@@ -810,7 +914,8 @@ int launch_bn(const TcGemm &g, int sms, cudaStream_t st) {
 
 }  // namespace
 
-int launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
+int launch_tc_gemm(const TcGemm &g0, cudaStream_t st) {
+    TcGemm g = g0;
     if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return ALTXS_OK;
     if (g.K <= 0 || !op_ok(g.a) || (!g.bq && !op_ok(g.b))) return ALTXS_EINVAL;
     if (g.causal < 0 || g.causal > 3) return ALTXS_EINVAL;
@@ -833,8 +938,23 @@ int launch_tc_gemm(const TcGemm &g, cudaStream_t st) {
     if (dev < 0 || dev >= 64) return ALTXS_ECUDA;
     if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     const int64_t mt = (g.M + kBM - 1) / kBM;
-    // wide tiles when they still fill the device, narrow ones otherwise
-    if (mt * ((g.N + 127) / 128) * g.batch >= sms[dev]) return launch_bn<128>(g, sms[dev], st);
+    // chunked K: every chunk's accumulator stays in tensor memory until the epilogue
+    const int nk = (g.K + kBK - 1) / kBK, nch = (nk + kTcChunkKb - 1) / kTcChunkKb;
+    if (g.chunked && (g.causal != 0 || nch > kTcMaxChunks)) return ALTXS_EINVAL;
+    g.splits = 1;
+    // wide tiles when they still fill the device (and their chunks fit twice in
+    // tensor memory), narrow ones otherwise
+    if (mt * ((g.N + 127) / 128) * g.batch >= sms[dev] && (!g.chunked || nch <= 2))
+        return launch_bn<128>(g, sms[dev], st);
+    // few tiles: spread each tile's chunks over more CTAs (the sums do not depend on it)
+    const int64_t tiles = mt * ((g.N + 63) / 64) * g.batch;
+    if (g.chunked && g.part && g.cnt && nch >= 2 && tiles <= kTcSplitTiles && 2 * tiles <= sms[dev]) {
+        if ((reinterpret_cast<uintptr_t>(g.part) & 15) || (reinterpret_cast<uintptr_t>(g.cnt) & 3))
+            return ALTXS_EINVAL;
+        const int s0 = (int)(sms[dev] / tiles < nch ? sms[dev] / tiles : nch);
+        const int per = (nch + s0 - 1) / s0;
+        g.splits = (nch + per - 1) / per;  // no unit without a chunk
+    }
     return launch_bn<64>(g, sms[dev], st);
 }
 
@@ -879,7 +999,25 @@ int launch_tc(const TcArgs &a, cudaStream_t st) {
         g.wt = *a.wt;
         g.wq_row0 = a.row0;
     }
+    // chunked K whenever the chunks fit in tensor memory: a row's bits are then
+    // the same whether its tile's K loop runs on one CTA or is split
+    g.chunked = (a.K / kBK + kTcChunkKb - 1) / kTcChunkKb <= kTcMaxChunks ? 1 : 0;
+    g.part = a.part;
+    g.cnt = a.cnt;
     return launch_tc_gemm(g, st);
+}
+
+int64_t tc_linear_part_elems(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const int64_t nch = ((K + kBK - 1) / kBK + kTcChunkKb - 1) / kTcChunkKb;
+    const int64_t tiles = (int64_t)((M + kBM - 1) / kBM) * ((N + 63) / 64);
+    if (nch < 2 || nch > kTcMaxChunks || tiles > kTcSplitTiles) return 0;
+    return tiles * nch * kBM * 64;
+}
+
+int64_t tc_linear_cnt_elems(int M, int N, int K) {
+    if (tc_linear_part_elems(M, N, K) == 0) return 0;
+    return (int64_t)((M + kBM - 1) / kBM) * ((N + 63) / 64) * 4;
 }
 
 int set_wait_limit_tc(uint32_t limit) {
@@ -977,6 +1115,21 @@ __global__ void k_split_rows(const float *X, int64_t ldx, int K, uint16_t *hi, u
     for (int k = threadIdx.x; k < K; k += blockDim.x) altxs::split_store(hi, lo, m * K + k, X[m * ldx + k]);
 }
 
+// X planes [M][K] x 2, then (when the call can split K) the partials and the
+// arrival counters; the counters are zeroed on the stream.
+int linear_scratch(void *workspace, int64_t bytes, int M, int N, int K, bool want_split, uint16_t **xh,
+                   uint16_t **xl, altxs::TcArgs &t, cudaStream_t st) {
+    using namespace altxs;
+    unsigned char *p = static_cast<unsigned char *>(workspace);
+    const int64_t xb = align_up((int64_t)M * K * 2, 256);
+    *xh = reinterpret_cast<uint16_t *>(p);
+    *xl = reinterpret_cast<uint16_t *>(p + xb);
+    const int64_t pe = tc_linear_part_elems(M, N, K), ce = tc_linear_cnt_elems(M, N, K);
+    if (!want_split || pe == 0 || bytes < altxs_linear_tc_workspace_bytes(M, N, K)) return ALTXS_OK;
+    t.part = reinterpret_cast<float *>(p + 2 * xb);
+    t.cnt = reinterpret_cast<uint32_t *>(p + 2 * xb + align_up(pe * 4, 256));
+    return cudaMemsetAsync(t.cnt, 0, ce * 4, st) == cudaSuccess ? ALTXS_OK : ALTXS_ECUDA;
+}
 }  // namespace
 
 extern "C" {
@@ -1041,6 +1194,7 @@ int64_t altxs_linear_workspace_bytes(int M, int K) {
     return altxs::align_up((int64_t)M * K * 2, 256) * 2;
 }
 
+
 int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo, int row0, int N, const float *X,
                  int M, float *Y, void *workspace, int64_t workspace_bytes, altxs_stream_t stream) {
     using namespace altxs;
@@ -1063,11 +1217,11 @@ int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo
     }
     const int K = m->cols;
     if (!workspace || workspace_bytes < altxs_linear_workspace_bytes(M, K)) return ALTXS_EINVAL;
-    uint16_t *xh = static_cast<uint16_t *>(workspace);
-    uint16_t *xl = reinterpret_cast<uint16_t *>(static_cast<unsigned char *>(workspace) +
-                                                align_up((int64_t)M * K * 2, 256));
-    ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_rows<<<M, 256, 0, st>>>(X, K, K, xh, xl));
     TcArgs t{};
+    uint16_t *xh, *xl;
+    const int rc = linear_scratch(workspace, workspace_bytes, M, N, K, true, &xh, &xl, t, st);
+    if (rc != ALTXS_OK) return rc;
+    ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_rows<<<M, 256, 0, st>>>(X, K, K, xh, xl));
     t.a_hi = xh;
     t.a_lo = xl;
     t.lda = K;
@@ -1085,8 +1239,10 @@ int altxs_linear(const altxs_qmat *m, const uint16_t *w_hi, const uint16_t *w_lo
 }
 
 int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K) {
+    using namespace altxs;
     if (M < 0 || N < 0 || K < 0) return -1;
-    return altxs::align_up((int64_t)M * K * 2, 256) * 2;
+    return align_up((int64_t)M * K * 2, 256) * 2 + align_up(tc_linear_part_elems(M, N, K) * 4, 256) +
+           align_up(tc_linear_cnt_elems(M, N, K) * 4, 256);
 }
 
 int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int M, float *Y, void *workspace,
@@ -1097,11 +1253,11 @@ int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int 
     const int K = w->cols;
     if (!workspace || workspace_bytes < altxs_linear_tc_workspace_bytes(M, N, K)) return ALTXS_EINVAL;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    uint16_t *xh = static_cast<uint16_t *>(workspace);
-    uint16_t *xl = reinterpret_cast<uint16_t *>(static_cast<unsigned char *>(workspace) +
-                                                align_up((int64_t)M * K * 2, 256));
-    ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_rows<<<M, 256, 0, st>>>(X, K, K, xh, xl));
     TcArgs t{};
+    uint16_t *xh, *xl;
+    const int rc = linear_scratch(workspace, workspace_bytes, M, N, K, true, &xh, &xl, t, st);
+    if (rc != ALTXS_OK) return rc;
+    ALTXS_LAUNCH(::altxs::kKQmm, st, k_split_rows<<<M, 256, 0, st>>>(X, K, K, xh, xl));
     t.a_hi = xh;
     t.a_lo = xl;
     t.lda = K;

@@ -73,7 +73,21 @@ struct TcGemm {
     int bq;
     altxs_qtiles wt;
     int64_t wq_row0;
+    // chunked K (the step's linears; causal 0): the K loop runs in chunks of
+    // kTcChunkKb 64-wide slices, each accumulated from zero in its own
+    // tensor-memory accumulator, and the chunk sums are added in chunk order,
+    // so a result does not depend on how many CTAs share a tile's chunks.
+    // splits > 1: a unit is a range of one tile's chunks; its chunk sums go to
+    // part ([tile][chunk][4 warps][BN/4][32 rows] float4) and the last unit of
+    // each 32-row slab (arrival counters cnt [tile][4], zero before the launch
+    // and left zero after it) adds them and runs the epilogue.
+    int chunked, splits;
+    float *part;
+    uint32_t *cnt;
 };
+constexpr int kTcChunkKb = 8;     // slices per chunk (512 of K)
+constexpr int kTcMaxChunks = 8;   // chunks a tile's accumulators hold in tensor memory (K <= 4096)
+constexpr int kTcSplitTiles = 80; // most 64-wide tiles a split launch has
 
 // 0 on success.  K and the operands' K extents must be multiples of 8, plane
 // pointers 16-byte aligned, ld and bstride multiples of 8.
@@ -101,8 +115,15 @@ struct TcArgs {
     int64_t status_stride;
     // optional: the packed weights (B rows from wt instead of the planes)
     const altxs_qtiles *wt;
+    // optional: split-K scratch (tc_linear_part_elems floats, tc_linear_cnt_elems
+    // counters, zeroed before the call); without it the K loop is not split
+    float *part;
+    uint32_t *cnt;
 };
 int launch_tc(const TcArgs &a, cudaStream_t stream);
+// Scratch of launch_tc's split K for an M x N x K linear (0 when it never splits).
+int64_t tc_linear_part_elems(int M, int N, int K);
+int64_t tc_linear_cnt_elems(int M, int N, int K);
 
 // An fp32 GEMM with the semantics of GemmArgs (gemm.cuh: C[b] = alpha op(A)
 // op(B) + beta C, batch b reading A batch b / adiv and B batch b / bdiv,

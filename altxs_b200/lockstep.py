@@ -34,7 +34,7 @@ VERSION = 1
 HEADER_FLAG = 1 << 63
 # Bumped whenever a kernel change alters any result bit of the step or the
 # updates, so that payloads of an older build are refused rather than desynced.
-NUMERICS = 2
+NUMERICS = 3
 
 
 class LockstepMismatch(ValueError):
