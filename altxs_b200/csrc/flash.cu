@@ -1,0 +1,409 @@
+// Causal window attention on the tensor cores (sm_100a), one CTA per
+// (128-query tile, head), the scores never leaving the SM.
+//
+// Operands are hi/lo bf16 planes (tc.cuh: x = hi + lo to 16 significand
+// bits; a product is hi*hi + hi*lo + lo*hi with fp32 accumulation), written by
+// a split pass: Q and K as [head][T][64] (head dim zero-padded to one 128-byte
+// swizzle row), V transposed as [kv head][hd][align8(T)] so that every MMA
+// operand is K-major.  Per key tile j (128 keys):
+//   warp 4  TMA: Q once; K_j and V_j^T into a two-stage ring;
+//   warp 5  MMA: S_j = Q K_j^T into one of two tensor-memory score buffers,
+//           then (once the softmax has written P_{j-1}) O = P_{j-1} V_{j-1}
+//           into the output accumulator: S_{j+1} runs while the softmax
+//           works on S_j;
+//   warps 0-3  softmax, one query row per thread: the row max of the scaled,
+//           causally masked S_j; the previous tile's P V folded into the
+//           running output with its rescale (exp(m_{j-2} - m_{j-1})); then
+//           p = exp(s - m_j), the row sum, and p as hi/lo planes in shared
+//           memory (the A operand of the next P V).
+// After the last tile: y = O / l.  Every wait is bounded; a wait that gives up
+// stops the CTA's roles, drains its copies and MMAs, frees the tensor memory
+// and leaves y unwritten.
+//
+// The rows are the reference's causal softmax attention over the window
+// (model.py CausalSelfAttention via F.scaled_dot_product_attention, is_causal,
+// fp32), formed online instead of as a T x T matrix.
+#include "flash.cuh"
+#include "prof.cuh"
+#include "tc.cuh"
+#include "tcgen05.cuh"
+
+namespace altxs {
+namespace {
+
+constexpr int kFM = 128;  // queries per CTA
+constexpr int kFN = 128;  // keys per tile
+constexpr int kFD = 64;   // head dim of the Q/K planes (zero-padded)
+constexpr int kQT = kFM * kFD * 2;          // one Q plane tile: 16 KB
+constexpr int kKT = kFN * kFD * 2;          // one K plane tile: 16 KB
+constexpr int kVAtom = 64 * 128;            // one V^T plane atom (64 keys x up to 64 dims): 8 KB
+constexpr int kVT = 2 * kVAtom;             // one V^T plane tile: 16 KB
+constexpr int kStage = 2 * kKT + 2 * kVT;   // K hi, K lo, V^T hi, V^T lo
+constexpr int kPAtom = kFM * 128;           // one P plane atom (128 rows x 64 keys): 16 KB
+constexpr int kPT = 2 * kPAtom;             // one P plane: 32 KB
+constexpr int kSmem = 2 * kQT + 2 * kStage + 2 * kPT + 1024;
+static_assert(kSmem + 256 <= 227 * 1024, "shared memory");
+constexpr uint32_t kTmemCols = 512;  // S buffers at 0 and 128, O at 256
+constexpr unsigned kAll = 0xffffffffu;
+
+template <int N>
+constexpr uint32_t idesc_kmajor() {  // kind::f16: fp32 accumulate, bf16 A and B, both K-major, M = 128
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kFM >> 4) << 24);
+}
+
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo_elem)) |
+           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi_elem)) << 16);
+}
+
+// Q and K rows as zero-padded planes; V^T through a shared-memory transpose.
+// grid.x: 32-row blocks of T; block 256.
+__global__ void __launch_bounds__(256) k_flash_split(FlashArgs a, int64_t tp, uint16_t *qh, uint16_t *ql,
+                                                     uint16_t *kh, uint16_t *kl, uint16_t *vh, uint16_t *vl) {
+    __shared__ float tile[32][65];
+    const int t0 = blockIdx.x * 32, hd = a.hd;
+    // Q [H][T][64], K [Hkv][T][64]
+    for (int i = threadIdx.x; i < 32 * (a.H + a.Hkv) * kFD; i += blockDim.x) {
+        const int c = i % kFD, r = i / kFD;
+        const int t = t0 + r % 32, h = r / 32;
+        if (t >= a.T) continue;
+        if (h < a.H) {
+            const float x = c < hd ? a.q[(int64_t)t * a.ldq + h * hd + c] : 0.0f;
+            split_store(qh, ql, ((int64_t)h * a.T + t) * kFD + c, x);
+        } else {
+            const int g = h - a.H;
+            const float x = c < hd ? a.k[(int64_t)t * a.ldk + g * hd + c] : 0.0f;
+            split_store(kh, kl, ((int64_t)g * a.T + t) * kFD + c, x);
+        }
+    }
+    // V^T [Hkv][hd][tp]: columns T .. tp are zero (keys past T read as zero)
+    for (int g = 0; g < a.Hkv; ++g) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * hd; i += blockDim.x) {
+            const int r = i / hd, c = i % hd, t = t0 + r;
+            tile[r][c] = t < a.T ? a.v[(int64_t)t * a.ldv + g * hd + c] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * hd; i += blockDim.x) {
+            const int c = i / 32, r = i % 32, t = t0 + r;
+            if (t < tp) split_store(vh, vl, ((int64_t)g * hd + c) * tp + t, tile[r][c]);
+        }
+    }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    k_flash_fwd(const __grid_constant__ CUtensorMap tq_hi, const __grid_constant__ CUtensorMap tq_lo,
+                const __grid_constant__ CUtensorMap tk_hi, const __grid_constant__ CUtensorMap tk_lo,
+                const __grid_constant__ CUtensorMap tv_hi, const __grid_constant__ CUtensorMap tv_lo, FlashArgs a) {
+    extern __shared__ unsigned char fl_smem_raw[];
+    __shared__ __align__(8) uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_full, drainb;
+    __shared__ uint32_t tmem_sh;
+    __shared__ volatile int abort_sh;
+    const uint32_t raw_s = smem_u32(fl_smem_raw);
+    unsigned char *sm = fl_smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
+    const uint32_t sq = smem_u32(sm), sst = sq + 2 * kQT, sp = sst + 2 * kStage;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kFM, h = blockIdx.y, g = h / (a.H / a.Hkv);
+    const int last_q = min(a.T, q0 + kFM) - 1;
+    const int n = last_q / kFN + 1;  // key tiles up to the diagonal
+    if (threadIdx.x == 0) {
+        mbar_init(&q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+        }
+        mbar_init(&p_full, 4);  // one arrival per softmax warp
+        mbar_init(&o_full, 1);
+        mbar_init(&drainb, 1);
+        abort_sh = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_sh)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_sh;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            mbar_expect_tx(&q_full, 2 * kQT);
+            tma_load_3d(sm, &tq_hi, 0, q0, h, &q_full);
+            tma_load_3d(sm + kQT, &tq_lo, 0, q0, h, &q_full);
+            int j = 0;
+            for (; j < n && !abort_sh; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], ((j - 2) >> 1) & 1, wait_limit())) {
+                    abort_sh = 1;
+                    break;
+                }
+                unsigned char *st = sm + 2 * kQT + s * kStage;
+                mbar_expect_tx(&kv_full[s], 2 * kKT + 4 * 128 * HD);
+                tma_load_3d(st, &tk_hi, 0, j * kFN, g, &kv_full[s]);
+                tma_load_3d(st + kKT, &tk_lo, 0, j * kFN, g, &kv_full[s]);
+#pragma unroll
+                for (int at = 0; at < 2; ++at) {
+                    tma_load_3d(st + 2 * kKT + at * kVAtom, &tv_hi, j * kFN + 64 * at, 0, g, &kv_full[s]);
+                    tma_load_3d(st + 2 * kKT + kVT + at * kVAtom, &tv_lo, j * kFN + 64 * at, 0, g, &kv_full[s]);
+                }
+            }
+            if (abort_sh) {  // let the copies in flight land before the CTA can exit
+                mbar_wait_bounded(&q_full, 0, kWaitLimit);
+                for (int p = j - 2 > 0 ? j - 2 : 0; p < j; ++p) mbar_wait_bounded(&kv_full[p & 1], (p >> 1) & 1, kWaitLimit);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            bool ok = mbar_wait_bounded(&q_full, 0, wait_limit());
+            for (int j = 0; j <= n && ok && !abort_sh; ++j) {
+                if (j < n) {  // S_j = Q K_j^T (buffer j & 1, free once P_{j-2} was written)
+                    const int s = j & 1;
+                    if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, wait_limit())) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t kb = sst + s * kStage;
+#pragma unroll
+                    for (int kk = 0; kk < kFD / 16; ++kk) {
+                        const uint64_t qh = sw128_desc(sq + kk * 32, 16), qlo = sw128_desc(sq + kQT + kk * 32, 16);
+                        const uint64_t kh = sw128_desc(kb + kk * 32, 16), klo = sw128_desc(kb + kKT + kk * 32, 16);
+                        const uint32_t d = tmem + s * kFN;
+                        tc_mma(d, qh, kh, idesc_kmajor<kFN>(), kk != 0);
+                        tc_mma(d, qh, klo, idesc_kmajor<kFN>(), 1u);
+                        tc_mma(d, qlo, kh, idesc_kmajor<kFN>(), 1u);
+                    }
+                    tc_commit(&s_full[s]);
+                }
+                if (j >= 1) {  // O = P_{j-1} V_{j-1} (P written, O of j-2 read: both before p_full)
+                    const int jp = j - 1, s = jp & 1;
+                    if (!mbar_wait_bounded(&p_full, jp & 1, wait_limit())) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t vb = sst + s * kStage + 2 * kKT;
+#pragma unroll
+                    for (int kk = 0; kk < kFN / 16; ++kk) {
+                        const int at = kk >> 2, ko = (kk & 3) * 32;
+                        const uint64_t ph = sw128_desc(sp + at * kPAtom + ko, 16);
+                        const uint64_t pl = sw128_desc(sp + kPT + at * kPAtom + ko, 16);
+                        const uint64_t vh = sw128_desc(vb + at * kVAtom + ko, 16);
+                        const uint64_t vl = sw128_desc(vb + kVT + at * kVAtom + ko, 16);
+                        const uint32_t d = tmem + 2 * kFN;
+                        tc_mma(d, ph, vh, idesc_kmajor<HD>(), kk != 0);
+                        tc_mma(d, ph, vl, idesc_kmajor<HD>(), 1u);
+                        tc_mma(d, pl, vh, idesc_kmajor<HD>(), 1u);
+                    }
+                    tc_commit(&o_full);
+                    tc_commit(&kv_empty[s]);
+                }
+            }
+            if (!ok) abort_sh = 1;
+            // every MMA this thread issued has completed before the CTA can exit
+            tc_commit(&drainb);
+            mbar_wait_bounded(&drainb, 0, kWaitLimit);
+        }
+    } else {
+        // softmax: this thread's query row r of the tile (tensor-memory lane 32 warp + lane)
+        const int r = warp * 32 + lane;
+        const int qi = min(q0 + r, a.T - 1);  // rows past T mask like the last row and are not stored
+        const uint32_t lanes = (uint32_t)(warp * 32) << 16;
+        float o[HD];
+#pragma unroll
+        for (int c = 0; c < HD; ++c) o[c] = 0.0f;
+        float m = -INFINITY, l = 0.0f, a_prev = 0.0f;
+        bool ok = true;
+        for (int j = 0; j <= n; ++j) {
+            float m_new = m;
+            const uint32_t sb = tmem + lanes + (j & 1) * kFN;
+            if (j < n) {  // pass 1: the row max of the scaled, masked scores
+                ok = __all_sync(kAll, ok && !abort_sh && mbar_wait_bounded(&s_full[j & 1], (j >> 1) & 1, wait_limit()));
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c0 = 0; c0 < kFN; c0 += 32) {
+                    float v[32];
+                    tc_ld32(sb + c0, v);
+#pragma unroll
+                    for (int u = 0; u < 32; ++u)
+                        if (j * kFN + c0 + u <= qi) m_new = fmaxf(m_new, __fmul_rn(v[u], a.scale));
+                }
+            }
+            if (j >= 1) {  // fold the previous tile's P V: o = o * exp(m_{j-2} - m_{j-1}) + (P V)_{j-1}
+                ok = __all_sync(kAll, ok && !abort_sh && mbar_wait_bounded(&o_full, (j - 1) & 1, wait_limit()));
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < HD; c0 += 32) {
+                    float v[32];
+                    tc_ld32(tmem + lanes + 2 * kFN + c0, v);
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) o[c0 + u] = __fmaf_rn(o[c0 + u], a_prev, v[u]);
+                }
+            }
+            if (j == n) break;
+            // pass 2: p = exp(s - m_j) as hi/lo planes (the A operand of P V), row sum
+            const float alpha = expf(__fsub_rn(m, m_new));  // exp(-inf) = 0 on the first tile
+            float sum = 0.0f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kFN; c0 += 32) {
+                float v[32];
+                tc_ld32(sb + c0, v);
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const bool in = j * kFN + c0 + u <= qi;
+                    v[u] = in ? expf(__fsub_rn(__fmul_rn(v[u], a.scale), m_new)) : 0.0f;
+                    sum = __fadd_rn(sum, v[u]);
+                }
+                // 16-byte chunk k (keys c0 + 8k ..) of row r: atom c0 / 64, chunk (c0 % 64) / 8 + k, swizzled
+                const uint32_t row = sp + (c0 / 64) * kPAtom + r * 128;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float x0 = v[8 * k + 2 * e], x1 = v[8 * k + 2 * e + 1];
+                        const float h0 = __bfloat162float(__float2bfloat16_rn(x0));
+                        const float h1 = __bfloat162float(__float2bfloat16_rn(x1));
+                        hw[e] = pack_bf16(h0, h1);
+                        lw[e] = pack_bf16(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+                    }
+                    const uint32_t off = (uint32_t)(((((c0 % 64) / 8 + k) ^ (r & 7))) << 4);
+                    sts_v4(row + off, hw[0], hw[1], hw[2], hw[3]);
+                    sts_v4(row + kPT + off, lw[0], lw[1], lw[2], lw[3]);
+                }
+            }
+            l = __fmaf_rn(l, alpha, sum);
+            m = m_new;
+            a_prev = alpha;
+            // the tensor cores read P through the async proxy; S_j and O_{j-1} are consumed
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full);
+        }
+        if (!ok) {
+            abort_sh = 1;
+        } else if (q0 + r < a.T) {
+            float *y = a.y + (int64_t)(q0 + r) * a.ldy + (int64_t)h * HD;
+#pragma unroll
+            for (int c = 0; c < HD; c += 4)
+                *reinterpret_cast<float4 *>(y + c) = make_float4(__fdiv_rn(o[c], l), __fdiv_rn(o[c + 1], l),
+                                                                 __fdiv_rn(o[c + 2], l), __fdiv_rn(o[c + 3], l));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// 3-D bf16 tensor map over [nb][rows][cols] (row stride cols), box 64 x box_rows x 1, 128-byte swizzle
+bool map3(CUtensorMap *m, const uint16_t *p, int64_t cols, int64_t rows, int64_t nb, int box_rows) {
+    auto enc = encoder();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)nb};
+    cuuint64_t strides[2] = {(cuuint64_t)(cols * 2), (cuuint64_t)(cols * rows * 2)};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t *>(p), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HD>
+int launch_hd(const FlashArgs &a, const CUtensorMap (&m)[6], cudaStream_t st) {
+    static bool attr_done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ALTXS_ECUDA;
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(k_flash_fwd<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+            return ALTXS_ECUDA;
+        attr_done[dev] = true;
+    }
+    const dim3 grid((a.T + kFM - 1) / kFM, a.H);
+    ALTXS_LAUNCH(kKTtt, st, k_flash_fwd<HD><<<grid, 192, kSmem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a));
+    return ALTXS_OK;
+}
+
+}  // namespace
+
+int set_wait_limit_flash(uint32_t limit) {
+    return cudaMemcpyToSymbol(g_wait_limit, &limit, sizeof(limit)) == cudaSuccess ? ALTXS_OK : ALTXS_ECUDA;
+}
+
+int64_t flash_scratch_elems(int T, int H, int Hkv, int hd) {
+    if (T <= 0 || H <= 0 || Hkv <= 0 || hd <= 0) return 0;
+    const int64_t tp = align_up((int64_t)T, 8);
+    // Q, K and V^T planes (hi and lo), each part 16-byte aligned
+    return 2 * (align_up((int64_t)H * T * kFD, 8) + align_up((int64_t)Hkv * T * kFD, 8) + (int64_t)Hkv * hd * tp);
+}
+
+int launch_flash_fwd(const FlashArgs &a, cudaStream_t st) {
+    if (a.T <= 0) return ALTXS_OK;
+    if (!flash_ok(a.hd) || a.H <= 0 || a.Hkv <= 0 || a.H % a.Hkv || !a.q || !a.k || !a.v || !a.y || !a.scratch ||
+        (reinterpret_cast<uintptr_t>(a.scratch) & 15) || (reinterpret_cast<uintptr_t>(a.y) & 15) || a.ldy % 4)
+        return ALTXS_EINVAL;
+    const int64_t tp = align_up((int64_t)a.T, 8);
+    const int64_t nq = align_up((int64_t)a.H * a.T * kFD, 8), nk = align_up((int64_t)a.Hkv * a.T * kFD, 8);
+    const int64_t nv = (int64_t)a.Hkv * a.hd * tp;
+    uint16_t *qh = a.scratch, *ql = qh + nq, *kh = ql + nq, *kl = kh + nk, *vh = kl + nk, *vl = vh + nv;
+    ALTXS_LAUNCH(kKTtt, st, k_flash_split<<<(a.T + 31) / 32, 256, 0, st>>>(a, tp, qh, ql, kh, kl, vh, vl));
+    CUtensorMap m[6];
+    if (!map3(&m[0], qh, kFD, a.T, a.H, kFM) || !map3(&m[1], ql, kFD, a.T, a.H, kFM) ||
+        !map3(&m[2], kh, kFD, a.T, a.Hkv, kFN) || !map3(&m[3], kl, kFD, a.T, a.Hkv, kFN) ||
+        !map3(&m[4], vh, tp, a.hd, a.Hkv, a.hd) || !map3(&m[5], vl, tp, a.hd, a.Hkv, a.hd))
+        return ALTXS_EINVAL;
+    return a.hd == 32 ? launch_hd<32>(a, m, st) : launch_hd<64>(a, m, st);
+}
+
+}  // namespace altxs
+
+extern "C" {
+
+int64_t altxs_window_attention_workspace_bytes(int T, int H, int Hkv, int hd) {
+    if (T < 0 || H <= 0 || Hkv <= 0 || hd <= 0) return -1;
+    return altxs::flash_scratch_elems(T, H, Hkv, hd) * 2;
+}
+
+int altxs_window_attention(int T, int H, int Hkv, int hd, float scale, const float *q, int64_t ldq, const float *k,
+                           int64_t ldk, const float *v, int64_t ldv, float *y, int64_t ldy, void *workspace,
+                           int64_t workspace_bytes, altxs_stream_t stream) {
+    using namespace altxs;
+    if (T < 0 || H <= 0 || Hkv <= 0 || H % Hkv || ldq < (int64_t)H * hd || ldk < (int64_t)Hkv * hd ||
+        ldv < (int64_t)Hkv * hd || ldy < (int64_t)H * hd)
+        return ALTXS_EINVAL;
+    if (!flash_ok(hd)) return ALTXS_ENOTSUP;
+    if (T == 0) return ALTXS_OK;
+    if (!workspace || workspace_bytes < altxs_window_attention_workspace_bytes(T, H, Hkv, hd)) return ALTXS_EINVAL;
+    FlashArgs a{};
+    a.T = T;
+    a.H = H;
+    a.Hkv = Hkv;
+    a.hd = hd;
+    a.scale = scale;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.ldq = ldq;
+    a.ldk = ldk;
+    a.ldv = ldv;
+    a.y = y;
+    a.ldy = ldy;
+    a.scratch = static_cast<uint16_t *>(workspace);
+    return launch_flash_fwd(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

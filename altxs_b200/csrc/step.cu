@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "coder.cuh"
+#include "flash.cuh"
 #include "model.cuh"
 #include "prof.cuh"
 #include "qmm.cuh"
@@ -1342,10 +1343,13 @@ extern "C" {
 
 int altxs_set_wait_limit(uint32_t limit) {
     if (cudaMemcpyToSymbol(g_wait_limit, &limit, sizeof(limit)) != cudaSuccess) return ALTXS_ECUDA;
+    if (altxs::set_wait_limit_flash(limit) != ALTXS_OK) return ALTXS_ECUDA;
     return altxs::set_wait_limit_tc(limit);
 }
 
 uint32_t altxs_default_wait_limit(void) { return altxs::kWaitLimit; }
+
+int altxs_set_flash(int on) { return altxs::set_flash(on); }
 
 int altxs_set_linear_packed(int on) {
     g_linear_packed = on ? 1 : 0;

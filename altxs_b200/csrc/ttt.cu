@@ -14,6 +14,7 @@
 // decoder compute identical updates.
 #include <math.h>
 
+#include "flash.cuh"
 #include "gemm.cuh"
 #include "model.cuh"
 #include "prof.cuh"
@@ -1642,6 +1643,24 @@ int attn_probs(const Run &R, int l) {
     return ALTXS_OK;
 }
 
+// Window attention of the forward without the T x T probabilities (the flash
+// kernel): the context prefill, and the full-parameter gradient, whose
+// backward recomputes them; the LoRA update keeps them for its backward.
+int g_flash = 1;
+}  // namespace
+
+int altxs::set_flash(int on) {
+    g_flash = on ? 1 : 0;
+    return ALTXS_OK;
+}
+
+namespace {
+bool use_flash(const Run &R, bool head) {
+    const TD &D = R.D;
+    return g_flash && R.sp && (D.full || !head) && flash_ok(D.hd) &&
+           flash_scratch_elems(D.T, D.H, D.Hkv, D.hd) <= R.tca_n;
+}
+
 int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out,
             bool head = true) {
     const TD &D = R.D;
@@ -1687,7 +1706,8 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
                          tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
         }
         ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
-        TRY(attn_probs(R, l));
+        const bool flash = use_flash(R, head);
+        if (!flash) TRY(attn_probs(R, l));
         // the full-parameter gradient keeps every application's attention output and projections
         const bool o_on_y = r > 0 && (mask & 64);
         float *yb = D.full || o_on_y ? tp.yl + (int64_t)l * Tn * d : tp.y;
@@ -1695,7 +1715,24 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
         const bool ym = ymotif(D, i);
         float *ya = ym ? tp.yraw + (int64_t)l * Tn * d : yb;  // P v, before XSA and the gate
         const int64_t ldp = align_up(Tn, 8);
-        if (R.sp) {
+        if (flash) {  // y = softmax(q k^T / sqrt(hd)) v without the scores leaving the SM
+            FlashArgs fa{};
+            fa.T = Tn;
+            fa.H = D.H;
+            fa.Hkv = D.Hkv;
+            fa.hd = D.hd;
+            fa.scale = 1.0f / __builtin_sqrtf((float)D.hd);
+            fa.q = tp.qr + (int64_t)l * Tn * d;
+            fa.ldq = d;
+            fa.k = tp.kr + (int64_t)l * Tn * D.kvd;
+            fa.ldk = D.kvd;
+            fa.v = qkv + d + D.kvd;
+            fa.ldv = D.qn;
+            fa.y = ya;
+            fa.ldy = d;
+            fa.scratch = R.tca;
+            TRY(launch_flash_fwd(fa, st));
+        } else if (R.sp) {
             const uint16_t *Ph = p_planes(R, l), *Pl = Ph + D.H * Tn * ldp;
             TcOp a{Ph, Pl, 0, Tn, Tn, ldp, Tn * ldp, D.H, 0, 1, 1, 0}, b{};
             TRY(split_b(R, qkv + d + D.kvd, Tn, D.hd, D.qn, D.Hkv, D.hd, 1, D.G, 1, 0, b));  // v, [n=c][k=t']

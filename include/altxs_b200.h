@@ -359,6 +359,21 @@ int64_t altxs_linear_tc_workspace_bytes(int M, int N, int K);
 int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int M, float *Y, void *workspace,
                     int64_t workspace_bytes, altxs_stream_t stream);
 
+/* Causal attention over a window on the tensor cores (the flash kernel of the
+ * context prefill and the full-parameter forward; the reference's
+ * F.scaled_dot_product_attention(q, k, v, is_causal=True) inside
+ * CausalSelfAttention.forward, altxs src/xsa_ttt/model.py, and its training
+ * attention train_attn.py:67 _train_attn_fwd):
+ *   y[t][h*hd + c] = sum_{s <= t} softmax_s(scale * q_t,h . k_s,g) v_s,g[c],
+ * g = h / (H / Hkv); q [T][ldq], k [T][ldk], v [T][ldv], y [T][ldy] fp32
+ * (ldy a multiple of 4, y 16-byte aligned).  hd 32 or 64 (else
+ * ALTXS_ENOTSUP).  Products as hi/lo bf16 planes with fp32 accumulation, an
+ * online softmax per 128-key tile; no T x T buffer. */
+int64_t altxs_window_attention_workspace_bytes(int T, int H, int Hkv, int hd);
+int altxs_window_attention(int T, int H, int Hkv, int hd, float scale, const float *q, int64_t ldq, const float *k,
+                           int64_t ldk, const float *v, int64_t ldv, float *y, int64_t ldy, void *workspace,
+                           int64_t workspace_bytes, altxs_stream_t stream);
+
 /* Segment-reset context (the reference's reset_segment, altxs
  * src/xsa_ttt/incremental.py:858-897, with _chunk_ctx_start, compress.py:122-125):
  * after a boundary update the stream's context is rebuilt from its last
@@ -542,6 +557,17 @@ int altxs_set_step_fusion(int max_streams);
  * planes.  Both feed the tensor cores the same values in the same order, so
  * the results are bit-identical; only the speed differs.  Process-wide. */
 int altxs_set_linear_packed(int on);
+
+/* Window attention of the context prefill (altxs_prefill) and of the
+ * full-parameter gradient's forward (altxs_full_loss_grad) on the tensor-core
+ * path: 1 (default) = the flash kernel (scores and probabilities stay in
+ * tensor and shared memory; head_dim 32 or 64), 0 = the materialised T x T
+ * probabilities (every head size).  The two agree to fp32 rounding, not bit
+ * for bit: an encoder and its decoder use the same setting.  Replaces the
+ * reference's causal attention over the window (model.py
+ * CausalSelfAttention.forward, F.scaled_dot_product_attention is_causal).
+ * Process-wide. */
+int altxs_set_flash(int on);
 
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these
