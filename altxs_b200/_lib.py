@@ -27,7 +27,7 @@ EXPORTS = (
     "altxs_dequant", "altxs_split_weights", "altxs_linear_workspace_bytes", "altxs_linear",
     "altxs_linear_tc_workspace_bytes", "altxs_linear_tc", "altxs_set_lockstep", "altxs_lockstep_id",
     "altxs_set_linear_packed",
-    "altxs_set_flash", "altxs_window_attention_workspace_bytes", "altxs_window_attention",
+    "altxs_set_flash", "altxs_window_attention_workspace_bytes", "altxs_window_attention", "altxs_last_cuda_error",
     "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
     "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit", "altxs_set_step_fusion",
     "altxs_param_layout_of", "altxs_full_workspace_bytes", "altxs_full_loss_grad", "altxs_adamw",
@@ -158,6 +158,7 @@ def lib():
             "altxs_set_step_fusion": (C.c_int, [C.c_int]),
             "altxs_set_linear_packed": (C.c_int, [C.c_int]),
             "altxs_set_flash": (C.c_int, [C.c_int]),
+            "altxs_last_cuda_error": (C.c_int, []),
             "altxs_window_attention_workspace_bytes": (i64, [C.c_int, C.c_int, C.c_int, C.c_int]),
             "altxs_window_attention": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp, i64, vp, i64, vp,
                                                  i64, vp, i64, vp, i64, vp]),

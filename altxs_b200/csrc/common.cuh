@@ -10,10 +10,16 @@
 #define ALTXS_LAUNCH_CHECK()                                   \
     do {                                                       \
         cudaError_t e_ = cudaGetLastError();                   \
-        if (e_ != cudaSuccess) return ALTXS_ECUDA;             \
+        if (e_ != cudaSuccess) {                               \
+            ::altxs::note_cuda_error(e_);                      \
+            return ALTXS_ECUDA;                                \
+        }                                                      \
     } while (0)
 
 namespace altxs {
+
+// Records the CUDA error behind an ALTXS_ECUDA return (altxs_last_cuda_error).
+void note_cuda_error(cudaError_t e);
 
 constexpr uint64_t kTop = 1ull << 32;
 constexpr uint64_t kHalf = 1ull << 31;

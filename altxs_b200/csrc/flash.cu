@@ -54,53 +54,75 @@ constexpr uint32_t idesc_kmajor() {  // kind::f16: fp32 accumulate, bf16 A and B
 __device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
-    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo_elem)) |
-           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi_elem)) << 16);
+// hi/lo bf16 planes of 8 consecutive values at element e (16-byte aligned)
+__device__ __forceinline__ void store8_split(uint16_t *hi, uint16_t *lo, int64_t e, const float *x) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(x[2 * k], x[2 * k + 1]);
+        const float2 hf = __bfloat1622float2(h2);
+        const __nv_bfloat162 l2 = __floats2bfloat162_rn(__fsub_rn(x[2 * k], hf.x), __fsub_rn(x[2 * k + 1], hf.y));
+        hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
+        lw[k] = *reinterpret_cast<const uint32_t *>(&l2);
+    }
+    *reinterpret_cast<uint4 *>(hi + e) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(lo + e) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
-// Q and K rows as zero-padded planes; V^T through a shared-memory transpose.
-// grid.x: 32-row blocks of T; block 256.
+// Q and K rows as zero-padded planes, V^T through a shared-memory transpose.
+// grid (32-row blocks of T, H + 2 Hkv): y < H a Q head, then K heads, then V heads.
 __global__ void __launch_bounds__(256) k_flash_split(FlashArgs a, int64_t tp, uint16_t *qh, uint16_t *ql,
                                                      uint16_t *kh, uint16_t *kl, uint16_t *vh, uint16_t *vl) {
     __shared__ float tile[32][65];
-    const int t0 = blockIdx.x * 32, hd = a.hd;
-    // Q [H][T][64], K [Hkv][T][64]
-    for (int i = threadIdx.x; i < 32 * (a.H + a.Hkv) * kFD; i += blockDim.x) {
-        const int c = i % kFD, r = i / kFD;
-        const int t = t0 + r % 32, h = r / 32;
-        if (t >= a.T) continue;
-        if (h < a.H) {
-            const float x = c < hd ? a.q[(int64_t)t * a.ldq + h * hd + c] : 0.0f;
-            split_store(qh, ql, ((int64_t)h * a.T + t) * kFD + c, x);
-        } else {
-            const int g = h - a.H;
-            const float x = c < hd ? a.k[(int64_t)t * a.ldk + g * hd + c] : 0.0f;
-            split_store(kh, kl, ((int64_t)g * a.T + t) * kFD + c, x);
+    const int t0 = blockIdx.x * 32, hd = a.hd, y = blockIdx.y;
+    if (y < a.H + a.Hkv) {  // Q [H][T][64], K [Hkv][T][64]
+        const bool isq = y < a.H;
+        const int hh = isq ? y : y - a.H;
+        const float *src = isq ? a.q : a.k;
+        const int64_t ld = isq ? a.ldq : a.ldk;
+        uint16_t *dh = isq ? qh : kh, *dl = isq ? ql : kl;
+        // one 16-byte store per plane and thread: 8 consecutive columns of one row
+        for (int i = threadIdx.x; i < 32 * (kFD / 8); i += blockDim.x) {
+            const int c8 = (i % (kFD / 8)) * 8, t = t0 + i / (kFD / 8);
+            if (t >= a.T) break;
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = c8 + e < hd ? src[(int64_t)t * ld + hh * hd + c8 + e] : 0.0f;
+            store8_split(dh, dl, ((int64_t)hh * a.T + t) * kFD + c8, x);
         }
+        return;
     }
     // V^T [Hkv][hd][tp]: columns T .. tp are zero (keys past T read as zero)
-    for (int g = 0; g < a.Hkv; ++g) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < 32 * hd; i += blockDim.x) {
-            const int r = i / hd, c = i % hd, t = t0 + r;
-            tile[r][c] = t < a.T ? a.v[(int64_t)t * a.ldv + g * hd + c] : 0.0f;
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < 32 * hd; i += blockDim.x) {
-            const int c = i / 32, r = i % 32, t = t0 + r;
-            if (t < tp) split_store(vh, vl, ((int64_t)g * hd + c) * tp + t, tile[r][c]);
-        }
+    const int g = y - a.H - a.Hkv;
+    for (int i = threadIdx.x; i < 32 * hd; i += blockDim.x) {
+        const int r = i / hd, c = i % hd, t = t0 + r;
+        tile[r][c] = t < a.T ? a.v[(int64_t)t * a.ldv + g * hd + c] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 4 * hd; i += blockDim.x) {  // 8 consecutive keys of one dim per thread
+        const int c = i / 4, r8 = (i % 4) * 8;
+        if (t0 + r8 >= tp) continue;  // tp is a multiple of 8: a group is all below tp or all past it
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = tile[r8 + e][c];
+        store8_split(vh, vl, ((int64_t)g * hd + c) * tp + t0 + r8, x);
     }
 }
 
+__device__ __forceinline__ float ex2(float x) {  // 2^x (the SFU instruction; 2^-inf = 0)
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     k_flash_fwd(const __grid_constant__ CUtensorMap tq_hi, const __grid_constant__ CUtensorMap tq_lo,
                 const __grid_constant__ CUtensorMap tk_hi, const __grid_constant__ CUtensorMap tk_lo,
                 const __grid_constant__ CUtensorMap tv_hi, const __grid_constant__ CUtensorMap tv_lo, FlashArgs a) {
     extern __shared__ unsigned char fl_smem_raw[];
-    __shared__ __align__(8) uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_full, drainb;
+    __shared__ __align__(8) uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], drainb,
+        xbar[4];
     __shared__ uint32_t tmem_sh;
     __shared__ volatile int abort_sh;
     const uint32_t raw_s = smem_u32(fl_smem_raw);
@@ -117,13 +139,16 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&kv_empty[s], 1);
             mbar_init(&s_full[s], 1);
         }
-        mbar_init(&p_full, 4);  // one arrival per softmax warp
-        mbar_init(&o_full, 1);
+        for (int hh = 0; hh < 2; ++hh) {
+            mbar_init(&p_full[hh], 4);  // one arrival per softmax warp of the key half
+            mbar_init(&o_full[hh], 1);
+        }
+        for (int qq = 0; qq < 4; ++qq) mbar_init(&xbar[qq], 1);  // the key-half-1 warp of a lane quarter
         mbar_init(&drainb, 1);
         abort_sh = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_sh)),
                      "r"(kTmemCols)
                      : "memory");
@@ -134,7 +159,7 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_sh;
 
-    if (warp == 4) {
+    if (warp == 8) {
         if (lane == 0) {
             mbar_expect_tx(&q_full, 2 * kQT);
             tma_load_3d(sm, &tq_hi, 0, q0, h, &q_full);
@@ -161,7 +186,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int p = j - 2 > 0 ? j - 2 : 0; p < j; ++p) mbar_wait_bounded(&kv_full[p & 1], (p >> 1) & 1, kWaitLimit);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         if (lane == 0) {
             bool ok = mbar_wait_bounded(&q_full, 0, wait_limit());
             for (int j = 0; j <= n && ok && !abort_sh; ++j) {
@@ -184,27 +209,29 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     tc_commit(&s_full[s]);
                 }
-                if (j >= 1) {  // O = P_{j-1} V_{j-1} (P written, O of j-2 read: both before p_full)
+                if (j >= 1) {  // O_h = P_h V_h of tile j-1 for each key half h (P_h written, O_h of j-2 read)
                     const int jp = j - 1, s = jp & 1;
-                    if (!mbar_wait_bounded(&p_full, jp & 1, wait_limit())) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
                     const uint32_t vb = sst + s * kStage + 2 * kKT;
+                    for (int hh = 0; hh < 2 && ok; ++hh) {
+                        if (!mbar_wait_bounded(&p_full[hh], jp & 1, wait_limit())) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < kFN / 16; ++kk) {
-                        const int at = kk >> 2, ko = (kk & 3) * 32;
-                        const uint64_t ph = sw128_desc(sp + at * kPAtom + ko, 16);
-                        const uint64_t pl = sw128_desc(sp + kPT + at * kPAtom + ko, 16);
-                        const uint64_t vh = sw128_desc(vb + at * kVAtom + ko, 16);
-                        const uint64_t vl = sw128_desc(vb + kVT + at * kVAtom + ko, 16);
-                        const uint32_t d = tmem + 2 * kFN;
-                        tc_mma(d, ph, vh, idesc_kmajor<HD>(), kk != 0);
-                        tc_mma(d, ph, vl, idesc_kmajor<HD>(), 1u);
-                        tc_mma(d, pl, vh, idesc_kmajor<HD>(), 1u);
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t ph = sw128_desc(sp + hh * kPAtom + kk * 32, 16);
+                            const uint64_t pl = sw128_desc(sp + kPT + hh * kPAtom + kk * 32, 16);
+                            const uint64_t vh = sw128_desc(vb + hh * kVAtom + kk * 32, 16);
+                            const uint64_t vl = sw128_desc(vb + kVT + hh * kVAtom + kk * 32, 16);
+                            const uint32_t d = tmem + 2 * kFN + hh * 64;
+                            tc_mma(d, ph, vh, idesc_kmajor<HD>(), kk != 0);
+                            tc_mma(d, ph, vl, idesc_kmajor<HD>(), 1u);
+                            tc_mma(d, pl, vh, idesc_kmajor<HD>(), 1u);
+                        }
+                        tc_commit(&o_full[hh]);
                     }
-                    tc_commit(&o_full);
+                    if (!ok) break;
                     tc_commit(&kv_empty[s]);
                 }
             }
@@ -214,10 +241,18 @@ __global__ void __launch_bounds__(192, 1)
             mbar_wait_bounded(&drainb, 0, kWaitLimit);
         }
     } else {
-        // softmax: this thread's query row r of the tile (tensor-memory lane 32 warp + lane)
-        const int r = warp * 32 + lane;
+        // softmax, warps 0-7: warp w reads tensor-memory lanes 32 (w % 4) ..
+        // (query rows) and key half h = w / 4 of every score tile, with its own
+        // running max m_h, sum l_h and output o_h = sum over its keys of p v
+        // (the tensor cores form P_h V_h per half).  At the end the half-1 warp
+        // of each lane quarter hands (m_1, l_1, o_1) to the half-0 warp through a
+        // free shared-memory stage, which combines and stores y.  Scores in
+        // log2 units: x = s * scale * log2(e), p = 2^(x - m).
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = quarter * 32 + lane;
         const int qi = min(q0 + r, a.T - 1);  // rows past T mask like the last row and are not stored
-        const uint32_t lanes = (uint32_t)(warp * 32) << 16;
+        const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+        const float c2 = __fmul_rn(a.scale, 1.4426950408889634f);  // log2(e)
         float o[HD];
 #pragma unroll
         for (int c = 0; c < HD; ++c) o[c] = 0.0f;
@@ -225,60 +260,64 @@ __global__ void __launch_bounds__(192, 1)
         bool ok = true;
         for (int j = 0; j <= n; ++j) {
             float m_new = m;
-            const uint32_t sb = tmem + lanes + (j & 1) * kFN;
-            if (j < n) {  // pass 1: the row max of the scaled, masked scores
+            const uint32_t sb = tmem + lanes + (j & 1) * kFN + half * 64;
+            const int kb = j * kFN + half * 64;  // first key of this warp's half
+            const bool whole = kb + 63 <= q0;    // every row of the tile sees all 64 keys
+            if (j < n) {  // pass 1: the max of this half's scaled, masked scores (log2 units)
                 ok = __all_sync(kAll, ok && !abort_sh && mbar_wait_bounded(&s_full[j & 1], (j >> 1) & 1, wait_limit()));
                 if (!ok) break;
                 tc_fence_after();
-#pragma unroll 1
-                for (int c0 = 0; c0 < kFN; c0 += 32) {
+#pragma unroll
+                for (int c0 = 0; c0 < 64; c0 += 32) {
                     float v[32];
                     tc_ld32(sb + c0, v);
 #pragma unroll
                     for (int u = 0; u < 32; ++u)
-                        if (j * kFN + c0 + u <= qi) m_new = fmaxf(m_new, __fmul_rn(v[u], a.scale));
+                        m_new = fmaxf(m_new, whole || kb + c0 + u <= qi ? __fmul_rn(v[u], c2) : -INFINITY);
                 }
             }
-            if (j >= 1) {  // fold the previous tile's P V: o = o * exp(m_{j-2} - m_{j-1}) + (P V)_{j-1}
-                ok = __all_sync(kAll, ok && !abort_sh && mbar_wait_bounded(&o_full, (j - 1) & 1, wait_limit()));
+            if (j >= 1) {  // fold the previous tile: o = o * 2^(m_{j-2} - m_{j-1}) + (P_h V_h)_{j-1}
+                ok = __all_sync(kAll, ok && !abort_sh && mbar_wait_bounded(&o_full[half], (j - 1) & 1, wait_limit()));
                 if (!ok) break;
                 tc_fence_after();
+                const uint32_t ob = tmem + lanes + 2 * kFN + half * 64;
 #pragma unroll
                 for (int c0 = 0; c0 < HD; c0 += 32) {
                     float v[32];
-                    tc_ld32(tmem + lanes + 2 * kFN + c0, v);
+                    tc_ld32(ob + c0, v);
 #pragma unroll
                     for (int u = 0; u < 32; ++u) o[c0 + u] = __fmaf_rn(o[c0 + u], a_prev, v[u]);
                 }
             }
             if (j == n) break;
-            // pass 2: p = exp(s - m_j) as hi/lo planes (the A operand of P V), row sum
-            const float alpha = expf(__fsub_rn(m, m_new));  // exp(-inf) = 0 on the first tile
+            // pass 2: p = 2^(x - m_j) as hi/lo planes (atom `half` of P), this half's sum;
+            // a half that has seen no key yet keeps m = -inf, p = 0 and alpha = 0
+            const bool seen = m_new != -INFINITY;
+            const float alpha = seen ? ex2(__fsub_rn(m, m_new)) : 0.0f;
             float sum = 0.0f;
-#pragma unroll 1
-            for (int c0 = 0; c0 < kFN; c0 += 32) {
+            const uint32_t row = sp + half * kPAtom + r * 128;
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 32) {
                 float v[32];
-                tc_ld32(sb + c0, v);
+                tc_ld32(sb + c0, v);  // the scores again (tensor-memory reads are cheaper than 64 more registers)
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
-                    const bool in = j * kFN + c0 + u <= qi;
-                    v[u] = in ? expf(__fsub_rn(__fmul_rn(v[u], a.scale), m_new)) : 0.0f;
+                    v[u] = seen && (whole || kb + c0 + u <= qi) ? ex2(__fsub_rn(__fmul_rn(v[u], c2), m_new)) : 0.0f;
                     sum = __fadd_rn(sum, v[u]);
                 }
-                // 16-byte chunk k (keys c0 + 8k ..) of row r: atom c0 / 64, chunk (c0 % 64) / 8 + k, swizzled
-                const uint32_t row = sp + (c0 / 64) * kPAtom + r * 128;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < 4; ++k) {  // 16-byte chunk c0 / 8 + k of the row, swizzled
                     uint32_t hw[4], lw[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const float x0 = v[8 * k + 2 * e], x1 = v[8 * k + 2 * e + 1];
-                        const float h0 = __bfloat162float(__float2bfloat16_rn(x0));
-                        const float h1 = __bfloat162float(__float2bfloat16_rn(x1));
-                        hw[e] = pack_bf16(h0, h1);
-                        lw[e] = pack_bf16(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+                        const __nv_bfloat162 hi2 = __floats2bfloat162_rn(x0, x1);
+                        const float2 hf = __bfloat1622float2(hi2);
+                        const __nv_bfloat162 lo2 = __floats2bfloat162_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
+                        hw[e] = *reinterpret_cast<const uint32_t *>(&hi2);
+                        lw[e] = *reinterpret_cast<const uint32_t *>(&lo2);
                     }
-                    const uint32_t off = (uint32_t)(((((c0 % 64) / 8 + k) ^ (r & 7))) << 4);
+                    const uint32_t off = (uint32_t)((((c0 / 8 + k) ^ (r & 7))) << 4);
                     sts_v4(row + off, hw[0], hw[1], hw[2], hw[3]);
                     sts_v4(row + kPT + off, lw[0], lw[1], lw[2], lw[3]);
                 }
@@ -286,25 +325,48 @@ __global__ void __launch_bounds__(192, 1)
             l = __fmaf_rn(l, alpha, sum);
             m = m_new;
             a_prev = alpha;
-            // the tensor cores read P through the async proxy; S_j and O_{j-1} are consumed
+            // the tensor cores read P through the async proxy; S_j and O_h of j-1 are consumed
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full);
+            if (lane == 0) mbar_arrive(&p_full[half]);
         }
-        if (!ok) {
-            abort_sh = 1;
-        } else if (q0 + r < a.T) {
-            float *y = a.y + (int64_t)(q0 + r) * a.ldy + (int64_t)h * HD;
+        // combine the halves: y = (o_0 2^(m_0 - M) + o_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M)).
+        // Hand-off region: the stage of tile n-2 (or the unused stage when n == 1), free once this
+        // warp saw its last P V complete (the tensor cores finish MMAs in issue order, tile by tile).
+        float *xf = reinterpret_cast<float *>(sm + 2 * kQT + (n & 1) * kStage) + quarter * 32 * (HD + 2);
+        if (ok && half == 1) {
+            xf[lane] = m;
+            xf[32 + lane] = l;
 #pragma unroll
-            for (int c = 0; c < HD; c += 4)
-                *reinterpret_cast<float4 *>(y + c) = make_float4(__fdiv_rn(o[c], l), __fdiv_rn(o[c + 1], l),
-                                                                 __fdiv_rn(o[c + 2], l), __fdiv_rn(o[c + 3], l));
+            for (int c = 0; c < HD; ++c) xf[(c + 2) * 32 + lane] = o[c];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[quarter]);
         }
+        if (ok && half == 0) {
+            ok = __all_sync(kAll, mbar_wait_bounded(&xbar[quarter], 0, wait_limit()));
+            if (ok && q0 + r < a.T) {
+                const float m1 = xf[lane], l1 = xf[32 + lane];
+                const float mx = fmaxf(m, m1);  // m (half 0) is finite: key 0 of tile 0 is seen by every row
+                const float f0 = ex2(__fsub_rn(m, mx)), f1 = m1 == -INFINITY ? 0.0f : ex2(__fsub_rn(m1, mx));
+                const float lt = __fadd_rn(__fmul_rn(l, f0), __fmul_rn(l1, f1));
+                float *y = a.y + (int64_t)(q0 + r) * a.ldy + (int64_t)h * HD;
+#pragma unroll
+                for (int c = 0; c < HD; c += 4) {
+                    float w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        w[e] = __fdiv_rn(__fadd_rn(__fmul_rn(o[c + e], f0), __fmul_rn(xf[(c + e + 2) * 32 + lane], f1)),
+                                         lt);
+                    *reinterpret_cast<float4 *>(y + c) = make_float4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+        if (!ok) abort_sh = 1;
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
@@ -334,7 +396,7 @@ int launch_hd(const FlashArgs &a, const CUtensorMap (&m)[6], cudaStream_t st) {
         attr_done[dev] = true;
     }
     const dim3 grid((a.T + kFM - 1) / kFM, a.H);
-    ALTXS_LAUNCH(kKTtt, st, k_flash_fwd<HD><<<grid, 192, kSmem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a));
+    ALTXS_LAUNCH(kKTtt, st, k_flash_fwd<HD><<<grid, 320, kSmem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a));
     return ALTXS_OK;
 }
 
@@ -360,7 +422,8 @@ int launch_flash_fwd(const FlashArgs &a, cudaStream_t st) {
     const int64_t nq = align_up((int64_t)a.H * a.T * kFD, 8), nk = align_up((int64_t)a.Hkv * a.T * kFD, 8);
     const int64_t nv = (int64_t)a.Hkv * a.hd * tp;
     uint16_t *qh = a.scratch, *ql = qh + nq, *kh = ql + nq, *kl = kh + nk, *vh = kl + nk, *vl = vh + nv;
-    ALTXS_LAUNCH(kKTtt, st, k_flash_split<<<(a.T + 31) / 32, 256, 0, st>>>(a, tp, qh, ql, kh, kl, vh, vl));
+    ALTXS_LAUNCH(kKTtt, st,
+                 k_flash_split<<<dim3((a.T + 31) / 32, a.H + 2 * a.Hkv), 256, 0, st>>>(a, tp, qh, ql, kh, kl, vh, vl));
     CUtensorMap m[6];
     if (!map3(&m[0], qh, kFD, a.T, a.H, kFM) || !map3(&m[1], ql, kFD, a.T, a.H, kFM) ||
         !map3(&m[2], kh, kFD, a.T, a.Hkv, kFN) || !map3(&m[3], kl, kFD, a.T, a.Hkv, kFN) ||

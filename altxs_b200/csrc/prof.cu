@@ -50,7 +50,16 @@ void prof_end(cudaStream_t s) {
 
 using namespace altxs;
 
+namespace altxs {
+namespace {
+thread_local int g_last_cuda_error = 0;
+}
+void note_cuda_error(cudaError_t e) { g_last_cuda_error = (int)e; }
+}  // namespace altxs
+
 extern "C" {
+
+int altxs_last_cuda_error(void) { return altxs::g_last_cuda_error; }
 
 int64_t altxs_launch_count(void) { return g_launches.load(); }
 

@@ -32,6 +32,7 @@ megakernel and GPU coder, from the offline install in baseline/_ref) on one GPU.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -84,6 +85,9 @@ def parse_args():
                     help="instead of the decode benchmark: one test-time LoRA boundary update (33M model, full "
                          "window), for 1 and for --update-rows streams, one JSON line each")
     ap.add_argument("--update-rows", type=int, default=8)
+    ap.add_argument("--attention", action="store_true",
+                    help="instead of the decode benchmark: the window attention kernel at the 33M window shape "
+                         "and the reset-mode context prefill with it and with the materialised attention")
     ap.add_argument("--c2", action="store_true",
                     help="instead of the decode benchmark: the linear-layer microbenchmark (the C3 layer "
                          "shapes K x N at M = 1, 16, 128, 512 rows, tensor-core and CUDA-core paths), one "
@@ -502,6 +506,83 @@ def run_replenish(args) -> None:
     }), flush=True)
 
 
+def run_attention(args) -> None:
+    """Window attention (``altxs_window_attention``: the flash kernel of the
+    prefill and the full-parameter forward) at the 33M window (T 2047, 8 heads
+    of 64), CUDA events around 20 calls each after a warm-up, median; tensor
+    roofline on the executed products (3 hi/lo bf16 MMAs per fp32 product:
+    6 T^2 hd H flops for the causal half) over the measured bf16 peak.  Then
+    one reset-mode context prefill of the 33M model (2047 rows, 8 layers) on
+    the flash kernel and on the materialised T x T attention."""
+    import ctypes
+
+    from altxs_b200 import _lib
+    from altxs_b200 import codec as C
+    from altxs_b200.config import c3_config
+    from altxs_b200.engine import ContextReset, DeviceModel, StreamBatch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    peaks, kind = load_peaks()
+    st = torch.cuda.current_stream().cuda_stream
+    for T, H, Hkv, hd in ((2047, 8, 8, 64), (2047, 4, 4, 32)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(1)
+        q = torch.randn(T, H * hd, generator=g, device=dev)
+        k = torch.randn(T, Hkv * hd, generator=g, device=dev)
+        v = torch.randn(T, Hkv * hd, generator=g, device=dev)
+        y = torch.empty(T, H * hd, device=dev)
+        wsb = int(L.altxs_window_attention_workspace_bytes(T, H, Hkv, hd))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+
+        def call():
+            _lib.check(L.altxs_window_attention(T, H, Hkv, hd, ctypes.c_float(1.0 / hd ** 0.5), q.data_ptr(),
+                                                q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                                                y.data_ptr(), y.stride(0), ws.data_ptr(), wsb, st),
+                       "altxs_window_attention")
+
+        for _ in range(3):
+            call()
+        times = []
+        for _ in range(20):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        us = statistics.median(times) * 1e3
+        flops = 6.0 * T * T * hd * H
+        tf = flops / (us / 1e6) / 1e12
+        print(json.dumps({"attention": True, "T": T, "H": H, "Hkv": Hkv, "hd": hd, "us": us,
+                          "executed_tflops": tf, "frac": tf / peaks["bf16_tflops"],
+                          "peak_source": f"{kind} bf16_tflops", "note": "split pass + flash kernel"}), flush=True)
+    cfg = dataclasses.replace(c3_config(), context_mode="reset")
+    dm = DeviceModel(C.synth_weights(cfg, seed=WEIGHT_SEED), dev, tensor_cores=True)
+    b = StreamBatch(dm, 1, words_per_stream=8, hist_len=cfg.ctx + 2)
+    b.hist[0, : cfg.ctx] = torch.randint(0, cfg.vocab_size, (cfg.ctx,), device=dev, dtype=torch.int32)
+    reset = ContextReset(dm)
+    out = {}
+    try:
+        for on in (1, 0):
+            L.altxs_set_flash(on)
+            reset(b, [0], cfg.ctx)
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(5):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                reset(b, [0], cfg.ctx)
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            out["flash" if on else "materialised"] = statistics.median(times)
+    finally:
+        L.altxs_set_flash(1)
+    print(json.dumps({"prefill": True, "rows": cfg.ctx - 1, "layers": cfg.num_layers, "ms": out}), flush=True)
+
+
 def run_lora_update(args) -> None:
     """One test-time LoRA boundary update of the benchmark's model (33M, rank-8
     q/k/v/o + lm_head adapters) on the full 2047-token window, for 1 and for
@@ -618,6 +699,10 @@ def main():
     if args.lora_update:
         if rank == 0:
             run_lora_update(args)
+        return
+    if args.attention:
+        if rank == 0:
+            run_attention(args)
         return
     if args.impl == "reference":
         run_reference(args, rank, world)

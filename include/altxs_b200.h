@@ -569,6 +569,10 @@ int altxs_set_linear_packed(int on);
  * Process-wide. */
 int altxs_set_flash(int on);
 
+/* The cudaError_t code behind the calling thread's last ALTXS_ECUDA from a
+ * failed kernel launch (0 when none): a diagnostic only. */
+int altxs_last_cuda_error(void);
+
 /* ---- accounting -----------------------------------------------------------
  * No counterpart in the reference (which has no tracing); these
  * give the benchmark per-kernel device time measured live on the launch

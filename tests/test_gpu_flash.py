@@ -63,7 +63,7 @@ def test_matches_float64(T, H, Hkv, hd):
     q, k, v = qkv[:, :d], qkv[:, d:d + kvd], qkv[:, d + kvd:]
     scale = 1.0 / math.sqrt(hd)
     rc, y = _run(T, H, Hkv, hd, scale, q, k, v)
-    assert rc == 0
+    assert rc == 0, (rc, _lib.lib().altxs_last_cuda_error())
     err = float((y.double() - _ref(q, k, v, H, Hkv, hd, scale)).abs().max())
     print(f"T={T} H={H} Hkv={Hkv} hd={hd}: max abs error {err:.2e}")
     assert err < TOL
