@@ -269,7 +269,7 @@ typedef struct altxs_batch {
  * is a fixed 16 MiB array inside the library's device image (held on every
  * GPU that loads the library until exit; altxs_step_noalloc_max_bytes()).
  * Batches whose scratch would exceed it return ALTXS_ENOSPC (at the 33M
- * shapes, 133 streams fit).  The first call on a device resolves the
+ * shapes, 125 streams fit).  The first call on a device resolves the
  * array's device address with that device current; make that first call
  * before any stream capture.  The address is kept for the life of the
  * process, so do not call this entry point again on a device after
