@@ -28,6 +28,7 @@ EXPORTS = (
     "altxs_linear_tc_workspace_bytes", "altxs_linear_tc", "altxs_set_lockstep", "altxs_lockstep_id",
     "altxs_set_linear_packed",
     "altxs_set_flash", "altxs_window_attention_workspace_bytes", "altxs_window_attention", "altxs_last_cuda_error",
+    "altxs_window_attention_backward_workspace_bytes", "altxs_window_attention_backward",
     "altxs_gemm_workspace_bytes", "altxs_gemm", "altxs_profile_mask", "altxs_prefill",
     "altxs_prefill_workspace_bytes", "altxs_set_wait_limit", "altxs_default_wait_limit", "altxs_set_step_fusion",
     "altxs_param_layout_of", "altxs_full_workspace_bytes", "altxs_full_loss_grad", "altxs_adamw",
@@ -161,7 +162,11 @@ def lib():
             "altxs_last_cuda_error": (C.c_int, []),
             "altxs_window_attention_workspace_bytes": (i64, [C.c_int, C.c_int, C.c_int, C.c_int]),
             "altxs_window_attention": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp, i64, vp, i64, vp,
-                                                 i64, vp, i64, vp, i64, vp]),
+                                                 i64, vp, i64, vp, vp, i64, vp]),
+            "altxs_window_attention_backward_workspace_bytes": (i64, [C.c_int, C.c_int, C.c_int, C.c_int]),
+            "altxs_window_attention_backward": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp, i64, vp,
+                                                          i64, vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp,
+                                                          i64, vp, i64, vp]),
             "altxs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64)]),
             "altxs_step_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(Weights), C.POINTER(Batch), C.c_int,
                                              vp]),

@@ -62,6 +62,8 @@ struct Tape {
     // before XSA and the gate [A][T][d]; the second lane and its gradient, the
     // gradient of the attention read of a parallel block [T][d]; XSA's d(v) [T][kvd]
     float *esm, *yraw, *lane1, *dl1, *dread, *dvx;
+    // flash attention: each application's rows' log-sum-exp [A][H][T] (the backward's input)
+    float *lse;
 };
 
 constexpr int kColChunks = 64;  // row chunks of a column sum (summed in order)
@@ -190,6 +192,7 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.dt = take(T * 3 * (D.r > 0 ? D.r : 1));  // up to three adapters sharing an input
     t.grad = nullptr;  // set by caller (lora_floats)
     t.red = take(1024);
+    t.lse = take(L * D.H * T);
     const bool o_on_y = D.r > 0 && (D.omask & 64);
     if (o_on_y && !D.full) t.yl = take(L * T * d);  // the o adapter's input, per layer
     if (D.par && !D.full) {  // the lanes' combine and its backward read each application's outputs
@@ -1731,6 +1734,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             fa.y = ya;
             fa.ldy = d;
             fa.scratch = R.tca;
+            fa.lse = head && D.full ? tp.lse + (int64_t)l * D.H * Tn : nullptr;  // for the flash backward
             TRY(launch_flash_fwd(fa, st));
         } else if (R.sp) {
             const uint16_t *Ph = p_planes(R, l), *Pl = Ph + D.H * Tn * ldp;
@@ -1910,7 +1914,37 @@ int backward(const Run &R, const float *lora, float *grad) {
             if (full && D.sgate) TRY(colsum(tp.colbuf, (int64_t)D.H * D.gw, nullptr, 0, D.H * D.gw,
                                     FG + lay.attn_gate_w + (int64_t)i * D.H * D.gw));
         }
-        // attention backward
+        // attention backward: the flash kernels from the forward's output and
+        // log-sum-exp, or the probabilities recomputed (full-parameter gradient)
+        // or kept (update) and the products over them
+        const bool fbwd = full && use_flash(R, true) && flash_bwd_scratch_elems(Tn, D.H, D.Hkv) <= R.tca_n;
+        if (fbwd) {
+            FlashBwdArgs fb{};
+            fb.T = Tn;
+            fb.H = D.H;
+            fb.Hkv = D.Hkv;
+            fb.hd = D.hd;
+            fb.scale = att_scale;
+            fb.q = tp.qr + (int64_t)l * Td;
+            fb.ldq = d;
+            fb.k = tp.kr + (int64_t)l * Tn * D.kvd;
+            fb.ldk = D.kvd;
+            fb.v = tp.qkv + (int64_t)l * Tn * D.qn + d + D.kvd;
+            fb.ldv = D.qn;
+            fb.out = ym ? tp.yraw + (int64_t)l * Tn * d : tp.yl + (int64_t)l * Tn * d;  // the forward's P v
+            fb.ldo = d;
+            fb.lse = tp.lse + (int64_t)l * D.H * Tn;
+            fb.dout = tp.dy;
+            fb.lddo = d;
+            fb.dq = tp.dqr;
+            fb.lddq = d;
+            fb.dk = tp.dkr;
+            fb.lddk = D.kvd;
+            fb.dv = tp.dqkv + d + D.kvd;
+            fb.lddv = D.qn;
+            fb.scratch = R.tca;
+            TRY(launch_flash_bwd(fb, st));
+        } else {
         if (full) TRY(attn_probs(R, l));
         const float *P = p_f32(R, l);
         const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
@@ -1990,6 +2024,7 @@ int backward(const Run &R, const float *lora, float *grad) {
                 g.causal = 3;
                 TRY(gemm(R, g));
             }
+        }
         }
         if (ym && i >= D.xsa_from)
             ALTXS_LAUNCH(kKTtt, st, t_add_v<<<g1((int64_t)Tn * D.kvd, 256), 256, 0, st>>>(

@@ -539,7 +539,7 @@ def run_attention(args) -> None:
         def call():
             _lib.check(L.altxs_window_attention(T, H, Hkv, hd, ctypes.c_float(1.0 / hd ** 0.5), q.data_ptr(),
                                                 q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
-                                                y.data_ptr(), y.stride(0), ws.data_ptr(), wsb, st),
+                                                y.data_ptr(), y.stride(0), None, ws.data_ptr(), wsb, st),
                        "altxs_window_attention")
 
         for _ in range(3):

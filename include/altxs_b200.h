@@ -370,9 +370,25 @@ int altxs_linear_tc(const altxs_qtiles *w, int row0, int N, const float *X, int 
  * ALTXS_ENOTSUP).  Products as hi/lo bf16 planes with fp32 accumulation, an
  * online softmax per 128-key tile; no T x T buffer. */
 int64_t altxs_window_attention_workspace_bytes(int T, int H, int Hkv, int hd);
+/* lse: optional [H][T] output (NULL to skip), each row's log2 of its softmax
+ * sum of 2^(scale * log2(e) * q . k), the input of the backward. */
 int altxs_window_attention(int T, int H, int Hkv, int hd, float scale, const float *q, int64_t ldq, const float *k,
-                           int64_t ldk, const float *v, int64_t ldv, float *y, int64_t ldy, void *workspace,
-                           int64_t workspace_bytes, altxs_stream_t stream);
+                           int64_t ldk, const float *v, int64_t ldv, float *y, int64_t ldy, float *lse,
+                           void *workspace, int64_t workspace_bytes, altxs_stream_t stream);
+
+/* Gradient of altxs_window_attention (the backward of the reference's
+ * training attention, train_attn.py:578 triton_causal_sdpa / autograd of
+ * F.scaled_dot_product_attention): dq, dk, dv from dy (= d y), y and lse of
+ * the forward, in the same layouts (dk and dv sum over the query heads of
+ * each group).  dq, dk, dv 16-byte aligned with row strides a multiple of 4.
+ * Flash-style on the tensor cores (no T x T buffer); every sum in a fixed
+ * order, so equal inputs give equal bits. */
+int64_t altxs_window_attention_backward_workspace_bytes(int T, int H, int Hkv, int hd);
+int altxs_window_attention_backward(int T, int H, int Hkv, int hd, float scale, const float *q, int64_t ldq,
+                                    const float *k, int64_t ldk, const float *v, int64_t ldv, const float *y,
+                                    int64_t ldy, const float *lse, const float *dy, int64_t lddy, float *dq,
+                                    int64_t lddq, float *dk, int64_t lddk, float *dv, int64_t lddv, void *workspace,
+                                    int64_t workspace_bytes, altxs_stream_t stream);
 
 /* Segment-reset context (the reference's reset_segment, altxs
  * src/xsa_ttt/incremental.py:858-897, with _chunk_ctx_start, compress.py:122-125):

@@ -38,17 +38,48 @@ def _ref(q, k, v, H, Hkv, hd, scale):
     return out
 
 
-def _run(T, H, Hkv, hd, scale, q, k, v, ldy=None):
+def _run(T, H, Hkv, hd, scale, q, k, v, ldy=None, lse=None):
     L = _lib.lib()
     ldy = ldy or H * hd
     y = torch.full((max(T, 1), ldy), float("nan"), device=DEV)
     wsb = int(L.altxs_window_attention_workspace_bytes(T, H, Hkv, hd))
     ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=DEV)
     rc = L.altxs_window_attention(T, H, Hkv, hd, ctypes.c_float(scale), q.data_ptr(), q.stride(0), k.data_ptr(),
-                                  k.stride(0), v.data_ptr(), v.stride(0), y.data_ptr(), ldy, ws.data_ptr(), wsb,
+                                  k.stride(0), v.data_ptr(), v.stride(0), y.data_ptr(), ldy,
+                                  None if lse is None else lse.data_ptr(), ws.data_ptr(), wsb,
                                   torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     return rc, y
+
+
+def _ref_grads(q, k, v, dy, H, Hkv, hd, scale):
+    """float64 autograd of the causal attention: (dq, dk, dv)."""
+    T, G = q.shape[0], H // Hkv
+    qd, kd, vd = (x.detach().double().requires_grad_() for x in (q, k, v))
+    mask = torch.ones(T, T, dtype=torch.bool, device=q.device).tril()
+    outs = []
+    for h in range(H):
+        g = h // G
+        s = (qd[:, h * hd:(h + 1) * hd] @ kd[:, g * hd:(g + 1) * hd].T) * scale
+        outs.append(torch.softmax(s.masked_fill(~mask, float("-inf")), dim=1) @ vd[:, g * hd:(g + 1) * hd])
+    torch.cat(outs, dim=1).backward(dy.double())
+    return qd.grad, kd.grad, vd.grad
+
+
+def _run_bwd(T, H, Hkv, hd, scale, q, k, v, y, lse, dy):
+    L = _lib.lib()
+    dq = torch.full((T, H * hd), float("nan"), device=DEV)
+    dk = torch.full((T, Hkv * hd), float("nan"), device=DEV)
+    dv = torch.full((T, Hkv * hd), float("nan"), device=DEV)
+    wsb = int(L.altxs_window_attention_backward_workspace_bytes(T, H, Hkv, hd))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=DEV)
+    rc = L.altxs_window_attention_backward(
+        T, H, Hkv, hd, ctypes.c_float(scale), q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
+        v.stride(0), y.data_ptr(), y.stride(0), lse.data_ptr(), dy.data_ptr(), dy.stride(0), dq.data_ptr(), dq.stride(0),
+        dk.data_ptr(), dk.stride(0), dv.data_ptr(), dv.stride(0), ws.data_ptr(), wsb,
+        torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return rc, dq, dk, dv
 
 
 @pytest.mark.parametrize("T,H,Hkv,hd", [(1, 4, 4, 32), (5, 4, 2, 32), (127, 4, 4, 64), (128, 8, 8, 64),
@@ -84,6 +115,35 @@ def test_peaked_rows_and_padded_output():
     err = float((y[:, :H * hd].double() - ref).abs().max())
     assert err < 4 * TOL, err
     assert bool(torch.isnan(y[:, H * hd:]).all())  # the padding columns are not written
+
+
+@pytest.mark.parametrize("T,H,Hkv,hd", [(1, 4, 4, 32), (70, 4, 2, 32), (129, 8, 4, 64), (300, 4, 1, 32),
+                                         (1000, 8, 2, 64), (2047, 8, 8, 64)])
+def test_backward_matches_float64(T, H, Hkv, hd):
+    """dq, dk, dv (GQA sums over a group's heads) against float64 autograd, from
+    the forward's own output and log-sum-exp; two calls give the same bits."""
+    g = torch.Generator(device=DEV)
+    g.manual_seed(T * 17 + hd)
+    d, kvd = H * hd, Hkv * hd
+    qkv = torch.randn(T, d + 2 * kvd, generator=g, device=DEV)
+    q, k, v = qkv[:, :d], qkv[:, d:d + kvd], qkv[:, d + kvd:]
+    dy = torch.randn(T, d, generator=g, device=DEV)
+    scale = 1.0 / math.sqrt(hd)
+    lse = torch.empty(H, T, device=DEV)
+    rc, y = _run(T, H, Hkv, hd, scale, q, k, v, lse=lse)
+    assert rc == 0
+    rc, dq, dk, dv = _run_bwd(T, H, Hkv, hd, scale, q, k, v, y, lse, dy)
+    assert rc == 0, (rc, _lib.lib().altxs_last_cuda_error())
+    ref = _ref_grads(q, k, v, dy, H, Hkv, hd, scale)
+    for name, got, want in zip(("dq", "dk", "dv"), (dq, dk, dv), ref):
+        # relative to the largest entry (at least 1: with one key dq and dk are 0 up to rounding)
+        err = float((got.double() - want).abs().max()) / max(float(want.abs().max()), 1.0)
+        print(f"T={T} H={H} Hkv={Hkv} hd={hd} {name}: max error / max(|ref|, 1) = {err:.2e}")
+        assert err < 2e-4, name
+    rc, dq2, dk2, dv2 = _run_bwd(T, H, Hkv, hd, scale, q, k, v, y, lse, dy)
+    assert rc == 0
+    for a, b in ((dq, dq2), (dk, dk2), (dv, dv2)):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
 
 
 def test_refuses_unsupported_shapes():
