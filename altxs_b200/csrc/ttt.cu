@@ -193,8 +193,9 @@ int64_t carve(const TD &D, void *base, Tape *tp) {
     t.grad = nullptr;  // set by caller (lora_floats)
     t.red = take(1024);
     t.lse = take(L * D.H * T);
-    const bool o_on_y = D.r > 0 && (D.omask & 64);
-    if (o_on_y && !D.full) t.yl = take(L * T * d);  // the o adapter's input, per layer
+    // the attention output per layer (the o adapter's input on y, and the flash
+    // backward's; the full-parameter gradient takes it below)
+    if (!D.full) t.yl = take(L * T * d);
     if (D.par && !D.full) {  // the lanes' combine and its backward read each application's outputs
         t.aol = take(L * T * d);
         t.doutl = take(L * T * d);
@@ -1646,9 +1647,10 @@ int attn_probs(const Run &R, int l) {
     return ALTXS_OK;
 }
 
-// Window attention of the forward without the T x T probabilities (the flash
-// kernel): the context prefill, and the full-parameter gradient, whose
-// backward recomputes them; the LoRA update keeps them for its backward.
+// Window attention without the T x T probabilities (the flash kernels): the
+// context prefill, and the forward and backward of the update and of the
+// full-parameter gradient (the backward reads the forward's output and
+// log-sum-exp instead of the probabilities).
 int g_flash = 1;
 }  // namespace
 
@@ -1658,10 +1660,9 @@ int altxs::set_flash(int on) {
 }
 
 namespace {
-bool use_flash(const Run &R, bool head) {
+bool use_flash(const Run &R) {
     const TD &D = R.D;
-    return g_flash && R.sp && (D.full || !head) && flash_ok(D.hd) &&
-           flash_scratch_elems(D.T, D.H, D.Hkv, D.hd) <= R.tca_n;
+    return g_flash && R.sp && flash_ok(D.hd) && flash_scratch_elems(D.T, D.H, D.Hkv, D.hd) <= R.tca_n;
 }
 
 int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *lora, float *loss_out,
@@ -1709,11 +1710,11 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
                          tp.tv + (int64_t)l * Tn * r, qkv + d + D.kvd, D.qn));
         }
         ALTXS_LAUNCH(kKTtt, st, t_qk<<<Tn, 256, 0, st>>>(D, l, i, tp, *w));
-        const bool flash = use_flash(R, head);
+        const bool flash = use_flash(R);
         if (!flash) TRY(attn_probs(R, l));
         // the full-parameter gradient keeps every application's attention output and projections
         const bool o_on_y = r > 0 && (mask & 64);
-        float *yb = D.full || o_on_y ? tp.yl + (int64_t)l * Tn * d : tp.y;
+        float *yb = D.full || o_on_y || flash ? tp.yl + (int64_t)l * Tn * d : tp.y;
         float *aob = tp.aol ? tp.aol + (int64_t)l * Tn * d : tp.ao;
         const bool ym = ymotif(D, i);
         float *ya = ym ? tp.yraw + (int64_t)l * Tn * d : yb;  // P v, before XSA and the gate
@@ -1734,7 +1735,7 @@ int forward(const Run &R, const int32_t *tok, const int32_t *tgt, const float *l
             fa.y = ya;
             fa.ldy = d;
             fa.scratch = R.tca;
-            fa.lse = head && D.full ? tp.lse + (int64_t)l * D.H * Tn : nullptr;  // for the flash backward
+            fa.lse = head ? tp.lse + (int64_t)l * D.H * Tn : nullptr;  // for the flash backward
             TRY(launch_flash_fwd(fa, st));
         } else if (R.sp) {
             const uint16_t *Ph = p_planes(R, l), *Pl = Ph + D.H * Tn * ldp;
@@ -1917,7 +1918,8 @@ int backward(const Run &R, const float *lora, float *grad) {
         // attention backward: the flash kernels from the forward's output and
         // log-sum-exp, or the probabilities recomputed (full-parameter gradient)
         // or kept (update) and the products over them
-        const bool fbwd = full && use_flash(R, true) && flash_bwd_scratch_elems(Tn, D.H, D.Hkv) <= R.tca_n;
+        const bool fwd_flash = use_flash(R);
+        const bool fbwd = fwd_flash && flash_bwd_scratch_elems(Tn, D.H, D.Hkv) <= R.tca_n;
         if (fbwd) {
             FlashBwdArgs fb{};
             fb.T = Tn;
@@ -1945,7 +1947,7 @@ int backward(const Run &R, const float *lora, float *grad) {
             fb.scratch = R.tca;
             TRY(launch_flash_bwd(fb, st));
         } else {
-        if (full) TRY(attn_probs(R, l));
+        if (full || fwd_flash) TRY(attn_probs(R, l));
         const float *P = p_f32(R, l);
         const float *qkv = tp.qkv + (int64_t)l * Tn * D.qn;
         const float *qr = tp.qr + (int64_t)l * Td, *kr = tp.kr + (int64_t)l * Tn * D.kvd;
