@@ -508,10 +508,12 @@ def run_replenish(args) -> None:
 
 def run_attention(args) -> None:
     """Window attention (``altxs_window_attention``: the flash kernel of the
-    prefill and the full-parameter forward) at the 33M window (T 2047, 8 heads
-    of 64), CUDA events around 20 calls each after a warm-up, median; tensor
+    prefill, the update and the full-parameter forward) and its backward
+    (``altxs_window_attention_backward``) at the 33M window (T 2047, 8 heads of
+    64), CUDA events around 20 calls each after a warm-up, median; tensor
     roofline on the executed products (3 hi/lo bf16 MMAs per fp32 product:
-    6 T^2 hd H flops for the causal half) over the measured bf16 peak.  Then
+    6 T^2 hd H flops for the causal half of each of the forward's 2 and the
+    backward's 7 products) over the measured bf16 peak.  Then
     one reset-mode context prefill of the 33M model (2047 rows, 8 layers) on
     the flash kernel and on the materialised T x T attention."""
     import ctypes
@@ -558,6 +560,41 @@ def run_attention(args) -> None:
         print(json.dumps({"attention": True, "T": T, "H": H, "Hkv": Hkv, "hd": hd, "us": us,
                           "executed_tflops": tf, "frac": tf / peaks["bf16_tflops"],
                           "peak_source": f"{kind} bf16_tflops", "note": "split pass + flash kernel"}), flush=True)
+        # the backward from this forward's output and log-sum-exp
+        lse = torch.empty(H, T, device=dev)
+        _lib.check(L.altxs_window_attention(T, H, Hkv, hd, ctypes.c_float(1.0 / hd ** 0.5), q.data_ptr(),
+                                            q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                                            y.data_ptr(), y.stride(0), lse.data_ptr(), ws.data_ptr(), wsb, st),
+                   "altxs_window_attention")
+        dy = torch.randn(T, H * hd, generator=g, device=dev)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        wbb = int(L.altxs_window_attention_backward_workspace_bytes(T, H, Hkv, hd))
+        wsbw = torch.empty(wbb, dtype=torch.uint8, device=dev)
+
+        def bwd():
+            _lib.check(L.altxs_window_attention_backward(
+                T, H, Hkv, hd, ctypes.c_float(1.0 / hd ** 0.5), q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
+                v.data_ptr(), v.stride(0), y.data_ptr(), y.stride(0), lse.data_ptr(), dy.data_ptr(), dy.stride(0),
+                dq.data_ptr(), dq.stride(0), dk.data_ptr(), dk.stride(0), dv.data_ptr(), dv.stride(0),
+                wsbw.data_ptr(), wbb, st), "altxs_window_attention_backward")
+
+        for _ in range(3):
+            bwd()
+        times = []
+        for _ in range(20):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            bwd()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        us = statistics.median(times) * 1e3
+        flops = 7 * 3.0 * T * T * hd * H  # S, dP, dq; S^T, dP^T, dk, dv: causal halves, 3 MMAs per product
+        tf = flops / (us / 1e6) / 1e12
+        print(json.dumps({"attention_backward": True, "T": T, "H": H, "Hkv": Hkv, "hd": hd, "us": us,
+                          "executed_tflops": tf, "frac": tf / peaks["bf16_tflops"],
+                          "peak_source": f"{kind} bf16_tflops",
+                          "note": "split pass + dsum + dk/dv kernel + dq kernel"}), flush=True)
     cfg = dataclasses.replace(c3_config(), context_mode="reset")
     dm = DeviceModel(C.synth_weights(cfg, seed=WEIGHT_SEED), dev, tensor_cores=True)
     b = StreamBatch(dm, 1, words_per_stream=8, hist_len=cfg.ctx + 2)
