@@ -625,6 +625,15 @@ __global__ void __launch_bounds__(320, 1)
             tc_fence_after();
             int col0, ch;
             col_of(t, col0, ch);
+            // dk / dv: the 32 columns' lse and D, one coalesced load per lane, shared by shuffle
+            float lse_c = 0.0f, d_c = 0.0f;
+            if (KV) {
+                const int cq = col0 + half * (CN / 2) + lane;
+                if (cq < a.T) {
+                    lse_c = a.lse[(int64_t)ch * a.T + cq];
+                    d_c = dsum[(int64_t)ch * a.T + cq];
+                }
+            }
 #pragma unroll
             for (int c0 = 0; c0 < CN / 2; c0 += 32) {
                 const int cl = half * (CN / 2) + c0;  // first local column of this block
@@ -636,10 +645,10 @@ __global__ void __launch_bounds__(320, 1)
                     const int col = col0 + cl + u;
                     float lse, dd;
                     bool in;
-                    if (KV) {  // row = key, col = query of head ch
+                    if (KV) {  // row = key, col = query of head ch (CN / 2 = 32: lane u holds column u)
                         in = col < a.T && row <= col;
-                        lse = in ? a.lse[(int64_t)ch * a.T + col] : 0.0f;
-                        dd = in ? dsum[(int64_t)ch * a.T + col] : 0.0f;
+                        lse = __shfl_sync(kAll, lse_c, u);
+                        dd = __shfl_sync(kAll, d_c, u);
                     } else {  // row = query, col = key
                         in = col <= rq;
                         lse = lse_r;
