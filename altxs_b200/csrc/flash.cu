@@ -17,9 +17,10 @@
 //           P_h V_h folded in with its rescale, then p = 2^(x - m), the sum,
 //           and p as hi/lo planes in shared memory (the A operand of P V).
 // After the last tile the two halves of each row are combined: y = O / l
-// (and, on request, the row's log-sum-exp for the backward).  Every wait is bounded; a wait that gives up
-// stops the CTA's roles, drains its copies and MMAs, frees the tensor memory
-// and leaves y unwritten.
+// (and, on request, the row's log-sum-exp for the backward).  Every wait is
+// bounded; a wait that gives up stops the CTA's roles, drains its copies and
+// MMAs, frees the tensor memory and leaves y unwritten.  The backward kernels
+// (dq; dk and dv) follow after the forward, below.
 //
 // The rows are the reference's causal softmax attention over the window
 // (model.py CausalSelfAttention via F.scaled_dot_product_attention, is_causal,
